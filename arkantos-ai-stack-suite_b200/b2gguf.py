@@ -1,0 +1,268 @@
+"""ctypes binding for libb2gguf.so (the C ABI declared in include/b2gguf.h).
+
+There is no fallback: if the shared library is missing or fails to load,
+importing this module raises.  Build it with `make -C arkantos-ai-stack-suite_b200`
+(or __graft_entry__.build()).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libb2gguf.so")
+HEADER = os.path.join(ROOT, "include", "b2gguf.h")
+
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, Q8_K = 0, 1, 2, 8, 12, 14, 15
+OK, NO_KV_SLOT, ABORTED = 0, 1, 2
+ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_FORMAT, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NCCL, ERR_IO = -1, -2, -3, -4, -5, -6, -7, -8
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"libb2gguf.so not built at {LIB_PATH}; run make -C {HERE}")
+
+lib = ctypes.CDLL(LIB_PATH)
+
+_vp, _i, _i64, _u64, _f, _sz = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_uint64,
+                                ctypes.c_float, ctypes.c_size_t)
+_TYPES = {"void*": _vp, "const void*": _vp, "int": _i, "int64_t": _i64, "uint64_t": _u64, "float": _f,
+          "size_t": _sz, "int32_t": ctypes.c_int32, "uint32_t": ctypes.c_uint32}
+
+
+def header_functions() -> list[str]:
+    """Names of every function declared in include/b2gguf.h."""
+    with open(HEADER) as f:
+        src = f.read()
+    return re.findall(r"^B2_API\s+[\w\s\*]+?\b(b2_\w+)\s*\(", src, flags=re.M)
+
+
+def _bind() -> None:
+    # Every pointer is passed as c_void_p; integers and floats are typed so
+    # ctypes converts them exactly.
+    sig = {
+        "b2_abi_version": (_i, []),
+        "b2_last_error": (ctypes.c_char_p, []),
+        "b2_device_count": (_i, [_vp]),
+        "b2_set_device": (_i, [_i]),
+        "b2_get_device": (_i, [_vp]),
+        "b2_malloc": (_i, [_vp, _sz]),
+        "b2_free": (_i, [_vp]),
+        "b2_host_alloc": (_i, [_vp, _sz]),
+        "b2_host_free": (_i, [_vp]),
+        "b2_memcpy_h2d": (_i, [_vp, _vp, _sz, _vp]),
+        "b2_memcpy_d2h": (_i, [_vp, _vp, _sz, _vp]),
+        "b2_memcpy_d2d": (_i, [_vp, _vp, _sz, _vp]),
+        "b2_memset": (_i, [_vp, _i, _sz, _vp]),
+        "b2_stream_create": (_i, [_vp]),
+        "b2_stream_destroy": (_i, [_vp]),
+        "b2_stream_synchronize": (_i, [_vp]),
+        "b2_device_synchronize": (_i, []),
+        "b2_event_create": (_i, [_vp]),
+        "b2_event_destroy": (_i, [_vp]),
+        "b2_event_record": (_i, [_vp, _vp]),
+        "b2_event_elapsed_ms": (_i, [_vp, _vp, _vp]),
+        "b2_set_pdl": (_i, [_i]),
+        "b2_row_bytes": (_sz, [_i, _i64]),
+        "b2_quantize_weights": (_i, [_i, _vp, _i64, _i64, _vp, _i]),
+        "b2_synth_normal": (_i, [_u64, _u64, _i64, _f, _f, _vp, _i]),
+        "b2_rope_table": (_i, [_f, _i, _i, _i, _vp]),
+        "b2_qmatrix_upload": (_i, [_i, _vp, _i64, _i64, _vp]),
+        "b2_qmatrix_free": (_i, [_vp]),
+        "b2_qmatrix_device_bytes": (_i, [_vp, _vp]),
+        "b2_qmatrix_dequantize": (_i, [_vp, _vp, _vp]),
+        "b2_quantize_act": (_i, [_i, _vp, _i, _i64, _vp, _vp]),
+        "b2_gemv": (_i, [_vp, _vp, _i, _vp, _vp]),
+        "b2_gemv_host": (_i, [_vp, _vp, _i, _vp]),
+        "b2_block_dots": (_i, [_vp, _i64, _vp, _vp, _vp, _vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+_bind()
+
+
+class B2Error(RuntimeError):
+    def __init__(self, rc: int, what: str):
+        msg = lib.b2_last_error()
+        super().__init__(f"{what} failed rc={rc}: {msg.decode() if msg else ''}")
+        self.rc = rc
+
+
+def check(rc: int, what: str = "b2 call") -> int:
+    if rc < 0:
+        raise B2Error(rc, what)
+    return rc
+
+
+def ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"], "array must be C-contiguous"
+    return a.ctypes.data
+
+
+# ---- device memory -----------------------------------------------------------------------
+class DeviceBuffer:
+    """Raw device allocation owned by Python."""
+
+    def __init__(self, nbytes: int):
+        p = ctypes.c_void_p()
+        check(lib.b2_malloc(ctypes.byref(p), max(1, int(nbytes))), "b2_malloc")
+        self.ptr = p.value
+        self.nbytes = int(nbytes)
+
+    @classmethod
+    def from_array(cls, a: np.ndarray) -> "DeviceBuffer":
+        a = np.ascontiguousarray(a)
+        b = cls(a.nbytes)
+        b.upload(a)
+        return b
+
+    def upload(self, a: np.ndarray, stream: int | None = None) -> None:
+        a = np.ascontiguousarray(a)
+        assert a.nbytes <= self.nbytes
+        check(lib.b2_memcpy_h2d(self.ptr, ptr(a), a.nbytes, stream), "h2d")
+        if stream is None:
+            check(lib.b2_stream_synchronize(None), "sync")
+
+    def download(self, dtype, count: int | None = None, stream: int | None = None) -> np.ndarray:
+        dt = np.dtype(dtype)
+        n = self.nbytes // dt.itemsize if count is None else int(count)
+        out = np.empty(n, dt)
+        check(lib.b2_memcpy_d2h(ptr(out), self.ptr, out.nbytes, stream), "d2h")
+        check(lib.b2_stream_synchronize(stream), "sync")
+        return out
+
+    def zero(self) -> None:
+        check(lib.b2_memset(self.ptr, 0, self.nbytes, None), "memset")
+
+    def free(self) -> None:
+        if getattr(self, "ptr", None):
+            lib.b2_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def synchronize() -> None:
+    check(lib.b2_device_synchronize(), "device_synchronize")
+
+
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    rc = lib.b2_device_count(ctypes.byref(n))
+    return n.value if rc == 0 else 0
+
+
+class Event:
+    def __init__(self):
+        p = ctypes.c_void_p()
+        check(lib.b2_event_create(ctypes.byref(p)), "event_create")
+        self.h = p.value
+
+    def record(self, stream: int | None = None) -> None:
+        check(lib.b2_event_record(self.h, stream), "event_record")
+
+    def elapsed_ms(self, end: "Event") -> float:
+        ms = ctypes.c_float()
+        check(lib.b2_event_elapsed_ms(self.h, end.h, ctypes.byref(ms)), "event_elapsed")
+        return ms.value
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.b2_event_destroy(self.h)
+
+
+# ---- host helpers ---------------------------------------------------------------------------
+BLOCK = {Q4_0: 32, Q8_0: 32, Q4_K: 256, Q6_K: 256, Q8_K: 256, F32: 1, F16: 1}
+
+
+def row_bytes(t: int, k: int) -> int:
+    return int(lib.b2_row_bytes(t, k))
+
+
+def quantize_weights(t: int, w: np.ndarray, n_threads: int = 8) -> np.ndarray:
+    w = np.ascontiguousarray(w, np.float32)
+    n, k = w.shape
+    out = np.empty((n, row_bytes(t, k)), np.uint8)
+    check(lib.b2_quantize_weights(t, ptr(w), n, k, ptr(out), n_threads), "quantize_weights")
+    return out
+
+
+def synth_normal(seed: int, n: int, std: float = 1.0, mean: float = 0.0, offset: int = 0,
+                 n_threads: int = 8) -> np.ndarray:
+    out = np.empty(int(n), np.float32)
+    check(lib.b2_synth_normal(seed, offset, int(n), mean, std, ptr(out), n_threads), "synth_normal")
+    return out
+
+
+def rope_table(theta: float, head_dim: int, p0: int, n_pos: int) -> np.ndarray:
+    out = np.empty((n_pos, head_dim), np.float32)
+    check(lib.b2_rope_table(theta, head_dim, p0, n_pos, ptr(out)), "rope_table")
+    return out
+
+
+# ---- quantized matrices and single ops --------------------------------------------------------
+class QMatrix:
+    """A GGUF tensor uploaded to the current device in the repacked layout."""
+
+    def __init__(self, qtype: int, gguf_bytes: np.ndarray, n_rows: int, k: int):
+        gguf_bytes = np.ascontiguousarray(gguf_bytes, np.uint8)
+        assert gguf_bytes.nbytes == n_rows * row_bytes(qtype, k)
+        h = ctypes.c_void_p()
+        check(lib.b2_qmatrix_upload(qtype, ptr(gguf_bytes), n_rows, k, ctypes.byref(h)), "qmatrix_upload")
+        self.h = h.value
+        self.qtype, self.n_rows, self.k = qtype, n_rows, k
+
+    def device_bytes(self) -> int:
+        v = ctypes.c_int64()
+        check(lib.b2_qmatrix_device_bytes(self.h, ctypes.byref(v)), "qmatrix_device_bytes")
+        return v.value
+
+    def dequantize(self) -> np.ndarray:
+        buf = DeviceBuffer(self.n_rows * self.k * 4)
+        check(lib.b2_qmatrix_dequantize(self.h, buf.ptr, None), "qmatrix_dequantize")
+        return buf.download(np.float32).reshape(self.n_rows, self.k)
+
+    def gemv_device(self, x: DeviceBuffer, n_tok: int, y: DeviceBuffer, stream: int | None = None) -> None:
+        check(lib.b2_gemv(self.h, x.ptr, n_tok, y.ptr, stream), "gemv")
+
+    def gemv(self, x: np.ndarray) -> np.ndarray:
+        """Device GEMV from host arrays (the e2e path): x [n_tok, k] -> y [n_tok, n_rows]."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        y = np.empty((x.shape[0], self.n_rows), np.float32)
+        check(lib.b2_gemv_host(self.h, ptr(x), x.shape[0], ptr(y)), "gemv_host")
+        return y
+
+    def block_dots(self, row: int, x: np.ndarray):
+        x = np.ascontiguousarray(x, np.float32)
+        nb = self.k // BLOCK[self.qtype]
+        xd = DeviceBuffer.from_array(x)
+        oi = DeviceBuffer(nb * 4)
+        om = DeviceBuffer(nb * 4) if self.qtype == Q4_K else None
+        check(lib.b2_block_dots(self.h, row, xd.ptr, oi.ptr, om.ptr if om else None, None), "block_dots")
+        a = oi.download(np.int32)
+        return (a, om.download(np.int32)) if om else a
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.b2_qmatrix_free(self.h)
+            self.h = None
+
+
+def quantize_act(act_type: int, x: np.ndarray) -> np.ndarray:
+    """Device activation quantization -> GGUF block bytes [n_tok, row_bytes]."""
+    x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+    n_tok, k = x.shape
+    xd = DeviceBuffer.from_array(x)
+    out = DeviceBuffer(n_tok * row_bytes(act_type, k))
+    check(lib.b2_quantize_act(act_type, xd.ptr, n_tok, k, out.ptr, None), "quantize_act")
+    return out.download(np.uint8).reshape(n_tok, -1)

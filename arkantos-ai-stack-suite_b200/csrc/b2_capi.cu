@@ -1,0 +1,342 @@
+// C ABI: device utilities, host format helpers, the GGUF tensor upload and the
+// single-op entry points.  Every function is noexcept and maps failures to a
+// status code with a message for b2_last_error().
+#include <string.h>
+
+#include <new>
+#include <thread>
+#include <vector>
+
+#include "b2_common.cuh"
+
+struct b2_qmatrix {
+  b2::QMatrix m;
+};
+
+namespace b2 {
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Stream-ordered planar activation buffer for n_tok rows of kp values.
+int alloc_act(ActQ& a, int type, int n_tok, int64_t kp, cudaStream_t s) {
+  a.type = type;
+  a.n_tok = n_tok;
+  a.kp = kp;
+  const size_t nq = (size_t)n_tok * kp;
+  const size_t nd = (size_t)n_tok * (type == B2_Q8_0 ? kp / 32 : kp / 256);
+  const size_t nb = type == B2_Q8_K ? (size_t)n_tok * (kp / 16) : 0;
+  void* base = nullptr;
+  const size_t bytes = (nq + 15) / 16 * 16 + nd * 4 + nb * 2 + 64;
+  B2_CUDA_TRY(cudaMallocAsync(&base, bytes, s));
+  a.qs = static_cast<int8_t*>(base);
+  a.d = reinterpret_cast<float*>(static_cast<uint8_t*>(base) + (nq + 15) / 16 * 16);
+  a.bsum = nb ? reinterpret_cast<int16_t*>(a.d + nd) : nullptr;
+  return B2_OK;
+}
+
+void free_act(ActQ& a, cudaStream_t s) {
+  if (a.qs) cudaFreeAsync(a.qs, s);
+  a.qs = nullptr;
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+int b2_abi_version(void) { return B2_ABI_VERSION; }
+const char* b2_last_error(void) { return b2::last_error(); }
+
+int b2_device_count(int* n) {
+  B2_CHECK_ARG(n, "n");
+  B2_CUDA_TRY(cudaGetDeviceCount(n));
+  return B2_OK;
+}
+int b2_set_device(int device) {
+  B2_CUDA_TRY(cudaSetDevice(device));
+  return B2_OK;
+}
+int b2_get_device(int* device) {
+  B2_CHECK_ARG(device, "device");
+  B2_CUDA_TRY(cudaGetDevice(device));
+  return B2_OK;
+}
+int b2_malloc(void** dptr, size_t bytes) {
+  B2_CHECK_ARG(dptr, "dptr");
+  B2_CUDA_TRY(cudaMalloc(dptr, bytes ? bytes : 1));
+  return B2_OK;
+}
+int b2_free(void* dptr) {
+  B2_CUDA_TRY(cudaFree(dptr));
+  return B2_OK;
+}
+int b2_host_alloc(void** hptr, size_t bytes) {
+  B2_CHECK_ARG(hptr, "hptr");
+  B2_CUDA_TRY(cudaMallocHost(hptr, bytes ? bytes : 1));
+  return B2_OK;
+}
+int b2_host_free(void* hptr) {
+  B2_CUDA_TRY(cudaFreeHost(hptr));
+  return B2_OK;
+}
+int b2_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+  B2_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, as_stream(stream)));
+  return B2_OK;
+}
+int b2_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+  B2_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, as_stream(stream)));
+  return B2_OK;
+}
+int b2_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
+  B2_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
+  return B2_OK;
+}
+int b2_memset(void* dst, int value, size_t bytes, void* stream) {
+  B2_CUDA_TRY(cudaMemsetAsync(dst, value, bytes, as_stream(stream)));
+  return B2_OK;
+}
+int b2_stream_create(void** stream) {
+  B2_CHECK_ARG(stream, "stream");
+  cudaStream_t s;
+  B2_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = s;
+  return B2_OK;
+}
+int b2_stream_destroy(void* stream) {
+  B2_CUDA_TRY(cudaStreamDestroy(as_stream(stream)));
+  return B2_OK;
+}
+int b2_stream_synchronize(void* stream) {
+  B2_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
+  return B2_OK;
+}
+int b2_device_synchronize(void) {
+  B2_CUDA_TRY(cudaDeviceSynchronize());
+  return B2_OK;
+}
+int b2_event_create(void** event) {
+  B2_CHECK_ARG(event, "event");
+  cudaEvent_t e;
+  B2_CUDA_TRY(cudaEventCreate(&e));
+  *event = e;
+  return B2_OK;
+}
+int b2_event_destroy(void* event) {
+  B2_CUDA_TRY(cudaEventDestroy(static_cast<cudaEvent_t>(event)));
+  return B2_OK;
+}
+int b2_event_record(void* event, void* stream) {
+  B2_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(event), as_stream(stream)));
+  return B2_OK;
+}
+int b2_event_elapsed_ms(void* start, void* stop, float* ms) {
+  B2_CHECK_ARG(ms, "ms");
+  B2_CUDA_TRY(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop)));
+  return B2_OK;
+}
+int b2_set_pdl(int enabled) {
+  b2::set_pdl(enabled != 0);
+  return B2_OK;
+}
+
+// ---- host format helpers -------------------------------------------------------------
+size_t b2_row_bytes(int type, int64_t k) { return b2::row_bytes(type, k); }
+
+int b2_quantize_weights(int type, const float* src, int64_t n_rows, int64_t k, void* dst, int n_threads) {
+  B2_CHECK_ARG(src && dst && n_rows >= 0 && k > 0, "quantize_weights arguments");
+  try {
+    return b2::quantize_weights(type, src, n_rows, k, dst, n_threads);
+  } catch (...) {
+    b2::set_error("quantize_weights: host exception");
+    return B2_ERR_OOM;
+  }
+}
+
+int b2_synth_normal(uint64_t seed, uint64_t offset, int64_t n, float mean, float std_dev, float* out, int n_threads) {
+  B2_CHECK_ARG(out && n >= 0, "synth_normal arguments");
+  try {
+    return b2::synth_normal(seed, offset, n, mean, std_dev, out, n_threads);
+  } catch (...) {
+    b2::set_error("synth_normal: host exception");
+    return B2_ERR_OOM;
+  }
+}
+
+int b2_rope_table(float theta, int head_dim, int p0, int n_pos, float* out) {
+  B2_CHECK_ARG(out && head_dim > 0 && (head_dim % 2) == 0 && n_pos >= 0, "rope_table arguments");
+  b2::rope_table(theta, head_dim, p0, n_pos, out);
+  return B2_OK;
+}
+
+// ---- GGUF tensor upload ----------------------------------------------------------------
+int b2_qmatrix_upload(int type, const void* gguf_bytes, int64_t n_rows, int64_t k, b2_qmatrix** out) {
+  B2_CHECK_ARG(out && gguf_bytes && n_rows > 0 && k > 0, "qmatrix_upload arguments");
+  B2_CHECK_ARG(b2::is_weight_type(type), "weight type must be Q4_0, Q8_0, Q4_K or Q6_K");
+  B2_CHECK_ARG(k % b2::block_elems(type) == 0, "k must be a multiple of the block size");
+  *out = nullptr;
+  b2_qmatrix* h = new (std::nothrow) b2_qmatrix;
+  if (!h) {
+    set_error("qmatrix_upload: host allocation");
+    return B2_ERR_OOM;
+  }
+  QMatrix& m = h->m;
+  m.type = type;
+  m.n_rows = n_rows;
+  m.k = k;
+  plan_qmatrix(m);
+  cudaGetDevice(&m.device);
+  const size_t b0 = (size_t)m.p0_row * n_rows, b1 = (size_t)m.p1_row * n_rows;
+  cudaError_t e = cudaMalloc(&m.plane0, b0);
+  if (e == cudaSuccess && b1) e = cudaMalloc(&m.plane1, b1);
+  if (e != cudaSuccess) {
+    if (m.plane0) cudaFree(m.plane0);
+    delete h;
+    set_error("qmatrix_upload: device allocation of %zu bytes: %s", b0 + b1, cudaGetErrorString(e));
+    return B2_ERR_OOM;
+  }
+  // Repack in slabs through pinned staging buffers, rows split over threads.
+  const int64_t slab = std::max<int64_t>(1, (int64_t)(64u << 20) / std::max<int64_t>(1, m.p0_row + m.p1_row));
+  uint8_t *h0 = nullptr, *h1 = nullptr;
+  e = cudaMallocHost(&h0, (size_t)m.p0_row * slab);
+  if (e == cudaSuccess && b1) e = cudaMallocHost(&h1, (size_t)m.p1_row * slab);
+  int rc = B2_OK;
+  if (e != cudaSuccess) {
+    set_error("qmatrix_upload: pinned staging: %s", cudaGetErrorString(e));
+    rc = B2_ERR_OOM;
+  }
+  const int nt = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  for (int64_t r0 = 0; rc == B2_OK && r0 < n_rows; r0 += slab) {
+    const int64_t r1 = std::min(n_rows, r0 + slab);
+    std::vector<std::thread> th;
+    auto work = [&](int64_t a, int64_t b) {
+      repack_rows_host(m, static_cast<const uint8_t*>(gguf_bytes), a, b, h0 + (a - r0) * m.p0_row,
+                       h1 ? h1 + (a - r0) * m.p1_row : nullptr);
+    };
+    const int64_t n = r1 - r0;
+    for (int t = 1; t < nt; ++t) th.emplace_back(work, r0 + n * t / nt, r0 + n * (t + 1) / nt);
+    work(r0, r0 + n / nt);
+    for (auto& x : th) x.join();
+    e = cudaMemcpy(m.plane0 + r0 * m.p0_row, h0, (size_t)n * m.p0_row, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && h1) e = cudaMemcpy(m.plane1 + r0 * m.p1_row, h1, (size_t)n * m.p1_row, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      set_error("qmatrix_upload: copy: %s", cudaGetErrorString(e));
+      rc = B2_ERR_CUDA;
+    }
+  }
+  if (h0) cudaFreeHost(h0);
+  if (h1) cudaFreeHost(h1);
+  if (rc != B2_OK) {
+    cudaFree(m.plane0);
+    if (m.plane1) cudaFree(m.plane1);
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return B2_OK;
+}
+
+int b2_qmatrix_free(b2_qmatrix* h) {
+  if (!h) return B2_OK;
+  if (h->m.owns) {
+    cudaFree(h->m.plane0);
+    if (h->m.plane1) cudaFree(h->m.plane1);
+  }
+  delete h;
+  return B2_OK;
+}
+
+int b2_qmatrix_device_bytes(const b2_qmatrix* h, int64_t* bytes) {
+  B2_CHECK_ARG(h && bytes, "qmatrix_device_bytes arguments");
+  *bytes = (h->m.p0_row + h->m.p1_row) * h->m.n_rows;
+  return B2_OK;
+}
+
+int b2_qmatrix_dequantize(const b2_qmatrix* h, float* dst, void* stream) {
+  B2_CHECK_ARG(h && dst, "qmatrix_dequantize arguments");
+  return launch_dequantize(h->m, dst, as_stream(stream));
+}
+
+// ---- single ops ---------------------------------------------------------------------------
+int b2_quantize_act(int act_type, const float* x, int n_tok, int64_t k, void* blocks, void* stream) {
+  B2_CHECK_ARG(x && blocks && n_tok > 0 && k > 0, "quantize_act arguments");
+  B2_CHECK_ARG(act_type == B2_Q8_0 || act_type == B2_Q8_K, "act_type must be Q8_0 or Q8_K");
+  const int64_t be = act_type == B2_Q8_0 ? 32 : 256;
+  B2_CHECK_ARG(k % be == 0, "k must be a multiple of the block size");
+  cudaStream_t s = as_stream(stream);
+  ActQ a;
+  int rc = alloc_act(a, act_type, n_tok, (k + 255) / 256 * 256, s);
+  if (rc != B2_OK) return rc;
+  rc = launch_quantize_act(act_type, x, k, n_tok, k, a, s);
+  if (rc == B2_OK) rc = launch_act_to_blocks(a, k, blocks, s);
+  free_act(a, s);
+  return rc;
+}
+
+int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stream) {
+  B2_CHECK_ARG(w && x && y, "gemv arguments");
+  GemvArgs a = {};
+  a.w = &w->m;
+  a.x = x;
+  a.x_stride = w->m.k;
+  a.n_tok = n_tok;
+  a.y = y;
+  a.y_stride = w->m.n_rows;
+  a.epilogue = EPI_STORE;
+  a.row_begin = 0;
+  a.row_end = w->m.n_rows;
+  cudaStream_t s = as_stream(stream);
+  int rc = launch_gemv(a, s);
+  if (rc == B2_ERR_UNSUPPORTED) {
+    // Activations too large for shared memory next to the weight ring:
+    // quantize them once into planes, then stream.
+    ActQ act;
+    rc = alloc_act(act, act_type_for(w->m.type), n_tok, w->m.kp, s);
+    if (rc != B2_OK) return rc;
+    rc = launch_quantize_act(act.type, x, w->m.k, n_tok, w->m.k, act, s);
+    if (rc == B2_OK) {
+      a.act = &act;
+      rc = launch_gemv(a, s);
+    }
+    free_act(act, s);
+  }
+  return rc;
+}
+
+int b2_gemv_host(const b2_qmatrix* w, const float* x_host, int n_tok, float* y_host) {
+  B2_CHECK_ARG(w && x_host && y_host && n_tok >= 1 && n_tok <= 8, "gemv_host arguments");
+  const size_t xb = (size_t)n_tok * w->m.k * 4, yb = (size_t)n_tok * w->m.n_rows * 4;
+  cudaStream_t s = 0;
+  void* buf = nullptr;
+  B2_CUDA_TRY(cudaMallocAsync(&buf, xb + yb + 256, s));
+  float* xd = static_cast<float*>(buf);
+  float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + (xb + 255) / 256 * 256);
+  int rc = B2_OK;
+  if (cudaMemcpyAsync(xd, x_host, xb, cudaMemcpyHostToDevice, s) != cudaSuccess) rc = B2_ERR_CUDA;
+  if (rc == B2_OK) rc = b2_gemv(w, xd, n_tok, yd, s);
+  if (rc == B2_OK && cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, s) != cudaSuccess) rc = B2_ERR_CUDA;
+  cudaFreeAsync(buf, s);
+  const cudaError_t e = cudaStreamSynchronize(s);
+  if (rc == B2_OK && e != cudaSuccess) {
+    set_error("gemv_host: %s", cudaGetErrorString(e));
+    rc = B2_ERR_CUDA;
+  }
+  return rc;
+}
+
+int b2_block_dots(const b2_qmatrix* w, int64_t row, const float* x, int32_t* out_i, int32_t* out_m, void* stream) {
+  B2_CHECK_ARG(w && x && out_i && row >= 0 && row < w->m.n_rows, "block_dots arguments");
+  B2_CHECK_ARG(w->m.type != B2_Q4_K || out_m, "Q4_K needs out_m");
+  cudaStream_t s = as_stream(stream);
+  ActQ a;
+  int rc = alloc_act(a, act_type_for(w->m.type), 1, w->m.kp, s);
+  if (rc != B2_OK) return rc;
+  rc = launch_quantize_act(a.type, x, w->m.k, 1, w->m.k, a, s);
+  if (rc == B2_OK) rc = launch_block_dots(w->m, a, row, out_i, out_m, s);
+  free_act(a, s);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,265 @@
+// Activation quantization to planar Q8 buffers, conversion back to GGUF
+// blocks, exact integer block dots, and on-device dequantization of a
+// repacked matrix (parity paths).
+#include "b2_common.cuh"
+#include "b2_quant.cuh"
+
+namespace b2 {
+namespace {
+
+// One warp per 32-block (Q8_0) or 256-block (Q8_K) of one token row.
+__global__ void quantize_q8_0_kernel(const float* __restrict__ x, int64_t x_stride, int n_tok, int64_t k,
+                                     int64_t kp, int8_t* __restrict__ qs, float* __restrict__ d) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t nbk = kp / 32;
+  const int64_t total = (int64_t)n_tok * nbk;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t i = wid; i < total; i += nw) {
+    const int t = (int)(i / nbk);
+    const int64_t kb = i - (int64_t)t * nbk;
+    const int64_t e = kb * 32 + lane;
+    const float xv = e < k ? x[t * x_stride + e] : 0.0f;
+    uint16_t d16;
+    const int8_t q = quant_q8_0_lane(xv, &d16);
+    qs[t * kp + e] = q;
+    if (lane == 0) d[t * nbk + kb] = h2f(d16);
+  }
+}
+
+__global__ void quantize_q8_k_kernel(const float* __restrict__ x, int64_t x_stride, int n_tok, int64_t k,
+                                     int64_t kp, int8_t* __restrict__ qs, float* __restrict__ d,
+                                     int16_t* __restrict__ bsum) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t nbk = kp / 256;
+  const int64_t total = (int64_t)n_tok * nbk;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t i = wid; i < total; i += nw) {
+    const int t = (int)(i / nbk);
+    const int64_t kb = i - (int64_t)t * nbk;
+    const int64_t e0 = kb * 256 + lane * 8;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (e0 + j) < k ? x[t * x_stride + e0 + j] : 0.0f;
+    int8_t q[8];
+    int bs;
+    const float dd = quant_q8_k_lane(v, q, &bs);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qs[t * kp + e0 + j] = q[j];
+    if ((lane & 1) == 0) bsum[t * (kp / 16) + kb * 16 + lane / 2] = (int16_t)bs;
+    if (lane == 0) d[t * nbk + kb] = dd;
+  }
+}
+
+// Planar activations -> GGUF blocks (Q8_0: fp16 d + 32 int8; Q8_K: fp32 d,
+// 256 int8, 16 int16 sums).  One thread per block.
+__global__ void act_to_blocks_kernel(int type, const int8_t* qs, const float* d, const int16_t* bsum, int n_tok,
+                                     int64_t k, int64_t kp, uint8_t* out) {
+  const int64_t bs = type == B2_Q8_0 ? 32 : 256;
+  const int64_t nb = k / bs;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n_tok * nb) return;
+  const int t = (int)(i / nb);
+  const int64_t b = i - (int64_t)t * nb;
+  if (type == B2_Q8_0) {
+    uint8_t* o = out + (t * nb + b) * 34;
+    const uint16_t h = f2h_rn(d[t * (kp / 32) + b]);
+    o[0] = h & 0xFF;
+    o[1] = h >> 8;
+    for (int j = 0; j < 32; ++j) o[2 + j] = (uint8_t)qs[t * kp + b * 32 + j];
+  } else {
+    uint8_t* o = out + (t * nb + b) * 292;
+    const float dv = d[t * (kp / 256) + b];
+    memcpy(o, &dv, 4);
+    for (int j = 0; j < 256; ++j) o[4 + j] = (uint8_t)qs[t * kp + b * 256 + j];
+    for (int g = 0; g < 16; ++g) {
+      const int16_t s = bsum[t * (kp / 16) + b * 16 + g];
+      memcpy(o + 260 + 2 * g, &s, 2);
+    }
+  }
+}
+
+// Exact integer block dots of one repacked row against token 0 of `a`.
+__global__ void block_dots_kernel(int type, const uint8_t* p0, const uint8_t* p1, int64_t p0_row, int64_t p0_chunk,
+                                  int64_t p1_row, int64_t p1_chunk, int kc, int64_t k, int64_t row, const int8_t* qs,
+                                  const int16_t* bsum, int32_t* out_i, int32_t* out_m) {
+  const int64_t bsz = (type == B2_Q4_0 || type == B2_Q8_0) ? 32 : 256;
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= k / bsz) return;
+  const int64_t col = b * bsz;
+  const int64_t c = col / kc, cc = col - c * kc;
+  const uint8_t* r0 = p0 + row * p0_row + c * p0_chunk;
+  if (type == B2_Q4_0) {
+    const uint8_t* q = r0 + (cc / 32) * 16;
+    int s = 0;
+    for (int j = 0; j < 16; ++j) s += ((int)(q[j] & 15) - 8) * qs[col + j] + ((int)(q[j] >> 4) - 8) * qs[col + j + 16];
+    out_i[b] = s;
+  } else if (type == B2_Q8_0) {
+    const int8_t* q = reinterpret_cast<const int8_t*>(r0 + cc);
+    int s = 0;
+    for (int j = 0; j < 32; ++j) s += (int)q[j] * qs[col + j];
+    out_i[b] = s;
+  } else if (type == B2_Q4_K) {
+    const uint8_t* bp = r0 + (cc / 256) * 144;
+    const uint8_t* sc = bp + 4;
+    int is = 0, ms = 0;
+    for (int j = 0; j < 8; ++j) {
+      int s, m;
+      if (j < 4) {
+        s = sc[j] & 63;
+        m = sc[j + 4] & 63;
+      } else {
+        s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
+        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+      }
+      int dot = 0;
+      for (int l = 0; l < 32; ++l) {
+        const int e = j * 32 + l;
+        const uint8_t byte = bp[16 + (e >> 6) * 32 + (e & 31)];
+        const int qv = ((e >> 5) & 1) ? (byte >> 4) : (byte & 15);
+        dot += qv * qs[col + e];
+      }
+      is += s * dot;
+      ms += m * ((int)bsum[col / 16 + 2 * j] + (int)bsum[col / 16 + 2 * j + 1]);
+    }
+    out_i[b] = is;
+    if (out_m) out_m[b] = ms;
+  } else {
+    const uint8_t* bp = r0 + (cc / 256) * 208;
+    const int8_t* sc = reinterpret_cast<const int8_t*>(bp + 192);
+    int is = 0;
+    for (int g = 0; g < 16; ++g) {
+      int dot = 0;
+      for (int l = 0; l < 16; ++l) {
+        const int e = g * 16 + l;
+        const int h = e >> 7, gg = (e >> 5) & 3, ll = e & 31;
+        const int lo = (bp[h * 64 + (gg & 1) * 32 + ll] >> (4 * (gg >> 1))) & 15;
+        const int hi = (bp[128 + h * 32 + ll] >> (2 * gg)) & 3;
+        dot += ((lo | (hi << 4)) - 32) * qs[col + e];
+      }
+      is += (int)sc[g] * dot;
+    }
+    out_i[b] = is;
+  }
+  (void)p1;
+  (void)p1_row;
+  (void)p1_chunk;
+}
+
+// fp32 dequantization of a repacked matrix: one thread per output value, the
+// same operation order as the GGUF layouts define (Q4_0: (q-8)·d; Q8_0: q·d;
+// Q4_K: (d·sc)·q − dmin·m; Q6_K: (d·sc)·q).
+__global__ void dequantize_kernel(int type, const uint8_t* p0, const uint8_t* p1, int64_t p0_row, int64_t p0_chunk,
+                                  int64_t p1_row, int64_t p1_chunk, int kc, int64_t n_rows, int64_t k, float* dst) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_rows * k) return;
+  const int64_t r = i / k, col = i - r * k;
+  const int64_t c = col / kc, cc = col - c * kc;
+  const uint8_t* r0 = p0 + r * p0_row + c * p0_chunk;
+  const uint8_t* r1 = p1 ? p1 + r * p1_row + c * p1_chunk : nullptr;
+  float v = 0.0f;
+  if (type == B2_Q4_0) {
+    const int b = (int)(cc / 32), j = (int)(cc % 32);
+    const uint8_t byte = r0[b * 16 + (j & 15)];
+    const int q = (j < 16 ? (byte & 15) : (byte >> 4)) - 8;
+    v = __fmul_rn((float)q, h2f(reinterpret_cast<const uint16_t*>(r1)[b]));
+  } else if (type == B2_Q8_0) {
+    const int b = (int)(cc / 32);
+    v = __fmul_rn((float)reinterpret_cast<const int8_t*>(r0)[cc], h2f(reinterpret_cast<const uint16_t*>(r1)[b]));
+  } else if (type == B2_Q4_K) {
+    const int sb = (int)(cc / 256), e = (int)(cc % 256);
+    const uint8_t* bp = r0 + sb * 144;
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(bp));
+    const float dmin = h2f(*reinterpret_cast<const uint16_t*>(bp + 2));
+    const uint8_t* sc = bp + 4;
+    const int j = e >> 5;
+    int s, m;
+    if (j < 4) {
+      s = sc[j] & 63;
+      m = sc[j + 4] & 63;
+    } else {
+      s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
+      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    const uint8_t byte = bp[16 + (e >> 6) * 32 + (e & 31)];
+    const int q = (j & 1) ? (byte >> 4) : (byte & 15);
+    v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s), (float)q), __fmul_rn(dmin, (float)m));
+  } else if (type == B2_Q6_K) {
+    const int sb = (int)(cc / 256), e = (int)(cc % 256);
+    const uint8_t* bp = r0 + sb * 208;
+    const int h = e >> 7, g = (e >> 5) & 3, l = e & 31;
+    const int lo = (bp[h * 64 + (g & 1) * 32 + l] >> (4 * (g >> 1))) & 15;
+    const int hi = (bp[128 + h * 32 + l] >> (2 * g)) & 3;
+    const int q = (lo | (hi << 4)) - 32;
+    const float d = h2f(reinterpret_cast<const uint16_t*>(r1)[sb]);
+    const float sc = (float)reinterpret_cast<const int8_t*>(bp + 192)[e >> 4];
+    v = __fmul_rn(__fmul_rn(d, sc), (float)q);
+  }
+  dst[i] = v;
+}
+
+int grid_for(int64_t n, int block) { return (int)std::min<int64_t>((n + block - 1) / block, 1 << 30); }
+
+}  // namespace
+
+int launch_quantize_act(int act_type, const float* x, int64_t x_stride, int n_tok, int64_t k, ActQ& out,
+                        cudaStream_t s) {
+  B2_CHECK_ARG(out.kp >= k && out.n_tok >= n_tok, "activation buffer too small");
+  const int block = 256;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(block);
+  cfg.stream = s;
+  if (act_type == B2_Q8_0) {
+    const int64_t warps = (int64_t)n_tok * (out.kp / 32);
+    cfg.gridDim = dim3(std::max(1, std::min(grid_for(warps * 32, block), 4 * kSMs)));
+    B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, quantize_q8_0_kernel, x, x_stride, n_tok, k, out.kp, out.qs, out.d));
+  } else if (act_type == B2_Q8_K) {
+    const int64_t warps = (int64_t)n_tok * (out.kp / 256);
+    cfg.gridDim = dim3(std::max(1, std::min(grid_for(warps * 32, block), 4 * kSMs)));
+    B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, quantize_q8_k_kernel, x, x_stride, n_tok, k, out.kp, out.qs, out.d,
+                                   out.bsum));
+  } else {
+    set_error("quantize_act: unsupported activation type %d", act_type);
+    return B2_ERR_UNSUPPORTED;
+  }
+  out.type = act_type;
+  return B2_OK;
+}
+
+int launch_act_to_blocks(const ActQ& a, int64_t k, void* blocks, cudaStream_t s) {
+  const int64_t nb = (int64_t)a.n_tok * (k / (a.type == B2_Q8_0 ? 32 : 256));
+  if (nb == 0) return B2_OK;
+  act_to_blocks_kernel<<<grid_for(nb, 128), 128, 0, s>>>(a.type, a.qs, a.d, a.bsum, a.n_tok, k, a.kp,
+                                                         static_cast<uint8_t*>(blocks));
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+int launch_block_dots(const QMatrix& w, const ActQ& a, int64_t row, int32_t* out_i, int32_t* out_m, cudaStream_t s) {
+  const int64_t nb = w.k / block_elems(w.type);
+  block_dots_kernel<<<grid_for(nb, 128), 128, 0, s>>>(w.type, w.plane0, w.plane1, w.p0_row, w.p0_chunk, w.p1_row,
+                                                      w.p1_chunk, w.kc, w.k, row, a.qs, a.bsum, out_i, out_m);
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+int launch_dequantize(const QMatrix& w, float* dst, cudaStream_t s) {
+  const int64_t n = w.n_rows * w.k;
+  if (n == 0) return B2_OK;
+  dequantize_kernel<<<grid_for(n, 256), 256, 0, s>>>(w.type, w.plane0, w.plane1, w.p0_row, w.p0_chunk, w.p1_row,
+                                                     w.p1_chunk, w.kc, w.n_rows, w.k, dst);
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+}  // namespace b2

@@ -1,0 +1,120 @@
+/*
+ * CPU ORACLE — test infrastructure only.
+ *
+ * A plain-C restatement of the reference's CPU arithmetic for the quantized
+ * decode path.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline / reference arm may load it, and only as the checker or the
+ * timed CPU baseline.  The product library never links or calls it.
+ *
+ * Sources restated (paths relative to the reference project root):
+ *   Singularity/tests/test_and_bench_a5.cpp:150-293   scalar reference ops
+ *   Singularity/src/core/cortex_a5_engine.cpp:429-659  GGUF parse
+ *   Singularity/src/core/cortex_a5_engine.cpp:997-1293 matmul + forward order
+ *   Milda/src/engine.cpp:1642-1675                     KV shift semantics
+ *   ggml (llama.cpp, version unpinned, not vendored)   Q8_K quantize, K-quant
+ *                                                      block layouts and dots
+ *
+ * Parity pins: the op-level functions are checked bit-for-bit against the
+ * reference's own scalar refs compiled from its sources (oracle/_ref), and the
+ * block layouts against gguf-py 0.19.0 (tests/golden).  The K-quant dot
+ * products and Q8_K activation quantizer have no in-tree reference; they
+ * restate ggml's published algorithm.
+ *
+ * Build with -ffp-contract=off: every fp32 multiply and add rounds on its own,
+ * as in the reference's scalar refs.
+ */
+#ifndef B2_ORACLE_H
+#define B2_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids (Singularity/src/core/cortex_a5_engine.hpp:31-36,
+ * Sutra/src/llm_backends.cpp:3396-3401). */
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14, ORC_Q8_K = 15 };
+
+/* Block sizes in bytes. */
+enum { ORC_Q4_0_BYTES = 18, ORC_Q8_0_BYTES = 34, ORC_Q4_K_BYTES = 144, ORC_Q6_K_BYTES = 210, ORC_Q8_K_BYTES = 292 };
+
+float    orc_fp16_to_fp32(uint16_t h);
+uint16_t orc_fp32_to_fp16(float f);
+void     orc_fp32_to_fp16_row(const float* x, uint16_t* y, int64_t n);
+void     orc_fp16_to_fp32_row(const uint16_t* x, float* y, int64_t n);
+
+/* Activation quantizers. */
+void orc_quantize_row_q8_0(const float* x, void* y, int k);   /* Singularity formula */
+void orc_quantize_row_q8_k(const float* x, void* y, int k);   /* ggml formula        */
+
+/* Block dot products: weights x (left) · activation y (right). */
+float orc_vec_dot_q4_0_q8_0(int n, const void* x, const void* y);
+float orc_vec_dot_q8_0_q8_0(int n, const void* x, const void* y);
+float orc_vec_dot_q4_k_q8_k(int n, const void* x, const void* y);
+float orc_vec_dot_q6_k_q8_k(int n, const void* x, const void* y);
+/* Exact integer block sums (one int32 per 32-weight block for Q4_0/Q8_0; per
+ * 256-weight super-block the scaled sum Σ sc_j·dot_j for Q4_K/Q6_K, and the
+ * min term Σ m_j·bsum_j for Q4_K in mins[]). */
+void orc_block_dots_q4_0_q8_0(int n, const void* x, const void* y, int32_t* sumi);
+void orc_block_dots_q8_0_q8_0(int n, const void* x, const void* y, int32_t* sumi);
+void orc_block_dots_q4_k_q8_k(int n, const void* x, const void* y, int32_t* isum, int32_t* msum);
+void orc_block_dots_q6_k_q8_k(int n, const void* x, const void* y, int32_t* isum);
+
+/* Weight dequantizers (one row of k weights). */
+void orc_dequantize_row(int type, const void* x, float* y, int k);
+
+/* Elementwise ops. */
+void orc_rmsnorm(const float* x, const float* w, float* out, int n, float eps);
+void orc_softmax(const float* x, float* out, int n);
+void orc_rope_pairs(float* x, const float* cos_sin, int head_dim, int n_heads);
+void orc_silu_mul(float* hb, const float* hb2, int n);
+
+/* RoPE cos/sin table: out[p*hd + 2i] = cos(p·θ^(−2i/hd)), [+1] = sin(...),
+ * p in [p0, p0+n_pos).  Angles in double, cos/sin in double, rounded once. */
+void orc_rope_table(float theta, int head_dim, int p0, int n_pos, float* out);
+
+/* Row-parallel quantized matmul: y[r] = dot(W row r, xq), rows split over
+ * n_threads POSIX threads.  xq is Q8_0 for Q4_0/Q8_0 weights and Q8_K for
+ * Q4_K/Q6_K weights.  row_bytes is the GGUF row size. */
+void orc_matmul(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int n_threads);
+
+/* Activation type the reference's CPU dot pairs with each weight type. */
+int orc_vec_dot_type(int wtype);
+size_t orc_row_bytes(int type, int k);
+
+/* Decode attention over an fp16 cache for one token.
+ * q: [n_heads*hd] fp32; kc/vc: fp16, element (t, kvh, i) at t*kv_stride + kvh*hd + i;
+ * positions t in [0, n_pos).  out: [n_heads*hd] fp32. */
+void orc_attn_decode(const float* q, const uint16_t* kc, const uint16_t* vc, int64_t kv_stride,
+                     int n_pos, int n_heads, int n_kv_heads, int hd, float* out);
+
+/* In-place K re-rotation for a KV shift by delta positions on n_pos cached
+ * rows (fp16 → fp32 → rotate by cos/sin(delta·θ_i) → RNE fp16). */
+void orc_kv_shift_k(uint16_t* kc, int64_t kv_stride, int n_pos, int n_kv_heads, int hd,
+                    int delta, float theta);
+
+/* ---- GGUF + Llama forward (Singularity forward_token order) ---- */
+typedef struct orc_model orc_model;
+orc_model* orc_model_open(const char* path);   /* mmap a GGUF file */
+orc_model* orc_model_from_memory(const void* data, size_t size);
+void       orc_model_free(orc_model* m);
+int        orc_model_info(const orc_model* m, int32_t* out, int n_out);
+/* Per-sequence fp16 KV cache of n_ctx positions. */
+int  orc_model_init_cache(orc_model* m, int n_seq, int n_ctx);
+/* Runs token `token` at position `pos` of sequence `seq`; writes logits
+ * (n_vocab) when logits != NULL.  Returns 0 on success. */
+int  orc_model_forward(orc_model* m, int seq, int32_t token, int pos, float* logits, int n_threads);
+/* As forward, but stops after n_layers_run layers (for bounded CPU timing). */
+int  orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, float* logits,
+                              int n_threads, int n_layers_run);
+/* KV shift on one sequence: drop [p0, p1), re-rotate K of [p1, n_past). */
+int  orc_model_kv_shift(orc_model* m, int seq, int p0, int p1, int n_past);
+/* Copy of the hidden state after the last forward (n_embd floats). */
+int  orc_model_hidden(const orc_model* m, float* out, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

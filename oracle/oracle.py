@@ -1,0 +1,285 @@
+"""ctypes wrapper over the CPU oracle (liboracle.so) and the reference's own
+scalar ops built from its sources (_ref/libsingularity_ref.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's cpu_baseline / reference arm, always as the checker or the timed
+CPU baseline, never as the product path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libsingularity_ref.so")
+
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, Q8_K = 0, 1, 2, 8, 12, 14, 15
+BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292),
+         F32: (1, 4), F16: (1, 2)}
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+
+
+def build() -> None:
+    """Compile liboracle.so (and the reference shim when its sources exist)."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        build()
+    lib = ctypes.CDLL(LIB_PATH)
+    sig = {
+        "orc_fp16_to_fp32": (_f, [ctypes.c_uint16]),
+        "orc_fp32_to_fp16": (ctypes.c_uint16, [_f]),
+        "orc_fp32_to_fp16_row": (None, [_vp, _vp, ctypes.c_int64]),
+        "orc_quantize_row_q8_0": (None, [_vp, _vp, _i]),
+        "orc_quantize_row_q8_k": (None, [_vp, _vp, _i]),
+        "orc_vec_dot_q4_0_q8_0": (_f, [_i, _vp, _vp]),
+        "orc_vec_dot_q8_0_q8_0": (_f, [_i, _vp, _vp]),
+        "orc_vec_dot_q4_k_q8_k": (_f, [_i, _vp, _vp]),
+        "orc_vec_dot_q6_k_q8_k": (_f, [_i, _vp, _vp]),
+        "orc_block_dots_q4_0_q8_0": (None, [_i, _vp, _vp, _vp]),
+        "orc_block_dots_q8_0_q8_0": (None, [_i, _vp, _vp, _vp]),
+        "orc_block_dots_q4_k_q8_k": (None, [_i, _vp, _vp, _vp, _vp]),
+        "orc_block_dots_q6_k_q8_k": (None, [_i, _vp, _vp, _vp]),
+        "orc_dequantize_row": (None, [_i, _vp, _vp, _i]),
+        "orc_rmsnorm": (None, [_vp, _vp, _vp, _i, _f]),
+        "orc_softmax": (None, [_vp, _vp, _i]),
+        "orc_rope_pairs": (None, [_vp, _vp, _i, _i]),
+        "orc_silu_mul": (None, [_vp, _vp, _i]),
+        "orc_rope_table": (None, [_f, _i, _i, _i, _vp]),
+        "orc_matmul": (None, [_i, _vp, ctypes.c_int64, _i, _vp, _vp, _i]),
+        "orc_attn_decode": (None, [_vp, _vp, _vp, ctypes.c_int64, _i, _i, _i, _i, _vp]),
+        "orc_kv_shift_k": (None, [_vp, ctypes.c_int64, _i, _i, _i, _i, _f]),
+        "orc_model_open": (_vp, [ctypes.c_char_p]),
+        "orc_model_from_memory": (_vp, [_vp, ctypes.c_size_t]),
+        "orc_model_free": (None, [_vp]),
+        "orc_model_info": (_i, [_vp, _vp, _i]),
+        "orc_model_init_cache": (_i, [_vp, _i, _i]),
+        "orc_model_forward": (_i, [_vp, _i, ctypes.c_int32, _i, _vp, _i]),
+        "orc_model_forward_layers": (_i, [_vp, _i, ctypes.c_int32, _i, _vp, _i, _i]),
+        "orc_model_kv_shift": (_i, [_vp, _i, _i, _i, _i]),
+        "orc_model_hidden": (_i, [_vp, _vp, _i]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def row_bytes(t: int, k: int) -> int:
+    bs, nb = BLOCK[t]
+    return k // bs * nb
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    """Rows of fp32 -> Q8_0 bytes with the reference's activation formula."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    out = np.zeros((rows.shape[0], row_bytes(Q8_0, rows.shape[1])), np.uint8)
+    for r in range(rows.shape[0]):
+        xr = np.ascontiguousarray(rows[r])
+        lib.orc_quantize_row_q8_0(_p(xr), _p(out[r]), rows.shape[1])
+    return out
+
+
+def quantize_q8_k(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    out = np.zeros((rows.shape[0], row_bytes(Q8_K, rows.shape[1])), np.uint8)
+    for r in range(rows.shape[0]):
+        xr = np.ascontiguousarray(rows[r])
+        lib.orc_quantize_row_q8_k(_p(xr), _p(out[r]), rows.shape[1])
+    return out
+
+
+def quantize_act(wtype: int, x: np.ndarray) -> np.ndarray:
+    return quantize_q8_k(x) if wtype in (Q4_K, Q6_K) else quantize_q8_0(x)
+
+
+def dequantize(t: int, w: np.ndarray, k: int) -> np.ndarray:
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1, row_bytes(t, k))
+    out = np.zeros((w.shape[0], k), np.float32)
+    for r in range(w.shape[0]):
+        lib.orc_dequantize_row(t, _p(w[r]), _p(out[r]), k)
+    return out
+
+
+def matmul(wtype: int, w: np.ndarray, n_rows: int, k: int, xq: np.ndarray, n_threads: int = 8) -> np.ndarray:
+    """y[r] = vec_dot(W row r, xq) for one activation row xq (bytes)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    xq = np.ascontiguousarray(xq, dtype=np.uint8)
+    y = np.zeros(n_rows, np.float32)
+    lib.orc_matmul(wtype, _p(w), n_rows, k, _p(xq), _p(y), n_threads)
+    return y
+
+
+def gemv(wtype: int, w: np.ndarray, n_rows: int, k: int, x: np.ndarray, n_threads: int = 8) -> np.ndarray:
+    """Full oracle GEMV: quantize each activation row, then matmul. x: [B, k]."""
+    x = np.atleast_2d(np.asarray(x, np.float32))
+    xq = quantize_act(wtype, x)
+    return np.stack([matmul(wtype, w, n_rows, k, xq[b], n_threads) for b in range(x.shape[0])])
+
+
+def block_dots(wtype: int, w_row: np.ndarray, xq: np.ndarray, k: int):
+    w_row = np.ascontiguousarray(w_row, np.uint8)
+    xq = np.ascontiguousarray(xq, np.uint8)
+    if wtype == Q4_0:
+        out = np.zeros(k // 32, np.int32)
+        lib.orc_block_dots_q4_0_q8_0(k, _p(w_row), _p(xq), _p(out))
+        return out
+    if wtype == Q8_0:
+        out = np.zeros(k // 32, np.int32)
+        lib.orc_block_dots_q8_0_q8_0(k, _p(w_row), _p(xq), _p(out))
+        return out
+    if wtype == Q4_K:
+        a = np.zeros(k // 256, np.int32)
+        b = np.zeros(k // 256, np.int32)
+        lib.orc_block_dots_q4_k_q8_k(k, _p(w_row), _p(xq), _p(a), _p(b))
+        return a, b
+    a = np.zeros(k // 256, np.int32)
+    lib.orc_block_dots_q6_k_q8_k(k, _p(w_row), _p(xq), _p(a))
+    return a
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.zeros_like(x)
+    lib.orc_rmsnorm(_p(x), _p(w), _p(out), x.size, eps)
+    return out
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros_like(x)
+    lib.orc_softmax(_p(x), _p(out), x.size)
+    return out
+
+
+def rope_pairs(x: np.ndarray, cos_sin: np.ndarray, head_dim: int, n_heads: int) -> np.ndarray:
+    x = np.array(x, np.float32, copy=True, order="C")
+    cs = np.ascontiguousarray(cos_sin, np.float32)
+    lib.orc_rope_pairs(_p(x), _p(cs), head_dim, n_heads)
+    return x
+
+
+def silu_mul(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    a = np.array(a, np.float32, copy=True, order="C")
+    b = np.ascontiguousarray(b, np.float32)
+    lib.orc_silu_mul(_p(a), _p(b), a.size)
+    return a
+
+
+def rope_table(theta: float, head_dim: int, p0: int, n_pos: int) -> np.ndarray:
+    out = np.zeros((n_pos, head_dim), np.float32)
+    lib.orc_rope_table(theta, head_dim, p0, n_pos, _p(out))
+    return out
+
+
+def fp32_to_fp16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(x.shape, np.uint16)
+    lib.orc_fp32_to_fp16_row(_p(x), _p(out), x.size)
+    return out
+
+
+def attn_decode(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, n_pos: int, n_heads: int, n_kv: int, hd: int) -> np.ndarray:
+    """q: [n_heads*hd] fp32; kc/vc: uint16 fp16 bits [n_pos, n_kv*hd]."""
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(kc, np.uint16)
+    vc = np.ascontiguousarray(vc, np.uint16)
+    out = np.zeros(n_heads * hd, np.float32)
+    lib.orc_attn_decode(_p(q), _p(kc), _p(vc), n_kv * hd, n_pos, n_heads, n_kv, hd, _p(out))
+    return out
+
+
+def kv_shift_k(kc: np.ndarray, n_pos: int, n_kv: int, hd: int, delta: int, theta: float) -> np.ndarray:
+    kc = np.array(kc, np.uint16, copy=True, order="C")
+    lib.orc_kv_shift_k(_p(kc), n_kv * hd, n_pos, n_kv, hd, delta, theta)
+    return kc
+
+
+class Model:
+    """Oracle Llama forward over a GGUF file or buffer."""
+
+    def __init__(self, path: str | None = None, buf: np.ndarray | None = None):
+        self._buf = buf
+        if path is not None:
+            self.h = lib.orc_model_open(path.encode())
+        else:
+            assert buf is not None
+            self.h = lib.orc_model_from_memory(_p(buf), buf.nbytes)
+        if not self.h:
+            raise RuntimeError("oracle: GGUF parse failed")
+        info = np.zeros(12, np.int32)
+        lib.orc_model_info(self.h, _p(info), 12)
+        (self.n_layers, self.dim, self.hidden, self.n_heads, self.n_kv, self.vocab,
+         self.head_dim, self.ctx_len, self.wtype, self.embd_type, self.out_type, _) = [int(v) for v in info]
+
+    def init_cache(self, n_seq: int, n_ctx: int) -> None:
+        if lib.orc_model_init_cache(self.h, n_seq, n_ctx) != 0:
+            raise MemoryError("oracle cache")
+
+    def forward(self, seq: int, token: int, pos: int, logits: bool = True, n_threads: int = 8,
+                n_layers: int | None = None):
+        out = np.zeros(self.vocab, np.float32) if logits else None
+        nl = self.n_layers if n_layers is None else n_layers
+        rc = lib.orc_model_forward_layers(self.h, seq, token, pos, _p(out) if logits else None, n_threads, nl)
+        if rc != 0:
+            raise RuntimeError(f"oracle forward rc={rc}")
+        return out
+
+    def hidden(self) -> np.ndarray:
+        out = np.zeros(self.dim, np.float32)
+        lib.orc_model_hidden(self.h, _p(out), self.dim)
+        return out
+
+    def kv_shift(self, seq: int, p0: int, p1: int, n_past: int) -> None:
+        if lib.orc_model_kv_shift(self.h, seq, p0, p1, n_past) != 0:
+            raise RuntimeError("oracle kv shift")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.orc_model_free(self.h)
+            self.h = None
+
+
+def load_reference() -> ctypes.CDLL | None:
+    """The reference's own scalar ops (built by build_ref.sh), or None."""
+    if not os.path.exists(REF_PATH):
+        return None
+    r = ctypes.CDLL(REF_PATH)
+    sig = {
+        "sref_fp16_to_fp32": (_f, [ctypes.c_uint16]),
+        "sref_fp32_to_fp16": (ctypes.c_uint16, [_f]),
+        "sref_vec_dot_q4_0_q8_0": (_f, [_i, _vp, _vp]),
+        "sref_vec_dot_q8_0_q8_0": (_f, [_i, _vp, _vp]),
+        "sref_quantize_row_q8_0": (None, [_vp, _vp, _i]),
+        "sref_rmsnorm_f32": (None, [_vp, _vp, _vp, _i, _f]),
+        "sref_softmax_f32": (None, [_vp, _vp, _i]),
+        "sref_rope_f32": (None, [_vp, _vp, _i, _i]),
+        "sref_xorshift_fill": (None, [ctypes.c_uint32, _vp, _i, _vp]),
+        "sref_rel_error": (_f, [_f, _f]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(r, name)
+        fn.restype = res
+        fn.argtypes = args
+    return r

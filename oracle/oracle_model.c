@@ -1,0 +1,343 @@
+/*
+ * CPU ORACLE — test infrastructure only (see oracle.h).
+ *
+ * GGUF v3 parse (Singularity/src/core/cortex_a5_engine.cpp:429-659) and the
+ * Llama decoder forward in Singularity's order
+ * (Singularity/src/core/cortex_a5_engine.cpp:1029-1293), with two documented
+ * departures: RoPE uses the θ^(−2i/hd) table for llama (adjacent pairs),
+ * and K-quant weights pair with Q8_K activations as in ggml's CPU backend.
+ */
+#include "oracle.h"
+
+#include <fcntl.h>
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+typedef struct {
+    int type;
+    const uint8_t* data;
+    int64_t ne[4];
+    int n_dims;
+} orc_tensor;
+
+typedef struct {
+    orc_tensor attn_norm, ffn_norm, wq, wk, wv, wo, w1, w2, w3;
+} orc_layer;
+
+struct orc_model {
+    const uint8_t* base;
+    size_t size;
+    int mapped;
+    uint8_t* owned;
+    int n_layers, dim, hidden, n_heads, n_kv, vocab, ctx_len, head_dim;
+    float eps, theta;
+    orc_tensor embd, out_norm, out;
+    orc_layer* layers;
+    /* runtime */
+    int n_seq, n_ctx;
+    uint16_t *kc, *vc; /* [seq][layer][pos][kv_dim] */
+    float *x, *xb, *xb2, *q, *k, *v, *hb, *hb2;
+    void* xq;
+    float* rope;
+};
+
+static uint32_t rd_u32(const uint8_t* p) { uint32_t v; memcpy(&v, p, 4); return v; }
+static uint64_t rd_u64(const uint8_t* p) { uint64_t v; memcpy(&v, p, 8); return v; }
+
+static int key_eq(const char* k, size_t n, const char* s) { return strlen(s) == n && memcmp(k, s, n) == 0; }
+static int key_ends(const char* k, size_t n, const char* s) {
+    const size_t m = strlen(s);
+    return n >= m && memcmp(k + n - m, s, m) == 0;
+}
+
+/* Byte size of one scalar GGUF value type; 0 for string / array. */
+static size_t gguf_scalar_size(uint32_t t) {
+    switch (t) {
+    case 0: case 1: case 7: return 1;
+    case 2: case 3: return 2;
+    case 4: case 5: case 6: return 4;
+    case 10: case 11: case 12: return 8;
+    default: return 0;
+    }
+}
+
+/* Skip one value (Milda/src/engine.cpp:89-146 skip_gguf_value, restated). */
+static const uint8_t* gguf_skip(const uint8_t* p, const uint8_t* end, uint32_t t) {
+    if (t == 8) {
+        if (p + 8 > end) return end;
+        return p + 8 + rd_u64(p);
+    }
+    if (t == 9) {
+        if (p + 12 > end) return end;
+        const uint32_t et = rd_u32(p);
+        const uint64_t n = rd_u64(p + 4);
+        p += 12;
+        const size_t es = gguf_scalar_size(et);
+        if (es) return p + es * n;
+        for (uint64_t i = 0; i < n && p < end; ++i) p = gguf_skip(p, end, et);
+        return p;
+    }
+    return p + gguf_scalar_size(t);
+}
+
+static size_t tensor_bytes(const orc_tensor* t) {
+    int64_t rows = 1;
+    for (int i = 1; i < t->n_dims; ++i) rows *= t->ne[i];
+    return orc_row_bytes(t->type, (int)t->ne[0]) * (size_t)rows;
+}
+
+static int parse(orc_model* m) {
+    const uint8_t* p = m->base;
+    const uint8_t* end = m->base + m->size;
+    if (m->size < 24 || rd_u32(p) != 0x46554747u) return -1;
+    const uint32_t version = rd_u32(p + 4);
+    if (version != 2 && version != 3) return -1;
+    const uint64_t n_tensors = rd_u64(p + 8), n_kv = rd_u64(p + 16);
+    p += 24;
+    size_t alignment = 32;
+    m->eps = 1e-5f;
+    m->theta = 10000.0f;
+    for (uint64_t i = 0; i < n_kv; ++i) {
+        if (p + 12 > end) return -1;
+        const uint64_t klen = rd_u64(p);
+        const char* key = (const char*)(p + 8);
+        p += 8 + klen;
+        const uint32_t vt = rd_u32(p);
+        p += 4;
+        if (vt == 4 || vt == 5) {
+            const uint32_t v = rd_u32(p);
+            if (key_eq(key, klen, "general.alignment")) alignment = v;
+            else if (key_ends(key, klen, ".block_count")) m->n_layers = (int)v;
+            else if (key_ends(key, klen, ".embedding_length")) m->dim = (int)v;
+            else if (key_ends(key, klen, ".feed_forward_length")) m->hidden = (int)v;
+            else if (key_ends(key, klen, ".attention.head_count")) m->n_heads = (int)v;
+            else if (key_ends(key, klen, ".attention.head_count_kv")) m->n_kv = (int)v;
+            else if (key_ends(key, klen, ".context_length")) m->ctx_len = (int)v;
+            else if (key_ends(key, klen, ".vocab_size")) m->vocab = (int)v;
+        } else if (vt == 6) {
+            float f;
+            memcpy(&f, p, 4);
+            if (key_ends(key, klen, ".layer_norm_rms_epsilon")) m->eps = f;
+            else if (key_ends(key, klen, ".rope.freq_base")) m->theta = f;
+        }
+        p = gguf_skip(p, end, vt);
+        if (p > end) return -1;
+    }
+    if (m->n_layers <= 0 || m->dim <= 0 || (m->dim & 31) || m->n_heads <= 0) return -1;
+    if (m->n_kv <= 0) m->n_kv = m->n_heads;
+    m->layers = (orc_layer*)calloc((size_t)m->n_layers, sizeof(orc_layer));
+    orc_tensor* tab = (orc_tensor*)calloc(n_tensors ? n_tensors : 1, sizeof(orc_tensor));
+    char** names = (char**)calloc(n_tensors ? n_tensors : 1, sizeof(char*));
+    size_t* offs = (size_t*)calloc(n_tensors ? n_tensors : 1, sizeof(size_t));
+    for (uint64_t i = 0; i < n_tensors; ++i) {
+        if (p + 8 > end) return -1;
+        const uint64_t nlen = rd_u64(p);
+        names[i] = (char*)calloc(nlen + 1, 1);
+        memcpy(names[i], p + 8, nlen);
+        p += 8 + nlen;
+        const uint32_t nd = rd_u32(p);
+        p += 4;
+        tab[i].n_dims = (int)nd;
+        for (uint32_t d = 0; d < 4; ++d) tab[i].ne[d] = 1;
+        for (uint32_t d = 0; d < nd; ++d) {
+            if (d < 4) tab[i].ne[d] = (int64_t)rd_u64(p);
+            p += 8;
+        }
+        tab[i].type = (int)rd_u32(p);
+        offs[i] = (size_t)rd_u64(p + 4);
+        p += 12;
+    }
+    const size_t hdr = (size_t)(p - m->base);
+    const size_t data_off = (hdr + alignment - 1) / alignment * alignment;
+    for (uint64_t i = 0; i < n_tensors; ++i) {
+        orc_tensor t = tab[i];
+        t.data = m->base + data_off + offs[i];
+        if (t.data + tensor_bytes(&t) > end) return -1;
+        const char* n = names[i];
+        if (!strcmp(n, "token_embd.weight")) m->embd = t;
+        else if (!strcmp(n, "output_norm.weight")) m->out_norm = t;
+        else if (!strcmp(n, "output.weight")) m->out = t;
+        else if (!strncmp(n, "blk.", 4)) {
+            char* e;
+            const long l = strtol(n + 4, &e, 10);
+            if (l >= 0 && l < m->n_layers && *e == '.') {
+                orc_layer* L = &m->layers[l];
+                const char* s = e + 1;
+                if (!strcmp(s, "attn_norm.weight")) L->attn_norm = t;
+                else if (!strcmp(s, "ffn_norm.weight")) L->ffn_norm = t;
+                else if (!strcmp(s, "attn_q.weight")) L->wq = t;
+                else if (!strcmp(s, "attn_k.weight")) L->wk = t;
+                else if (!strcmp(s, "attn_v.weight")) L->wv = t;
+                else if (!strcmp(s, "attn_output.weight")) L->wo = t;
+                else if (!strcmp(s, "ffn_gate.weight")) L->w1 = t;
+                else if (!strcmp(s, "ffn_down.weight")) L->w2 = t;
+                else if (!strcmp(s, "ffn_up.weight")) L->w3 = t;
+            }
+        }
+        free(names[i]);
+    }
+    free(names);
+    free(offs);
+    free(tab);
+    if (!m->embd.data || !m->out_norm.data) return -1;
+    if (!m->out.data) m->out = m->embd; /* tied head, Singularity :650-654 */
+    if (m->vocab <= 0) m->vocab = (int)m->out.ne[1];
+    if (m->hidden <= 0 && m->layers[0].w1.data) m->hidden = (int)m->layers[0].w1.ne[1];
+    m->head_dim = m->dim / m->n_heads;
+    for (int l = 0; l < m->n_layers; ++l) {
+        const orc_layer* L = &m->layers[l];
+        if (!L->attn_norm.data || !L->ffn_norm.data || !L->wq.data || !L->wk.data || !L->wv.data ||
+            !L->wo.data || !L->w1.data || !L->w2.data || !L->w3.data)
+            return -1;
+    }
+    return 0;
+}
+
+orc_model* orc_model_from_memory(const void* data, size_t size) {
+    orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
+    m->base = (const uint8_t*)data;
+    m->size = size;
+    if (parse(m) != 0) {
+        orc_model_free(m);
+        return NULL;
+    }
+    return m;
+}
+
+orc_model* orc_model_open(const char* path) {
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return NULL;
+    struct stat st;
+    if (fstat(fd, &st) != 0) { close(fd); return NULL; }
+    void* p = mmap(NULL, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) return NULL;
+    orc_model* m = orc_model_from_memory(p, (size_t)st.st_size);
+    if (!m) { munmap(p, (size_t)st.st_size); return NULL; }
+    m->mapped = 1;
+    return m;
+}
+
+void orc_model_free(orc_model* m) {
+    if (!m) return;
+    if (m->mapped) munmap((void*)m->base, m->size);
+    free(m->layers);
+    free(m->kc); free(m->vc);
+    free(m->x); free(m->xb); free(m->xb2); free(m->q); free(m->k); free(m->v);
+    free(m->hb); free(m->hb2); free(m->xq); free(m->rope);
+    free(m);
+}
+
+int orc_model_info(const orc_model* m, int32_t* out, int n) {
+    const int32_t v[12] = {m->n_layers, m->dim, m->hidden, m->n_heads, m->n_kv, m->vocab,
+                           m->head_dim, m->ctx_len, m->layers[0].wq.type, m->embd.type, m->out.type,
+                           (int32_t)0};
+    for (int i = 0; i < n && i < 12; ++i) out[i] = v[i];
+    return 12;
+}
+
+int orc_model_init_cache(orc_model* m, int n_seq, int n_ctx) {
+    const int kv_dim = m->head_dim * m->n_kv;
+    free(m->kc); free(m->vc); free(m->rope);
+    m->n_seq = n_seq;
+    m->n_ctx = n_ctx;
+    const size_t n = (size_t)n_seq * m->n_layers * n_ctx * kv_dim;
+    m->kc = (uint16_t*)calloc(n, 2);
+    m->vc = (uint16_t*)calloc(n, 2);
+    m->rope = (float*)malloc(sizeof(float) * (size_t)n_ctx * m->head_dim);
+    orc_rope_table(m->theta, m->head_dim, 0, n_ctx, m->rope);
+    const int big = m->dim > m->hidden ? m->dim : m->hidden;
+    if (!m->x) {
+        m->x = (float*)calloc((size_t)m->dim, 4);
+        m->xb = (float*)calloc((size_t)big, 4);
+        m->xb2 = (float*)calloc((size_t)big, 4);
+        m->q = (float*)calloc((size_t)m->dim, 4);
+        m->k = (float*)calloc((size_t)kv_dim, 4);
+        m->v = (float*)calloc((size_t)kv_dim, 4);
+        m->hb = (float*)calloc((size_t)m->hidden, 4);
+        m->hb2 = (float*)calloc((size_t)m->hidden, 4);
+        m->xq = calloc((size_t)big / 32 + 8, ORC_Q8_K_BYTES);
+    }
+    return (m->kc && m->vc) ? 0 : -1;
+}
+
+/* matmul_quantized with the activation quantized for the weight's dot type
+ * (Singularity quantizes to Q8_0 before every projection, :1127, :1257,
+ * :1269, :1275, :1290; K-quant weights take Q8_K as in ggml). */
+static void proj(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) {
+    const int k = (int)w->ne[0];
+    if (orc_vec_dot_type(w->type) == ORC_Q8_K) orc_quantize_row_q8_k(x, m->xq, k);
+    else orc_quantize_row_q8_0(x, m->xq, k);
+    orc_matmul(w->type, w->data, w->ne[1], k, m->xq, y, nt);
+}
+
+int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, float* logits, int nt,
+                             int n_layers_run) {
+    if (!m->kc || seq < 0 || seq >= m->n_seq || pos < 0 || pos >= m->n_ctx) return -1;
+    if (token < 0 || token >= (int32_t)m->embd.ne[1]) token = 0;
+    const int dim = m->dim, hd = m->head_dim, nkv = m->n_kv, kv_dim = hd * nkv;
+    /* 1. embedding row (:1066-1105) */
+    orc_dequantize_row(m->embd.type, m->embd.data + orc_row_bytes(m->embd.type, dim) * (size_t)token,
+                       m->x, dim);
+    const float* cs = m->rope + (size_t)pos * hd;
+    const size_t seq_stride = (size_t)m->n_layers * m->n_ctx * kv_dim;
+    const int nl = n_layers_run < m->n_layers ? n_layers_run : m->n_layers;
+    for (int l = 0; l < nl; ++l) {
+        const orc_layer* L = &m->layers[l];
+        orc_rmsnorm(m->x, (const float*)L->attn_norm.data, m->xb, dim, m->eps);      /* :1121 */
+        proj(m, &L->wq, m->xb, m->q, nt);                                             /* :1129 */
+        proj(m, &L->wk, m->xb, m->k, nt);
+        proj(m, &L->wv, m->xb, m->v, nt);
+        orc_rope_pairs(m->q, cs, hd, m->n_heads);                                     /* :1187 */
+        orc_rope_pairs(m->k, cs, hd, nkv);
+        uint16_t* kc = m->kc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
+        uint16_t* vc = m->vc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
+        orc_fp32_to_fp16_row(m->k, kc + (size_t)pos * kv_dim, kv_dim);                /* :1195 */
+        orc_fp32_to_fp16_row(m->v, vc + (size_t)pos * kv_dim, kv_dim);
+        orc_attn_decode(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);   /* :1205 */
+        proj(m, &L->wo, m->xb, m->xb2, nt);                                           /* :1256 */
+        for (int i = 0; i < dim; ++i) m->x[i] += m->xb2[i];
+        orc_rmsnorm(m->x, (const float*)L->ffn_norm.data, m->xb, dim, m->eps);        /* :1264 */
+        proj(m, &L->w1, m->xb, m->hb, nt);                                            /* :1270 */
+        proj(m, &L->w3, m->xb, m->hb2, nt);
+        orc_silu_mul(m->hb, m->hb2, m->hidden);                                       /* :1277 */
+        proj(m, &L->w2, m->hb, m->xb, nt);                                            /* :1280 */
+        for (int i = 0; i < dim; ++i) m->x[i] += m->xb[i];
+    }
+    if (!logits) return 0;
+    orc_rmsnorm(m->x, (const float*)m->out_norm.data, m->xb, dim, m->eps);            /* :1287 */
+    proj(m, &m->out, m->xb, logits, nt);                                              /* :1292 */
+    return 0;
+}
+
+int orc_model_forward(orc_model* m, int seq, int32_t token, int pos, float* logits, int nt) {
+    return orc_model_forward_layers(m, seq, token, pos, logits, nt, m->n_layers);
+}
+
+int orc_model_hidden(const orc_model* m, float* out, int n) {
+    for (int i = 0; i < n && i < m->dim; ++i) out[i] = m->x[i];
+    return m->dim;
+}
+
+/* Milda shift_kv_cache_in_place (Milda/src/engine.cpp:1642-1675) on one
+ * sequence: drop positions [p0, p1), move [p1, n_past) down to p0 and
+ * re-rotate those K rows by −(p1−p0). */
+int orc_model_kv_shift(orc_model* m, int seq, int p0, int p1, int n_past) {
+    if (!m->kc || p0 < 0 || p1 < p0 || n_past < p1 || n_past > m->n_ctx) return -1;
+    const int kv_dim = m->head_dim * m->n_kv;
+    const size_t seq_stride = (size_t)m->n_layers * m->n_ctx * kv_dim;
+    const int n_move = n_past - p1;
+    for (int l = 0; l < m->n_layers; ++l) {
+        uint16_t* kc = m->kc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
+        uint16_t* vc = m->vc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
+        memmove(kc + (size_t)p0 * kv_dim, kc + (size_t)p1 * kv_dim, (size_t)n_move * kv_dim * 2);
+        memmove(vc + (size_t)p0 * kv_dim, vc + (size_t)p1 * kv_dim, (size_t)n_move * kv_dim * 2);
+        orc_kv_shift_k(kc + (size_t)p0 * kv_dim, kv_dim, n_move, m->n_kv, m->head_dim, -(p1 - p0), m->theta);
+    }
+    return 0;
+}

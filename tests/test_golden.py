@@ -1,0 +1,90 @@
+"""Golden-vector pins (CPU): the oracle and the library's host-side weight
+quantizers against fixtures from gguf-py 0.19.0 and from the reference's own
+scalar ops (tests/golden/make_golden.py)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _load(name):
+    return np.load(os.path.join(GOLD, name))
+
+
+def _bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+def test_oracle_dequant_matches_gguf_py_all_types():
+    w = _load("weight_quant_gguf.npz")
+    k = w["x"].shape[1]
+    for t, key in ((O.Q4_0, "q4_0"), (O.Q8_0, "q8_0")):
+        got = O.dequantize(t, w[key], k)
+        assert np.array_equal(_bits(got), _bits(w[key + "_deq"])), key
+    kq = _load("kquant_gguf.npz")
+    for t, key in ((O.Q4_K, "q4_k"), (O.Q6_K, "q6_k")):
+        k = kq[key + "_deq"].shape[1]
+        got = O.dequantize(t, kq[key], k)
+        assert np.array_equal(_bits(got), _bits(kq[key + "_deq"])), key
+
+
+def test_oracle_matches_reference_scalar_fixture():
+    g = {key: v for key, v in _load("singularity_ref_ops.npz").items()}
+    x, k = g["x"], g["x"].shape[1]
+    q8, q4 = g["q8_0"], g["q4_0"]
+    assert np.array_equal(O.quantize_q8_0(x), q8)
+    n = x.shape[0]
+    for r in range(n):
+        a = O.lib.orc_vec_dot_q4_0_q8_0(k, q4[r].ctypes.data, q8[(r + 1) % n].ctypes.data)
+        assert _bits(a) == _bits(g["dot_q4_0_q8_0"][r])
+        b = O.lib.orc_vec_dot_q8_0_q8_0(k, q8[r].ctypes.data, q8[(r + 1) % n].ctypes.data)
+        assert _bits(b) == _bits(g["dot_q8_0_q8_0"][r])
+        assert np.array_equal(_bits(O.rmsnorm(x[r], g["norm_w"], 1e-5)), _bits(g["rmsnorm"][r]))
+        assert np.array_equal(_bits(O.softmax(x[r])), _bits(g["softmax"][r]))
+
+
+def test_library_weight_quantizer_matches_gguf_py():
+    b2 = pytest.importorskip("b2gguf")
+    w = _load("weight_quant_gguf.npz")
+    x = w["x"]
+    assert np.array_equal(b2.quantize_weights(b2.Q4_0, x), w["q4_0"])
+    assert np.array_equal(b2.quantize_weights(b2.Q8_0, x), w["q8_0"])
+
+
+@pytest.mark.parametrize("qt", ["Q4_K", "Q6_K"])
+def test_library_kquant_quantizer_round_trip(qt):
+    b2 = pytest.importorskip("b2gguf")
+    t = getattr(b2, qt)
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((16, 1024)) * 0.02).astype(np.float32)
+    q = b2.quantize_weights(t, x)
+    deq = O.dequantize(t, q, 1024)
+    err = np.sqrt(np.mean((deq - x) ** 2)) / np.sqrt(np.mean(x ** 2))
+    # 4-bit affine (Q4_K) and 6-bit symmetric (Q6_K) encodings of N(0, 0.02)
+    assert err < (0.12 if qt == "Q4_K" else 0.04), err
+    # edge rows: zeros stay zero, constants stay close
+    z = np.zeros((2, 256), np.float32)
+    z[1] = 0.25
+    dz = O.dequantize(t, b2.quantize_weights(t, z), 256)
+    assert np.all(dz[0] == 0.0)
+    assert np.max(np.abs(dz[1] - 0.25)) < 0.02
+
+
+def test_oracle_q8_k_properties():
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((4, 512)).astype(np.float32)
+    x[1] = 0.0
+    x[2, :256] = np.tile([2.0, -2.0], 128)   # |max| tie: first element wins
+    qb = O.quantize_q8_k(x).reshape(4, 2, 292)
+    d = qb[..., 0:4].copy().view(np.float32)[..., 0]
+    qs = qb[..., 4:260].copy().view(np.int8)
+    bs = qb[..., 260:292].copy().view(np.int16)
+    assert np.all(qb[1] == 0)
+    assert np.array_equal(bs, qs.reshape(4, 2, 16, 16).astype(np.int32).sum(-1))
+    assert qs[2, 0, 0] == -127 and d[2, 0] < 0   # first max is +2 -> iscale = -127/2
+    deq = qs.astype(np.float32) * d[..., None]
+    assert np.max(np.abs(deq.reshape(4, 512)[0] - x[0])) <= np.max(np.abs(x[0])) / 127 * 0.51 + 1e-6

@@ -1,0 +1,48 @@
+"""Host-side checks (no GPU): the library loads and exports every declared
+entry point, and its host helpers agree with the oracle."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+b2 = pytest.importorskip("b2gguf")
+
+
+def test_library_exports_every_header_symbol():
+    names = b2.header_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(b2.lib, n)]
+    assert not missing, missing
+    assert b2.lib.b2_abi_version() == 1
+
+
+def test_row_bytes():
+    assert b2.row_bytes(b2.Q4_0, 4096) == 128 * 18
+    assert b2.row_bytes(b2.Q8_0, 4096) == 128 * 34
+    assert b2.row_bytes(b2.Q4_K, 4096) == 16 * 144
+    assert b2.row_bytes(b2.Q6_K, 4096) == 16 * 210
+    assert b2.row_bytes(b2.Q8_K, 4096) == 16 * 292
+
+
+@pytest.mark.parametrize("theta,hd,p0,n", [(10000.0, 64, 0, 300), (500000.0, 128, 0, 64), (10000.0, 128, -1024, 3)])
+def test_rope_table_matches_oracle(theta, hd, p0, n):
+    a = b2.rope_table(theta, hd, p0, n)
+    b = O.rope_table(theta, hd, p0, n)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_synth_normal_is_seeded_sliceable_and_normal():
+    a = b2.synth_normal(7, 200000, std=0.02)
+    b = b2.synth_normal(7, 200000, std=0.02)
+    assert np.array_equal(a, b)
+    c = b2.synth_normal(7, 1000, std=0.02, offset=12345)
+    assert np.array_equal(c, a[12345:13345])
+    assert abs(a.mean()) < 2e-4 and abs(a.std() - 0.02) < 2e-4
+    assert not np.array_equal(a[:1000], b2.synth_normal(8, 1000, std=0.02))
+
+
+def test_error_reporting_on_bad_arguments():
+    with pytest.raises(b2.B2Error):
+        b2.quantize_weights(b2.Q4_0, np.zeros((2, 33), np.float32))
+    with pytest.raises(b2.B2Error):
+        b2.quantize_weights(99, np.zeros((2, 32), np.float32))
