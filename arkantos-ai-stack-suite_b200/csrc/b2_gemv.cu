@@ -57,38 +57,80 @@ template <int WT, int B>
 __device__ void load_act(const GemvP& p, int8_t* aq, float* ad, int16_t* ab, int warp, int lane) {
   const int64_t kp = p.kp;
   if (p.x != nullptr) {
+    // Issue every load of a batch of blocks before quantizing any of them, so
+    // a warp waits for one memory round trip per batch, not one per block.
     if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
+      constexpr int U = 16;
       const int64_t nbk = kp / 32;
-      for (int64_t i = warp; i < (int64_t)B * nbk; i += kNCW) {
-        const int t = (int)(i / nbk);
-        const int64_t kb = i - (int64_t)t * nbk;
-        const int64_t e = kb * 32 + lane;
-        const float xv = e < p.k ? p.x[t * p.x_stride + e] : 0.0f;
-        uint16_t d16;
-        const int8_t q = quant_q8_0_lane(xv, &d16);
-        aq[t * kp + e] = q;
-        if (lane == 0) ad[t * nbk + kb] = h2f(d16);
+      const int64_t total = (int64_t)B * nbk;
+      for (int64_t i0 = warp; i0 < total; i0 += (int64_t)kNCW * U) {
+        float xv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + (int64_t)u * kNCW;
+          float v = 0.0f;
+          if (i < total) {
+            const int t = (int)(i / nbk);
+            const int64_t e = (i - (int64_t)t * nbk) * 32 + lane;
+            if (e < p.k) v = __ldg(p.x + t * p.x_stride + e);
+          }
+          xv[u] = v;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + (int64_t)u * kNCW;
+          if (i < total) {
+            const int t = (int)(i / nbk);
+            const int64_t kb = i - (int64_t)t * nbk;
+            uint16_t d16;
+            const int8_t q = quant_q8_0_lane(xv[u], &d16);
+            aq[t * kp + kb * 32 + lane] = q;
+            if (lane == 0) ad[t * nbk + kb] = h2f(d16);
+          }
+        }
       }
     } else {
+      constexpr int U = 4;
       const int64_t nbk = kp / 256;
-      for (int64_t i = warp; i < (int64_t)B * nbk; i += kNCW) {
-        const int t = (int)(i / nbk);
-        const int64_t kb = i - (int64_t)t * nbk;
-        float v[8];
-        const int64_t e0 = kb * 256 + lane * 8;
+      const int64_t total = (int64_t)B * nbk;
+      for (int64_t i0 = warp; i0 < total; i0 += (int64_t)kNCW * U) {
+        float v[U][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (e0 + j) < p.k ? p.x[t * p.x_stride + e0 + j] : 0.0f;
-        int8_t q[8];
-        int bs;
-        const float d = quant_q8_k_lane(v, q, &bs);
-        uint2 packed;
-        packed.x = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) | ((uint32_t)(uint8_t)q[2] << 16) |
-                   ((uint32_t)(uint8_t)q[3] << 24);
-        packed.y = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
-                   ((uint32_t)(uint8_t)q[7] << 24);
-        *reinterpret_cast<uint2*>(aq + t * kp + e0) = packed;
-        if ((lane & 1) == 0) ab[t * (kp / 16) + kb * 16 + lane / 2] = (int16_t)bs;
-        if (lane == 0) ad[t * nbk + kb] = d;
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + (int64_t)u * kNCW;
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+          if (i < total) {
+            const int t = (int)(i / nbk);
+            const int64_t e0 = (i - (int64_t)t * nbk) * 256 + lane * 8;
+            if (e0 < p.k) {   // k is a multiple of 256: all 8 values are in range
+              const float4* src = reinterpret_cast<const float4*>(p.x + t * p.x_stride + e0);
+              a = __ldg(src);
+              c = __ldg(src + 1);
+            }
+          }
+          v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+          v[u][4] = c.x; v[u][5] = c.y; v[u][6] = c.z; v[u][7] = c.w;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + (int64_t)u * kNCW;
+          if (i < total) {
+            const int t = (int)(i / nbk);
+            const int64_t kb = i - (int64_t)t * nbk;
+            const int64_t e0 = kb * 256 + lane * 8;
+            int8_t q[8];
+            int bs;
+            const float d = quant_q8_k_lane(v[u], q, &bs);
+            uint2 packed;
+            packed.x = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) | ((uint32_t)(uint8_t)q[2] << 16) |
+                       ((uint32_t)(uint8_t)q[3] << 24);
+            packed.y = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
+                       ((uint32_t)(uint8_t)q[7] << 24);
+            *reinterpret_cast<uint2*>(aq + t * kp + e0) = packed;
+            if ((lane & 1) == 0) ab[t * (kp / 16) + kb * 16 + lane / 2] = (int16_t)bs;
+            if (lane == 0) ad[t * nbk + kb] = d;
+          }
+        }
       }
     }
   } else {
@@ -300,7 +342,7 @@ __device__ __forceinline__ void compute_stage(const GemvP& p, const uint8_t* sp0
 }
 
 template <int WT, int B>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvP p) {
+__global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const GemvP p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;

@@ -1,0 +1,39 @@
+// Launchers for the decoder-layer kernels (b2_layers.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b2 {
+
+// Per-sequence KV bookkeeping, read by kernels from device memory.  Logical
+// position p lives in physical slot p when p < n_keep (the pinned prefix),
+// otherwise in n_keep + (ring_head + p − n_keep) mod (cap − n_keep): the
+// slots after the prefix form a ring, so dropping the oldest positions
+// after the prefix (Milda's KV shift) only advances ring_head.
+struct KvSeqState {
+  int32_t n_keep;
+  int32_t ring_head;
+};
+
+int launch_embed(const int32_t* tokens, int n_tok, int n_vocab, int type, const uint8_t* table, int64_t row_bytes,
+                 int n_embd, float* x, cudaStream_t s);
+int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
+                       cudaStream_t s);
+int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
+                   const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int cap,
+                   cudaStream_t s);
+// Split-K attention: positions are cut into chunks of P, one CTA per (chunk,
+// kv head, query); part_o [n_tok][n_head][n_split][hd], part_ml
+// [n_tok][n_head][n_split][2] hold the partial results (scratch).
+int attn_splits(int cap, int P);
+int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
+                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int cap, int P, float* part_o,
+                     float* part_ml, float* out, cudaStream_t s);
+int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
+                    const float* cs, cudaStream_t s);
+int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int dst0,
+                      int src0, int n, const float* cs, cudaStream_t s);
+int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s);
+
+}  // namespace b2

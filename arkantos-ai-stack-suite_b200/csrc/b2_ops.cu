@@ -57,31 +57,38 @@ __global__ void quantize_q8_k_kernel(const float* __restrict__ x, int64_t x_stri
 }
 
 // Planar activations -> GGUF blocks (Q8_0: fp16 d + 32 int8; Q8_K: fp32 d,
-// 256 int8, 16 int16 sums).  One thread per block.
+// 256 int8, 16 int16 sums).  One thread per output byte.
 __global__ void act_to_blocks_kernel(int type, const int8_t* qs, const float* d, const int16_t* bsum, int n_tok,
                                      int64_t k, int64_t kp, uint8_t* out) {
   const int64_t bs = type == B2_Q8_0 ? 32 : 256;
+  const int64_t bb = type == B2_Q8_0 ? 34 : 292;
   const int64_t nb = k / bs;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)n_tok * nb) return;
-  const int t = (int)(i / nb);
-  const int64_t b = i - (int64_t)t * nb;
+  if (i >= (int64_t)n_tok * nb * bb) return;
+  const int64_t blk = i / bb;
+  const int j = (int)(i - blk * bb);
+  const int t = (int)(blk / nb);
+  const int64_t b = blk - (int64_t)t * nb;
+  uint32_t v;
   if (type == B2_Q8_0) {
-    uint8_t* o = out + (t * nb + b) * 34;
-    const uint16_t h = f2h_rn(d[t * (kp / 32) + b]);
-    o[0] = h & 0xFF;
-    o[1] = h >> 8;
-    for (int j = 0; j < 32; ++j) o[2 + j] = (uint8_t)qs[t * kp + b * 32 + j];
+    if (j < 2) {
+      const uint32_t h = f2h_rn(d[t * (kp / 32) + b]);
+      v = (h >> (8 * j)) & 0xFFu;
+    } else {
+      v = (uint8_t)qs[t * kp + b * 32 + (j - 2)];
+    }
   } else {
-    uint8_t* o = out + (t * nb + b) * 292;
-    const float dv = d[t * (kp / 256) + b];
-    memcpy(o, &dv, 4);
-    for (int j = 0; j < 256; ++j) o[4 + j] = (uint8_t)qs[t * kp + b * 256 + j];
-    for (int g = 0; g < 16; ++g) {
-      const int16_t s = bsum[t * (kp / 16) + b * 16 + g];
-      memcpy(o + 260 + 2 * g, &s, 2);
+    if (j < 4) {
+      v = (__float_as_uint(d[t * (kp / 256) + b]) >> (8 * j)) & 0xFFu;
+    } else if (j < 260) {
+      v = (uint8_t)qs[t * kp + b * 256 + (j - 4)];
+    } else {
+      const int g = (j - 260) >> 1;
+      const uint32_t s = (uint16_t)bsum[t * (kp / 16) + b * 16 + g];
+      v = (s >> (8 * ((j - 260) & 1))) & 0xFFu;
     }
   }
+  out[i] = (uint8_t)v;
 }
 
 // Exact integer block dots of one repacked row against token 0 of `a`.
@@ -237,9 +244,9 @@ int launch_quantize_act(int act_type, const float* x, int64_t x_stride, int n_to
 }
 
 int launch_act_to_blocks(const ActQ& a, int64_t k, void* blocks, cudaStream_t s) {
-  const int64_t nb = (int64_t)a.n_tok * (k / (a.type == B2_Q8_0 ? 32 : 256));
-  if (nb == 0) return B2_OK;
-  act_to_blocks_kernel<<<grid_for(nb, 128), 128, 0, s>>>(a.type, a.qs, a.d, a.bsum, a.n_tok, k, a.kp,
+  const int64_t nbytes = (int64_t)a.n_tok * (int64_t)row_bytes(a.type, k);
+  if (nbytes == 0) return B2_OK;
+  act_to_blocks_kernel<<<grid_for(nbytes, 256), 256, 0, s>>>(a.type, a.qs, a.d, a.bsum, a.n_tok, k, a.kp,
                                                          static_cast<uint8_t*>(blocks));
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
