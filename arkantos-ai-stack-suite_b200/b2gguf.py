@@ -65,6 +65,10 @@ def _bind() -> None:
         "b2_event_record": (_i, [_vp, _vp]),
         "b2_event_elapsed_ms": (_i, [_vp, _vp, _vp]),
         "b2_set_pdl": (_i, [_i]),
+        "b2_graph_capture_begin": (_i, [_vp]),
+        "b2_graph_capture_end": (_i, [_vp, _vp]),
+        "b2_graph_launch": (_i, [_vp, _vp]),
+        "b2_graph_destroy": (_i, [_vp]),
         "b2_row_bytes": (_sz, [_i, _i64]),
         "b2_quantize_weights": (_i, [_i, _vp, _i64, _i64, _vp, _i]),
         "b2_synth_normal": (_i, [_u64, _u64, _i64, _f, _f, _vp, _i]),
@@ -150,6 +154,42 @@ class DeviceBuffer:
             self.free()
         except Exception:
             pass
+
+
+class Stream:
+    def __init__(self):
+        p = ctypes.c_void_p()
+        check(lib.b2_stream_create(ctypes.byref(p)), "stream_create")
+        self.h = p.value
+
+    def synchronize(self) -> None:
+        check(lib.b2_stream_synchronize(self.h), "stream_synchronize")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.b2_stream_destroy(self.h)
+
+
+class Graph:
+    """Captures the library calls made by fn(stream) once; launch() replays them."""
+
+    def __init__(self, stream: Stream, fn):
+        check(lib.b2_graph_capture_begin(stream.h), "graph_capture_begin")
+        try:
+            fn(stream.h)
+        finally:
+            e = ctypes.c_void_p()
+            rc = lib.b2_graph_capture_end(stream.h, ctypes.byref(e))
+        check(rc, "graph_capture_end")
+        self.h = e.value
+        self.stream = stream
+
+    def launch(self) -> None:
+        check(lib.b2_graph_launch(self.h, self.stream.h), "graph_launch")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.b2_graph_destroy(self.h)
 
 
 def synchronize() -> None:

@@ -137,6 +137,30 @@ int b2_event_elapsed_ms(void* start, void* stop, float* ms) {
   B2_CUDA_TRY(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop)));
   return B2_OK;
 }
+int b2_graph_capture_begin(void* stream) {
+  B2_CHECK_ARG(stream, "graph capture needs a created stream");
+  B2_CUDA_TRY(cudaStreamBeginCapture(as_stream(stream), cudaStreamCaptureModeThreadLocal));
+  return B2_OK;
+}
+int b2_graph_capture_end(void* stream, void** graph_exec) {
+  B2_CHECK_ARG(stream && graph_exec, "graph_capture_end arguments");
+  cudaGraph_t g = nullptr;
+  B2_CUDA_TRY(cudaStreamEndCapture(as_stream(stream), &g));
+  cudaGraphExec_t e = nullptr;
+  const cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+  cudaGraphDestroy(g);
+  B2_CUDA_TRY(err);
+  *graph_exec = e;
+  return B2_OK;
+}
+int b2_graph_launch(void* graph_exec, void* stream) {
+  B2_CUDA_TRY(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), as_stream(stream)));
+  return B2_OK;
+}
+int b2_graph_destroy(void* graph_exec) {
+  B2_CUDA_TRY(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)));
+  return B2_OK;
+}
 int b2_set_pdl(int enabled) {
   b2::set_pdl(enabled != 0);
   return B2_OK;
@@ -305,25 +329,49 @@ int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stre
   return rc;
 }
 
+namespace {
+// Per-thread device staging for the host-buffer entry points, grown on demand
+// and kept, so a call does no allocation once warm.
+struct HostStage {
+  void* dev = nullptr;
+  size_t bytes = 0;
+  int device = -1;
+  ~HostStage() {
+    if (dev) cudaFree(dev);
+  }
+};
+thread_local HostStage g_stage;
+int stage_reserve(size_t bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (g_stage.dev && (g_stage.bytes < bytes || g_stage.device != dev)) {
+    cudaFree(g_stage.dev);
+    g_stage.dev = nullptr;
+  }
+  if (!g_stage.dev) {
+    B2_CUDA_TRY(cudaMalloc(&g_stage.dev, bytes));
+    g_stage.bytes = bytes;
+    g_stage.device = dev;
+  }
+  return B2_OK;
+}
+}  // namespace
+
 int b2_gemv_host(const b2_qmatrix* w, const float* x_host, int n_tok, float* y_host) {
   B2_CHECK_ARG(w && x_host && y_host && n_tok >= 1 && n_tok <= 8, "gemv_host arguments");
   const size_t xb = (size_t)n_tok * w->m.k * 4, yb = (size_t)n_tok * w->m.n_rows * 4;
+  const size_t xoff = (xb + 255) / 256 * 256;
+  int rc = stage_reserve(xoff + yb);
+  if (rc != B2_OK) return rc;
   cudaStream_t s = 0;
-  void* buf = nullptr;
-  B2_CUDA_TRY(cudaMallocAsync(&buf, xb + yb + 256, s));
-  float* xd = static_cast<float*>(buf);
-  float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + (xb + 255) / 256 * 256);
-  int rc = B2_OK;
-  if (cudaMemcpyAsync(xd, x_host, xb, cudaMemcpyHostToDevice, s) != cudaSuccess) rc = B2_ERR_CUDA;
-  if (rc == B2_OK) rc = b2_gemv(w, xd, n_tok, yd, s);
-  if (rc == B2_OK && cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, s) != cudaSuccess) rc = B2_ERR_CUDA;
-  cudaFreeAsync(buf, s);
-  const cudaError_t e = cudaStreamSynchronize(s);
-  if (rc == B2_OK && e != cudaSuccess) {
-    set_error("gemv_host: %s", cudaGetErrorString(e));
-    rc = B2_ERR_CUDA;
-  }
-  return rc;
+  float* xd = static_cast<float*>(g_stage.dev);
+  float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(g_stage.dev) + xoff);
+  B2_CUDA_TRY(cudaMemcpyAsync(xd, x_host, xb, cudaMemcpyHostToDevice, s));
+  rc = b2_gemv(w, xd, n_tok, yd, s);
+  if (rc != B2_OK) return rc;
+  B2_CUDA_TRY(cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, s));
+  B2_CUDA_TRY(cudaStreamSynchronize(s));
+  return B2_OK;
 }
 
 int b2_block_dots(const b2_qmatrix* w, int64_t row, const float* x, int32_t* out_i, int32_t* out_m, void* stream) {

@@ -27,6 +27,19 @@ void set_error(const char* fmt, ...) {
 }
 const char* last_error() { return g_err; }
 bool pdl_enabled() { return g_pdl; }
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
 void set_pdl(bool on) { g_pdl = on; }
 
 int block_elems(int type) {
@@ -67,41 +80,24 @@ int p0_bytes_per_256(int type) {
   }
   return 0;
 }
-int kc_max(int type) {
-  switch (type) {
-    case B2_Q4_0: return 3072;
-    case B2_Q8_0: return 1536;
-    case B2_Q4_K: return 2816;
-    case B2_Q6_K: return 2048;
-  }
-  return 2048;
-}
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 }  // namespace
 
+// One chunk spanning the padded row: consecutive rows of a plane are then one
+// contiguous range, so a stage of several whole rows is a single bulk copy
+// per plane.
 void plan_qmatrix(QMatrix& m) {
-  const int64_t k256 = (m.k + 255) / 256;
-  const int64_t nmin = std::max<int64_t>(1, (k256 * 256 + kc_max(m.type) - 1) / kc_max(m.type));
-  int64_t best_n = nmin, best_kp = INT64_MAX;
-  for (int64_t n = nmin; n < nmin + 4; ++n) {
-    const int64_t kc256 = (k256 + n - 1) / n;
-    const int64_t kp = n * kc256 * 256;
-    if (kp < best_kp) {
-      best_kp = kp;
-      best_n = n;
-    }
-  }
-  m.n_chunks = (int)best_n;
-  m.kc = (int)(((k256 + best_n - 1) / best_n) * 256);
-  m.kp = (int64_t)m.n_chunks * m.kc;
-  m.p0_chunk = (int64_t)(m.kc / 256) * p0_bytes_per_256(m.type);
-  m.p0_row = m.p0_chunk * m.n_chunks;
+  m.kp = round_up(m.k, 256);
+  m.n_chunks = 1;
+  m.kc = (int)m.kp;
+  m.p0_chunk = (m.kp / 256) * p0_bytes_per_256(m.type);
+  m.p0_row = m.p0_chunk;
   switch (m.type) {
-    case B2_Q4_0: case B2_Q8_0: m.p1_chunk = m.kc / 16; break;
-    case B2_Q6_K: m.p1_chunk = round_up((m.kc / 256) * 2, 16); break;
+    case B2_Q4_0: case B2_Q8_0: m.p1_chunk = m.kp / 16; break;
+    case B2_Q6_K: m.p1_chunk = round_up((m.kp / 256) * 2, 16); break;
     default: m.p1_chunk = 0;
   }
-  m.p1_row = m.p1_chunk * m.n_chunks;
+  m.p1_row = m.p1_chunk;
 }
 
 void repack_rows_host(const QMatrix& m, const uint8_t* gguf, int64_t r0, int64_t r1, uint8_t* p0, uint8_t* p1) {

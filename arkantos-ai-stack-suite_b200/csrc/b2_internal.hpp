@@ -121,6 +121,9 @@ int launch_block_dots(const QMatrix& w, const ActQ& a, int64_t row, int32_t* out
                       cudaStream_t s);
 int launch_dequantize(const QMatrix& w, float* dst, cudaStream_t s);
 
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+
 // Programmatic dependent launch between this library's kernels (per thread).
 bool pdl_enabled();
 void set_pdl(bool on);

@@ -82,6 +82,13 @@ B2_API int b2_event_create(void** event);
 B2_API int b2_event_destroy(void* event);
 B2_API int b2_event_record(void* event, void* stream);
 B2_API int b2_event_elapsed_ms(void* start, void* stop, float* ms);
+/* CUDA-graph capture of work issued on a (non-default) stream: everything
+ * this library launches between begin and end is recorded once and replayed
+ * by b2_graph_launch with one host call, as the engines' decode loop does. */
+B2_API int b2_graph_capture_begin(void* stream);
+B2_API int b2_graph_capture_end(void* stream, void** graph_exec);
+B2_API int b2_graph_launch(void* graph_exec, void* stream);
+B2_API int b2_graph_destroy(void* graph_exec);
 /* Enables (1) or disables (0) programmatic dependent launch between this
  * library's kernels on the calling thread (default 1). */
 B2_API int b2_set_pdl(int enabled);
