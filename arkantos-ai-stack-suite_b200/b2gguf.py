@@ -81,6 +81,32 @@ def _bind() -> None:
         "b2_gemv": (_i, [_vp, _vp, _i, _vp, _vp]),
         "b2_gemv_host": (_i, [_vp, _vp, _i, _vp]),
         "b2_block_dots": (_i, [_vp, _i64, _vp, _vp, _vp, _vp]),
+        "b2_gguf_write_synthetic_llama": (_i, [_vp, ctypes.c_char_p, _i]),
+        "b2_embed": (_i, [_i, _vp, _i, _i, _vp, _i, _vp, _vp]),
+        "b2_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _f, _vp]),
+        "b2_rope_kv_store": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
+        "b2_attn_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+        "b2_kv_shift_k": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
+        "b2_model_default_params": (None, [_vp]),
+        "b2_nccl_unique_id": (_i, [_vp]),
+        "b2_model_load": (_i, [ctypes.c_char_p, _vp, _vp]),
+        "b2_model_free": (_i, [_vp]),
+        "b2_model_info": (_i, [_vp, _vp, _i]),
+        "b2_model_device_bytes": (_i, [_vp, _vp]),
+        "b2_context_default_params": (None, [_vp]),
+        "b2_context_create": (_i, [_vp, _vp, _vp]),
+        "b2_context_free": (_i, [_vp]),
+        "b2_context_stream": (_i, [_vp, _vp]),
+        "b2_decode": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32]),
+        "b2_get_logits": (_i, [_vp, ctypes.c_int32, _vp, _i64]),
+        "b2_get_argmax": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32]),
+        "b2_synchronize_context": (_i, [_vp]),
+        "b2_kv_clear": (_i, [_vp]),
+        "b2_kv_seq_rm": (_i, [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+        "b2_kv_seq_add": (_i, [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+        "b2_kv_seq_pos_max": (_i, [_vp, ctypes.c_int32, _vp]),
+        "b2_set_abort_callback": (_i, [_vp, _vp, _vp]),
+        "b2_set_eval_callback": (_i, [_vp, _vp, _vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -306,3 +332,143 @@ def quantize_act(act_type: int, x: np.ndarray) -> np.ndarray:
     out = DeviceBuffer(n_tok * row_bytes(act_type, k))
     check(lib.b2_quantize_act(act_type, xd.ptr, n_tok, k, out.ptr, None), "quantize_act")
     return out.download(np.uint8).reshape(n_tok, -1)
+
+
+# ---- GGUF models and the engine -------------------------------------------------------------
+class LlamaHParams(ctypes.Structure):
+    _fields_ = [("n_layer", ctypes.c_int32), ("n_embd", ctypes.c_int32), ("n_ff", ctypes.c_int32),
+                ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32), ("n_vocab", ctypes.c_int32),
+                ("n_ctx_train", ctypes.c_int32), ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+                ("wtype", ctypes.c_int32), ("embd_type", ctypes.c_int32), ("out_type", ctypes.c_int32),
+                ("seed", ctypes.c_uint64), ("w_std", ctypes.c_float)]
+
+
+def write_synthetic_llama(path: str, n_layer: int, n_embd: int, n_ff: int, n_head: int, n_head_kv: int,
+                          n_vocab: int, wtype: int, embd_type: int | None = None, out_type: int | None = None,
+                          seed: int = 0, w_std: float = 0.02, rms_eps: float = 1e-5, rope_theta: float = 10000.0,
+                          n_ctx_train: int = 4096, n_threads: int = 0) -> None:
+    hp = LlamaHParams(n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab, n_ctx_train, rms_eps, rope_theta, wtype,
+                      wtype if embd_type is None else embd_type, wtype if out_type is None else out_type, seed, w_std)
+    nt = n_threads or (os.cpu_count() or 1)
+    check(lib.b2_gguf_write_synthetic_llama(ctypes.byref(hp), path.encode(), nt), "write_synthetic_llama")
+
+
+class ModelParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32),
+                ("nccl_id", ctypes.c_void_p)]
+
+
+class ContextParams(ctypes.Structure):
+    _fields_ = [("n_ctx", ctypes.c_int32), ("n_seq_max", ctypes.c_int32), ("use_graph", ctypes.c_int32)]
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    check(lib.b2_nccl_unique_id(buf), "nccl_unique_id")
+    return buf.raw
+
+
+class Model:
+    INFO = ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "n_vocab", "head_dim", "n_ctx_train", "wtype",
+            "out_type", "tp_rank", "tp_size")
+
+    def __init__(self, path: str, device: int = -1, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None):
+        self._id = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
+        p = ModelParams(device, tp_rank, tp_size, ctypes.cast(self._id, ctypes.c_void_p) if self._id else None)
+        h = ctypes.c_void_p()
+        check(lib.b2_model_load(path.encode(), ctypes.byref(p), ctypes.byref(h)), "model_load")
+        self.h = h.value
+        info = (ctypes.c_int32 * 12)()
+        check(lib.b2_model_info(self.h, info, 12), "model_info")
+        for k, v in zip(self.INFO, info):
+            setattr(self, k, int(v))
+
+    def device_bytes(self) -> int:
+        v = ctypes.c_int64()
+        check(lib.b2_model_device_bytes(self.h, ctypes.byref(v)), "model_device_bytes")
+        return v.value
+
+    def free(self) -> None:
+        if getattr(self, "h", None):
+            lib.b2_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.free()
+
+
+class Context:
+    def __init__(self, model: Model, n_ctx: int = 4096, n_seq: int = 1, use_graph: bool = True):
+        self.model = model
+        p = ContextParams(n_ctx, n_seq, 1 if use_graph else 0)
+        h = ctypes.c_void_p()
+        check(lib.b2_context_create(model.h, ctypes.byref(p), ctypes.byref(h)), "context_create")
+        self.h = h.value
+        s = ctypes.c_void_p()
+        check(lib.b2_context_stream(self.h, ctypes.byref(s)), "context_stream")
+        self.stream = s.value
+        self.last_n = 0
+
+    def decode(self, tokens, pos=None, seq=None, want_logits: int = 2) -> int:
+        t = np.ascontiguousarray(tokens, np.int32)
+        pp = None if pos is None else np.ascontiguousarray(pos, np.int32)
+        ss = None if seq is None else np.ascontiguousarray(seq, np.int32)
+        rc = lib.b2_decode(self.h, ptr(t), ptr(pp) if pp is not None else None, ptr(ss) if ss is not None else None,
+                           t.size, want_logits)
+        check(rc, "decode")
+        self.last_n = min(t.size, 8) if t.size <= 8 else (t.size - 1) % 8 + 1
+        return rc
+
+    def logits(self, i: int = -1) -> np.ndarray:
+        out = np.empty(self.model.n_vocab, np.float32)
+        check(lib.b2_get_logits(self.h, i, ptr(out), out.size), "get_logits")
+        return out
+
+    def argmax(self, n: int | None = None):
+        n = self.last_n if n is None else n
+        ids = np.empty(max(n, 8), np.int32)
+        top = np.empty(max(n, 8), np.float32)
+        mar = np.empty(max(n, 8), np.float32)
+        check(lib.b2_get_argmax(self.h, ptr(ids), ptr(top), ptr(mar), ids.size), "get_argmax")
+        return ids[:n], top[:n], mar[:n]
+
+    def synchronize(self) -> None:
+        check(lib.b2_synchronize_context(self.h), "synchronize_context")
+
+    EVAL = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p)
+
+    def set_eval_callback(self, fn) -> None:
+        """fn(name, layer, np.ndarray) with each intermediate of eager steps (llama cb_eval)."""
+        if fn is None:
+            self._eval = None
+            check(lib.b2_set_eval_callback(self.h, None, None), "set_eval_callback")
+            return
+        def cb(name, layer, dptr, n, user):
+            out = np.empty(n, np.float32)
+            lib.b2_memcpy_d2h(out.ctypes.data, dptr, out.nbytes, None)
+            lib.b2_device_synchronize()
+            fn(name.decode(), layer, out)
+        self._eval = self.EVAL(cb)
+        check(lib.b2_set_eval_callback(self.h, ctypes.cast(self._eval, ctypes.c_void_p), None), "set_eval_callback")
+
+    def kv_clear(self) -> None:
+        check(lib.b2_kv_clear(self.h), "kv_clear")
+
+    def kv_seq_rm(self, seq: int, p0: int, p1: int) -> None:
+        check(lib.b2_kv_seq_rm(self.h, seq, p0, p1), "kv_seq_rm")
+
+    def kv_seq_add(self, seq: int, p0: int, p1: int, delta: int) -> None:
+        check(lib.b2_kv_seq_add(self.h, seq, p0, p1, delta), "kv_seq_add")
+
+    def kv_pos_max(self, seq: int) -> int:
+        v = ctypes.c_int32()
+        check(lib.b2_kv_seq_pos_max(self.h, seq, ctypes.byref(v)), "kv_seq_pos_max")
+        return v.value
+
+    def free(self) -> None:
+        if getattr(self, "h", None):
+            lib.b2_context_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.free()

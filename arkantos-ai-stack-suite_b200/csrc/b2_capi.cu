@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "b2_common.cuh"
+#include "b2_layers.hpp"
 
 struct b2_qmatrix {
   b2::QMatrix m;
@@ -384,6 +385,101 @@ int b2_block_dots(const b2_qmatrix* w, int64_t row, const float* x, int32_t* out
   rc = launch_quantize_act(a.type, x, w->m.k, 1, w->m.k, a, s);
   if (rc == B2_OK) rc = launch_block_dots(w->m, a, row, out_i, out_m, s);
   free_act(a, s);
+  return rc;
+}
+
+int b2_embed(int type, const void* table, int n_vocab, int n_embd, const int32_t* tokens, int n_tok, float* out,
+             void* stream) {
+  B2_CHECK_ARG(table && tokens && out && n_vocab > 0 && n_embd > 0 && n_tok > 0, "embed arguments");
+  B2_CHECK_ARG(type == B2_F32 || type == B2_F16 || b2::is_weight_type(type), "embedding type");
+  B2_CHECK_ARG(n_embd % b2::block_elems(type) == 0, "n_embd must be a multiple of the block size");
+  return launch_embed(tokens, n_tok, n_vocab, type, static_cast<const uint8_t*>(table),
+                      (int64_t)b2::row_bytes(type, n_embd), n_embd, out, as_stream(stream));
+}
+
+int b2_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_rows, int n, float eps, void* stream) {
+  B2_CHECK_ARG(x && w && out && n_rows > 0 && n > 0, "rmsnorm arguments");
+  return launch_add_rmsnorm(x, delta, w, out, n_rows, n, eps, as_stream(stream));
+}
+
+namespace {
+// Zeroed per-sequence KV states (plain layout: slot = position).
+int zero_states(KvSeqState** st, int n_seq, cudaStream_t s) {
+  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(st), sizeof(KvSeqState) * (size_t)n_seq, s));
+  B2_CUDA_TRY(cudaMemsetAsync(*st, 0, sizeof(KvSeqState) * (size_t)n_seq, s));
+  return B2_OK;
+}
+int max_seq_on_host(const int32_t* seq, int n, int* out, cudaStream_t s) {
+  std::vector<int32_t> h((size_t)n);
+  B2_CUDA_TRY(cudaMemcpyAsync(h.data(), seq, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+  B2_CUDA_TRY(cudaStreamSynchronize(s));
+  int m = 0;
+  for (int v : h) {
+    if (v < 0) {
+      set_error("sequence id %d out of range", v);
+      return B2_ERR_INVALID;
+    }
+    m = std::max(m, v);
+  }
+  *out = m + 1;
+  return B2_OK;
+}
+}  // namespace
+
+int b2_rope_kv_store(const float* qkv, int n_tok, int n_head, int n_kv, int head_dim, const int32_t* pos,
+                     const int32_t* seq, const float* rope, float* q_out, uint16_t* k_cache, uint16_t* v_cache, int cap,
+                     void* stream) {
+  B2_CHECK_ARG(qkv && pos && seq && rope && q_out && k_cache && v_cache && n_tok > 0 && cap > 0,
+               "rope_kv_store arguments");
+  B2_CHECK_ARG(head_dim % 2 == 0 && n_head > 0 && n_kv > 0, "head shape");
+  cudaStream_t s = as_stream(stream);
+  int n_seq = 0;
+  int rc = max_seq_on_host(seq, n_tok, &n_seq, s);
+  if (rc) return rc;
+  KvSeqState* st = nullptr;
+  if ((rc = zero_states(&st, n_seq, s))) return rc;
+  rc = launch_rope_kv(qkv, n_tok, n_head, n_kv, head_dim, pos, seq, rope, q_out, k_cache, v_cache, st, cap, s);
+  cudaFreeAsync(st, s);
+  return rc;
+}
+
+int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
+                   const int32_t* seq, int n_q, int n_head, int n_kv, int head_dim, int cap, float* out, void* stream) {
+  B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && n_q > 0 && cap > 0, "attn_decode arguments");
+  B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
+  cudaStream_t s = as_stream(stream);
+  int n_seq = 0;
+  int rc = max_seq_on_host(seq, n_q, &n_seq, s);
+  if (rc) return rc;
+  constexpr int P = 256;
+  const int n_split = attn_splits(cap, P);
+  const size_t po = (size_t)n_q * n_head * n_split * head_dim, pm = (size_t)n_q * n_head * n_split * 2;
+  void* scratch = nullptr;
+  B2_CUDA_TRY(cudaMallocAsync(&scratch, (po + pm) * 4, s));
+  KvSeqState* st = nullptr;
+  if ((rc = zero_states(&st, n_seq, s)) == B2_OK) {
+    float* part_o = static_cast<float*>(scratch);
+    rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, st, cap, P, part_o, part_o + po,
+                          out, s);
+    cudaFreeAsync(st, s);
+  }
+  cudaFreeAsync(scratch, s);
+  return rc;
+}
+
+int b2_kv_shift_k(uint16_t* k_cache, int seq, int n_kv, int head_dim, int cap, int p_begin, int p_end, int delta,
+                  float theta, void* stream) {
+  B2_CHECK_ARG(k_cache && seq >= 0 && p_begin >= 0 && p_end <= cap && head_dim % 2 == 0, "kv_shift_k arguments");
+  cudaStream_t s = as_stream(stream);
+  std::vector<float> cs((size_t)head_dim);
+  rope_table(theta, head_dim, delta, 1, cs.data());
+  float* csd = nullptr;
+  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&csd), cs.size() * 4, s));
+  B2_CUDA_TRY(cudaMemcpyAsync(csd, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, s));
+  const KvSeqState st{0, 0};
+  const int rc = launch_kv_shift(k_cache, n_kv, head_dim, seq, st, cap, p_begin, p_end, csd, s);
+  cudaFreeAsync(csd, s);
+  B2_CUDA_TRY(cudaStreamSynchronize(s));
   return rc;
 }
 

@@ -1,0 +1,819 @@
+// The llama.cpp-shaped engine behind the C ABI: model load (GGUF -> repacked
+// device shards), context (fp16 KV ring per sequence, step buffers), decode
+// (one CUDA graph per step shape), KV shift / removal, greedy argmax, and
+// tensor parallelism over NCCL.
+//
+// Mirrors the calls Milda and Sutra make (Milda/src/engine.cpp:703-1292,
+// 1521-1548, 1642-1675, 1962-2117; Sutra/src/llm_backends.cpp:2395-2760) and
+// the forward order of Singularity's forward_token
+// (Singularity/src/core/cortex_a5_engine.cpp:1029-1293).
+//
+// Tensor parallelism (tp ranks, one process per GPU): Q/K/V and gate/up are
+// split by output rows (heads / FFN features), O and down by input columns
+// (their partial sums are all-reduced), the output head by vocabulary rows
+// (the logits are all-gathered).  Shard boundaries fall on quantization
+// block boundaries, so each rank quantizes its activation slice exactly as
+// the full vector would be quantized.
+#include <math.h>
+#include <nccl.h>
+#include <string.h>
+
+#include <memory>
+#include <new>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "b2_gguf.hpp"
+#include "b2_internal.hpp"
+#include "b2_layers.hpp"
+
+namespace b2 {
+
+int write_synthetic_llama(const b2_llama_hparams& hp, const char* path, int n_threads);
+
+namespace {
+
+constexpr int kStepMax = 8;          // tokens per device step (GEMV batch)
+constexpr int kAttnChunk = 256;      // positions per split-K attention CTA
+
+struct DevQ {
+  QMatrix m;
+  ~DevQ() {
+    if (m.plane0) cudaFree(m.plane0);
+    if (m.plane1) cudaFree(m.plane1);
+  }
+};
+
+// Uploads rows given by pointers to their first byte (all rows k values of
+// `type` starting at the slice's first column).
+int upload_rows(DevQ& q, int type, int64_t k, const std::vector<const uint8_t*>& rows) {
+  QMatrix& m = q.m;
+  m.type = type;
+  m.n_rows = (int64_t)rows.size();
+  m.k = k;
+  plan_qmatrix(m);
+  cudaGetDevice(&m.device);
+  const size_t b0 = (size_t)m.p0_row * m.n_rows, b1 = (size_t)m.p1_row * m.n_rows;
+  B2_CUDA_TRY(cudaMalloc(&m.plane0, b0));
+  if (b1) B2_CUDA_TRY(cudaMalloc(&m.plane1, b1));
+  const size_t rb = row_bytes(type, k);
+  std::vector<uint8_t> h0(b0), h1(b1), rowbuf;
+  const int nt = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  auto work = [&](int64_t a, int64_t b) {
+    for (int64_t r = a; r < b; ++r)
+      repack_rows_host(m, rows[r], 0, 1, h0.data() + r * m.p0_row, b1 ? h1.data() + r * m.p1_row : nullptr);
+  };
+  (void)rb;
+  std::vector<std::thread> th;
+  for (int t = 1; t < nt; ++t) th.emplace_back(work, m.n_rows * t / nt, m.n_rows * (t + 1) / nt);
+  work(0, m.n_rows / nt);
+  for (auto& x : th) x.join();
+  B2_CUDA_TRY(cudaMemcpy(m.plane0, h0.data(), b0, cudaMemcpyHostToDevice));
+  if (b1) B2_CUDA_TRY(cudaMemcpy(m.plane1, h1.data(), b1, cudaMemcpyHostToDevice));
+  return B2_OK;
+}
+
+struct Layer {
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  DevQ wqkv, wo, wgu, wdown;
+};
+
+}  // namespace
+}  // namespace b2
+
+struct b2_model {
+  int device = 0;
+  int tp_rank = 0, tp_size = 1;
+  ncclComm_t comm = nullptr;
+  b2::GgufFile gguf;
+  int n_layer = 0, n_embd = 0, n_ff = 0, n_head = 0, n_head_kv = 0, n_vocab = 0, head_dim = 0, n_ctx_train = 0;
+  int nh_l = 0, nkv_l = 0, ff_l = 0, v_l = 0;   // per-rank shares
+  float eps = 1e-5f, theta = 10000.0f;
+  int wtype = 0, embd_type = 0, out_type = 0;
+  std::vector<std::unique_ptr<b2::Layer>> layers;
+  uint8_t* embd = nullptr;
+  int64_t embd_row_bytes = 0;
+  float* out_norm = nullptr;
+  b2::DevQ head;
+  int64_t device_bytes = 0;
+  ~b2_model();
+};
+
+b2_model::~b2_model() {
+  if (device >= 0) cudaSetDevice(device);
+  for (auto& l : layers) {
+    if (l->attn_norm) cudaFree(l->attn_norm);
+    if (l->ffn_norm) cudaFree(l->ffn_norm);
+  }
+  layers.clear();
+  if (embd) cudaFree(embd);
+  if (out_norm) cudaFree(out_norm);
+  if (comm) ncclCommDestroy(comm);
+}
+
+struct b2_context {
+  b2_model* model = nullptr;
+  int n_ctx = 0, n_seq = 0;
+  cudaStream_t stream = nullptr;
+  // KV ring per layer: [n_seq][nkv_l][n_ctx][head_dim] fp16
+  std::vector<uint16_t*> kc, vc;
+  b2::KvSeqState* st_d = nullptr;
+  std::vector<b2::KvSeqState> st;
+  std::vector<int> n_past;
+  float* rope = nullptr;        // [n_ctx][head_dim]
+  float* shift_cs = nullptr;    // [head_dim] rotation of the last shift
+  // step inputs (device + pinned host staging)
+  int32_t *tok_d = nullptr, *pos_d = nullptr, *seq_d = nullptr;
+  int32_t* in_h = nullptr;      // [2 slots][3][kStepMax] pinned
+  cudaEvent_t in_ev[2] = {nullptr, nullptr};
+  int in_slot = 0;
+  // step buffers
+  float *x = nullptr, *delta = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
+  float *logits_l = nullptr, *logits = nullptr, *part_o = nullptr, *part_ml = nullptr, *top = nullptr;
+  int32_t* ids = nullptr;
+  int* status = nullptr;
+  // last decode
+  int last_n = 0;
+  bool last_logits = false;
+  // graphs per (n_tok, with_logits)
+  cudaGraphExec_t graphs[b2::kStepMax + 1][2] = {};
+  bool use_graph = true;
+  b2_abort_callback abort_cb = nullptr;
+  void* abort_user = nullptr;
+  b2_eval_callback eval_cb = nullptr;
+  void* eval_user = nullptr;
+  std::vector<void*> allocs;
+  ~b2_context();
+};
+
+b2_context::~b2_context() {
+  if (model) cudaSetDevice(model->device);
+  for (auto& row : graphs)
+    for (auto& g : row)
+      if (g) cudaGraphExecDestroy(g);
+  for (void* p : allocs) cudaFree(p);
+  if (in_h) cudaFreeHost(in_h);
+  for (auto& e : in_ev)
+    if (e) cudaEventDestroy(e);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+namespace b2 {
+namespace {
+
+template <typename T>
+int dalloc(b2_context* c, T** p, size_t count) {
+  void* v = nullptr;
+  B2_CUDA_TRY(cudaMalloc(&v, std::max<size_t>(count * sizeof(T), 16)));
+  c->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return B2_OK;
+}
+
+int upload_f32(const GgufTensor* t, int64_t n, float** out) {
+  std::vector<float> v((size_t)n);
+  if (t->type == B2_F32) {
+    memcpy(v.data(), t->data, (size_t)n * 4);
+  } else if (t->type == B2_F16) {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(t->data);
+    for (int64_t i = 0; i < n; ++i) v[i] = host_f16_to_f32(h[i]);
+  } else {
+    set_error("norm tensor %s: type %d not F32/F16", t->name.c_str(), t->type);
+    return B2_ERR_FORMAT;
+  }
+  B2_CUDA_TRY(cudaMalloc(out, (size_t)n * 4));
+  B2_CUDA_TRY(cudaMemcpy(*out, v.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+  return B2_OK;
+}
+
+#define B2_NCCL_TRY(expr)                                                         \
+  do {                                                                            \
+    ncclResult_t r_ = (expr);                                                     \
+    if (r_ != ncclSuccess) {                                                      \
+      ::b2::set_error("%s: %s", #expr, ncclGetErrorString(r_));                   \
+      return B2_ERR_NCCL;                                                         \
+    }                                                                             \
+  } while (0)
+
+int load_model(b2_model* m, const char* path, const b2_model_params* p) {
+  if (p->device >= 0) B2_CUDA_TRY(cudaSetDevice(p->device));
+  cudaGetDevice(&m->device);
+  m->tp_rank = p->tp_rank;
+  m->tp_size = p->tp_size;
+  std::string err;
+  if (!m->gguf.open(path, &err)) {
+    set_error("model load: %s", err.c_str());
+    return B2_ERR_FORMAT;
+  }
+  const GgufFile& g = m->gguf;
+  m->n_layer = (int)g.get_int(".block_count", 0);
+  m->n_embd = (int)g.get_int(".embedding_length", 0);
+  m->n_ff = (int)g.get_int(".feed_forward_length", 0);
+  m->n_head = (int)g.get_int(".attention.head_count", 0);
+  m->n_head_kv = (int)g.get_int(".attention.head_count_kv", m->n_head);
+  m->n_ctx_train = (int)g.get_int(".context_length", 0);
+  m->eps = (float)g.get_float(".layer_norm_rms_epsilon", 1e-5);
+  m->theta = (float)g.get_float(".rope.freq_base", 10000.0);
+  const GgufTensor* te = g.tensor("token_embd.weight");
+  const GgufTensor* tn = g.tensor("output_norm.weight");
+  const GgufTensor* to = g.tensor("output.weight");
+  if (!to) to = te;   // tied head (Singularity/src/core/cortex_a5_engine.cpp:650-654)
+  if (m->n_layer <= 0 || m->n_embd <= 0 || m->n_head <= 0 || !te || !tn || m->n_embd % m->n_head) {
+    set_error("model load: missing llama hyper-parameters or tensors");
+    return B2_ERR_FORMAT;
+  }
+  m->n_vocab = (int)te->ne[1];
+  m->head_dim = m->n_embd / m->n_head;
+  const int tp = m->tp_size, r = m->tp_rank;
+  if (tp < 1 || r < 0 || r >= tp || m->n_head % tp || m->n_head_kv % tp || m->n_ff % tp || m->n_vocab % tp ||
+      (int)to->ne[1] != m->n_vocab) {
+    set_error("model load: heads / ffn / vocab not divisible by tp=%d", tp);
+    return B2_ERR_UNSUPPORTED;
+  }
+  if (m->head_dim != 64 && m->head_dim != 128) {
+    set_error("model load: head_dim %d unsupported (64 or 128)", m->head_dim);
+    return B2_ERR_UNSUPPORTED;
+  }
+  m->nh_l = m->n_head / tp;
+  m->nkv_l = m->n_head_kv / tp;
+  m->ff_l = m->n_ff / tp;
+  m->v_l = m->n_vocab / tp;
+  const int hd = m->head_dim, d = m->n_embd;
+  if (tp > 1) {
+    if (!p->nccl_id) {
+      set_error("model load: tp_size > 1 needs an NCCL unique id");
+      return B2_ERR_INVALID;
+    }
+    ncclUniqueId id;
+    memcpy(&id, p->nccl_id, sizeof id);
+    B2_NCCL_TRY(ncclCommInitRank(&m->comm, tp, id, r));
+  }
+  // Embedding table (replicated, GGUF bytes as-is) and output norm.
+  m->embd_type = te->type;
+  m->embd_row_bytes = (int64_t)row_bytes(te->type, d);
+  B2_CUDA_TRY(cudaMalloc(&m->embd, te->bytes));
+  B2_CUDA_TRY(cudaMemcpy(m->embd, te->data, te->bytes, cudaMemcpyHostToDevice));
+  m->device_bytes += (int64_t)te->bytes;
+  int rc = upload_f32(tn, d, &m->out_norm);
+  if (rc) return rc;
+  // Output head: vocabulary rows [r*v_l, (r+1)*v_l).
+  m->out_type = to->type;
+  if (!is_weight_type(to->type)) {
+    set_error("model load: output head type %d unsupported", to->type);
+    return B2_ERR_UNSUPPORTED;
+  }
+  {
+    std::vector<const uint8_t*> rows;
+    const size_t rb = row_bytes(to->type, d);
+    for (int64_t i = 0; i < m->v_l; ++i) rows.push_back(to->data + (size_t)(r * (int64_t)m->v_l + i) * rb);
+    if ((rc = upload_rows(m->head, to->type, d, rows))) return rc;
+  }
+  for (int l = 0; l < m->n_layer; ++l) {
+    auto L = std::make_unique<Layer>();
+    const std::string b = "blk." + std::to_string(l) + ".";
+    auto T = [&](const char* n) { return g.tensor(b + n); };
+    const GgufTensor *an = T("attn_norm.weight"), *fn = T("ffn_norm.weight"), *wq = T("attn_q.weight"),
+                     *wk = T("attn_k.weight"), *wv = T("attn_v.weight"), *wo = T("attn_output.weight"),
+                     *wg = T("ffn_gate.weight"), *wu = T("ffn_up.weight"), *wd = T("ffn_down.weight");
+    if (!an || !fn || !wq || !wk || !wv || !wo || !wg || !wu || !wd) {
+      set_error("model load: layer %d tensors missing", l);
+      return B2_ERR_FORMAT;
+    }
+    if (wq->type != wk->type || wq->type != wv->type || wg->type != wu->type) {
+      set_error("model load: layer %d mixes quantization types within fused projections", l);
+      return B2_ERR_UNSUPPORTED;
+    }
+    if (l == 0) m->wtype = wq->type;
+    if ((rc = upload_f32(an, d, &L->attn_norm)) || (rc = upload_f32(fn, d, &L->ffn_norm))) return rc;
+    // Q/K/V rows of this rank's heads, concatenated.
+    {
+      std::vector<const uint8_t*> rows;
+      const size_t rb = row_bytes(wq->type, d);
+      for (int64_t i = 0; i < (int64_t)m->nh_l * hd; ++i) rows.push_back(wq->data + ((int64_t)r * m->nh_l * hd + i) * rb);
+      for (int64_t i = 0; i < (int64_t)m->nkv_l * hd; ++i) rows.push_back(wk->data + ((int64_t)r * m->nkv_l * hd + i) * rb);
+      for (int64_t i = 0; i < (int64_t)m->nkv_l * hd; ++i) rows.push_back(wv->data + ((int64_t)r * m->nkv_l * hd + i) * rb);
+      if ((rc = upload_rows(L->wqkv, wq->type, d, rows))) return rc;
+    }
+    // O: all rows, input columns of this rank's heads.
+    {
+      const int64_t k_all = (int64_t)m->n_head * hd, k_l = (int64_t)m->nh_l * hd;
+      if (k_l % block_elems(wo->type)) {
+        set_error("model load: attention-out shard not block aligned");
+        return B2_ERR_UNSUPPORTED;
+      }
+      std::vector<const uint8_t*> rows;
+      const size_t rb = row_bytes(wo->type, k_all), off = row_bytes(wo->type, r * k_l);
+      for (int64_t i = 0; i < d; ++i) rows.push_back(wo->data + i * rb + off);
+      if ((rc = upload_rows(L->wo, wo->type, k_l, rows))) return rc;
+    }
+    // gate/up interleaved (gate_i, up_i) for this rank's FFN features.
+    {
+      std::vector<const uint8_t*> rows;
+      const size_t rb = row_bytes(wg->type, d);
+      for (int64_t i = 0; i < m->ff_l; ++i) {
+        rows.push_back(wg->data + ((int64_t)r * m->ff_l + i) * rb);
+        rows.push_back(wu->data + ((int64_t)r * m->ff_l + i) * rb);
+      }
+      if ((rc = upload_rows(L->wgu, wg->type, d, rows))) return rc;
+    }
+    // down: all rows, input columns of this rank's FFN features.
+    {
+      if (m->ff_l % block_elems(wd->type)) {
+        set_error("model load: ffn-down shard not block aligned");
+        return B2_ERR_UNSUPPORTED;
+      }
+      std::vector<const uint8_t*> rows;
+      const size_t rb = row_bytes(wd->type, m->n_ff), off = row_bytes(wd->type, (int64_t)r * m->ff_l);
+      for (int64_t i = 0; i < d; ++i) rows.push_back(wd->data + i * rb + off);
+      if ((rc = upload_rows(L->wdown, wd->type, m->ff_l, rows))) return rc;
+    }
+    for (const DevQ* q : {&L->wqkv, &L->wo, &L->wgu, &L->wdown})
+      m->device_bytes += (q->m.p0_row + q->m.p1_row) * q->m.n_rows;
+    m->device_bytes += 2 * d * 4;
+    m->layers.push_back(std::move(L));
+  }
+  m->device_bytes += (m->head.m.p0_row + m->head.m.p1_row) * m->head.m.n_rows;
+  return B2_OK;
+}
+
+int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
+  B2_CUDA_TRY(cudaSetDevice(m->device));
+  c->model = m;
+  c->n_ctx = p->n_ctx;
+  c->n_seq = p->n_seq_max;
+  c->use_graph = p->use_graph != 0;
+  B2_CUDA_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  const int hd = m->head_dim, d = m->n_embd;
+  const size_t kv = (size_t)c->n_seq * m->nkv_l * c->n_ctx * hd;
+  c->kc.resize(m->n_layer);
+  c->vc.resize(m->n_layer);
+  int rc;
+  for (int l = 0; l < m->n_layer; ++l) {
+    if ((rc = dalloc(c, &c->kc[l], kv)) || (rc = dalloc(c, &c->vc[l], kv))) return rc;
+    B2_CUDA_TRY(cudaMemset(c->kc[l], 0, kv * 2));
+    B2_CUDA_TRY(cudaMemset(c->vc[l], 0, kv * 2));
+  }
+  c->st.assign(c->n_seq, KvSeqState{0, 0});
+  c->n_past.assign(c->n_seq, 0);
+  if ((rc = dalloc(c, &c->st_d, c->n_seq))) return rc;
+  B2_CUDA_TRY(cudaMemcpy(c->st_d, c->st.data(), c->n_seq * sizeof(KvSeqState), cudaMemcpyHostToDevice));
+  std::vector<float> rope((size_t)c->n_ctx * hd);
+  rope_table(m->theta, hd, 0, c->n_ctx, rope.data());
+  if ((rc = dalloc(c, &c->rope, rope.size())) || (rc = dalloc(c, &c->shift_cs, hd))) return rc;
+  B2_CUDA_TRY(cudaMemcpy(c->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice));
+  if ((rc = dalloc(c, &c->tok_d, kStepMax)) || (rc = dalloc(c, &c->pos_d, kStepMax)) ||
+      (rc = dalloc(c, &c->seq_d, kStepMax)))
+    return rc;
+  B2_CUDA_TRY(cudaMallocHost(&c->in_h, 2 * 3 * kStepMax * sizeof(int32_t)));
+  for (auto& e : c->in_ev) B2_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  if ((rc = prepare_gemv_kernels())) return rc;
+  const int T = kStepMax;
+  const int n_split = attn_splits(c->n_ctx, kAttnChunk);
+  if ((rc = dalloc(c, &c->x, (size_t)T * d)) || (rc = dalloc(c, &c->delta, (size_t)T * d)) ||
+      (rc = dalloc(c, &c->xn, (size_t)T * d)) ||
+      (rc = dalloc(c, &c->qkv, (size_t)T * (m->nh_l + 2 * m->nkv_l) * hd)) ||
+      (rc = dalloc(c, &c->q, (size_t)T * m->nh_l * hd)) || (rc = dalloc(c, &c->att, (size_t)T * m->nh_l * hd)) ||
+      (rc = dalloc(c, &c->h, (size_t)T * m->ff_l)) || (rc = dalloc(c, &c->logits_l, (size_t)T * m->v_l)) ||
+      (rc = dalloc(c, &c->logits, (size_t)T * m->n_vocab)) ||
+      (rc = dalloc(c, &c->part_o, (size_t)T * m->nh_l * n_split * hd)) ||
+      (rc = dalloc(c, &c->part_ml, (size_t)T * m->nh_l * n_split * 2)) || (rc = dalloc(c, &c->top, 2 * T)) ||
+      (rc = dalloc(c, &c->ids, T)) || (rc = dalloc(c, &c->status, 4)))
+    return rc;
+  B2_CUDA_TRY(cudaMemset(c->status, 0, 16));
+  return B2_OK;
+}
+
+// One device step over n tokens already staged in tok_d/pos_d/seq_d.
+int enqueue_step(b2_context* c, int n, bool with_logits) {
+  b2_model* m = c->model;
+  cudaStream_t s = c->stream;
+  const int d = m->n_embd, hd = m->head_dim;
+  int rc = launch_embed(c->tok_d, n, m->n_vocab, m->embd_type, m->embd, m->embd_row_bytes, d, c->x, s);
+  if (rc) return rc;
+  auto gemv = [&](const DevQ& w, const float* x, int64_t xs, float* y, int64_t ys, int epi) {
+    GemvArgs a = {};
+    a.w = &w.m;
+    a.x = x;
+    a.x_stride = xs;
+    a.n_tok = n;
+    a.y = y;
+    a.y_stride = ys;
+    a.epilogue = epi;
+    a.row_begin = 0;
+    a.row_end = w.m.n_rows;
+    a.status = c->status;
+    return launch_gemv(a, s);
+  };
+  // cb_eval-style tap (eager steps only).
+  auto tap = [&](const char* name, int layer, const float* p, int64_t count) -> int {
+    if (!c->eval_cb) return B2_OK;
+    B2_CUDA_TRY(cudaStreamSynchronize(s));
+    c->eval_cb(name, layer, p, count, c->eval_user);
+    return B2_OK;
+  };
+  if ((rc = tap("embed", -1, c->x, (int64_t)n * d))) return rc;
+  const int qkv_w = (m->nh_l + 2 * m->nkv_l) * hd;
+  for (int l = 0; l < m->n_layer; ++l) {
+    Layer& L = *m->layers[l];
+    if ((rc = launch_add_rmsnorm(c->x, l ? c->delta : nullptr, L.attn_norm, c->xn, n, d, m->eps, s))) return rc;
+    if ((rc = tap("attn_norm", l, c->xn, (int64_t)n * d))) return rc;
+    if ((rc = gemv(L.wqkv, c->xn, d, c->qkv, qkv_w, EPI_STORE))) return rc;
+    if ((rc = tap("qkv", l, c->qkv, (int64_t)n * qkv_w))) return rc;
+    if ((rc = launch_rope_kv(c->qkv, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->rope, c->q, c->kc[l], c->vc[l],
+                             c->st_d, c->n_ctx, s)))
+      return rc;
+    if ((rc = tap("q_rope", l, c->q, (int64_t)n * m->nh_l * hd))) return rc;
+    if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->vc[l], c->st_d,
+                               c->n_ctx, kAttnChunk, c->part_o, c->part_ml, c->att, s)))
+      return rc;
+    if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
+    if ((rc = gemv(L.wo, c->att, (int64_t)m->nh_l * hd, c->delta, d, EPI_STORE))) return rc;
+    if (m->tp_size > 1) B2_NCCL_TRY(ncclAllReduce(c->delta, c->delta, (size_t)n * d, ncclFloat, ncclSum, m->comm, s));
+    if ((rc = tap("attn_proj", l, c->delta, (int64_t)n * d))) return rc;
+    if ((rc = launch_add_rmsnorm(c->x, c->delta, L.ffn_norm, c->xn, n, d, m->eps, s))) return rc;
+    if ((rc = tap("ffn_norm", l, c->xn, (int64_t)n * d))) return rc;
+    if ((rc = gemv(L.wgu, c->xn, d, c->h, m->ff_l, EPI_SWIGLU))) return rc;
+    if ((rc = tap("ffn_act", l, c->h, (int64_t)n * m->ff_l))) return rc;
+    if ((rc = gemv(L.wdown, c->h, m->ff_l, c->delta, d, EPI_STORE))) return rc;
+    if (m->tp_size > 1) B2_NCCL_TRY(ncclAllReduce(c->delta, c->delta, (size_t)n * d, ncclFloat, ncclSum, m->comm, s));
+    if ((rc = tap("ffn_out", l, c->delta, (int64_t)n * d))) return rc;
+  }
+  if ((rc = launch_add_rmsnorm(c->x, c->delta, m->out_norm, c->xn, n, d, m->eps, s))) return rc;
+  if ((rc = tap("result_norm", -1, c->xn, (int64_t)n * d))) return rc;
+  if (!with_logits) return B2_OK;
+  float* out = m->tp_size > 1 ? c->logits_l : c->logits;
+  if ((rc = gemv(m->head, c->xn, d, out, m->v_l, EPI_STORE))) return rc;
+  if (m->tp_size > 1)
+    B2_NCCL_TRY(ncclAllGather(c->logits_l, c->logits, (size_t)n * m->v_l, ncclFloat, m->comm, s));
+  return launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s);
+}
+
+int run_step(b2_context* c, int n, bool with_logits) {
+  if (!c->use_graph || c->eval_cb) return enqueue_step(c, n, with_logits);
+  cudaGraphExec_t& g = c->graphs[n][with_logits ? 1 : 0];
+  if (!g) {
+    B2_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_step(c, n, with_logits);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    B2_CUDA_TRY(e);
+    const cudaError_t ei = cudaGraphInstantiate(&g, graph, 0);
+    cudaGraphDestroy(graph);
+    B2_CUDA_TRY(ei);
+  }
+  B2_CUDA_TRY(cudaGraphLaunch(g, c->stream));
+  return B2_OK;
+}
+
+int check_status(b2_context* c) {
+  int st = 0;
+  B2_CUDA_TRY(cudaMemcpyAsync(&st, c->status, 4, cudaMemcpyDeviceToHost, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (st != 0) {
+    cudaMemsetAsync(c->status, 0, 4, c->stream);
+    set_error("device wait timed out (status %d)", st);
+    return B2_ERR_TIMEOUT;
+  }
+  return B2_OK;
+}
+
+int decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32_t* seq, int n, int want_logits) {
+  b2_model* m = c->model;
+  B2_CUDA_TRY(cudaSetDevice(m->device));
+  B2_CHECK_ARG(tokens && n > 0, "decode arguments");
+  // Validate: every token appends to its sequence at the next position.
+  std::vector<int> next(c->n_past);
+  std::vector<int32_t> pv(n), sv(n);
+  for (int i = 0; i < n; ++i) {
+    const int s = seq ? seq[i] : 0;
+    if (s < 0 || s >= c->n_seq) {
+      set_error("decode: sequence id %d out of range", s);
+      return B2_ERR_INVALID;
+    }
+    const int p = pos ? pos[i] : next[s];
+    if (p != next[s]) {
+      set_error("decode: token %d of sequence %d at position %d, expected %d", i, s, p, next[s]);
+      return B2_ERR_INVALID;
+    }
+    if (p >= c->n_ctx) return B2_NO_KV_SLOT;
+    next[s] = p + 1;
+    pv[i] = p;
+    sv[i] = s;
+  }
+  // Steps of up to kStepMax tokens; a step never holds two tokens of one
+  // sequence out of order (they are consecutive and written before the
+  // step's attention reads them).
+  int i0 = 0;
+  c->last_n = 0;
+  c->last_logits = false;
+  while (i0 < n) {
+    if (c->abort_cb && c->abort_cb(c->abort_user)) return B2_ABORTED;
+    const int k = std::min(kStepMax, n - i0);
+    const bool last = i0 + k == n;
+    const bool with_logits = want_logits == 1 || (want_logits == 2 && last);
+    // Two pinned staging slots: a slot is rewritten only after the copies
+    // that read it two steps ago have completed.
+    const int slot = c->in_slot;
+    c->in_slot ^= 1;
+    B2_CUDA_TRY(cudaEventSynchronize(c->in_ev[slot]));
+    int32_t* hs = c->in_h + slot * 3 * kStepMax;
+    for (int i = 0; i < k; ++i) {
+      hs[i] = tokens[i0 + i];
+      hs[kStepMax + i] = pv[i0 + i];
+      hs[2 * kStepMax + i] = sv[i0 + i];
+    }
+    B2_CUDA_TRY(cudaMemcpyAsync(c->tok_d, hs, k * 4, cudaMemcpyHostToDevice, c->stream));
+    B2_CUDA_TRY(cudaMemcpyAsync(c->pos_d, hs + kStepMax, k * 4, cudaMemcpyHostToDevice, c->stream));
+    B2_CUDA_TRY(cudaMemcpyAsync(c->seq_d, hs + 2 * kStepMax, k * 4, cudaMemcpyHostToDevice, c->stream));
+    B2_CUDA_TRY(cudaEventRecord(c->in_ev[slot], c->stream));
+    int rc = run_step(c, k, with_logits);
+    if (rc) return rc;
+    c->last_n = k;
+    c->last_logits = with_logits;
+    i0 += k;
+  }
+  for (int s = 0; s < c->n_seq; ++s) c->n_past[s] = next[s];
+  return B2_OK;
+}
+
+// Milda's shift (seq_rm [p0,p1) then seq_add(p1, end, -(p1-p0))), applied
+// when the add arrives.  Fast path: p0 is the start of the ring (the pinned
+// prefix length) — rotate the kept K in place and advance the ring head.
+// Otherwise rows are compacted with the same rotation.
+int kv_shift(b2_context* c, int s, int p0, int p1) {
+  b2_model* m = c->model;
+  const int n_past = c->n_past[s];
+  const int nd = p1 - p0;
+  if (nd <= 0) return B2_OK;
+  KvSeqState& st = c->st[s];
+  const bool fresh = st.ring_head == 0 && st.n_keep == 0;
+  if (fresh) st.n_keep = p0;
+  std::vector<float> cs(m->head_dim);
+  rope_table(m->theta, m->head_dim, -nd, 1, cs.data());
+  B2_CUDA_TRY(cudaMemcpyAsync(c->shift_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
+  int rc = B2_OK;
+  if (p0 == st.n_keep) {
+    for (int l = 0; l < m->n_layer && !rc; ++l)
+      rc = launch_kv_shift(c->kc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p1, n_past, c->shift_cs, c->stream);
+    const int ring = c->n_ctx - st.n_keep;
+    st.ring_head = ring > 0 ? (st.ring_head + nd) % ring : 0;
+  } else {
+    for (int l = 0; l < m->n_layer && !rc; ++l)
+      rc = launch_kv_compact(c->kc[l], c->vc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p0, p1, n_past - p1,
+                             c->shift_cs, c->stream);
+  }
+  if (rc) return rc;
+  c->n_past[s] = n_past - nd;
+  B2_CUDA_TRY(cudaMemcpyAsync(c->st_d + s, &st, sizeof(KvSeqState), cudaMemcpyHostToDevice, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return B2_OK;
+}
+
+// Pending middle removals per sequence (seq_rm waiting for its seq_add).
+struct Pending {
+  int p0 = -1, p1 = -1;
+};
+thread_local std::vector<std::pair<const b2_context*, std::vector<Pending>>> g_pending;
+std::vector<Pending>& pending_for(const b2_context* c) {
+  for (auto& e : g_pending)
+    if (e.first == c) return e.second;
+  g_pending.push_back({c, std::vector<Pending>(c->n_seq)});
+  return g_pending.back().second;
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+int b2_gguf_write_synthetic_llama(const b2_llama_hparams* hp, const char* path, int n_threads) {
+  B2_CHECK_ARG(hp && path, "synthetic llama arguments");
+  return write_synthetic_llama(*hp, path, n_threads);
+}
+
+void b2_model_default_params(b2_model_params* p) {
+  if (!p) return;
+  p->device = -1;
+  p->tp_rank = 0;
+  p->tp_size = 1;
+  p->nccl_id = nullptr;
+}
+
+int b2_nccl_unique_id(void* out) {
+  B2_CHECK_ARG(out, "out");
+  ncclUniqueId id;
+  B2_NCCL_TRY(ncclGetUniqueId(&id));
+  memcpy(out, &id, sizeof id);
+  return B2_OK;
+}
+
+int b2_model_load(const char* path, const b2_model_params* params, b2_model** out) {
+  B2_CHECK_ARG(path && out, "model_load arguments");
+  *out = nullptr;
+  b2_model_params p;
+  b2_model_default_params(&p);
+  if (params) p = *params;
+  b2_model* m = new (std::nothrow) b2_model;
+  if (!m) return B2_ERR_OOM;
+  int rc;
+  try {
+    rc = load_model(m, path, &p);
+  } catch (const std::bad_alloc&) {
+    set_error("model load: host out of memory");
+    rc = B2_ERR_OOM;
+  }
+  if (rc) {
+    delete m;
+    return rc;
+  }
+  *out = m;
+  return B2_OK;
+}
+
+int b2_model_free(b2_model* m) {
+  delete m;
+  return B2_OK;
+}
+
+int b2_model_info(const b2_model* m, int32_t* out, int32_t n) {
+  B2_CHECK_ARG(m && out, "model_info arguments");
+  const int32_t v[12] = {m->n_layer, m->n_embd,   m->n_ff,        m->n_head,  m->n_head_kv, m->n_vocab,
+                         m->head_dim, m->n_ctx_train, m->wtype, m->out_type, m->tp_rank,  m->tp_size};
+  for (int i = 0; i < n && i < 12; ++i) out[i] = v[i];
+  return B2_OK;
+}
+
+int b2_model_device_bytes(const b2_model* m, int64_t* bytes) {
+  B2_CHECK_ARG(m && bytes, "model_device_bytes arguments");
+  *bytes = m->device_bytes;
+  return B2_OK;
+}
+
+void b2_context_default_params(b2_context_params* p) {
+  if (!p) return;
+  p->n_ctx = 4096;
+  p->n_seq_max = 1;
+  p->use_graph = 1;
+}
+
+int b2_context_create(b2_model* m, const b2_context_params* params, b2_context** out) {
+  B2_CHECK_ARG(m && out, "context_create arguments");
+  *out = nullptr;
+  b2_context_params p;
+  b2_context_default_params(&p);
+  if (params) p = *params;
+  B2_CHECK_ARG(p.n_ctx > 0 && p.n_seq_max > 0, "n_ctx and n_seq_max must be positive");
+  b2_context* c = new (std::nothrow) b2_context;
+  if (!c) return B2_ERR_OOM;
+  int rc;
+  try {
+    rc = create_context(c, m, &p);
+  } catch (const std::bad_alloc&) {
+    rc = B2_ERR_OOM;
+  }
+  if (rc) {
+    delete c;
+    return rc;
+  }
+  *out = c;
+  return B2_OK;
+}
+
+int b2_context_free(b2_context* c) {
+  for (auto it = g_pending.begin(); it != g_pending.end(); ++it)
+    if (it->first == c) {
+      g_pending.erase(it);
+      break;
+    }
+  delete c;
+  return B2_OK;
+}
+
+int b2_context_stream(b2_context* c, void** stream) {
+  B2_CHECK_ARG(c && stream, "context_stream arguments");
+  *stream = c->stream;
+  return B2_OK;
+}
+
+int b2_decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32_t* seq, int32_t n_tokens,
+              int32_t want_logits) {
+  B2_CHECK_ARG(c, "context");
+  for (const auto& p : pending_for(c))
+    if (p.p0 >= 0) {
+      set_error("decode: a KV removal is waiting for its position shift (b2_kv_seq_add)");
+      return B2_ERR_INVALID;
+    }
+  return decode(c, tokens, pos, seq, n_tokens, want_logits);
+}
+
+int b2_get_logits(b2_context* c, int32_t i, float* out, int64_t n) {
+  B2_CHECK_ARG(c && out, "get_logits arguments");
+  B2_CHECK_ARG(c->last_logits, "the last decode computed no logits");
+  if (i < 0) i += c->last_n;
+  B2_CHECK_ARG(i >= 0 && i < c->last_n, "logits row out of range");
+  b2_model* m = c->model;
+  B2_CUDA_TRY(cudaSetDevice(m->device));
+  const int64_t cnt = std::min<int64_t>(n, m->n_vocab);
+  const int64_t vl = m->v_l;
+  // gathered layout [tp][n_tok][v_l]
+  for (int r = 0; r < m->tp_size && r * vl < cnt; ++r) {
+    const int64_t len = std::min<int64_t>(vl, cnt - r * vl);
+    B2_CUDA_TRY(cudaMemcpyAsync(out + r * vl, c->logits + ((int64_t)r * c->last_n + i) * vl, len * 4,
+                                cudaMemcpyDeviceToHost, c->stream));
+  }
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return check_status(c);
+}
+
+int b2_get_argmax(b2_context* c, int32_t* ids, float* top1, float* margin, int32_t n) {
+  B2_CHECK_ARG(c && ids, "get_argmax arguments");
+  B2_CHECK_ARG(c->last_logits, "the last decode computed no logits");
+  B2_CHECK_ARG(n >= c->last_n, "output arrays shorter than the last batch");
+  B2_CUDA_TRY(cudaSetDevice(c->model->device));
+  float top[2 * kStepMax];
+  B2_CUDA_TRY(cudaMemcpyAsync(ids, c->ids, c->last_n * 4, cudaMemcpyDeviceToHost, c->stream));
+  B2_CUDA_TRY(cudaMemcpyAsync(top, c->top, c->last_n * 8, cudaMemcpyDeviceToHost, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  for (int i = 0; i < c->last_n; ++i) {
+    if (top1) top1[i] = top[2 * i];
+    if (margin) margin[i] = top[2 * i + 1];
+  }
+  return check_status(c);
+}
+
+int b2_synchronize_context(b2_context* c) {
+  B2_CHECK_ARG(c, "context");
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return check_status(c);
+}
+
+int b2_kv_clear(b2_context* c) {
+  B2_CHECK_ARG(c, "context");
+  B2_CUDA_TRY(cudaSetDevice(c->model->device));
+  for (int s = 0; s < c->n_seq; ++s) {
+    c->st[s] = KvSeqState{0, 0};
+    c->n_past[s] = 0;
+  }
+  for (auto& p : pending_for(c)) p = Pending{};
+  B2_CUDA_TRY(cudaMemcpyAsync(c->st_d, c->st.data(), c->n_seq * sizeof(KvSeqState), cudaMemcpyHostToDevice, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return B2_OK;
+}
+
+int b2_kv_seq_rm(b2_context* c, int32_t seq, int32_t p0, int32_t p1) {
+  B2_CHECK_ARG(c && seq >= 0 && seq < c->n_seq, "kv_seq_rm arguments");
+  const int n_past = c->n_past[seq];
+  if (p0 < 0) p0 = 0;
+  if (p1 < 0 || p1 > n_past) p1 = n_past;
+  if (p0 >= p1) return B2_OK;
+  if (p1 == n_past) {   // suffix: truncate
+    c->n_past[seq] = p0;
+    return B2_OK;
+  }
+  pending_for(c)[seq] = Pending{p0, p1};
+  return B2_OK;
+}
+
+int b2_kv_seq_add(b2_context* c, int32_t seq, int32_t p0, int32_t p1, int32_t delta) {
+  B2_CHECK_ARG(c && seq >= 0 && seq < c->n_seq, "kv_seq_add arguments");
+  Pending& pd = pending_for(c)[seq];
+  if (p1 < 0) p1 = c->n_past[seq];
+  if (pd.p0 < 0 || p0 != pd.p1 || p1 != c->n_past[seq] || delta != -(pd.p1 - pd.p0)) {
+    set_error("kv_seq_add: only the shift that closes a preceding kv_seq_rm gap is supported");
+    return B2_ERR_UNSUPPORTED;
+  }
+  B2_CUDA_TRY(cudaSetDevice(c->model->device));
+  const int rc = kv_shift(c, seq, pd.p0, pd.p1);
+  pd = Pending{};
+  return rc;
+}
+
+int b2_kv_seq_pos_max(b2_context* c, int32_t seq, int32_t* pos) {
+  B2_CHECK_ARG(c && pos && seq >= 0 && seq < c->n_seq, "kv_seq_pos_max arguments");
+  *pos = c->n_past[seq] - 1;
+  return B2_OK;
+}
+
+int b2_set_eval_callback(b2_context* c, b2_eval_callback cb, void* user) {
+  B2_CHECK_ARG(c, "context");
+  c->eval_cb = cb;
+  c->eval_user = user;
+  return B2_OK;
+}
+
+int b2_set_abort_callback(b2_context* c, b2_abort_callback cb, void* user) {
+  B2_CHECK_ARG(c, "context");
+  c->abort_cb = cb;
+  c->abort_user = user;
+  return B2_OK;
+}
+
+}  // extern "C"

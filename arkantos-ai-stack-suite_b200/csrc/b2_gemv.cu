@@ -452,14 +452,31 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
   }
 }
 
+// 227 KB opt-in per block, less 1 KB for the kernel's static shared memory.
+constexpr int kSmemCap = 227 * 1024 - 1024;
+
+template <int WT, int B>
+int set_smem_attr() {
+  B2_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<WT, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap));
+  return B2_OK;
+}
+
+template <int WT>
+int set_smem_attr_all() {
+  int rc = set_smem_attr<WT, 1>();
+  if (!rc) rc = set_smem_attr<WT, 2>();
+  if (!rc) rc = set_smem_attr<WT, 3>();
+  if (!rc) rc = set_smem_attr<WT, 4>();
+  if (!rc) rc = set_smem_attr<WT, 5>();
+  if (!rc) rc = set_smem_attr<WT, 6>();
+  if (!rc) rc = set_smem_attr<WT, 7>();
+  if (!rc) rc = set_smem_attr<WT, 8>();
+  return rc;
+}
+
 template <int WT, int B>
 int launch_t(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
   auto kern = gemv_kernel<WT, B>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured = smem;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -492,7 +509,22 @@ int launch_w(const GemvP& p, int B, int grid, size_t smem, cudaStream_t s) {
 
 }  // namespace
 
+int prepare_gemv_kernels() {
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return B2_OK;
+  int rc = set_smem_attr_all<B2_Q4_0>();
+  if (!rc) rc = set_smem_attr_all<B2_Q8_0>();
+  if (!rc) rc = set_smem_attr_all<B2_Q4_K>();
+  if (!rc) rc = set_smem_attr_all<B2_Q6_K>();
+  if (!rc && dev >= 0 && dev < 64) done[dev] = true;
+  return rc;
+}
+
 int launch_gemv(const GemvArgs& a, cudaStream_t s) {
+  int prc = prepare_gemv_kernels();
+  if (prc) return prc;
   const QMatrix& w = *a.w;
   B2_CHECK_ARG(a.n_tok >= 1 && a.n_tok <= kMaxTok, "n_tok must be in [1, 8]");
   B2_CHECK_ARG(a.row_begin >= 0 && a.row_end <= w.n_rows && a.row_begin <= a.row_end, "row range");
@@ -534,7 +566,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   while (rg > 1 && (size_t)rg * row_b > 24 * 1024) rg /= 2;
   if (a.epilogue == EPI_SWIGLU && rg < 2) rg = 2;
   const size_t stage = ((size_t)rg * row_b + 127) / 128 * 128;
-  const size_t smem_cap = 227 * 1024;
+  const size_t smem_cap = kSmemCap;
   const size_t fixed = kBarBytes + ((act_bytes + 127) / 128 * 128);
   if (fixed + 2 * stage > smem_cap) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);

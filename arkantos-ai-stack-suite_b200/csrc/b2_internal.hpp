@@ -114,6 +114,9 @@ struct GemvArgs {
   int* status;          // device status word (bounded waits), may be nullptr
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
+// Sets the large dynamic shared-memory limit of every GEMV instantiation on
+// the current device (done outside graph capture).
+int prepare_gemv_kernels();
 int launch_quantize_act(int act_type, const float* x, int64_t x_stride, int n_tok, int64_t k, ActQ& out,
                         cudaStream_t s);
 int launch_act_to_blocks(const ActQ& a, int64_t k, void* blocks, cudaStream_t s);

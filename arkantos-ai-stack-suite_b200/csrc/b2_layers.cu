@@ -80,7 +80,13 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, int n_vocab, in
 }
 
 // ---- residual add + RMSNorm ----------------------------------------------------------------
-// x += delta (when delta != nullptr); out = (x · 1/sqrt(Σx²/n + eps)) · w.
+// x += delta (when delta != nullptr); out = (x·scale)·w with the squares
+// rounded to fp32 and summed in double, mean = (float)(sum/n),
+// scale = 1/sqrtf(mean + eps) — ggml's rms_norm (llama.cpp CPU backend).
+// A double sum of 2^12..2^15 fp32 squares is exact to far below fp32
+// resolution, so the tree order here rounds to the same mean as the
+// sequential CPU sum (bit-identical outputs, which keeps the following Q8
+// activation codes identical even on exact rounding ties).
 __global__ void add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                    float* __restrict__ out, int n, float eps) {
   pdl_wait();
@@ -88,35 +94,37 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const float* __restric
   const int b = blockIdx.x;
   float* xr = x + (int64_t)b * n;
   const float* dr = delta ? delta + (int64_t)b * n : nullptr;
-  float ss = 0.0f;
+  double ss = 0.0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float v = xr[i];
     if (dr) {
       v = __fadd_rn(v, dr[i]);
       xr[i] = v;
     }
-    ss = __fadd_rn(ss, __fmul_rn(v, v));
+    ss += (double)__fmul_rn(v, v);
   }
-  __shared__ float red[32];
-  ss = warp_sum(ss);
+  __shared__ double red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-    v = warp_sum(v);
+    double v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (threadIdx.x == 0) red[0] = v;
   }
   __syncthreads();
-  const float mean_sq = __fadd_rn(__fdiv_rn(red[0], (float)n), eps);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(mean_sq));
+  const float mean = __double2float_rn(__ddiv_rn(red[0], (double)n));
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   float* orow = out + (int64_t)b * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
 }
 
 // ---- RoPE + KV store -------------------------------------------------------------------------
 __device__ __forceinline__ int64_t kv_slot(const KvSeqState& st, int p, int cap) {
-  if (p < st.n_keep) return p;
   const int ring = cap - st.n_keep;
+  if (p < st.n_keep || ring <= 0) return p;
   int r = (st.ring_head + (p - st.n_keep)) % ring;
   return st.n_keep + r;
 }

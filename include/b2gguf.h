@@ -164,6 +164,153 @@ B2_API int b2_gemv_host(const b2_qmatrix* w, const float* x_host, int n_tok, flo
  * device int32 [blocks] (out_m only for Q4_K, may be NULL otherwise). */
 B2_API int b2_block_dots(const b2_qmatrix* w, int64_t row, const float* x, int32_t* out_i, int32_t* out_m, void* stream);
 
+
+
+/* Token-embedding row dequantization (Singularity/src/core/cortex_a5_engine.cpp:1066-1105):
+ * out[i][:] = dequant(table row tokens[i]) for a GGUF table of `type`
+ * (F32, F16, Q4_0, Q8_0, Q4_K, Q6_K) with rows of n_embd values; ids outside
+ * [0, n_vocab) read row 0.  tokens device int32 [n_tok], out fp32 [n_tok][n_embd]. */
+B2_API int b2_embed(int type, const void* table, int n_vocab, int n_embd, const int32_t* tokens, int n_tok,
+                    float* out, void* stream);
+
+/* Residual add + RMSNorm, one row per token (ref_rmsnorm_f32,
+ * Singularity/tests/test_and_bench_a5.cpp:247-258; the residual adds of
+ * Singularity/src/core/cortex_a5_engine.cpp:1259-1261, 1281-1283):
+ * x += delta (delta may be NULL), out = (x·1/sqrt(mean(x²)+eps))·w.
+ * x, delta, out fp32 [n_rows][n], w fp32 [n]. */
+B2_API int b2_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_rows, int n, float eps,
+                      void* stream);
+
+/* RoPE (adjacent pairs, ref_rope_f32 test_and_bench_a5.cpp:280-293) on the
+ * q and k heads of fused qkv rows, k and v stored to an fp16 cache
+ * (cortex_a5_engine.cpp:1144-1203).  qkv fp32 [n_tok][(n_head+2·n_kv)·hd];
+ * rope fp32 [positions][hd] (b2_rope_table); pos, seq device int32 [n_tok];
+ * q_out fp32 [n_tok][n_head][hd]; k_cache / v_cache fp16
+ * [n_seq][n_kv][cap][hd], token written at [seq][·][pos]. */
+B2_API int b2_rope_kv_store(const float* qkv, int n_tok, int n_head, int n_kv, int head_dim, const int32_t* pos,
+                            const int32_t* seq, const float* rope, float* q_out, uint16_t* k_cache,
+                            uint16_t* v_cache, int cap, void* stream);
+
+/* Decode attention over the fp16 cache (cortex_a5_engine.cpp:1205-1254),
+ * split-K over positions: query i attends to positions 0..pos[i] of sequence
+ * seq[i] with its n_head/n_kv grouped heads.  q fp32 [n_q][n_head][hd],
+ * out fp32 [n_q][n_head][hd]; caches as above.  Partial results go to
+ * stream-ordered scratch allocated by the call. */
+B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
+                          const int32_t* seq, int n_q, int n_head, int n_kv, int head_dim, int cap, float* out,
+                          void* stream);
+
+/* The KV shift's re-rotation (Milda/src/engine.cpp:1642-1675): K rows of
+ * positions [p_begin, p_end) of sequence seq rotated in place by `delta`
+ * positions (fp16 -> fp32 -> rotate -> fp16 RNE). */
+B2_API int b2_kv_shift_k(uint16_t* k_cache, int seq, int n_kv, int head_dim, int cap, int p_begin, int p_end,
+                         int delta, float theta, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* GGUF model files                                                           */
+/* ------------------------------------------------------------------------ */
+
+/* Shape and types of a synthetic Llama-architecture GGUF (random weights). */
+typedef struct b2_llama_hparams {
+    int32_t  n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab, n_ctx_train;
+    float    rms_eps, rope_theta;
+    int32_t  wtype;       /* attention / FFN weights: Q4_0, Q8_0, Q4_K, Q6_K */
+    int32_t  embd_type;   /* token_embd.weight (also F32) */
+    int32_t  out_type;    /* output.weight, or -1 for a head tied to token_embd */
+    uint64_t seed;        /* weights N(0, w_std) from this seed */
+    float    w_std;
+} b2_llama_hparams;
+
+/* Writes a GGUF v3 file with llama metadata and tensors named as the engines
+ * bind them (Singularity/src/core/cortex_a5_engine.cpp:579-654), the weights
+ * quantized with b2_quantize_weights and norm weights set to 1.  This plays
+ * the part of the converter / quantizer that produces the engines' model
+ * files. */
+B2_API int b2_gguf_write_synthetic_llama(const b2_llama_hparams* hp, const char* path, int n_threads);
+
+/* ------------------------------------------------------------------------ */
+/* Engine (the llama.cpp calls Milda and Sutra make)                          */
+/* ------------------------------------------------------------------------ */
+
+typedef struct b2_model b2_model;
+typedef struct b2_context b2_context;
+
+#define B2_NCCL_ID_BYTES 128
+
+typedef struct b2_model_params {
+    int32_t     device;     /* CUDA device of this rank, -1 = current */
+    int32_t     tp_rank;    /* tensor-parallel rank of this process */
+    int32_t     tp_size;    /* tensor-parallel degree (1 = whole model here) */
+    const void* nccl_id;    /* B2_NCCL_ID_BYTES from b2_nccl_unique_id (rank 0),
+                               the same bytes on every rank; NULL when tp_size = 1 */
+} b2_model_params;
+
+/* llama_model_default_params (Milda/src/engine.cpp:897). */
+B2_API void b2_model_default_params(b2_model_params* p);
+B2_API int  b2_nccl_unique_id(void* out);
+/* llama_model_load_from_file (Milda/src/engine.cpp:919,
+ * Sutra/src/llm_backends.cpp:1540): parses the GGUF, uploads this rank's
+ * shard in the repacked layout.  All ranks of a TP group call it together. */
+B2_API int  b2_model_load(const char* path, const b2_model_params* params, b2_model** out);
+B2_API int  b2_model_free(b2_model* m);      /* llama_model_free */
+/* out[0..11]: n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab, head_dim,
+ * n_ctx_train, weight type, head type, tp_rank, tp_size
+ * (llama_model_n_layer / llama_vocab_n_tokens, Milda/src/engine.cpp:1150-1157). */
+B2_API int  b2_model_info(const b2_model* m, int32_t* out, int32_t n);
+B2_API int  b2_model_device_bytes(const b2_model* m, int64_t* bytes);
+
+typedef struct b2_context_params {
+    int32_t n_ctx;        /* KV positions per sequence (llama n_ctx) */
+    int32_t n_seq_max;    /* concurrent sequences (decode batch) */
+    int32_t use_graph;    /* replay each decode step as a CUDA graph */
+} b2_context_params;
+
+/* llama_context_default_params / llama_init_from_model
+ * (Milda/src/engine.cpp:1180-1206): fp16 KV cache. */
+B2_API void b2_context_default_params(b2_context_params* p);
+B2_API int  b2_context_create(b2_model* m, const b2_context_params* params, b2_context** out);
+B2_API int  b2_context_free(b2_context* c);   /* llama_free */
+/* The context's CUDA stream (for event timing by callers). */
+B2_API int  b2_context_stream(b2_context* c, void** stream);
+
+/* llama_decode over a llama_batch (Milda/src/engine.cpp:1539-1541, 2077-2081;
+ * Sutra/src/llm_backends.cpp:2544, 2714): token i at position pos[i] of
+ * sequence seq[i] (pos/seq NULL = next position of sequence 0).  Each token
+ * must extend its sequence at its next position.  want_logits: 0 none,
+ * 1 every token, 2 the last token of the call.  Returns 1 when a sequence is
+ * full (no KV slot), 2 when the abort callback asked to stop. */
+B2_API int b2_decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32_t* seq,
+                     int32_t n_tokens, int32_t want_logits);
+/* llama_get_logits_ith (Milda/src/engine.cpp:2019, Sutra/src/llm_backends.cpp:3335):
+ * fp32 logits of row i of the last decode step that computed logits. */
+B2_API int b2_get_logits(b2_context* c, int32_t i, float* out, int64_t n);
+/* Greedy pick on the device for every logits row of that step: token id,
+ * top-1 logit and top-1 − top-2 margin (NULL outputs are skipped). */
+B2_API int b2_get_argmax(b2_context* c, int32_t* ids, float* top1, float* margin, int32_t n);
+B2_API int b2_synchronize_context(b2_context* c);
+
+/* KV cache: llama_memory_clear / seq_rm / seq_add / seq_pos_max
+ * (Milda/src/engine.cpp:1650-1658, 1686, 2125-2148).  seq_rm of a suffix
+ * truncates; seq_rm of [p0,p1) followed by seq_add(p1, -1, -(p1-p0)) is
+ * Milda's in-place shift: K rows are re-rotated by the position delta. */
+B2_API int b2_kv_clear(b2_context* c);
+B2_API int b2_kv_seq_rm(b2_context* c, int32_t seq, int32_t p0, int32_t p1);
+B2_API int b2_kv_seq_add(b2_context* c, int32_t seq, int32_t p0, int32_t p1, int32_t delta);
+B2_API int b2_kv_seq_pos_max(b2_context* c, int32_t seq, int32_t* pos);
+
+/* Intermediate-tensor callback, the analogue of llama.cpp's cb_eval context
+ * parameter: when set, decode steps run without graph replay and after each
+ * op the callback receives the op name, layer (-1 outside layers), a device
+ * pointer and the number of fp32 values written (rows of the step's tokens).
+ * The stream is synchronized before the call.  NULL removes it. */
+typedef void (*b2_eval_callback)(const char* name, int32_t layer, const float* data, int64_t n, void* user);
+B2_API int b2_set_eval_callback(b2_context* c, b2_eval_callback cb, void* user);
+
+/* llama_set_abort_callback (Sutra/src/llm_backends.cpp:3017): polled between
+ * decode steps; non-zero stops the call with status 2. */
+typedef int (*b2_abort_callback)(void* user);
+B2_API int b2_set_abort_callback(b2_context* c, b2_abort_callback cb, void* user);
+
 #ifdef __cplusplus
 }
 #endif

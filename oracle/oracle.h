@@ -66,7 +66,8 @@ void orc_block_dots_q6_k_q8_k(int n, const void* x, const void* y, int32_t* isum
 void orc_dequantize_row(int type, const void* x, float* y, int k);
 
 /* Elementwise ops. */
-void orc_rmsnorm(const float* x, const float* w, float* out, int n, float eps);
+void orc_rmsnorm(const float* x, const float* w, float* out, int n, float eps);       /* Singularity ref */
+void orc_rmsnorm_ggml(const float* x, const float* w, float* out, int n, float eps);  /* ggml (double sum) */
 void orc_softmax(const float* x, float* out, int n);
 void orc_rope_pairs(float* x, const float* cos_sin, int head_dim, int n_heads);
 void orc_silu_mul(float* hb, const float* hb2, int n);
@@ -111,6 +112,9 @@ int  orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, flo
                               int n_threads, int n_layers_run);
 /* KV shift on one sequence: drop [p0, p1), re-rotate K of [p1, n_past). */
 int  orc_model_kv_shift(orc_model* m, int seq, int p0, int p1, int n_past);
+/* Per-op tap with the same names as the engine's evaluation callback. */
+typedef void (*orc_tap_fn)(const char* name, int layer, const float* data, long n, void* user);
+void orc_model_set_tap(orc_model* m, orc_tap_fn fn, void* user);
 /* Copy of the hidden state after the last forward (n_embd floats). */
 int  orc_model_hidden(const orc_model* m, float* out, int n);
 

@@ -51,6 +51,7 @@ def _load() -> ctypes.CDLL:
         "orc_block_dots_q6_k_q8_k": (None, [_i, _vp, _vp, _vp]),
         "orc_dequantize_row": (None, [_i, _vp, _vp, _i]),
         "orc_rmsnorm": (None, [_vp, _vp, _vp, _i, _f]),
+        "orc_rmsnorm_ggml": (None, [_vp, _vp, _vp, _i, _f]),
         "orc_softmax": (None, [_vp, _vp, _i]),
         "orc_rope_pairs": (None, [_vp, _vp, _i, _i]),
         "orc_silu_mul": (None, [_vp, _vp, _i]),
@@ -67,6 +68,7 @@ def _load() -> ctypes.CDLL:
         "orc_model_forward_layers": (_i, [_vp, _i, ctypes.c_int32, _i, _vp, _i, _i]),
         "orc_model_kv_shift": (_i, [_vp, _i, _i, _i, _i]),
         "orc_model_hidden": (_i, [_vp, _vp, _i]),
+        "orc_model_set_tap": (None, [_vp, _vp, _vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -166,6 +168,14 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     return out
 
 
+def rmsnorm_ggml(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.zeros_like(x)
+    lib.orc_rmsnorm_ggml(_p(x), _p(w), _p(out), x.size, eps)
+    return out
+
+
 def softmax(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32)
     out = np.zeros_like(x)
@@ -245,6 +255,20 @@ class Model:
         if rc != 0:
             raise RuntimeError(f"oracle forward rc={rc}")
         return out
+
+    TAP = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_long,
+                           ctypes.c_void_p)
+
+    def set_tap(self, fn) -> None:
+        """fn(name, layer, np.ndarray copy) after each op; None removes it."""
+        if fn is None:
+            self._tap = None
+            lib.orc_model_set_tap(self.h, None, None)
+            return
+        def cb(name, layer, data, n, user):
+            fn(name.decode(), layer, np.ctypeslib.as_array(data, shape=(n,)).copy())
+        self._tap = self.TAP(cb)
+        lib.orc_model_set_tap(self.h, ctypes.cast(self._tap, ctypes.c_void_p), None)
 
     def hidden(self) -> np.ndarray:
         out = np.zeros(self.dim, np.float32)

@@ -3,9 +3,11 @@
  *
  * GGUF v3 parse (Singularity/src/core/cortex_a5_engine.cpp:429-659) and the
  * Llama decoder forward in Singularity's order
- * (Singularity/src/core/cortex_a5_engine.cpp:1029-1293), with two documented
- * departures: RoPE uses the θ^(−2i/hd) table for llama (adjacent pairs),
- * and K-quant weights pair with Q8_K activations as in ggml's CPU backend.
+ * (Singularity/src/core/cortex_a5_engine.cpp:1029-1293), with three
+ * documented departures toward llama.cpp, the engines' actual CPU path:
+ * RoPE uses the θ^(−2i/hd) table for llama (adjacent pairs), K-quant weights
+ * pair with Q8_K activations, and RMSNorm sums its squares in double as
+ * ggml's rms_norm does (orc_rmsnorm_ggml).
  */
 #include "oracle.h"
 
@@ -44,7 +46,15 @@ struct orc_model {
     float *x, *xb, *xb2, *q, *k, *v, *hb, *hb2;
     void* xq;
     float* rope;
+    orc_tap_fn tap;
+    void* tap_user;
 };
+
+void orc_model_set_tap(orc_model* m, orc_tap_fn fn, void* user) {
+    m->tap = fn;
+    m->tap_user = user;
+}
+#define TAP(name, layer, ptr, n) do { if (m->tap) m->tap(name, layer, ptr, (long)(n), m->tap_user); } while (0)
 
 static uint32_t rd_u32(const uint8_t* p) { uint32_t v; memcpy(&v, p, 4); return v; }
 static uint64_t rd_u64(const uint8_t* p) { uint64_t v; memcpy(&v, p, 8); return v; }
@@ -287,30 +297,42 @@ int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, floa
     const float* cs = m->rope + (size_t)pos * hd;
     const size_t seq_stride = (size_t)m->n_layers * m->n_ctx * kv_dim;
     const int nl = n_layers_run < m->n_layers ? n_layers_run : m->n_layers;
+    TAP("embed", -1, m->x, dim);
     for (int l = 0; l < nl; ++l) {
         const orc_layer* L = &m->layers[l];
-        orc_rmsnorm(m->x, (const float*)L->attn_norm.data, m->xb, dim, m->eps);      /* :1121 */
+        orc_rmsnorm_ggml(m->x, (const float*)L->attn_norm.data, m->xb, dim, m->eps); /* :1121 */
+        TAP("attn_norm", l, m->xb, dim);
         proj(m, &L->wq, m->xb, m->q, nt);                                             /* :1129 */
         proj(m, &L->wk, m->xb, m->k, nt);
         proj(m, &L->wv, m->xb, m->v, nt);
+        TAP("q", l, m->q, dim);
+        TAP("k", l, m->k, kv_dim);
+        TAP("v", l, m->v, kv_dim);
         orc_rope_pairs(m->q, cs, hd, m->n_heads);                                     /* :1187 */
         orc_rope_pairs(m->k, cs, hd, nkv);
+        TAP("q_rope", l, m->q, dim);
         uint16_t* kc = m->kc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
         uint16_t* vc = m->vc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
         orc_fp32_to_fp16_row(m->k, kc + (size_t)pos * kv_dim, kv_dim);                /* :1195 */
         orc_fp32_to_fp16_row(m->v, vc + (size_t)pos * kv_dim, kv_dim);
         orc_attn_decode(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);   /* :1205 */
+        TAP("attn_out", l, m->xb, dim);
         proj(m, &L->wo, m->xb, m->xb2, nt);                                           /* :1256 */
+        TAP("attn_proj", l, m->xb2, dim);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb2[i];
-        orc_rmsnorm(m->x, (const float*)L->ffn_norm.data, m->xb, dim, m->eps);        /* :1264 */
+        orc_rmsnorm_ggml(m->x, (const float*)L->ffn_norm.data, m->xb, dim, m->eps);  /* :1264 */
+        TAP("ffn_norm", l, m->xb, dim);
         proj(m, &L->w1, m->xb, m->hb, nt);                                            /* :1270 */
         proj(m, &L->w3, m->xb, m->hb2, nt);
         orc_silu_mul(m->hb, m->hb2, m->hidden);                                       /* :1277 */
+        TAP("ffn_act", l, m->hb, m->hidden);
         proj(m, &L->w2, m->hb, m->xb, nt);                                            /* :1280 */
+        TAP("ffn_out", l, m->xb, dim);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb[i];
     }
     if (!logits) return 0;
-    orc_rmsnorm(m->x, (const float*)m->out_norm.data, m->xb, dim, m->eps);            /* :1287 */
+    orc_rmsnorm_ggml(m->x, (const float*)m->out_norm.data, m->xb, dim, m->eps);      /* :1287 */
+    TAP("result_norm", -1, m->xb, dim);
     proj(m, &m->out, m->xb, logits, nt);                                              /* :1292 */
     return 0;
 }

@@ -411,6 +411,20 @@ void orc_rmsnorm(const float* x, const float* w, float* out, int n, float eps) {
     for (int i = 0; i < n; ++i) out[i] = (x[i] * inv_rms) * w[i];
 }
 
+/* RMSNorm as ggml's CPU backend computes it (llama.cpp
+ * ggml_compute_forward_rms_norm_f32, version unpinned, not vendored): the
+ * squares are rounded to fp32 and summed in double, mean = (float)(sum / n),
+ * scale = 1/sqrtf(mean + eps), out = (x·scale)·w (the weight is a separate
+ * ggml_mul).  The double sum makes the result independent of summation
+ * order, so a parallel reduction reproduces it bit for bit. */
+void orc_rmsnorm_ggml(const float* x, const float* w, float* out, int n, float eps) {
+    double sum = 0.0;
+    for (int i = 0; i < n; ++i) sum += (double)(x[i] * x[i]);
+    const float mean = (float)(sum / (double)n);
+    const float scale = 1.0f / sqrtf(mean + eps);
+    for (int i = 0; i < n; ++i) out[i] = (x[i] * scale) * w[i];
+}
+
 /* Follows ref_softmax_f32, Singularity/tests/test_and_bench_a5.cpp:260-278. */
 void orc_softmax(const float* x, float* out, int n) {
     float max_val = x[0];

@@ -1,0 +1,54 @@
+"""Model files on the host (no GPU): the library's GGUF writer read back by
+gguf-py 0.19.0 and by the oracle's parser; the oracle forward on it."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+b2 = pytest.importorskip("b2gguf")
+gguf = pytest.importorskip("gguf")
+
+
+@pytest.fixture(scope="module")
+def tiny_gguf(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("m") / "tiny_q4k.gguf")
+    b2.write_synthetic_llama(path, n_layer=2, n_embd=256, n_ff=768, n_head=4, n_head_kv=2, n_vocab=512,
+                             wtype=b2.Q4_K, out_type=b2.Q6_K, seed=5, rope_theta=500000.0)
+    return path
+
+
+def test_writer_metadata_and_tensors_read_by_gguf_py(tiny_gguf):
+    r = gguf.GGUFReader(tiny_gguf)
+    f = r.fields
+    assert bytes(f["general.architecture"].parts[-1]).decode() == "llama"
+    assert int(f["llama.block_count"].parts[-1][0]) == 2
+    assert int(f["llama.attention.head_count_kv"].parts[-1][0]) == 2
+    assert float(f["llama.rope.freq_base"].parts[-1][0]) == 500000.0
+    names = {t.name: t for t in r.tensors}
+    assert names["output.weight"].tensor_type.name == "Q6_K"
+    assert names["blk.1.ffn_down.weight"].tensor_type.name == "Q4_K"
+    assert list(names["blk.1.ffn_down.weight"].shape) == [768, 256]
+    # gguf-py's dequantization and the oracle's agree bit for bit on the file's bytes
+    for name, t in (("blk.0.attn_q.weight", O.Q4_K), ("output.weight", O.Q6_K)):
+        raw = np.ascontiguousarray(names[name].data).view(np.uint8)
+        k = int(names[name].shape[0])
+        ref = gguf.dequantize(raw, names[name].tensor_type).reshape(-1, k)
+        got = O.dequantize(t, raw, k)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        assert 0.015 < float(np.std(got)) < 0.025   # N(0, 0.02) weights
+
+
+def test_oracle_parses_and_runs(tiny_gguf):
+    m = O.Model(tiny_gguf)
+    assert (m.n_layers, m.dim, m.hidden, m.n_heads, m.n_kv, m.vocab, m.head_dim) == (2, 256, 768, 4, 2, 512, 64)
+    m.init_cache(1, 64)
+    for p, t in enumerate([1, 7, 300]):
+        lg = m.forward(0, t, p, logits=(p == 2))
+    assert lg.shape == (512,) and np.all(np.isfinite(lg))
+
+
+def test_writer_is_deterministic(tmp_path):
+    a, b = str(tmp_path / "a.gguf"), str(tmp_path / "b.gguf")
+    for p in (a, b):
+        b2.write_synthetic_llama(p, 1, 64, 128, 2, 1, 64, b2.Q4_0, seed=3)
+    assert open(a, "rb").read() == open(b, "rb").read()

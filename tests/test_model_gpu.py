@@ -1,0 +1,158 @@
+"""Model-level parity on the GPU through the C ABI: logits of every step
+against the oracle forward (Singularity's forward order), greedy tokens,
+batched sequences and the in-place KV shift.
+
+Tolerance on logits: |gpu − oracle| <= 1e-3 · max(|oracle|, rms(row)).
+Greedy tokens must agree wherever the oracle's top-2 margin exceeds 1e-3 of
+the row's scale."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+b2 = pytest.importorskip("b2gguf")
+
+TOL = 1e-3
+
+
+def logits_close(got, want, tol=TOL):
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    bound = tol * np.maximum(np.abs(want), rms)
+    return bool(np.all(np.abs(got - want) <= bound)), float(np.max(np.abs(got - want)) / max(rms, 1e-30))
+
+
+MODELS = {
+    # name: (layers, d, ff, heads, kv heads, vocab, wtype, out type, theta)
+    "q4_0_hd64": (2, 256, 768, 4, 2, 512, 2, 2, 10000.0),
+    "q4_k_hd128": (2, 512, 1024, 4, 1, 768, 12, 14, 500000.0),
+    "q8_0_hd64": (2, 256, 512, 4, 4, 256, 8, 8, 10000.0),
+}
+
+
+@pytest.fixture(scope="module", params=sorted(MODELS))
+def model_file(request, tmp_path_factory):
+    L, d, ff, nh, nkv, V, wt, ot, theta = MODELS[request.param]
+    path = str(tmp_path_factory.mktemp("m") / f"{request.param}.gguf")
+    b2.write_synthetic_llama(path, L, d, ff, nh, nkv, V, wt, out_type=ot, seed=11, rope_theta=theta)
+    return path
+
+
+def oracle_run(path, n_seq, n_ctx):
+    m = O.Model(path)
+    m.init_cache(n_seq, n_ctx)
+    return m
+
+
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_prefill_and_greedy_decode_match_oracle(model_file, use_graph):
+    rng = np.random.default_rng(0)
+    om = oracle_run(model_file, 1, 128)
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=128, n_seq=1, use_graph=use_graph)
+    prompt = rng.integers(0, om.vocab, 19).tolist()
+    ctx.decode(prompt, want_logits=2)
+    got = ctx.logits(-1)
+    for p, t in enumerate(prompt):
+        want = om.forward(0, t, p, logits=(p == len(prompt) - 1))
+    ok, err = logits_close(got, want)
+    assert ok, f"prefill logits rel err {err:.2e}"
+    pos = len(prompt)
+    agree = 0
+    for step in range(10):
+        ids, top, margin = ctx.argmax()
+        tok = int(ids[-1])                  # the last token of the last step
+        assert tok == int(np.argmax(got)) or abs(float(np.max(got)) - float(got[tok])) < 1e-6
+        rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+        srt = np.sort(want)
+        if srt[-1] - srt[-2] > TOL * rms:
+            assert tok == int(np.argmax(want)), f"greedy token differs at step {step}"
+            agree += 1
+        ctx.decode([tok], want_logits=1)
+        got = ctx.logits(0)
+        want = om.forward(0, tok, pos)
+        pos += 1
+        ok, err = logits_close(got, want)
+        assert ok, f"decode step {step} logits rel err {err:.2e}"
+    assert agree >= 5
+
+
+def test_batched_sequences_match_oracle(model_file):
+    rng = np.random.default_rng(1)
+    n_seq = 3
+    om = oracle_run(model_file, n_seq, 64)
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=64, n_seq=n_seq)
+    prompts = [rng.integers(0, om.vocab, n).tolist() for n in (5, 9, 3)]
+    last = {}
+    for s, pr in enumerate(prompts):
+        ctx.decode(pr, pos=list(range(len(pr))), seq=[s] * len(pr), want_logits=2)
+        for p, t in enumerate(pr):
+            last[s] = om.forward(s, t, p, logits=(p == len(pr) - 1))
+        ok, err = logits_close(ctx.logits(-1), last[s])
+        assert ok, err
+    pos = [len(p) for p in prompts]
+    for step in range(4):
+        toks = rng.integers(0, om.vocab, n_seq).tolist()
+        ctx.decode(toks, pos=pos, seq=list(range(n_seq)), want_logits=1)
+        for s in range(n_seq):
+            want = om.forward(s, toks[s], pos[s])
+            ok, err = logits_close(ctx.logits(s), want)
+            assert ok, f"seq {s} step {step}: {err:.2e}"
+        pos = [p + 1 for p in pos]
+
+
+@pytest.mark.parametrize("n_keep", [0, 4])
+def test_kv_shift_matches_oracle(model_file, n_keep):
+    """Milda's shift_kv_cache_in_place: seq_rm(n_keep, n_keep+n_discard) then
+    seq_add(n_keep+n_discard, -1, -n_discard); later tokens see re-rotated K."""
+    rng = np.random.default_rng(2)
+    om = oracle_run(model_file, 1, 64)
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=64, n_seq=1)
+    toks = rng.integers(0, om.vocab, 40).tolist()
+    ctx.decode(toks, want_logits=0)
+    for p, t in enumerate(toks):
+        om.forward(0, t, p, logits=False)
+    n_discard = 16
+    ctx.kv_seq_rm(0, n_keep, n_keep + n_discard)
+    ctx.kv_seq_add(0, n_keep + n_discard, -1, -n_discard)
+    om.kv_shift(0, n_keep, n_keep + n_discard, 40)
+    assert ctx.kv_pos_max(0) == 40 - n_discard - 1
+    pos = 40 - n_discard
+    for step in range(6):
+        t = int(rng.integers(0, om.vocab))
+        ctx.decode([t], want_logits=1)
+        want = om.forward(0, t, pos)
+        ok, err = logits_close(ctx.logits(0), want)
+        assert ok, f"after shift step {step}: {err:.2e}"
+        pos += 1
+    # a second shift on the same ring (the pinned prefix stays fixed)
+    ctx.kv_seq_rm(0, n_keep, n_keep + 8)
+    ctx.kv_seq_add(0, n_keep + 8, -1, -8)
+    om.kv_shift(0, n_keep, n_keep + 8, pos)
+    pos -= 8
+    for step in range(3):
+        t = int(rng.integers(0, om.vocab))
+        ctx.decode([t], want_logits=1)
+        want = om.forward(0, t, pos)
+        ok, err = logits_close(ctx.logits(0), want)
+        assert ok, f"after second shift step {step}: {err:.2e}"
+        pos += 1
+
+
+def test_decode_errors_and_truncation(model_file):
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=16, n_seq=1)
+    ctx.decode(list(range(10)), want_logits=0)
+    with pytest.raises(b2.B2Error):
+        ctx.decode([1], pos=[3])                    # not the next position
+    eight = np.zeros(8, np.int32)
+    assert b2.lib.b2_decode(ctx.h, eight.ctypes.data, None, None, 8, 0) == b2.NO_KV_SLOT
+    ctx.kv_seq_rm(0, 6, -1)                          # suffix removal (Milda excise)
+    assert ctx.kv_pos_max(0) == 5
+    ctx.decode([1, 2], want_logits=2)
+    assert np.all(np.isfinite(ctx.logits(-1)))
+    ctx.kv_clear()
+    assert ctx.kv_pos_max(0) == -1
