@@ -103,6 +103,41 @@ __device__ __forceinline__ int nib_hi_s8(uint32_t v) {
   return (int)(((((v >> 4) & 0x0F0F0F0Fu) + 0x78787878u)) ^ 0x80808080u);
 }
 
+// exp(x) in fp32: Cody-Waite reduction x = n·ln2 + r (|r| <= ln2/2, ln2 split
+// into a 16-bit head so n·ln2_hi is exact), the degree-7 Taylor polynomial of
+// e^r by Horner's rule (truncation < 0.2 ulp), then scaling by 2^n built
+// from exponent bits.  Every step is one IEEE-rounded operation written as an
+// explicit intrinsic, so the result is the same bits as the oracle's C copy
+// of this algorithm on any conforming fp32 unit.
+__device__ __forceinline__ float b2_expf(float x) {
+  if (!(x == x)) return x;
+  if (x > 88.7228394f) return __int_as_float(0x7f800000);
+  if (x < -103.972084f) return 0.0f;
+  const float t = __fmul_rn(x, 1.44269502f);
+  const float n = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
+  float r = __fsub_rn(x, __fmul_rn(n, 0.693145751953125f));
+  r = __fsub_rn(r, __fmul_rn(n, 1.42860677e-06f));
+  float p = 1.98412698e-04f;
+  p = __fadd_rn(__fmul_rn(p, r), 1.38888889e-03f);
+  p = __fadd_rn(__fmul_rn(p, r), 8.33333333e-03f);
+  p = __fadd_rn(__fmul_rn(p, r), 4.16666667e-02f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.66666667e-01f);
+  p = __fadd_rn(__fmul_rn(p, r), 0.5f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  int ni = (int)n;
+  float s2 = 1.0f;
+  if (ni > 127) {
+    ni -= 1;
+    s2 = 2.0f;
+  } else if (ni < -126) {
+    ni += 64;
+    s2 = 5.42101086e-20f;   // 2^-64
+  }
+  const float s1 = __int_as_float((ni + 127) << 23);
+  return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

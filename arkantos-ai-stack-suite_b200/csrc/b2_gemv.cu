@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
           u = __fadd_rn(u, red[st & 1][(2 * pr + 1) * wpr + w][t]);
         }
         const int64_t row = rb + 2 * pr;
-        p.y[t * p.y_stride + row / 2] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+        p.y[t * p.y_stride + row / 2] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, b2_expf(-g))), u);
       }
     } else if (tid < rows * B) {
       const int r = tid / B, t = tid - r * B;

@@ -250,9 +250,9 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
   for (int g = 0; g < G; ++g) {
     float l = 0.0f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const float e = expf(sc[g * P + i] - mg[g]);
+      const float e = b2_expf(__fsub_rn(sc[g * P + i], mg[g]));
       sc[g * P + i] = e;
-      l += e;
+      l = __fadd_rn(l, e);
     }
     l = warp_sum(l);
     if (lane == 0) red[g][warp] = l;
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
   if (threadIdx.x < G) {
     const int g = threadIdx.x;
     pml[(int64_t)g * n_split * 2 + 0] = mg[g];
-    pml[(int64_t)g * n_split * 2 + 1] = red[g][0] + red[g][1] + red[g][2] + red[g][3];
+    pml[(int64_t)g * n_split * 2 + 1] = __fadd_rn(__fadd_rn(__fadd_rn(red[g][0], red[g][1]), red[g][2]), red[g][3]);
   }
   // P·V: threads over head dims (HD/2 __half2 pairs per thread group)
   constexpr int PAIRS = HD / 2;                     // 64 for HD=128, 32 for HD=64
@@ -294,11 +294,14 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
     const int g = i / HD, d = i - g * HD;
     float v = 0.0f;
 #pragma unroll
-    for (int t = 0; t < TSPLIT; ++t) v += acc[(t * G + g) * HD + d];
+    for (int t = 0; t < TSPLIT; ++t) v = __fadd_rn(v, acc[(t * G + g) * HD + d]);
     po[(int64_t)g * n_split * HD + d] = v;
   }
 }
 
+// Combines the chunks of one query head: M = max m_s, L = Σ_s e^(m_s−M)·l_s,
+// out = (Σ_s e^(m_s−M)·O_s) · (1/L), chunks in order, each step one rounded
+// operation.
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_head,
                                     int hd, int n_split, float* __restrict__ out) {
   pdl_wait();
@@ -309,13 +312,15 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
   float M = -FLT_MAX;
   for (int s = 0; s < n_split; ++s) M = fmaxf(M, ml[2 * s]);
   float L = 0.0f;
-  for (int s = 0; s < n_split; ++s) L += ml[2 * s + 1] > 0.0f ? expf(ml[2 * s] - M) * ml[2 * s + 1] : 0.0f;
-  const float invL = 1.0f / L;
+  for (int s = 0; s < n_split; ++s)
+    if (ml[2 * s + 1] > 0.0f) L = __fadd_rn(L, __fmul_rn(b2_expf(__fsub_rn(ml[2 * s], M)), ml[2 * s + 1]));
+  const float invL = __fdiv_rn(1.0f, L);
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float v = 0.0f;
     for (int s = 0; s < n_split; ++s)
-      if (ml[2 * s + 1] > 0.0f) v += expf(ml[2 * s] - M) * po[(int64_t)s * hd + d];
-    out[((int64_t)b * n_head + h) * hd + d] = v * invL;
+      if (ml[2 * s + 1] > 0.0f)
+        v = __fadd_rn(v, __fmul_rn(b2_expf(__fsub_rn(ml[2 * s], M)), po[(int64_t)s * hd + d]));
+    out[((int64_t)b * n_head + h) * hd + d] = __fmul_rn(v, invL);
   }
 }
 

@@ -96,6 +96,16 @@ void orc_attn_decode(const float* q, const uint16_t* kc, const uint16_t* vc, int
 void orc_kv_shift_k(uint16_t* kc, int64_t kv_stride, int n_pos, int n_kv_heads, int hd,
                     int delta, float theta);
 
+/* ---- Device-order arithmetic (the GPU kernels' evaluation order) ---- */
+float orc_expf_dev(float x);
+void  orc_silu_mul_dev(float* hb, const float* hb2, int n);
+int   orc_dev_warps_per_row(int wtype, int k, int swiglu);
+float orc_dev_row_dot(int wtype, const void* wrow, int k, const void* xq, int wpr, int direct);
+void  orc_matmul_dev(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int swiglu,
+                     int n_threads);
+void  orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc, int64_t kv_stride, int n_pos,
+                          int n_heads, int n_kv_heads, int hd, float* out);
+
 /* ---- GGUF + Llama forward (Singularity forward_token order) ---- */
 typedef struct orc_model orc_model;
 orc_model* orc_model_open(const char* path);   /* mmap a GGUF file */
@@ -112,6 +122,8 @@ int  orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, flo
                               int n_threads, int n_layers_run);
 /* KV shift on one sequence: drop [p0, p1), re-rotate K of [p1, n_past). */
 int  orc_model_kv_shift(orc_model* m, int seq, int p0, int p1, int n_past);
+/* 1: evaluate in the GPU kernels' order (orc_*_dev), 0: the reference's. */
+void orc_model_set_device_order(orc_model* m, int on);
 /* Per-op tap with the same names as the engine's evaluation callback. */
 typedef void (*orc_tap_fn)(const char* name, int layer, const float* data, long n, void* user);
 void orc_model_set_tap(orc_model* m, orc_tap_fn fn, void* user);

@@ -69,6 +69,11 @@ def _load() -> ctypes.CDLL:
         "orc_model_kv_shift": (_i, [_vp, _i, _i, _i, _i]),
         "orc_model_hidden": (_i, [_vp, _vp, _i]),
         "orc_model_set_tap": (None, [_vp, _vp, _vp]),
+        "orc_model_set_device_order": (None, [_vp, _i]),
+        "orc_expf_dev": (_f, [_f]),
+        "orc_dev_warps_per_row": (_i, [_i, _i, _i]),
+        "orc_matmul_dev": (None, [_i, _vp, ctypes.c_int64, _i, _vp, _vp, _i, _i]),
+        "orc_attn_decode_dev": (None, [_vp, _vp, _vp, ctypes.c_int64, _i, _i, _i, _i, _vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -137,6 +142,31 @@ def gemv(wtype: int, w: np.ndarray, n_rows: int, k: int, x: np.ndarray, n_thread
     x = np.atleast_2d(np.asarray(x, np.float32))
     xq = quantize_act(wtype, x)
     return np.stack([matmul(wtype, w, n_rows, k, xq[b], n_threads) for b in range(x.shape[0])])
+
+
+def matmul_dev(wtype: int, w: np.ndarray, n_rows: int, k: int, xq: np.ndarray, swiglu: bool = False,
+               n_threads: int = 8) -> np.ndarray:
+    """The device GEMV's evaluation order for one activation row."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    xq = np.ascontiguousarray(xq, dtype=np.uint8)
+    y = np.zeros(n_rows, np.float32)
+    lib.orc_matmul_dev(wtype, _p(w), n_rows, k, _p(xq), _p(y), 1 if swiglu else 0, n_threads)
+    return y
+
+
+def gemv_dev(wtype: int, w: np.ndarray, n_rows: int, k: int, x: np.ndarray, n_threads: int = 8) -> np.ndarray:
+    x = np.atleast_2d(np.asarray(x, np.float32))
+    xq = quantize_act(wtype, x)
+    return np.stack([matmul_dev(wtype, w, n_rows, k, xq[b], False, n_threads) for b in range(x.shape[0])])
+
+
+def attn_decode_dev(q, kc, vc, n_pos: int, n_heads: int, n_kv: int, hd: int) -> np.ndarray:
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(kc, np.uint16)
+    vc = np.ascontiguousarray(vc, np.uint16)
+    out = np.zeros(n_heads * hd, np.float32)
+    lib.orc_attn_decode_dev(_p(q), _p(kc), _p(vc), n_kv * hd, n_pos, n_heads, n_kv, hd, _p(out))
+    return out
 
 
 def block_dots(wtype: int, w_row: np.ndarray, xq: np.ndarray, k: int):
@@ -242,6 +272,9 @@ class Model:
         lib.orc_model_info(self.h, _p(info), 12)
         (self.n_layers, self.dim, self.hidden, self.n_heads, self.n_kv, self.vocab,
          self.head_dim, self.ctx_len, self.wtype, self.embd_type, self.out_type, _) = [int(v) for v in info]
+
+    def set_device_order(self, on: bool = True) -> None:
+        lib.orc_model_set_device_order(self.h, 1 if on else 0)
 
     def init_cache(self, n_seq: int, n_ctx: int) -> None:
         if lib.orc_model_init_cache(self.h, n_seq, n_ctx) != 0:

@@ -48,7 +48,10 @@ struct orc_model {
     float* rope;
     orc_tap_fn tap;
     void* tap_user;
+    int device_order;   /* 1: evaluate in the GPU kernels' order (bit-exact check) */
 };
+
+void orc_model_set_device_order(orc_model* m, int on) { m->device_order = on; }
 
 void orc_model_set_tap(orc_model* m, orc_tap_fn fn, void* user) {
     m->tap = fn;
@@ -279,12 +282,14 @@ int orc_model_init_cache(orc_model* m, int n_seq, int n_ctx) {
 /* matmul_quantized with the activation quantized for the weight's dot type
  * (Singularity quantizes to Q8_0 before every projection, :1127, :1257,
  * :1269, :1275, :1290; K-quant weights take Q8_K as in ggml). */
-static void proj(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) {
+static void proj_mode(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt, int swiglu) {
     const int k = (int)w->ne[0];
     if (orc_vec_dot_type(w->type) == ORC_Q8_K) orc_quantize_row_q8_k(x, m->xq, k);
     else orc_quantize_row_q8_0(x, m->xq, k);
-    orc_matmul(w->type, w->data, w->ne[1], k, m->xq, y, nt);
+    if (m->device_order) orc_matmul_dev(w->type, w->data, w->ne[1], k, m->xq, y, swiglu, nt);
+    else orc_matmul(w->type, w->data, w->ne[1], k, m->xq, y, nt);
 }
+static void proj(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) { proj_mode(m, w, x, y, nt, 0); }
 
 int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, float* logits, int nt,
                              int n_layers_run) {
@@ -315,16 +320,18 @@ int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, floa
         uint16_t* vc = m->vc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
         orc_fp32_to_fp16_row(m->k, kc + (size_t)pos * kv_dim, kv_dim);                /* :1195 */
         orc_fp32_to_fp16_row(m->v, vc + (size_t)pos * kv_dim, kv_dim);
-        orc_attn_decode(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);   /* :1205 */
+        if (m->device_order) orc_attn_decode_dev(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);
+        else orc_attn_decode(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);   /* :1205 */
         TAP("attn_out", l, m->xb, dim);
         proj(m, &L->wo, m->xb, m->xb2, nt);                                           /* :1256 */
         TAP("attn_proj", l, m->xb2, dim);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb2[i];
         orc_rmsnorm_ggml(m->x, (const float*)L->ffn_norm.data, m->xb, dim, m->eps);  /* :1264 */
         TAP("ffn_norm", l, m->xb, dim);
-        proj(m, &L->w1, m->xb, m->hb, nt);                                            /* :1270 */
-        proj(m, &L->w3, m->xb, m->hb2, nt);
-        orc_silu_mul(m->hb, m->hb2, m->hidden);                                       /* :1277 */
+        proj_mode(m, &L->w1, m->xb, m->hb, nt, 1);                                    /* :1270 */
+        proj_mode(m, &L->w3, m->xb, m->hb2, nt, 1);
+        if (m->device_order) orc_silu_mul_dev(m->hb, m->hb2, m->hidden);
+        else orc_silu_mul(m->hb, m->hb2, m->hidden);                                  /* :1277 */
         TAP("ffn_act", l, m->hb, m->hidden);
         proj(m, &L->w2, m->hb, m->xb, nt);                                            /* :1280 */
         TAP("ffn_out", l, m->xb, dim);

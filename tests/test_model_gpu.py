@@ -1,10 +1,12 @@
-"""Model-level parity on the GPU through the C ABI: logits of every step
-against the oracle forward (Singularity's forward order), greedy tokens,
-batched sequences and the in-place KV shift.
+"""Model-level parity on the GPU through the C ABI.
 
-Tolerance on logits: |gpu − oracle| <= 1e-3 · max(|oracle|, rms(row)).
-Greedy tokens must agree wherever the oracle's top-2 margin exceeds 1e-3 of
-the row's scale."""
+The quantized forward of a random-weight model is chaotic: a last-ulp change
+in any fp32 sum can move an activation across a Q8 rounding boundary and the
+logits then differ by percent.  So the model is checked bit for bit against
+the oracle's forward evaluated in the GPU kernels' order (every op of which
+is itself checked against the reference's order within tolerance by the op
+tests): logits of every step, greedy tokens, batched sequences and the
+in-place KV shift."""
 import numpy as np
 import pytest
 
@@ -14,39 +16,43 @@ pytestmark = pytest.mark.gpu
 
 b2 = pytest.importorskip("b2gguf")
 
-TOL = 1e-3
+
+def _bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
 
 
-def logits_close(got, want, tol=TOL):
-    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
-    bound = tol * np.maximum(np.abs(want), rms)
-    return bool(np.all(np.abs(got - want) <= bound)), float(np.max(np.abs(got - want)) / max(rms, 1e-30))
+def assert_same(got, want, what):
+    if not np.array_equal(_bits(got), _bits(want)):
+        rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+        raise AssertionError(f"{what}: logits differ (max |d|/rms {float(np.max(np.abs(got - want))) / rms:.2e}, "
+                             f"{int(np.sum(got != want))} of {got.size})")
 
 
 MODELS = {
-    # name: (layers, d, ff, heads, kv heads, vocab, wtype, out type, theta)
-    "q4_0_hd64": (2, 256, 768, 4, 2, 512, 2, 2, 10000.0),
-    "q4_k_hd128": (2, 512, 1024, 4, 1, 768, 12, 14, 500000.0),
-    "q8_0_hd64": (2, 256, 512, 4, 4, 256, 8, 8, 10000.0),
+    # name: (layers, d, ff, heads, kv heads, vocab, wtype, embd type, out type, theta)
+    "q4_0_hd64": (2, 256, 768, 4, 2, 512, 2, 2, 2, 10000.0),
+    "q4_k_hd128": (2, 512, 1024, 4, 1, 768, 12, 12, 14, 500000.0),
+    "q8_0_hd64": (2, 256, 512, 4, 4, 256, 8, 8, 8, 10000.0),
 }
 
 
 @pytest.fixture(scope="module", params=sorted(MODELS))
 def model_file(request, tmp_path_factory):
-    L, d, ff, nh, nkv, V, wt, ot, theta = MODELS[request.param]
+    L, d, ff, nh, nkv, V, wt, et, ot, theta = MODELS[request.param]
     path = str(tmp_path_factory.mktemp("m") / f"{request.param}.gguf")
-    b2.write_synthetic_llama(path, L, d, ff, nh, nkv, V, wt, out_type=ot, seed=11, rope_theta=theta)
+    b2.write_synthetic_llama(path, L, d, ff, nh, nkv, V, wt, embd_type=et, out_type=ot, seed=11, rope_theta=theta)
     return path
 
 
 def oracle_run(path, n_seq, n_ctx):
     m = O.Model(path)
+    m.set_device_order(True)
     m.init_cache(n_seq, n_ctx)
     return m
 
 
 @pytest.mark.parametrize("use_graph", [True, False])
-def test_prefill_and_greedy_decode_match_oracle(model_file, use_graph):
+def test_prefill_and_greedy_decode_bit_exact(model_file, use_graph):
     rng = np.random.default_rng(0)
     om = oracle_run(model_file, 1, 128)
     gm = b2.Model(model_file)
@@ -56,55 +62,45 @@ def test_prefill_and_greedy_decode_match_oracle(model_file, use_graph):
     got = ctx.logits(-1)
     for p, t in enumerate(prompt):
         want = om.forward(0, t, p, logits=(p == len(prompt) - 1))
-    ok, err = logits_close(got, want)
-    assert ok, f"prefill logits rel err {err:.2e}"
+    assert_same(got, want, "prefill")
     pos = len(prompt)
-    agree = 0
-    for step in range(10):
+    for step in range(12):
         ids, top, margin = ctx.argmax()
-        tok = int(ids[-1])                  # the last token of the last step
-        assert tok == int(np.argmax(got)) or abs(float(np.max(got)) - float(got[tok])) < 1e-6
-        rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+        tok = int(ids[-1])                      # greedy pick of the last token of the step
+        assert tok == int(np.argmax(want)), f"greedy token differs at step {step}"
+        assert top[-1] == np.max(want)
         srt = np.sort(want)
-        if srt[-1] - srt[-2] > TOL * rms:
-            assert tok == int(np.argmax(want)), f"greedy token differs at step {step}"
-            agree += 1
+        assert margin[-1] == np.float32(srt[-1] - srt[-2])
         ctx.decode([tok], want_logits=1)
         got = ctx.logits(0)
         want = om.forward(0, tok, pos)
         pos += 1
-        ok, err = logits_close(got, want)
-        assert ok, f"decode step {step} logits rel err {err:.2e}"
-    assert agree >= 5
+        assert_same(got, want, f"decode step {step}")
 
 
-def test_batched_sequences_match_oracle(model_file):
+def test_batched_sequences_bit_exact(model_file):
     rng = np.random.default_rng(1)
     n_seq = 3
     om = oracle_run(model_file, n_seq, 64)
     gm = b2.Model(model_file)
     ctx = b2.Context(gm, n_ctx=64, n_seq=n_seq)
     prompts = [rng.integers(0, om.vocab, n).tolist() for n in (5, 9, 3)]
-    last = {}
     for s, pr in enumerate(prompts):
         ctx.decode(pr, pos=list(range(len(pr))), seq=[s] * len(pr), want_logits=2)
         for p, t in enumerate(pr):
-            last[s] = om.forward(s, t, p, logits=(p == len(pr) - 1))
-        ok, err = logits_close(ctx.logits(-1), last[s])
-        assert ok, err
+            want = om.forward(s, t, p, logits=(p == len(pr) - 1))
+        assert_same(ctx.logits(-1), want, f"prompt {s}")
     pos = [len(p) for p in prompts]
     for step in range(4):
         toks = rng.integers(0, om.vocab, n_seq).tolist()
         ctx.decode(toks, pos=pos, seq=list(range(n_seq)), want_logits=1)
         for s in range(n_seq):
-            want = om.forward(s, toks[s], pos[s])
-            ok, err = logits_close(ctx.logits(s), want)
-            assert ok, f"seq {s} step {step}: {err:.2e}"
+            assert_same(ctx.logits(s), om.forward(s, toks[s], pos[s]), f"seq {s} step {step}")
         pos = [p + 1 for p in pos]
 
 
 @pytest.mark.parametrize("n_keep", [0, 4])
-def test_kv_shift_matches_oracle(model_file, n_keep):
+def test_kv_shift_bit_exact(model_file, n_keep):
     """Milda's shift_kv_cache_in_place: seq_rm(n_keep, n_keep+n_discard) then
     seq_add(n_keep+n_discard, -1, -n_discard); later tokens see re-rotated K."""
     rng = np.random.default_rng(2)
@@ -112,9 +108,10 @@ def test_kv_shift_matches_oracle(model_file, n_keep):
     gm = b2.Model(model_file)
     ctx = b2.Context(gm, n_ctx=64, n_seq=1)
     toks = rng.integers(0, om.vocab, 40).tolist()
-    ctx.decode(toks, want_logits=0)
+    ctx.decode(toks, want_logits=2)
     for p, t in enumerate(toks):
-        om.forward(0, t, p, logits=False)
+        want = om.forward(0, t, p, logits=(p == 39))
+    assert_same(ctx.logits(-1), want, "before shift")
     n_discard = 16
     ctx.kv_seq_rm(0, n_keep, n_keep + n_discard)
     ctx.kv_seq_add(0, n_keep + n_discard, -1, -n_discard)
@@ -124,9 +121,7 @@ def test_kv_shift_matches_oracle(model_file, n_keep):
     for step in range(6):
         t = int(rng.integers(0, om.vocab))
         ctx.decode([t], want_logits=1)
-        want = om.forward(0, t, pos)
-        ok, err = logits_close(ctx.logits(0), want)
-        assert ok, f"after shift step {step}: {err:.2e}"
+        assert_same(ctx.logits(0), om.forward(0, t, pos), f"after shift step {step}")
         pos += 1
     # a second shift on the same ring (the pinned prefix stays fixed)
     ctx.kv_seq_rm(0, n_keep, n_keep + 8)
@@ -136,10 +131,21 @@ def test_kv_shift_matches_oracle(model_file, n_keep):
     for step in range(3):
         t = int(rng.integers(0, om.vocab))
         ctx.decode([t], want_logits=1)
-        want = om.forward(0, t, pos)
-        ok, err = logits_close(ctx.logits(0), want)
-        assert ok, f"after second shift step {step}: {err:.2e}"
+        assert_same(ctx.logits(0), om.forward(0, t, pos), f"after second shift step {step}")
         pos += 1
+
+
+def test_eval_callback_reports_intermediates(model_file):
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=16, n_seq=1)
+    seen = []
+    ctx.set_eval_callback(lambda name, layer, a: seen.append((name, layer, a.size)))
+    ctx.decode([1, 2], want_logits=1)
+    names = [s[0] for s in seen]
+    assert names[0] == "embed" and names[-1] == "result_norm"
+    assert ("attn_out", gm.n_layer - 1) in [(n, l) for n, l, _ in seen]
+    ctx.set_eval_callback(None)
+    ctx.decode([3], want_logits=1)
 
 
 def test_decode_errors_and_truncation(model_file):
