@@ -200,6 +200,25 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
                           const int32_t* seq, int n_q, int n_head, int n_kv, int head_dim, int cap, float* out,
                           void* stream);
 
+/* b2_attn_decode for callers that cannot allocate device memory while they
+ * run (a host that gives the library a fixed device-memory budget at
+ * start-up, or a real-time decode loop that must not pay an allocation's
+ * latency or risk its failure mid-turn).  No counterpart in the reference.
+ * Same arguments and results as b2_attn_decode; the split-K partials live in
+ * one static device array of B2_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * the library holds until exit.  Limits: n_q <= B2_NOALLOC_MAX_QUERIES,
+ * sequence ids < B2_NOALLOC_MAX_SEQ, and n_q·n_head·ceil(cap/256)·(head_dim+2)·4
+ * bytes within the array (larger requests return B2_ERR_INVALID).  The first
+ * call on a device looks up the array's address (call it once before any
+ * stream capture).  Calls share the array: calls that overlap on the GPU
+ * race and must be serialized by the caller. */
+#define B2_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+#define B2_NOALLOC_MAX_QUERIES 64
+#define B2_NOALLOC_MAX_SEQ 4096
+B2_API int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                  const int32_t* pos, const int32_t* seq, int n_q, int n_head, int n_kv,
+                                  int head_dim, int cap, float* out, void* stream);
+
 /* The KV shift's re-rotation (Milda/src/engine.cpp:1642-1675): K rows of
  * positions [p_begin, p_end) of sequence seq rotated in place by `delta`
  * positions (fp16 -> fp32 -> rotate -> fp16 RNE). */
