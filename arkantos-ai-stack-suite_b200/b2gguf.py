@@ -101,6 +101,7 @@ def _bind() -> None:
         "b2_decode": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32]),
         "b2_get_logits": (_i, [_vp, ctypes.c_int32, _vp, _i64]),
         "b2_get_argmax": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32]),
+        "b2_generate": (_i, [_vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp]),
         "b2_synchronize_context": (_i, [_vp]),
         "b2_kv_clear": (_i, [_vp]),
         "b2_kv_seq_rm": (_i, [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
@@ -432,6 +433,16 @@ class Context:
         mar = np.empty(max(n, 8), np.float32)
         check(lib.b2_get_argmax(self.h, ptr(ids), ptr(top), ptr(mar), ids.size), "get_argmax")
         return ids[:n], top[:n], mar[:n]
+
+    def generate(self, first, n_steps: int, seq=None) -> np.ndarray:
+        """Greedy continuation on the device: returns ids [n_steps, n]."""
+        f = np.ascontiguousarray(first, np.int32).ravel()
+        ss = None if seq is None else np.ascontiguousarray(seq, np.int32)
+        out = np.zeros((max(n_steps, 1), f.size), np.int32)
+        rc = lib.b2_generate(self.h, ptr(f), ptr(ss) if ss is not None else None, f.size, n_steps, ptr(out))
+        check(rc, "generate")
+        self.last_n = f.size
+        return out[:n_steps]
 
     def synchronize(self) -> None:
         check(lib.b2_synchronize_context(self.h), "synchronize_context")

@@ -69,6 +69,40 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// ---- peer flags (system scope: written and read across GPUs) -------------------------
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits until flags[0..n) all reach `target`, for at most kPeerWaitNs of
+// wall time; on expiry records `code` in *status and returns false (the
+// caller then proceeds on whatever the buffers hold, so a lost peer ends the
+// step with an error status instead of hanging the GPU).
+constexpr uint64_t kPeerWaitNs = 2000000000ull;
+__device__ __forceinline__ bool wait_peer_flags(const unsigned long long* flags, int n, unsigned long long target,
+                                                int* status, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int j = 0; j < n; ++j) {
+    while (ld_acquire_sys_u64(flags + j) < target) {
+      if (globaltimer_ns() - t0 > kPeerWaitNs) {
+        if (status) atomicExch(status, code);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
 // ---- bulk async copy (1-D TMA, global -> shared, completes on an mbarrier) ----
 // Both addresses 16-byte aligned, size a multiple of 16 bytes.  No multicast.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {

@@ -1,7 +1,7 @@
 // The llama.cpp-shaped engine behind the C ABI: model load (GGUF -> repacked
 // device shards), context (fp16 KV ring per sequence, step buffers), decode
 // (one CUDA graph per step shape), KV shift / removal, greedy argmax, and
-// tensor parallelism over NCCL.
+// tensor parallelism over NVLink peer memory.
 //
 // Mirrors the calls Milda and Sutra make (Milda/src/engine.cpp:703-1292,
 // 1521-1548, 1642-1675, 1962-2117; Sutra/src/llm_backends.cpp:2395-2760) and
@@ -9,11 +9,17 @@
 // (Singularity/src/core/cortex_a5_engine.cpp:1029-1293).
 //
 // Tensor parallelism (tp ranks, one process per GPU): Q/K/V and gate/up are
-// split by output rows (heads / FFN features), O and down by input columns
-// (their partial sums are all-reduced), the output head by vocabulary rows
-// (the logits are all-gathered).  Shard boundaries fall on quantization
+// split by output rows (heads / FFN features), O and down by input columns,
+// the output head by vocabulary rows.  Shard boundaries fall on quantization
 // block boundaries, so each rank quantizes its activation slice exactly as
-// the full vector would be quantized.
+// the full vector would be quantized.  The O / down partial outputs and the
+// head's logit shards are exchanged without a library collective: each
+// rank's GEMV stores its outputs straight into its slot of every rank's
+// gather buffer (CUDA IPC mappings over NVLink) and raises a per-phase epoch
+// flag; the next kernel on each rank waits for all flags and sums the slots
+// in rank order, so every rank holds bit-identical activations and the
+// result does not depend on timing.  NCCL is used once per context, to
+// exchange the IPC handles.
 #include <math.h>
 #include <nccl.h>
 #include <string.h>
@@ -35,6 +41,7 @@ int write_synthetic_llama(const b2_llama_hparams& hp, const char* path, int n_th
 namespace {
 
 constexpr int kStepMax = 8;          // tokens per device step (GEMV batch)
+constexpr int kResWords = 32;        // ids, top-1/margin pairs, status (3*kStepMax+1, padded)
 constexpr int kAttnChunk = 256;      // positions per split-K attention CTA
 
 struct DevQ {
@@ -125,26 +132,40 @@ struct b2_context {
   float* rope = nullptr;        // [n_ctx][head_dim]
   float* shift_cs = nullptr;    // [head_dim] rotation of the last shift
   // step inputs (device + pinned host staging)
-  int32_t *tok_d = nullptr, *pos_d = nullptr, *seq_d = nullptr;
-  int32_t* in_h = nullptr;      // [2 slots][3][kStepMax] pinned
+  // [tok | pos | seq] x kStepMax in one allocation: one H2D copy per step
+  int32_t *in_d = nullptr, *tok_d = nullptr, *pos_d = nullptr, *seq_d = nullptr;
+  int32_t* in_h = nullptr;      // [2 slots][3][kStepMax] pinned, then res_h
+  int32_t* res_h = nullptr;     // [kResWords] pinned copy of res
   cudaEvent_t in_ev[2] = {nullptr, nullptr};
   int in_slot = 0;
   // step buffers
   float *x = nullptr, *delta = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
-  float *logits_l = nullptr, *logits = nullptr, *part_o = nullptr, *part_ml = nullptr, *top = nullptr;
+  float *logits = nullptr, *part_o = nullptr, *part_ml = nullptr, *top = nullptr;
+  // [ids kStepMax | top-1, margin 2*kStepMax | status] in one allocation: one
+  // D2H copy returns a step's greedy result and the device-wait status
+  int32_t* res = nullptr;
   int32_t* ids = nullptr;
   int* status = nullptr;
+  // device-side greedy loop: [n_ctx][kStepMax] generated ids, per-row counts
+  int32_t *gen_out = nullptr, *gen_count = nullptr;
   // last decode
   int last_n = 0;
   bool last_logits = false;
   // graphs per (n_tok, with_logits)
   cudaGraphExec_t graphs[b2::kStepMax + 1][2] = {};
+  cudaGraphExec_t gen_graphs[b2::kStepMax + 1] = {};
   bool use_graph = true;
   b2_abort_callback abort_cb = nullptr;
   void* abort_user = nullptr;
   b2_eval_callback eval_cb = nullptr;
   void* eval_user = nullptr;
   std::vector<void*> allocs;
+  // tensor-parallel exchange (tp > 1): one IPC-exported allocation per rank
+  // [parts: 2 phases x tp slots x kStepMax x n_embd][logits: tp x kStepMax x v_l]
+  // [flags: 3 phases x tp][epochs: 3][done counters: 3]
+  uint8_t* xbuf = nullptr;
+  std::vector<uint8_t*> peer_xbuf;   // per rank (own = xbuf)
+  size_t x_parts = 0, x_logits = 0, x_flags = 0, x_epoch = 0, x_done = 0;   // byte offsets
   ~b2_context();
 };
 
@@ -153,6 +174,11 @@ b2_context::~b2_context() {
   for (auto& row : graphs)
     for (auto& g : row)
       if (g) cudaGraphExecDestroy(g);
+  for (auto& g : gen_graphs)
+    if (g) cudaGraphExecDestroy(g);
+  for (size_t j = 0; j < peer_xbuf.size(); ++j)
+    if (peer_xbuf[j] && peer_xbuf[j] != xbuf) cudaIpcCloseMemHandle(peer_xbuf[j]);
+  if (xbuf) cudaFree(xbuf);
   for (void* p : allocs) cudaFree(p);
   if (in_h) cudaFreeHost(in_h);
   for (auto& e : in_ev)
@@ -338,6 +364,99 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
   return B2_OK;
 }
 
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Collective over the model's ranks (every rank creates its contexts in the
+// same order): allocates the exchange buffer, exports it, gathers every
+// rank's IPC handle through NCCL and maps the peers' buffers.
+int setup_exchange(b2_context* c) {
+  b2_model* m = c->model;
+  const int tp = m->tp_size, r = m->tp_rank;
+  if (tp > kMaxTp) {
+    set_error("context: tensor parallelism over %d ranks, at most %d", tp, kMaxTp);
+    return B2_ERR_UNSUPPORTED;
+  }
+  c->x_parts = 0;
+  c->x_logits = align256(c->x_parts + (size_t)2 * tp * kStepMax * m->n_embd * 4);
+  c->x_flags = align256(c->x_logits + (size_t)tp * kStepMax * m->v_l * 4);
+  c->x_epoch = align256(c->x_flags + (size_t)3 * tp * 8);
+  c->x_done = align256(c->x_epoch + 3 * 8);
+  const size_t bytes = align256(c->x_done + 3 * 4);
+  B2_CUDA_TRY(cudaMalloc(&c->xbuf, bytes));
+  B2_CUDA_TRY(cudaMemset(c->xbuf, 0, bytes));
+  cudaIpcMemHandle_t h;
+  B2_CUDA_TRY(cudaIpcGetMemHandle(&h, c->xbuf));
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  uint8_t* dh = nullptr;
+  B2_CUDA_TRY(cudaMalloc(&dh, (size_t)tp * 64));
+  std::vector<cudaIpcMemHandle_t> all(tp);
+  int rc = B2_OK;
+  {
+    cudaError_t e = cudaMemcpyAsync(dh + (size_t)r * 64, &h, 64, cudaMemcpyHostToDevice, c->stream);
+    ncclResult_t nr = e == cudaSuccess ? ncclAllGather(dh + (size_t)r * 64, dh, 64, ncclChar, m->comm, c->stream)
+                                       : ncclSuccess;
+    if (e == cudaSuccess && nr == ncclSuccess) e = cudaMemcpyAsync(all.data(), dh, (size_t)tp * 64,
+                                                                    cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess && nr == ncclSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(dh);
+    if (nr != ncclSuccess) {
+      set_error("context: IPC handle exchange: %s", ncclGetErrorString(nr));
+      return B2_ERR_NCCL;
+    }
+    B2_CUDA_TRY(e);
+  }
+  c->logits = reinterpret_cast<float*>(c->xbuf + c->x_logits);   // [tp][n][v_l], filled by the ranks' heads
+  c->peer_xbuf.assign(tp, nullptr);
+  for (int j = 0; j < tp; ++j) {
+    if (j == r) {
+      c->peer_xbuf[j] = c->xbuf;
+      continue;
+    }
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, all[j], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      set_error("context: mapping rank %d's exchange buffer: %s (needs peer access between the GPUs)", j,
+                cudaGetErrorString(e));
+      rc = B2_ERR_CUDA;
+      break;
+    }
+    c->peer_xbuf[j] = static_cast<uint8_t*>(p);
+  }
+  return rc;
+}
+
+// Exchange descriptors of one phase (0 attention-out, 1 FFN-down, 2 head
+// logits of an n-token step).
+PeerOut peer_out(const b2_context* c, int phase, int n) {
+  const b2_model* m = c->model;
+  const int tp = m->tp_size, r = m->tp_rank;
+  PeerOut o;
+  o.n = tp;
+  for (int j = 0; j < tp; ++j) {
+    uint8_t* base = c->peer_xbuf[j];
+    if (phase < 2)
+      o.dst[j] = reinterpret_cast<float*>(base + c->x_parts) + ((size_t)phase * tp + r) * kStepMax * m->n_embd;
+    else
+      o.dst[j] = reinterpret_cast<float*>(base + c->x_logits) + (size_t)r * n * m->v_l;
+    o.flag[j] = reinterpret_cast<unsigned long long*>(base + c->x_flags) + (size_t)phase * tp + r;
+  }
+  o.done = reinterpret_cast<unsigned int*>(c->xbuf + c->x_done) + phase;
+  o.epoch = reinterpret_cast<unsigned long long*>(c->xbuf + c->x_epoch) + phase;
+  return o;
+}
+
+PeerIn peer_in(const b2_context* c, int phase) {
+  const b2_model* m = c->model;
+  const int tp = m->tp_size;
+  PeerIn in;
+  in.n = tp;
+  in.parts = reinterpret_cast<const float*>(c->xbuf + c->x_parts) + (size_t)phase * tp * kStepMax * m->n_embd;
+  in.slot = (int64_t)kStepMax * m->n_embd;
+  in.flags = reinterpret_cast<const unsigned long long*>(c->xbuf + c->x_flags) + (size_t)phase * tp;
+  in.epoch = reinterpret_cast<const unsigned long long*>(c->xbuf + c->x_epoch) + phase;
+  return in;
+}
+
 int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   B2_CUDA_TRY(cudaSetDevice(m->device));
   c->model = m;
@@ -363,10 +482,12 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   rope_table(m->theta, hd, 0, c->n_ctx, rope.data());
   if ((rc = dalloc(c, &c->rope, rope.size())) || (rc = dalloc(c, &c->shift_cs, hd))) return rc;
   B2_CUDA_TRY(cudaMemcpy(c->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice));
-  if ((rc = dalloc(c, &c->tok_d, kStepMax)) || (rc = dalloc(c, &c->pos_d, kStepMax)) ||
-      (rc = dalloc(c, &c->seq_d, kStepMax)))
-    return rc;
-  B2_CUDA_TRY(cudaMallocHost(&c->in_h, 2 * 3 * kStepMax * sizeof(int32_t)));
+  if ((rc = dalloc(c, &c->in_d, 3 * kStepMax))) return rc;
+  c->tok_d = c->in_d;
+  c->pos_d = c->in_d + kStepMax;
+  c->seq_d = c->in_d + 2 * kStepMax;
+  B2_CUDA_TRY(cudaMallocHost(&c->in_h, (2 * 3 * kStepMax + kResWords) * sizeof(int32_t)));
+  c->res_h = c->in_h + 2 * 3 * kStepMax;
   for (auto& e : c->in_ev) B2_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   if ((rc = prepare_gemv_kernels())) return rc;
   const int T = kStepMax;
@@ -375,24 +496,41 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
       (rc = dalloc(c, &c->xn, (size_t)T * d)) ||
       (rc = dalloc(c, &c->qkv, (size_t)T * (m->nh_l + 2 * m->nkv_l) * hd)) ||
       (rc = dalloc(c, &c->q, (size_t)T * m->nh_l * hd)) || (rc = dalloc(c, &c->att, (size_t)T * m->nh_l * hd)) ||
-      (rc = dalloc(c, &c->h, (size_t)T * m->ff_l)) || (rc = dalloc(c, &c->logits_l, (size_t)T * m->v_l)) ||
-      (rc = dalloc(c, &c->logits, (size_t)T * m->n_vocab)) ||
+      (rc = dalloc(c, &c->h, (size_t)T * m->ff_l)) ||
+      (m->tp_size == 1 && (rc = dalloc(c, &c->logits, (size_t)T * m->n_vocab))) ||
       (rc = dalloc(c, &c->part_o, (size_t)T * m->nh_l * n_split * hd)) ||
-      (rc = dalloc(c, &c->part_ml, (size_t)T * m->nh_l * n_split * 2)) || (rc = dalloc(c, &c->top, 2 * T)) ||
-      (rc = dalloc(c, &c->ids, T)) || (rc = dalloc(c, &c->status, 4)))
+      (rc = dalloc(c, &c->part_ml, (size_t)T * m->nh_l * n_split * 2)) || (rc = dalloc(c, &c->res, kResWords)) ||
+      (rc = dalloc(c, &c->gen_out, (size_t)c->n_ctx * T)) || (rc = dalloc(c, &c->gen_count, T)))
     return rc;
-  B2_CUDA_TRY(cudaMemset(c->status, 0, 16));
+  c->ids = c->res;
+  c->top = reinterpret_cast<float*>(c->res + kStepMax);
+  c->status = c->res + 3 * kStepMax;
+  B2_CUDA_TRY(cudaMemset(c->res, 0, kResWords * 4));
+  if (m->tp_size > 1) return setup_exchange(c);
   return B2_OK;
 }
 
-// One device step over n tokens already staged in tok_d/pos_d/seq_d.
-int enqueue_step(b2_context* c, int n, bool with_logits) {
+// One device step over n tokens already staged in tok_d/pos_d/seq_d.  With
+// `feed`, the step ends by writing its argmax ids back as the next tokens.
+int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
   b2_model* m = c->model;
   cudaStream_t s = c->stream;
   const int d = m->n_embd, hd = m->head_dim;
   int rc = launch_embed(c->tok_d, n, m->n_vocab, m->embd_type, m->embd, m->embd_row_bytes, d, c->x, s);
   if (rc) return rc;
-  auto gemv = [&](const DevQ& w, const float* x, int64_t xs, float* y, int64_t ys, int epi) {
+  const bool tp = m->tp_size > 1;
+  PeerOut out_o, out_down, out_head;
+  PeerIn in_o, in_down, in_head;
+  if (tp) {
+    out_o = peer_out(c, 0, n);
+    out_down = peer_out(c, 1, n);
+    out_head = peer_out(c, 2, n);
+    in_o = peer_in(c, 0);
+    in_down = peer_in(c, 1);
+    in_head = peer_in(c, 2);
+  }
+  auto gemv = [&](const DevQ& w, const float* x, int64_t xs, float* y, int64_t ys, int epi,
+                  const PeerOut* peer = nullptr) {
     GemvArgs a = {};
     a.w = &w.m;
     a.x = x;
@@ -404,6 +542,7 @@ int enqueue_step(b2_context* c, int n, bool with_logits) {
     a.row_begin = 0;
     a.row_end = w.m.n_rows;
     a.status = c->status;
+    a.peer = peer;
     return launch_gemv(a, s);
   };
   // cb_eval-style tap (eager steps only).
@@ -417,7 +556,9 @@ int enqueue_step(b2_context* c, int n, bool with_logits) {
   const int qkv_w = (m->nh_l + 2 * m->nkv_l) * hd;
   for (int l = 0; l < m->n_layer; ++l) {
     Layer& L = *m->layers[l];
-    if ((rc = launch_add_rmsnorm(c->x, l ? c->delta : nullptr, L.attn_norm, c->xn, n, d, m->eps, s))) return rc;
+    if ((rc = launch_add_rmsnorm(c->x, l ? c->delta : nullptr, L.attn_norm, c->xn, n, d, m->eps, s,
+                                 tp && l ? &in_down : nullptr, c->status)))
+      return rc;
     if ((rc = tap("attn_norm", l, c->xn, (int64_t)n * d))) return rc;
     if ((rc = gemv(L.wqkv, c->xn, d, c->qkv, qkv_w, EPI_STORE))) return rc;
     if ((rc = tap("qkv", l, c->qkv, (int64_t)n * qkv_w))) return rc;
@@ -429,33 +570,40 @@ int enqueue_step(b2_context* c, int n, bool with_logits) {
                                c->n_ctx, kAttnChunk, c->part_o, c->part_ml, c->att, s)))
       return rc;
     if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
-    if ((rc = gemv(L.wo, c->att, (int64_t)m->nh_l * hd, c->delta, d, EPI_STORE))) return rc;
-    if (m->tp_size > 1) B2_NCCL_TRY(ncclAllReduce(c->delta, c->delta, (size_t)n * d, ncclFloat, ncclSum, m->comm, s));
-    if ((rc = tap("attn_proj", l, c->delta, (int64_t)n * d))) return rc;
-    if ((rc = launch_add_rmsnorm(c->x, c->delta, L.ffn_norm, c->xn, n, d, m->eps, s))) return rc;
+    if ((rc = gemv(L.wo, c->att, (int64_t)m->nh_l * hd, c->delta, d, EPI_STORE, tp ? &out_o : nullptr))) return rc;
+    if (!tp && (rc = tap("attn_proj", l, c->delta, (int64_t)n * d))) return rc;
+    if ((rc = launch_add_rmsnorm(c->x, c->delta, L.ffn_norm, c->xn, n, d, m->eps, s, tp ? &in_o : nullptr,
+                                 c->status)))
+      return rc;
     if ((rc = tap("ffn_norm", l, c->xn, (int64_t)n * d))) return rc;
     if ((rc = gemv(L.wgu, c->xn, d, c->h, m->ff_l, EPI_SWIGLU))) return rc;
     if ((rc = tap("ffn_act", l, c->h, (int64_t)n * m->ff_l))) return rc;
-    if ((rc = gemv(L.wdown, c->h, m->ff_l, c->delta, d, EPI_STORE))) return rc;
-    if (m->tp_size > 1) B2_NCCL_TRY(ncclAllReduce(c->delta, c->delta, (size_t)n * d, ncclFloat, ncclSum, m->comm, s));
-    if ((rc = tap("ffn_out", l, c->delta, (int64_t)n * d))) return rc;
+    if ((rc = gemv(L.wdown, c->h, m->ff_l, c->delta, d, EPI_STORE, tp ? &out_down : nullptr))) return rc;
+    if (!tp && (rc = tap("ffn_out", l, c->delta, (int64_t)n * d))) return rc;
   }
-  if ((rc = launch_add_rmsnorm(c->x, c->delta, m->out_norm, c->xn, n, d, m->eps, s))) return rc;
+  if ((rc = launch_add_rmsnorm(c->x, c->delta, m->out_norm, c->xn, n, d, m->eps, s, tp ? &in_down : nullptr,
+                               c->status)))
+    return rc;
   if ((rc = tap("result_norm", -1, c->xn, (int64_t)n * d))) return rc;
   if (!with_logits) return B2_OK;
-  float* out = m->tp_size > 1 ? c->logits_l : c->logits;
-  if ((rc = gemv(m->head, c->xn, d, out, m->v_l, EPI_STORE))) return rc;
-  if (m->tp_size > 1)
-    B2_NCCL_TRY(ncclAllGather(c->logits_l, c->logits, (size_t)n * m->v_l, ncclFloat, m->comm, s));
-  return launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s);
+  if ((rc = gemv(m->head, c->xn, d, c->logits, m->v_l, EPI_STORE, tp ? &out_head : nullptr))) return rc;
+  GreedyFeed f;
+  if (feed) {
+    f.tok = c->tok_d;
+    f.pos = c->pos_d;
+    f.out = c->gen_out;
+    f.count = c->gen_count;
+    f.cap = c->n_ctx;
+  }
+  return launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s, f, tp ? &in_head : nullptr, c->status);
 }
 
-int run_step(b2_context* c, int n, bool with_logits) {
-  if (!c->use_graph || c->eval_cb) return enqueue_step(c, n, with_logits);
-  cudaGraphExec_t& g = c->graphs[n][with_logits ? 1 : 0];
+int run_step(b2_context* c, int n, bool with_logits, bool feed = false) {
+  if (!c->use_graph || c->eval_cb) return enqueue_step(c, n, with_logits, feed);
+  cudaGraphExec_t& g = feed ? c->gen_graphs[n] : c->graphs[n][with_logits ? 1 : 0];
   if (!g) {
     B2_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    const int rc = enqueue_step(c, n, with_logits);
+    const int rc = enqueue_step(c, n, with_logits, feed);
     cudaGraph_t graph = nullptr;
     const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
     if (rc) {
@@ -528,9 +676,7 @@ int decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32
       hs[kStepMax + i] = pv[i0 + i];
       hs[2 * kStepMax + i] = sv[i0 + i];
     }
-    B2_CUDA_TRY(cudaMemcpyAsync(c->tok_d, hs, k * 4, cudaMemcpyHostToDevice, c->stream));
-    B2_CUDA_TRY(cudaMemcpyAsync(c->pos_d, hs + kStepMax, k * 4, cudaMemcpyHostToDevice, c->stream));
-    B2_CUDA_TRY(cudaMemcpyAsync(c->seq_d, hs + 2 * kStepMax, k * 4, cudaMemcpyHostToDevice, c->stream));
+    B2_CUDA_TRY(cudaMemcpyAsync(c->in_d, hs, 3 * kStepMax * 4, cudaMemcpyHostToDevice, c->stream));
     B2_CUDA_TRY(cudaEventRecord(c->in_ev[slot], c->stream));
     int rc = run_step(c, k, with_logits);
     if (rc) return rc;
@@ -540,6 +686,61 @@ int decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32
   }
   for (int s = 0; s < c->n_seq; ++s) c->n_past[s] = next[s];
   return B2_OK;
+}
+
+// Greedy generation with the loop on the device: step t feeds every row the
+// argmax of step t-1 (step 0 feeds `first`), so consecutive steps are graph
+// replays with no host round trip.  The ids come back in one copy at the end.
+int generate(b2_context* c, const int32_t* first, const int32_t* seq, int n, int n_steps, int32_t* out) {
+  b2_model* m = c->model;
+  B2_CUDA_TRY(cudaSetDevice(m->device));
+  B2_CHECK_ARG(first && out && n > 0 && n <= kStepMax && n_steps >= 0, "generate arguments");
+  std::vector<int32_t> sv(n);
+  std::vector<char> used(c->n_seq, 0);
+  for (int i = 0; i < n; ++i) {
+    const int s = seq ? seq[i] : i;
+    if (s < 0 || s >= c->n_seq || used[s]) {
+      set_error("generate: sequence id %d out of range or repeated", s);
+      return B2_ERR_INVALID;
+    }
+    used[s] = 1;
+    sv[i] = s;
+    if (first[i] < 0 || first[i] >= m->n_vocab) {
+      set_error("generate: token %d outside the vocabulary", first[i]);
+      return B2_ERR_INVALID;
+    }
+    if (c->n_past[s] + n_steps > c->n_ctx) return B2_NO_KV_SLOT;
+  }
+  if (n_steps == 0) return B2_OK;
+  const int slot = c->in_slot;
+  c->in_slot ^= 1;
+  B2_CUDA_TRY(cudaEventSynchronize(c->in_ev[slot]));
+  int32_t* hs = c->in_h + slot * 3 * kStepMax;
+  for (int i = 0; i < n; ++i) {
+    hs[i] = first[i];
+    hs[kStepMax + i] = c->n_past[sv[i]];
+    hs[2 * kStepMax + i] = sv[i];
+  }
+  B2_CUDA_TRY(cudaMemcpyAsync(c->in_d, hs, 3 * kStepMax * 4, cudaMemcpyHostToDevice, c->stream));
+  B2_CUDA_TRY(cudaEventRecord(c->in_ev[slot], c->stream));
+  B2_CUDA_TRY(cudaMemsetAsync(c->gen_count, 0, n * 4, c->stream));
+  int done = 0, rc = B2_OK;
+  for (; done < n_steps; ++done) {
+    if (c->abort_cb && c->abort_cb(c->abort_user)) {
+      rc = B2_ABORTED;
+      break;
+    }
+    if ((rc = run_step(c, n, true, true))) return rc;
+  }
+  if (done > 0) {
+    B2_CUDA_TRY(cudaMemcpyAsync(out, c->gen_out, (size_t)done * n * 4, cudaMemcpyDeviceToHost, c->stream));
+    c->last_n = n;
+    c->last_logits = true;
+  }
+  const int st = check_status(c);
+  if (st) return st;
+  for (int i = 0; i < n; ++i) c->n_past[sv[i]] += done;
+  return rc;
 }
 
 // Milda's shift (seq_rm [p0,p1) then seq_add(p1, end, -(p1-p0))), applied
@@ -714,6 +915,16 @@ int b2_decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const in
   return decode(c, tokens, pos, seq, n_tokens, want_logits);
 }
 
+int b2_generate(b2_context* c, const int32_t* first, const int32_t* seq, int32_t n, int32_t n_steps, int32_t* out) {
+  B2_CHECK_ARG(c, "context");
+  for (const auto& p : pending_for(c))
+    if (p.p0 >= 0) {
+      set_error("generate: a KV removal is waiting for its position shift (b2_kv_seq_add)");
+      return B2_ERR_INVALID;
+    }
+  return generate(c, first, seq, n, n_steps, out);
+}
+
 int b2_get_logits(b2_context* c, int32_t i, float* out, int64_t n) {
   B2_CHECK_ARG(c && out, "get_logits arguments");
   B2_CHECK_ARG(c->last_logits, "the last decode computed no logits");
@@ -738,15 +949,17 @@ int b2_get_argmax(b2_context* c, int32_t* ids, float* top1, float* margin, int32
   B2_CHECK_ARG(c->last_logits, "the last decode computed no logits");
   B2_CHECK_ARG(n >= c->last_n, "output arrays shorter than the last batch");
   B2_CUDA_TRY(cudaSetDevice(c->model->device));
-  float top[2 * kStepMax];
-  B2_CUDA_TRY(cudaMemcpyAsync(ids, c->ids, c->last_n * 4, cudaMemcpyDeviceToHost, c->stream));
-  B2_CUDA_TRY(cudaMemcpyAsync(top, c->top, c->last_n * 8, cudaMemcpyDeviceToHost, c->stream));
+  int32_t* r = c->res_h;
+  B2_CUDA_TRY(cudaMemcpyAsync(r, c->res, kResWords * 4, cudaMemcpyDeviceToHost, c->stream));
   B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  const float* top = reinterpret_cast<const float*>(r + kStepMax);
   for (int i = 0; i < c->last_n; ++i) {
+    ids[i] = r[i];
     if (top1) top1[i] = top[2 * i];
     if (margin) margin[i] = top[2 * i + 1];
   }
-  return check_status(c);
+  if (r[3 * kStepMax] != 0) return check_status(c);
+  return B2_OK;
 }
 
 int b2_synchronize_context(b2_context* c) {

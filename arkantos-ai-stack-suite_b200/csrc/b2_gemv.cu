@@ -49,9 +49,38 @@ struct GemvP {
   int rg;                 // rows per stage (1, 2, 4 or 8)
   uint32_t stage_bytes;
   int* status;
+  PeerOut peer;
 };
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNCW * 32) : "memory"); }
+
+// Output (token t, row) of the store / residual-add epilogues; with a
+// tensor-parallel exchange the value goes to this rank's slot of every rank.
+__device__ __forceinline__ void store_y(const GemvP& p, int t, int64_t row, float v) {
+  const int64_t off = t * p.y_stride + row;
+  if (p.peer.n) {
+    for (int j = 0; j < p.peer.n; ++j) p.peer.dst[j][off] = v;
+    return;
+  }
+  float* yp = p.y + off;
+  *yp = p.epilogue == EPI_ACCUM ? __fadd_rn(*yp, v) : v;
+}
+
+// After every consumer thread of the CTA has stored: count the CTA; the last
+// CTA of the grid publishes the next epoch to every rank's flag.  Stores reach
+// peers before the count (fence.sys by the counting thread after the CTA
+// barrier), and the count before the flags (fence.sys in the last CTA).
+__device__ __forceinline__ void signal_peers(const GemvP& p) {
+  __threadfence_system();
+  const unsigned int prev = atomicAdd(p.peer.done, 1u);
+  if (prev == gridDim.x - 1) {
+    __threadfence_system();
+    const unsigned long long e = *p.peer.epoch + 1ull;
+    *p.peer.epoch = e;
+    *p.peer.done = 0u;
+    for (int j = 0; j < p.peer.n; ++j) st_release_sys_u64(p.peer.flag[j], e);
+  }
+}
 
 // ---- activation prologue ---------------------------------------------------------
 template <int WT, int B>
@@ -389,9 +418,13 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
   }
 
   // ---------------- consumers ----------------
+  // A timed-out wait does not leave the loop early: the warp keeps taking the
+  // same named barriers as the others (skipping its waits and math), so the
+  // CTA always reaches its end and, with an exchange, still signals peers.
   pdl_wait();
   load_act<WT, B>(p, aq, ad, ab, warp, lane);
   consumer_sync();
+  bool ok = true;
 
   const int wpr = kNCW / rg;               // warps per row
   const int my_row = warp / wpr;           // row of the stage this warp works on
@@ -401,14 +434,14 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
   for (int st = 0; st < total; ++st) {
     const int s = st % ns;
     const uint32_t ph = (uint32_t)(st / ns) & 1u;
-    if (!mbar_wait_bounded(&full[s], ph, p.status, 1)) return;
+    if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
     const uint8_t* sp = ring + (size_t)s * p.stage_bytes;
     const int64_t rb = r0 + (int64_t)st * rg;
     const int rows = (int)min((int64_t)rg, r1 - rb);
     float acc[B];
 #pragma unroll
     for (int t = 0; t < B; ++t) acc[t] = 0.0f;
-    if (my_row < rows)
+    if (ok && my_row < rows)
       compute_row<WT, B>(sp + my_row * p.p0_row, sp + p1_off + my_row * p.p1_row, kp, aq, ad, ab, first, step, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -417,10 +450,7 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
 #pragma unroll
       for (int t = 0; t < B; ++t) {
         const float v = warp_sum(acc[t]);
-        if (lane == 0 && my_row < rows) {
-          float* yp = p.y + t * p.y_stride + rb + my_row;
-          *yp = p.epilogue == EPI_ACCUM ? __fadd_rn(*yp, v) : v;
-        }
+        if (lane == 0 && my_row < rows) store_y(p, t, rb + my_row, v);
       }
       continue;
     }
@@ -446,9 +476,13 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
       const int r = tid / B, t = tid - r * B;
       float v = 0.0f;
       for (int w = 0; w < wpr; ++w) v = __fadd_rn(v, red[st & 1][r * wpr + w][t]);
-      float* yp = p.y + t * p.y_stride + rb + r;
-      *yp = p.epilogue == EPI_ACCUM ? __fadd_rn(*yp, v) : v;
+      store_y(p, t, rb + r, v);
     }
+  }
+  if (p.peer.n) {
+    __threadfence_system();   // this thread's peer stores, before the CTA is counted
+    consumer_sync();
+    if (warp == 0 && lane == 0) signal_peers(p);
   }
 }
 
@@ -555,6 +589,13 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.y_stride = a.y_stride;
   p.epilogue = a.epilogue;
   p.status = a.status;
+  if (a.peer && a.peer->n > 0) {
+    B2_CHECK_ARG(a.epilogue == EPI_STORE && a.peer->n <= kMaxTp && a.peer->done && a.peer->epoch,
+                 "peer exchange needs the store epilogue and its counters");
+    p.peer = *a.peer;
+  } else {
+    p.peer = PeerOut{};
+  }
   const bool k_quant = (w.type == B2_Q4_K || w.type == B2_Q6_K);
   // Same carve-up as the kernel: qs [B][kp] | d [B][nd] fp32 (16 B aligned end) | bsum [B][kp/16].
   const size_t nd = (size_t)(k_quant ? w.kp / 256 : w.kp / 32);

@@ -101,6 +101,28 @@ enum Epilogue : int {
   EPI_SWIGLU = 2,      // rows (2i, 2i+1) are (gate_i, up_i): y[i] = silu(gate)·up
 };
 
+// Tensor-parallel exchange over peer memory (CUDA IPC mappings over NVLink).
+// A row-split projection (attention-out, FFN-down, the vocabulary-sharded
+// head) on rank r stores its outputs into slot r of every rank's gather
+// buffer; its last CTA then raises the phase's epoch in every rank's flag r.
+// The consumer on each rank waits until all flags reach the epoch and sums the
+// slots in rank order — a fixed-order allreduce with no library collective.
+constexpr int kMaxTp = 8;
+struct PeerOut {
+  int n = 0;                                   // ranks (0: plain local store)
+  float* dst[kMaxTp] = {};                     // per rank: this rank's slot in its gather buffer
+  unsigned long long* flag[kMaxTp] = {};       // per rank: this rank's flag word of the phase
+  unsigned int* done = nullptr;                // local: CTAs of the launch that have stored
+  unsigned long long* epoch = nullptr;         // local: epochs of the phase so far
+};
+struct PeerIn {
+  int n = 0;                                   // ranks (0: no exchange)
+  const float* parts = nullptr;                // local gather buffer, slot j at parts + j * slot
+  int64_t slot = 0;                            // elements between slots
+  const unsigned long long* flags = nullptr;   // local flags of the phase [n]
+  const unsigned long long* epoch = nullptr;   // local epoch counter of the phase
+};
+
 struct GemvArgs {
   const QMatrix* w;
   const float* x;       // fp32 [n_tok][x_stride] when act == nullptr (quantized in-kernel)
@@ -112,6 +134,7 @@ struct GemvArgs {
   int epilogue;
   int64_t row_begin, row_end;   // rows of W to compute (TP slices, tests); end<=n_rows
   int* status;          // device status word (bounded waits), may be nullptr
+  const PeerOut* peer = nullptr;   // tensor-parallel exchange of the outputs (EPI_STORE only)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 // Sets the large dynamic shared-memory limit of every GEMV instantiation on

@@ -87,17 +87,33 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, int n_vocab, in
 // resolution, so the tree order here rounds to the same mean as the
 // sequential CPU sum (bit-identical outputs, which keeps the following Q8
 // activation codes identical even on exact rounding ties).
+// With a tensor-parallel exchange (in.n > 0) the residual delta is the sum of
+// the ranks' partial outputs in rank order, ((p0 + p1) + p2) + ..., read from
+// the local gather buffer once every rank's flag shows this phase's epoch.
 __global__ void add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
-                                   float* __restrict__ out, int n, float eps) {
+                                   float* __restrict__ out, int n, float eps, PeerIn in, int* status) {
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;
   float* xr = x + (int64_t)b * n;
   const float* dr = delta ? delta + (int64_t)b * n : nullptr;
+  if (in.n) {
+    if (threadIdx.x == 0) {
+      wait_peer_flags(in.flags, in.n, *in.epoch, status, 3);
+      __threadfence();
+    }
+    __syncthreads();
+  }
   double ss = 0.0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float v = xr[i];
-    if (dr) {
+    if (in.n) {
+      const float* pp = in.parts + (int64_t)b * n + i;
+      float sum = __ldcg(pp);
+      for (int j = 1; j < in.n; ++j) sum = __fadd_rn(sum, __ldcg(pp + j * in.slot));
+      v = __fadd_rn(v, sum);
+      xr[i] = v;
+    } else if (dr) {
       v = __fadd_rn(v, dr[i]);
       xr[i] = v;
     }
@@ -385,16 +401,27 @@ __global__ void kv_compact_kernel(uint16_t* __restrict__ kc, uint16_t* __restric
 // Logits of token b, vocabulary entry v, live at
 //   logits[(v / v_local) * n_tok * v_local + b * v_local + v % v_local]
 // (tensor-parallel gather layout; v_local = n_vocab without TP).  Ties pick
-// the lowest id.  Writes id, top-1 value and top-1 − top-2 margin.
+// the lowest id.  Writes id, top-1 value and top-1 − top-2 margin.  With a
+// feed (device-side greedy loop) it also makes the id the next step's token of
+// row b, advances the row's position and appends the id to the row's output
+// list; the step's other kernels have finished reading tok/pos by then.
 __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n_vocab, int v_local,
-                              int32_t* __restrict__ ids, float* __restrict__ top) {
+                              int32_t* __restrict__ ids, float* __restrict__ top, GreedyFeed feed, PeerIn in,
+                              int* status) {
   pdl_wait();
-  pdl_launch_dependents();
+  if (!feed.tok) pdl_launch_dependents();
+  if (in.n) {   // the ranks' head shards arrive in the gather layout
+    if (threadIdx.x == 0) {
+      wait_peer_flags(in.flags, in.n, *in.epoch, status, 4);
+      __threadfence();
+    }
+    __syncthreads();
+  }
   const int b = blockIdx.x;
   float v1 = -FLT_MAX, v2 = -FLT_MAX;
   int i1 = 0x7fffffff;
   for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) {
-    const float x = logits[(int64_t)(v / v_local) * n_tok * v_local + (int64_t)b * v_local + v % v_local];
+    const float x = __ldcg(logits + (int64_t)(v / v_local) * n_tok * v_local + (int64_t)b * v_local + v % v_local);
     if (x > v1 || (x == v1 && v < i1)) {
       v2 = v1;
       v1 = x;
@@ -440,6 +467,13 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n
     ids[b] = bi;
     top[2 * b] = b1;
     top[2 * b + 1] = b1 - b2;
+    if (feed.tok) {
+      feed.tok[b] = bi;
+      feed.pos[b] += 1;
+      const int t = feed.count[b];
+      if (t < feed.cap) feed.out[(int64_t)t * n_tok + b] = bi;
+      feed.count[b] = t + 1;
+    }
   }
 }
 
@@ -467,8 +501,9 @@ int launch_embed(const int32_t* tokens, int n_tok, int n_vocab, int type, const 
 }
 
 int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
-                       cudaStream_t s) {
-  return launch_pdl(add_rmsnorm_kernel, dim3(n_tok), dim3(512), 0, s, x, delta, w, out, n, eps);
+                       cudaStream_t s, const PeerIn* in, int* status) {
+  return launch_pdl(add_rmsnorm_kernel, dim3(n_tok), dim3(512), 0, s, x, delta, w, out, n, eps, in ? *in : PeerIn{},
+                    status);
 }
 
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
@@ -538,8 +573,10 @@ int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, con
   return B2_OK;
 }
 
-int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s) {
-  return launch_pdl(argmax_kernel, dim3(n_tok), dim3(1024), 0, s, logits, n_tok, n_vocab, v_local, ids, top);
+int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s,
+                  const GreedyFeed& feed, const PeerIn* in, int* status) {
+  return launch_pdl(argmax_kernel, dim3(n_tok), dim3(1024), 0, s, logits, n_tok, n_vocab, v_local, ids, top, feed,
+                    in ? *in : PeerIn{}, status);
 }
 
 }  // namespace b2

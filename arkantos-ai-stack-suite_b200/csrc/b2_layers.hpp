@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "b2_internal.hpp"
+
 namespace b2 {
 
 // Per-sequence KV bookkeeping, read by kernels from device memory.  Logical
@@ -19,7 +21,7 @@ struct KvSeqState {
 int launch_embed(const int32_t* tokens, int n_tok, int n_vocab, int type, const uint8_t* table, int64_t row_bytes,
                  int n_embd, float* x, cudaStream_t s);
 int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
-                       cudaStream_t s);
+                       cudaStream_t s, const PeerIn* in = nullptr, int* status = nullptr);
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                    const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int cap,
                    cudaStream_t s);
@@ -34,6 +36,15 @@ int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& s
                     const float* cs, cudaStream_t s);
 int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int dst0,
                       int src0, int n, const float* cs, cudaStream_t s);
-int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s);
+// Device-side greedy loop: argmax ids become the next step's tokens.
+struct GreedyFeed {
+  int32_t* tok = nullptr;    // [n_tok] next step's tokens (null: no feed)
+  int32_t* pos = nullptr;    // [n_tok] positions, advanced by one
+  int32_t* out = nullptr;    // [cap][n_tok] generated ids
+  int32_t* count = nullptr;  // [n_tok] ids appended so far
+  int cap = 0;
+};
+int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s,
+                  const GreedyFeed& feed = GreedyFeed{}, const PeerIn* in = nullptr, int* status = nullptr);
 
 }  // namespace b2

@@ -3,6 +3,17 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Prints one JSON line (rank 0).  Workloads:
+  decode_8b_q4k (default)
+              Random-init Llama-architecture 8B decoder, GGUF Q4_K with a Q6_K
+              head (32 layers, d 4096, FFN 14336, 32/8 heads, vocab 128256,
+              theta 5e5, weights N(0,0.02) seed 6), tensor parallel over the
+              torchrun ranks.  8 prompts of 2048 uniform random ids are
+              prefilled, then one step = one greedy decode step of the batch
+              of 8.  `value` times K steps of b2_generate (argmax fed back on
+              the device); `e2e` times the same K steps as the host loop
+              b2_decode + b2_get_argmax.  Every step reads all weights (4.36 GB
+              / TP per rank) from HBM.  The line also carries the Q4_0 GEMV
+              below as "q4_0_gemv".
   gemv_q4_0   Q4_0 block-quantized GEMV, batch 1: W 4096x4096 N(0,0.02) seed 0
               -> GGUF Q4_0, x fp32[4096] N(0,1) seed 1 quantized to Q8_0 in the
               kernel, y fp32[4096].  One step = one GEMV; consecutive steps
@@ -223,6 +234,32 @@ def run_gemv_ours(args, dist, rank, world, local):
     return out
 
 
+def gemv_q4_0_measure(b2, steps: int) -> dict:
+    """Config-1 Q4_0 GEMV (the metric's second half) on the current device:
+    CUDA-event time of `steps` GEMVs captured in one graph over rotating copies."""
+    q, x = gemv_inputs(b2)
+    mats = [b2.QMatrix(b2.Q4_0, q, GEMV_N, GEMV_K) for _ in range(GEMV_COPIES)]
+    xd = b2.DeviceBuffer.from_array(x)
+    yd = b2.DeviceBuffer(GEMV_N * 4)
+    stream = b2.Stream()
+    for i in range(GEMV_COPIES):
+        mats[i].gemv_device(xd, 1, yd, stream.h)
+    graph = b2.Graph(stream, lambda s: [mats[i % GEMV_COPIES].gemv_device(xd, 1, yd, s) for i in range(steps)])
+    graph.launch()
+    stream.synchronize()
+    e0, e1 = b2.Event(), b2.Event()
+    e0.record(stream.h)
+    graph.launch()
+    e1.record(stream.h)
+    stream.synchronize()
+    ms = e0.elapsed_ms(e1) / steps
+    gbs = GEMV_BYTES / (ms * 1e-3) / 1e9
+    peaks = measured_peaks()
+    return {"metric": "Q4_0 GEMV HBM GB/s (4096x4096, batch 1)", "value": round(gbs, 1), "unit": "GB/s",
+            "frac": round(gbs / peaks["hbm_gbs"], 4), "peak": peaks["hbm_gbs"], "ms_per_gemv": ms,
+            "algorithmic_bytes_per_launch": GEMV_BYTES, "launches": steps}
+
+
 def cpu_gemv_baseline(q, x, seconds: float) -> dict:
     from oracle import oracle as O
     nt = os.cpu_count() or 1
@@ -262,21 +299,356 @@ def run_gemv_reference(args, dist, rank, world, local):
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-WORKLOADS = {"gemv_q4_0": (run_gemv_ours, run_gemv_reference)}
+# ------------------------------------------------------------------------------------------
+# Workload: 8B Q4_K decode, tensor parallel (config 5)
+# ------------------------------------------------------------------------------------------
+LLAMA_8B = dict(n_layer=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, n_vocab=128256, seed=6,
+                rope_theta=500000.0, n_ctx_train=8192)
+BATCH = 8
+PROMPT = 2048
+CLOCK_LOAD_STEPS = 32
+
+
+def q_bytes(t: int, n: int, k: int) -> int:
+    per = {2: 18 / 32, 8: 34 / 32, 12: 144 / 256, 14: 210 / 256}[t]
+    return int(n * k * per)
+
+
+def decode_weight_bytes(world: int = 1) -> int:
+    """Algorithmic weight bytes one decode step reads on one rank (GGUF block bytes)."""
+    c = LLAMA_8B
+    d, ff, hd = c["n_embd"], c["n_ff"], c["n_embd"] // c["n_head"]
+    kv = c["n_head_kv"] * hd
+    layer = q_bytes(12, d + 2 * kv, d) + q_bytes(12, d, d) + q_bytes(12, 2 * ff, d) + q_bytes(12, d, ff)
+    head = q_bytes(14, c["n_vocab"], d)
+    return (c["n_layer"] * layer + head) // world
+
+
+def decode_kv_bytes(ctx_lens, world: int = 1) -> int:
+    """fp16 K and V bytes the attention of one step reads on one rank: per sequence
+    and layer 2 x (n_kv heads x head_dim) x 2 B x the positions attended."""
+    c = LLAMA_8B
+    kv = c["n_head_kv"] * (c["n_embd"] // c["n_head"])
+    return sum(c["n_layer"] * 2 * kv * 2 * int(n) for n in ctx_lens) // world
+
+
+def model_path(tag: str) -> str:
+    base = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
+    try:
+        st = os.statvfs(base)
+        if st.f_bavail * st.f_frsize < 8 << 30:
+            base = "/tmp"
+    except OSError:
+        base = "/tmp"
+    return os.path.join(base, f"b2_bench_{tag}_{os.getpid() if tag == 'local' else 'shared'}.gguf")
+
+
+def write_8b(b2, path: str) -> float:
+    t0 = time.perf_counter()
+    c = LLAMA_8B
+    b2.write_synthetic_llama(path + ".part", c["n_layer"], c["n_embd"], c["n_ff"], c["n_head"], c["n_head_kv"],
+                             c["n_vocab"], b2.Q4_K, embd_type=b2.Q4_K, out_type=b2.Q6_K, seed=c["seed"],
+                             rope_theta=c["rope_theta"], n_ctx_train=c["n_ctx_train"])
+    os.replace(path + ".part", path)
+    return time.perf_counter() - t0
+
+
+def prompts_8b() -> np.ndarray:
+    rng = np.random.default_rng(LLAMA_8B["seed"])
+    return rng.integers(0, LLAMA_8B["n_vocab"], (BATCH, PROMPT)).astype(np.int32)
+
+
+def launches_per_step(n_layer: int) -> int:
+    """Kernels of this library one decode step launches: embed; per layer
+    rmsnorm, QKV GEMV, rope+KV store, attention split + combine, O GEMV,
+    rmsnorm, gate|up GEMV (SwiGLU epilogue), down GEMV; then rmsnorm, head
+    GEMV and argmax.  NCCL's collective kernels are not counted."""
+    return 1 + 9 * n_layer + 3
+
+
+def time_gemv_shape(b2, qtype: int, n: int, k: int, n_tok: int, steps: int, seed: int) -> dict:
+    """CUDA-event timing of one GEMV shape over rotating weight copies (> 2x L2)."""
+    w = b2.synth_normal(seed, n * k, std=0.02).reshape(n, k)
+    q = b2.quantize_weights(qtype, w)
+    wb = q.nbytes
+    copies = max(2, -(-300_000_000 // wb))
+    mats = [b2.QMatrix(qtype, q, n, k) for _ in range(copies)]
+    x = b2.synth_normal(seed + 1, n_tok * k).reshape(n_tok, k)
+    xd = b2.DeviceBuffer.from_array(x)
+    yd = b2.DeviceBuffer(n_tok * n * 4)
+    stream = b2.Stream()
+    for i in range(3 * copies):
+        mats[i % copies].gemv_device(xd, n_tok, yd, stream.h)
+    graph = b2.Graph(stream, lambda s: [mats[i % copies].gemv_device(xd, n_tok, yd, s) for i in range(steps)])
+    graph.launch()
+    stream.synchronize()
+    e0, e1 = b2.Event(), b2.Event()
+    e0.record(stream.h)
+    graph.launch()
+    e1.record(stream.h)
+    stream.synchronize()
+    ms = e0.elapsed_ms(e1) / steps
+    nbytes = wb + n_tok * k * 4 + n_tok * n * 4
+    return {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9, "copies": copies}
+
+
+def tp_share(dist, rank: int, world: int, make_id, path: str):
+    """Rank 0's NCCL unique id (tensor parallelism) and model path, sent to every rank."""
+    obj = [make_id() if rank == 0 and world > 1 else None, path]
+    if dist is not None:
+        dist.broadcast_object_list(obj, src=0)
+    return obj[0], obj[1]
+
+
+def run_decode_ours(args, dist, rank, world, local):
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    c = LLAMA_8B
+    path = model_path("8b_q4k")
+    t_write = 0.0
+    if rank == 0 and not os.path.exists(path):
+        t_write = write_8b(b2, path)
+    nccl_id, path = tp_share(dist, rank, world, b2.nccl_unique_id, path)
+    barrier(dist)
+    t0 = time.perf_counter()
+    model = b2.Model(path, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    t_load = time.perf_counter() - t0
+    warm = max(args.warmup, 3)
+    n_ctx = PROMPT + warm + CLOCK_LOAD_STEPS + args.steps + 8
+    ctx = b2.Context(model, n_ctx=n_ctx, n_seq=BATCH)
+    prompts = prompts_8b()
+    # Prefill: each prompt through b2_decode (8-token steps), last logits -> first greedy token.
+    barrier(dist)
+    t0 = time.perf_counter()
+    first = []
+    for s in range(BATCH):
+        ctx.decode(prompts[s], pos=np.arange(PROMPT), seq=np.full(PROMPT, s), want_logits=2)
+        first.append(int(ctx.argmax()[0][-1]))
+    t_prefill = dist_max(dist, time.perf_counter() - t0)
+    seqs = np.arange(BATCH, dtype=np.int32)
+    # Warm-up steps (graph capture on the first), then the state the timed steps start from.
+    ids = ctx.generate(first, warm, seq=seqs)
+    start_tok = ids[-1].copy()
+    p_start = PROMPT + warm
+
+    def rewind():
+        for s in range(BATCH):
+            ctx.kv_seq_rm(s, p_start, -1)
+
+    e0, e1 = b2.Event(), b2.Event()
+    barrier(dist)
+    with ClockSampler(local) as clk:
+        ctx.generate(start_tok, CLOCK_LOAD_STEPS, seq=seqs)     # untimed load: clocks seen under work
+        rewind()
+        barrier(dist)
+        e0.record(ctx.stream)
+        gen = ctx.generate(start_tok, args.steps, seq=seqs)
+        e1.record(ctx.stream)
+        ctx.synchronize()
+    ms_total = dist_max(dist, e0.elapsed_ms(e1))
+    ms_step = ms_total / args.steps
+    tok_s = BATCH * args.steps / (ms_total * 1e-3)
+
+    # e2e: the llama-style host loop through the C ABI (b2_decode with host
+    # token/pos/seq arrays, b2_get_argmax back to the host) from the same state.
+    rewind()
+    tok = start_tok.copy()
+    e2e_ids = np.empty_like(gen)
+    barrier(dist)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        ctx.decode(tok, pos=np.full(BATCH, p_start + k, np.int32), seq=seqs, want_logits=1)
+        tok = ctx.argmax(BATCH)[0].copy()
+        e2e_ids[k] = tok
+    e2e_s = dist_max(dist, time.perf_counter() - t0)
+    e2e_tok_s = BATCH * args.steps / e2e_s
+
+    # Roofline of the whole step (weights + KV this rank reads) and of the
+    # dominant kernel measured alone: the gate|up Q4_K GEMV at batch 8.
+    peaks = measured_peaks()
+    ctx_lens = [p_start + k + 1 for k in range(args.steps) for _ in range(BATCH)]
+    step_bytes = decode_weight_bytes(world) + decode_kv_bytes(ctx_lens, world) / args.steps
+    step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
+    ff_l = c["n_ff"] // world
+    g = time_gemv_shape(b2, b2.Q4_K, 2 * ff_l, c["n_embd"], BATCH, 64, 7)
+    del ctx, model
+    q40 = gemv_q4_0_measure(b2, 200) if rank == 0 else None
+    out = {
+        "metric": "decode tok/s (Llama-shape 8B Q4_K, batch 8)",
+        "value": round(tok_s, 1),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": warm,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "q4_k/q6_k x q8_k -> int32 -> f32, fp16 KV",
+        "data": "synthetic: random-init Llama 8B (N(0,0.02) seed 6) GGUF Q4_K + Q6_K head; uniform random prompt ids",
+        "config": {"workload": "decode_8b_q4k: 32 layers, d 4096, ffn 14336, 32/8 heads, hd 128, vocab 128256, "
+                               "theta 5e5; batch 8 x 2048-token prompts, greedy steps (config 5)",
+                   "global_batch": BATCH, "seq_len": PROMPT, "parallelism": f"tp{world}",
+                   "l2": f"inputs larger than L2 ({decode_weight_bytes(world) / 1e9:.2f} GB of weights per rank per step)",
+                   "context_at_start": p_start, "timed_region": "b2_generate: K greedy steps, device-side feedback"},
+        "roofline": {"bound": "hbm", "kernel": f"gemv Q4_K batch 8, {2 * ff_l}x{c['n_embd']} (ffn gate|up)",
+                     "achieved": round(g["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(g["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
+                     "algorithmic_bytes_per_launch": g["bytes"], "ms_per_launch": g["ms"]},
+        "step_roofline": {"achieved": round(step_gbs, 1), "unit": "GB/s", "frac": round(step_gbs / peaks["hbm_gbs"], 4),
+                          "algorithmic_bytes_per_step": int(step_bytes),
+                          "note": "weights + fp16 KV read per rank per step / device time per step"},
+        "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 3 * BATCH * 4,
+                "d2h_bytes_per_step": 32 * 4, "greedy_ids_equal_device_loop": bool(np.array_equal(e2e_ids, gen))},
+        "gpu_launches": launches_per_step(c["n_layer"]) * args.steps,
+        "clocks": clk.summary(),
+        "setup_s": {"write_gguf": round(t_write, 1), "load": round(t_load, 1), "prefill": round(t_prefill, 1)},
+        "prefill_tok_s": round(BATCH * PROMPT / t_prefill, 1),
+    }
+    if q40 is not None:
+        out["q4_0_gemv"] = q40
+    if rank == 0:
+        out["cpu_baseline"] = cpu_decode_baseline(path, args.cpu_seconds)
+    barrier(dist)
+    if rank == 0 and not args.keep_model:
+        try:
+            os.remove(path)
+        except OSError:
+            pass
+    return out
+
+
+def cpu_decode_samples(path: str, n_samples: int | None, seconds: float | None, warm: int):
+    """Oracle decode of one token of the 8B model at context PROMPT, timed as
+    samples: one decoder layer per sample (cycling over all layers, so every
+    layer's weights come from DRAM), plus embed+final norm+head samples.
+    Returns (seconds per token extrapolated, samples, threads)."""
+    from oracle import oracle as O
+    nt = os.cpu_count() or 1
+    m = O.Model(path)
+    m.init_cache(1, PROMPT + 8)
+    m.cache_fill(0x3C00)
+    nl = m.n_layers
+    tok, pos = 17, PROMPT
+    t_layer, t_head = [], []
+
+    def sample(i):
+        j = i % (nl + 1)
+        t0 = time.perf_counter()
+        if j == nl:
+            m.forward_range(0, tok, pos, 0, 0, logits=True, n_threads=nt)
+            t_head.append(time.perf_counter() - t0)
+        else:
+            m.forward_range(0, tok, pos, j, j + 1, logits=False, n_threads=nt)
+            t_layer.append(time.perf_counter() - t0)
+
+    for i in range(warm):
+        sample(nl - i % 2)           # head and last layer: page the mapping in
+    t_layer.clear()
+    t_head.clear()
+    i, t_start = 0, time.perf_counter()
+    while True:
+        if n_samples is not None and i >= n_samples:
+            break
+        if seconds is not None and time.perf_counter() - t_start >= seconds and t_head and t_layer:
+            break
+        sample(i)
+        i += 1
+    if not t_head:
+        sample(nl)
+    per_tok = nl * float(np.mean(t_layer)) + float(np.mean(t_head))
+    return per_tok, i, nt
+
+
+def cpu_decode_baseline(path: str, seconds: float) -> dict:
+    per_tok, n, nt = cpu_decode_samples(path, None, seconds, 2)
+    return {"value": round(1.0 / per_tok, 4), "unit": "tok/s", "cores": nt, "kind": "port",
+            "sample": f"{n} samples of one token at context {PROMPT}: single decoder layers cycling over all 32 "
+                      f"plus embed+norm+head; tok/s = 1 / (32 x mean layer + head) (the CPU path decodes the batch "
+                      f"token by token, so batch 8 does not change tok/s)"}
+
+
+def run_decode_reference(args, dist, rank, world, local):
+    if rank != 0:
+        return None
+    import b2gguf as b2  # host-only: the synthetic GGUF writer
+    path = model_path("8b_q4k")
+    if not os.path.exists(path):
+        write_8b(b2, path)
+    t0 = time.perf_counter()
+    per_tok, n, nt = cpu_decode_samples(path, args.steps, None, args.warmup)
+    wall = time.perf_counter() - t0
+    if not args.keep_model:
+        try:
+            os.remove(path)
+        except OSError:
+            pass
+    v = round(1.0 / per_tok, 4)
+    return {"metric": "decode tok/s (Llama-shape 8B Q4_K, batch 8)", "value": v, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_tok * BATCH * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q4_k/q6_k x q8_k -> int32 -> f32, fp16 KV", "data": "synthetic",
+            "config": {"workload": "decode_8b_q4k (config 5)", "global_batch": BATCH, "seq_len": PROMPT,
+                       "parallelism": "host cores"},
+            "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": nt, "kind": "port",
+                             "sample": f"each step one sample: a single decoder layer (cycling over all 32) or "
+                                       f"embed+norm+head of one token at context {PROMPT}; tok/s = 1 / (32 x mean "
+                                       f"layer + head); {n} samples in {wall:.0f} s"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+TYPE_NAMES = {"q4_0": 2, "q8_0": 8, "q4_k": 12, "q6_k": 14}
+
+
+def run_gemv_op(args, dist, rank, world, local):
+    """One GEMV shape (--qtype/--rows/--cols/--batch) timed alone: the
+    profiling target for a projection of the decode step."""
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    r = time_gemv_shape(b2, TYPE_NAMES[args.qtype], args.rows, args.cols, args.batch, args.steps, 7)
+    peaks = measured_peaks()
+    gbs = dist_max(dist, r["ms"])
+    gbs = r["bytes"] * world / (gbs * 1e-3) / 1e9
+    return {"metric": f"{args.qtype} GEMV HBM GB/s ({args.rows}x{args.cols}, batch {args.batch})",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 3,
+            "ms_per_step": r["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": f"{args.qtype} x q8 -> int32 -> f32", "data": "synthetic: W N(0,0.02) seed 7, x N(0,1) seed 8",
+            "config": {"workload": f"gemv_op {args.qtype} {args.rows}x{args.cols} batch {args.batch}",
+                       "rotating_weight_copies": r["copies"], "l2": "inputs larger than L2 (rotating copies)"},
+            "roofline": {"bound": "hbm", "achieved": round(r["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(r["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
+                         "algorithmic_bytes_per_launch": r["bytes"]},
+            "gpu_launches": args.steps}
+
+
+WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
+             "gemv_q4_0": (run_gemv_ours, run_gemv_reference),
+             "gemv_op": (run_gemv_op, None)}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 512 decode / 200 GEMV)")
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemv_q4_0", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode_8b_q4k", choices=sorted(WORKLOADS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--keep-model", action="store_true", help="keep the synthetic GGUF file after the run")
+    ap.add_argument("--qtype", default="q4_k", choices=sorted(TYPE_NAMES), help="gemv_op weight type")
+    ap.add_argument("--rows", type=int, default=28672, help="gemv_op output rows")
+    ap.add_argument("--cols", type=int, default=4096, help="gemv_op input columns")
+    ap.add_argument("--batch", type=int, default=8, help="gemv_op tokens per GEMV (1..8)")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 512 if args.workload == "decode_8b_q4k" else 200
     dist, rank, world, local = dist_init()
     ours, ref = WORKLOADS[args.workload]
-    out = (ref if args.impl == "reference" else ours)(args, dist, rank, world, local)
+    if args.impl == "reference" and ref is None:
+        out = {"impl": "reference", "unavailable": f"workload {args.workload} has no CPU reference arm"}
+    else:
+        out = (ref if args.impl == "reference" else ours)(args, dist, rank, world, local)
     if rank == 0 and out is not None:
         print(json.dumps(out), flush=True)
     if dist is not None:

@@ -306,6 +306,19 @@ B2_API int b2_get_logits(b2_context* c, int32_t i, float* out, int64_t n);
 /* Greedy pick on the device for every logits row of that step: token id,
  * top-1 logit and top-1 − top-2 margin (NULL outputs are skipped). */
 B2_API int b2_get_argmax(b2_context* c, int32_t* ids, float* top1, float* margin, int32_t n);
+/* Greedy generation with the loop on the device.  No llama.cpp counterpart:
+ * it is the device-resident form of Milda's greedy turn loop, llama_decode of
+ * one token → llama_get_logits_ith → pick → feed (Milda/src/engine.cpp:1962-2117),
+ * for rows on greedy sampling.  Runs n_steps steps over the n (<= 8) distinct
+ * sequences seq[0..n) (NULL: 0..n-1), each continuing at its next position.
+ * Step 0 feeds first[i]; step t feeds row i the argmax of step t-1; the argmax
+ * of step t lands in out[t*n + i].  Steps are graph replays with no host
+ * synchronization between them; the logits of the last step stay readable
+ * through b2_get_logits / b2_get_argmax.  Returns 1 (no KV slot) without
+ * running when a sequence would pass n_ctx, 2 when the abort callback (polled
+ * before each step) stopped it, with the finished steps kept. */
+B2_API int b2_generate(b2_context* c, const int32_t* first, const int32_t* seq, int32_t n, int32_t n_steps,
+                       int32_t* out);
 B2_API int b2_synchronize_context(b2_context* c);
 
 /* KV cache: llama_memory_clear / seq_rm / seq_add / seq_pos_max

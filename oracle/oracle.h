@@ -103,6 +103,10 @@ int   orc_dev_warps_per_row(int wtype, int k, int swiglu);
 float orc_dev_row_dot(int wtype, const void* wrow, int k, const void* xq, int wpr, int direct);
 void  orc_matmul_dev(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int swiglu,
                      int n_threads);
+/* As orc_matmul_dev over k columns of rows `row_stride` bytes apart (a column
+ * slice of a wider matrix: the tensor-parallel shard of one rank). */
+void  orc_matmul_dev_strided(int wtype, const void* w, int64_t n_rows, size_t row_stride, int k, const void* xq,
+                             float* y, int swiglu, int n_threads);
 void  orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc, int64_t kv_stride, int n_pos,
                           int n_heads, int n_kv_heads, int hd, float* out);
 
@@ -114,16 +118,29 @@ void       orc_model_free(orc_model* m);
 int        orc_model_info(const orc_model* m, int32_t* out, int n_out);
 /* Per-sequence fp16 KV cache of n_ctx positions. */
 int  orc_model_init_cache(orc_model* m, int n_seq, int n_ctx);
+/* Sets every cached K and V value to the fp16 `bits` (touches the pages, so
+ * timed attention reads real memory rather than never-written zero pages). */
+void orc_model_cache_fill(orc_model* m, uint16_t bits);
 /* Runs token `token` at position `pos` of sequence `seq`; writes logits
  * (n_vocab) when logits != NULL.  Returns 0 on success. */
 int  orc_model_forward(orc_model* m, int seq, int32_t token, int pos, float* logits, int n_threads);
 /* As forward, but stops after n_layers_run layers (for bounded CPU timing). */
 int  orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, float* logits,
                               int n_threads, int n_layers_run);
+/* Layers [l0, l1) only, continuing from the residual the previous call left
+ * (the embedding is taken when l0 == 0; logits when logits != NULL).  Timing
+ * samples of single layers of a large model use it. */
+int  orc_model_forward_range(orc_model* m, int seq, int32_t token, int pos, int l0, int l1, float* logits,
+                             int n_threads);
 /* KV shift on one sequence: drop [p0, p1), re-rotate K of [p1, n_past). */
 int  orc_model_kv_shift(orc_model* m, int seq, int p0, int p1, int n_past);
 /* 1: evaluate in the GPU kernels' order (orc_*_dev), 0: the reference's. */
 void orc_model_set_device_order(orc_model* m, int on);
+/* Emulates tp tensor-parallel ranks in device order: attention-out and
+ * FFN-down become per-rank column-slice partials summed in rank order (every
+ * other projection is row-sharded and needs no change).  Returns -1 when the
+ * shapes do not split (heads, kv heads, FFN, vocab, 256-column shards). */
+int  orc_model_set_tp(orc_model* m, int tp);
 /* Per-op tap with the same names as the engine's evaluation callback. */
 typedef void (*orc_tap_fn)(const char* name, int layer, const float* data, long n, void* user);
 void orc_model_set_tap(orc_model* m, orc_tap_fn fn, void* user);

@@ -66,6 +66,9 @@ def _load() -> ctypes.CDLL:
         "orc_model_init_cache": (_i, [_vp, _i, _i]),
         "orc_model_forward": (_i, [_vp, _i, ctypes.c_int32, _i, _vp, _i]),
         "orc_model_forward_layers": (_i, [_vp, _i, ctypes.c_int32, _i, _vp, _i, _i]),
+        "orc_model_forward_range": (_i, [_vp, _i, ctypes.c_int32, _i, _i, _i, _vp, _i]),
+        "orc_model_cache_fill": (None, [_vp, ctypes.c_uint16]),
+        "orc_model_set_tp": (_i, [_vp, _i]),
         "orc_model_kv_shift": (_i, [_vp, _i, _i, _i, _i]),
         "orc_model_hidden": (_i, [_vp, _vp, _i]),
         "orc_model_set_tap": (None, [_vp, _vp, _vp]),
@@ -285,6 +288,23 @@ class Model:
         out = np.zeros(self.vocab, np.float32) if logits else None
         nl = self.n_layers if n_layers is None else n_layers
         rc = lib.orc_model_forward_layers(self.h, seq, token, pos, _p(out) if logits else None, n_threads, nl)
+        if rc != 0:
+            raise RuntimeError(f"oracle forward rc={rc}")
+        return out
+
+    def set_tp(self, tp: int) -> None:
+        """Device-order forward as `tp` tensor-parallel ranks compute it."""
+        if lib.orc_model_set_tp(self.h, tp) != 0:
+            raise ValueError(f"model does not split over {tp} ranks")
+
+    def cache_fill(self, bits: int = 0x3C00) -> None:
+        lib.orc_model_cache_fill(self.h, bits)
+
+    def forward_range(self, seq: int, token: int, pos: int, l0: int, l1: int, logits: bool = False,
+                      n_threads: int = 8):
+        """Layers [l0, l1) from the current residual (embedding when l0 == 0)."""
+        out = np.zeros(self.vocab, np.float32) if logits else None
+        rc = lib.orc_model_forward_range(self.h, seq, token, pos, l0, l1, _p(out) if logits else None, n_threads)
         if rc != 0:
             raise RuntimeError(f"oracle forward rc={rc}")
         return out

@@ -49,9 +49,23 @@ struct orc_model {
     orc_tap_fn tap;
     void* tap_user;
     int device_order;   /* 1: evaluate in the GPU kernels' order (bit-exact check) */
+    int tp;             /* tensor-parallel ranks emulated by the row-sharded projections */
+    float* part;        /* [tp][dim] partial outputs */
 };
 
 void orc_model_set_device_order(orc_model* m, int on) { m->device_order = on; }
+
+int orc_model_set_tp(orc_model* m, int tp) {
+    if (tp < 1 || m->n_heads % tp || m->n_kv % tp || m->hidden % tp || m->vocab % tp) return -1;
+    /* each rank's column slice starts on an activation block (32, or 256 for K-quants) */
+    const int bo = orc_vec_dot_type(m->layers[0].wo.type) == ORC_Q8_K ? 256 : 32;
+    const int bd = orc_vec_dot_type(m->layers[0].w2.type) == ORC_Q8_K ? 256 : 32;
+    if ((m->n_heads / tp * m->head_dim) % bo || (m->hidden / tp) % bd) return -1;
+    free(m->part);
+    m->part = (float*)malloc(sizeof(float) * (size_t)tp * m->dim);
+    m->tp = tp;
+    return m->part ? 0 : -1;
+}
 
 void orc_model_set_tap(orc_model* m, orc_tap_fn fn, void* user) {
     m->tap = fn;
@@ -242,7 +256,7 @@ void orc_model_free(orc_model* m) {
     free(m->layers);
     free(m->kc); free(m->vc);
     free(m->x); free(m->xb); free(m->xb2); free(m->q); free(m->k); free(m->v);
-    free(m->hb); free(m->hb2); free(m->xq); free(m->rope);
+    free(m->hb); free(m->hb2); free(m->xq); free(m->rope); free(m->part);
     free(m);
 }
 
@@ -279,6 +293,11 @@ int orc_model_init_cache(orc_model* m, int n_seq, int n_ctx) {
     return (m->kc && m->vc) ? 0 : -1;
 }
 
+void orc_model_cache_fill(orc_model* m, uint16_t bits) {
+    const size_t n = (size_t)m->n_seq * m->n_layers * m->n_ctx * m->head_dim * m->n_kv;
+    for (size_t i = 0; i < n; ++i) { m->kc[i] = bits; m->vc[i] = bits; }
+}
+
 /* matmul_quantized with the activation quantized for the weight's dot type
  * (Singularity quantizes to Q8_0 before every projection, :1127, :1257,
  * :1269, :1275, :1290; K-quant weights take Q8_K as in ggml). */
@@ -291,19 +310,43 @@ static void proj_mode(orc_model* m, const orc_tensor* w, const float* x, float* 
 }
 static void proj(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) { proj_mode(m, w, x, y, nt, 0); }
 
-int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, float* logits, int nt,
-                             int n_layers_run) {
+/* Attention-out and FFN-down under tensor parallelism (device order): rank r
+ * owns input columns [r*k/tp, (r+1)*k/tp) and produces a partial output over
+ * them; the partials are summed in rank order, y = ((p0 + p1) + p2) + ...,
+ * which is the reduction the GPU ranks perform after exchanging partials. */
+static void proj_reduce(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) {
+    if (m->tp <= 1 || !m->device_order) { proj(m, w, x, y, nt); return; }
+    const int k = (int)w->ne[0], n = (int)w->ne[1], kl = k / m->tp;
+    const int at = orc_vec_dot_type(w->type);
+    if (at == ORC_Q8_K) orc_quantize_row_q8_k(x, m->xq, k);
+    else orc_quantize_row_q8_0(x, m->xq, k);
+    const size_t rb = orc_row_bytes(w->type, k);
+    for (int r = 0; r < m->tp; ++r)
+        orc_matmul_dev_strided(w->type, w->data + orc_row_bytes(w->type, r * kl), n, rb, kl,
+                               (const uint8_t*)m->xq + orc_row_bytes(at, r * kl), m->part + (size_t)r * n, 0, nt);
+    for (int i = 0; i < n; ++i) {
+        float s = m->part[i];
+        for (int r = 1; r < m->tp; ++r) s = s + m->part[(size_t)r * n + i];
+        y[i] = s;
+    }
+}
+
+int orc_model_forward_range(orc_model* m, int seq, int32_t token, int pos, int l0, int l1, float* logits,
+                            int nt) {
     if (!m->kc || seq < 0 || seq >= m->n_seq || pos < 0 || pos >= m->n_ctx) return -1;
     if (token < 0 || token >= (int32_t)m->embd.ne[1]) token = 0;
     const int dim = m->dim, hd = m->head_dim, nkv = m->n_kv, kv_dim = hd * nkv;
-    /* 1. embedding row (:1066-1105) */
-    orc_dequantize_row(m->embd.type, m->embd.data + orc_row_bytes(m->embd.type, dim) * (size_t)token,
-                       m->x, dim);
+    if (l0 <= 0) {
+        /* 1. embedding row (:1066-1105) */
+        orc_dequantize_row(m->embd.type, m->embd.data + orc_row_bytes(m->embd.type, dim) * (size_t)token,
+                           m->x, dim);
+        TAP("embed", -1, m->x, dim);
+        l0 = 0;
+    }
     const float* cs = m->rope + (size_t)pos * hd;
     const size_t seq_stride = (size_t)m->n_layers * m->n_ctx * kv_dim;
-    const int nl = n_layers_run < m->n_layers ? n_layers_run : m->n_layers;
-    TAP("embed", -1, m->x, dim);
-    for (int l = 0; l < nl; ++l) {
+    const int nl = l1 < m->n_layers ? l1 : m->n_layers;
+    for (int l = l0; l < nl; ++l) {
         const orc_layer* L = &m->layers[l];
         orc_rmsnorm_ggml(m->x, (const float*)L->attn_norm.data, m->xb, dim, m->eps); /* :1121 */
         TAP("attn_norm", l, m->xb, dim);
@@ -323,7 +366,7 @@ int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, floa
         if (m->device_order) orc_attn_decode_dev(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);
         else orc_attn_decode(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);   /* :1205 */
         TAP("attn_out", l, m->xb, dim);
-        proj(m, &L->wo, m->xb, m->xb2, nt);                                           /* :1256 */
+        proj_reduce(m, &L->wo, m->xb, m->xb2, nt);                                    /* :1256 */
         TAP("attn_proj", l, m->xb2, dim);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb2[i];
         orc_rmsnorm_ggml(m->x, (const float*)L->ffn_norm.data, m->xb, dim, m->eps);  /* :1264 */
@@ -333,7 +376,7 @@ int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, floa
         if (m->device_order) orc_silu_mul_dev(m->hb, m->hb2, m->hidden);
         else orc_silu_mul(m->hb, m->hb2, m->hidden);                                  /* :1277 */
         TAP("ffn_act", l, m->hb, m->hidden);
-        proj(m, &L->w2, m->hb, m->xb, nt);                                            /* :1280 */
+        proj_reduce(m, &L->w2, m->hb, m->xb, nt);                                     /* :1280 */
         TAP("ffn_out", l, m->xb, dim);
         for (int i = 0; i < dim; ++i) m->x[i] += m->xb[i];
     }
@@ -342,6 +385,11 @@ int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, floa
     TAP("result_norm", -1, m->xb, dim);
     proj(m, &m->out, m->xb, logits, nt);                                              /* :1292 */
     return 0;
+}
+
+int orc_model_forward_layers(orc_model* m, int seq, int32_t token, int pos, float* logits, int nt,
+                             int n_layers_run) {
+    return orc_model_forward_range(m, seq, token, pos, 0, n_layers_run, logits, nt);
 }
 
 int orc_model_forward(orc_model* m, int seq, int32_t token, int pos, float* logits, int nt) {

@@ -646,6 +646,11 @@ static void* mmd_worker(void* arg) {
 
 void orc_matmul_dev(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int swiglu,
                     int n_threads) {
+    orc_matmul_dev_strided(wtype, w, n_rows, orc_row_bytes(wtype, k), k, xq, y, swiglu, n_threads);
+}
+
+void orc_matmul_dev_strided(int wtype, const void* w, int64_t n_rows, size_t row_stride, int k, const void* xq,
+                            float* y, int swiglu, int n_threads) {
     if (n_threads < 1) n_threads = 1;
     if (n_threads > 256) n_threads = 256;
     if ((int64_t)n_threads > n_rows) n_threads = (int)n_rows;
@@ -657,7 +662,7 @@ void orc_matmul_dev(int wtype, const void* w, int64_t n_rows, int k, const void*
         jobs[t].wpr = orc_dev_warps_per_row(wtype, k, swiglu);
         jobs[t].direct = !swiglu;
         jobs[t].w = (const uint8_t*)w;
-        jobs[t].row_bytes = orc_row_bytes(wtype, k);
+        jobs[t].row_bytes = row_stride;
         jobs[t].xq = xq;
         jobs[t].y = y;
         jobs[t].r0 = n_rows * t / n_threads;

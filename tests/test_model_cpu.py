@@ -52,3 +52,17 @@ def test_writer_is_deterministic(tmp_path):
     for p in (a, b):
         b2.write_synthetic_llama(p, 1, 64, 128, 2, 1, 64, b2.Q4_0, seed=3)
     assert open(a, "rb").read() == open(b, "rb").read()
+
+
+def test_oracle_layer_range_forward_composes(tiny_gguf):
+    """Layer-range steps (the bounded CPU-timing samples) compose to the full forward."""
+    a, b = O.Model(tiny_gguf), O.Model(tiny_gguf)
+    a.init_cache(1, 16)
+    b.init_cache(1, 16)
+    for p, t in enumerate([3, 9, 411]):
+        want = a.forward(0, t, p)
+        b.forward_range(0, t, p, 0, 1)
+        got = b.forward_range(0, t, p, 1, 2, logits=True)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    b.cache_fill(0x3C00)
+    assert np.all(np.isfinite(b.forward(0, 5, 3)))

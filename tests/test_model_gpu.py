@@ -162,3 +162,40 @@ def test_decode_errors_and_truncation(model_file):
     assert np.all(np.isfinite(ctx.logits(-1)))
     ctx.kv_clear()
     assert ctx.kv_pos_max(0) == -1
+
+
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_device_greedy_generate_bit_exact(model_file, use_graph):
+    """b2_generate feeds each row its own argmax on the device: ids equal the
+    oracle's greedy continuation and the last step's logits are bit-exact."""
+    rng = np.random.default_rng(3)
+    n_seq, n_steps = 2, 9
+    om = oracle_run(model_file, n_seq, 64)
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=64, n_seq=n_seq, use_graph=use_graph)
+    prompts = [rng.integers(0, om.vocab, n).tolist() for n in (7, 4)]
+    first, pos = [], []
+    for s, pr in enumerate(prompts):
+        ctx.decode(pr, pos=list(range(len(pr))), seq=[s] * len(pr), want_logits=2)
+        for p, t in enumerate(pr):
+            want = om.forward(s, t, p, logits=(p == len(pr) - 1))
+        first.append(int(np.argmax(want)))
+        pos.append(len(pr))
+    # rows in the opposite order of the sequence ids
+    got = ctx.generate(first[::-1], n_steps, seq=[1, 0])
+    assert got.shape == (n_steps, n_seq)
+    for s in range(n_seq):
+        tok = first[s]
+        for t in range(n_steps):
+            want = om.forward(s, tok, pos[s] + t)
+            tok = int(np.argmax(want))
+            assert got[t, 1 - s] == tok, f"sequence {s} step {t}"
+        assert_same(ctx.logits(1 - s), want, f"sequence {s} last step")
+    # the context continues at the next positions
+    assert ctx.kv_pos_max(0) == pos[0] + n_steps - 1
+    ctx.decode([5], pos=[pos[0] + n_steps], seq=[0], want_logits=1)
+    assert_same(ctx.logits(0), om.forward(0, 5, pos[0] + n_steps), "decode after generate")
+    rc = b2.lib.b2_generate(ctx.h, np.array([1], np.int32).ctypes.data, None, 1, 64, np.zeros(64, np.int32).ctypes.data)
+    assert rc == b2.NO_KV_SLOT
+    with pytest.raises(b2.B2Error):
+        ctx.generate([1, 2], 2, seq=[0, 0])          # repeated sequence
