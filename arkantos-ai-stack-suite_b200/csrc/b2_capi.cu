@@ -211,51 +211,11 @@ int b2_qmatrix_upload(int type, const void* gguf_bytes, int64_t n_rows, int64_t 
   m.type = type;
   m.n_rows = n_rows;
   m.k = k;
-  plan_qmatrix(m);
-  cudaGetDevice(&m.device);
-  const size_t b0 = (size_t)m.p0_row * n_rows, b1 = (size_t)m.p1_row * n_rows;
-  cudaError_t e = cudaMalloc(&m.plane0, b0);
-  if (e == cudaSuccess && b1) e = cudaMalloc(&m.plane1, b1);
-  if (e != cudaSuccess) {
-    if (m.plane0) cudaFree(m.plane0);
-    delete h;
-    set_error("qmatrix_upload: device allocation of %zu bytes: %s", b0 + b1, cudaGetErrorString(e));
-    return B2_ERR_OOM;
-  }
-  // Repack in slabs through pinned staging buffers, rows split over threads.
-  const int64_t slab = std::max<int64_t>(1, (int64_t)(64u << 20) / std::max<int64_t>(1, m.p0_row + m.p1_row));
-  uint8_t *h0 = nullptr, *h1 = nullptr;
-  e = cudaMallocHost(&h0, (size_t)m.p0_row * slab);
-  if (e == cudaSuccess && b1) e = cudaMallocHost(&h1, (size_t)m.p1_row * slab);
-  int rc = B2_OK;
-  if (e != cudaSuccess) {
-    set_error("qmatrix_upload: pinned staging: %s", cudaGetErrorString(e));
-    rc = B2_ERR_OOM;
-  }
-  const int nt = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
-  for (int64_t r0 = 0; rc == B2_OK && r0 < n_rows; r0 += slab) {
-    const int64_t r1 = std::min(n_rows, r0 + slab);
-    std::vector<std::thread> th;
-    auto work = [&](int64_t a, int64_t b) {
-      repack_rows_host(m, static_cast<const uint8_t*>(gguf_bytes), a, b, h0 + (a - r0) * m.p0_row,
-                       h1 ? h1 + (a - r0) * m.p1_row : nullptr);
-    };
-    const int64_t n = r1 - r0;
-    for (int t = 1; t < nt; ++t) th.emplace_back(work, r0 + n * t / nt, r0 + n * (t + 1) / nt);
-    work(r0, r0 + n / nt);
-    for (auto& x : th) x.join();
-    e = cudaMemcpy(m.plane0 + r0 * m.p0_row, h0, (size_t)n * m.p0_row, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess && h1) e = cudaMemcpy(m.plane1 + r0 * m.p1_row, h1, (size_t)n * m.p1_row, cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-      set_error("qmatrix_upload: copy: %s", cudaGetErrorString(e));
-      rc = B2_ERR_CUDA;
-    }
-  }
-  if (h0) cudaFreeHost(h0);
-  if (h1) cudaFreeHost(h1);
+  std::vector<const uint8_t*> rows((size_t)n_rows);
+  const size_t rb = b2::row_bytes(type, k);
+  for (int64_t r = 0; r < n_rows; ++r) rows[(size_t)r] = static_cast<const uint8_t*>(gguf_bytes) + (size_t)r * rb;
+  const int rc = upload_tiles(m, rows.data());
   if (rc != B2_OK) {
-    cudaFree(m.plane0);
-    if (m.plane1) cudaFree(m.plane1);
     delete h;
     return rc;
   }
@@ -265,17 +225,14 @@ int b2_qmatrix_upload(int type, const void* gguf_bytes, int64_t n_rows, int64_t 
 
 int b2_qmatrix_free(b2_qmatrix* h) {
   if (!h) return B2_OK;
-  if (h->m.owns) {
-    cudaFree(h->m.plane0);
-    if (h->m.plane1) cudaFree(h->m.plane1);
-  }
+  if (h->m.owns && h->m.data) cudaFree(h->m.data);
   delete h;
   return B2_OK;
 }
 
 int b2_qmatrix_device_bytes(const b2_qmatrix* h, int64_t* bytes) {
   B2_CHECK_ARG(h && bytes, "qmatrix_device_bytes arguments");
-  *bytes = (h->m.p0_row + h->m.p1_row) * h->m.n_rows;
+  *bytes = h->m.bytes();
   return B2_OK;
 }
 
@@ -310,24 +267,7 @@ int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stre
   a.y = y;
   a.y_stride = w->m.n_rows;
   a.epilogue = EPI_STORE;
-  a.row_begin = 0;
-  a.row_end = w->m.n_rows;
-  cudaStream_t s = as_stream(stream);
-  int rc = launch_gemv(a, s);
-  if (rc == B2_ERR_UNSUPPORTED) {
-    // Activations too large for shared memory next to the weight ring:
-    // quantize them once into planes, then stream.
-    ActQ act;
-    rc = alloc_act(act, act_type_for(w->m.type), n_tok, w->m.kp, s);
-    if (rc != B2_OK) return rc;
-    rc = launch_quantize_act(act.type, x, w->m.k, n_tok, w->m.k, act, s);
-    if (rc == B2_OK) {
-      a.act = &act;
-      rc = launch_gemv(a, s);
-    }
-    free_act(act, s);
-  }
-  return rc;
+  return launch_gemv(a, as_stream(stream));
 }
 
 namespace {
@@ -380,7 +320,7 @@ int b2_block_dots(const b2_qmatrix* w, int64_t row, const float* x, int32_t* out
   B2_CHECK_ARG(w->m.type != B2_Q4_K || out_m, "Q4_K needs out_m");
   cudaStream_t s = as_stream(stream);
   ActQ a;
-  int rc = alloc_act(a, act_type_for(w->m.type), 1, w->m.kp, s);
+  int rc = alloc_act(a, act_type_for(w->m.type), 1, (w->m.k + 255) / 256 * 256, s);
   if (rc != B2_OK) return rc;
   rc = launch_quantize_act(a.type, x, w->m.k, 1, w->m.k, a, s);
   if (rc == B2_OK) rc = launch_block_dots(w->m, a, row, out_i, out_m, s);

@@ -47,38 +47,17 @@ constexpr int kAttnChunk = 256;      // positions per split-K attention CTA
 struct DevQ {
   QMatrix m;
   ~DevQ() {
-    if (m.plane0) cudaFree(m.plane0);
-    if (m.plane1) cudaFree(m.plane1);
+    if (m.data) cudaFree(m.data);
   }
 };
 
 // Uploads rows given by pointers to their first byte (all rows k values of
 // `type` starting at the slice's first column).
 int upload_rows(DevQ& q, int type, int64_t k, const std::vector<const uint8_t*>& rows) {
-  QMatrix& m = q.m;
-  m.type = type;
-  m.n_rows = (int64_t)rows.size();
-  m.k = k;
-  plan_qmatrix(m);
-  cudaGetDevice(&m.device);
-  const size_t b0 = (size_t)m.p0_row * m.n_rows, b1 = (size_t)m.p1_row * m.n_rows;
-  B2_CUDA_TRY(cudaMalloc(&m.plane0, b0));
-  if (b1) B2_CUDA_TRY(cudaMalloc(&m.plane1, b1));
-  const size_t rb = row_bytes(type, k);
-  std::vector<uint8_t> h0(b0), h1(b1), rowbuf;
-  const int nt = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
-  auto work = [&](int64_t a, int64_t b) {
-    for (int64_t r = a; r < b; ++r)
-      repack_rows_host(m, rows[r], 0, 1, h0.data() + r * m.p0_row, b1 ? h1.data() + r * m.p1_row : nullptr);
-  };
-  (void)rb;
-  std::vector<std::thread> th;
-  for (int t = 1; t < nt; ++t) th.emplace_back(work, m.n_rows * t / nt, m.n_rows * (t + 1) / nt);
-  work(0, m.n_rows / nt);
-  for (auto& x : th) x.join();
-  B2_CUDA_TRY(cudaMemcpy(m.plane0, h0.data(), b0, cudaMemcpyHostToDevice));
-  if (b1) B2_CUDA_TRY(cudaMemcpy(m.plane1, h1.data(), b1, cudaMemcpyHostToDevice));
-  return B2_OK;
+  q.m.type = type;
+  q.m.n_rows = (int64_t)rows.size();
+  q.m.k = k;
+  return upload_tiles(q.m, rows.data());
 }
 
 struct Layer {
@@ -355,12 +334,11 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
       for (int64_t i = 0; i < d; ++i) rows.push_back(wd->data + i * rb + off);
       if ((rc = upload_rows(L->wdown, wd->type, m->ff_l, rows))) return rc;
     }
-    for (const DevQ* q : {&L->wqkv, &L->wo, &L->wgu, &L->wdown})
-      m->device_bytes += (q->m.p0_row + q->m.p1_row) * q->m.n_rows;
+    for (const DevQ* q : {&L->wqkv, &L->wo, &L->wgu, &L->wdown}) m->device_bytes += q->m.bytes();
     m->device_bytes += 2 * d * 4;
     m->layers.push_back(std::move(L));
   }
-  m->device_bytes += (m->head.m.p0_row + m->head.m.p1_row) * m->head.m.n_rows;
+  m->device_bytes += m->head.m.bytes();
   return B2_OK;
 }
 
@@ -539,8 +517,6 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     a.y = y;
     a.y_stride = ys;
     a.epilogue = epi;
-    a.row_begin = 0;
-    a.row_end = w.m.n_rows;
     a.status = c->status;
     a.peer = peer;
     return launch_gemv(a, s);

@@ -1,24 +1,33 @@
-// Decode GEMV / skinny GEMM over repacked GGUF weights (Q4_0, Q8_0, Q4_K, Q6_K)
+// Decode GEMV / skinny GEMM over tiled GGUF weights (Q4_0, Q8_0, Q4_K, Q6_K)
 // for 1..8 token rows — the B200 version of the reference's matmul_quantized
 // (Singularity/src/core/cortex_a5_engine.cpp:997-1027), whose per-row dot is
 // ref_vec_dot_q4_0_q8_0 / _q8_0_q8_0 (Singularity/tests/test_and_bench_a5.cpp:184-221)
 // and, for K-quants, ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K.
 //
-// Structure (one persistent CTA per SM, rows split evenly between CTAs):
-//   * warp 8 is the producer: for each stage of RG consecutive whole rows its
-//     lane 0 issues one cp.async.bulk (1-D TMA) per plane — the rows of a
-//     repacked plane are contiguous — into a ring of smem stages, completing
-//     on a full[] mbarrier.  It runs ahead of the grid dependency, so weights
-//     stream while the previous kernel drains (PDL).
-//   * warps 0..7 wait on the grid dependency, bring the activations into smem
-//     (quantizing fp32 in the CTA, bit-exact with the reference's quantizer,
-//     or copying pre-quantized planes), then consume stages: 8/RG warps share
-//     a row, lanes stride over its blocks, integer dots with dp4a, per-block
-//     fp32 scale products, warp-shuffle reduction, then the warps of a row
-//     combine through shared memory.
-//   * epilogue: store, residual add, or SwiGLU over interleaved gate/up rows.
-// Every mbarrier wait is bounded; on expiry the kernel writes a status code
-// and returns.
+// Weights are in the tile layout (8-row tiles, S unit ranges per row, see
+// QMatrix).  One CTA per SM takes a contiguous run of tile groups; a group is
+// P = 8/S tiles whose S ranges are worked by the 8 consumer warps (warp w:
+// tile w/S, range w%S).
+//   * warp 8 is the producer: lane 0 streams each stage — for every tile of
+//     the group the next U unit slots of all its ranges, one contiguous
+//     cp.async.bulk (1-D TMA) per tile — into a ring of shared-memory stages
+//     completing on full[] mbarriers.  It starts before the grid dependency
+//     resolves, so weights stream while the previous kernel drains (PDL).
+//   * warps 0..7 wait for the dependency, quantize the activations into
+//     shared memory (bit-exact with the reference's quantizers), then take
+//     the stages.  Integer dots are exact: for 1-2 tokens with dp4a (lane =
+//     tile row x unit residue mod 4), for 3-8 tokens with int8 mma.sync
+//     (m16n8k32; m16n8k16 for Q6_K's 16-weight groups; tokens are the M
+//     rows, the tile's 8 rows the N columns).  Each unit's integer sums are
+//     scaled in fp32 as the reference does, into four partial sums by unit
+//     residue mod 4; a range's sum is (a0 + a1) + (a2 + a3) and the S ranges
+//     of a row are added in order through shared memory — one order for
+//     every batch size (restated by the oracle's orc_tile_row_dot).
+//   * epilogue: store, residual add, SwiGLU over interleaved gate/up rows,
+//     or the tensor-parallel exchange into every rank's gather buffer.
+// Every mbarrier wait is bounded; a warp whose wait expires records a status
+// code and runs to the end without waiting or computing, so the named
+// barriers stay matched and the CTA always exits.
 #include "b2_common.cuh"
 #include "b2_quant.cuh"
 
@@ -27,32 +36,430 @@ namespace {
 
 constexpr int kNCW = 8;                  // consumer warps
 constexpr int kThreads = (kNCW + 1) * 32;
-constexpr int kMaxStages = 8;
-constexpr int kBarBytes = 2 * kMaxStages * 8;
+constexpr int kMaxStages = 6;
+constexpr int kBarBytes = 128;           // full[kMaxStages] + empty[kMaxStages], padded
 constexpr int kMaxTok = 8;
+constexpr int kDp4aMaxTok = 2;           // dp4a up to this many tokens, mma.sync above
+constexpr uint32_t kM4 = 0x0F0F0F0Fu;
 
 struct GemvP {
-  const uint8_t* p0;
-  const uint8_t* p1;
-  int64_t p0_row, p1_row;
-  int64_t kp, k;
-  int64_t row_begin, row_end;
+  const uint8_t* w;
+  int type, nu, S, L, slot_bytes;
+  int64_t tile_bytes, n_rows, n_tiles, k;
+  int n_tok, n_act_tok;   // tokens computed; token rows quantized into shared memory (8 for mma)
   const float* x;
   int64_t x_stride;
-  const int8_t* aq;
-  const float* ad;
-  const int16_t* absum;
   float* y;
   int64_t y_stride;
   int epilogue;
-  int n_stages;
-  int rg;                 // rows per stage (1, 2, 4 or 8)
-  uint32_t stage_bytes;
+  int U, n_stages;
+  uint32_t stage_bytes;   // P tiles x U x S slots
+  int kq;                 // activation row bytes in shared memory (k rounded up to 128)
+  uint32_t off_dx, off_bs, act_bytes;   // activation carve-up (bytes from the activation base)
   int* status;
   PeerOut peer;
 };
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNCW * 32) : "memory"); }
+// The S warps of tile slot p (barrier ids 2..9).
+__device__ __forceinline__ void tile_sync(int p, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(2 + p), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Activation bytes of token t live at act + t*kq with 16-byte chunk c stored
+// at chunk (c & ~7) | ((c + t) & 7): the 8 tokens' copies of a chunk fall in
+// distinct banks for the mma fragment loads.
+__device__ __forceinline__ int act_chunk(int c, int t) { return (c & ~7) | ((c + t) & 7); }
+__device__ __forceinline__ uint32_t act_word(const uint8_t* trow, int wi, int t) {
+  return lds32(trow + act_chunk(wi >> 2, t) * 16 + (wi & 3) * 4);
+}
+__device__ __forceinline__ uint4 act_chunk16(const uint8_t* trow, int c, int t) {
+  return lds128(trow + act_chunk(c, t) * 16);
+}
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+
+// D[16x8] = A[16xK] (tokens x k, int8; rows 8..15 zero) * B[Kx8] (k x weight rows).
+__device__ __forceinline__ void mma_k32_s8u8(int& c0, int& c1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  int4 d;   // d.z, d.w: rows 8..15 of D, the zero token rows
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
+      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
+  c0 = d.x;
+  c1 = d.y;
+}
+__device__ __forceinline__ void mma_k32_s8s8(int& c0, int& c1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  int4 d;   // d.z, d.w: rows 8..15 of D, the zero token rows
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
+      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
+  c0 = d.x;
+  c1 = d.y;
+}
+__device__ __forceinline__ void mma_k16_s8u8(int& c0, int& c1, uint32_t a0, uint32_t b0) {
+  int4 d;   // d.z, d.w: rows 8..15 of D, the zero token rows
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+               : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
+               : "r"(a0), "r"(0), "r"(b0), "r"(0));
+  c0 = d.x;
+  c1 = d.y;
+}
+
+__device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)((w >> (8 * b)) & 0xFFu); }
+__device__ __forceinline__ int sbyte(uint32_t w, int b) { return (int)(int8_t)((w >> (8 * b)) & 0xFFu); }
+
+// Q4_K 6-bit scales and mins of one row's 12 packed bytes (words s0, s1, s2):
+// sc[0..3], m[0..3], sc[4..7], m[4..7] as the bytes of four words.
+__device__ __forceinline__ void q4k_scales(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t& sl, uint32_t& ml,
+                                           uint32_t& sh, uint32_t& mh) {
+  sl = s0 & 0x3F3F3F3Fu;
+  ml = s1 & 0x3F3F3F3Fu;
+  sh = (s2 & kM4) | ((s0 >> 2) & 0x30303030u);
+  mh = ((s2 >> 4) & kM4) | ((s1 >> 2) & 0x30303030u);
+}
+
+// ---- activation prologue -----------------------------------------------------------------
+// fp32 x [n_tok][k] -> shared memory: codes (rotated chunks), the fp32 scale
+// of every unit, and the block sums the unit terms need (Q4_0: per 32; Q4_K:
+// per 32 as pairs of Q8_K sums; Q6_K: Q8_K's per 16).  Token rows
+// n_tok..n_act_tok-1 and the k tail stay zero.
+__device__ void load_act(const GemvP& p, uint8_t* act, int warp, int lane) {
+  const int tid = warp * 32 + lane;
+  float* dxs = reinterpret_cast<float*>(act + p.off_dx);
+  int16_t* bss = reinterpret_cast<int16_t*>(act + p.off_bs);
+  const int kq = p.kq;
+  for (uint32_t i = tid * 16; i < p.act_bytes; i += kNCW * 32 * 16)
+    *reinterpret_cast<uint4*>(act + i) = make_uint4(0, 0, 0, 0);
+  consumer_sync();
+  const int nb = p.nu;
+  if (p.type == B2_Q4_0 || p.type == B2_Q8_0) {
+    // One 32-value block per thread: eight float4 loads in flight, then the
+    // reference quantizer on registers.
+    for (int i = tid; i < p.n_tok * nb; i += kNCW * 32) {
+      const int t = i / nb, b = i - t * nb;
+      const float4* src = reinterpret_cast<const float4*>(p.x + t * p.x_stride + (int64_t)b * 32);
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 f = __ldg(src + j);
+        v[4 * j] = f.x;
+        v[4 * j + 1] = f.y;
+        v[4 * j + 2] = f.z;
+        v[4 * j + 3] = f.w;
+      }
+      float amax = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+      const float d = __fmul_rn(amax, 1.0f / 127.0f);
+      const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+      uint32_t w[8];
+      int sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = 0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float sc = __fmul_rn(v[j], id);
+        const float tt = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
+        int q = __float2int_rz(tt);
+        q = q < -127 ? -127 : (q > 127 ? 127 : q);
+        sum += q;
+        w[j >> 2] |= ((uint32_t)(uint8_t)q) << (8 * (j & 3));
+      }
+      uint8_t* trow = act + t * kq;
+      *reinterpret_cast<uint4*>(trow + act_chunk(2 * b, t) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(trow + act_chunk(2 * b + 1, t) * 16) = make_uint4(w[4], w[5], w[6], w[7]);
+      dxs[t * nb + b] = h2f(f2h_rn(d));
+      if (p.type == B2_Q4_0) bss[t * nb + b] = (int16_t)sum;
+    }
+  } else {
+    // One 256-value super-block per warp, 8 values per lane.
+    for (int i = warp; i < p.n_tok * nb; i += kNCW) {
+      const int t = i / nb, b = i - t * nb;
+      const float4* src = reinterpret_cast<const float4*>(p.x + t * p.x_stride + (int64_t)b * 256 + lane * 8);
+      const float4 f0 = __ldg(src), f1 = __ldg(src + 1);
+      const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+      int8_t q[8];
+      int bs;
+      const float d = quant_q8_k_lane(v, q, &bs);
+      uint2 packed;
+      packed.x = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) | ((uint32_t)(uint8_t)q[2] << 16) |
+                 ((uint32_t)(uint8_t)q[3] << 24);
+      packed.y = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
+                 ((uint32_t)(uint8_t)q[7] << 24);
+      uint8_t* trow = act + t * kq;
+      *reinterpret_cast<uint2*>(trow + act_chunk(b * 16 + lane / 2, t) * 16 + (lane & 1) * 8) = packed;
+      if (lane == 0) dxs[t * nb + b] = d;
+      if (p.type == B2_Q6_K) {
+        if ((lane & 1) == 0) bss[(t * nb + b) * 16 + lane / 2] = (int16_t)bs;
+      } else {
+        const int b32 = bs + __shfl_xor_sync(0xffffffffu, bs, 2);
+        if ((lane & 3) == 0) bss[(t * nb + b) * 8 + lane / 4] = (int16_t)b32;
+      }
+    }
+  }
+}
+
+// ---- mma path: one unit for token g (= lane/4), tile rows 2q, 2q+1 (q = lane%4) ------------
+template <int WT>
+__device__ __forceinline__ void mma_unit(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, int g, int q,
+                                         float& acc0, float& acc1) {
+  const uint8_t* trow = act + g * p.kq;
+  const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
+  const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
+  const float dx = dxs[g * p.nu + u];
+  if constexpr (WT == B2_Q4_0) {
+    const uint32_t w = lds32(sl + 16 * g + 4 * q);
+    int c0, c1;
+    mma_k32_s8u8(c0, c1, act_word(trow, u * 8 + q, g), act_word(trow, u * 8 + 4 + q, g), w & kM4, (w >> 4) & kM4);
+    const int corr = 8 * (int)bss[g * p.nu + u];
+    const uint32_t dw = lds32(sl + 128 + 4 * q);
+    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw & 0xFFFFu)), dx), (float)(c0 - corr)));
+    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw >> 16)), dx), (float)(c1 - corr)));
+  } else if constexpr (WT == B2_Q8_0) {
+    int c0, c1;
+    mma_k32_s8s8(c0, c1, act_word(trow, u * 8 + q, g), act_word(trow, u * 8 + 4 + q, g), lds32(sl + 16 * g + 4 * q),
+                 lds32(sl + 128 + 16 * g + 4 * q));
+    const uint32_t dw = lds32(sl + 256 + 4 * q);
+    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw & 0xFFFFu)), dx), (float)c0));
+    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw >> 16)), dx), (float)c1));
+  } else if constexpr (WT == B2_Q4_K) {
+    const uint8_t* m0 = sl + 1024 + 32 * q;   // d|dmin|scales of rows 2q and 2q+1
+    uint32_t sl0, ml0, sh0, mh0, sl1, ml1, sh1, mh1;
+    q4k_scales(lds32(m0 + 4), lds32(m0 + 8), lds32(m0 + 12), sl0, ml0, sh0, mh0);
+    q4k_scales(lds32(m0 + 20), lds32(m0 + 24), lds32(m0 + 28), sl1, ml1, sh1, mh1);
+    const uint8_t* qrow = sl + 128 * g;
+    int is0 = 0, is1 = 0;
+#pragma unroll
+    for (int jc = 0; jc < 4; ++jc) {
+      const uint32_t w0 = lds32(qrow + 16 * ((2 * jc + g) & 7) + 4 * q);
+      const uint32_t w1 = lds32(qrow + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * jc + h;
+        const uint32_t b0 = h ? (w0 >> 4) & kM4 : w0 & kM4;
+        const uint32_t b1 = h ? (w1 >> 4) & kM4 : w1 & kM4;
+        int c0, c1;
+        mma_k32_s8u8(c0, c1, act_word(trow, u * 64 + 8 * j + q, g), act_word(trow, u * 64 + 8 * j + 4 + q, g), b0,
+                     b1);
+        const int s0 = j < 4 ? ubyte(sl0, j) : ubyte(sh0, j - 4);
+        const int s1 = j < 4 ? ubyte(sl1, j) : ubyte(sh1, j - 4);
+        is0 += s0 * c0;
+        is1 += s1 * c1;
+      }
+    }
+    const uint4 b32 = lds128(reinterpret_cast<const uint8_t*>(bss + (g * p.nu + u) * 8));
+    int ms0 = __dp2a_lo((int)b32.x, (int)ml0, 0);
+    ms0 = __dp2a_hi((int)b32.y, (int)ml0, ms0);
+    ms0 = __dp2a_lo((int)b32.z, (int)mh0, ms0);
+    ms0 = __dp2a_hi((int)b32.w, (int)mh0, ms0);
+    int ms1 = __dp2a_lo((int)b32.x, (int)ml1, 0);
+    ms1 = __dp2a_hi((int)b32.y, (int)ml1, ms1);
+    ms1 = __dp2a_lo((int)b32.z, (int)mh1, ms1);
+    ms1 = __dp2a_hi((int)b32.w, (int)mh1, ms1);
+    const uint32_t dd0 = lds32(m0), dd1 = lds32(m0 + 16);
+    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd0 & 0xFFFFu)), dx), (float)is0));
+    acc0 = __fsub_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd0 >> 16)), dx), (float)ms0));
+    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd1 & 0xFFFFu)), dx), (float)is1));
+    acc1 = __fsub_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd1 >> 16)), dx), (float)ms1));
+  } else {  // Q6_K
+    const uint8_t* qlr = sl + 128 * g;
+    const uint8_t* qhr = sl + 1024 + 64 * g;
+    const uint8_t* scp = sl + 1536 + 32 * q;   // scales of rows 2q and 2q+1
+    const int16_t* bs = bss + (g * p.nu + u) * 16;
+    int is0 = 0, is1 = 0;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const uint32_t qh0 = lds32(qhr + 16 * ((2 * hh + g) & 3) + 4 * q);
+      const uint32_t qh1 = lds32(qhr + 16 * ((2 * hh + 1 + g) & 3) + 4 * q);
+      const uint32_t sa0 = lds32(scp + 8 * hh), sb0 = lds32(scp + 8 * hh + 4);
+      const uint32_t sa1 = lds32(scp + 16 + 8 * hh), sb1 = lds32(scp + 16 + 8 * hh + 4);
+#pragma unroll
+      for (int a1 = 0; a1 < 2; ++a1) {
+        const uint32_t ql0 = lds32(qlr + 16 * ((4 * hh + 2 * a1 + g) & 7) + 4 * q);
+        const uint32_t ql1 = lds32(qlr + 16 * ((4 * hh + 2 * a1 + 1 + g) & 7) + 4 * q);
+#pragma unroll
+        for (int nh = 0; nh < 2; ++nh) {
+          const int a = a1 + 2 * nh;   // quartile of the half
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const uint32_t ql = hf ? ql1 : ql0;
+            const uint32_t qh = hf ? qh1 : qh0;
+            const uint32_t lo = nh ? (ql >> 4) & kM4 : ql & kM4;
+            const uint32_t b0 = lo | (((qh >> (2 * a)) & 0x03030303u) << 4);
+            const int i = hh * 8 + a * 2 + hf;   // 16-weight group of the super-block
+            int c0, c1;
+            mma_k16_s8u8(c0, c1, act_word(trow, u * 64 + 4 * i + q, g), b0);
+            const int b = 32 * (int)bs[i];
+            const int gi = a * 2 + hf;           // group within the half
+            const int s0 = gi < 4 ? sbyte(sa0, gi) : sbyte(sb0, gi - 4);
+            const int s1 = gi < 4 ? sbyte(sa1, gi) : sbyte(sb1, gi - 4);
+            is0 += s0 * (c0 - b);
+            is1 += s1 * (c1 - b);
+          }
+        }
+      }
+    }
+    const uint32_t dw = lds32(sl + 1664 + 4 * q);
+    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw & 0xFFFFu)), dx), (float)is0));
+    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw >> 16)), dx), (float)is1));
+  }
+}
+
+// ---- dp4a path: one unit, tile row g, tokens 0..B-1 -----------------------------------------
+template <int WT, int B>
+__device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, int g,
+                                          float (&acc)[B]) {
+  const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
+  const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
+  if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
+    uint32_t lo[4], hi[4];
+    float dw;
+    if constexpr (WT == B2_Q4_0) {
+      const uint4 w = lds128(sl + 16 * g);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo[j] = ww[j] & kM4;
+        hi[j] = (ww[j] >> 4) & kM4;
+      }
+      dw = h2f(*reinterpret_cast<const uint16_t*>(sl + 128 + 2 * g));
+    } else {
+      const uint4 a = lds128(sl + 16 * g), b = lds128(sl + 128 + 16 * g);
+      lo[0] = a.x; lo[1] = a.y; lo[2] = a.z; lo[3] = a.w;
+      hi[0] = b.x; hi[1] = b.y; hi[2] = b.z; hi[3] = b.w;
+      dw = h2f(*reinterpret_cast<const uint16_t*>(sl + 256 + 2 * g));
+    }
+#pragma unroll
+    for (int t = 0; t < B; ++t) {
+      const uint8_t* trow = act + t * p.kq;
+      const uint4 xa = act_chunk16(trow, 2 * u, t), xb = act_chunk16(trow, 2 * u + 1, t);
+      int s;
+      if constexpr (WT == B2_Q4_0) {
+        s = dp4a_us(lo[0], xa.x, 0);
+        s = dp4a_us(lo[1], xa.y, s);
+        s = dp4a_us(lo[2], xa.z, s);
+        s = dp4a_us(lo[3], xa.w, s);
+        s = dp4a_us(hi[0], xb.x, s);
+        s = dp4a_us(hi[1], xb.y, s);
+        s = dp4a_us(hi[2], xb.z, s);
+        s = dp4a_us(hi[3], xb.w, s);
+        s -= 8 * (int)bss[t * p.nu + u];
+      } else {
+        s = dp4a_ss(lo[0], xa.x, 0);
+        s = dp4a_ss(lo[1], xa.y, s);
+        s = dp4a_ss(lo[2], xa.z, s);
+        s = dp4a_ss(lo[3], xa.w, s);
+        s = dp4a_ss(hi[0], xb.x, s);
+        s = dp4a_ss(hi[1], xb.y, s);
+        s = dp4a_ss(hi[2], xb.z, s);
+        s = dp4a_ss(hi[3], xb.w, s);
+      }
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, dxs[t * p.nu + u]), (float)s));
+    }
+  } else if constexpr (WT == B2_Q4_K) {
+    const uint4 meta = lds128(sl + 1024 + 16 * g);
+    uint32_t sl4, ml4, sh4, mh4;
+    q4k_scales(meta.y, meta.z, meta.w, sl4, ml4, sh4, mh4);
+    const float dd = h2f((uint16_t)(meta.x & 0xFFFFu)), dm = h2f((uint16_t)(meta.x >> 16));
+    const uint8_t* qrow = sl + 128 * g;
+    int is[B];
+#pragma unroll
+    for (int t = 0; t < B; ++t) is[t] = 0;
+#pragma unroll
+    for (int jc = 0; jc < 4; ++jc) {
+      const uint4 qa = lds128(qrow + 16 * ((2 * jc + g) & 7));
+      const uint4 qb = lds128(qrow + 16 * ((2 * jc + 1 + g) & 7));
+      const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      const int s_lo = jc < 2 ? ubyte(sl4, 2 * jc) : ubyte(sh4, 2 * jc - 4);
+      const int s_hi = jc < 2 ? ubyte(sl4, 2 * jc + 1) : ubyte(sh4, 2 * jc - 3);
+#pragma unroll
+      for (int t = 0; t < B; ++t) {
+        const uint8_t* trow = act + t * p.kq;
+        const int c0 = u * 16 + 4 * jc;   // the 64 activation bytes of this 32-byte qs pair
+        const uint4 x0 = act_chunk16(trow, c0, t), x1 = act_chunk16(trow, c0 + 1, t);
+        const uint4 x2 = act_chunk16(trow, c0 + 2, t), x3 = act_chunk16(trow, c0 + 3, t);
+        const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+        int dl = 0, dh = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          dl = dp4a_us(qw[i] & kM4, xl[i], dl);
+          dh = dp4a_us((qw[i] >> 4) & kM4, xh[i], dh);
+        }
+        is[t] += s_lo * dl + s_hi * dh;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < B; ++t) {
+      const uint4 b32 = lds128(reinterpret_cast<const uint8_t*>(bss + (t * p.nu + u) * 8));
+      int m = __dp2a_lo((int)b32.x, (int)ml4, 0);
+      m = __dp2a_hi((int)b32.y, (int)ml4, m);
+      m = __dp2a_lo((int)b32.z, (int)mh4, m);
+      m = __dp2a_hi((int)b32.w, (int)mh4, m);
+      const float dx = dxs[t * p.nu + u];
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dd, dx), (float)is[t]));
+      acc[t] = __fsub_rn(acc[t], __fmul_rn(__fmul_rn(dm, dx), (float)m));
+    }
+  } else {  // Q6_K
+    const uint8_t* qlr = sl + 128 * g;
+    const uint8_t* qhr = sl + 1024 + 64 * g;
+    const uint4 sc4 = lds128(sl + 1536 + 16 * g);
+    const uint32_t scw[4] = {sc4.x, sc4.y, sc4.z, sc4.w};
+    const float d6 = h2f(*reinterpret_cast<const uint16_t*>(sl + 1664 + 2 * g));
+    int is[B];
+#pragma unroll
+    for (int t = 0; t < B; ++t) is[t] = 0;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const uint4 h0 = lds128(qhr + 16 * ((2 * hh + g) & 3)), h1 = lds128(qhr + 16 * ((2 * hh + 1 + g) & 3));
+      const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+      for (int a1 = 0; a1 < 2; ++a1) {
+        const uint4 l0 = lds128(qlr + 16 * ((4 * hh + 2 * a1 + g) & 7));
+        const uint4 l1 = lds128(qlr + 16 * ((4 * hh + 2 * a1 + 1 + g) & 7));
+        const uint32_t ql[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+        for (int nh = 0; nh < 2; ++nh) {
+          const int a = a1 + 2 * nh;   // quartile of the half
+          uint32_t v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            v[i] = (nh ? (ql[i] >> 4) & kM4 : ql[i] & kM4) | (((qh[i] >> (2 * a)) & 0x03030303u) << 4);
+          const int g0 = hh * 8 + a * 2;   // groups g0 (l 0..15) and g0+1 (l 16..31)
+          const int s0 = sbyte(scw[g0 >> 2], g0 & 3), s1 = sbyte(scw[(g0 + 1) >> 2], (g0 + 1) & 3);
+#pragma unroll
+          for (int t = 0; t < B; ++t) {
+            const uint8_t* trow = act + t * p.kq;
+            const uint4 xa = act_chunk16(trow, u * 16 + g0, t), xb = act_chunk16(trow, u * 16 + g0 + 1, t);
+            int d0 = dp4a_us(v[0], xa.x, 0);
+            d0 = dp4a_us(v[1], xa.y, d0);
+            d0 = dp4a_us(v[2], xa.z, d0);
+            d0 = dp4a_us(v[3], xa.w, d0);
+            int d1 = dp4a_us(v[4], xb.x, 0);
+            d1 = dp4a_us(v[5], xb.y, d1);
+            d1 = dp4a_us(v[6], xb.z, d1);
+            d1 = dp4a_us(v[7], xb.w, d1);
+            const int16_t* bs = bss + (t * p.nu + u) * 16;
+            is[t] += s0 * (d0 - 32 * (int)bs[g0]) + s1 * (d1 - 32 * (int)bs[g0 + 1]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < B; ++t)
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(d6, dxs[t * p.nu + u]), (float)is[t]));
+  }
+}
 
 // Output (token t, row) of the store / residual-add epilogues; with a
 // tensor-parallel exchange the value goes to this rank's slot of every rank.
@@ -68,7 +475,7 @@ __device__ __forceinline__ void store_y(const GemvP& p, int t, int64_t row, floa
 
 // After every consumer thread of the CTA has stored: count the CTA; the last
 // CTA of the grid publishes the next epoch to every rank's flag.  Stores reach
-// peers before the count (fence.sys by the counting thread after the CTA
+// peers before the count (fence.sys by each storing thread, then the CTA
 // barrier), and the count before the flags (fence.sys in the last CTA).
 __device__ __forceinline__ void signal_peers(const GemvP& p) {
   __threadfence_system();
@@ -82,303 +489,49 @@ __device__ __forceinline__ void signal_peers(const GemvP& p) {
   }
 }
 
-// ---- activation prologue ---------------------------------------------------------
-template <int WT, int B>
-__device__ void load_act(const GemvP& p, int8_t* aq, float* ad, int16_t* ab, int warp, int lane) {
-  const int64_t kp = p.kp;
-  const int tid = warp * 32 + lane;
-  if (p.x != nullptr) {
-    if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
-      // One 32-value block per thread: eight float4 loads in flight, then the
-      // reference quantizer on registers (no shuffles).
-      const int64_t nbk = kp / 32;
-      for (int64_t i = tid; i < (int64_t)B * nbk; i += kNCW * 32) {
-        const int t = (int)(i / nbk);
-        const int64_t kb = i - (int64_t)t * nbk;
-        float v[32];
-        if (kb * 32 < p.k) {   // k is a multiple of 32: the block is entirely in range
-          const float4* src = reinterpret_cast<const float4*>(p.x + t * p.x_stride + kb * 32);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 f = __ldg(src + j);
-            v[4 * j] = f.x;
-            v[4 * j + 1] = f.y;
-            v[4 * j + 2] = f.z;
-            v[4 * j + 3] = f.w;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-        }
-        float amax = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-        const float d = __fmul_rn(amax, 1.0f / 127.0f);
-        const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
-        uint32_t w[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = 0;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float sc = __fmul_rn(v[j], id);
-          const float tt = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
-          int q = __float2int_rz(tt);
-          q = q < -127 ? -127 : (q > 127 ? 127 : q);
-          w[j >> 2] |= ((uint32_t)(uint8_t)q) << (8 * (j & 3));
-        }
-        uint4* dst = reinterpret_cast<uint4*>(aq + t * kp + kb * 32);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        ad[t * nbk + kb] = h2f(f2h_rn(d));
+// Finishes a tile: red[r*64 + e] holds range r's sum of element e =
+// token*8 + row; one warp adds the ranges in order and writes.
+__device__ __forceinline__ void finish_tile(const GemvP& p, const float* red, int64_t tile, int lane) {
+  const int S = p.S;
+  if (p.epilogue == EPI_SWIGLU) {
+    // lane = token*4 + pair; tile rows (2*pair, 2*pair+1) are (gate, up) of one feature
+    const int t = lane >> 2, pr = lane & 3;
+    const int64_t row = tile * 8 + 2 * pr;
+    if (t < p.n_tok && row < p.n_rows) {
+      float gs = red[t * 8 + 2 * pr], us = red[t * 8 + 2 * pr + 1];
+      for (int r = 1; r < S; ++r) {
+        gs = __fadd_rn(gs, red[r * 64 + t * 8 + 2 * pr]);
+        us = __fadd_rn(us, red[r * 64 + t * 8 + 2 * pr + 1]);
       }
-    } else {
-      // One 256-value super-block per warp, batches of U in flight.
-      constexpr int U = 4;
-      const int64_t nbk = kp / 256;
-      const int64_t total = (int64_t)B * nbk;
-      for (int64_t i0 = warp; i0 < total; i0 += (int64_t)kNCW * U) {
-        float v[U][8];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t i = i0 + (int64_t)u * kNCW;
-          float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
-          if (i < total) {
-            const int t = (int)(i / nbk);
-            const int64_t e0 = (i - (int64_t)t * nbk) * 256 + lane * 8;
-            if (e0 < p.k) {   // k is a multiple of 256: all 8 values are in range
-              const float4* src = reinterpret_cast<const float4*>(p.x + t * p.x_stride + e0);
-              a = __ldg(src);
-              c = __ldg(src + 1);
-            }
-          }
-          v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
-          v[u][4] = c.x; v[u][5] = c.y; v[u][6] = c.z; v[u][7] = c.w;
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t i = i0 + (int64_t)u * kNCW;
-          if (i < total) {
-            const int t = (int)(i / nbk);
-            const int64_t kb = i - (int64_t)t * nbk;
-            const int64_t e0 = kb * 256 + lane * 8;
-            int8_t q[8];
-            int bs;
-            const float d = quant_q8_k_lane(v[u], q, &bs);
-            uint2 packed;
-            packed.x = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) | ((uint32_t)(uint8_t)q[2] << 16) |
-                       ((uint32_t)(uint8_t)q[3] << 24);
-            packed.y = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
-                       ((uint32_t)(uint8_t)q[7] << 24);
-            *reinterpret_cast<uint2*>(aq + t * kp + e0) = packed;
-            if ((lane & 1) == 0) ab[t * (kp / 16) + kb * 16 + lane / 2] = (int16_t)bs;
-            if (lane == 0) ad[t * nbk + kb] = d;
-          }
-        }
-      }
+      p.y[t * p.y_stride + row / 2] = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, b2_expf(-gs))), us);
     }
-  } else {
-    const int64_t nq = (int64_t)B * kp / 16;
-    for (int64_t i = tid; i < nq; i += kNCW * 32)
-      reinterpret_cast<uint4*>(aq)[i] = reinterpret_cast<const uint4*>(p.aq)[i];
-    const int64_t nd = (WT == B2_Q4_0 || WT == B2_Q8_0) ? (int64_t)B * kp / 32 : (int64_t)B * kp / 256;
-    for (int64_t i = tid; i < nd; i += kNCW * 32) ad[i] = p.ad[i];
-    if constexpr (WT == B2_Q4_K || WT == B2_Q6_K) {
-      const int64_t nb = (int64_t)B * kp / 16;
-      for (int64_t i = tid; i < nb; i += kNCW * 32) ab[i] = p.absum[i];
+    return;
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int e = lane + 32 * h;
+    const int t = e >> 3, rr = e & 7;
+    const int64_t row = tile * 8 + rr;
+    if (t < p.n_tok && row < p.n_rows) {
+      float v = red[e];
+      for (int r = 1; r < S; ++r) v = __fadd_rn(v, red[r * 64 + e]);
+      store_y(p, t, row, v);
     }
   }
 }
 
-// ---- one row of a stage ---------------------------------------------------------------
-// Lanes of the warps sharing the row stride over its blocks starting at
-// `first` with step `step`; partial sums accumulate into acc[B].
-template <int WT, int B>
-__device__ __forceinline__ void compute_row(const uint8_t* rp0, const uint8_t* rp1, int64_t kp, const int8_t* aq,
-                                            const float* ad, const int16_t* ab, int first, int step, float (&acc)[B]) {
-  if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
-    const int nb = (int)(kp / 32);
-    constexpr int W32 = (WT == B2_Q4_0) ? 4 : 8;
-#pragma unroll 2
-    for (int blk = first; blk < nb; blk += step) {
-      uint32_t wv[W32];
-      const uint4* wp = reinterpret_cast<const uint4*>(rp0 + blk * (W32 * 4));
-#pragma unroll
-      for (int v = 0; v < W32 / 4; ++v) {
-        const uint4 u = wp[v];
-        wv[4 * v + 0] = u.x;
-        wv[4 * v + 1] = u.y;
-        wv[4 * v + 2] = u.z;
-        wv[4 * v + 3] = u.w;
-      }
-      const float dw = h2f(reinterpret_cast<const uint16_t*>(rp1)[blk]);
-      int lo[4], hi[4];
-      if constexpr (WT == B2_Q4_0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          lo[j] = nib_lo_s8(wv[j]);
-          hi[j] = nib_hi_s8(wv[j]);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < B; ++t) {
-        const uint4* xp = reinterpret_cast<const uint4*>(aq + t * kp + blk * 32);
-        const uint4 xa = xp[0], xb = xp[1];
-        int s;
-        if constexpr (WT == B2_Q4_0) {
-          s = __dp4a(lo[0], (int)xa.x, 0);
-          s = __dp4a(lo[1], (int)xa.y, s);
-          s = __dp4a(lo[2], (int)xa.z, s);
-          s = __dp4a(lo[3], (int)xa.w, s);
-          s = __dp4a(hi[0], (int)xb.x, s);
-          s = __dp4a(hi[1], (int)xb.y, s);
-          s = __dp4a(hi[2], (int)xb.z, s);
-          s = __dp4a(hi[3], (int)xb.w, s);
-        } else {
-          s = __dp4a((int)wv[0], (int)xa.x, 0);
-          s = __dp4a((int)wv[1], (int)xa.y, s);
-          s = __dp4a((int)wv[2], (int)xa.z, s);
-          s = __dp4a((int)wv[3], (int)xa.w, s);
-          s = __dp4a((int)wv[4], (int)xb.x, s);
-          s = __dp4a((int)wv[5], (int)xb.y, s);
-          s = __dp4a((int)wv[6], (int)xb.z, s);
-          s = __dp4a((int)wv[7], (int)xb.w, s);
-        }
-        acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, ad[t * (kp / 32) + blk]), (float)s));
-      }
-    }
-  } else if constexpr (WT == B2_Q4_K) {
-    const int ntask = (int)(kp / 256) * 4;
-    for (int task = first; task < ntask; task += step) {
-      const int sb = task >> 2, c4 = task & 3;
-      const uint8_t* bp = rp0 + sb * 144;
-      const uint32_t dpair = *reinterpret_cast<const uint32_t*>(bp);
-      const float dd = h2f((uint16_t)(dpair & 0xFFFFu));
-      const float dm = h2f((uint16_t)(dpair >> 16));
-      const uint8_t* s = bp + 4;
-      const int ja = 2 * c4, jb = 2 * c4 + 1;
-      int sc0, sc1, m0, m1;
-      if (ja < 4) {
-        sc0 = s[ja] & 63;
-        m0 = s[ja + 4] & 63;
-        sc1 = s[jb] & 63;
-        m1 = s[jb + 4] & 63;
-      } else {
-        sc0 = (s[ja + 4] & 0x0F) | ((s[ja - 4] >> 6) << 4);
-        m0 = (s[ja + 4] >> 4) | ((s[ja] >> 6) << 4);
-        sc1 = (s[jb + 4] & 0x0F) | ((s[jb - 4] >> 6) << 4);
-        m1 = (s[jb + 4] >> 4) | ((s[jb] >> 6) << 4);
-      }
-      const uint4 q0 = *reinterpret_cast<const uint4*>(bp + 16 + c4 * 32);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(bp + 32 + c4 * 32);
-      const uint32_t m4 = 0x0F0F0F0Fu;
-      const int l[8] = {(int)(q0.x & m4), (int)(q0.y & m4), (int)(q0.z & m4), (int)(q0.w & m4),
-                        (int)(q1.x & m4), (int)(q1.y & m4), (int)(q1.z & m4), (int)(q1.w & m4)};
-      const int h[8] = {(int)((q0.x >> 4) & m4), (int)((q0.y >> 4) & m4), (int)((q0.z >> 4) & m4),
-                        (int)((q0.w >> 4) & m4), (int)((q1.x >> 4) & m4), (int)((q1.y >> 4) & m4),
-                        (int)((q1.z >> 4) & m4), (int)((q1.w >> 4) & m4)};
-      const int64_t col0 = (int64_t)sb * 256;
-#pragma unroll
-      for (int t = 0; t < B; ++t) {
-        const uint4* xp = reinterpret_cast<const uint4*>(aq + t * kp + col0 + c4 * 64);
-        const uint4 xa0 = xp[0], xa1 = xp[1], xb0 = xp[2], xb1 = xp[3];
-        const uint2 bs = *reinterpret_cast<const uint2*>(ab + t * (kp / 16) + col0 / 16 + c4 * 4);
-        const int b01 = (int)(int16_t)(bs.x & 0xFFFFu) + (int)(int16_t)(bs.x >> 16);
-        const int b23 = (int)(int16_t)(bs.y & 0xFFFFu) + (int)(int16_t)(bs.y >> 16);
-        const float dy = ad[t * (kp / 256) + sb];
-        int lo = __dp4a(l[0], (int)xa0.x, 0);
-        lo = __dp4a(l[1], (int)xa0.y, lo);
-        lo = __dp4a(l[2], (int)xa0.z, lo);
-        lo = __dp4a(l[3], (int)xa0.w, lo);
-        lo = __dp4a(l[4], (int)xa1.x, lo);
-        lo = __dp4a(l[5], (int)xa1.y, lo);
-        lo = __dp4a(l[6], (int)xa1.z, lo);
-        lo = __dp4a(l[7], (int)xa1.w, lo);
-        int hi = __dp4a(h[0], (int)xb0.x, 0);
-        hi = __dp4a(h[1], (int)xb0.y, hi);
-        hi = __dp4a(h[2], (int)xb0.z, hi);
-        hi = __dp4a(h[3], (int)xb0.w, hi);
-        hi = __dp4a(h[4], (int)xb1.x, hi);
-        hi = __dp4a(h[5], (int)xb1.y, hi);
-        hi = __dp4a(h[6], (int)xb1.z, hi);
-        hi = __dp4a(h[7], (int)xb1.w, hi);
-        const int isum = sc0 * lo + sc1 * hi;
-        const int msum = m0 * b01 + m1 * b23;
-        acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dd, dy), (float)isum));
-        acc[t] = __fsub_rn(acc[t], __fmul_rn(__fmul_rn(dm, dy), (float)msum));
-      }
-    }
-  } else {  // Q6_K
-    const int ntask = (int)(kp / 256) * 4;
-    for (int task = first; task < ntask; task += step) {
-      const int sb = task >> 2, hh = (task >> 1) & 1, gp = task & 1;
-      const uint8_t* bp = rp0 + sb * 208;
-      const uint4 l0 = *reinterpret_cast<const uint4*>(bp + hh * 64 + gp * 32);
-      const uint4 l1 = *reinterpret_cast<const uint4*>(bp + hh * 64 + gp * 32 + 16);
-      const uint4 h0 = *reinterpret_cast<const uint4*>(bp + 128 + hh * 32);
-      const uint4 h1 = *reinterpret_cast<const uint4*>(bp + 128 + hh * 32 + 16);
-      const uint32_t qlw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-      const uint32_t qhw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-      int la[8], lb[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t a = (qlw[i] & 0x0F0F0F0Fu) | (((qhw[i] >> (2 * gp)) & 0x03030303u) << 4);
-        const uint32_t b = ((qlw[i] >> 4) & 0x0F0F0F0Fu) | (((qhw[i] >> (2 * gp + 4)) & 0x03030303u) << 4);
-        la[i] = (int)((a + 0x60606060u) ^ 0x80808080u);
-        lb[i] = (int)((b + 0x60606060u) ^ 0x80808080u);
-      }
-      const int8_t* sc = reinterpret_cast<const int8_t*>(bp + 192);
-      const int sca0 = sc[hh * 8 + 2 * gp], sca1 = sc[hh * 8 + 2 * gp + 1];
-      const int scb0 = sc[hh * 8 + 2 * (gp + 2)], scb1 = sc[hh * 8 + 2 * (gp + 2) + 1];
-      const float d6 = h2f(reinterpret_cast<const uint16_t*>(rp1)[sb]);
-      const int64_t col0 = (int64_t)sb * 256 + hh * 128;
-#pragma unroll
-      for (int t = 0; t < B; ++t) {
-        const int8_t* xb = aq + t * kp + col0;
-        const uint4 xa0 = *reinterpret_cast<const uint4*>(xb + gp * 32);
-        const uint4 xa1 = *reinterpret_cast<const uint4*>(xb + gp * 32 + 16);
-        const uint4 xb0 = *reinterpret_cast<const uint4*>(xb + (gp + 2) * 32);
-        const uint4 xb1 = *reinterpret_cast<const uint4*>(xb + (gp + 2) * 32 + 16);
-        const float dy = ad[t * (kp / 256) + sb];
-        int a0 = __dp4a(la[0], (int)xa0.x, 0);
-        a0 = __dp4a(la[1], (int)xa0.y, a0);
-        a0 = __dp4a(la[2], (int)xa0.z, a0);
-        a0 = __dp4a(la[3], (int)xa0.w, a0);
-        int a1 = __dp4a(la[4], (int)xa1.x, 0);
-        a1 = __dp4a(la[5], (int)xa1.y, a1);
-        a1 = __dp4a(la[6], (int)xa1.z, a1);
-        a1 = __dp4a(la[7], (int)xa1.w, a1);
-        int b0 = __dp4a(lb[0], (int)xb0.x, 0);
-        b0 = __dp4a(lb[1], (int)xb0.y, b0);
-        b0 = __dp4a(lb[2], (int)xb0.z, b0);
-        b0 = __dp4a(lb[3], (int)xb0.w, b0);
-        int b1 = __dp4a(lb[4], (int)xb1.x, 0);
-        b1 = __dp4a(lb[5], (int)xb1.y, b1);
-        b1 = __dp4a(lb[6], (int)xb1.z, b1);
-        b1 = __dp4a(lb[7], (int)xb1.w, b1);
-        const int isum = sca0 * a0 + sca1 * a1 + scb0 * b0 + scb1 * b1;
-        acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(d6, dy), (float)isum));
-      }
-    }
-  }
-}
-
-template <int WT, int B>
-__global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const GemvP p) {
+template <int WT, int MODE>   // MODE 0: mma.sync; 1, 2: dp4a over that many tokens
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvP p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   uint8_t* ring = smem + kBarBytes;
-  int8_t* aq = reinterpret_cast<int8_t*>(ring + (size_t)p.n_stages * p.stage_bytes);
-  const int64_t kp = p.kp;
-  float* ad = reinterpret_cast<float*>(aq + (size_t)B * kp);
-  const int64_t nd = (WT == B2_Q4_0 || WT == B2_Q8_0) ? kp / 32 : kp / 256;
-  // bsum rows are read 8 bytes at a time: keep the array 16-byte aligned.
-  int16_t* ab = reinterpret_cast<int16_t*>(reinterpret_cast<uint8_t*>(ad) + (((size_t)B * nd * 4 + 15) / 16 * 16));
-  __shared__ float red[2][kNCW][kMaxTok];
+  uint8_t* act = ring + (size_t)p.n_stages * p.stage_bytes;
+  __shared__ float red[2][kNCW][64];   // [group parity][warp = slot*S + range][token*8 + row]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ns = p.n_stages;
-  const int rg = p.rg;
+  const int S = p.S, P = kNCW / S;
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
@@ -389,95 +542,108 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
   __syncthreads();
   pdl_launch_dependents();
 
-  // Balanced contiguous row range of this CTA, in whole row pairs.
-  const int64_t n = p.row_end - p.row_begin;
-  const int64_t n_pairs = (n + 1) / 2;
-  const int64_t pr0 = n_pairs * blockIdx.x / gridDim.x;
-  const int64_t pr1 = n_pairs * (blockIdx.x + 1) / gridDim.x;
-  const int64_t r0 = p.row_begin + 2 * pr0;
-  const int64_t r1 = min(p.row_begin + 2 * pr1, p.row_end);
-  const int total = r1 > r0 ? (int)((r1 - r0 + rg - 1) / rg) : 0;
-  const uint32_t p1_off = (uint32_t)(rg * p.p0_row);
+  // Tile groups of this CTA (contiguous, balanced) and the stage sequence.
+  const int64_t n_groups = (p.n_tiles + P - 1) / P;
+  const int64_t g0 = n_groups * blockIdx.x / gridDim.x, g1 = n_groups * (blockIdx.x + 1) / gridDim.x;
+  const int n_ch = (p.L + p.U - 1) / p.U;   // stages per group
+  const int64_t total = (g1 - g0) * n_ch;
+  const uint32_t piece = (uint32_t)p.U * S * p.slot_bytes;   // one tile's part of a stage
 
   if (warp == kNCW) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      for (int st = 0; st < total; ++st) {
-        const int s = st % ns;
+      for (int64_t st = 0; st < total; ++st) {
+        const int s = (int)(st % ns);
         const uint32_t ph = (uint32_t)(st / ns) & 1u;
         if (st >= ns && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.status, 2)) return;
-        const int64_t rb = r0 + (int64_t)st * rg;
-        const int rows = (int)min((int64_t)rg, r1 - rb);
+        const int64_t grp = g0 + st / n_ch;
+        const int ch = (int)(st % n_ch);
+        const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
+        const uint32_t bytes = (uint32_t)ni * S * p.slot_bytes;
+        uint32_t tx = 0;
+        for (int pp = 0; pp < P; ++pp)
+          if (grp * P + pp < p.n_tiles) tx += bytes;
+        mbar_arrive_expect_tx(&full[s], tx);
         uint8_t* sp = ring + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(rows * (p.p0_row + p.p1_row)));
-        bulk_g2s(sp, p.p0 + rb * p.p0_row, (uint32_t)(rows * p.p0_row), &full[s]);
-        if (p.p1_row) bulk_g2s(sp + p1_off, p.p1 + rb * p.p1_row, (uint32_t)(rows * p.p1_row), &full[s]);
+        for (int pp = 0; pp < P; ++pp) {
+          const int64_t tile = grp * P + pp;
+          if (tile < p.n_tiles)
+            bulk_g2s(sp + pp * piece, p.w + tile * p.tile_bytes + (int64_t)i0 * S * p.slot_bytes, bytes, &full[s]);
+        }
       }
     }
     return;
   }
 
   // ---------------- consumers ----------------
-  // A timed-out wait does not leave the loop early: the warp keeps taking the
-  // same named barriers as the others (skipping its waits and math), so the
-  // CTA always reaches its end and, with an exchange, still signals peers.
   pdl_wait();
-  load_act<WT, B>(p, aq, ad, ab, warp, lane);
+  load_act(p, act, warp, lane);
   consumer_sync();
-  bool ok = true;
 
-  const int wpr = kNCW / rg;               // warps per row
-  const int my_row = warp / wpr;           // row of the stage this warp works on
-  const int sub = warp - my_row * wpr;
-  const int first = sub * 32 + lane, step = wpr * 32;
-  const int tid = warp * 32 + lane;
-  for (int st = 0; st < total; ++st) {
-    const int s = st % ns;
-    const uint32_t ph = (uint32_t)(st / ns) & 1u;
-    if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
-    const uint8_t* sp = ring + (size_t)s * p.stage_bytes;
-    const int64_t rb = r0 + (int64_t)st * rg;
-    const int rows = (int)min((int64_t)rg, r1 - rb);
-    float acc[B];
+  const int slot_p = warp / S, r = warp - slot_p * S;
+  const int g = lane >> 2, q = lane & 3;     // mma: token g, tile rows 2q, 2q+1
+  const int dg = lane & 7, dq = lane >> 3;   // dp4a: tile row dg, unit residue dq
+  constexpr int NB = MODE == 0 ? 1 : MODE;
+  float acc[4][2];   // mma partial sums [residue][row]
+  float dacc[NB];    // dp4a partial sums [token] of residue dq
+  bool ok = true;
+  int64_t st = 0;
+  for (int64_t grp = g0; grp < g1; ++grp) {
+    const int64_t tile = grp * P + slot_p;
+    const bool live = tile < p.n_tiles;
 #pragma unroll
-    for (int t = 0; t < B; ++t) acc[t] = 0.0f;
-    if (ok && my_row < rows)
-      compute_row<WT, B>(sp + my_row * p.p0_row, sp + p1_off + my_row * p.p1_row, kp, aq, ad, ab, first, step, acc);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if (wpr == 1 && p.epilogue != EPI_SWIGLU) {
-      // Each warp owns a whole row: reduce and write, no cross-warp step.
+    for (int a = 0; a < 4; ++a) acc[a][0] = acc[a][1] = 0.0f;
 #pragma unroll
-      for (int t = 0; t < B; ++t) {
-        const float v = warp_sum(acc[t]);
-        if (lane == 0 && my_row < rows) store_y(p, t, rb + my_row, v);
-      }
-      continue;
-    }
-#pragma unroll
-    for (int t = 0; t < B; ++t) {
-      const float v = warp_sum(acc[t]);
-      if (lane == 0) red[st & 1][warp][t] = v;
-    }
-    consumer_sync();
-    // Combine the warps of each row; one thread per (row, token) writes.
-    if (p.epilogue == EPI_SWIGLU) {
-      if (tid < (rows / 2) * B) {
-        const int pr = tid / B, t = tid - pr * B;
-        float g = 0.0f, u = 0.0f;
-        for (int w = 0; w < wpr; ++w) {
-          g = __fadd_rn(g, red[st & 1][(2 * pr) * wpr + w][t]);
-          u = __fadd_rn(u, red[st & 1][(2 * pr + 1) * wpr + w][t]);
+    for (int t = 0; t < NB; ++t) dacc[t] = 0.0f;
+    for (int ch = 0; ch < n_ch; ++ch, ++st) {
+      const int s = (int)(st % ns);
+      const uint32_t ph = (uint32_t)(st / ns) & 1u;
+      if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
+      const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
+      if (ok && live) {
+        const uint8_t* base = ring + (size_t)s * p.stage_bytes + slot_p * piece;
+        // this stage holds units [ua, ub) of the warp's range
+        const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);
+        if constexpr (MODE == 0) {
+          for (int u = ua; u < ub; ++u) {
+            const uint8_t* sl = base + (size_t)((u - ua) * S + r) * p.slot_bytes;
+            // the residue is warp-uniform: a branch keeps the sums in registers
+            const int a = u & 3;
+            if (a == 0) mma_unit<WT>(p, sl, act, u, g, q, acc[0][0], acc[0][1]);
+            else if (a == 1) mma_unit<WT>(p, sl, act, u, g, q, acc[1][0], acc[1][1]);
+            else if (a == 2) mma_unit<WT>(p, sl, act, u, g, q, acc[2][0], acc[2][1]);
+            else mma_unit<WT>(p, sl, act, u, g, q, acc[3][0], acc[3][1]);
+          }
+        } else {
+          // the four lane groups take four consecutive units (residues 0..3) at once
+          for (int u4 = ua & ~3; u4 < ub; u4 += 4) {
+            const int u = u4 + dq;
+            if (u >= ua && u < ub)
+              dp4a_unit<WT, NB>(p, base + (size_t)((u - ua) * S + r) * p.slot_bytes, act, u, dg, dacc);
+          }
         }
-        const int64_t row = rb + 2 * pr;
-        p.y[t * p.y_stride + row / 2] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, b2_expf(-g))), u);
       }
-    } else if (tid < rows * B) {
-      const int r = tid / B, t = tid - r * B;
-      float v = 0.0f;
-      for (int w = 0; w < wpr; ++w) v = __fadd_rn(v, red[st & 1][r * wpr + w][t]);
-      store_y(p, t, rb + r, v);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
+    // The range's sums, (a0 + a1) + (a2 + a3), into red[parity][warp][token*8 + row].
+    float* rw = red[grp & 1][warp];
+    if constexpr (MODE == 0) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        rw[g * 8 + 2 * q + e] = __fadd_rn(__fadd_rn(acc[0][e], acc[1][e]), __fadd_rn(acc[2][e], acc[3][e]));
+    } else {
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+        // residues dq and dq^1 are 8 lanes apart, dq and dq^2 16 lanes apart
+        float v = __fadd_rn(dacc[t], __shfl_xor_sync(0xffffffffu, dacc[t], 8));
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 16));
+        if (dq == 0) rw[t * 8 + dg] = v;
+      }
+    }
+    if (S > 1) tile_sync(slot_p, S * 32);
+    else __syncwarp();
+    if (r == 0 && live) finish_tile(p, red[grp & 1][slot_p * S], tile, lane);
   }
   if (p.peer.n) {
     __threadfence_system();   // this thread's peer stores, before the CTA is counted
@@ -486,31 +652,25 @@ __global__ void __launch_bounds__(kThreads, (B <= 4) ? 2 : 1) gemv_kernel(const 
   }
 }
 
-// 227 KB opt-in per block, less 1 KB for the kernel's static shared memory.
-constexpr int kSmemCap = 227 * 1024 - 1024;
+// 227 KB opt-in per block, less the kernel's static shared memory.
+constexpr int kSmemCap = 227 * 1024 - (int)sizeof(float) * 2 * kNCW * 64 - 1024;
 
-template <int WT, int B>
-int set_smem_attr() {
-  B2_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<WT, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap));
+template <int WT, int MODE>
+int set_attr() {
+  B2_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<WT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap));
   return B2_OK;
 }
 
 template <int WT>
-int set_smem_attr_all() {
-  int rc = set_smem_attr<WT, 1>();
-  if (!rc) rc = set_smem_attr<WT, 2>();
-  if (!rc) rc = set_smem_attr<WT, 3>();
-  if (!rc) rc = set_smem_attr<WT, 4>();
-  if (!rc) rc = set_smem_attr<WT, 5>();
-  if (!rc) rc = set_smem_attr<WT, 6>();
-  if (!rc) rc = set_smem_attr<WT, 7>();
-  if (!rc) rc = set_smem_attr<WT, 8>();
+int set_attr_all() {
+  int rc = set_attr<WT, 0>();
+  if (!rc) rc = set_attr<WT, 1>();
+  if (!rc) rc = set_attr<WT, 2>();
   return rc;
 }
 
-template <int WT, int B>
+template <int WT, int MODE>
 int launch_t(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
-  auto kern = gemv_kernel<WT, B>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -521,24 +681,15 @@ int launch_t(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<WT, MODE>, p));
   return B2_OK;
 }
 
 template <int WT>
-int launch_w(const GemvP& p, int B, int grid, size_t smem, cudaStream_t s) {
-  switch (B) {
-    case 1: return launch_t<WT, 1>(p, grid, smem, s);
-    case 2: return launch_t<WT, 2>(p, grid, smem, s);
-    case 3: return launch_t<WT, 3>(p, grid, smem, s);
-    case 4: return launch_t<WT, 4>(p, grid, smem, s);
-    case 5: return launch_t<WT, 5>(p, grid, smem, s);
-    case 6: return launch_t<WT, 6>(p, grid, smem, s);
-    case 7: return launch_t<WT, 7>(p, grid, smem, s);
-    case 8: return launch_t<WT, 8>(p, grid, smem, s);
-  }
-  set_error("gemv: n_tok %d outside [1, 8]", B);
-  return B2_ERR_INVALID;
+int launch_w(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
+  if (p.n_tok > kDp4aMaxTok) return launch_t<WT, 0>(p, grid, smem, s);
+  if (p.n_tok == 1) return launch_t<WT, 1>(p, grid, smem, s);
+  return launch_t<WT, 2>(p, grid, smem, s);
 }
 
 }  // namespace
@@ -548,10 +699,10 @@ int prepare_gemv_kernels() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && done[dev]) return B2_OK;
-  int rc = set_smem_attr_all<B2_Q4_0>();
-  if (!rc) rc = set_smem_attr_all<B2_Q8_0>();
-  if (!rc) rc = set_smem_attr_all<B2_Q4_K>();
-  if (!rc) rc = set_smem_attr_all<B2_Q6_K>();
+  int rc = set_attr_all<B2_Q4_0>();
+  if (!rc) rc = set_attr_all<B2_Q8_0>();
+  if (!rc) rc = set_attr_all<B2_Q4_K>();
+  if (!rc) rc = set_attr_all<B2_Q6_K>();
   if (!rc && dev >= 0 && dev < 64) done[dev] = true;
   return rc;
 }
@@ -561,30 +712,26 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   if (prc) return prc;
   const QMatrix& w = *a.w;
   B2_CHECK_ARG(a.n_tok >= 1 && a.n_tok <= kMaxTok, "n_tok must be in [1, 8]");
-  B2_CHECK_ARG(a.row_begin >= 0 && a.row_end <= w.n_rows && a.row_begin <= a.row_end, "row range");
-  B2_CHECK_ARG(a.y != nullptr, "y");
-  B2_CHECK_ARG(a.x != nullptr || a.act != nullptr, "x or act");
-  B2_CHECK_ARG(w.n_chunks == 1, "matrix layout");
-  B2_CHECK_ARG(a.epilogue != EPI_SWIGLU || (a.row_begin % 2) == 0, "SwiGLU rows must start on a pair");
-  if (a.row_end == a.row_begin) return B2_OK;
+  B2_CHECK_ARG(a.y != nullptr && a.x != nullptr, "x and y");
+  B2_CHECK_ARG(w.data != nullptr && w.nu > 0, "matrix");
+  B2_CHECK_ARG(a.epilogue != EPI_SWIGLU || (w.n_rows % 2) == 0, "SwiGLU needs (gate, up) row pairs");
+  B2_CHECK_ARG((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride % 4) == 0,
+               "x must be 16-byte aligned with a stride of whole float4s");
   GemvP p = {};
-  p.p0 = w.plane0;
-  p.p1 = w.plane1;
-  p.p0_row = w.p0_row;
-  p.p1_row = w.p1_row;
-  p.kp = w.kp;
+  p.w = w.data;
+  p.type = w.type;
+  p.nu = w.nu;
+  p.S = w.splits;
+  p.L = w.ulen;
+  p.slot_bytes = w.slot_bytes;
+  p.tile_bytes = w.tile_bytes;
+  p.n_rows = w.n_rows;
+  p.n_tiles = w.n_tiles;
   p.k = w.k;
-  p.row_begin = a.row_begin;
-  p.row_end = a.row_end;
-  p.x = a.act ? nullptr : a.x;
+  p.n_tok = a.n_tok;
+  p.n_act_tok = a.n_tok > kDp4aMaxTok ? kMaxTok : a.n_tok;
+  p.x = a.x;
   p.x_stride = a.x_stride;
-  if (a.act) {
-    B2_CHECK_ARG(a.act->kp == w.kp && a.act->type == act_type_for(w.type) && a.act->n_tok >= a.n_tok,
-                 "activation planes do not match the matrix");
-    p.aq = a.act->qs;
-    p.ad = a.act->d;
-    p.absum = a.act->bsum;
-  }
   p.y = a.y;
   p.y_stride = a.y_stride;
   p.epilogue = a.epilogue;
@@ -596,38 +743,38 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   } else {
     p.peer = PeerOut{};
   }
-  const bool k_quant = (w.type == B2_Q4_K || w.type == B2_Q6_K);
-  // Same carve-up as the kernel: qs [B][kp] | d [B][nd] fp32 (16 B aligned end) | bsum [B][kp/16].
-  const size_t nd = (size_t)(k_quant ? w.kp / 256 : w.kp / 32);
-  const size_t act_bytes = (size_t)a.n_tok * w.kp + ((size_t)a.n_tok * nd * 4 + 15) / 16 * 16 +
-                           (k_quant ? (size_t)a.n_tok * (w.kp / 16) * 2 : 0);
-  const size_t row_b = (size_t)(w.p0_row + w.p1_row);
-  // Rows per stage: up to 8 whole rows within ~24 KB (at least 2 for SwiGLU pairs).
-  int rg = 8;
-  while (rg > 1 && (size_t)rg * row_b > 24 * 1024) rg /= 2;
-  if (a.epilogue == EPI_SWIGLU && rg < 2) rg = 2;
-  const size_t stage = ((size_t)rg * row_b + 127) / 128 * 128;
-  const size_t smem_cap = kSmemCap;
-  const size_t fixed = kBarBytes + ((act_bytes + 127) / 128 * 128);
-  if (fixed + 2 * stage > smem_cap) {
+  // Activation carve-up: codes [n_act_tok][kq] | scales [n_act_tok][nu] fp32 | block sums (int16).
+  p.kq = (int)((w.k + 127) / 128 * 128);
+  const int bs_per_unit = w.type == B2_Q4_0 ? 1 : w.type == B2_Q4_K ? 8 : w.type == B2_Q6_K ? 16 : 0;
+  const size_t qs_b = (size_t)p.n_act_tok * p.kq;
+  const size_t dx_b = ((size_t)p.n_act_tok * w.nu * 4 + 15) / 16 * 16;
+  const size_t bs_b = ((size_t)p.n_act_tok * w.nu * bs_per_unit * 2 + 15) / 16 * 16;
+  p.off_dx = (uint32_t)qs_b;
+  p.off_bs = (uint32_t)(qs_b + dx_b);
+  p.act_bytes = (uint32_t)(qs_b + dx_b + bs_b);
+  // Stages of P tiles x U unit steps of all S ranges, U as large as fits ~32 KB.
+  const int P = kNCW / w.splits;
+  const size_t step_b = (size_t)P * w.splits * w.slot_bytes;
+  int U = (int)std::max<size_t>(1, (32 * 1024) / step_b);
+  U = std::min(U, w.ulen);
+  const size_t stage = step_b * U;
+  const size_t fixed = kBarBytes + p.act_bytes;
+  if (fixed + 2 * stage > (size_t)kSmemCap) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
   }
-  int ns = (int)std::min<size_t>(6, (smem_cap - fixed) / stage);
-  // Keep two CTAs per SM possible when the activations are small.
-  while (ns > 3 && fixed + (size_t)ns * stage > 112 * 1024) --ns;
+  const int ns = (int)std::min<size_t>(kMaxStages, ((size_t)kSmemCap - fixed) / stage);
+  p.U = U;
   p.n_stages = ns;
-  p.rg = rg;
   p.stage_bytes = (uint32_t)stage;
   const size_t smem = fixed + (size_t)ns * stage;
-  const int n_sm = sm_count();
-  const int64_t rows = a.row_end - a.row_begin;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(n_sm, (rows + rg - 1) / rg));
+  const int64_t groups = (w.n_tiles + P - 1) / P;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), groups));
   switch (w.type) {
-    case B2_Q4_0: return launch_w<B2_Q4_0>(p, a.n_tok, grid, smem, s);
-    case B2_Q8_0: return launch_w<B2_Q8_0>(p, a.n_tok, grid, smem, s);
-    case B2_Q4_K: return launch_w<B2_Q4_K>(p, a.n_tok, grid, smem, s);
-    case B2_Q6_K: return launch_w<B2_Q6_K>(p, a.n_tok, grid, smem, s);
+    case B2_Q4_0: return launch_w<B2_Q4_0>(p, grid, smem, s);
+    case B2_Q8_0: return launch_w<B2_Q8_0>(p, grid, smem, s);
+    case B2_Q4_K: return launch_w<B2_Q4_K>(p, grid, smem, s);
+    case B2_Q6_K: return launch_w<B2_Q6_K>(p, grid, smem, s);
   }
   set_error("gemv: unsupported weight type %d", w.type);
   return B2_ERR_UNSUPPORTED;

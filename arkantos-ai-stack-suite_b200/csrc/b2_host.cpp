@@ -67,82 +67,73 @@ bool is_weight_type(int type) {
   return type == B2_Q4_0 || type == B2_Q8_0 || type == B2_Q4_K || type == B2_Q6_K;
 }
 
-// ---- repack plan ------------------------------------------------------------------
-namespace {
-// plane0 bytes per 256 columns, and the largest chunk (columns) that keeps a
-// 16-row stage near 16-27 KB of shared memory.
-int p0_bytes_per_256(int type) {
-  switch (type) {
-    case B2_Q4_0: return 128;
-    case B2_Q8_0: return 256;
-    case B2_Q4_K: return 144;
-    case B2_Q6_K: return 208;
-  }
-  return 0;
-}
-inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
-}  // namespace
-
-// One chunk spanning the padded row: consecutive rows of a plane are then one
-// contiguous range, so a stage of several whole rows is a single bulk copy
-// per plane.
+// ---- tile layout ----------------------------------------------------------------------
 void plan_qmatrix(QMatrix& m) {
-  m.kp = round_up(m.k, 256);
-  m.n_chunks = 1;
-  m.kc = (int)m.kp;
-  m.p0_chunk = (m.kp / 256) * p0_bytes_per_256(m.type);
-  m.p0_row = m.p0_chunk;
-  switch (m.type) {
-    case B2_Q4_0: case B2_Q8_0: m.p1_chunk = m.kp / 16; break;
-    case B2_Q6_K: m.p1_chunk = round_up((m.kp / 256) * 2, 16); break;
-    default: m.p1_chunk = 0;
-  }
-  m.p1_row = m.p1_chunk;
+  m.nu = (int)(m.k / unit_elems(m.type));
+  m.splits = tile_splits(m.type, m.k);
+  m.ulen = (m.nu + m.splits - 1) / m.splits;
+  m.slot_bytes = tile_slot_bytes(m.type);
+  m.n_tiles = (m.n_rows + 7) / 8;
+  m.tile_bytes = (int64_t)m.splits * m.ulen * m.slot_bytes;
 }
 
-void repack_rows_host(const QMatrix& m, const uint8_t* gguf, int64_t r0, int64_t r1, uint8_t* p0, uint8_t* p1) {
-  const size_t rb = row_bytes(m.type, m.k);
-  const int be = block_elems(m.type);
-  const int64_t nb_chunk = m.kc / be;
-  for (int64_t r = r0; r < r1; ++r) {
-    const uint8_t* src = gguf + (size_t)r * rb;
-    uint8_t* d0 = p0 + (size_t)(r - r0) * m.p0_row;
-    uint8_t* d1 = p1 ? p1 + (size_t)(r - r0) * m.p1_row : nullptr;
-    memset(d0, 0, (size_t)m.p0_row);
-    if (d1) memset(d1, 0, (size_t)m.p1_row);
-    for (int c = 0; c < m.n_chunks; ++c) {
-      for (int64_t i = 0; i < nb_chunk; ++i) {
-        const int64_t col = (int64_t)c * m.kc + i * be;
-        if (col >= m.k) break;
-        const int64_t b = col / be;
-        uint8_t* q0 = d0 + c * m.p0_chunk;
-        uint8_t* q1 = d1 ? d1 + c * m.p1_chunk : nullptr;
-        switch (m.type) {
-          case B2_Q4_0: {
-            const BlockQ4_0* blk = reinterpret_cast<const BlockQ4_0*>(src) + b;
-            memcpy(q0 + i * 16, blk->qs, 16);
-            memcpy(q1 + i * 2, &blk->d, 2);
-            break;
-          }
-          case B2_Q8_0: {
-            const BlockQ8_0* blk = reinterpret_cast<const BlockQ8_0*>(src) + b;
-            memcpy(q0 + i * 32, blk->qs, 32);
-            memcpy(q1 + i * 2, &blk->d, 2);
-            break;
-          }
-          case B2_Q4_K:
-            memcpy(q0 + i * 144, src + b * 144, 144);
-            break;
-          case B2_Q6_K: {
-            const BlockQ6_K* blk = reinterpret_cast<const BlockQ6_K*>(src) + b;
-            memcpy(q0 + i * 208, blk->ql, 128);
-            memcpy(q0 + i * 208 + 128, blk->qh, 64);
-            memcpy(q0 + i * 208 + 192, blk->scales, 16);
-            memcpy(q1 + i * 2, &blk->d, 2);
-            break;
-          }
-        }
-      }
+int upload_tiles(QMatrix& m, const uint8_t* const* rows) {
+  plan_qmatrix(m);
+  cudaGetDevice(&m.device);
+  m.data = nullptr;
+  const int64_t bytes = m.bytes();
+  cudaError_t e = cudaMalloc(&m.data, (size_t)std::max<int64_t>(bytes, 16));
+  if (e != cudaSuccess) {
+    m.data = nullptr;
+    set_error("matrix upload: device allocation of %lld bytes: %s", (long long)bytes, cudaGetErrorString(e));
+    return B2_ERR_OOM;
+  }
+  // Slabs of whole tiles through a pinned staging buffer, tiles split over threads.
+  const int64_t slab = std::max<int64_t>(1, (int64_t)(64 << 20) / std::max<int64_t>(1, m.tile_bytes));
+  uint8_t* h = nullptr;
+  e = cudaMallocHost(&h, (size_t)(std::min(slab, m.n_tiles) * m.tile_bytes));
+  if (e != cudaSuccess) {
+    cudaFree(m.data);
+    m.data = nullptr;
+    set_error("matrix upload: pinned staging: %s", cudaGetErrorString(e));
+    return B2_ERR_OOM;
+  }
+  const int nt = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  int rc = B2_OK;
+  for (int64_t t0 = 0; t0 < m.n_tiles; t0 += slab) {
+    const int64_t t1 = std::min(m.n_tiles, t0 + slab), n = t1 - t0;
+    auto work = [&](int64_t a, int64_t b) {
+      if (b > a) repack_tiles_host(m, rows, a, b, h + (a - t0) * m.tile_bytes);
+    };
+    std::vector<std::thread> th;
+    for (int t = 1; t < nt; ++t) th.emplace_back(work, t0 + n * t / nt, t0 + n * (t + 1) / nt);
+    work(t0, t0 + n / nt);
+    for (auto& x : th) x.join();
+    e = cudaMemcpy(m.data + t0 * m.tile_bytes, h, (size_t)(n * m.tile_bytes), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      set_error("matrix upload: copy: %s", cudaGetErrorString(e));
+      rc = B2_ERR_CUDA;
+      break;
+    }
+  }
+  cudaFreeHost(h);
+  if (rc != B2_OK) {
+    cudaFree(m.data);
+    m.data = nullptr;
+  }
+  return rc;
+}
+
+void repack_tiles_host(const QMatrix& m, const uint8_t* const* rows, int64_t t0, int64_t t1, uint8_t* out) {
+  const int ub = gguf_unit_bytes(m.type);
+  memset(out, 0, (size_t)((t1 - t0) * m.tile_bytes));
+  for (int64_t t = t0; t < t1; ++t) {
+    uint8_t* tile = out + (t - t0) * m.tile_bytes;
+    for (int g = 0; g < 8; ++g) {
+      const int64_t r = t * 8 + g;
+      if (r >= m.n_rows) break;
+      for (int u = 0; u < m.nu; ++u)
+        unit_to_slot(m.type, rows[r] + (size_t)u * ub, g, tile + slot_offset(m, 0, u));
     }
   }
 }

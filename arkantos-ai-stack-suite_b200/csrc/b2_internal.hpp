@@ -52,33 +52,115 @@ bool is_weight_type(int type);
 // Q8_0 for Q4_0/Q8_0, Q8_K for Q4_K/Q6_K.
 inline int act_type_for(int wtype) { return (wtype == B2_Q4_K || wtype == B2_Q6_K) ? B2_Q8_K : B2_Q8_0; }
 
-// ---- repacked quantized matrix (device) -----------------------------------------
-// W is [n_rows x k] in GGUF blocks along k.  On upload the columns are split
-// into n_chunks chunks of kc columns (kc a multiple of 256, kp = n_chunks*kc
-// >= k, the tail zero-padded), and the block bytes are split into planes so
-// every (row, chunk) piece is 16-byte aligned and a whole multiple of 16
-// bytes — one cp.async.bulk each:
-//   Q4_0  plane0 = nibbles   (16 B / 32 cols)       plane1 = fp16 d per 32 cols
-//   Q8_0  plane0 = int8 q    (32 B / 32 cols)       plane1 = fp16 d per 32 cols
-//   Q4_K  plane0 = the 144 B GGUF super-blocks as-is (d, dmin, scales, qs)
-//   Q6_K  plane0 = ql|qh|scales (208 B / 256 cols)  plane1 = fp16 d per 256 cols
-// plane0 row r, chunk c at r*p0_row + c*p0_chunk; plane1 at r*p1_row + c*p1_chunk
-// (p1_chunk padded up to 16 B).  Bytes are bit-identical to the GGUF input.
+// ---- tiled quantized matrix (device) ---------------------------------------------
+// W is [n_rows x k] in GGUF units along k: 32-weight blocks (Q4_0, Q8_0) or
+// 256-weight super-blocks (Q4_K, Q6_K), nu units per row.  On upload the rows
+// are grouped into tiles of 8 (the last tile zero-padded) and each row's
+// units into S = tile_splits(type, k) ranges of L = ceil(nu / S) units (range
+// w holds units [w*L, min((w+1)*L, nu))).  A tile is S*L unit slots; slot
+// i*S + w carries unit w*L + i of the tile's 8 rows (zeros past nu), so the
+// i-th units of all ranges are adjacent and the next few i of a tile are one
+// contiguous bulk copy.  Within a slot the 8 rows' unit bytes are moved into
+// planes, row g of each plane at g * (plane row bytes); planes of 64 or 128 B
+// per row have row g's 16-byte chunks rotated by g, so the GEMV's per-row
+// shared-memory reads hit distinct banks.  Bytes are those of the GGUF input.
+//   Q4_0  144 B: qs 8x16 @0,  d 8x2 @128
+//   Q8_0  272 B: qs[0:16] 8x16 @0, qs[16:32] 8x16 @128, d 8x2 @256
+//   Q4_K 1152 B: qs 8x128 @0 (rotated), d|dmin|scales 8x16 @1024
+//   Q6_K 1680 B: ql 8x128 @0 (rotated), qh 8x64 @1024 (rotated), scales 8x16 @1536, d 8x2 @1664
+#if defined(__CUDACC__)
+#define B2_HD __host__ __device__
+#else
+#define B2_HD
+#endif
 struct QMatrix {
   int type = 0;
-  int64_t n_rows = 0, k = 0, kp = 0;
-  int kc = 0, n_chunks = 0;
-  uint8_t* plane0 = nullptr;
-  uint8_t* plane1 = nullptr;
-  int64_t p0_row = 0, p0_chunk = 0, p1_row = 0, p1_chunk = 0;
+  int64_t n_rows = 0, k = 0;
+  int nu = 0, splits = 1, ulen = 0;      // units per row, S, L
+  int slot_bytes = 0;                    // one unit of the tile's 8 rows
+  int64_t n_tiles = 0, tile_bytes = 0;   // tiles of 8 rows, S*L*slot_bytes each
+  uint8_t* data = nullptr;
   int device = 0;
   bool owns = true;
+  int64_t bytes() const { return n_tiles * tile_bytes; }
 };
 
-// Chooses kc / n_chunks / plane strides for a matrix shape.
+B2_HD inline int unit_elems(int type) { return (type == B2_Q4_K || type == B2_Q6_K) ? 256 : 32; }
+B2_HD inline int gguf_unit_bytes(int type) {
+  return type == B2_Q4_0 ? 18 : type == B2_Q8_0 ? 34 : type == B2_Q4_K ? 144 : type == B2_Q6_K ? 210 : 0;
+}
+B2_HD inline int tile_slot_bytes(int type) {
+  return type == B2_Q4_0 ? 144 : type == B2_Q8_0 ? 272 : type == B2_Q4_K ? 1152 : type == B2_Q6_K ? 1680 : 0;
+}
+// Ranges per row: the largest power of two <= 8 that leaves >= 4 units per
+// range (the four interleaved partial sums of a range each get a unit).
+B2_HD inline int tile_splits(int type, int64_t k) {
+  const int64_t nu = k / unit_elems(type);
+  int s = 1;
+  while (s < 8 && 2 * s * 4 <= nu) s *= 2;
+  return s;
+}
+// Byte offset of (tile, unit u) in the matrix data.
+B2_HD inline int64_t slot_offset(const QMatrix& m, int64_t tile, int u) {
+  const int w = u / m.ulen, i = u - w * m.ulen;
+  return tile * m.tile_bytes + (int64_t)(i * m.splits + w) * m.slot_bytes;
+}
+
+B2_HD inline void copy_bytes(uint8_t* d, const uint8_t* s, int n) {
+  for (int i = 0; i < n; ++i) d[i] = s[i];
+}
+// Moves row g's GGUF unit into its slot, and back.
+B2_HD inline void unit_to_slot(int type, const uint8_t* src, int g, uint8_t* slot) {
+  switch (type) {
+    case B2_Q4_0: copy_bytes(slot + 128 + 2 * g, src, 2); copy_bytes(slot + 16 * g, src + 2, 16); break;
+    case B2_Q8_0:
+      copy_bytes(slot + 256 + 2 * g, src, 2);
+      copy_bytes(slot + 16 * g, src + 2, 16);
+      copy_bytes(slot + 128 + 16 * g, src + 18, 16);
+      break;
+    case B2_Q4_K:
+      copy_bytes(slot + 1024 + 16 * g, src, 16);
+      for (int c = 0; c < 8; ++c) copy_bytes(slot + 128 * g + 16 * ((c + g) & 7), src + 16 + 16 * c, 16);
+      break;
+    case B2_Q6_K:
+      for (int c = 0; c < 8; ++c) copy_bytes(slot + 128 * g + 16 * ((c + g) & 7), src + 16 * c, 16);
+      for (int c = 0; c < 4; ++c) copy_bytes(slot + 1024 + 64 * g + 16 * ((c + g) & 3), src + 128 + 16 * c, 16);
+      copy_bytes(slot + 1536 + 16 * g, src + 192, 16);
+      copy_bytes(slot + 1664 + 2 * g, src + 208, 2);
+      break;
+    default: break;
+  }
+}
+B2_HD inline void slot_to_unit(int type, const uint8_t* slot, int g, uint8_t* dst) {
+  switch (type) {
+    case B2_Q4_0: copy_bytes(dst, slot + 128 + 2 * g, 2); copy_bytes(dst + 2, slot + 16 * g, 16); break;
+    case B2_Q8_0:
+      copy_bytes(dst, slot + 256 + 2 * g, 2);
+      copy_bytes(dst + 2, slot + 16 * g, 16);
+      copy_bytes(dst + 18, slot + 128 + 16 * g, 16);
+      break;
+    case B2_Q4_K:
+      copy_bytes(dst, slot + 1024 + 16 * g, 16);
+      for (int c = 0; c < 8; ++c) copy_bytes(dst + 16 + 16 * c, slot + 128 * g + 16 * ((c + g) & 7), 16);
+      break;
+    case B2_Q6_K:
+      for (int c = 0; c < 8; ++c) copy_bytes(dst + 16 * c, slot + 128 * g + 16 * ((c + g) & 7), 16);
+      for (int c = 0; c < 4; ++c) copy_bytes(dst + 128 + 16 * c, slot + 1024 + 64 * g + 16 * ((c + g) & 3), 16);
+      copy_bytes(dst + 192, slot + 1536 + 16 * g, 16);
+      copy_bytes(dst + 208, slot + 1664 + 2 * g, 2);
+      break;
+    default: break;
+  }
+}
+
+// Fills the tile geometry of m from type, n_rows and k.
 void plan_qmatrix(QMatrix& m);
-// Repacks GGUF rows [r0, r1) into host plane buffers laid out as in QMatrix.
-void repack_rows_host(const QMatrix& m, const uint8_t* gguf, int64_t r0, int64_t r1, uint8_t* p0, uint8_t* p1);
+// Repacks into host buffer `out` the tiles [t0, t1); row r's GGUF bytes are
+// at rows[r] (rows past n_rows are zero).
+void repack_tiles_host(const QMatrix& m, const uint8_t* const* rows, int64_t t0, int64_t t1, uint8_t* out);
+// Plans m (type, n_rows, k set), allocates m.data on the current device and
+// uploads the repacked tiles; rows[r] points at row r's GGUF bytes.
+int upload_tiles(QMatrix& m, const uint8_t* const* rows);
 
 // ---- planar quantized activations (device) ---------------------------------------
 // B token rows of kp values: qs [B][kp] int8 (zero beyond k), d [B][kp/32]
@@ -125,14 +207,12 @@ struct PeerIn {
 
 struct GemvArgs {
   const QMatrix* w;
-  const float* x;       // fp32 [n_tok][x_stride] when act == nullptr (quantized in-kernel)
+  const float* x;       // fp32 [n_tok][x_stride], 16-byte aligned; quantized in-kernel
   int64_t x_stride;
-  const ActQ* act;      // pre-quantized activations, or nullptr
   int n_tok;
   float* y;             // [n_tok][y_stride]
   int64_t y_stride;
   int epilogue;
-  int64_t row_begin, row_end;   // rows of W to compute (TP slices, tests); end<=n_rows
   int* status;          // device status word (bounded waits), may be nullptr
   const PeerOut* peer = nullptr;   // tensor-parallel exchange of the outputs (EPI_STORE only)
 };

@@ -91,38 +91,36 @@ __global__ void act_to_blocks_kernel(int type, const int8_t* qs, const float* d,
   out[i] = (uint8_t)v;
 }
 
-// Exact integer block dots of one repacked row against token 0 of `a`.
-__global__ void block_dots_kernel(int type, const uint8_t* p0, const uint8_t* p1, int64_t p0_row, int64_t p0_chunk,
-                                  int64_t p1_row, int64_t p1_chunk, int kc, int64_t k, int64_t row, const int8_t* qs,
-                                  const int16_t* bsum, int32_t* out_i, int32_t* out_m) {
-  const int64_t bsz = (type == B2_Q4_0 || type == B2_Q8_0) ? 32 : 256;
-  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= k / bsz) return;
-  const int64_t col = b * bsz;
-  const int64_t c = col / kc, cc = col - c * kc;
-  const uint8_t* r0 = p0 + row * p0_row + c * p0_chunk;
-  if (type == B2_Q4_0) {
-    const uint8_t* q = r0 + (cc / 32) * 16;
+// Exact integer block dots of one row of a tiled matrix against token 0 of
+// `a`: one thread per unit, which rebuilds the unit's GGUF bytes from its slot.
+__global__ void block_dots_kernel(QMatrix m, int64_t row, const int8_t* qs, const int16_t* bsum, int32_t* out_i,
+                                  int32_t* out_m) {
+  const int b = (int)((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (b >= m.nu) return;
+  uint8_t bp[210];
+  slot_to_unit(m.type, m.data + slot_offset(m, row / 8, b), (int)(row % 8), bp);
+  const int64_t col = (int64_t)b * unit_elems(m.type);
+  if (m.type == B2_Q4_0) {
+    const uint8_t* q = bp + 2;
     int s = 0;
     for (int j = 0; j < 16; ++j) s += ((int)(q[j] & 15) - 8) * qs[col + j] + ((int)(q[j] >> 4) - 8) * qs[col + j + 16];
     out_i[b] = s;
-  } else if (type == B2_Q8_0) {
-    const int8_t* q = reinterpret_cast<const int8_t*>(r0 + cc);
+  } else if (m.type == B2_Q8_0) {
+    const int8_t* q = reinterpret_cast<const int8_t*>(bp + 2);
     int s = 0;
     for (int j = 0; j < 32; ++j) s += (int)q[j] * qs[col + j];
     out_i[b] = s;
-  } else if (type == B2_Q4_K) {
-    const uint8_t* bp = r0 + (cc / 256) * 144;
+  } else if (m.type == B2_Q4_K) {
     const uint8_t* sc = bp + 4;
     int is = 0, ms = 0;
     for (int j = 0; j < 8; ++j) {
-      int s, m;
+      int s, mm;
       if (j < 4) {
         s = sc[j] & 63;
-        m = sc[j + 4] & 63;
+        mm = sc[j + 4] & 63;
       } else {
         s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
-        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+        mm = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
       }
       int dot = 0;
       for (int l = 0; l < 32; ++l) {
@@ -132,12 +130,11 @@ __global__ void block_dots_kernel(int type, const uint8_t* p0, const uint8_t* p1
         dot += qv * qs[col + e];
       }
       is += s * dot;
-      ms += m * ((int)bsum[col / 16 + 2 * j] + (int)bsum[col / 16 + 2 * j + 1]);
+      ms += mm * ((int)bsum[col / 16 + 2 * j] + (int)bsum[col / 16 + 2 * j + 1]);
     }
     out_i[b] = is;
     if (out_m) out_m[b] = ms;
   } else {
-    const uint8_t* bp = r0 + (cc / 256) * 208;
     const int8_t* sc = reinterpret_cast<const int8_t*>(bp + 192);
     int is = 0;
     for (int g = 0; g < 16; ++g) {
@@ -153,61 +150,58 @@ __global__ void block_dots_kernel(int type, const uint8_t* p0, const uint8_t* p1
     }
     out_i[b] = is;
   }
-  (void)p1;
-  (void)p1_row;
-  (void)p1_chunk;
 }
 
-// fp32 dequantization of a repacked matrix: one thread per output value, the
-// same operation order as the GGUF layouts define (Q4_0: (q-8)·d; Q8_0: q·d;
+// fp32 dequantization of a tiled matrix: one thread per (row, unit), the same
+// operation order as the GGUF layouts define (Q4_0: (q-8)·d; Q8_0: q·d;
 // Q4_K: (d·sc)·q − dmin·m; Q6_K: (d·sc)·q).
-__global__ void dequantize_kernel(int type, const uint8_t* p0, const uint8_t* p1, int64_t p0_row, int64_t p0_chunk,
-                                  int64_t p1_row, int64_t p1_chunk, int kc, int64_t n_rows, int64_t k, float* dst) {
+__global__ void dequantize_kernel(QMatrix m, float* dst) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_rows * k) return;
-  const int64_t r = i / k, col = i - r * k;
-  const int64_t c = col / kc, cc = col - c * kc;
-  const uint8_t* r0 = p0 + r * p0_row + c * p0_chunk;
-  const uint8_t* r1 = p1 ? p1 + r * p1_row + c * p1_chunk : nullptr;
-  float v = 0.0f;
-  if (type == B2_Q4_0) {
-    const int b = (int)(cc / 32), j = (int)(cc % 32);
-    const uint8_t byte = r0[b * 16 + (j & 15)];
-    const int q = (j < 16 ? (byte & 15) : (byte >> 4)) - 8;
-    v = __fmul_rn((float)q, h2f(reinterpret_cast<const uint16_t*>(r1)[b]));
-  } else if (type == B2_Q8_0) {
-    const int b = (int)(cc / 32);
-    v = __fmul_rn((float)reinterpret_cast<const int8_t*>(r0)[cc], h2f(reinterpret_cast<const uint16_t*>(r1)[b]));
-  } else if (type == B2_Q4_K) {
-    const int sb = (int)(cc / 256), e = (int)(cc % 256);
-    const uint8_t* bp = r0 + sb * 144;
+  if (i >= m.n_rows * m.nu) return;
+  const int64_t r = i / m.nu;
+  const int u = (int)(i - r * m.nu);
+  uint8_t bp[210];
+  slot_to_unit(m.type, m.data + slot_offset(m, r / 8, u), (int)(r % 8), bp);
+  const int ue = unit_elems(m.type);
+  float* out = dst + r * m.k + (int64_t)u * ue;
+  if (m.type == B2_Q4_0) {
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(bp));
+    for (int j = 0; j < 32; ++j) {
+      const uint8_t byte = bp[2 + (j & 15)];
+      out[j] = __fmul_rn((float)((j < 16 ? (byte & 15) : (byte >> 4)) - 8), d);
+    }
+  } else if (m.type == B2_Q8_0) {
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(bp));
+    for (int j = 0; j < 32; ++j) out[j] = __fmul_rn((float)reinterpret_cast<const int8_t*>(bp + 2)[j], d);
+  } else if (m.type == B2_Q4_K) {
     const float d = h2f(*reinterpret_cast<const uint16_t*>(bp));
     const float dmin = h2f(*reinterpret_cast<const uint16_t*>(bp + 2));
     const uint8_t* sc = bp + 4;
-    const int j = e >> 5;
-    int s, m;
-    if (j < 4) {
-      s = sc[j] & 63;
-      m = sc[j + 4] & 63;
-    } else {
-      s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
-      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    for (int e = 0; e < 256; ++e) {
+      const int j = e >> 5;
+      int s, mm;
+      if (j < 4) {
+        s = sc[j] & 63;
+        mm = sc[j + 4] & 63;
+      } else {
+        s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
+        mm = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+      }
+      const uint8_t byte = bp[16 + (e >> 6) * 32 + (e & 31)];
+      const int q = (j & 1) ? (byte >> 4) : (byte & 15);
+      out[e] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s), (float)q), __fmul_rn(dmin, (float)mm));
     }
-    const uint8_t byte = bp[16 + (e >> 6) * 32 + (e & 31)];
-    const int q = (j & 1) ? (byte >> 4) : (byte & 15);
-    v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s), (float)q), __fmul_rn(dmin, (float)m));
-  } else if (type == B2_Q6_K) {
-    const int sb = (int)(cc / 256), e = (int)(cc % 256);
-    const uint8_t* bp = r0 + sb * 208;
-    const int h = e >> 7, g = (e >> 5) & 3, l = e & 31;
-    const int lo = (bp[h * 64 + (g & 1) * 32 + l] >> (4 * (g >> 1))) & 15;
-    const int hi = (bp[128 + h * 32 + l] >> (2 * g)) & 3;
-    const int q = (lo | (hi << 4)) - 32;
-    const float d = h2f(reinterpret_cast<const uint16_t*>(r1)[sb]);
-    const float sc = (float)reinterpret_cast<const int8_t*>(bp + 192)[e >> 4];
-    v = __fmul_rn(__fmul_rn(d, sc), (float)q);
+  } else {
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(bp + 208));
+    for (int e = 0; e < 256; ++e) {
+      const int h = e >> 7, g = (e >> 5) & 3, l = e & 31;
+      const int lo = (bp[h * 64 + (g & 1) * 32 + l] >> (4 * (g >> 1))) & 15;
+      const int hi = (bp[128 + h * 32 + l] >> (2 * g)) & 3;
+      const int q = (lo | (hi << 4)) - 32;
+      const float sc = (float)reinterpret_cast<const int8_t*>(bp + 192)[e >> 4];
+      out[e] = __fmul_rn(__fmul_rn(d, sc), (float)q);
+    }
   }
-  dst[i] = v;
 }
 
 int grid_for(int64_t n, int block) { return (int)std::min<int64_t>((n + block - 1) / block, 1 << 30); }
@@ -253,18 +247,16 @@ int launch_act_to_blocks(const ActQ& a, int64_t k, void* blocks, cudaStream_t s)
 }
 
 int launch_block_dots(const QMatrix& w, const ActQ& a, int64_t row, int32_t* out_i, int32_t* out_m, cudaStream_t s) {
-  const int64_t nb = w.k / block_elems(w.type);
-  block_dots_kernel<<<grid_for(nb, 128), 128, 0, s>>>(w.type, w.plane0, w.plane1, w.p0_row, w.p0_chunk, w.p1_row,
-                                                      w.p1_chunk, w.kc, w.k, row, a.qs, a.bsum, out_i, out_m);
+  B2_CHECK_ARG(row >= 0 && row < w.n_rows, "block_dots row");
+  block_dots_kernel<<<grid_for(w.nu, 128), 128, 0, s>>>(w, row, a.qs, a.bsum, out_i, out_m);
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
 }
 
 int launch_dequantize(const QMatrix& w, float* dst, cudaStream_t s) {
-  const int64_t n = w.n_rows * w.k;
+  const int64_t n = w.n_rows * w.nu;
   if (n == 0) return B2_OK;
-  dequantize_kernel<<<grid_for(n, 256), 256, 0, s>>>(w.type, w.plane0, w.plane1, w.p0_row, w.p0_chunk, w.p1_row,
-                                                     w.p1_chunk, w.kc, w.n_rows, w.k, dst);
+  dequantize_kernel<<<grid_for(n, 128), 128, 0, s>>>(w, dst);
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
 }

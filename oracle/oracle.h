@@ -99,8 +99,11 @@ void orc_kv_shift_k(uint16_t* kc, int64_t kv_stride, int n_pos, int n_kv_heads, 
 /* ---- Device-order arithmetic (the GPU kernels' evaluation order) ---- */
 float orc_expf_dev(float x);
 void  orc_silu_mul_dev(float* hb, const float* hb2, int n);
-int   orc_dev_warps_per_row(int wtype, int k, int swiglu);
-float orc_dev_row_dot(int wtype, const void* wrow, int k, const void* xq, int wpr, int direct);
+/* Tile GEMV order (both tile kernels, any batch): units split into
+ * orc_tile_splits() ranges of ceil(nu/S) units, four interleaved partial sums per
+ * range combined pairwise, ranges added in order. */
+int   orc_tile_splits(int wtype, int k);
+float orc_tile_row_dot(int wtype, const void* wrow, int k, const void* xq);
 void  orc_matmul_dev(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int swiglu,
                      int n_threads);
 /* As orc_matmul_dev over k columns of rows `row_stride` bytes apart (a column

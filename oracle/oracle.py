@@ -74,7 +74,6 @@ def _load() -> ctypes.CDLL:
         "orc_model_set_tap": (None, [_vp, _vp, _vp]),
         "orc_model_set_device_order": (None, [_vp, _i]),
         "orc_expf_dev": (_f, [_f]),
-        "orc_dev_warps_per_row": (_i, [_i, _i, _i]),
         "orc_matmul_dev": (None, [_i, _vp, ctypes.c_int64, _i, _vp, _vp, _i, _i]),
         "orc_attn_decode_dev": (None, [_vp, _vp, _vp, ctypes.c_int64, _i, _i, _i, _i, _vp]),
     }

@@ -530,106 +530,75 @@ void orc_silu_mul_dev(float* hb, const float* hb2, int n) {
     }
 }
 
-/* Rows-per-stage rule of the device GEMV: up to 8 whole padded rows within
- * 24 KB (at least 2 for the fused SwiGLU), 8/rows warps share a row. */
-int orc_dev_warps_per_row(int wtype, int k, int swiglu) {
-    const int64_t kp = ((int64_t)k + 255) / 256 * 256;
-    int64_t p0 = 0, p1 = 0;
+/* ---- tiled GEMV order ------------------------------------------------------
+ * The tile GEMV kernels (dp4a for small batches, int8 mma for larger ones)
+ * share one evaluation order per (row, token), independent of the batch:
+ *   units u = 32-weight blocks (Q4_0, Q8_0) or 256-weight super-blocks
+ *   (Q4_K, Q6_K), nu per row; S = orc_tile_splits() ranges of L = ceil(nu/S)
+ *   units, R_w = [w·L, min((w+1)·L, nu)); inside R_w four partial sums a_q
+ *   take the units with u mod 4 == q in increasing u; the range's sum is
+ *   (a_0 + a_1) + (a_2 + a_3); the row's value is ((S_0 + S_1) + S_2) + ...
+ * A unit adds its exact integer dot scaled as the reference does:
+ *   Q4_0/Q8_0: acc + (d_w·d_x)·isum;  Q6_K: acc + (d_w·d_x)·isum;
+ *   Q4_K: (acc + (d·d_x)·isum) − (dmin·d_x)·msum. */
+int orc_tile_splits(int wtype, int k) {
+    const int nu = (wtype == ORC_Q4_K || wtype == ORC_Q6_K) ? k / 256 : k / 32;
+    int s = 1;
+    while (s < 8 && 2 * s * 4 <= nu) s *= 2;
+    return s;
+}
+
+static float tile_unit(int wtype, const uint8_t* wrow, const uint8_t* xrow, int u, float acc) {
     switch (wtype) {
-    case ORC_Q4_0: p0 = kp / 256 * 128; p1 = kp / 16; break;
-    case ORC_Q8_0: p0 = kp / 256 * 256; p1 = kp / 16; break;
-    case ORC_Q4_K: p0 = kp / 256 * 144; break;
-    case ORC_Q6_K: p0 = kp / 256 * 208; p1 = ((kp / 256) * 2 + 15) / 16 * 16; break;
-    default: break;
-    }
-    int rg = 8;
-    while (rg > 1 && (int64_t)rg * (p0 + p1) > 24 * 1024) rg /= 2;
-    if (swiglu && rg < 2) rg = 2;
-    return 8 / rg;
-}
-
-/* One accumulation unit of the device GEMV: a 32-weight block (Q4_0/Q8_0),
- * a 64-weight quarter super-block (Q4_K) or a 64-weight (half, group pair) of
- * a Q6_K super-block.  Applies the unit's terms to *acc in kernel order. */
-static void dev_unit(int wtype, const uint8_t* wrow, const uint8_t* xrow, int u, float* acc) {
-    if (wtype == ORC_Q4_0 || wtype == ORC_Q8_0) {
+    case ORC_Q4_0: {
+        const blk_q4_0* x = (const blk_q4_0*)wrow + u;
+        const blk_q8_0* y = (const blk_q8_0*)xrow + u;
         int32_t s;
-        float dw, dy;
-        if (wtype == ORC_Q4_0) {
-            const blk_q4_0* x = (const blk_q4_0*)wrow + u;
-            orc_block_dots_q4_0_q8_0(32, x, (const blk_q8_0*)xrow + u, &s);
-            dw = orc_fp16_to_fp32(x->d);
-        } else {
-            const blk_q8_0* x = (const blk_q8_0*)wrow + u;
-            orc_block_dots_q8_0_q8_0(32, x, (const blk_q8_0*)xrow + u, &s);
-            dw = orc_fp16_to_fp32(x->d);
-        }
-        dy = orc_fp16_to_fp32(((const blk_q8_0*)xrow + u)->d);
-        *acc = *acc + (dw * dy) * (float)s;
-    } else if (wtype == ORC_Q4_K) {
-        const int sb = u >> 2, c4 = u & 3;
-        const blk_q4_k* x = (const blk_q4_k*)wrow + sb;
-        const blk_q8_k* y = (const blk_q8_k*)xrow + sb;
-        uint8_t sc[8], m[8];
-        q4k_scale_min(x->scales, sc, m);
-        int32_t lo = 0, hi = 0;
-        for (int l = 0; l < 32; ++l) {
-            lo += q4k_q(x, c4 * 64 + l) * (int32_t)y->qs[c4 * 64 + l];
-            hi += q4k_q(x, c4 * 64 + 32 + l) * (int32_t)y->qs[c4 * 64 + 32 + l];
-        }
-        const int32_t isum = (int32_t)sc[2 * c4] * lo + (int32_t)sc[2 * c4 + 1] * hi;
-        const int32_t msum = (int32_t)m[2 * c4] * ((int32_t)y->bsums[4 * c4] + y->bsums[4 * c4 + 1]) +
-                             (int32_t)m[2 * c4 + 1] * ((int32_t)y->bsums[4 * c4 + 2] + y->bsums[4 * c4 + 3]);
-        const float dd = orc_fp16_to_fp32(x->d), dm = orc_fp16_to_fp32(x->dmin);
-        *acc = *acc + (dd * y->d) * (float)isum;
-        *acc = *acc - (dm * y->d) * (float)msum;
-    } else {
-        const int sb = u >> 2, hh = (u >> 1) & 1, gp = u & 1;
-        const blk_q6_k* x = (const blk_q6_k*)wrow + sb;
-        const blk_q8_k* y = (const blk_q8_k*)xrow + sb;
-        int32_t part[4] = {0, 0, 0, 0};
-        for (int half = 0; half < 2; ++half) {
-            const int g = gp + 2 * half;
-            for (int l = 0; l < 32; ++l) {
-                const int e = hh * 128 + g * 32 + l;
-                part[2 * half + (l >> 4)] += q6k_q(x, e) * (int32_t)y->qs[e];
-            }
-        }
-        const int32_t isum = (int32_t)x->scales[hh * 8 + 2 * gp] * part[0] +
-                             (int32_t)x->scales[hh * 8 + 2 * gp + 1] * part[1] +
-                             (int32_t)x->scales[hh * 8 + 2 * (gp + 2)] * part[2] +
-                             (int32_t)x->scales[hh * 8 + 2 * (gp + 2) + 1] * part[3];
-        const float d6 = orc_fp16_to_fp32(x->d);
-        *acc = *acc + (d6 * y->d) * (float)isum;
+        orc_block_dots_q4_0_q8_0(32, x, y, &s);
+        return acc + (orc_fp16_to_fp32(x->d) * orc_fp16_to_fp32(y->d)) * (float)s;
+    }
+    case ORC_Q8_0: {
+        const blk_q8_0* x = (const blk_q8_0*)wrow + u;
+        const blk_q8_0* y = (const blk_q8_0*)xrow + u;
+        int32_t s;
+        orc_block_dots_q8_0_q8_0(32, x, y, &s);
+        return acc + (orc_fp16_to_fp32(x->d) * orc_fp16_to_fp32(y->d)) * (float)s;
+    }
+    case ORC_Q4_K: {
+        const blk_q4_k* x = (const blk_q4_k*)wrow + u;
+        const blk_q8_k* y = (const blk_q8_k*)xrow + u;
+        int32_t is, ms;
+        orc_block_dots_q4_k_q8_k(256, x, y, &is, &ms);
+        acc = acc + (orc_fp16_to_fp32(x->d) * y->d) * (float)is;
+        return acc - (orc_fp16_to_fp32(x->dmin) * y->d) * (float)ms;
+    }
+    default: {
+        const blk_q6_k* x = (const blk_q6_k*)wrow + u;
+        const blk_q8_k* y = (const blk_q8_k*)xrow + u;
+        int32_t is;
+        orc_block_dots_q6_k_q8_k(256, x, y, &is);
+        return acc + (orc_fp16_to_fp32(x->d) * y->d) * (float)is;
+    }
     }
 }
 
-/* One row of the device GEMV: units u go to slot u mod (32·wpr) and are
- * accumulated there in increasing u; each warp's 32 slots are combined by the
- * xor butterfly (16, 8, 4, 2, 1); the warps of a row are added to 0 in warp
- * order, except a single warp's result is taken as is (direct = 1). */
-float orc_dev_row_dot(int wtype, const void* wrow, int k, const void* xq, int wpr, int direct) {
-    const int nu = (wtype == ORC_Q4_0 || wtype == ORC_Q8_0) ? k / 32 : (k / 256) * 4;
-    const int L = 32 * wpr;
-    float acc[256];
-    for (int j = 0; j < L; ++j) acc[j] = 0.0f;
-    for (int u = 0; u < nu; ++u) dev_unit(wtype, (const uint8_t*)wrow, (const uint8_t*)xq, u, &acc[u % L]);
-    float tot = 0.0f, warp0 = 0.0f;
-    for (int w = 0; w < wpr; ++w) {
-        float v[32], t[32];
-        for (int l = 0; l < 32; ++l) v[l] = acc[w * 32 + l];
-        for (int o = 16; o > 0; o >>= 1) {
-            for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
-            for (int l = 0; l < 32; ++l) v[l] = t[l];
-        }
-        if (w == 0) warp0 = v[0];
-        tot = tot + v[0];
+float orc_tile_row_dot(int wtype, const void* wrow, int k, const void* xq) {
+    const int nu = (wtype == ORC_Q4_K || wtype == ORC_Q6_K) ? k / 256 : k / 32;
+    const int S = orc_tile_splits(wtype, k);
+    const int L = (nu + S - 1) / S;
+    float total = 0.0f;
+    for (int w = 0; w < S; ++w) {
+        const int u0 = w * L < nu ? w * L : nu, u1 = (w + 1) * L < nu ? (w + 1) * L : nu;
+        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int u = u0; u < u1; ++u) a[u & 3] = tile_unit(wtype, (const uint8_t*)wrow, (const uint8_t*)xq, u, a[u & 3]);
+        const float sw = (a[0] + a[1]) + (a[2] + a[3]);
+        total = w == 0 ? sw : total + sw;
     }
-    return (direct && wpr == 1) ? warp0 : tot;
+    return total;
 }
 
 typedef struct {
-    int wtype, k, wpr, direct;
+    int wtype, k;
     const uint8_t* w;
     size_t row_bytes;
     const void* xq;
@@ -640,7 +609,7 @@ typedef struct {
 static void* mmd_worker(void* arg) {
     const mmd_job* j = (const mmd_job*)arg;
     for (int64_t r = j->r0; r < j->r1; ++r)
-        j->y[r] = orc_dev_row_dot(j->wtype, j->w + (size_t)r * j->row_bytes, j->k, j->xq, j->wpr, j->direct);
+        j->y[r] = orc_tile_row_dot(j->wtype, j->w + (size_t)r * j->row_bytes, j->k, j->xq);
     return NULL;
 }
 
@@ -659,8 +628,6 @@ void orc_matmul_dev_strided(int wtype, const void* w, int64_t n_rows, size_t row
     for (int t = 0; t < n_threads; ++t) {
         jobs[t].wtype = wtype;
         jobs[t].k = k;
-        jobs[t].wpr = orc_dev_warps_per_row(wtype, k, swiglu);
-        jobs[t].direct = !swiglu;
         jobs[t].w = (const uint8_t*)w;
         jobs[t].row_bytes = row_stride;
         jobs[t].xq = xq;

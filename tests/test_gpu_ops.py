@@ -92,7 +92,7 @@ def test_block_dots_bit_exact(t, k):
 
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("n,k", [(1, 256), (100, 2048), (257, 4096), (64, 5632), (48, 14336)])
-@pytest.mark.parametrize("n_tok", [1, 3, 8])
+@pytest.mark.parametrize("n_tok", [1, 2, 3, 8])
 def test_gemv_matches_oracle(t, n, k, n_tok):
     q = _weights(t, n, k, 21)
     m = b2.QMatrix(t, q, n, k)
