@@ -84,9 +84,9 @@ def _bind() -> None:
         "b2_gguf_write_synthetic_llama": (_i, [_vp, ctypes.c_char_p, _i]),
         "b2_embed": (_i, [_i, _vp, _i, _i, _vp, _i, _vp, _vp]),
         "b2_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _f, _vp]),
-        "b2_rope_kv_store": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
-        "b2_attn_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
-        "b2_attn_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+        "b2_rope_kv_store": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
+        "b2_attn_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
+        "b2_attn_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
         "b2_kv_shift_k": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
         "b2_model_default_params": (None, [_vp]),
         "b2_nccl_unique_id": (_i, [_vp]),

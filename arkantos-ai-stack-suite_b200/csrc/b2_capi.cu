@@ -267,7 +267,15 @@ int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stre
   a.y = y;
   a.y_stride = w->m.n_rows;
   a.epilogue = EPI_STORE;
-  return launch_gemv(a, as_stream(stream));
+  B2_CHECK_ARG(n_tok >= 1 && n_tok <= 8, "n_tok must be in [1, 8]");
+  cudaStream_t s = as_stream(stream);
+  // stream-ordered scratch for the quantized activations (graph-capturable)
+  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&a.act_img), gemv_act_image_bytes(w->m, n_tok), s));
+  const int rc = launch_gemv(a, s);
+  const cudaError_t e = cudaFreeAsync(a.act_img, s);
+  if (rc) return rc;
+  B2_CUDA_TRY(e);
+  return B2_OK;
 }
 
 namespace {
@@ -342,85 +350,42 @@ int b2_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_r
   return launch_add_rmsnorm(x, delta, w, out, n_rows, n, eps, as_stream(stream));
 }
 
-namespace {
-// Zeroed per-sequence KV states (plain layout: slot = position).
-int zero_states(KvSeqState** st, int n_seq, cudaStream_t s) {
-  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(st), sizeof(KvSeqState) * (size_t)n_seq, s));
-  B2_CUDA_TRY(cudaMemsetAsync(*st, 0, sizeof(KvSeqState) * (size_t)n_seq, s));
-  return B2_OK;
-}
-int max_seq_on_host(const int32_t* seq, int n, int* out, cudaStream_t s) {
-  std::vector<int32_t> h((size_t)n);
-  B2_CUDA_TRY(cudaMemcpyAsync(h.data(), seq, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
-  B2_CUDA_TRY(cudaStreamSynchronize(s));
-  int m = 0;
-  for (int v : h) {
-    if (v < 0) {
-      set_error("sequence id %d out of range", v);
-      return B2_ERR_INVALID;
-    }
-    m = std::max(m, v);
-  }
-  *out = m + 1;
-  return B2_OK;
-}
-}  // namespace
-
-int b2_rope_kv_store(const float* qkv, int n_tok, int n_head, int n_kv, int head_dim, const int32_t* pos,
+int b2_rope_kv_store(const float* qkv, int n_tok, int n_seq, int n_head, int n_kv, int head_dim, const int32_t* pos,
                      const int32_t* seq, const float* rope, float* q_out, uint16_t* k_cache, uint16_t* v_cache, int cap,
                      void* stream) {
-  B2_CHECK_ARG(qkv && pos && seq && rope && q_out && k_cache && v_cache && n_tok > 0 && cap > 0,
+  B2_CHECK_ARG(qkv && pos && seq && rope && q_out && k_cache && v_cache && n_tok > 0 && n_seq > 0 && cap > 0,
                "rope_kv_store arguments");
   B2_CHECK_ARG(head_dim % 2 == 0 && n_head > 0 && n_kv > 0, "head shape");
-  cudaStream_t s = as_stream(stream);
-  int n_seq = 0;
-  int rc = max_seq_on_host(seq, n_tok, &n_seq, s);
-  if (rc) return rc;
-  KvSeqState* st = nullptr;
-  if ((rc = zero_states(&st, n_seq, s))) return rc;
-  rc = launch_rope_kv(qkv, n_tok, n_head, n_kv, head_dim, pos, seq, rope, q_out, k_cache, v_cache, st, cap, s);
-  cudaFreeAsync(st, s);
-  return rc;
+  return launch_rope_kv(qkv, n_tok, n_head, n_kv, head_dim, pos, seq, rope, q_out, k_cache, v_cache, nullptr, n_seq, cap,
+                        as_stream(stream));
 }
 
 int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
-                   const int32_t* seq, int n_q, int n_head, int n_kv, int head_dim, int cap, float* out, void* stream) {
-  B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && n_q > 0 && cap > 0, "attn_decode arguments");
+                   const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv, int head_dim, int cap, float* out,
+                   void* stream) {
+  B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && n_q > 0 && n_seq > 0 && cap > 0,
+               "attn_decode arguments");
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
   cudaStream_t s = as_stream(stream);
-  int n_seq = 0;
-  int rc = max_seq_on_host(seq, n_q, &n_seq, s);
-  if (rc) return rc;
-  constexpr int P = 256;
-  const int n_split = attn_splits(cap, P);
+  const int n_split = attn_splits(cap);
   const size_t po = (size_t)n_q * n_head * n_split * head_dim, pm = (size_t)n_q * n_head * n_split * 2;
   void* scratch = nullptr;
   B2_CUDA_TRY(cudaMallocAsync(&scratch, (po + pm) * 4, s));
-  KvSeqState* st = nullptr;
-  if ((rc = zero_states(&st, n_seq, s)) == B2_OK) {
-    float* part_o = static_cast<float*>(scratch);
-    rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, st, cap, P, part_o, part_o + po,
-                          out, s);
-    cudaFreeAsync(st, s);
-  }
+  float* part_o = static_cast<float*>(scratch);
+  const int rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap,
+                                  part_o, part_o + po, out, s);
   cudaFreeAsync(scratch, s);
   return rc;
 }
 
 int b2_kv_shift_k(uint16_t* k_cache, int seq, int n_kv, int head_dim, int cap, int p_begin, int p_end, int delta,
                   float theta, void* stream) {
-  B2_CHECK_ARG(k_cache && seq >= 0 && p_begin >= 0 && p_end <= cap && head_dim % 2 == 0, "kv_shift_k arguments");
-  cudaStream_t s = as_stream(stream);
-  std::vector<float> cs((size_t)head_dim);
-  rope_table(theta, head_dim, delta, 1, cs.data());
-  float* csd = nullptr;
-  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&csd), cs.size() * 4, s));
-  B2_CUDA_TRY(cudaMemcpyAsync(csd, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, s));
+  B2_CHECK_ARG(k_cache && seq >= 0 && p_begin >= 0 && p_end <= cap && head_dim % 2 == 0 && head_dim <= 2 * kRotPairs,
+               "kv_shift_k arguments");
+  RotTable cs;
+  rope_table(theta, head_dim, delta, 1, cs.cs);
   const KvSeqState st{0, 0};
-  const int rc = launch_kv_shift(k_cache, n_kv, head_dim, seq, st, cap, p_begin, p_end, csd, s);
-  cudaFreeAsync(csd, s);
-  B2_CUDA_TRY(cudaStreamSynchronize(s));
-  return rc;
+  return launch_kv_shift(k_cache, n_kv, head_dim, seq, st, cap, p_begin, p_end, cs, as_stream(stream));
 }
 
 }  // extern "C"

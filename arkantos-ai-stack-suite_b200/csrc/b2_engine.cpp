@@ -42,7 +42,6 @@ namespace {
 
 constexpr int kStepMax = 8;          // tokens per device step (GEMV batch)
 constexpr int kResWords = 32;        // ids, top-1/margin pairs, status (3*kStepMax+1, padded)
-constexpr int kAttnChunk = 256;      // positions per split-K attention CTA
 
 struct DevQ {
   QMatrix m;
@@ -109,7 +108,6 @@ struct b2_context {
   std::vector<b2::KvSeqState> st;
   std::vector<int> n_past;
   float* rope = nullptr;        // [n_ctx][head_dim]
-  float* shift_cs = nullptr;    // [head_dim] rotation of the last shift
   // step inputs (device + pinned host staging)
   // [tok | pos | seq] x kStepMax in one allocation: one H2D copy per step
   int32_t *in_d = nullptr, *tok_d = nullptr, *pos_d = nullptr, *seq_d = nullptr;
@@ -127,6 +125,7 @@ struct b2_context {
   int* status = nullptr;
   // device-side greedy loop: [n_ctx][kStepMax] generated ids, per-row counts
   int32_t *gen_out = nullptr, *gen_count = nullptr;
+  uint8_t* act_img = nullptr;   // quantized activations of the GEMV being run
   // last decode
   int last_n = 0;
   bool last_logits = false;
@@ -458,7 +457,7 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   B2_CUDA_TRY(cudaMemcpy(c->st_d, c->st.data(), c->n_seq * sizeof(KvSeqState), cudaMemcpyHostToDevice));
   std::vector<float> rope((size_t)c->n_ctx * hd);
   rope_table(m->theta, hd, 0, c->n_ctx, rope.data());
-  if ((rc = dalloc(c, &c->rope, rope.size())) || (rc = dalloc(c, &c->shift_cs, hd))) return rc;
+  if ((rc = dalloc(c, &c->rope, rope.size()))) return rc;
   B2_CUDA_TRY(cudaMemcpy(c->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice));
   if ((rc = dalloc(c, &c->in_d, 3 * kStepMax))) return rc;
   c->tok_d = c->in_d;
@@ -469,7 +468,7 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   for (auto& e : c->in_ev) B2_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   if ((rc = prepare_gemv_kernels())) return rc;
   const int T = kStepMax;
-  const int n_split = attn_splits(c->n_ctx, kAttnChunk);
+  const int n_split = attn_splits(c->n_ctx);
   if ((rc = dalloc(c, &c->x, (size_t)T * d)) || (rc = dalloc(c, &c->delta, (size_t)T * d)) ||
       (rc = dalloc(c, &c->xn, (size_t)T * d)) ||
       (rc = dalloc(c, &c->qkv, (size_t)T * (m->nh_l + 2 * m->nkv_l) * hd)) ||
@@ -480,6 +479,13 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
       (rc = dalloc(c, &c->part_ml, (size_t)T * m->nh_l * n_split * 2)) || (rc = dalloc(c, &c->res, kResWords)) ||
       (rc = dalloc(c, &c->gen_out, (size_t)c->n_ctx * T)) || (rc = dalloc(c, &c->gen_count, T)))
     return rc;
+  {
+    size_t img = gemv_act_image_bytes(m->head.m, T);
+    const Layer& L0 = *m->layers[0];
+    for (const DevQ* q : {&L0.wqkv, &L0.wo, &L0.wgu, &L0.wdown})
+      for (int n = 1; n <= T; ++n) img = std::max(img, gemv_act_image_bytes(q->m, n));
+    if ((rc = dalloc(c, &c->act_img, img))) return rc;
+  }
   c->ids = c->res;
   c->top = reinterpret_cast<float*>(c->res + kStepMax);
   c->status = c->res + 3 * kStepMax;
@@ -518,6 +524,7 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     a.y_stride = ys;
     a.epilogue = epi;
     a.status = c->status;
+    a.act_img = c->act_img;
     a.peer = peer;
     return launch_gemv(a, s);
   };
@@ -539,11 +546,11 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     if ((rc = gemv(L.wqkv, c->xn, d, c->qkv, qkv_w, EPI_STORE))) return rc;
     if ((rc = tap("qkv", l, c->qkv, (int64_t)n * qkv_w))) return rc;
     if ((rc = launch_rope_kv(c->qkv, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->rope, c->q, c->kc[l], c->vc[l],
-                             c->st_d, c->n_ctx, s)))
+                             c->st_d, c->n_seq, c->n_ctx, s)))
       return rc;
     if ((rc = tap("q_rope", l, c->q, (int64_t)n * m->nh_l * hd))) return rc;
     if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->vc[l], c->st_d,
-                               c->n_ctx, kAttnChunk, c->part_o, c->part_ml, c->att, s)))
+                               c->n_seq, c->n_ctx, c->part_o, c->part_ml, c->att, s, c->status)))
       return rc;
     if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
     if ((rc = gemv(L.wo, c->att, (int64_t)m->nh_l * hd, c->delta, d, EPI_STORE, tp ? &out_o : nullptr))) return rc;
@@ -731,19 +738,18 @@ int kv_shift(b2_context* c, int s, int p0, int p1) {
   KvSeqState& st = c->st[s];
   const bool fresh = st.ring_head == 0 && st.n_keep == 0;
   if (fresh) st.n_keep = p0;
-  std::vector<float> cs(m->head_dim);
-  rope_table(m->theta, m->head_dim, -nd, 1, cs.data());
-  B2_CUDA_TRY(cudaMemcpyAsync(c->shift_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
+  RotTable cs;
+  rope_table(m->theta, m->head_dim, -nd, 1, cs.cs);
   int rc = B2_OK;
   if (p0 == st.n_keep) {
     for (int l = 0; l < m->n_layer && !rc; ++l)
-      rc = launch_kv_shift(c->kc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p1, n_past, c->shift_cs, c->stream);
+      rc = launch_kv_shift(c->kc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p1, n_past, cs, c->stream);
     const int ring = c->n_ctx - st.n_keep;
     st.ring_head = ring > 0 ? (st.ring_head + nd) % ring : 0;
   } else {
     for (int l = 0; l < m->n_layer && !rc; ++l)
-      rc = launch_kv_compact(c->kc[l], c->vc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p0, p1, n_past - p1,
-                             c->shift_cs, c->stream);
+      rc = launch_kv_compact(c->kc[l], c->vc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p0, p1, n_past - p1, cs,
+                             c->stream);
   }
   if (rc) return rc;
   c->n_past[s] = n_past - nd;

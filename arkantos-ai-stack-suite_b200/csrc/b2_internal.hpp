@@ -207,9 +207,13 @@ struct PeerIn {
 
 struct GemvArgs {
   const QMatrix* w;
-  const float* x;       // fp32 [n_tok][x_stride], 16-byte aligned; quantized in-kernel
+  const float* x;       // fp32 [n_tok][x_stride], 16-byte aligned
   int64_t x_stride;
   int n_tok;
+  // Device scratch of gemv_act_image_bytes(w, n_tok) bytes: x quantized into
+  // the image the GEMV's CTAs copy into shared memory (written by a quantize
+  // kernel launched first).
+  uint8_t* act_img;
   float* y;             // [n_tok][y_stride]
   int64_t y_stride;
   int epilogue;
@@ -217,6 +221,7 @@ struct GemvArgs {
   const PeerOut* peer = nullptr;   // tensor-parallel exchange of the outputs (EPI_STORE only)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
+size_t gemv_act_image_bytes(const QMatrix& w, int n_tok);
 // Sets the large dynamic shared-memory limit of every GEMV instantiation on
 // the current device (done outside graph capture).
 int prepare_gemv_kernels();

@@ -148,15 +148,19 @@ __device__ __forceinline__ int64_t kv_slot(const KvSeqState& st, int p, int cap)
 __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_kv, int hd, const int32_t* __restrict__ pos,
                                const int32_t* __restrict__ seq, const float* __restrict__ rope, float* __restrict__ q_out,
                                uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, const KvSeqState* __restrict__ st,
-                               int cap) {
+                               int n_seq, int cap) {
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;
   const int p = pos[b], s = seq[b];
+  if (s < 0 || s >= n_seq || p < 0 || p >= cap) {   // outside the cache: zero q, store nothing
+    for (int i = threadIdx.x; i < n_head * hd; i += blockDim.x) q_out[(int64_t)b * n_head * hd + i] = 0.0f;
+    return;
+  }
   const int row_len = (n_head + 2 * n_kv) * hd;
   const float* src = qkv + (int64_t)b * row_len;
   const float* cs = rope + (int64_t)p * hd;
-  const int64_t slot = kv_slot(st[s], p, cap);
+  const int64_t slot = kv_slot(st ? st[s] : KvSeqState{0, 0}, p, cap);
   const int half = hd / 2;
   for (int i = threadIdx.x; i < (n_head + n_kv) * half; i += blockDim.x) {
     const int h = i / half, pr = i - h * half;
@@ -181,137 +185,191 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_
 }
 
 // ---- split-K decode attention ----------------------------------------------------------------
-// CTA (split, kv head, query): positions [split*P, split*P+P) ∩ [0, pos+1) of
-// the query's sequence, for the G query heads sharing the kv head.  Writes
-// unnormalised partial outputs with their running max and sum.
+// CTA (chunk, kv head, query): positions [chunk*128, chunk*128+128) ∩ [0, pos+1)
+// of the query's sequence, for the G query heads sharing the kv head.  The
+// chunk's K and V rows are brought into shared memory by cp.async.bulk (1-D
+// TMA; a chunk crossing the ring's seam or the pinned prefix is up to three
+// copies), then, per head:
+//   scores: lane i of an 8-lane group holds dims [i*HD/8, (i+1)*HD/8) of q and
+//     k; an fmaf chain over its dims, a butterfly over the 8 lanes (xor 4, 2,
+//     1), times 1/sqrt(HD);
+//   m = the chunk's max; e = exp(s − m); the chunk sum l = ((W0 + W1) + W2) + W3
+//     with W_w the 32-lane butterfly (xor 16..1) of e over positions 32w..32w+31;
+//   P·V: output dim d keeps four sums a_r of e·v over the positions i with
+//     i mod 4 == r (fmaf chains in position order; warp r of a dim half takes
+//     them, one position for all heads at a time), then (a0 + a1) + (a2 + a3).
+// Writes the unnormalised partial output with its max and sum.  Every wait is
+// bounded; a query outside the cache attends to nothing.
+constexpr int kAttnP = 128;
 template <int HD, int G>
-__global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict__ q, int n_head, int n_kv,
+__global__ void __launch_bounds__(256) attn_chunk_kernel(const float* __restrict__ q, int n_head, int n_kv,
                                                          const int32_t* __restrict__ pos, const int32_t* __restrict__ seq,
                                                          const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
-                                                         const KvSeqState* __restrict__ st, int cap, int P, float scale,
-                                                         float* __restrict__ part_o, float* __restrict__ part_ml,
-                                                         int n_split) {
+                                                         const KvSeqState* __restrict__ st, int n_seq, int cap,
+                                                         float scale, float* __restrict__ part_o,
+                                                         float* __restrict__ part_ml, int n_split, int* status) {
+  constexpr int P = kAttnP, DL = HD / 8;        // dims per lane of an 8-lane group
+  constexpr int HG = (DL * G <= 64) ? G : 64 / DL;   // heads per score pass (q in registers)
+  constexpr int PAIRS = HD / 2;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);   // [P][HD]
+  uint16_t* vs = ks + P * HD;                                 // [P][HD]
+  float* sc = reinterpret_cast<float*>(vs + P * HD);          // [P][G]: scores, then e
+  __shared__ float mh[G], lh[G], wred[G][4];
   pdl_wait();
   pdl_launch_dependents();
-  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
-  const int n_pos = pos[b] + 1, s = seq[b];
-  const int t0 = split * P, t1 = min(t0 + P, n_pos);
+  const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  const int s = seq[b], pb = pos[b];
+  const int n_pos = (s >= 0 && s < n_seq && pb >= 0 && pb < cap) ? pb + 1 : 0;
+  const int t0 = chunk * P, n = min(P, n_pos - t0);
   const int hq0 = kh * G;
-  float* po = part_o + (((int64_t)b * n_head + hq0) * n_split + split) * HD;
-  float* pml = part_ml + (((int64_t)b * n_head + hq0) * n_split + split) * 2;
-  if (t0 >= t1) {
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-      const int g = i / HD, d = i - g * HD;
-      po[(int64_t)g * n_split * HD + d] = 0.0f;
-    }
-    if (threadIdx.x < G) {
-      pml[(int64_t)threadIdx.x * n_split * 2 + 0] = -FLT_MAX;
-      pml[(int64_t)threadIdx.x * n_split * 2 + 1] = 0.0f;
+  float* po = part_o + (((int64_t)b * n_head + hq0) * n_split + chunk) * HD;
+  float* pml = part_ml + (((int64_t)b * n_head + hq0) * n_split + chunk) * 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (n <= 0) {
+    for (int i = tid; i < G * HD; i += blockDim.x) po[(int64_t)(i / HD) * n_split * HD + i % HD] = 0.0f;
+    if (tid < G) {
+      pml[(int64_t)tid * n_split * 2 + 0] = -FLT_MAX;
+      pml[(int64_t)tid * n_split * 2 + 1] = 0.0f;
     }
     return;
   }
-  extern __shared__ float sm[];
-  float* qs = sm;               // [G][HD]
-  float* sc = qs + G * HD;      // [G][P]
-  __shared__ float red[G][4];
-  const KvSeqState sst = st[s];
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x)
-    qs[i] = q[((int64_t)b * n_head + hq0) * HD + i];
+  const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
+  const int64_t base = ((int64_t)s * n_kv + kh) * cap;   // row of slot 0
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar, (uint32_t)(2 * n * HD * 2));
+    // logical positions [t0, t0+n) as runs of consecutive slots
+    int p = t0;
+    while (p < t0 + n) {
+      const int64_t slot = kv_slot(sst, p, cap);
+      int len = t0 + n - p;
+      if (p < sst.n_keep) len = min(len, sst.n_keep - p);
+      else len = (int)min((int64_t)len, (int64_t)cap - slot);   // up to the end of the ring
+      bulk_g2s(ks + (p - t0) * HD, kc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
+      bulk_g2s(vs + (p - t0) * HD, vc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
+      p += len;
+    }
+  }
+  // q of this lane's dims, for the heads of the first pass, while the copies fly
+  const int li = lane & 7, grp = lane >> 3;
   __syncthreads();
-  const uint16_t* kbase = kc + ((int64_t)s * n_kv + kh) * cap * HD;
-  const uint16_t* vbase = vc + ((int64_t)s * n_kv + kh) * cap * HD;
-  const int n = t1 - t0;
-  // scores: one thread per position
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int64_t slot = kv_slot(sst, t0 + i, cap);
-    const uint4* kr = reinterpret_cast<const uint4*>(kbase + slot * HD);
-    float acc[G];
+  mbar_wait_bounded(bar, 0, status, 5);
+
+  // ---- scores ----
+#pragma unroll 1
+  for (int h0 = 0; h0 < G; h0 += HG) {
+    float qr[HG][DL];
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0.0f;
-#pragma unroll 4
-    for (int c = 0; c < HD / 8; ++c) {
-      const uint4 u = __ldg(kr + c);
-      const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-      float kf[8];
+    for (int h = 0; h < HG; ++h) {
+      const float* qh = q + ((int64_t)b * n_head + hq0 + h0 + h) * HD + li * DL;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(h2[j]);
-        kf[2 * j] = f.x;
-        kf[2 * j + 1] = f.y;
+      for (int d = 0; d < DL; d += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(qh + d);
+        qr[h][d] = v.x;
+        qr[h][d + 1] = v.y;
+        qr[h][d + 2] = v.z;
+        qr[h][d + 3] = v.w;
+      }
+    }
+    for (int it = 0; it < P / 32; ++it) {
+      const int i = warp * (P / 8) + it * 4 + grp;   // position of this lane group
+      float kf[DL];
+      if (i < n) {
+        const uint4* kr = reinterpret_cast<const uint4*>(ks + i * HD + li * DL);
+#pragma unroll
+        for (int c = 0; c < DL / 8; ++c) {
+          const uint4 w = kr[c];
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            kf[c * 8 + 2 * e] = h2f((uint16_t)(ww[e] & 0xFFFFu));
+            kf[c * 8 + 2 * e + 1] = h2f((uint16_t)(ww[e] >> 16));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int d = 0; d < DL; ++d) kf[d] = 0.0f;
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g)
+      for (int h = 0; h < HG; ++h) {
+        float a = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[g] = fmaf(qs[g * HD + c * 8 + j], kf[j], acc[g]);
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) sc[g * P + i] = __fmul_rn(acc[g], scale);
-  }
-  __syncthreads();
-  // per-head max and exp-sum over this split
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = -FLT_MAX;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, sc[g * P + i]);
-    m = warp_max(m);
-    if (lane == 0) red[g][warp] = m;
-  }
-  __syncthreads();
-  float mg[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) mg[g] = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float l = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const float e = b2_expf(__fsub_rn(sc[g * P + i], mg[g]));
-      sc[g * P + i] = e;
-      l = __fadd_rn(l, e);
-    }
-    l = warp_sum(l);
-    if (lane == 0) red[g][warp] = l;
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    const int g = threadIdx.x;
-    pml[(int64_t)g * n_split * 2 + 0] = mg[g];
-    pml[(int64_t)g * n_split * 2 + 1] = __fadd_rn(__fadd_rn(__fadd_rn(red[g][0], red[g][1]), red[g][2]), red[g][3]);
-  }
-  // P·V: threads over head dims (HD/2 __half2 pairs per thread group)
-  constexpr int PAIRS = HD / 2;                     // 64 for HD=128, 32 for HD=64
-  constexpr int TSPLIT = 128 / PAIRS;               // position interleave: 2 or 4
-  const int pr = threadIdx.x % PAIRS, ts = threadIdx.x / PAIRS;
-  float o0[G], o1[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) o0[g] = o1[g] = 0.0f;
-  for (int i = ts; i < n; i += TSPLIT) {
-    const int64_t slot = kv_slot(sst, t0 + i, cap);
-    const float2 v = __half22float2(__ldg(reinterpret_cast<const __half2*>(vbase + slot * HD) + pr));
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float pgi = sc[g * P + i];
-      o0[g] = fmaf(pgi, v.x, o0[g]);
-      o1[g] = fmaf(pgi, v.y, o1[g]);
+        for (int d = 0; d < DL; ++d) a = fmaf(qr[h][d], kf[d], a);
+        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        if (li == 0 && i < n) sc[i * G + h0 + h] = __fmul_rn(a, scale);
+      }
     }
   }
   __syncthreads();
-  // reduce the TSPLIT position interleaves through shared memory (reuse qs)
-  float* acc = qs;   // [TSPLIT][G][HD]
-  if (TSPLIT * G * HD > G * HD + G * P) return;  // not reached for the instantiated shapes
+  // ---- max, exp and the chunk sum: 128 threads per head, 2 heads per round ----
+#pragma unroll 1
+  for (int h0 = 0; h0 < G; h0 += 2) {
+    const int h = h0 + (tid >> 7), w = (tid >> 5) & 3, i = tid & 127;
+    const bool act = h < G;
+    float v = (act && i < n) ? sc[i * G + h] : -FLT_MAX;
+    v = warp_max(v);
+    if (act && lane == 0) wred[h][w] = v;
+    __syncthreads();
+    const float m = act ? fmaxf(fmaxf(wred[h][0], wred[h][1]), fmaxf(wred[h][2], wred[h][3])) : 0.0f;
+    float e = 0.0f;
+    if (act && i < n) {
+      e = b2_expf(__fsub_rn(sc[i * G + h], m));
+      sc[i * G + h] = e;
+    }
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    acc[(ts * G + g) * HD + 2 * pr] = o0[g];
-    acc[(ts * G + g) * HD + 2 * pr + 1] = o1[g];
+    for (int o = 16; o > 0; o >>= 1) e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, o));
+    __syncthreads();   // every wred max read before the sums reuse it
+    if (act && lane == 0) wred[h][w] = e;
+    __syncthreads();
+    if (act && i == 0) {
+      mh[h] = m;
+      lh[h] = __fadd_rn(__fadd_rn(__fadd_rn(wred[h][0], wred[h][1]), wred[h][2]), wred[h][3]);
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-    const int g = i / HD, d = i - g * HD;
-    float v = 0.0f;
+  // ---- P·V: warp (residue r, dim half), lane = dim pair; all heads per position ----
+  float* pv = reinterpret_cast<float*>(ks);   // [4 residues][G][HD] partials, K is no longer needed
+  {
+    const int r = warp & 3, pr = (warp >> 2) * 32 + lane;
+    if (pr < PAIRS) {
+      float acc[G][2];
 #pragma unroll
-    for (int t = 0; t < TSPLIT; ++t) v = __fadd_rn(v, acc[(t * G + g) * HD + d]);
-    po[(int64_t)g * n_split * HD + d] = v;
+      for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0.0f;
+      for (int i = r; i < n; i += 4) {
+        const uint32_t vv = *reinterpret_cast<const uint32_t*>(vs + i * HD + 2 * pr);
+        const float v0 = h2f((uint16_t)(vv & 0xFFFFu)), v1 = h2f((uint16_t)(vv >> 16));
+        float e[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) e[h] = sc[i * G + h];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          acc[h][0] = fmaf(e[h], v0, acc[h][0]);
+          acc[h][1] = fmaf(e[h], v1, acc[h][1]);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        pv[(r * G + h) * HD + 2 * pr] = acc[h][0];
+        pv[(r * G + h) * HD + 2 * pr + 1] = acc[h][1];
+      }
+    }
+  }
+  __syncthreads();
+  for (int hd2 = tid; hd2 < G * HD; hd2 += blockDim.x) {
+    const int h = hd2 / HD, d = hd2 - h * HD;
+    const float a0 = pv[(0 * G + h) * HD + d], a1 = pv[(1 * G + h) * HD + d];
+    const float a2 = pv[(2 * G + h) * HD + d], a3 = pv[(3 * G + h) * HD + d];
+    po[(int64_t)h * n_split * HD + d] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+  }
+  if (tid < G) {
+    pml[(int64_t)tid * n_split * 2 + 0] = mh[tid];
+    pml[(int64_t)tid * n_split * 2 + 1] = lh[tid];
   }
 }
 
@@ -330,7 +388,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
   float L = 0.0f;
   for (int s = 0; s < n_split; ++s)
     if (ml[2 * s + 1] > 0.0f) L = __fadd_rn(L, __fmul_rn(b2_expf(__fsub_rn(ml[2 * s], M)), ml[2 * s + 1]));
-  const float invL = __fdiv_rn(1.0f, L);
+  const float invL = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;   // L == 0: a query that attended to nothing
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float v = 0.0f;
     for (int s = 0; s < n_split; ++s)
@@ -342,10 +400,14 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
 
 // ---- KV shift ----------------------------------------------------------------------------
 // Rotates K rows of logical positions [p_begin, p_end) of sequence s (slots
-// computed with the state before the shift) by the angle table cs[hd] of the
-// position delta, in place: fp16 -> fp32 -> rotate -> fp16 (RNE).
+// computed with the state before the shift) by the angle table of the
+// position delta, in place: fp16 -> fp32 -> rotate -> fp16 (RNE).  The table
+// comes by value (no upload, so the call is stream-ordered and capturable).
 __global__ void kv_shift_kernel(uint16_t* __restrict__ kc, int n_kv, int hd, int s, KvSeqState stt, int cap, int p_begin,
-                                int p_end, const float* __restrict__ cs) {
+                                int p_end, RotTable rt) {
+  __shared__ float cs[2 * kRotPairs];
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) cs[i] = rt.cs[i];
+  __syncthreads();
   const int half = hd / 2;
   const int64_t total = (int64_t)(p_end - p_begin) * n_kv * half;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -365,7 +427,10 @@ __global__ void kv_shift_kernel(uint16_t* __restrict__ kc, int n_kv, int hd, int
 // sequence (dst0 < src0, processed in ascending order by a single CTA per
 // head so overlapping ranges move safely), rotating K by cs (delta table).
 __global__ void kv_compact_kernel(uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int n_kv, int hd, int s,
-                                  KvSeqState stt, int cap, int dst0, int src0, int n, const float* __restrict__ cs) {
+                                  KvSeqState stt, int cap, int dst0, int src0, int n, RotTable rt) {
+  __shared__ float cs[2 * kRotPairs];
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) cs[i] = rt.cs[i];
+  __syncthreads();
   const int kh = blockIdx.x;
   const int half = hd / 2;
   for (int t = 0; t < n; ++t) {
@@ -507,35 +572,29 @@ int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out,
 }
 
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                   const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int cap,
+                   const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int n_seq, int cap,
                    cudaStream_t s) {
   return launch_pdl(rope_kv_kernel, dim3(n_tok), dim3(256), 0, s, qkv, n_head, n_kv, hd, pos, seq, rope, q_out, kc, vc,
-                    st, cap);
+                    st, n_seq, cap);
 }
 
-int attn_splits(int cap, int P) { return (cap + P - 1) / P; }
+int attn_splits(int cap) { return (cap + kAttnP - 1) / kAttnP; }
 
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int cap, int P, float* part_o,
-                     float* part_ml, float* out, cudaStream_t s) {
+                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* part_o,
+                     float* part_ml, float* out, cudaStream_t s, int* status) {
   const int G = n_head / n_kv;
-  const int n_split = attn_splits(cap, P);
+  const int n_split = attn_splits(cap);
   const float scale = 1.0f / sqrtf((float)hd);
   const dim3 grid(n_split, n_kv, n_tok);
   int rc = B2_ERR_UNSUPPORTED;
-  auto smem_for = [&](int g) {
-    const size_t a = (size_t)(g * hd + g * P) * 4;
-    const size_t b = (size_t)(128 / (hd / 2)) * g * hd * 4;
-    return std::max(a, b);
-  };
 #define B2_ATTN_CASE(HDV, GV)                                                                                       \
   if (hd == HDV && G == GV) {                                                                                       \
-    const size_t sm = smem_for(GV);                                                                                 \
-    if (sm > 48 * 1024)                                                                                             \
-      B2_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<HDV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
-                                       (int)sm));                                                                   \
-    rc = launch_pdl(attn_split_kernel<HDV, GV>, grid, dim3(128), sm, s, q, n_head, n_kv, pos, seq, kc, vc, st, cap, \
-                    P, scale, part_o, part_ml, n_split);                                                            \
+    const size_t sm = 128 + (size_t)2 * kAttnP * HDV * 2 + (size_t)GV * kAttnP * 4;                                 \
+    B2_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<HDV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                     (int)sm));                                                                     \
+    rc = launch_pdl(attn_chunk_kernel<HDV, GV>, grid, dim3(256), sm, s, q, n_head, n_kv, pos, seq, kc, vc, st,      \
+                    n_seq, cap, scale, part_o, part_ml, n_split, status);                                           \
   }
   B2_ATTN_CASE(128, 1)
   B2_ATTN_CASE(128, 2)
@@ -556,7 +615,8 @@ int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, co
 }
 
 int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
-                    const float* cs, cudaStream_t s) {
+                    const RotTable& cs, cudaStream_t s) {
+  B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
   if (p_end <= p_begin) return B2_OK;
   const int64_t total = (int64_t)(p_end - p_begin) * n_kv * (hd / 2);
   const int grid = (int)std::min<int64_t>((total + 255) / 256, 4 * kSMs);
@@ -566,7 +626,8 @@ int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& s
 }
 
 int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int dst0,
-                      int src0, int n, const float* cs, cudaStream_t s) {
+                      int src0, int n, const RotTable& cs, cudaStream_t s) {
+  B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
   if (n <= 0) return B2_OK;
   kv_compact_kernel<<<n_kv, std::max(32, hd / 2), 0, s>>>(kc, vc, n_kv, hd, seq, st, cap, dst0, src0, n, cs);
   B2_CUDA_TRY(cudaGetLastError());

@@ -8,7 +8,8 @@
 
 namespace b2 {
 
-// Per-sequence KV bookkeeping, read by kernels from device memory.  Logical
+// Per-sequence KV bookkeeping, read by kernels from device memory (a null
+// state array means every sequence is in the plain layout, slot = position).  Logical
 // position p lives in physical slot p when p < n_keep (the pinned prefix),
 // otherwise in n_keep + (ring_head + p − n_keep) mod (cap − n_keep): the
 // slots after the prefix form a ring, so dropping the oldest positions
@@ -23,19 +24,29 @@ int launch_embed(const int32_t* tokens, int n_tok, int n_vocab, int type, const 
 int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
                        cudaStream_t s, const PeerIn* in = nullptr, int* status = nullptr);
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                   const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int cap,
+                   const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int n_seq, int cap,
                    cudaStream_t s);
 // Split-K attention: positions are cut into chunks of P, one CTA per (chunk,
 // kv head, query); part_o [n_tok][n_head][n_split][hd], part_ml
 // [n_tok][n_head][n_split][2] hold the partial results (scratch).
-int attn_splits(int cap, int P);
+// Split-K decode attention in chunks of 128 positions (attn_splits(cap)
+// partials per query head in part_o [n_tok][n_head][n_split][hd] and
+// part_ml [.][.][n_split][2]), then the combine.  Queries whose sequence id
+// is outside [0, n_seq) or whose position is outside [0, cap) read nothing
+// and produce zero outputs.  st may be null (plain layout).
+int attn_splits(int cap);
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int cap, int P, float* part_o,
-                     float* part_ml, float* out, cudaStream_t s);
+                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* part_o,
+                     float* part_ml, float* out, cudaStream_t s, int* status = nullptr);
+// cos/sin pairs of one position delta for every rotated pair (head_dim <= 256).
+constexpr int kRotPairs = 128;
+struct RotTable {
+  float cs[2 * kRotPairs];
+};
 int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
-                    const float* cs, cudaStream_t s);
+                    const RotTable& cs, cudaStream_t s);
 int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int dst0,
-                      int src0, int n, const float* cs, cudaStream_t s);
+                      int src0, int n, const RotTable& cs, cudaStream_t s);
 // Device-side greedy loop: argmax ids become the next step's tokens.
 struct GreedyFeed {
   int32_t* tok = nullptr;    // [n_tok] next step's tokens (null: no feed)

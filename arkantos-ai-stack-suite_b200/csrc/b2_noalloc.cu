@@ -21,10 +21,7 @@ namespace {
 
 constexpr size_t kScratchBytes = (size_t)B2_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
-constexpr int kStateBytes = B2_NOALLOC_MAX_SEQ * (int)sizeof(KvSeqState);
-constexpr int kChunk = 256;   // positions per attention CTA, as b2_attn_decode
 
-// [KV states of up to B2_NOALLOC_MAX_SEQ sequences, zeroed per call]
 // [per-chunk max/sum][per-chunk partial outputs]
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
@@ -55,43 +52,31 @@ int scratch_address(void** out) {
 using namespace b2;
 
 extern "C" int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                      const int32_t* pos, const int32_t* seq, int n_q, int n_head, int n_kv,
+                                      const int32_t* pos, const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv,
                                       int head_dim, int cap, float* out, void* stream) {
-  B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && cap > 0, "attn_decode_noalloc arguments");
+  B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && cap > 0 && n_seq > 0, "attn_decode_noalloc arguments");
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
   if (n_q < 1 || n_q > B2_NOALLOC_MAX_QUERIES) {
     set_error("attn_decode_noalloc: n_q=%d outside [1, %d]", n_q, B2_NOALLOC_MAX_QUERIES);
     return B2_ERR_INVALID;
   }
-  const int n_split = attn_splits(cap, kChunk);
+  const int n_split = attn_splits(cap);
   const size_t ml_bytes = (size_t)n_q * n_head * n_split * 2 * sizeof(float);
   const size_t o_bytes = (size_t)n_q * n_head * n_split * head_dim * sizeof(float);
-  const size_t ml_off = kStateBytes, o_off = (ml_off + ml_bytes + 255) / 256 * 256;
+  const size_t o_off = (ml_bytes + 255) / 256 * 256;
   if (o_off + o_bytes > kScratchBytes) {
     set_error("attn_decode_noalloc: %d queries x %d heads x %d positions x head_dim %d need %zu scratch bytes, "
               "more than the %zu built in",
               n_q, n_head, cap, head_dim, o_off + o_bytes, kScratchBytes);
     return B2_ERR_INVALID;
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Sequence ids index the zeroed state block: check them on the host.
-  int32_t ids[B2_NOALLOC_MAX_QUERIES];
-  B2_CUDA_TRY(cudaMemcpyAsync(ids, seq, (size_t)n_q * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-  B2_CUDA_TRY(cudaStreamSynchronize(s));
-  for (int i = 0; i < n_q; ++i) {
-    if (ids[i] < 0 || ids[i] >= B2_NOALLOC_MAX_SEQ) {
-      set_error("attn_decode_noalloc: sequence id %d outside [0, %d)", ids[i], B2_NOALLOC_MAX_SEQ);
-      return B2_ERR_INVALID;
-    }
-  }
   void* base = nullptr;
-  int rc = scratch_address(&base);
+  const int rc = scratch_address(&base);
   if (rc) return rc;
   uint8_t* b = static_cast<uint8_t*>(base);
-  // The array keeps the previous call's contents: clear the states (plain
-  // layout, slot = position).  The partial results are fully rewritten.
-  B2_CUDA_TRY(cudaMemsetAsync(b, 0, kStateBytes, s));
-  return launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache,
-                          reinterpret_cast<const KvSeqState*>(b), cap, kChunk, reinterpret_cast<float*>(b + o_off),
-                          reinterpret_cast<float*>(b + ml_off), out, s);
+  // Every partial is rewritten by the call; sequence ids and positions are
+  // bounds-checked by the kernels, so no state block and no host round trip.
+  return launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap,
+                          reinterpret_cast<float*>(b + o_off), reinterpret_cast<float*>(b), out,
+                          static_cast<cudaStream_t>(stream));
 }

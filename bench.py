@@ -598,6 +598,83 @@ def run_decode_reference(args, dist, rank, world, local):
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ------------------------------------------------------------------------------------------
+# Workload: decode attention over an fp16 KV cache + in-place KV shift (config 3)
+# ------------------------------------------------------------------------------------------
+ATTN_HEADS, ATTN_KV, ATTN_HD, ATTN_CTX = 32, 8, 128, 4096
+
+
+def attn_measure(b2, n_seq: int, steps: int) -> dict:
+    """CUDA-event time of b2_attn_decode (one query per sequence at position
+    ctx-1, all ctx positions attended) over rotating KV copies larger than L2,
+    and of the shift that drops the first 1024 positions and re-ropes K."""
+    rng = np.random.default_rng(4)
+    per_seq = ATTN_KV * ATTN_CTX * ATTN_HD            # fp16 values per sequence per cache
+    kv_bytes = 2 * 2 * per_seq * n_seq
+    copies = max(1, -(-300_000_000 // kv_bytes))
+    kv = rng.standard_normal(per_seq * n_seq, dtype=np.float32).astype(np.float16).view(np.uint16)
+    ks = [b2.DeviceBuffer.from_array(kv) for _ in range(copies)]
+    vs = [b2.DeviceBuffer.from_array(kv[::-1].copy()) for _ in range(copies)]
+    q = b2.DeviceBuffer.from_array(rng.standard_normal((n_seq, ATTN_HEADS * ATTN_HD), dtype=np.float32))
+    out = b2.DeviceBuffer(n_seq * ATTN_HEADS * ATTN_HD * 4)
+    pos = b2.DeviceBuffer.from_array(np.full(n_seq, ATTN_CTX - 1, np.int32))
+    seq = b2.DeviceBuffer.from_array(np.arange(n_seq, dtype=np.int32))
+    stream = b2.Stream()
+
+    def one(i, s):
+        b2.check(b2.lib.b2_attn_decode(q.ptr, ks[i % copies].ptr, vs[i % copies].ptr, pos.ptr, seq.ptr, n_seq,
+                                       n_seq, ATTN_HEADS, ATTN_KV, ATTN_HD, ATTN_CTX, out.ptr, s), "attn_decode")
+
+    for i in range(2 * copies):
+        one(i, stream.h)
+    graph = b2.Graph(stream, lambda s: [one(i, s) for i in range(steps)])
+    graph.launch()
+    stream.synchronize()
+    e0, e1 = b2.Event(), b2.Event()
+    e0.record(stream.h)
+    graph.launch()
+    e1.record(stream.h)
+    stream.synchronize()
+    ms = e0.elapsed_ms(e1) / steps
+    nbytes = kv_bytes + n_seq * ATTN_HEADS * ATTN_HD * 8
+    # KV shift: positions [1024, 4096) of every sequence rotated by -1024 (K read + write)
+    def shift(i, s):
+        for sq in range(n_seq):
+            b2.check(b2.lib.b2_kv_shift_k(ks[i % copies].ptr, sq, ATTN_KV, ATTN_HD, ATTN_CTX, 1024, ATTN_CTX, -1024,
+                                          10000.0, s), "kv_shift_k")
+    shift(0, stream.h)
+    sg = b2.Graph(stream, lambda s: [shift(i, s) for i in range(max(1, steps // 4))])
+    sg.launch()
+    stream.synchronize()
+    e0.record(stream.h)
+    sg.launch()
+    e1.record(stream.h)
+    stream.synchronize()
+    ms_shift = e0.elapsed_ms(e1) / max(1, steps // 4)
+    shift_bytes = n_seq * 2 * (ATTN_CTX - 1024) * ATTN_KV * ATTN_HD * 2
+    return {"batch": n_seq, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes, "copies": copies,
+            "shift_ms": ms_shift, "shift_gbs": shift_bytes / (ms_shift * 1e-3) / 1e9, "shift_bytes": shift_bytes}
+
+
+def run_attn_ours(args, dist, rank, world, local):
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    res = [attn_measure(b2, n, args.steps) for n in (1, 4, 16)]
+    peaks = measured_peaks()
+    big = res[-1]
+    return {"metric": "decode attention HBM GB/s (32 q / 8 kv heads, hd 128, ctx 4096, fp16 KV)",
+            "value": round(big["gbs"] * world, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 2,
+            "ms_per_step": big["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16 KV, fp32 math", "data": "synthetic: q, k, v N(0,1) fp16, seed 4",
+            "config": {"workload": "attn_decode batch 16, ctx 4096 (config 3); batches 1 and 4 in 'batches'",
+                       "l2": "inputs larger than L2 (rotating KV copies)"},
+            "roofline": {"bound": "hbm", "achieved": round(big["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(big["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
+                         "algorithmic_bytes_per_launch": big["bytes"]},
+            "batches": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()} for r in res],
+            "gpu_launches": args.steps * 2}
+
+
 TYPE_NAMES = {"q4_0": 2, "q8_0": 8, "q4_k": 12, "q6_k": 14}
 
 
@@ -624,7 +701,8 @@ def run_gemv_op(args, dist, rank, world, local):
 
 WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
              "gemv_q4_0": (run_gemv_ours, run_gemv_reference),
-             "gemv_op": (run_gemv_op, None)}
+             "gemv_op": (run_gemv_op, None),
+             "attn": (run_attn_ours, None)}
 
 
 def main():

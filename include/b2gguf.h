@@ -184,21 +184,26 @@ B2_API int b2_rmsnorm(float* x, const float* delta, const float* w, float* out, 
 /* RoPE (adjacent pairs, ref_rope_f32 test_and_bench_a5.cpp:280-293) on the
  * q and k heads of fused qkv rows, k and v stored to an fp16 cache
  * (cortex_a5_engine.cpp:1144-1203).  qkv fp32 [n_tok][(n_head+2·n_kv)·hd];
- * rope fp32 [positions][hd] (b2_rope_table); pos, seq device int32 [n_tok];
+ * rope fp32 [cap][hd] (b2_rope_table); pos, seq device int32 [n_tok];
  * q_out fp32 [n_tok][n_head][hd]; k_cache / v_cache fp16
- * [n_seq][n_kv][cap][hd], token written at [seq][·][pos]. */
-B2_API int b2_rope_kv_store(const float* qkv, int n_tok, int n_head, int n_kv, int head_dim, const int32_t* pos,
-                            const int32_t* seq, const float* rope, float* q_out, uint16_t* k_cache,
-                            uint16_t* v_cache, int cap, void* stream);
+ * [n_seq][n_kv][cap][hd], token written at [seq][·][pos].  A token whose
+ * sequence id is outside [0, n_seq) or position outside [0, cap) stores
+ * nothing and gets a zero q row.  Stream-ordered, no host synchronization. */
+B2_API int b2_rope_kv_store(const float* qkv, int n_tok, int n_seq, int n_head, int n_kv, int head_dim,
+                            const int32_t* pos, const int32_t* seq, const float* rope, float* q_out,
+                            uint16_t* k_cache, uint16_t* v_cache, int cap, void* stream);
 
 /* Decode attention over the fp16 cache (cortex_a5_engine.cpp:1205-1254),
  * split-K over positions: query i attends to positions 0..pos[i] of sequence
  * seq[i] with its n_head/n_kv grouped heads.  q fp32 [n_q][n_head][hd],
- * out fp32 [n_q][n_head][hd]; caches as above.  Partial results go to
- * stream-ordered scratch allocated by the call. */
+ * out fp32 [n_q][n_head][hd]; caches as above ([n_seq][n_kv][cap][hd]).  A
+ * query whose sequence id is outside [0, n_seq) or position outside
+ * [0, cap) reads nothing and gets a zero row.  Partial results go to
+ * stream-ordered scratch allocated by the call; no host synchronization, so
+ * the call can be captured into a CUDA graph. */
 B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
-                          const int32_t* seq, int n_q, int n_head, int n_kv, int head_dim, int cap, float* out,
-                          void* stream);
+                          const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv, int head_dim, int cap,
+                          float* out, void* stream);
 
 /* b2_attn_decode for callers that cannot allocate device memory while they
  * run (a host that gives the library a fixed device-memory budget at
@@ -206,22 +211,22 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
  * latency or risk its failure mid-turn).  No counterpart in the reference.
  * Same arguments and results as b2_attn_decode; the split-K partials live in
  * one static device array of B2_NOALLOC_SCRATCH_BYTES that every GPU loading
- * the library holds until exit.  Limits: n_q <= B2_NOALLOC_MAX_QUERIES,
- * sequence ids < B2_NOALLOC_MAX_SEQ, and n_q·n_head·ceil(cap/256)·(head_dim+2)·4
- * bytes within the array (larger requests return B2_ERR_INVALID).  The first
+ * the library holds until exit.  Limits: n_q <= B2_NOALLOC_MAX_QUERIES and
+ * n_q·n_head·ceil(cap/128)·(head_dim+2)·4 bytes within the array (larger
+ * requests return B2_ERR_INVALID).  The first
  * call on a device looks up the array's address (call it once before any
  * stream capture).  Calls share the array: calls that overlap on the GPU
  * race and must be serialized by the caller. */
-#define B2_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+#define B2_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
 #define B2_NOALLOC_MAX_QUERIES 64
-#define B2_NOALLOC_MAX_SEQ 4096
 B2_API int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                  const int32_t* pos, const int32_t* seq, int n_q, int n_head, int n_kv,
+                                  const int32_t* pos, const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv,
                                   int head_dim, int cap, float* out, void* stream);
 
 /* The KV shift's re-rotation (Milda/src/engine.cpp:1642-1675): K rows of
  * positions [p_begin, p_end) of sequence seq rotated in place by `delta`
- * positions (fp16 -> fp32 -> rotate -> fp16 RNE). */
+ * positions (fp16 -> fp32 -> rotate -> fp16 RNE).  head_dim <= 256;
+ * stream-ordered, no host synchronization. */
 B2_API int b2_kv_shift_k(uint16_t* k_cache, int seq, int n_kv, int head_dim, int cap, int p_begin, int p_end,
                          int delta, float theta, void* stream);
 

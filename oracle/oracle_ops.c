@@ -641,15 +641,27 @@ void orc_matmul_dev_strided(int wtype, const void* w, int64_t n_rows, size_t row
 }
 
 /* Split-K decode attention in the device kernels' order: positions in chunks
- * of 256; per chunk scores by fmaf over d, max, e = exp_dev(s − m), the
- * chunk's sum by 128 per-thread partial sums (positions ≡ t mod 128), a
- * butterfly per 32-thread warp and the four warps added in order; P·V by
- * fmaf over the positions ≡ ts mod TS (TS = 128/(hd/2)) per output pair,
- * the TS partials added to 0 in order; chunks combined with exp_dev(m_s − M). */
+ * of 128; per chunk and head, the score of a position is eight fmaf chains
+ * over hd/8 consecutive dims each (chain i over dims [i·hd/8, (i+1)·hd/8)),
+ * combined by the 8-lane butterfly (xor 4, 2, 1), times 1/sqrt(hd); m = the
+ * chunk max; e = exp_dev(s − m); the chunk sum is ((W0 + W1) + W2) + W3, W_w
+ * the 32-lane butterfly (xor 16..1) over positions 32w..32w+31 (0 past the
+ * end); P·V per dim keeps four sums a_r of e·v by fmaf over the positions
+ * i ≡ r (mod 4) in order, then (a0 + a1) + (a2 + a3); chunks combined with
+ * exp_dev(m_s − M). */
+static float butterfly(float* v, int n) {
+    float t[32];
+    for (int o = n / 2; o > 0; o >>= 1) {
+        for (int l = 0; l < n; ++l) t[l] = v[l] + v[l ^ o];
+        for (int l = 0; l < n; ++l) v[l] = t[l];
+    }
+    return v[0];
+}
+
 void orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc, int64_t kv_stride, int n_pos,
                          int n_heads, int n_kv_heads, int hd, float* out) {
     const int G = n_heads / n_kv_heads;
-    const int P = 256, NT = 128, PAIRS = hd / 2, TS = NT / PAIRS;
+    const int P = 128, DL = hd / 8;
     const float scale = 1.0f / sqrtf((float)hd);
     const int n_split = (n_pos + P - 1) / P;
     float* sc = (float*)malloc(sizeof(float) * P);
@@ -657,7 +669,6 @@ void orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc,
     float* ls = (float*)malloc(sizeof(float) * (size_t)n_split);
     float* os = (float*)malloc(sizeof(float) * (size_t)n_split * hd);
     float* kt = (float*)malloc(sizeof(float) * (size_t)hd);
-    float* acc = (float*)malloc(sizeof(float) * (size_t)TS * hd);
     for (int h = 0; h < n_heads; ++h) {
         const int kvh = h / G;
         const float* qh = q + (size_t)h * hd;
@@ -666,46 +677,33 @@ void orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc,
             float m = -FLT_MAX;
             for (int i = 0; i < n; ++i) {
                 orc_fp16_to_fp32_row(kc + (size_t)(t0 + i) * kv_stride + (size_t)kvh * hd, kt, hd);
-                float a = 0.0f;
-                for (int d = 0; d < hd; ++d) a = fmaf(qh[d], kt[d], a);
-                sc[i] = a * scale;
+                float a[8];
+                for (int l = 0; l < 8; ++l) {
+                    a[l] = 0.0f;
+                    for (int d = l * DL; d < (l + 1) * DL; ++d) a[l] = fmaf(qh[d], kt[d], a[l]);
+                }
+                sc[i] = butterfly(a, 8) * scale;
                 m = fmaxf(m, sc[i]);
             }
-            float red[4];
-            /* exp and the per-thread partial sums */
-            float lt[128];
-            for (int t = 0; t < NT; ++t) lt[t] = 0.0f;
-            for (int i = 0; i < n; ++i) {
-                sc[i] = orc_expf_dev(sc[i] - m);
-                lt[i % NT] = lt[i % NT] + sc[i];
-            }
+            float W[4];
             for (int w = 0; w < 4; ++w) {
-                float v[32], t[32];
-                for (int l = 0; l < 32; ++l) v[l] = lt[w * 32 + l];
-                for (int o = 16; o > 0; o >>= 1) {
-                    for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
-                    for (int l = 0; l < 32; ++l) v[l] = t[l];
+                float v[32];
+                for (int l = 0; l < 32; ++l) {
+                    const int i = 32 * w + l;
+                    v[l] = i < n ? orc_expf_dev(sc[i] - m) : 0.0f;
                 }
-                red[w] = v[0];
+                W[w] = butterfly(v, 32);
             }
+            for (int i = 0; i < n; ++i) sc[i] = orc_expf_dev(sc[i] - m);
             ms[s] = m;
-            ls[s] = ((red[0] + red[1]) + red[2]) + red[3];
-            for (int ts = 0; ts < TS; ++ts) {
-                for (int pr = 0; pr < PAIRS; ++pr) {
-                    float o0 = 0.0f, o1 = 0.0f;
-                    for (int i = ts; i < n; i += TS) {
-                        const uint16_t* vr = vc + (size_t)(t0 + i) * kv_stride + (size_t)kvh * hd;
-                        o0 = fmaf(sc[i], orc_fp16_to_fp32(vr[2 * pr]), o0);
-                        o1 = fmaf(sc[i], orc_fp16_to_fp32(vr[2 * pr + 1]), o1);
-                    }
-                    acc[ts * hd + 2 * pr] = o0;
-                    acc[ts * hd + 2 * pr + 1] = o1;
-                }
-            }
+            ls[s] = ((W[0] + W[1]) + W[2]) + W[3];
             for (int d = 0; d < hd; ++d) {
-                float v = 0.0f;
-                for (int ts = 0; ts < TS; ++ts) v += acc[ts * hd + d];
-                os[(size_t)s * hd + d] = v;
+                float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (int i = 0; i < n; ++i) {
+                    const float v = orc_fp16_to_fp32(vc[(size_t)(t0 + i) * kv_stride + (size_t)kvh * hd + d]);
+                    a[i & 3] = fmaf(sc[i], v, a[i & 3]);
+                }
+                os[(size_t)s * hd + d] = (a[0] + a[1]) + (a[2] + a[3]);
             }
         }
         float M = -FLT_MAX;
@@ -721,7 +719,7 @@ void orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc,
             out[(size_t)h * hd + d] = v * invL;
         }
     }
-    free(sc); free(ms); free(ls); free(os); free(kt); free(acc);
+    free(sc); free(ms); free(ls); free(os); free(kt);
 }
 
 /* ------------------------------------------------------------------------ */

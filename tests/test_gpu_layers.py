@@ -81,7 +81,7 @@ def test_rope_kv_store_bit_exact(n_head, n_kv, hd):
     vc = np.zeros_like(kc)
     kd, vd, qo = _dev(kc), _dev(vc), b2.DeviceBuffer(n_tok * n_head * hd * 4)
     keep = [_dev(qkv), _dev(pos), _dev(seq), _dev(table)]
-    b2.check(b2.lib.b2_rope_kv_store(keep[0].ptr, n_tok, n_head, n_kv, hd, keep[1].ptr, keep[2].ptr,
+    b2.check(b2.lib.b2_rope_kv_store(keep[0].ptr, n_tok, n_seq, n_head, n_kv, hd, keep[1].ptr, keep[2].ptr,
                                      keep[3].ptr, qo.ptr, kd.ptr, vd.ptr, cap, None))
     q = qo.download(np.float32).reshape(n_tok, n_head * hd)
     kg = kd.download(np.uint16).reshape(kc.shape)
@@ -110,7 +110,7 @@ def test_attn_decode_matches_oracle(n_q, n_pos, n_head, n_kv, hd):
     out = b2.DeviceBuffer(q.nbytes)
     keep = [_dev(q), _dev(kc), _dev(vc), _dev(pos), _dev(seq)]
     b2.check(b2.lib.b2_attn_decode(keep[0].ptr, keep[1].ptr, keep[2].ptr, keep[3].ptr, keep[4].ptr, n_q,
-                                   n_head, n_kv, hd, cap, out.ptr, None))
+                                   n_seq, n_head, n_kv, hd, cap, out.ptr, None))
     got = out.download(np.float32).reshape(n_q, -1)
     for i in range(n_q):
         n = int(pos[i]) + 1
@@ -136,3 +136,33 @@ def test_kv_shift_bit_exact(delta):
     assert np.array_equal(got[1, :, :p0], kc[1, :, :p0])  # positions outside the range untouched
     want = O.kv_shift_k(_cache_to_oracle(kc, 1, cap)[p0:p1], p1 - p0, n_kv, hd, delta, theta)
     assert np.array_equal(_cache_to_oracle(got, 1, cap)[p0:p1], want)
+
+
+def test_out_of_range_queries_read_nothing():
+    """Sequence ids outside [0, n_seq) and positions outside [0, cap) are
+    bounds-checked in the kernels: zero outputs, nothing stored, valid
+    neighbours unaffected."""
+    rng = np.random.default_rng(9)
+    n_seq, n_head, n_kv, hd, cap = 2, 8, 2, 64, 64
+    kc = rng.standard_normal((n_seq, n_kv, cap, hd)).astype(np.float16).view(np.uint16)
+    vc = rng.standard_normal((n_seq, n_kv, cap, hd)).astype(np.float16).view(np.uint16)
+    q = rng.standard_normal((4, n_head * hd)).astype(np.float32)
+    pos = np.array([10, 5, cap, 7], np.int32)
+    seq = np.array([0, n_seq, 1, -1], np.int32)
+    out = b2.DeviceBuffer(q.nbytes)
+    keep = [_dev(q), _dev(kc), _dev(vc), _dev(pos), _dev(seq)]
+    b2.check(b2.lib.b2_attn_decode(keep[0].ptr, keep[1].ptr, keep[2].ptr, keep[3].ptr, keep[4].ptr, 4, n_seq, n_head,
+                                   n_kv, hd, cap, out.ptr, None))
+    got = out.download(np.float32).reshape(4, -1)
+    assert np.all(got[1:] == 0.0)
+    dev = O.attn_decode_dev(q[0], _cache_to_oracle(kc, 0, 11), _cache_to_oracle(vc, 0, 11), 11, n_head, n_kv, hd)
+    assert np.array_equal(_bits(got[0]), _bits(dev))
+    qkv = rng.standard_normal((2, (n_head + 2 * n_kv) * hd)).astype(np.float32)
+    kd, vd, qo = _dev(np.zeros_like(kc)), _dev(np.zeros_like(vc)), b2.DeviceBuffer(2 * n_head * hd * 4)
+    keep = [_dev(qkv), _dev(np.array([3, 3], np.int32)), _dev(np.array([5, 0], np.int32)),
+            _dev(b2.rope_table(10000.0, hd, 0, cap))]
+    b2.check(b2.lib.b2_rope_kv_store(keep[0].ptr, 2, n_seq, n_head, n_kv, hd, keep[1].ptr, keep[2].ptr, keep[3].ptr,
+                                     qo.ptr, kd.ptr, vd.ptr, cap, None))
+    assert np.all(qo.download(np.float32).reshape(2, -1)[0] == 0.0)
+    kg = kd.download(np.uint16).reshape(kc.shape)
+    assert np.all(kg[1] == 0) and np.any(kg[0, :, 3] != 0)

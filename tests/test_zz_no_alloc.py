@@ -21,7 +21,8 @@ def _dev(a):
 def _run(fn, q, kc, vc, pos, seq, n_head, n_kv, hd, cap):
     bufs = [_dev(q), _dev(kc), _dev(vc), _dev(pos), _dev(seq)]
     out = b2.DeviceBuffer(q.nbytes)
-    rc = fn(bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, bufs[3].ptr, bufs[4].ptr, q.shape[0], n_head, n_kv, hd, cap,
+    n_seq = kc.shape[0]
+    rc = fn(bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, bufs[3].ptr, bufs[4].ptr, q.shape[0], n_seq, n_head, n_kv, hd, cap,
             out.ptr, None)
     b2.check(rc, fn.__name__)
     return out.download(np.float32).reshape(q.shape)
