@@ -65,6 +65,7 @@ def _bind() -> None:
         "b2_event_record": (_i, [_vp, _vp]),
         "b2_event_elapsed_ms": (_i, [_vp, _vp, _vp]),
         "b2_set_pdl": (_i, [_i]),
+        "b2_profiler_range": (_i, [_i]),
         "b2_graph_capture_begin": (_i, [_vp]),
         "b2_graph_capture_end": (_i, [_vp, _vp]),
         "b2_graph_launch": (_i, [_vp, _vp]),
@@ -79,6 +80,7 @@ def _bind() -> None:
         "b2_qmatrix_dequantize": (_i, [_vp, _vp, _vp]),
         "b2_quantize_act": (_i, [_i, _vp, _i, _i64, _vp, _vp]),
         "b2_gemv": (_i, [_vp, _vp, _i, _vp, _vp]),
+        "b2_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _vp]),
         "b2_gemv_host": (_i, [_vp, _vp, _i, _vp]),
         "b2_block_dots": (_i, [_vp, _i64, _vp, _vp, _vp, _vp]),
         "b2_gguf_write_synthetic_llama": (_i, [_vp, ctypes.c_char_p, _i]),
@@ -302,6 +304,23 @@ class QMatrix:
 
     def gemv_device(self, x: DeviceBuffer, n_tok: int, y: DeviceBuffer, stream: int | None = None) -> None:
         check(lib.b2_gemv(self.h, x.ptr, n_tok, y.ptr, stream), "gemv")
+
+    def gemm_device(self, x: DeviceBuffer, n_tok: int, y: DeviceBuffer, status: DeviceBuffer | None = None,
+                    stream: int | None = None) -> None:
+        """Tensor-core prefill GEMM (Q4_K): x fp32 [n_tok, k] -> y fp32 [n_tok, n_rows] on the device."""
+        check(lib.b2_gemm(self.h, x.ptr, n_tok, y.ptr, status.ptr if status else None, stream), "gemm")
+
+    def gemm(self, x: np.ndarray) -> np.ndarray:
+        """Prefill GEMM from host arrays; raises if a pipeline wait expired."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        xd = DeviceBuffer.from_array(x)
+        yd = DeviceBuffer(x.shape[0] * self.n_rows * 4)
+        st = DeviceBuffer.from_array(np.zeros(1, np.int32))
+        self.gemm_device(xd, x.shape[0], yd, st)
+        code = int(st.download(np.int32)[0])
+        if code:
+            raise RuntimeError(f"gemm pipeline wait expired (code {code})")
+        return yd.download(np.float32).reshape(x.shape[0], self.n_rows)
 
     def gemv(self, x: np.ndarray) -> np.ndarray:
         """Device GEMV from host arrays (the e2e path): x [n_tok, k] -> y [n_tok, n_rows]."""

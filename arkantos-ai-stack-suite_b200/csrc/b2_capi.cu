@@ -7,6 +7,8 @@
 #include <thread>
 #include <vector>
 
+#include <cuda_profiler_api.h>
+
 #include "b2_common.cuh"
 #include "b2_layers.hpp"
 
@@ -162,6 +164,11 @@ int b2_graph_destroy(void* graph_exec) {
   B2_CUDA_TRY(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)));
   return B2_OK;
 }
+int b2_profiler_range(int start) {
+  B2_CUDA_TRY(start ? cudaProfilerStart() : cudaProfilerStop());
+  return B2_OK;
+}
+
 int b2_set_pdl(int enabled) {
   b2::set_pdl(enabled != 0);
   return B2_OK;
@@ -273,6 +280,19 @@ int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stre
   B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&a.act_img), gemv_act_image_bytes(w->m, n_tok), s));
   const int rc = launch_gemv(a, s);
   const cudaError_t e = cudaFreeAsync(a.act_img, s);
+  if (rc) return rc;
+  B2_CUDA_TRY(e);
+  return B2_OK;
+}
+
+int b2_gemm(const b2_qmatrix* w, const float* x, int n_tok, float* y, int* status, void* stream) {
+  B2_CHECK_ARG(w && x && y && n_tok >= 1, "gemm arguments");
+  B2_CHECK_ARG(w->m.type == B2_Q4_K, "b2_gemm takes Q4_K weights");
+  cudaStream_t s = as_stream(stream);
+  uint8_t* img = nullptr;
+  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&img), gemm_act_image_bytes(w->m, n_tok), s));
+  const int rc = launch_gemm(w->m, x, w->m.k, n_tok, y, img, status, s);
+  const cudaError_t e = cudaFreeAsync(img, s);
   if (rc) return rc;
   B2_CUDA_TRY(e);
   return B2_OK;

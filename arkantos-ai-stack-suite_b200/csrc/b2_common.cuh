@@ -90,6 +90,9 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kPeerWaitNs = 2000000000ull;
 __device__ __forceinline__ bool wait_peer_flags(const unsigned long long* flags, int n, unsigned long long target,
                                                 int* status, int code) {
+  // after one expiry in this step the others give up at once (a lost peer
+  // costs one wait, not one per phase)
+  if (status && *reinterpret_cast<volatile int*>(status) != 0) return false;
   const uint64_t t0 = globaltimer_ns();
   for (int j = 0; j < n; ++j) {
     while (ld_acquire_sys_u64(flags + j) < target) {

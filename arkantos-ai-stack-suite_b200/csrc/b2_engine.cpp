@@ -21,6 +21,7 @@
 // result does not depend on timing.  NCCL is used once per context, to
 // exchange the IPC handles.
 #include <math.h>
+#include <stdlib.h>
 #include <nccl.h>
 #include <string.h>
 
@@ -252,6 +253,9 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
     }
     ncclUniqueId id;
     memcpy(&id, p->nccl_id, sizeof id);
+    // NCCL only carries the IPC-handle exchange here: no NVLink multicast
+    // (NVLS) objects are wanted, unless the user asked for them.
+    setenv("NCCL_NVLS_ENABLE", "0", 0);
     B2_NCCL_TRY(ncclCommInitRank(&m->comm, tp, id, r));
   }
   // Embedding table (replicated, GGUF bytes as-is) and output norm.

@@ -222,6 +222,13 @@ struct GemvArgs {
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 size_t gemv_act_image_bytes(const QMatrix& w, int n_tok);
+
+// Tensor-core prefill GEMM (Q4_K weights, any number of tokens), summation
+// order identical to the reference's per-row vec_dot.  `img` is device
+// scratch of gemm_act_image_bytes(w, n_tok) bytes; y fp32 [n_tok][n_rows].
+size_t gemm_act_image_bytes(const QMatrix& w, int n_tok);
+int launch_gemm(const QMatrix& w, const float* x, int64_t x_stride, int n_tok, float* y, uint8_t* img, int* status,
+                cudaStream_t s);
 // Sets the large dynamic shared-memory limit of every GEMV instantiation on
 // the current device (done outside graph capture).
 int prepare_gemv_kernels();

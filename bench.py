@@ -441,10 +441,14 @@ def run_decode_ours(args, dist, rank, world, local):
         ctx.generate(start_tok, CLOCK_LOAD_STEPS, seq=seqs)     # untimed load: clocks seen under work
         rewind()
         barrier(dist)
+        if args.profile_range:
+            b2.check(b2.lib.b2_profiler_range(1), "profiler_range")
         e0.record(ctx.stream)
         gen = ctx.generate(start_tok, args.steps, seq=seqs)
         e1.record(ctx.stream)
         ctx.synchronize()
+        if args.profile_range:
+            b2.check(b2.lib.b2_profiler_range(0), "profiler_range")
     ms_total = dist_max(dist, e0.elapsed_ms(e1))
     ms_step = ms_total / args.steps
     tok_s = BATCH * args.steps / (ms_total * 1e-3)
@@ -659,14 +663,15 @@ def attn_measure(b2, n_seq: int, steps: int) -> dict:
 def run_attn_ours(args, dist, rank, world, local):
     import b2gguf as b2
     b2.check(b2.lib.b2_set_device(local), "set_device")
-    res = [attn_measure(b2, n, args.steps) for n in (1, 4, 16)]
+    batches = (1, 4, 16) if args.attn_batch is None else (args.attn_batch,)
+    res = [attn_measure(b2, n, args.steps) for n in batches]
     peaks = measured_peaks()
     big = res[-1]
     return {"metric": "decode attention HBM GB/s (32 q / 8 kv heads, hd 128, ctx 4096, fp16 KV)",
             "value": round(big["gbs"] * world, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 2,
             "ms_per_step": big["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp16 KV, fp32 math", "data": "synthetic: q, k, v N(0,1) fp16, seed 4",
-            "config": {"workload": "attn_decode batch 16, ctx 4096 (config 3); batches 1 and 4 in 'batches'",
+            "config": {"workload": f"attn_decode batch {big['batch']}, ctx 4096 (config 3); all batches in 'batches'",
                        "l2": "inputs larger than L2 (rotating KV copies)"},
             "roofline": {"bound": "hbm", "achieved": round(big["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(big["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
@@ -714,6 +719,9 @@ def main():
     ap.add_argument("--workload", default="decode_8b_q4k", choices=sorted(WORKLOADS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--keep-model", action="store_true", help="keep the synthetic GGUF file after the run")
+    ap.add_argument("--attn-batch", type=int, default=None, help="attn: one batch size (default 1, 4 and 16)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="open the profiler range around the timed decode steps only")
     ap.add_argument("--qtype", default="q4_k", choices=sorted(TYPE_NAMES), help="gemv_op weight type")
     ap.add_argument("--rows", type=int, default=28672, help="gemv_op output rows")
     ap.add_argument("--cols", type=int, default=4096, help="gemv_op input columns")

@@ -92,6 +92,10 @@ B2_API int b2_graph_destroy(void* graph_exec);
 /* Enables (1) or disables (0) programmatic dependent launch between this
  * library's kernels on the calling thread (default 1). */
 B2_API int b2_set_pdl(int enabled);
+/* Opens (1) or closes (0) the profiler collection range (cudaProfilerStart /
+ * cudaProfilerStop): a profiler started with collection off records only
+ * the work issued inside the range. */
+B2_API int b2_profiler_range(int start);
 
 /* ------------------------------------------------------------------------ */
 /* Host-side format helpers (CPU only; no device needed)                     */
@@ -151,6 +155,15 @@ B2_API int b2_quantize_act(int act_type, const float* x, int n_tok, int64_t k, v
  * quantized exactly as the reference's CPU path does (Q8_0 for Q4_0/Q8_0,
  * Q8_K for Q4_K/Q6_K).  x fp32 [n_tok][k], y fp32 [n_tok][n_rows]. */
 B2_API int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stream);
+
+/* Prefill GEMM on the tensor cores (tcgen05, fp32 accumulation in TMEM),
+ * the reference's matmul_quantized (Singularity/src/core/cortex_a5_engine.cpp:997-1027)
+ * for any n_tok >= 1: y[t][r] = vec_dot(W row r, Q8_K(x[t])), super-blocks
+ * added in order exactly as the CPU vec_dot adds them, so y is bit-identical
+ * to the reference's per-row result.  Q4_K weights.  x fp32 [n_tok][k]
+ * (16-byte aligned), y fp32 [n_tok][n_rows].  `status` (device int, may be
+ * NULL) receives a nonzero code if a pipeline wait expired. */
+B2_API int b2_gemm(const b2_qmatrix* w, const float* x, int n_tok, float* y, int* status, void* stream);
 
 /* Same GEMV through host buffers: uploads x, runs, reads y back, synchronous.
  * The call a host engine makes per projection when it keeps activations on
