@@ -80,7 +80,9 @@ def _bind() -> None:
         "b2_qmatrix_dequantize": (_i, [_vp, _vp, _vp]),
         "b2_quantize_act": (_i, [_i, _vp, _i, _i64, _vp, _vp]),
         "b2_gemv": (_i, [_vp, _vp, _i, _vp, _vp]),
-        "b2_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _vp]),
+        "b2_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _sz, _vp, _vp]),
+        "b2_gemm_workspace_bytes": (_i, [_vp, _i, _vp]),
+        "b2_gemm_host": (_i, [_vp, _vp, _i, _vp]),
         "b2_gemv_host": (_i, [_vp, _vp, _i, _vp]),
         "b2_block_dots": (_i, [_vp, _i64, _vp, _vp, _vp, _vp]),
         "b2_gguf_write_synthetic_llama": (_i, [_vp, ctypes.c_char_p, _i]),
@@ -140,6 +142,30 @@ def ptr(a: np.ndarray) -> int:
 
 
 # ---- device memory -----------------------------------------------------------------------
+class PinnedArray:
+    """Page-locked host memory (b2_host_alloc) viewed as a numpy array."""
+
+    def __init__(self, shape, dtype=np.float32):
+        self.nbytes = int(np.prod(shape)) * np.dtype(dtype).itemsize
+        p = ctypes.c_void_p()
+        check(lib.b2_host_alloc(ctypes.byref(p), max(self.nbytes, 1)), "host_alloc")
+        self.p = p.value
+        buf = (ctypes.c_uint8 * max(self.nbytes, 1)).from_address(self.p)
+        self.array = np.frombuffer(buf, np.uint8, self.nbytes).view(dtype).reshape(shape)
+
+    @classmethod
+    def from_array(cls, a: np.ndarray) -> "PinnedArray":
+        h = cls(a.shape, a.dtype)
+        h.array[...] = a
+        return h
+
+    def __del__(self):
+        if getattr(self, "p", None):
+            self.array = None
+            lib.b2_host_free(self.p)
+            self.p = None
+
+
 class DeviceBuffer:
     """Raw device allocation owned by Python."""
 
@@ -305,22 +331,25 @@ class QMatrix:
     def gemv_device(self, x: DeviceBuffer, n_tok: int, y: DeviceBuffer, stream: int | None = None) -> None:
         check(lib.b2_gemv(self.h, x.ptr, n_tok, y.ptr, stream), "gemv")
 
-    def gemm_device(self, x: DeviceBuffer, n_tok: int, y: DeviceBuffer, status: DeviceBuffer | None = None,
-                    stream: int | None = None) -> None:
-        """Tensor-core prefill GEMM (Q4_K): x fp32 [n_tok, k] -> y fp32 [n_tok, n_rows] on the device."""
-        check(lib.b2_gemm(self.h, x.ptr, n_tok, y.ptr, status.ptr if status else None, stream), "gemm")
+    def gemm_workspace_bytes(self, n_tok: int) -> int:
+        v = ctypes.c_size_t()
+        check(lib.b2_gemm_workspace_bytes(self.h, n_tok, ctypes.byref(v)), "gemm_workspace_bytes")
+        return v.value
 
-    def gemm(self, x: np.ndarray) -> np.ndarray:
-        """Prefill GEMM from host arrays; raises if a pipeline wait expired."""
+    def gemm_device(self, x: DeviceBuffer, n_tok: int, y: DeviceBuffer, status: DeviceBuffer | None = None,
+                    stream: int | None = None, workspace: DeviceBuffer | None = None) -> None:
+        """Tensor-core prefill GEMM (Q4_K): x fp32 [n_tok, k] -> y fp32 [n_tok, n_rows] on the device."""
+        check(lib.b2_gemm(self.h, x.ptr, n_tok, y.ptr, workspace.ptr if workspace else None,
+                          workspace.nbytes if workspace else 0, status.ptr if status else None, stream), "gemm")
+
+    def gemm(self, x: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """Prefill GEMM from host arrays (the e2e path; pass pinned arrays for
+        full copy bandwidth); raises if a pipeline wait expired."""
         x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
-        xd = DeviceBuffer.from_array(x)
-        yd = DeviceBuffer(x.shape[0] * self.n_rows * 4)
-        st = DeviceBuffer.from_array(np.zeros(1, np.int32))
-        self.gemm_device(xd, x.shape[0], yd, st)
-        code = int(st.download(np.int32)[0])
-        if code:
-            raise RuntimeError(f"gemm pipeline wait expired (code {code})")
-        return yd.download(np.float32).reshape(x.shape[0], self.n_rows)
+        y = out if out is not None else np.empty((x.shape[0], self.n_rows), np.float32)
+        assert y.shape == (x.shape[0], self.n_rows) and y.dtype == np.float32 and y.flags.c_contiguous
+        check(lib.b2_gemm_host(self.h, ptr(x), x.shape[0], ptr(y)), "gemm_host")
+        return y
 
     def gemv(self, x: np.ndarray) -> np.ndarray:
         """Device GEMV from host arrays (the e2e path): x [n_tok, k] -> y [n_tok, n_rows]."""

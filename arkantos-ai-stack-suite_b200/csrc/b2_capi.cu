@@ -276,7 +276,10 @@ int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stre
   a.epilogue = EPI_STORE;
   B2_CHECK_ARG(n_tok >= 1 && n_tok <= 8, "n_tok must be in [1, 8]");
   cudaStream_t s = as_stream(stream);
-  // stream-ordered scratch for the quantized activations (graph-capturable)
+  // Small activations are quantized inside the GEMV: no scratch, so a
+  // captured sequence of GEMVs is kernels only and keeps its programmatic
+  // (PDL) edges.  Larger ones get stream-ordered scratch for the image.
+  if (!gemv_needs_image(w->m, n_tok)) return launch_gemv(a, s);
   B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&a.act_img), gemv_act_image_bytes(w->m, n_tok), s));
   const int rc = launch_gemv(a, s);
   const cudaError_t e = cudaFreeAsync(a.act_img, s);
@@ -285,12 +288,25 @@ int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stre
   return B2_OK;
 }
 
-int b2_gemm(const b2_qmatrix* w, const float* x, int n_tok, float* y, int* status, void* stream) {
+int b2_gemm_workspace_bytes(const b2_qmatrix* w, int n_tok, size_t* bytes) {
+  B2_CHECK_ARG(w && bytes && n_tok >= 1, "gemm_workspace_bytes arguments");
+  *bytes = gemm_act_image_bytes(w->m, n_tok);
+  return B2_OK;
+}
+
+int b2_gemm(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* workspace, size_t workspace_bytes,
+            int* status, void* stream) {
   B2_CHECK_ARG(w && x && y && n_tok >= 1, "gemm arguments");
   B2_CHECK_ARG(w->m.type == B2_Q4_K, "b2_gemm takes Q4_K weights");
   cudaStream_t s = as_stream(stream);
+  const size_t need = gemm_act_image_bytes(w->m, n_tok);
+  if (workspace) {
+    B2_CHECK_ARG(workspace_bytes >= need && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0,
+                 "gemm workspace too small or not 16-byte aligned");
+    return launch_gemm(w->m, x, w->m.k, n_tok, y, static_cast<uint8_t*>(workspace), status, s);
+  }
   uint8_t* img = nullptr;
-  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&img), gemm_act_image_bytes(w->m, n_tok), s));
+  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&img), need, s));
   const int rc = launch_gemm(w->m, x, w->m.k, n_tok, y, img, status, s);
   const cudaError_t e = cudaFreeAsync(img, s);
   if (rc) return rc;
@@ -341,6 +357,28 @@ int b2_gemv_host(const b2_qmatrix* w, const float* x_host, int n_tok, float* y_h
   B2_CUDA_TRY(cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, s));
   B2_CUDA_TRY(cudaStreamSynchronize(s));
   return B2_OK;
+}
+
+int b2_gemm_host(const b2_qmatrix* w, const float* x_host, int n_tok, float* y_host) {
+  B2_CHECK_ARG(w && x_host && y_host && n_tok >= 1, "gemm_host arguments");
+  const size_t xb = (size_t)n_tok * w->m.k * 4, yb = (size_t)n_tok * w->m.n_rows * 4;
+  const size_t xoff = (xb + 255) / 256 * 256, soff = xoff + (yb + 255) / 256 * 256;
+  int rc = stage_reserve(soff + 256);
+  if (rc != B2_OK) return rc;
+  cudaStream_t s = 0;
+  uint8_t* base = static_cast<uint8_t*>(g_stage.dev);
+  float* xd = reinterpret_cast<float*>(base);
+  float* yd = reinterpret_cast<float*>(base + xoff);
+  int* st = reinterpret_cast<int*>(base + soff);
+  B2_CUDA_TRY(cudaMemsetAsync(st, 0, sizeof(int), s));
+  B2_CUDA_TRY(cudaMemcpyAsync(xd, x_host, xb, cudaMemcpyHostToDevice, s));
+  rc = b2_gemm(w, xd, n_tok, yd, nullptr, 0, st, s);
+  if (rc != B2_OK) return rc;
+  int code = 0;
+  B2_CUDA_TRY(cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, s));
+  B2_CUDA_TRY(cudaMemcpyAsync(&code, st, sizeof(int), cudaMemcpyDeviceToHost, s));
+  B2_CUDA_TRY(cudaStreamSynchronize(s));
+  return code ? B2_ERR_TIMEOUT : B2_OK;
 }
 
 int b2_block_dots(const b2_qmatrix* w, int64_t row, const float* x, int32_t* out_i, int32_t* out_m, void* stream) {

@@ -830,6 +830,10 @@ int launch_quantize_image(const QMatrix& w, const float* x, int64_t x_stride, in
 
 size_t gemv_act_image_bytes(const QMatrix& w, int n_tok) { return act_geom(w, n_tok).bytes; }
 
+// Small activations (<= 32 KB of fp32) are quantized by every CTA itself;
+// larger ones go through the image in global memory.
+bool gemv_needs_image(const QMatrix& w, int n_tok) { return (size_t)n_tok * w.k * 4 > 32 * 1024; }
+
 int prepare_gemv_kernels() {
   static bool done[64] = {false};
   int dev = 0;
@@ -853,7 +857,8 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   B2_CHECK_ARG(a.epilogue != EPI_SWIGLU || (w.n_rows % 2) == 0, "SwiGLU needs (gate, up) row pairs");
   B2_CHECK_ARG((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride % 4) == 0,
                "x must be 16-byte aligned with a stride of whole float4s");
-  B2_CHECK_ARG(a.act_img != nullptr && (reinterpret_cast<uintptr_t>(a.act_img) & 15) == 0,
+  B2_CHECK_ARG(!gemv_needs_image(w, a.n_tok) ||
+                   (a.act_img != nullptr && (reinterpret_cast<uintptr_t>(a.act_img) & 15) == 0),
                "activation image scratch (16-byte aligned)");
   GemvP p = {};
   p.w = w.data;
@@ -889,7 +894,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   // Small activations are quantized by each CTA itself (no extra kernel and
   // no dependency on a shared image between consecutive launches); large ones
   // once, into the image every CTA copies.
-  const bool in_kernel = (size_t)a.n_tok * w.k * 4 <= 32 * 1024;
+  const bool in_kernel = !gemv_needs_image(w, a.n_tok);
   p.act_img = in_kernel ? nullptr : a.act_img;
   // Stages of P tiles x U unit steps of all S ranges, U as large as fits ~32 KB.
   const int P = 8 / w.splits;

@@ -222,6 +222,7 @@ struct GemvArgs {
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 size_t gemv_act_image_bytes(const QMatrix& w, int n_tok);
+bool gemv_needs_image(const QMatrix& w, int n_tok);
 
 // Tensor-core prefill GEMM (Q4_K weights, any number of tokens), summation
 // order identical to the reference's per-row vec_dot.  `img` is device

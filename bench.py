@@ -14,6 +14,10 @@ Prints one JSON line (rank 0).  Workloads:
               b2_decode + b2_get_argmax.  Every step reads all weights (4.36 GB
               / TP per rank) from HBM.  The line also carries the Q4_0 GEMV
               below as "q4_0_gemv".
+  gemm_q4k    Prefill GEMM on the tensor cores: W 11008x4096 N(0,0.02)
+              seed 2 -> GGUF Q4_K, X fp32 [512x4096] N(0,1) seed 3, Y fp32
+              [512x11008]; one step = one b2_gemm (activation quantize +
+              tcgen05 GEMM) over rotating W copies (> 2x L2).
   gemv_q4_0   Q4_0 block-quantized GEMV, batch 1: W 4096x4096 N(0,0.02) seed 0
               -> GGUF Q4_0, x fp32[4096] N(0,1) seed 1 quantized to Q8_0 in the
               kernel, y fp32[4096].  One step = one GEMV; consecutive steps
@@ -680,6 +684,130 @@ def run_attn_ours(args, dist, rank, world, local):
             "gpu_launches": args.steps * 2}
 
 
+# ------------------------------------------------------------------------------------------
+# Workload: quantized prefill GEMM on the tensor cores (config 2)
+# ------------------------------------------------------------------------------------------
+GEMM_N, GEMM_K, GEMM_T = 11008, 4096, 512
+GEMM_FLOP = 2 * GEMM_N * GEMM_K * GEMM_T
+GEMM_REF_TOKENS = 8          # tokens per reference-arm step (a bounded sample of the 512)
+
+
+def gemm_inputs(b2):
+    w = b2.synth_normal(2, GEMM_N * GEMM_K, std=0.02).reshape(GEMM_N, GEMM_K)
+    q = b2.quantize_weights(b2.Q4_K, w)
+    x = b2.synth_normal(3, GEMM_T * GEMM_K).reshape(GEMM_T, GEMM_K)
+    return q, x
+
+
+def cpu_gemm_rate(q, x, seconds: float | None, n_tok: int | None, nt: int) -> tuple[float, int]:
+    """Oracle (reference-order) matmul of whole tokens on nt host threads:
+    returns (seconds per token, tokens done)."""
+    from oracle import oracle as O
+    xq = O.quantize_act(O.Q4_K, x[:1])
+    O.matmul(O.Q4_K, q, GEMM_N, GEMM_K, xq[0], nt)
+    n, t0 = 0, time.perf_counter()
+    while (n_tok is not None and n < n_tok) or (seconds is not None and time.perf_counter() - t0 < seconds):
+        xq = O.quantize_act(O.Q4_K, x[n % GEMM_T:n % GEMM_T + 1])
+        O.matmul(O.Q4_K, q, GEMM_N, GEMM_K, xq[0], nt)
+        n += 1
+    return (time.perf_counter() - t0) / n, n
+
+
+def run_gemm_ours(args, dist, rank, world, local):
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    q, x = gemm_inputs(b2)
+    wb = q.nbytes
+    copies = max(2, -(-300_000_000 // wb))               # rotating W copies, > 2x L2
+    mats = [b2.QMatrix(b2.Q4_K, q, GEMM_N, GEMM_K) for _ in range(copies)]
+    xd = b2.DeviceBuffer.from_array(x)
+    yd = b2.DeviceBuffer(GEMM_T * GEMM_N * 4)
+    st = b2.DeviceBuffer.from_array(np.zeros(1, np.int32))
+    ws = b2.DeviceBuffer(mats[0].gemm_workspace_bytes(GEMM_T))
+    stream = b2.Stream()
+
+    def step(i, s):
+        mats[i % copies].gemm_device(xd, GEMM_T, yd, st, s, ws)
+
+    for i in range(max(args.warmup, 3)):
+        step(i, stream.h)
+    stream.synchronize()
+    graph = b2.Graph(stream, lambda s: [step(i, s) for i in range(args.steps)])
+    graph.launch()
+    stream.synchronize()
+    e0, e1 = b2.Event(), b2.Event()
+    barrier(dist)
+    with ClockSampler(local) as clk:
+        t_end = time.time() + 0.4
+        while time.time() < t_end:
+            graph.launch()
+            stream.synchronize()
+        e0.record(stream.h)
+        graph.launch()
+        e1.record(stream.h)
+        stream.synchronize()
+    ms_step = dist_max(dist, e0.elapsed_ms(e1) / args.steps)
+    code = int(st.download(np.int32)[0])
+    if code:
+        raise RuntimeError(f"gemm pipeline wait expired (code {code})")
+    tflops = GEMM_FLOP / (ms_step * 1e-3) / 1e12
+
+    # e2e: X from pinned host memory, Y back to pinned host memory, inside the timed region
+    xh = b2.PinnedArray.from_array(x)
+    yh = b2.PinnedArray((GEMM_T, GEMM_N))
+    n_e2e = max(5, min(args.steps, 50))
+    for _ in range(2):
+        mats[0].gemm(xh.array, yh.array)
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        mats[0].gemm(xh.array, yh.array)
+    e2e_s = dist_max(dist, (time.perf_counter() - t0) / n_e2e)
+    peaks = measured_peaks()
+    out = {
+        "metric": "Q4_K prefill GEMM TFLOP/s (W 11008x4096, X 512x4096)",
+        "value": round(tflops * world, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_k x q8_k -> f16 exact integers -> f32 (TMEM)",
+        "data": "synthetic: W N(0,0.02) seed 2 -> GGUF Q4_K; X N(0,1) seed 3",
+        "config": {"workload": "gemm_q4k 11008x4096 x 512 tokens (config 2)", "rotating_weight_copies": copies,
+                   "l2": f"inputs larger than L2 ({copies} rotating W copies, {copies * wb / 1e6:.0f} MB)",
+                   "replicas": world},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": None,
+                     "peak_src": peaks["src"] + " bf16 burst", "algorithmic_flop_per_launch": GEMM_FLOP},
+        "e2e": {"value": round(GEMM_FLOP * world / e2e_s / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": GEMM_T * GEMM_K * 4, "d2h_bytes_per_step": GEMM_T * GEMM_N * 4},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        nt = os.cpu_count() or 1
+        per_tok, n = cpu_gemm_rate(q, x, args.cpu_seconds, None, nt)
+        out["cpu_baseline"] = {"value": round(2 * GEMM_N * GEMM_K / per_tok / 1e12, 5), "unit": "TFLOP/s",
+                               "cores": nt, "kind": "port",
+                               "sample": f"{n} tokens (Q8_K quantize + 11008 row vec_dots) in {args.cpu_seconds:.0f} s"}
+    return out
+
+
+def run_gemm_reference(args, dist, rank, world, local):
+    if rank != 0:
+        return None
+    import b2gguf as b2  # host-only helpers (quantizer, generator)
+    q, x = gemm_inputs(b2)
+    nt = os.cpu_count() or 1
+    cpu_gemm_rate(q, x, None, max(1, args.warmup), nt)
+    per_tok, n = cpu_gemm_rate(q, x, None, GEMM_REF_TOKENS * args.steps, nt)
+    v = round(2 * GEMM_N * GEMM_K / per_tok / 1e12, 5)
+    return {"metric": "Q4_K prefill GEMM TFLOP/s (W 11008x4096, X 512x4096)", "value": v, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per_tok * GEMM_REF_TOKENS * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k x q8_k -> int32 -> f32", "data": "synthetic",
+            "config": {"workload": "gemm_q4k 11008x4096 x 512 tokens (config 2)"}, "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port",
+                             "sample": f"{n} of the 512 tokens ({GEMM_REF_TOKENS} per step) on {nt} host threads"},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 TYPE_NAMES = {"q4_0": 2, "q8_0": 8, "q4_k": 12, "q6_k": 14}
 
 
@@ -707,6 +835,7 @@ def run_gemv_op(args, dist, rank, world, local):
 WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
              "gemv_q4_0": (run_gemv_ours, run_gemv_reference),
              "gemv_op": (run_gemv_op, None),
+             "gemm_q4k": (run_gemm_ours, run_gemm_reference),
              "attn": (run_attn_ours, None)}
 
 

@@ -156,14 +156,24 @@ B2_API int b2_quantize_act(int act_type, const float* x, int n_tok, int64_t k, v
  * Q8_K for Q4_K/Q6_K).  x fp32 [n_tok][k], y fp32 [n_tok][n_rows]. */
 B2_API int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stream);
 
+/* Device scratch b2_gemm needs for n_tok tokens (the quantized activations). */
+B2_API int b2_gemm_workspace_bytes(const b2_qmatrix* w, int n_tok, size_t* bytes);
+
 /* Prefill GEMM on the tensor cores (tcgen05, fp32 accumulation in TMEM),
  * the reference's matmul_quantized (Singularity/src/core/cortex_a5_engine.cpp:997-1027)
  * for any n_tok >= 1: y[t][r] = vec_dot(W row r, Q8_K(x[t])), super-blocks
  * added in order exactly as the CPU vec_dot adds them, so y is bit-identical
  * to the reference's per-row result.  Q4_K weights.  x fp32 [n_tok][k]
- * (16-byte aligned), y fp32 [n_tok][n_rows].  `status` (device int, may be
- * NULL) receives a nonzero code if a pipeline wait expired. */
-B2_API int b2_gemm(const b2_qmatrix* w, const float* x, int n_tok, float* y, int* status, void* stream);
+ * (16-byte aligned), y fp32 [n_tok][n_rows].  `workspace` (device, 16-byte
+ * aligned, b2_gemm_workspace_bytes) may be NULL: the call then allocates
+ * stream-ordered scratch.  `status` (device int, may be NULL) receives a
+ * nonzero code if a pipeline wait expired. */
+B2_API int b2_gemm(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* workspace,
+                   size_t workspace_bytes, int* status, void* stream);
+
+/* Same GEMM through host buffers (pinned for full copy bandwidth): uploads x,
+ * runs, reads y back, synchronous; fails if a pipeline wait expired. */
+B2_API int b2_gemm_host(const b2_qmatrix* w, const float* x_host, int n_tok, float* y_host);
 
 /* Same GEMV through host buffers: uploads x, runs, reads y back, synchronous.
  * The call a host engine makes per projection when it keeps activations on
