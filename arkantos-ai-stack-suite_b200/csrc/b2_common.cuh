@@ -56,14 +56,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls (each try_wait itself suspends
-// for a hardware-chosen interval), records the failure in *status and
-// returns false.  Every wait in these kernels is bounded so a lost transfer
-// ends the kernel with an error code instead of hanging the GPU.
-constexpr uint32_t kWaitLimit = 1u << 24;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: gives up after kMbarWaitNs of wall time (each try_wait itself
+// suspends for a hardware-chosen interval, so the bound is on the clock, not
+// on the number of polls), records the failure in *status and returns false.
+// Every wait in these kernels is bounded so a lost transfer ends the kernel
+// with an error code instead of hanging the GPU.
+constexpr uint64_t kMbarWaitNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0 && globaltimer_ns() - t0 > kMbarWaitNs) break;
   }
   if (status) atomicExch(status, code);
   return false;
@@ -77,11 +87,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
-}
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 // Waits until flags[0..n) all reach `target`, for at most kPeerWaitNs of
 // wall time; on expiry records `code` in *status and returns false (the

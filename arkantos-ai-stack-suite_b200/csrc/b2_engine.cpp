@@ -119,6 +119,7 @@ struct b2_context {
   // step buffers
   float *x = nullptr, *delta = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
   float *logits = nullptr, *part_o = nullptr, *part_ml = nullptr, *top = nullptr;
+  unsigned int* attn_cnt = nullptr;   // [kStepMax][n_kv] arrival counters of the fused attention combine
   // [ids kStepMax | top-1, margin 2*kStepMax | status] in one allocation: one
   // D2H copy returns a step's greedy result and the device-wait status
   int32_t* res = nullptr;
@@ -490,6 +491,8 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
       for (int n = 1; n <= T; ++n) img = std::max(img, gemv_act_image_bytes(q->m, n));
     if ((rc = dalloc(c, &c->act_img, img))) return rc;
   }
+  if ((rc = dalloc(c, &c->attn_cnt, (size_t)T * m->nkv_l))) return rc;
+  B2_CUDA_TRY(cudaMemset(c->attn_cnt, 0, (size_t)T * m->nkv_l * sizeof(unsigned int)));
   c->ids = c->res;
   c->top = reinterpret_cast<float*>(c->res + kStepMax);
   c->status = c->res + 3 * kStepMax;
@@ -540,40 +543,130 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     return B2_OK;
   };
   if ((rc = tap("embed", -1, c->x, (int64_t)n * d))) return rc;
+  // Fused form (no evaluation taps): each RMSNorm writes the next GEMV's
+  // quantized activation image, and the QKV GEMV's epilogue applies RoPE and
+  // stores K/V into the cache.  Same operations, fewer launches.
+  const bool fuse = !c->eval_cb && add_rmsnorm_q_supported(d, m->layers[0]->wqkv.m.type);
+  // Residual add + RMSNorm, then the GEMV over its output (fused or not).
+  auto norm_gemv = [&](const float* delta, const float* nw, const PeerIn* in, const DevQ& w, float* y, int64_t ys,
+                       int epi, const RopeKvEpi* rk) -> int {
+    GemvArgs a = {};
+    a.w = &w.m;
+    a.x = c->xn;
+    a.x_stride = d;
+    a.n_tok = n;
+    a.y = y;
+    a.y_stride = ys;
+    a.epilogue = epi;
+    a.status = c->status;
+    a.act_img = c->act_img;
+    a.rope = rk;
+    int r;
+    if (fuse) {
+      const ActImage im = gemv_act_image(w.m, n, c->act_img);
+      if ((r = launch_add_rmsnorm_q(c->x, delta, nw, nullptr, n, d, m->eps, im, s, in, c->status))) return r;
+      a.image_ready = true;
+    } else if ((r = launch_add_rmsnorm(c->x, delta, nw, c->xn, n, d, m->eps, s, in, c->status))) {
+      return r;
+    }
+    return launch_gemv(a, s);
+  };
   const int qkv_w = (m->nh_l + 2 * m->nkv_l) * hd;
   for (int l = 0; l < m->n_layer; ++l) {
     Layer& L = *m->layers[l];
-    if ((rc = launch_add_rmsnorm(c->x, l ? c->delta : nullptr, L.attn_norm, c->xn, n, d, m->eps, s,
-                                 tp && l ? &in_down : nullptr, c->status)))
-      return rc;
-    if ((rc = tap("attn_norm", l, c->xn, (int64_t)n * d))) return rc;
-    if ((rc = gemv(L.wqkv, c->xn, d, c->qkv, qkv_w, EPI_STORE))) return rc;
-    if ((rc = tap("qkv", l, c->qkv, (int64_t)n * qkv_w))) return rc;
-    if ((rc = launch_rope_kv(c->qkv, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->rope, c->q, c->kc[l], c->vc[l],
-                             c->st_d, c->n_seq, c->n_ctx, s)))
-      return rc;
-    if ((rc = tap("q_rope", l, c->q, (int64_t)n * m->nh_l * hd))) return rc;
+    if (fuse) {
+      RopeKvEpi rk;
+      rk.pos = c->pos_d;
+      rk.seq = c->seq_d;
+      rk.rope = c->rope;
+      rk.q_out = c->q;
+      rk.kc = c->kc[l];
+      rk.vc = c->vc[l];
+      rk.st = c->st_d;
+      rk.n_head = m->nh_l;
+      rk.n_kv = m->nkv_l;
+      rk.hd = hd;
+      rk.n_seq = c->n_seq;
+      rk.cap = c->n_ctx;
+      if ((rc = norm_gemv(l ? c->delta : nullptr, L.attn_norm, tp && l ? &in_down : nullptr, L.wqkv, nullptr, 0,
+                          EPI_ROPE_KV, &rk)))
+        return rc;
+    } else {
+      if ((rc = launch_add_rmsnorm(c->x, l ? c->delta : nullptr, L.attn_norm, c->xn, n, d, m->eps, s,
+                                   tp && l ? &in_down : nullptr, c->status)))
+        return rc;
+      if ((rc = tap("attn_norm", l, c->xn, (int64_t)n * d))) return rc;
+      if ((rc = gemv(L.wqkv, c->xn, d, c->qkv, qkv_w, EPI_STORE))) return rc;
+      if ((rc = tap("qkv", l, c->qkv, (int64_t)n * qkv_w))) return rc;
+      if ((rc = launch_rope_kv(c->qkv, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->rope, c->q, c->kc[l],
+                               c->vc[l], c->st_d, c->n_seq, c->n_ctx, s)))
+        return rc;
+      if ((rc = tap("q_rope", l, c->q, (int64_t)n * m->nh_l * hd))) return rc;
+    }
+    // Fused: the attention's last CTAs combine the chunks and quantize the O
+    // projection's input image.
+    const bool fuse_o = fuse && attn_fusable(m->nh_l, m->nkv_l, hd, L.wo.m.type);
+    const ActImage o_img = gemv_act_image(L.wo.m, n, c->act_img);
     if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->vc[l], c->st_d,
-                               c->n_seq, c->n_ctx, c->part_o, c->part_ml, c->att, s, c->status)))
+                               c->n_seq, c->n_ctx, c->part_o, c->part_ml, c->att, s, c->status,
+                               fuse ? c->attn_cnt : nullptr, fuse_o ? &o_img : nullptr)))
       return rc;
     if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
-    if ((rc = gemv(L.wo, c->att, (int64_t)m->nh_l * hd, c->delta, d, EPI_STORE, tp ? &out_o : nullptr))) return rc;
+    {
+      GemvArgs a = {};
+      a.w = &L.wo.m;
+      a.x = c->att;
+      a.x_stride = (int64_t)m->nh_l * hd;
+      a.n_tok = n;
+      a.y = c->delta;
+      a.y_stride = d;
+      a.epilogue = EPI_STORE;
+      a.status = c->status;
+      a.act_img = c->act_img;
+      a.peer = tp ? &out_o : nullptr;
+      a.image_ready = fuse_o;
+      if ((rc = launch_gemv(a, s))) return rc;
+    }
     if (!tp && (rc = tap("attn_proj", l, c->delta, (int64_t)n * d))) return rc;
-    if ((rc = launch_add_rmsnorm(c->x, c->delta, L.ffn_norm, c->xn, n, d, m->eps, s, tp ? &in_o : nullptr,
-                                 c->status)))
-      return rc;
-    if ((rc = tap("ffn_norm", l, c->xn, (int64_t)n * d))) return rc;
-    if ((rc = gemv(L.wgu, c->xn, d, c->h, m->ff_l, EPI_SWIGLU))) return rc;
+    if (fuse) {
+      if ((rc = norm_gemv(c->delta, L.ffn_norm, tp ? &in_o : nullptr, L.wgu, c->h, m->ff_l, EPI_SWIGLU, nullptr)))
+        return rc;
+    } else {
+      if ((rc = launch_add_rmsnorm(c->x, c->delta, L.ffn_norm, c->xn, n, d, m->eps, s, tp ? &in_o : nullptr,
+                                   c->status)))
+        return rc;
+      if ((rc = tap("ffn_norm", l, c->xn, (int64_t)n * d))) return rc;
+      if ((rc = gemv(L.wgu, c->xn, d, c->h, m->ff_l, EPI_SWIGLU))) return rc;
+    }
     if ((rc = tap("ffn_act", l, c->h, (int64_t)n * m->ff_l))) return rc;
     if ((rc = gemv(L.wdown, c->h, m->ff_l, c->delta, d, EPI_STORE, tp ? &out_down : nullptr))) return rc;
     if (!tp && (rc = tap("ffn_out", l, c->delta, (int64_t)n * d))) return rc;
   }
-  if ((rc = launch_add_rmsnorm(c->x, c->delta, m->out_norm, c->xn, n, d, m->eps, s, tp ? &in_down : nullptr,
-                               c->status)))
-    return rc;
-  if ((rc = tap("result_norm", -1, c->xn, (int64_t)n * d))) return rc;
-  if (!with_logits) return B2_OK;
-  if ((rc = gemv(m->head, c->xn, d, c->logits, m->v_l, EPI_STORE, tp ? &out_head : nullptr))) return rc;
+  if (fuse && with_logits) {
+    // the head GEMV reads the image; its rows of x are still completed in place
+    GemvArgs a = {};
+    a.w = &m->head.m;
+    a.n_tok = n;
+    a.y = c->logits;
+    a.y_stride = m->v_l;
+    a.epilogue = EPI_STORE;
+    a.status = c->status;
+    a.act_img = c->act_img;
+    a.peer = tp ? &out_head : nullptr;
+    a.image_ready = true;
+    const ActImage im = gemv_act_image(m->head.m, n, c->act_img);
+    if ((rc = launch_add_rmsnorm_q(c->x, c->delta, m->out_norm, c->xn, n, d, m->eps, im, s,
+                                   tp ? &in_down : nullptr, c->status)))
+      return rc;
+    if ((rc = launch_gemv(a, s))) return rc;
+  } else {
+    if ((rc = launch_add_rmsnorm(c->x, c->delta, m->out_norm, c->xn, n, d, m->eps, s, tp ? &in_down : nullptr,
+                                 c->status)))
+      return rc;
+    if ((rc = tap("result_norm", -1, c->xn, (int64_t)n * d))) return rc;
+    if (!with_logits) return B2_OK;
+    if ((rc = gemv(m->head, c->xn, d, c->logits, m->v_l, EPI_STORE, tp ? &out_head : nullptr))) return rc;
+  }
   GreedyFeed f;
   if (feed) {
     f.tok = c->tok_d;

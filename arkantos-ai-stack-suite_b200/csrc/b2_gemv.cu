@@ -5,26 +5,28 @@
 // and, for K-quants, ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K.
 //
 // Weights are in the tile layout (8-row tiles, S unit ranges per row, see
-// QMatrix).  One CTA per SM takes a contiguous run of tile groups; a group is
-// P = 8/S tiles whose S ranges are worked by the 8 consumer warps (warp w:
-// tile w/S, range w%S).
-//   * warp 8 is the producer: lane 0 streams each stage — for every tile of
-//     the group the next U unit slots of all its ranges, one contiguous
-//     cp.async.bulk (1-D TMA) per tile — into a ring of shared-memory stages
-//     completing on full[] mbarriers.  It starts before the grid dependency
-//     resolves, so weights stream while the previous kernel drains (PDL).
-//   * the activations are quantized once per launch by a small kernel
-//     (bit-exact with the reference's quantizers) into an image of the
-//     shared-memory layout; the producer copies that image into every CTA
-//     once the grid dependency resolves, and warps 0..7 then take the
-//     stages.  Integer dots are exact: for 1-2 tokens with dp4a (lane =
-//     tile row x unit residue mod 4), for 3-8 tokens with int8 mma.sync
-//     (m16n8k32; m16n8k16 for Q6_K's 16-weight groups; tokens are the M
-//     rows, the tile's 8 rows the N columns).  Each unit's integer sums are
-//     scaled in fp32 as the reference does, into four partial sums by unit
-//     residue mod 4; a range's sum is (a0 + a1) + (a2 + a3) and the S ranges
-//     of a row are added in order through shared memory — one order for
-//     every batch size (restated by the oracle's orc_tile_row_dot).
+// QMatrix).  One CTA per SM takes a contiguous run of items: tile pairs
+// (16 rows) for the mma kernels, groups of P = 8/S tiles for dp4a.
+//   * the last warp is the producer: lane 0 streams each stage — for every
+//     tile of the item the next U unit slots of all its ranges, one
+//     contiguous cp.async.bulk (1-D TMA) per tile — into a ring of
+//     shared-memory stages completing on full[] mbarriers.  It starts before
+//     the grid dependency resolves, so weights stream while the previous
+//     kernel drains (PDL).
+//   * the activations are quantized (bit-exact with the reference's
+//     quantizers) either by every CTA into shared memory (small inputs) or
+//     once per launch by a small kernel into an image of the shared-memory
+//     layout that the producer copies in after the grid dependency resolves.
+//   * integer dots are exact: for 1-2 tokens with dp4a (8 warps; warp = tile
+//     of the group x range, lane = tile row x unit residue mod 4); for 3-8
+//     tokens with int8 mma.sync m16n8k32 (m16n8k16 for Q6_K's 16-weight
+//     groups) with the tile pair's 16 weight rows as M and the tokens as N
+//     (16 warps in sets of S; a set works one tile pair, a warp one range of
+//     it for all four unit residues).  Each unit's integer sums are scaled in
+//     fp32 as the reference does, into four partial sums by unit residue mod
+//     4; a range's sum is (a0 + a1) + (a2 + a3) and the S ranges of a row are
+//     added in order through shared memory — one order for every batch size
+//     (restated by the oracle's orc_tile_row_dot).
 //   * epilogue: store, residual add, SwiGLU over interleaved gate/up rows,
 //     or the tensor-parallel exchange into every rank's gather buffer.
 // Every mbarrier wait is bounded; a warp whose wait expires records a status
@@ -36,12 +38,12 @@
 namespace b2 {
 namespace {
 
-// Consumer warps: 16 for the mma kernels (the two warps of a range split its
-// four unit residues into pairs), 8 for the dp4a kernels; plus one producer.
+// Consumer warps: 16 for the mma kernels, 8 for the dp4a kernels; plus one
+// producer.
 constexpr int kMaxNCW = 16;
 constexpr int ncw_for(int mode) { return mode == 0 ? 16 : 8; }
-constexpr int kMaxStages = 6;
-constexpr int kBarBytes = 128;           // full[kMaxStages], empty[kMaxStages], act, padded
+constexpr int kMaxStages = 16;
+constexpr int kBarBytes = 512;           // full[kMaxStages], empty[kMaxStages], act, padded
 constexpr int kMaxTok = 8;
 constexpr int kDp4aMaxTok = 2;           // dp4a up to this many tokens, mma.sync above
 constexpr uint32_t kM4 = 0x0F0F0F0Fu;
@@ -64,6 +66,7 @@ struct GemvP {
                           // the consumers quantize x into shared memory themselves
   int* status;
   PeerOut peer;
+  RopeKvEpi rope;
 };
 
 __device__ __forceinline__ void consumer_sync(int nthreads) {
@@ -77,17 +80,8 @@ __device__ __forceinline__ void tile_sync(int p, int nthreads) {
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
-// Activation image (global and in shared memory): codes [n_act_tok][kq] |
-// fp32 scale per (token, unit) | int16 block sums per (token, unit).  The
-// codes of token t start at t*kq.  For the dp4a kernels they are in natural
-// order; for the mma kernels each token's codes are stored in fragment order:
-//   Q8_K (256-value units, 64 words w): the 16 words thread q of a warp
-//     needs, idx = 2j + h <-> word 8j + 4h + q, sit in 16-byte chunks i = idx/4
-//     at physical chunk ((4i + q) + 4*(t & 1)) & 15 of the unit's 256 bytes;
-//   Q8_0 (32-value blocks): words q and q+4 of block u are one 8-byte slot,
-//     slot ((u & 3)*4 + q + 4*(t & 3)) & 15 of the 128 bytes of blocks u & ~3.
-// The rotations by token spread the 8 tokens of a fragment load over all
-// banks.
+// Activation image (global and in shared memory): the ActImage carve-up,
+// stored by store_q8k_unit / store_q8_0_block (b2_quant.cuh).
 __device__ __forceinline__ void act_frag16(const uint8_t* trow, int u, int g, int q, uint32_t (&a)[16]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -110,32 +104,27 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 }
 __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
-// D[16x8] = A[16xK] (tokens x k, int8; rows 8..15 zero) * B[Kx8] (k x weight rows).
-__device__ __forceinline__ void mma_k32_s8u8(int& c0, int& c1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  int4 d;   // d.z, d.w: rows 8..15 of D, the zero token rows
+// Rows-as-M forms: D[16x8] = A[16xK] (weight rows of a tile pair) * B[Kx8]
+// (k x tokens).  d[0..3] = (row g, token 2q), (row g, 2q+1), (row g+8, 2q),
+// (row g+8, 2q+1) for lane = 4g + q.
+__device__ __forceinline__ void mma16_k32_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
-      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
-  c0 = d.x;
-  c1 = d.y;
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
-__device__ __forceinline__ void mma_k32_s8s8(int& c0, int& c1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  int4 d;   // d.z, d.w: rows 8..15 of D, the zero token rows
+__device__ __forceinline__ void mma16_k32_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
-      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
-  c0 = d.x;
-  c1 = d.y;
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
-__device__ __forceinline__ void mma_k16_s8u8(int& c0, int& c1, uint32_t a0, uint32_t b0) {
-  int4 d;   // d.z, d.w: rows 8..15 of D, the zero token rows
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
-               : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
-               : "r"(a0), "r"(0), "r"(b0), "r"(0));
-  c0 = d.x;
-  c1 = d.y;
+__device__ __forceinline__ void mma16_k16_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
 
 __device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)((w >> (8 * b)) & 0xFFu); }
@@ -157,16 +146,13 @@ __device__ __forceinline__ void q4k_scales(uint32_t s0, uint32_t s1, uint32_t s2
 // Q8_K sums; Q6_K: Q8_K's per 16).  Token rows n_tok..n_act_tok-1 are zero.
 // Threads tid of nthreads (a multiple of 32) share the work; img is global
 // memory (the quantize kernel) or the GEMV's shared memory.
-template <bool MMA>
-__device__ void quantize_image(const float* __restrict__ x, int64_t x_stride, int n_tok, int n_act_tok, int type,
-                               int nu, int kq, uint32_t off_dx, uint32_t off_bs, uint8_t* img, int64_t tid,
-                               int64_t nthreads) {
-  float* dxs = reinterpret_cast<float*>(img + off_dx);
-  int16_t* bss = reinterpret_cast<int16_t*>(img + off_bs);
-  if (type == B2_Q4_0 || type == B2_Q8_0) {
+__device__ void quantize_image(const float* __restrict__ x, int64_t x_stride, int n_tok, const ActImage& img,
+                               int64_t tid, int64_t nthreads) {
+  const int nu = img.nu;
+  if (img.type == B2_Q4_0 || img.type == B2_Q8_0) {
     // One 32-value block per thread: eight float4 loads in flight, then the
     // reference quantizer on registers.
-    for (int64_t i = tid; i < (int64_t)n_act_tok * nu; i += nthreads) {
+    for (int64_t i = tid; i < (int64_t)img.n_act_tok * nu; i += nthreads) {
       const int t = (int)(i / nu), b = (int)(i - (int64_t)t * nu);
       uint32_t w[8];
       int sum = 0;
@@ -200,23 +186,12 @@ __device__ void quantize_image(const float* __restrict__ x, int64_t x_stride, in
         }
         dq = h2f(f2h_rn(d));
       }
-      uint8_t* trow = img + (int64_t)t * kq;
-      if constexpr (MMA) {
-        uint8_t* base = trow + (b >> 2) * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint2*>(base + ((((b & 3) * 4 + q) + 4 * (t & 3)) & 15) * 8) = make_uint2(w[q], w[q + 4]);
-      } else {
-        *reinterpret_cast<uint4*>(trow + b * 32) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(trow + b * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
-      }
-      dxs[t * nu + b] = dq;
-      if (type == B2_Q4_0) bss[t * nu + b] = (int16_t)sum;
+      store_q8_0_block(img, t, b, w, dq, sum);
     }
   } else {
     // One 256-value super-block per warp, 8 values per lane.
     const int lane = threadIdx.x & 31;
-    for (int64_t i = tid >> 5; i < (int64_t)n_act_tok * nu; i += nthreads >> 5) {
+    for (int64_t i = tid >> 5; i < (int64_t)img.n_act_tok * nu; i += nthreads >> 5) {
       const int t = (int)(i / nu), b = (int)(i - (int64_t)t * nu);
       int8_t q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       int bs = 0;
@@ -227,150 +202,151 @@ __device__ void quantize_image(const float* __restrict__ x, int64_t x_stride, in
         const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
         d = quant_q8_k_lane(v, q, &bs);
       }
-      const uint32_t w0 = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) |
-                          ((uint32_t)(uint8_t)q[2] << 16) | ((uint32_t)(uint8_t)q[3] << 24);
-      const uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) |
-                          ((uint32_t)(uint8_t)q[6] << 16) | ((uint32_t)(uint8_t)q[7] << 24);
-      uint8_t* unit = img + (int64_t)t * kq + (int64_t)b * 256;
-      if constexpr (MMA) {
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int wi = 2 * lane + h2;   // word 8j + 4h + q of the unit
-          const int j = wi >> 3, h = (wi >> 2) & 1, qq = wi & 3;
-          const int idx = 2 * j + h;
-          *reinterpret_cast<uint32_t*>(unit + ((((idx >> 2) * 4 + qq) + 4 * (t & 1)) & 15) * 16 + (idx & 3) * 4) =
-              h2 ? w1 : w0;
-        }
-      } else {
-        *reinterpret_cast<uint2*>(unit + lane * 8) = make_uint2(w0, w1);
-      }
-      if (lane == 0) dxs[t * nu + b] = d;
-      if (type == B2_Q6_K) {
-        if ((lane & 1) == 0) bss[(t * nu + b) * 16 + lane / 2] = (int16_t)bs;
-      } else {
-        const int b32 = bs + __shfl_xor_sync(0xffffffffu, bs, 2);
-        if ((lane & 3) == 0) bss[(t * nu + b) * 8 + lane / 4] = (int16_t)b32;
-      }
+      store_q8k_unit(img, t, b, q, d, bs);
     }
   }
 }
 
-template <bool MMA>
-__global__ void quantize_image_kernel(const float* __restrict__ x, int64_t x_stride, int n_tok, int n_act_tok,
-                                      int type, int nu, int kq, uint32_t off_dx, uint32_t off_bs, uint8_t* img) {
+__global__ void quantize_image_kernel(const float* __restrict__ x, int64_t x_stride, int n_tok, const ActImage img) {
   pdl_wait();
   pdl_launch_dependents();
-  quantize_image<MMA>(x, x_stride, n_tok, n_act_tok, type, nu, kq, off_dx, off_bs, img,
-                      (int64_t)blockIdx.x * blockDim.x + threadIdx.x, (int64_t)gridDim.x * blockDim.x);
+  quantize_image(x, x_stride, n_tok, img, (int64_t)blockIdx.x * blockDim.x + threadIdx.x,
+                 (int64_t)gridDim.x * blockDim.x);
 }
 
-// ---- mma path: one unit for token g (= lane/4), tile rows 2q, 2q+1 (q = lane%4) ------------
+// ---- mma path: one unit of a 16-row tile pair for tokens 0..7 ------------------------------
+// sa, sb: the unit's slot in tile a (rows 0..7 -> D rows 0..7) and tile b
+// (D rows 8..15).  Lane 4g + q holds outputs i = 2*tb + e: tile row g of
+// tile tb (0: a, 1: b) for token 2q + e.  Each output's fp32 update is the
+// reference's per-unit sequence.
 template <int WT>
-__device__ __forceinline__ void mma_unit(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, int g, int q,
-                                         float& acc0, float& acc1) {
-  const uint8_t* trow = act + g * p.kq;
+__device__ __forceinline__ void mma2_unit(const GemvP& p, const uint8_t* sa, const uint8_t* sb, const uint8_t* act,
+                                          int u, int g, int q, float (&acc)[4]) {
   const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
   const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
-  const float dx = dxs[g * p.nu + u];
+  const float dx0 = dxs[(2 * q) * p.nu + u], dx1 = dxs[(2 * q + 1) * p.nu + u];
+  const uint8_t* trow = act + g * p.kq;   // B column g = token g
   if constexpr (WT == B2_Q4_0) {
-    const uint32_t w = lds32(sl + 16 * g + 4 * q);
-    const uint2 a = act_frag2(trow, u, g, q);
-    int c0, c1;
-    mma_k32_s8u8(c0, c1, a.x, a.y, w & kM4, (w >> 4) & kM4);
-    const int corr = 8 * (int)bss[g * p.nu + u];
-    const uint32_t dw = lds32(sl + 128 + 4 * q);
-    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw & 0xFFFFu)), dx), (float)(c0 - corr)));
-    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw >> 16)), dx), (float)(c1 - corr)));
+    const uint32_t wa = lds32(sa + 16 * g + 4 * q), wb = lds32(sb + 16 * g + 4 * q);
+    const uint2 b = act_frag2(trow, u, g, q);
+    int c[4];
+    mma16_k32_u8s8(c, wa & kM4, wb & kM4, (wa >> 4) & kM4, (wb >> 4) & kM4, b.x, b.y);
+    const int corr0 = 8 * (int)bss[(2 * q) * p.nu + u], corr1 = 8 * (int)bss[(2 * q + 1) * p.nu + u];
+    const float da = h2f(*reinterpret_cast<const uint16_t*>(sa + 128 + 2 * g));
+    const float db = h2f(*reinterpret_cast<const uint16_t*>(sb + 128 + 2 * g));
+    acc[0] = __fadd_rn(acc[0], __fmul_rn(__fmul_rn(da, dx0), (float)(c[0] - corr0)));
+    acc[1] = __fadd_rn(acc[1], __fmul_rn(__fmul_rn(da, dx1), (float)(c[1] - corr1)));
+    acc[2] = __fadd_rn(acc[2], __fmul_rn(__fmul_rn(db, dx0), (float)(c[2] - corr0)));
+    acc[3] = __fadd_rn(acc[3], __fmul_rn(__fmul_rn(db, dx1), (float)(c[3] - corr1)));
   } else if constexpr (WT == B2_Q8_0) {
-    const uint2 a = act_frag2(trow, u, g, q);
-    int c0, c1;
-    mma_k32_s8s8(c0, c1, a.x, a.y, lds32(sl + 16 * g + 4 * q), lds32(sl + 128 + 16 * g + 4 * q));
-    const uint32_t dw = lds32(sl + 256 + 4 * q);
-    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw & 0xFFFFu)), dx), (float)c0));
-    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw >> 16)), dx), (float)c1));
+    const uint2 b = act_frag2(trow, u, g, q);
+    int c[4];
+    mma16_k32_s8s8(c, lds32(sa + 16 * g + 4 * q), lds32(sb + 16 * g + 4 * q), lds32(sa + 128 + 16 * g + 4 * q),
+                   lds32(sb + 128 + 16 * g + 4 * q), b.x, b.y);
+    const float da = h2f(*reinterpret_cast<const uint16_t*>(sa + 256 + 2 * g));
+    const float db = h2f(*reinterpret_cast<const uint16_t*>(sb + 256 + 2 * g));
+    acc[0] = __fadd_rn(acc[0], __fmul_rn(__fmul_rn(da, dx0), (float)c[0]));
+    acc[1] = __fadd_rn(acc[1], __fmul_rn(__fmul_rn(da, dx1), (float)c[1]));
+    acc[2] = __fadd_rn(acc[2], __fmul_rn(__fmul_rn(db, dx0), (float)c[2]));
+    acc[3] = __fadd_rn(acc[3], __fmul_rn(__fmul_rn(db, dx1), (float)c[3]));
   } else if constexpr (WT == B2_Q4_K) {
-    const uint8_t* m0 = sl + 1024 + 32 * q;   // d|dmin|scales of rows 2q and 2q+1
-    uint32_t sl0, ml0, sh0, mh0, sl1, ml1, sh1, mh1;
-    q4k_scales(lds32(m0 + 4), lds32(m0 + 8), lds32(m0 + 12), sl0, ml0, sh0, mh0);
-    q4k_scales(lds32(m0 + 20), lds32(m0 + 24), lds32(m0 + 28), sl1, ml1, sh1, mh1);
-    const uint8_t* qrow = sl + 128 * g;
+    const uint4 ma = lds128(sa + 1024 + 16 * g), mb = lds128(sb + 1024 + 16 * g);
+    uint32_t sla, mla, sha, mha, slb, mlb, shb, mhb;
+    q4k_scales(ma.y, ma.z, ma.w, sla, mla, sha, mha);
+    q4k_scales(mb.y, mb.z, mb.w, slb, mlb, shb, mhb);
+    const uint8_t* qa = sa + 128 * g;
+    const uint8_t* qb = sb + 128 * g;
     uint32_t af[16];
     act_frag16(trow, u, g, q, af);
-    int is0 = 0, is1 = 0;
+    int is[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int jc = 0; jc < 4; ++jc) {
-      const uint32_t w0 = lds32(qrow + 16 * ((2 * jc + g) & 7) + 4 * q);
-      const uint32_t w1 = lds32(qrow + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
+      const uint32_t wa0 = lds32(qa + 16 * ((2 * jc + g) & 7) + 4 * q);
+      const uint32_t wa1 = lds32(qa + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
+      const uint32_t wb0 = lds32(qb + 16 * ((2 * jc + g) & 7) + 4 * q);
+      const uint32_t wb1 = lds32(qb + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int j = 2 * jc + h;
-        const uint32_t b0 = h ? (w0 >> 4) & kM4 : w0 & kM4;
-        const uint32_t b1 = h ? (w1 >> 4) & kM4 : w1 & kM4;
-        int c0, c1;
-        mma_k32_s8u8(c0, c1, af[2 * j], af[2 * j + 1], b0, b1);
-        const int s0 = j < 4 ? ubyte(sl0, j) : ubyte(sh0, j - 4);
-        const int s1 = j < 4 ? ubyte(sl1, j) : ubyte(sh1, j - 4);
-        is0 += s0 * c0;
-        is1 += s1 * c1;
+        int c[4];
+        if (h == 0)
+          mma16_k32_u8s8(c, wa0 & kM4, wb0 & kM4, wa1 & kM4, wb1 & kM4, af[2 * j], af[2 * j + 1]);
+        else
+          mma16_k32_u8s8(c, (wa0 >> 4) & kM4, (wb0 >> 4) & kM4, (wa1 >> 4) & kM4, (wb1 >> 4) & kM4, af[2 * j],
+                         af[2 * j + 1]);
+        const int sa_j = j < 4 ? ubyte(sla, j) : ubyte(sha, j - 4);
+        const int sb_j = j < 4 ? ubyte(slb, j) : ubyte(shb, j - 4);
+        is[0] += sa_j * c[0];
+        is[1] += sa_j * c[1];
+        is[2] += sb_j * c[2];
+        is[3] += sb_j * c[3];
       }
     }
-    const uint4 b32 = lds128(reinterpret_cast<const uint8_t*>(bss + (g * p.nu + u) * 8));
-    int ms0 = __dp2a_lo((int)b32.x, (int)ml0, 0);
-    ms0 = __dp2a_hi((int)b32.y, (int)ml0, ms0);
-    ms0 = __dp2a_lo((int)b32.z, (int)mh0, ms0);
-    ms0 = __dp2a_hi((int)b32.w, (int)mh0, ms0);
-    int ms1 = __dp2a_lo((int)b32.x, (int)ml1, 0);
-    ms1 = __dp2a_hi((int)b32.y, (int)ml1, ms1);
-    ms1 = __dp2a_lo((int)b32.z, (int)mh1, ms1);
-    ms1 = __dp2a_hi((int)b32.w, (int)mh1, ms1);
-    const uint32_t dd0 = lds32(m0), dd1 = lds32(m0 + 16);
-    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd0 & 0xFFFFu)), dx), (float)is0));
-    acc0 = __fsub_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd0 >> 16)), dx), (float)ms0));
-    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd1 & 0xFFFFu)), dx), (float)is1));
-    acc1 = __fsub_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dd1 >> 16)), dx), (float)ms1));
-  } else {  // Q6_K
-    const uint8_t* qlr = sl + 128 * g;
-    const uint8_t* qhr = sl + 1024 + 64 * g;
-    const uint8_t* scp = sl + 1536 + 32 * q;   // scales of rows 2q and 2q+1
-    const int16_t* bs = bss + (g * p.nu + u) * 16;
+    const uint4 b0 = lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q) * p.nu + u) * 8));
+    const uint4 b1 = lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q + 1) * p.nu + u) * 8));
+    auto msum = [](const uint4& bq, uint32_t ml, uint32_t mh) {
+      int m = __dp2a_lo((int)bq.x, (int)ml, 0);
+      m = __dp2a_hi((int)bq.y, (int)ml, m);
+      m = __dp2a_lo((int)bq.z, (int)mh, m);
+      return __dp2a_hi((int)bq.w, (int)mh, m);
+    };
+    const int ms[4] = {msum(b0, mla, mha), msum(b1, mla, mha), msum(b0, mlb, mhb), msum(b1, mlb, mhb)};
+    const float dd[2] = {h2f((uint16_t)(ma.x & 0xFFFFu)), h2f((uint16_t)(mb.x & 0xFFFFu))};
+    const float dm[2] = {h2f((uint16_t)(ma.x >> 16)), h2f((uint16_t)(mb.x >> 16))};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float dx = (i & 1) ? dx1 : dx0;
+      acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dd[i >> 1], dx), (float)is[i]));
+      acc[i] = __fsub_rn(acc[i], __fmul_rn(__fmul_rn(dm[i >> 1], dx), (float)ms[i]));
+    }
+  } else {  // Q6_K: 16 groups of 16 weights, m16n8k16
+    const uint8_t* qla = sa + 128 * g;
+    const uint8_t* qlb = sb + 128 * g;
+    const uint8_t* qha = sa + 1024 + 64 * g;
+    const uint8_t* qhb = sb + 1024 + 64 * g;
+    const uint4 sca = lds128(sa + 1536 + 16 * g), scb = lds128(sb + 1536 + 16 * g);
+    const uint32_t swa[4] = {sca.x, sca.y, sca.z, sca.w}, swb[4] = {scb.x, scb.y, scb.z, scb.w};
+    const int16_t* bs0 = bss + ((2 * q) * p.nu + u) * 16;
+    const int16_t* bs1 = bss + ((2 * q + 1) * p.nu + u) * 16;
     uint32_t af[16];
     act_frag16(trow, u, g, q, af);
-    int is0 = 0, is1 = 0;
+    int is[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      const uint32_t qh0 = lds32(qhr + 16 * ((2 * hh + g) & 3) + 4 * q);
-      const uint32_t qh1 = lds32(qhr + 16 * ((2 * hh + 1 + g) & 3) + 4 * q);
-      const uint32_t sa0 = lds32(scp + 8 * hh), sb0 = lds32(scp + 8 * hh + 4);
-      const uint32_t sa1 = lds32(scp + 16 + 8 * hh), sb1 = lds32(scp + 16 + 8 * hh + 4);
 #pragma unroll
-      for (int a1 = 0; a1 < 2; ++a1) {
-        const uint32_t ql0 = lds32(qlr + 16 * ((4 * hh + 2 * a1 + g) & 7) + 4 * q);
-        const uint32_t ql1 = lds32(qlr + 16 * ((4 * hh + 2 * a1 + 1 + g) & 7) + 4 * q);
+      for (int hf = 0; hf < 2; ++hf) {
+        // qh word of l = 16*hf + 4q.. of half hh; ql words of quartiles a = 0/2 (lo/hi nibble of
+        // chunk 4hh + hf) and a = 1/3 (chunk 4hh + 2 + hf)
+        const uint32_t ha = lds32(qha + 16 * ((2 * hh + hf + g) & 3) + 4 * q);
+        const uint32_t hb = lds32(qhb + 16 * ((2 * hh + hf + g) & 3) + 4 * q);
 #pragma unroll
-        for (int nh = 0; nh < 2; ++nh) {
-          const int a = a1 + 2 * nh;   // quartile of the half
+        for (int a1 = 0; a1 < 2; ++a1) {
+          const uint32_t la = lds32(qla + 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q);
+          const uint32_t lb = lds32(qlb + 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q);
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            const uint32_t ql = hf ? ql1 : ql0;
-            const uint32_t qh = hf ? qh1 : qh0;
-            const uint32_t lo = nh ? (ql >> 4) & kM4 : ql & kM4;
-            const uint32_t b0 = lo | (((qh >> (2 * a)) & 0x03030303u) << 4);
-            const int i = hh * 8 + a * 2 + hf;   // 16-weight group of the super-block
-            int c0, c1;
-            mma_k16_s8u8(c0, c1, af[i], b0);
-            const int b = 32 * (int)bs[i];
-            const int gi = a * 2 + hf;           // group within the half
-            const int s0 = gi < 4 ? sbyte(sa0, gi) : sbyte(sb0, gi - 4);
-            const int s1 = gi < 4 ? sbyte(sa1, gi) : sbyte(sb1, gi - 4);
-            is0 += s0 * (c0 - b);
-            is1 += s1 * (c1 - b);
+          for (int nh = 0; nh < 2; ++nh) {
+            const int a = a1 + 2 * nh;          // quartile of the half
+            const int i = hh * 8 + a * 2 + hf;  // 16-weight group of the super-block
+            const uint32_t va = (nh ? (la >> 4) & kM4 : la & kM4) | (((ha >> (2 * a)) & 0x03030303u) << 4);
+            const uint32_t vb = (nh ? (lb >> 4) & kM4 : lb & kM4) | (((hb >> (2 * a)) & 0x03030303u) << 4);
+            int c[4];
+            mma16_k16_u8s8(c, va, vb, af[i]);
+            const int o0 = 32 * (int)bs0[i], o1 = 32 * (int)bs1[i];
+            const int s_a = sbyte(swa[i >> 2], i & 3), s_b = sbyte(swb[i >> 2], i & 3);
+            is[0] += s_a * (c[0] - o0);
+            is[1] += s_a * (c[1] - o1);
+            is[2] += s_b * (c[2] - o0);
+            is[3] += s_b * (c[3] - o1);
           }
         }
       }
     }
-    const uint32_t dw = lds32(sl + 1664 + 4 * q);
-    acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw & 0xFFFFu)), dx), (float)is0));
-    acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(h2f((uint16_t)(dw >> 16)), dx), (float)is1));
+    const float da = h2f(*reinterpret_cast<const uint16_t*>(sa + 1664 + 2 * g));
+    const float db = h2f(*reinterpret_cast<const uint16_t*>(sb + 1664 + 2 * g));
+    acc[0] = __fadd_rn(acc[0], __fmul_rn(__fmul_rn(da, dx0), (float)is[0]));
+    acc[1] = __fadd_rn(acc[1], __fmul_rn(__fmul_rn(da, dx1), (float)is[1]));
+    acc[2] = __fadd_rn(acc[2], __fmul_rn(__fmul_rn(db, dx0), (float)is[2]));
+    acc[3] = __fadd_rn(acc[3], __fmul_rn(__fmul_rn(db, dx1), (float)is[3]));
   }
 }
 
@@ -548,58 +524,120 @@ __device__ __forceinline__ void signal_peers(const GemvP& p) {
   }
 }
 
-// Finishes a tile: red[(r*WR + h)*64 + e] holds the partial of range r (half
-// h of its residues when WR = 2) for element e = token*8 + row; one warp adds
-// them — range sums (A + B), then the ranges in order — and writes.
-template <int WR>
-__device__ __forceinline__ float tile_total(const float* red, int S, int e) {
-  float v = WR == 2 ? __fadd_rn(red[e], red[64 + e]) : red[e];
-  for (int r = 1; r < S; ++r)
-    v = __fadd_rn(v, WR == 2 ? __fadd_rn(red[r * 128 + e], red[r * 128 + 64 + e]) : red[r * 64 + e]);
+// Sum of the S range partials of output e, ranges added in order.  red
+// holds S blocks of `stride` floats (block r: range r).
+__device__ __forceinline__ float range_total(const float* red, int S, int stride, int e) {
+  float v = red[e];
+  for (int r = 1; r < S; ++r) v = __fadd_rn(v, red[r * stride + e]);
   return v;
 }
 
-template <int WR>
-__device__ __forceinline__ void finish_tile(const GemvP& p, const float* red, int64_t tile, int lane) {
+// Writes the outputs of `nt` consecutive 8-row tiles starting at tile t0 from
+// red (S blocks of nt*64 floats, element e = token*(8*nt) + tile_row), one
+// warp: store / residual add / peer store, or SwiGLU over (gate, up) row
+// pairs of a tile.
+// The fused QKV epilogue for one (token, row pair): see RopeKvEpi.
+__device__ __forceinline__ void rope_kv_store(const RopeKvEpi& e, int t, int64_t row, float x0, float x1) {
+  const int s = e.seq[t], ps = e.pos[t];
+  const int h = (int)(row / e.hd), pr = (int)(row - (int64_t)h * e.hd) / 2;
+  if (s < 0 || s >= e.n_seq || ps < 0 || ps >= e.cap) {   // outside the cache: zero q, store nothing
+    if (h < e.n_head) {
+      float* qo = e.q_out + (int64_t)t * e.n_head * e.hd + row;
+      qo[0] = 0.0f;
+      qo[1] = 0.0f;
+    }
+    return;
+  }
+  const int64_t slot = kv_slot(e.st ? e.st[s] : KvSeqState{0, 0}, ps, e.cap);
+  if (h < e.n_head + e.n_kv) {
+    const float c = e.rope[(int64_t)ps * e.hd + 2 * pr], sn = e.rope[(int64_t)ps * e.hd + 2 * pr + 1];
+    const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    if (h < e.n_head) {
+      float* qo = e.q_out + (int64_t)t * e.n_head * e.hd + row;
+      qo[0] = y0;
+      qo[1] = y1;
+    } else {
+      uint16_t* dst = e.kc + (((int64_t)s * e.n_kv + (h - e.n_head)) * e.cap + slot) * e.hd + 2 * pr;
+      dst[0] = f2h_rn(y0);
+      dst[1] = f2h_rn(y1);
+    }
+  } else {
+    uint16_t* dst = e.vc + (((int64_t)s * e.n_kv + (h - e.n_head - e.n_kv)) * e.cap + slot) * e.hd + 2 * pr;
+    dst[0] = f2h_rn(x0);
+    dst[1] = f2h_rn(x1);
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void finish_tiles(const GemvP& p, const float* red, int64_t t0, int lane) {
+  constexpr int R = 8 * NT;   // rows per item
+  if (p.epilogue == EPI_ROPE_KV) {
+    // R/2 row pairs x 8 tokens
+#pragma unroll
+    for (int k = 0; k < (R / 2 * 8 + 31) / 32; ++k) {
+      const int e = lane + 32 * k;
+      if (e >= R / 2 * 8) break;
+      const int t = e / (R / 2), f = e % (R / 2);
+      const int64_t row = t0 * 8 + 2 * f;
+      if (t < p.n_tok && row < p.n_rows)
+        rope_kv_store(p.rope, t, row, range_total(red, p.S, R * 8, t * R + 2 * f),
+                      range_total(red, p.S, R * 8, t * R + 2 * f + 1));
+    }
+    return;
+  }
   if (p.epilogue == EPI_SWIGLU) {
-    // lane = token*4 + pair; tile rows (2*pair, 2*pair+1) are (gate, up) of one feature
-    const int t = lane >> 2, pr = lane & 3;
-    const int64_t row = tile * 8 + 2 * pr;
-    if (t < p.n_tok && row < p.n_rows) {
-      const float gs = tile_total<WR>(red, p.S, t * 8 + 2 * pr);
-      const float us = tile_total<WR>(red, p.S, t * 8 + 2 * pr + 1);
-      p.y[t * p.y_stride + row / 2] = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, b2_expf(-gs))), us);
+    // R/2 features x 8 tokens: feature f = rows (2f, 2f+1)
+#pragma unroll
+    for (int k = 0; k < (R / 2 * 8 + 31) / 32; ++k) {
+      const int e = lane + 32 * k;
+      if (e >= R / 2 * 8) break;
+      const int t = e / (R / 2), f = e % (R / 2);
+      const int64_t row = t0 * 8 + 2 * f;
+      if (t < p.n_tok && row < p.n_rows) {
+        const float gs = range_total(red, p.S, R * 8, t * R + 2 * f);
+        const float us = range_total(red, p.S, R * 8, t * R + 2 * f + 1);
+        p.y[t * p.y_stride + row / 2] = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, b2_expf(-gs))), us);
+      }
     }
     return;
   }
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int e = lane + 32 * hh;
-    const int t = e >> 3, rr = e & 7;
-    const int64_t row = tile * 8 + rr;
-    if (t < p.n_tok && row < p.n_rows) store_y(p, t, row, tile_total<WR>(red, p.S, e));
+  for (int k = 0; k < R * 8 / 32; ++k) {
+    const int e = lane + 32 * k;
+    const int t = e / R, rr = e % R;
+    const int64_t row = t0 * 8 + rr;
+    if (t < p.n_tok && row < p.n_rows) store_y(p, t, row, range_total(red, p.S, R * 8, e));
   }
 }
 
-template <int WT, int MODE>   // MODE 0: mma.sync; 1, 2: dp4a over that many tokens
+// MODE 0 (3..8 tokens, int8 mma.sync, weight rows as the M dimension): items
+// are tile pairs (16 rows).  The 16 consumer warps form NSET = 16/S sets of S
+// warps; set j works items j, j + NSET, ... of the CTA's run, warp r of a set
+// one unit range of the pair for all four residues.  A stage holds one item's
+// next U units of all ranges, so the sets consume the ring concurrently.
+// MODES 1, 2 (dp4a over 1-2 tokens): items are P = 8/S tiles; all 8 consumer
+// warps (tile w/S, range w%S) work every stage.
+template <int WT, int MODE>
 __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const GemvP p) {
   constexpr int NW = ncw_for(MODE);        // consumer warps
-  constexpr int WR = MODE == 0 ? 2 : 1;    // warps per range
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   uint64_t* act_bar = empty + kMaxStages;
   uint8_t* ring = smem + kBarBytes;
   uint8_t* act = ring + (size_t)p.n_stages * p.stage_bytes;
-  __shared__ float red[2][NW][64];   // [group parity][warp = (slot*S + range)*WR + half][token*8 + row]
+  // mma: [iteration parity][set][range][token*16 + pair row]; dp4a: [group parity][tile slot][range][token*8 + row]
+  __shared__ float red[2][kMaxNCW * 128];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ns = p.n_stages;
-  const int S = p.S, P = 8 / S;      // tile slots: P tiles of S ranges of WR warps
+  const int S = p.S;
+  const int P = MODE == 0 ? 2 : 8 / S;   // tiles per item
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NW);
+      mbar_init(&empty[s], MODE == 0 ? S : NW);
     }
     mbar_init(act_bar, 1);
     fence_mbar_init();
@@ -607,46 +645,61 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
   __syncthreads();
   pdl_launch_dependents();
 
-  // Tile groups of this CTA (contiguous, balanced) and the stage sequence.
-  const int64_t n_groups = (p.n_tiles + P - 1) / P;
-  const int64_t g0 = n_groups * blockIdx.x / gridDim.x, g1 = n_groups * (blockIdx.x + 1) / gridDim.x;
-  const int n_ch = (p.L + p.U - 1) / p.U;   // stages per group
-  const int64_t total = (g1 - g0) * n_ch;
+  // Items of this CTA (contiguous, balanced) and the stage sequence.  The
+  // consumer sets (MODE 0: NSET sets; dp4a: one) each own a ring of nss =
+  // ns/NSET consecutive slots and take their stages in order, so a set never
+  // waits on a slot whose previous use (by the same set) is still in flight.
+  // Set j works items j, j + NSET, ...; its local stage l is chunk l % n_ch of
+  // its item l / n_ch and lives in slot j*nss + l % nss.
+  const int64_t n_items = (p.n_tiles + P - 1) / P;
+  const int64_t g0 = n_items * blockIdx.x / gridDim.x, g1 = n_items * (blockIdx.x + 1) / gridDim.x;
+  const int n_ch = (p.L + p.U - 1) / p.U;   // stages per item
+  const int nset = MODE == 0 ? min(NW / S, 8) : 1;
+  const int nss = ns / nset;
   const uint32_t piece = (uint32_t)p.U * S * p.slot_bytes;   // one tile's part of a stage
 
   if (warp == NW) {
     // ---------------- producer ----------------
-    // The first ns stages need no free slot and go out at once; then, once the
-    // previous kernel (the activation quantizer) has finished, the image.
+    // Stages go out round-robin over the sets by local stage; the first nss
+    // of every set need no free slot.  Once those are out and the previous
+    // kernel (the activation quantizer) has finished, the image.
     if (lane == 0) {
-      auto issue = [&](int64_t st) {
-        const int s = (int)(st % ns);
-        const int64_t grp = g0 + st / n_ch;
-        const int ch = (int)(st % n_ch);
-        const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
-        const uint32_t bytes = (uint32_t)ni * S * p.slot_bytes;
-        uint32_t tx = 0;
-        for (int pp = 0; pp < P; ++pp)
-          if (grp * P + pp < p.n_tiles) tx += bytes;
-        mbar_arrive_expect_tx(&full[s], tx);
-        uint8_t* sp = ring + (size_t)s * p.stage_bytes;
-        for (int pp = 0; pp < P; ++pp) {
-          const int64_t tile = grp * P + pp;
-          if (tile < p.n_tiles)
-            bulk_g2s(sp + pp * piece, p.w + tile * p.tile_bytes + (int64_t)i0 * S * p.slot_bytes, bytes, &full[s]);
+      const int64_t items_here = g1 - g0;
+      const int64_t max_local = ((items_here + nset - 1) / nset) * n_ch;
+      bool act_sent = p.act_img == nullptr;
+      for (int64_t l = 0; l < max_local; ++l) {
+        if (l == nss && !act_sent) {
+          pdl_wait();
+          mbar_arrive_expect_tx(act_bar, p.act_bytes);
+          bulk_g2s(act, p.act_img, p.act_bytes, act_bar);
+          act_sent = true;
         }
-      };
-      const int64_t first = total < ns ? total : ns;
-      for (int64_t st = 0; st < first; ++st) issue(st);
-      if (p.act_img) {
+        for (int j = 0; j < nset; ++j) {
+          const int64_t i = j + (int64_t)nset * (l / n_ch);   // item index within the CTA's run
+          if (i >= items_here) continue;
+          const int ch = (int)(l % n_ch);
+          const int sl = j * nss + (int)(l % nss);
+          const int64_t use = l / nss;
+          if (use > 0 && !mbar_wait_bounded(&empty[sl], (uint32_t)((use - 1) & 1), p.status, 2)) return;
+          const int64_t item = g0 + i;
+          const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
+          const uint32_t bytes = (uint32_t)ni * S * p.slot_bytes;
+          uint32_t tx = 0;
+          for (int pp = 0; pp < P; ++pp)
+            if (item * P + pp < p.n_tiles) tx += bytes;
+          mbar_arrive_expect_tx(&full[sl], tx);
+          uint8_t* sp = ring + (size_t)sl * p.stage_bytes;
+          for (int pp = 0; pp < P; ++pp) {
+            const int64_t tile = item * P + pp;
+            if (tile < p.n_tiles)
+              bulk_g2s(sp + pp * piece, p.w + tile * p.tile_bytes + (int64_t)i0 * S * p.slot_bytes, bytes, &full[sl]);
+          }
+        }
+      }
+      if (!act_sent) {
         pdl_wait();
         mbar_arrive_expect_tx(act_bar, p.act_bytes);
         bulk_g2s(act, p.act_img, p.act_bytes, act_bar);
-      }
-      for (int64_t st = first; st < total; ++st) {
-        const uint32_t ph = (uint32_t)(st / ns) & 1u;
-        if (!mbar_wait_bounded(&empty[st % ns], ph ^ 1u, p.status, 2)) return;
-        issue(st);
       }
     }
     return;
@@ -658,83 +711,102 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
   if (p.act_img) {
     ok = mbar_wait_bounded(act_bar, 0, p.status, 3);
   } else {
-    quantize_image<MODE == 0>(p.x, p.x_stride, p.n_tok, p.n_act_tok, p.type, p.nu, p.kq, p.off_dx, p.off_bs, act,
-                              warp * 32 + lane, NW * 32);
+    ActImage ai;
+    ai.img = act;
+    ai.kq = p.kq;
+    ai.nu = p.nu;
+    ai.type = p.type;
+    ai.n_act_tok = p.n_act_tok;
+    ai.mma = MODE == 0;
+    ai.off_dx = p.off_dx;
+    ai.off_bs = p.off_bs;
+    quantize_image(p.x, p.x_stride, p.n_tok, ai, warp * 32 + lane, NW * 32);
     consumer_sync(NW * 32);
   }
+  const size_t us = (size_t)S * p.slot_bytes;   // slot stride between consecutive units of a range
 
-  const int slot_p = warp / (S * WR), r = (warp / WR) % S, half = warp % WR;
-  const int g = lane >> 2, q = lane & 3;     // mma: token g, tile rows 2q, 2q+1
-  const int dg = lane & 7, dq = lane >> 3;   // dp4a: tile row dg, unit residue dq
-  constexpr int NB = MODE == 0 ? 1 : MODE;
-  float acc[2][2];   // mma partial sums [residue of the pair][row]
-  float dacc[NB];    // dp4a partial sums [token] of residue dq
-  int64_t st = 0;
-  for (int64_t grp = g0; grp < g1; ++grp) {
-    const int64_t tile = grp * P + slot_p;
-    const bool live = tile < p.n_tiles;
-    acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.0f;
+  if constexpr (MODE == 0) {
+    const int set = warp / S, r = warp % S;
+    const int g = lane >> 2, q = lane & 3;      // D rows g, g+8; tokens 2q, 2q+1
+    int it = 0;
+    // (with S = 1 only the first 8 of the 16 warps form sets; the rest idle)
+    for (int64_t i = set; set < nset && g0 + i < g1; i += nset, ++it) {
+      const int64_t item = g0 + i;
+      float acc[4][4];   // [unit residue][output]
 #pragma unroll
-    for (int t = 0; t < NB; ++t) dacc[t] = 0.0f;
-    for (int ch = 0; ch < n_ch; ++ch, ++st) {
-      const int s = (int)(st % ns);
-      const uint32_t ph = (uint32_t)(st / ns) & 1u;
-      if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
-      const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
-      if (ok && live) {
-        const uint8_t* base = ring + (size_t)s * p.stage_bytes + slot_p * piece;
-        // this stage holds units [ua, ub) of the warp's range
-        const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);
-        const size_t us = (size_t)S * p.slot_bytes;   // slot stride between consecutive units
-        const uint8_t* rbase = base + (size_t)r * p.slot_bytes;   // unit ua of the range
-        if constexpr (MODE == 0) {
-          // units of residue 2*half (acc[0]) and 2*half+1 (acc[1]), in increasing order
-          int u = ua;
-          while (u < ub) {
-            const int res = u & 3;
-            if ((res >> 1) != half) {
-              u += half ? 2 - res : 4 - res;
-            } else if ((res & 1) == 0 && u + 1 < ub) {
-              mma_unit<WT>(p, rbase + (size_t)(u - ua) * us, act, u, g, q, acc[0][0], acc[0][1]);
-              mma_unit<WT>(p, rbase + (size_t)(u + 1 - ua) * us, act, u + 1, g, q, acc[1][0], acc[1][1]);
-              u += 4;
-            } else if ((res & 1) == 0) {
-              mma_unit<WT>(p, rbase + (size_t)(u - ua) * us, act, u, g, q, acc[0][0], acc[0][1]);
-              ++u;
-            } else {
-              mma_unit<WT>(p, rbase + (size_t)(u - ua) * us, act, u, g, q, acc[1][0], acc[1][1]);
-              u += 3;
+      for (int a = 0; a < 4; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.0f;
+      for (int ch = 0; ch < n_ch; ++ch) {
+        const int64_t lst = (int64_t)it * n_ch + ch;   // this set's local stage
+        const int s = set * nss + (int)(lst % nss);
+        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)(lst / nss) & 1u, p.status, 1);
+        const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
+        const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);   // units of this stage in range r
+        if (ok) {
+          const uint8_t* sa = ring + (size_t)s * p.stage_bytes + (size_t)r * p.slot_bytes;
+          const uint8_t* sb = sa + piece;
+          for (int u4 = ua & ~3; u4 < ub; u4 += 4) {
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+              const int u = u4 + a;
+              if (u >= ua && u < ub) mma2_unit<WT>(p, sa + (u - ua) * us, sb + (u - ua) * us, act, u, g, q, acc[a]);
             }
           }
-        } else {
-          // the four lane groups take four consecutive units (residues 0..3) at once
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // range partial (a0 + a1) + (a2 + a3) into red[it&1][set][r][token*16 + row]
+      float* rw = red[it & 1] + (set * S + r) * 128;
+#pragma unroll
+      for (int o = 0; o < 4; ++o) {
+        const float v = __fadd_rn(__fadd_rn(acc[0][o], acc[1][o]), __fadd_rn(acc[2][o], acc[3][o]));
+        rw[(2 * q + (o & 1)) * 16 + g + 8 * (o >> 1)] = v;
+      }
+      if (S > 1) tile_sync(set, S * 32);
+      else __syncwarp();
+      if (r == 0 && ok) finish_tiles<2>(p, red[it & 1] + set * S * 128, item * 2, lane);
+    }
+  } else {
+    const int slot_p = warp / S, r = warp % S;
+    const int dg = lane & 7, dq = lane >> 3;    // tile row dg, unit residue dq
+    constexpr int NB = MODE;
+    float dacc[NB];    // partial sums [token] of residue dq
+    int64_t st = 0;
+    for (int64_t grp = g0; grp < g1; ++grp) {
+      const int64_t tile = grp * P + slot_p;
+      const bool live = tile < p.n_tiles;
+#pragma unroll
+      for (int t = 0; t < NB; ++t) dacc[t] = 0.0f;
+      for (int ch = 0; ch < n_ch; ++ch, ++st) {
+        const int s = (int)(st % ns);
+        const uint32_t ph = (uint32_t)(st / ns) & 1u;
+        if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
+        const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
+        if (ok && live) {
+          const uint8_t* rbase = ring + (size_t)s * p.stage_bytes + slot_p * piece + (size_t)r * p.slot_bytes;
+          // this stage holds units [ua, ub) of the warp's range; the four lane
+          // groups take four consecutive units (residues 0..3) at once
+          const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);
           for (int u4 = ua & ~3; u4 < ub; u4 += 4) {
             const int u = u4 + dq;
             if (u >= ua && u < ub) dp4a_unit<WT, NB>(p, rbase + (size_t)(u - ua) * us, act, u, dg, dacc);
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    // The warp's partial into red[parity][warp][token*8 + row]: (a_2h + a_2h+1)
-    // for an mma warp, (a0 + a1) + (a2 + a3) for a dp4a warp.
-    float* rw = red[grp & 1][warp];
-    if constexpr (MODE == 0) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) rw[g * 8 + 2 * q + e] = __fadd_rn(acc[0][e], acc[1][e]);
-    } else {
+      // (a0 + a1) + (a2 + a3): residues dq and dq^1 are 8 lanes apart, dq and dq^2 16
+      float* rw = red[grp & 1] + (slot_p * S + r) * 64;
 #pragma unroll
       for (int t = 0; t < NB; ++t) {
-        // residues dq and dq^1 are 8 lanes apart, dq and dq^2 16 lanes apart
         float v = __fadd_rn(dacc[t], __shfl_xor_sync(0xffffffffu, dacc[t], 8));
         v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 16));
         if (dq == 0) rw[t * 8 + dg] = v;
       }
+      if (S > 1) tile_sync(slot_p, S * 32);
+      else __syncwarp();
+      if (r == 0 && live && ok) finish_tiles<1>(p, red[grp & 1] + slot_p * S * 64, tile, lane);
     }
-    if (S * WR > 1) tile_sync(slot_p, S * WR * 32);
-    else __syncwarp();
-    if (r == 0 && half == 0 && live) finish_tile<WR>(p, red[grp & 1][slot_p * S * WR], tile, lane);
   }
   if (p.peer.n) {
     __threadfence_system();   // this thread's peer stores, before the CTA is counted
@@ -744,7 +816,7 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
 }
 
 // 227 KB opt-in per block, less the kernel's static shared memory.
-constexpr int kSmemCap = 227 * 1024 - (int)sizeof(float) * 2 * kMaxNCW * 64 - 1024;
+constexpr int kSmemCap = 227 * 1024 - (int)sizeof(float) * 2 * kMaxNCW * 128 - 1024;
 
 template <int WT, int MODE>
 int set_attr() {
@@ -783,29 +855,9 @@ int launch_w(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
   return launch_t<WT, 2>(p, grid, smem, s);
 }
 
-// Carve-up of the activation image for w at n_tok tokens.
-struct ActGeom {
-  int n_act_tok, kq;
-  uint32_t off_dx, off_bs, bytes;
-};
-ActGeom act_geom(const QMatrix& w, int n_tok) {
-  ActGeom g;
-  g.n_act_tok = n_tok > kDp4aMaxTok ? kMaxTok : n_tok;
-  g.kq = (int)((w.k + 127) / 128 * 128);
-  const int bs_per_unit = w.type == B2_Q4_0 ? 1 : w.type == B2_Q4_K ? 8 : w.type == B2_Q6_K ? 16 : 0;
-  const size_t qs_b = (size_t)g.n_act_tok * g.kq;
-  const size_t dx_b = ((size_t)g.n_act_tok * w.nu * 4 + 15) / 16 * 16;
-  const size_t bs_b = ((size_t)g.n_act_tok * w.nu * bs_per_unit * 2 + 15) / 16 * 16;
-  g.off_dx = (uint32_t)qs_b;
-  g.off_bs = (uint32_t)(qs_b + dx_b);
-  g.bytes = (uint32_t)(qs_b + dx_b + bs_b);
-  return g;
-}
-
-int launch_quantize_image(const QMatrix& w, const float* x, int64_t x_stride, int n_tok, const ActGeom& g,
-                          uint8_t* img, cudaStream_t s) {
-  const bool k_quant = w.type == B2_Q4_K || w.type == B2_Q6_K;
-  const int64_t work = (int64_t)g.n_act_tok * w.nu * (k_quant ? 32 : 1);   // threads wanted
+int launch_quantize_image(const float* x, int64_t x_stride, int n_tok, const ActImage& g, cudaStream_t s) {
+  const bool k_quant = g.type == B2_Q4_K || g.type == B2_Q6_K;
+  const int64_t work = (int64_t)g.n_act_tok * g.nu * (k_quant ? 32 : 1);   // threads wanted
   const int block = 256;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + block - 1) / block, 4 * sm_count()));
   cudaLaunchConfig_t cfg = {};
@@ -817,18 +869,32 @@ int launch_quantize_image(const QMatrix& w, const float* x, int64_t x_stride, in
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (n_tok > kDp4aMaxTok)
-    B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, quantize_image_kernel<true>, x, x_stride, n_tok, g.n_act_tok, w.type, w.nu,
-                                   g.kq, g.off_dx, g.off_bs, img));
-  else
-    B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, quantize_image_kernel<false>, x, x_stride, n_tok, g.n_act_tok, w.type,
-                                   w.nu, g.kq, g.off_dx, g.off_bs, img));
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, quantize_image_kernel, x, x_stride, n_tok, g));
   return B2_OK;
 }
 
 }  // namespace
 
-size_t gemv_act_image_bytes(const QMatrix& w, int n_tok) { return act_geom(w, n_tok).bytes; }
+// Carve-up of the activation image for w at n_tok tokens.
+ActImage gemv_act_image(const QMatrix& w, int n_tok, uint8_t* img) {
+  ActImage g;
+  g.img = img;
+  g.type = w.type;
+  g.nu = w.nu;
+  g.mma = n_tok > kDp4aMaxTok;
+  g.n_act_tok = g.mma ? kMaxTok : n_tok;
+  g.kq = (int)((w.k + 127) / 128 * 128);
+  const int bs_per_unit = w.type == B2_Q4_0 ? 1 : w.type == B2_Q4_K ? 8 : w.type == B2_Q6_K ? 16 : 0;
+  const size_t qs_b = (size_t)g.n_act_tok * g.kq;
+  const size_t dx_b = ((size_t)g.n_act_tok * w.nu * 4 + 15) / 16 * 16;
+  const size_t bs_b = ((size_t)g.n_act_tok * w.nu * bs_per_unit * 2 + 15) / 16 * 16;
+  g.off_dx = (uint32_t)qs_b;
+  g.off_bs = (uint32_t)(qs_b + dx_b);
+  g.bytes = (uint32_t)(qs_b + dx_b + bs_b);
+  return g;
+}
+
+size_t gemv_act_image_bytes(const QMatrix& w, int n_tok) { return gemv_act_image(w, n_tok, nullptr).bytes; }
 
 // Small activations (<= 32 KB of fp32) are quantized by every CTA itself;
 // larger ones go through the image in global memory.
@@ -852,14 +918,21 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   if (prc) return prc;
   const QMatrix& w = *a.w;
   B2_CHECK_ARG(a.n_tok >= 1 && a.n_tok <= kMaxTok, "n_tok must be in [1, 8]");
-  B2_CHECK_ARG(a.y != nullptr && a.x != nullptr, "x and y");
+  B2_CHECK_ARG(a.image_ready || a.x != nullptr, "x");
+  B2_CHECK_ARG(a.epilogue == EPI_ROPE_KV ? a.rope != nullptr : a.y != nullptr, "outputs");
   B2_CHECK_ARG(w.data != nullptr && w.nu > 0, "matrix");
   B2_CHECK_ARG(a.epilogue != EPI_SWIGLU || (w.n_rows % 2) == 0, "SwiGLU needs (gate, up) row pairs");
-  B2_CHECK_ARG((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride % 4) == 0,
+  B2_CHECK_ARG(a.image_ready || ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride % 4) == 0),
                "x must be 16-byte aligned with a stride of whole float4s");
-  B2_CHECK_ARG(!gemv_needs_image(w, a.n_tok) ||
+  B2_CHECK_ARG(!(gemv_needs_image(w, a.n_tok) || a.image_ready) ||
                    (a.act_img != nullptr && (reinterpret_cast<uintptr_t>(a.act_img) & 15) == 0),
                "activation image scratch (16-byte aligned)");
+  if (a.epilogue == EPI_ROPE_KV) {
+    const RopeKvEpi& r = *a.rope;
+    B2_CHECK_ARG(r.pos && r.seq && r.rope && r.q_out && r.kc && r.vc && r.hd > 0 && (r.hd % 8) == 0 &&
+                     w.n_rows == (int64_t)(r.n_head + 2 * r.n_kv) * r.hd,
+                 "RoPE/KV epilogue arguments");
+  }
   GemvP p = {};
   p.w = w.data;
   p.type = w.type;
@@ -886,7 +959,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   } else {
     p.peer = PeerOut{};
   }
-  const ActGeom ag = act_geom(w, a.n_tok);
+  const ActImage ag = gemv_act_image(w, a.n_tok, a.act_img);
   p.kq = ag.kq;
   p.off_dx = ag.off_dx;
   p.off_bs = ag.off_bs;
@@ -894,31 +967,53 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   // Small activations are quantized by each CTA itself (no extra kernel and
   // no dependency on a shared image between consecutive launches); large ones
   // once, into the image every CTA copies.
-  const bool in_kernel = !gemv_needs_image(w, a.n_tok);
+  const bool in_kernel = !a.image_ready && !gemv_needs_image(w, a.n_tok);
   p.act_img = in_kernel ? nullptr : a.act_img;
-  // Stages of P tiles x U unit steps of all S ranges, U as large as fits ~32 KB.
-  const int P = 8 / w.splits;
+  if (a.epilogue == EPI_ROPE_KV) p.rope = *a.rope;
+  // Stages of P tiles x U unit steps of all S ranges.  mma: one tile pair per
+  // stage, U as large as fits ~16 KB, and whole rings of nss >= 2 slots for
+  // each of the nset consumer sets (smaller U, or the full shared memory,
+  // where needed); dp4a: P = 8/S tiles, ~32 KB.  With small activations stay
+  // within ~100 KB when that still gives the pipeline it needs, so that two
+  // CTAs fit on an SM and the next launch's producer can stream while this
+  // one drains.
+  const bool mma = a.n_tok > kDp4aMaxTok;
+  const int P = mma ? 2 : 8 / w.splits;
+  const int nset = mma ? std::min(16 / w.splits, 8) : 1;
   const size_t step_b = (size_t)P * w.splits * w.slot_bytes;
-  int U = (int)std::max<size_t>(1, (32 * 1024) / step_b);
-  U = std::min(U, w.ulen);
-  const size_t stage = step_b * U;
   const size_t fixed = kBarBytes + p.act_bytes;
-  if (fixed + 2 * stage > (size_t)kSmemCap) {
+  int U = 0, ns = 0;
+  size_t stage = 0;
+  auto fit = [&](size_t cap_, int want_per_set) -> bool {
+    for (int u = std::min<int>(w.ulen, (int)std::max<size_t>(1, (mma ? 16 * 1024 : 32 * 1024) / step_b)); u >= 1;
+         --u) {
+      const size_t st = step_b * u;
+      if (fixed + st > cap_) continue;
+      int n = (int)std::min<size_t>(kMaxStages, (cap_ - fixed) / st);
+      n = n / nset * nset;
+      if (n >= want_per_set * nset) {
+        U = u;
+        ns = n;
+        stage = st;
+        return true;
+      }
+    }
+    return false;
+  };
+  const bool ok_fit = (in_kernel && fit(100 * 1024, mma ? 2 : 3)) || fit((size_t)kSmemCap, 2) ||
+                      fit((size_t)kSmemCap, 1);
+  if (!ok_fit) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
   }
-  // With small activations stay within ~100 KB, so that two CTAs fit on an SM
-  // and the next launch's producer can stream while this one drains.
-  const size_t cap = (in_kernel && fixed + 3 * stage <= 100 * 1024) ? 100 * 1024 : (size_t)kSmemCap;
-  const int ns = (int)std::min<size_t>(kMaxStages, (cap - fixed) / stage);
   p.U = U;
   p.n_stages = ns;
   p.stage_bytes = (uint32_t)stage;
   const size_t smem = fixed + (size_t)ns * stage;
-  const int64_t groups = (w.n_tiles + P - 1) / P;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), groups));
-  if (!in_kernel) {
-    const int qrc = launch_quantize_image(w, a.x, a.x_stride, a.n_tok, ag, a.act_img, s);
+  const int64_t items = (w.n_tiles + P - 1) / P;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), items));
+  if (!in_kernel && !a.image_ready) {
+    const int qrc = launch_quantize_image(a.x, a.x_stride, a.n_tok, ag, s);
     if (qrc) return qrc;
   }
   switch (w.type) {

@@ -181,6 +181,53 @@ enum Epilogue : int {
   EPI_STORE = 0,       // y = W·x
   EPI_ACCUM = 1,       // y += W·x (residual add)
   EPI_SWIGLU = 2,      // rows (2i, 2i+1) are (gate_i, up_i): y[i] = silu(gate)·up
+  EPI_ROPE_KV = 3,     // fused Q/K/V rows: RoPE on q and k, q to q_out, k and v into the fp16 KV cache
+};
+
+// Per-sequence KV bookkeeping, read by kernels from device memory (a null
+// state array means every sequence is in the plain layout, slot = position).  Logical
+// position p lives in physical slot p when p < n_keep (the pinned prefix),
+// otherwise in n_keep + (ring_head + p − n_keep) mod (cap − n_keep): the
+// slots after the prefix form a ring, so dropping the oldest positions
+// after the prefix (Milda's KV shift) only advances ring_head.
+struct KvSeqState {
+  int32_t n_keep;
+  int32_t ring_head;
+};
+B2_HD inline int64_t kv_slot(const KvSeqState& st, int p, int cap) {
+  const int ring = cap - st.n_keep;
+  if (p < st.n_keep || ring <= 0) return p;
+  const int r = (st.ring_head + (p - st.n_keep)) % ring;
+  return st.n_keep + r;
+}
+
+// The QKV projection's fused epilogue (EPI_ROPE_KV): output row r of token t
+// is dim r % hd of head r / hd (n_head query heads, then n_kv key heads, then
+// n_kv value heads).  Pairs (2i, 2i+1) of q and k rows are rotated by the
+// token's position (rope: [position][hd] cos, sin pairs) exactly as
+// rope_kv_kernel does; q goes to q_out [t][n_head*hd], k and v to the cache
+// slot of (seq[t], pos[t]) in fp16 (RNE).  A token whose sequence or position
+// is outside the cache gets a zero q and stores nothing.
+struct RopeKvEpi {
+  const int32_t* pos = nullptr;
+  const int32_t* seq = nullptr;
+  const float* rope = nullptr;
+  float* q_out = nullptr;
+  uint16_t* kc = nullptr;
+  uint16_t* vc = nullptr;
+  const KvSeqState* st = nullptr;   // may be null (plain layout)
+  int n_head = 0, n_kv = 0, hd = 0, n_seq = 0, cap = 0;
+};
+
+// Where a GEMV's quantized activations live: the image carve-up of
+// gemv_act_image(w, n_tok) — codes [n_act_tok][kq] (fragment order for the
+// mma kernels, natural order for dp4a), fp32 scales per (token, unit), int16
+// block sums per (token, unit).  Producers other than the GEMV's own
+// quantizer (the fused RMSNorm) write it through the same store helpers.
+struct ActImage {
+  uint8_t* img = nullptr;
+  int kq = 0, nu = 0, type = 0, n_act_tok = 0, mma = 0;
+  uint32_t off_dx = 0, off_bs = 0, bytes = 0;
 };
 
 // Tensor-parallel exchange over peer memory (CUDA IPC mappings over NVLink).
@@ -219,10 +266,14 @@ struct GemvArgs {
   int epilogue;
   int* status;          // device status word (bounded waits), may be nullptr
   const PeerOut* peer = nullptr;   // tensor-parallel exchange of the outputs (EPI_STORE only)
+  const RopeKvEpi* rope = nullptr; // EPI_ROPE_KV targets
+  bool image_ready = false;        // act_img already holds x quantized (x is not read)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 size_t gemv_act_image_bytes(const QMatrix& w, int n_tok);
 bool gemv_needs_image(const QMatrix& w, int n_tok);
+// The image carve-up the GEMV over w expects for n_tok tokens, at img.
+ActImage gemv_act_image(const QMatrix& w, int n_tok, uint8_t* img);
 
 // Tensor-core prefill GEMM (Q4_K weights, any number of tokens), summation
 // order identical to the reference's per-row vec_dot.  `img` is device

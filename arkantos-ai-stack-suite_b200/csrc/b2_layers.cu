@@ -13,6 +13,7 @@
 
 #include "b2_common.cuh"
 #include "b2_layers.hpp"
+#include "b2_quant.cuh"
 
 namespace b2 {
 namespace {
@@ -137,13 +138,121 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const float* __restric
   for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
 }
 
-// ---- RoPE + KV store -------------------------------------------------------------------------
-__device__ __forceinline__ int64_t kv_slot(const KvSeqState& st, int p, int cap) {
-  const int ring = cap - st.n_keep;
-  if (p < st.n_keep || ring <= 0) return p;
-  int r = (st.ring_head + (p - st.n_keep)) % ring;
-  return st.n_keep + r;
+// Residual add + RMSNorm fused with the next GEMV's activation quantization:
+// one CTA per token, thread i owning values [8i, 8i+8) (n = 8·blockDim), so
+// warp w holds Q8_K super-block w and four consecutive lanes one Q8_0 block.
+// The residual sum, the double sum of squares and the scaling are the same
+// operations as add_rmsnorm_kernel; the quantizers are the reference's
+// (b2_quant.cuh) and write the image the GEMV copies.
+__global__ void add_rmsnorm_q_kernel(float* __restrict__ x, const float* __restrict__ delta,
+                                     const float* __restrict__ w, float* __restrict__ out, int n, float eps, PeerIn in,
+                                     int* status, ActImage img) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, i0 = 8 * tid;
+  float* xr = x + (int64_t)b * n + i0;
+  if (in.n) {
+    if (tid == 0) {
+      wait_peer_flags(in.flags, in.n, *in.epoch, status, 3);
+      __threadfence();
+    }
+    __syncthreads();
+  }
+  float v[8];
+  {
+    const float4 a0 = *reinterpret_cast<const float4*>(xr), a1 = *reinterpret_cast<const float4*>(xr + 4);
+    v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+    v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+  }
+  if (in.n || delta) {
+    float dsum[8];
+    if (in.n) {
+      for (int r = 0; r < in.n; ++r) {
+        const float* pp = in.parts + r * in.slot + (int64_t)b * n + i0;
+        const float4 p0 = __ldcg(reinterpret_cast<const float4*>(pp)), p1 = __ldcg(reinterpret_cast<const float4*>(pp + 4));
+        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dsum[j] = r ? __fadd_rn(dsum[j], pv[j]) : pv[j];
+      }
+    } else {
+      const float* dr = delta + (int64_t)b * n + i0;
+      const float4 d0 = *reinterpret_cast<const float4*>(dr), d1 = *reinterpret_cast<const float4*>(dr + 4);
+      dsum[0] = d0.x; dsum[1] = d0.y; dsum[2] = d0.z; dsum[3] = d0.w;
+      dsum[4] = d1.x; dsum[5] = d1.y; dsum[6] = d1.z; dsum[7] = d1.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], dsum[j]);
+    *reinterpret_cast<float4*>(xr) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(xr + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += (double)__fmul_rn(v[j], v[j]);
+  __shared__ double red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    double t = tid < (blockDim.x >> 5) ? red[tid] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (tid == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float mean = __double2float_rn(__ddiv_rn(red[0], (double)n));
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  float y[8];
+  {
+    const float4 w0 = *reinterpret_cast<const float4*>(w + i0), w1 = *reinterpret_cast<const float4*>(w + i0 + 4);
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__fmul_rn(v[j], scale), wv[j]);
+  }
+  if (out) {
+    float* orow = out + (int64_t)b * n + i0;
+    *reinterpret_cast<float4*>(orow) = make_float4(y[0], y[1], y[2], y[3]);
+    *reinterpret_cast<float4*>(orow + 4) = make_float4(y[4], y[5], y[6], y[7]);
+  }
+  if (img.type == B2_Q4_K || img.type == B2_Q6_K) {
+    int8_t q[8];
+    int bs = 0;
+    const float d = quant_q8_k_lane(y, q, &bs);
+    store_q8k_unit(img, b, tid >> 5, q, d, bs);
+  } else {
+    // Q8_0 block tid/4 over lanes 4k..4k+3 (ref_quantize_row_q8_0)
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fmul_rn(amax, 1.0f / 127.0f);
+    const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+    uint32_t wd[2] = {0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float sc = __fmul_rn(y[j], id);
+      const float tt = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
+      int q = __float2int_rz(tt);
+      q = q < -127 ? -127 : (q > 127 ? 127 : q);
+      sum += q;
+      wd[j >> 2] |= ((uint32_t)(uint8_t)q) << (8 * (j & 3));
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    uint32_t wb[8];
+    const int g0 = lane & ~3;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      wb[2 * m] = __shfl_sync(0xffffffffu, wd[0], g0 + m);
+      wb[2 * m + 1] = __shfl_sync(0xffffffffu, wd[1], g0 + m);
+    }
+    if ((lane & 3) == 0) store_q8_0_block(img, b, tid >> 2, wb, h2f(f2h_rn(d)), sum);
+  }
 }
+
+// ---- RoPE + KV store -------------------------------------------------------------------------
 
 __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_kv, int hd, const int32_t* __restrict__ pos,
                                const int32_t* __restrict__ seq, const float* __restrict__ rope, float* __restrict__ q_out,
@@ -189,34 +298,80 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_
 // of the query's sequence, for the G query heads sharing the kv head.  The
 // chunk's K and V rows are brought into shared memory by cp.async.bulk (1-D
 // TMA; a chunk crossing the ring's seam or the pinned prefix is up to three
-// copies), then, per head:
-//   scores: lane i of an 8-lane group holds dims [i*HD/8, (i+1)*HD/8) of q and
-//     k; an fmaf chain over its dims, a butterfly over the 8 lanes (xor 4, 2,
-//     1), times 1/sqrt(HD);
+// copies) while q goes to shared memory; then, per head:
+//   scores: lane i of an 8-lane group holds dims [B*i, B*i+B) and
+//     [HD/2 + B*i, HD/2 + B*i + B) (B = HD/16) of q and k (16-byte rows of a
+//     position per group, so the K reads are bank-conflict free); an fmaf
+//     chain over its dims in that order, a butterfly over the 8 lanes (xor 4,
+//     2, 1), times 1/sqrt(HD).  Each lane group scores 4 positions against
+//     all G heads at once (q from shared memory, packed f32x2 FMAs);
 //   m = the chunk's max; e = exp(s − m); the chunk sum l = ((W0 + W1) + W2) + W3
 //     with W_w the 32-lane butterfly (xor 16..1) of e over positions 32w..32w+31;
 //   P·V: output dim d keeps four sums a_r of e·v over the positions i with
 //     i mod 4 == r (fmaf chains in position order; warp r of a dim half takes
 //     them, one position for all heads at a time), then (a0 + a1) + (a2 + a3).
-// Writes the unnormalised partial output with its max and sum.  Every wait is
+// Writes the unnormalised partial output with its max and sum.  With
+// fz.count, the last CTA of each (query, kv head) to finish also combines the
+// chunks (attn_combine's arithmetic) into fz.out and, with fz.img, quantizes
+// those G·HD outputs into the O projection's activation image.  Every wait is
 // bounded; a query outside the cache attends to nothing.
 constexpr int kAttnP = 128;
+struct AttnFuse {
+  unsigned int* count = nullptr;   // [n_tok][n_kv] arrivals, zero between launches (null: separate combine)
+  float* out = nullptr;            // [n_tok][n_head][hd]
+  ActImage img;                    // O projection image (img.img null: none)
+};
+
+// Two fp32 FMAs in one instruction (fma.rn.f32x2): each lane is rounded like fmaf.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// B fp16 values at p (16-byte aligned for B = 8, 8-byte for B = 4) -> fp32.
+template <int B>
+__device__ __forceinline__ void ld_half_row(const uint16_t* p, float (&f)[B]) {
+  if constexpr (B == 8) {
+    const uint4 w = *reinterpret_cast<const uint4*>(p);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      f[2 * e] = h2f((uint16_t)(ww[e] & 0xFFFFu));
+      f[2 * e + 1] = h2f((uint16_t)(ww[e] >> 16));
+    }
+  } else {
+    const uint2 w = *reinterpret_cast<const uint2*>(p);
+    f[0] = h2f((uint16_t)(w.x & 0xFFFFu));
+    f[1] = h2f((uint16_t)(w.x >> 16));
+    f[2] = h2f((uint16_t)(w.y & 0xFFFFu));
+    f[3] = h2f((uint16_t)(w.y >> 16));
+  }
+}
+
 template <int HD, int G>
-__global__ void __launch_bounds__(256) attn_chunk_kernel(const float* __restrict__ q, int n_head, int n_kv,
-                                                         const int32_t* __restrict__ pos, const int32_t* __restrict__ seq,
-                                                         const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
-                                                         const KvSeqState* __restrict__ st, int n_seq, int cap,
-                                                         float scale, float* __restrict__ part_o,
-                                                         float* __restrict__ part_ml, int n_split, int* status) {
-  constexpr int P = kAttnP, DL = HD / 8;        // dims per lane of an 8-lane group
-  constexpr int HG = (DL * G <= 64) ? G : 64 / DL;   // heads per score pass (q in registers)
+__global__ void __launch_bounds__(256, 3) attn_chunk_kernel(const float* __restrict__ q, int n_head, int n_kv,
+                                                            const int32_t* __restrict__ pos,
+                                                            const int32_t* __restrict__ seq,
+                                                            const uint16_t* __restrict__ kc,
+                                                            const uint16_t* __restrict__ vc,
+                                                            const KvSeqState* __restrict__ st, int n_seq, int cap,
+                                                            float scale, float* __restrict__ part_o,
+                                                            float* __restrict__ part_ml, int n_split, int* status,
+                                                            AttnFuse fz) {
+  constexpr int P = kAttnP, B = HD / 16;
   constexpr int PAIRS = HD / 2;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);   // [P][HD]
   uint16_t* vs = ks + P * HD;                                 // [P][HD]
-  float* sc = reinterpret_cast<float*>(vs + P * HD);          // [P][G]: scores, then e
+  float* qs = reinterpret_cast<float*>(vs + P * HD);          // [G][HD]
+  float* sc = qs + G * HD;                                    // [P][G]: scores, then e
   __shared__ float mh[G], lh[G], wred[G][4];
+  __shared__ unsigned int last_cta;
   pdl_wait();
   pdl_launch_dependents();
   const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -233,143 +388,233 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float* __restrict
       pml[(int64_t)tid * n_split * 2 + 0] = -FLT_MAX;
       pml[(int64_t)tid * n_split * 2 + 1] = 0.0f;
     }
-    return;
-  }
-  const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
-  const int64_t base = ((int64_t)s * n_kv + kh) * cap;   // row of slot 0
-  if (tid == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-    mbar_arrive_expect_tx(bar, (uint32_t)(2 * n * HD * 2));
-    // logical positions [t0, t0+n) as runs of consecutive slots
-    int p = t0;
-    while (p < t0 + n) {
-      const int64_t slot = kv_slot(sst, p, cap);
-      int len = t0 + n - p;
-      if (p < sst.n_keep) len = min(len, sst.n_keep - p);
-      else len = (int)min((int64_t)len, (int64_t)cap - slot);   // up to the end of the ring
-      bulk_g2s(ks + (p - t0) * HD, kc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
-      bulk_g2s(vs + (p - t0) * HD, vc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
-      p += len;
-    }
-  }
-  // q of this lane's dims, for the heads of the first pass, while the copies fly
-  const int li = lane & 7, grp = lane >> 3;
-  __syncthreads();
-  mbar_wait_bounded(bar, 0, status, 5);
-
-  // ---- scores ----
-#pragma unroll 1
-  for (int h0 = 0; h0 < G; h0 += HG) {
-    float qr[HG][DL];
-#pragma unroll
-    for (int h = 0; h < HG; ++h) {
-      const float* qh = q + ((int64_t)b * n_head + hq0 + h0 + h) * HD + li * DL;
-#pragma unroll
-      for (int d = 0; d < DL; d += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(qh + d);
-        qr[h][d] = v.x;
-        qr[h][d + 1] = v.y;
-        qr[h][d + 2] = v.z;
-        qr[h][d + 3] = v.w;
+  } else {
+    const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
+    const int64_t base = ((int64_t)s * n_kv + kh) * cap;   // row of slot 0
+    if (tid == 0) {
+      mbar_init(bar, 1);
+      fence_mbar_init();
+      mbar_arrive_expect_tx(bar, (uint32_t)(2 * n * HD * 2));
+      // logical positions [t0, t0+n) as runs of consecutive slots
+      int p = t0;
+      while (p < t0 + n) {
+        const int64_t slot = kv_slot(sst, p, cap);
+        int len = t0 + n - p;
+        if (p < sst.n_keep) len = min(len, sst.n_keep - p);
+        else len = (int)min((int64_t)len, (int64_t)cap - slot);   // up to the end of the ring
+        bulk_g2s(ks + (p - t0) * HD, kc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
+        bulk_g2s(vs + (p - t0) * HD, vc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
+        p += len;
       }
     }
-    for (int it = 0; it < P / 32; ++it) {
-      const int i = warp * (P / 8) + it * 4 + grp;   // position of this lane group
-      float kf[DL];
-      if (i < n) {
-        const uint4* kr = reinterpret_cast<const uint4*>(ks + i * HD + li * DL);
+    // q of the G heads into shared memory while the copies fly
+    {
+      const float4* qg = reinterpret_cast<const float4*>(q + ((int64_t)b * n_head + hq0) * HD);
+      for (int i = tid; i < G * HD / 4; i += blockDim.x) reinterpret_cast<float4*>(qs)[i] = qg[i];
+    }
+    __syncthreads();
+    mbar_wait_bounded(bar, 0, status, 5);
+
+    // ---- scores: lane group grp of warp w takes positions w*16 + it*4 + grp, HG heads per pass ----
+    {
+      constexpr int HG = G < 4 ? G : 4;
+      const int li = lane & 7, grp = lane >> 3;
+#pragma unroll 1
+      for (int hb = 0; hb < G; hb += HG) {
+        float acc[4][HG];
 #pragma unroll
-        for (int c = 0; c < DL / 8; ++c) {
-          const uint4 w = kr[c];
-          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        for (int it = 0; it < 4; ++it)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            kf[c * 8 + 2 * e] = h2f((uint16_t)(ww[e] & 0xFFFFu));
-            kf[c * 8 + 2 * e + 1] = h2f((uint16_t)(ww[e] >> 16));
+          for (int h = 0; h < HG; ++h) acc[it][h] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int d0 = j * (HD / 2) + B * li;
+          float qv[HG][B];
+#pragma unroll
+          for (int h = 0; h < HG; ++h)
+#pragma unroll
+            for (int d = 0; d < B; d += 4) {
+              const float4 v = *reinterpret_cast<const float4*>(qs + (hb + h) * HD + d0 + d);
+              qv[h][d] = v.x;
+              qv[h][d + 1] = v.y;
+              qv[h][d + 2] = v.z;
+              qv[h][d + 3] = v.w;
+            }
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int i = warp * 16 + it * 4 + grp;
+            float kf[B];
+            if (i < n) {
+              ld_half_row<B>(ks + i * HD + d0, kf);
+            } else {
+#pragma unroll
+              for (int d = 0; d < B; ++d) kf[d] = 0.0f;
+            }
+#pragma unroll
+            for (int d = 0; d < B; ++d) {
+              if constexpr (HG == 1) {
+                acc[it][0] = fmaf(qv[0][d], kf[d], acc[it][0]);
+              } else {
+#pragma unroll
+                for (int h = 0; h < HG; h += 2)
+                  ffma2(acc[it][h], acc[it][h + 1], qv[h][d], qv[h + 1][d], kf[d], kf[d]);
+              }
+            }
           }
         }
-      } else {
 #pragma unroll
-        for (int d = 0; d < DL; ++d) kf[d] = 0.0f;
-      }
+        for (int it = 0; it < 4; ++it) {
+          const int i = warp * 16 + it * 4 + grp;
 #pragma unroll
-      for (int h = 0; h < HG; ++h) {
-        float a = 0.0f;
-#pragma unroll
-        for (int d = 0; d < DL; ++d) a = fmaf(qr[h][d], kf[d], a);
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-        if (li == 0 && i < n) sc[i * G + h0 + h] = __fmul_rn(a, scale);
-      }
-    }
-  }
-  __syncthreads();
-  // ---- max, exp and the chunk sum: 128 threads per head, 2 heads per round ----
-#pragma unroll 1
-  for (int h0 = 0; h0 < G; h0 += 2) {
-    const int h = h0 + (tid >> 7), w = (tid >> 5) & 3, i = tid & 127;
-    const bool act = h < G;
-    float v = (act && i < n) ? sc[i * G + h] : -FLT_MAX;
-    v = warp_max(v);
-    if (act && lane == 0) wred[h][w] = v;
-    __syncthreads();
-    const float m = act ? fmaxf(fmaxf(wred[h][0], wred[h][1]), fmaxf(wred[h][2], wred[h][3])) : 0.0f;
-    float e = 0.0f;
-    if (act && i < n) {
-      e = b2_expf(__fsub_rn(sc[i * G + h], m));
-      sc[i * G + h] = e;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, o));
-    __syncthreads();   // every wred max read before the sums reuse it
-    if (act && lane == 0) wred[h][w] = e;
-    __syncthreads();
-    if (act && i == 0) {
-      mh[h] = m;
-      lh[h] = __fadd_rn(__fadd_rn(__fadd_rn(wred[h][0], wred[h][1]), wred[h][2]), wred[h][3]);
-    }
-  }
-  __syncthreads();
-  // ---- P·V: warp (residue r, dim half), lane = dim pair; all heads per position ----
-  float* pv = reinterpret_cast<float*>(ks);   // [4 residues][G][HD] partials, K is no longer needed
-  {
-    const int r = warp & 3, pr = (warp >> 2) * 32 + lane;
-    if (pr < PAIRS) {
-      float acc[G][2];
-#pragma unroll
-      for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0.0f;
-      for (int i = r; i < n; i += 4) {
-        const uint32_t vv = *reinterpret_cast<const uint32_t*>(vs + i * HD + 2 * pr);
-        const float v0 = h2f((uint16_t)(vv & 0xFFFFu)), v1 = h2f((uint16_t)(vv >> 16));
-        float e[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) e[h] = sc[i * G + h];
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          acc[h][0] = fmaf(e[h], v0, acc[h][0]);
-          acc[h][1] = fmaf(e[h], v1, acc[h][1]);
+          for (int h = 0; h < HG; ++h) {
+            float a = acc[it][h];
+            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+            if (li == h && i < n) sc[i * G + hb + h] = __fmul_rn(a, scale);
+          }
         }
       }
-      __syncwarp();
+    }
+    __syncthreads();
+    // ---- max, exp and the chunk sum: 128 threads per head, 2 heads per round ----
+#pragma unroll 1
+    for (int h0 = 0; h0 < G; h0 += 2) {
+      const int h = h0 + (tid >> 7), w = (tid >> 5) & 3, i = tid & 127;
+      const bool act = h < G;
+      float v = (act && i < n) ? sc[i * G + h] : -FLT_MAX;
+      v = warp_max(v);
+      if (act && lane == 0) wred[h][w] = v;
+      __syncthreads();
+      const float m = act ? fmaxf(fmaxf(wred[h][0], wred[h][1]), fmaxf(wred[h][2], wred[h][3])) : 0.0f;
+      float e = 0.0f;
+      if (act && i < n) {
+        e = b2_expf(__fsub_rn(sc[i * G + h], m));
+        sc[i * G + h] = e;
+      }
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        pv[(r * G + h) * HD + 2 * pr] = acc[h][0];
-        pv[(r * G + h) * HD + 2 * pr + 1] = acc[h][1];
+      for (int o = 16; o > 0; o >>= 1) e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, o));
+      __syncthreads();   // every wred max read before the sums reuse it
+      if (act && lane == 0) wred[h][w] = e;
+      __syncthreads();
+      if (act && i == 0) {
+        mh[h] = m;
+        lh[h] = __fadd_rn(__fadd_rn(__fadd_rn(wred[h][0], wred[h][1]), wred[h][2]), wred[h][3]);
       }
     }
+    __syncthreads();
+    // ---- P·V: warp (residue r, dim half), lane = dim pair; all heads per position ----
+    float* pv = reinterpret_cast<float*>(ks);   // [4 residues][G][HD] partials, K is no longer needed
+    {
+      const int r = warp & 3, pr = (warp >> 2) * 32 + lane;
+      if (pr < PAIRS) {
+        float acc[G][2];
+#pragma unroll
+        for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0.0f;
+        for (int i = r; i < n; i += 4) {
+          const uint32_t vv = *reinterpret_cast<const uint32_t*>(vs + i * HD + 2 * pr);
+          const float v0 = h2f((uint16_t)(vv & 0xFFFFu)), v1 = h2f((uint16_t)(vv >> 16));
+          float e[G];
+#pragma unroll
+          for (int h = 0; h < G; h += (G >= 4 ? 4 : 1)) {
+            if constexpr (G >= 4) {
+              const float4 e4 = *reinterpret_cast<const float4*>(sc + i * G + h);
+              e[h] = e4.x;
+              e[h + 1] = e4.y;
+              e[h + 2] = e4.z;
+              e[h + 3] = e4.w;
+            } else {
+              e[h] = sc[i * G + h];
+            }
+          }
+#pragma unroll
+          for (int h = 0; h < G; ++h) ffma2(acc[h][0], acc[h][1], e[h], e[h], v0, v1);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+          *reinterpret_cast<float2*>(pv + (r * G + h) * HD + 2 * pr) = make_float2(acc[h][0], acc[h][1]);
+      }
+    }
+    __syncthreads();
+    for (int hd2 = tid; hd2 < G * HD; hd2 += blockDim.x) {
+      const int h = hd2 / HD, d = hd2 - h * HD;
+      const float a0 = pv[(0 * G + h) * HD + d], a1 = pv[(1 * G + h) * HD + d];
+      const float a2 = pv[(2 * G + h) * HD + d], a3 = pv[(3 * G + h) * HD + d];
+      po[(int64_t)h * n_split * HD + d] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+    }
+    if (tid < G) {
+      pml[(int64_t)tid * n_split * 2 + 0] = mh[tid];
+      pml[(int64_t)tid * n_split * 2 + 1] = lh[tid];
+    }
+  }
+  if (fz.count == nullptr) return;
+  // ---- the last CTA of this (query, kv head) combines the chunks ----
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    unsigned int* cnt = fz.count + (int64_t)b * n_kv + kh;
+    last_cta = atomicAdd(cnt, 1u) == (unsigned int)(n_split - 1);
+    if (last_cta) *cnt = 0u;   // ready for the next launch
   }
   __syncthreads();
+  if (!last_cta) return;
+  __threadfence();
+  float* ob = reinterpret_cast<float*>(smem + 128);   // [G][HD] outputs of this kv head
   for (int hd2 = tid; hd2 < G * HD; hd2 += blockDim.x) {
     const int h = hd2 / HD, d = hd2 - h * HD;
-    const float a0 = pv[(0 * G + h) * HD + d], a1 = pv[(1 * G + h) * HD + d];
-    const float a2 = pv[(2 * G + h) * HD + d], a3 = pv[(3 * G + h) * HD + d];
-    po[(int64_t)h * n_split * HD + d] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+    const float* ml = part_ml + ((int64_t)b * n_head + hq0 + h) * n_split * 2;
+    const float* pq = part_o + ((int64_t)b * n_head + hq0 + h) * n_split * HD;
+    float M = -FLT_MAX;
+    for (int c = 0; c < n_split; ++c) M = fmaxf(M, __ldcg(ml + 2 * c));
+    float L = 0.0f, v = 0.0f;
+    for (int c = 0; c < n_split; ++c) {
+      const float lc = __ldcg(ml + 2 * c + 1);
+      if (lc > 0.0f) {
+        const float ec = b2_expf(__fsub_rn(__ldcg(ml + 2 * c), M));
+        L = __fadd_rn(L, __fmul_rn(ec, lc));
+        v = __fadd_rn(v, __fmul_rn(ec, __ldcg(pq + (int64_t)c * HD + d)));
+      }
+    }
+    const float invL = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;   // L == 0: a query that attended to nothing
+    const float o = __fmul_rn(v, invL);
+    fz.out[((int64_t)b * n_head + hq0 + h) * HD + d] = o;
+    ob[hd2] = o;
   }
-  if (tid < G) {
-    pml[(int64_t)tid * n_split * 2 + 0] = mh[tid];
-    pml[(int64_t)tid * n_split * 2 + 1] = lh[tid];
+  if (fz.img.img == nullptr) return;
+  __syncthreads();
+  // quantize the G*HD outputs (columns [hq0*HD, (hq0+G)*HD) of the O input row)
+  const int col0 = hq0 * HD;
+  if (fz.img.type == B2_Q4_K || fz.img.type == B2_Q6_K) {
+    // one 256-value unit per warp, 8 values per lane
+    for (int u = warp; u < G * HD / 256; u += blockDim.x / 32) {
+      float v8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v8[j] = ob[u * 256 + lane * 8 + j];
+      int8_t q8[8];
+      int bs = 0;
+      const float d = quant_q8_k_lane(v8, q8, &bs);
+      store_q8k_unit(fz.img, b, col0 / 256 + u, q8, d, bs);
+    }
+  } else {
+    // one 32-value block per thread (ref_quantize_row_q8_0)
+    for (int u = tid; u < G * HD / 32; u += blockDim.x) {
+      float amax = 0.0f;
+      for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(ob[u * 32 + j]));
+      const float d = __fmul_rn(amax, 1.0f / 127.0f);
+      const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+      uint32_t w8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      int sum = 0;
+      for (int j = 0; j < 32; ++j) {
+        const float scv = __fmul_rn(ob[u * 32 + j], id);
+        const float tt = scv >= 0.0f ? __fadd_rn(scv, 0.5f) : __fsub_rn(scv, 0.5f);
+        int qv = __float2int_rz(tt);
+        qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+        sum += qv;
+        w8[j >> 2] |= ((uint32_t)(uint8_t)qv) << (8 * (j & 3));
+      }
+      store_q8_0_block(fz.img, b, col0 / 32 + u, w8, h2f(f2h_rn(d)), sum);
+    }
   }
 }
 
@@ -571,6 +816,18 @@ int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out,
                     status);
 }
 
+bool add_rmsnorm_q_supported(int n, int act_type) {
+  (void)act_type;
+  return n % 256 == 0 && n / 8 <= 1024;
+}
+
+int launch_add_rmsnorm_q(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
+                         const ActImage& img, cudaStream_t s, const PeerIn* in, int* status) {
+  if (!add_rmsnorm_q_supported(n, img.type) || img.kq < n || img.img == nullptr) return B2_ERR_UNSUPPORTED;
+  return launch_pdl(add_rmsnorm_q_kernel, dim3(n_tok), dim3(n / 8), 0, s, x, delta, w, out, n, eps,
+                    in ? *in : PeerIn{}, status, img);
+}
+
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                    const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int n_seq, int cap,
                    cudaStream_t s) {
@@ -580,21 +837,36 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
 
 int attn_splits(int cap) { return (cap + kAttnP - 1) / kAttnP; }
 
+bool attn_fusable(int n_head, int n_kv, int hd, int act_type) {
+  const int G = n_head / n_kv;
+  return (act_type == B2_Q4_K || act_type == B2_Q6_K) ? (G * hd) % 256 == 0 : (G * hd) % 32 == 0;
+}
+
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                      const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* part_o,
-                     float* part_ml, float* out, cudaStream_t s, int* status) {
+                     float* part_ml, float* out, cudaStream_t s, int* status, unsigned int* count,
+                     const ActImage* img) {
   const int G = n_head / n_kv;
   const int n_split = attn_splits(cap);
   const float scale = 1.0f / sqrtf((float)hd);
   const dim3 grid(n_split, n_kv, n_tok);
+  AttnFuse fz;
+  if (count) {
+    fz.count = count;
+    fz.out = out;
+    if (img) {
+      B2_CHECK_ARG(attn_fusable(n_head, n_kv, hd, img->type) && img->img, "attention: image not fusable");
+      fz.img = *img;
+    }
+  }
   int rc = B2_ERR_UNSUPPORTED;
 #define B2_ATTN_CASE(HDV, GV)                                                                                       \
   if (hd == HDV && G == GV) {                                                                                       \
-    const size_t sm = 128 + (size_t)2 * kAttnP * HDV * 2 + (size_t)GV * kAttnP * 4;                                 \
+    const size_t sm = 128 + (size_t)2 * kAttnP * HDV * 2 + (size_t)GV * HDV * 4 + (size_t)GV * kAttnP * 4;          \
     B2_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<HDV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                      (int)sm));                                                                     \
     rc = launch_pdl(attn_chunk_kernel<HDV, GV>, grid, dim3(256), sm, s, q, n_head, n_kv, pos, seq, kc, vc, st,      \
-                    n_seq, cap, scale, part_o, part_ml, n_split, status);                                           \
+                    n_seq, cap, scale, part_o, part_ml, n_split, status, fz);                                       \
   }
   B2_ATTN_CASE(128, 1)
   B2_ATTN_CASE(128, 2)
@@ -609,7 +881,7 @@ int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, co
     set_error("attention: unsupported head_dim %d / group %d", hd, G);
     return rc;
   }
-  if (rc != B2_OK) return rc;
+  if (rc != B2_OK || count) return rc;
   return launch_pdl(attn_combine_kernel, dim3(n_head, n_tok), dim3(hd), 0, s, (const float*)part_o,
                     (const float*)part_ml, n_head, hd, n_split, out);
 }

@@ -8,21 +8,18 @@
 
 namespace b2 {
 
-// Per-sequence KV bookkeeping, read by kernels from device memory (a null
-// state array means every sequence is in the plain layout, slot = position).  Logical
-// position p lives in physical slot p when p < n_keep (the pinned prefix),
-// otherwise in n_keep + (ring_head + p − n_keep) mod (cap − n_keep): the
-// slots after the prefix form a ring, so dropping the oldest positions
-// after the prefix (Milda's KV shift) only advances ring_head.
-struct KvSeqState {
-  int32_t n_keep;
-  int32_t ring_head;
-};
-
 int launch_embed(const int32_t* tokens, int n_tok, int n_vocab, int type, const uint8_t* table, int64_t row_bytes,
                  int n_embd, float* x, cudaStream_t s);
 int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
                        cudaStream_t s, const PeerIn* in = nullptr, int* status = nullptr);
+// Residual add + RMSNorm fused with the next GEMV's activation quantization:
+// writes the normalized rows to `out` (may be null) and their quantized image
+// to `img` (n % 32 == 0, n / 8 <= 1024; n % 256 == 0 for the K-quant images).
+// Returns B2_ERR_UNSUPPORTED for other shapes (callers then use the unfused
+// pair).
+int launch_add_rmsnorm_q(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
+                         const ActImage& img, cudaStream_t s, const PeerIn* in = nullptr, int* status = nullptr);
+bool add_rmsnorm_q_supported(int n, int act_type);
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                    const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int n_seq, int cap,
                    cudaStream_t s);
@@ -35,9 +32,15 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
 // is outside [0, n_seq) or whose position is outside [0, cap) read nothing
 // and produce zero outputs.  st may be null (plain layout).
 int attn_splits(int cap);
+// With `count` ([n_tok][n_kv] zeroed counters, left zeroed) the combine runs
+// in the last CTA of each (query, kv head) instead of a second kernel, and
+// with `img` that CTA also quantizes its outputs into the O projection's
+// activation image (attn_fusable must hold).
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                      const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* part_o,
-                     float* part_ml, float* out, cudaStream_t s, int* status = nullptr);
+                     float* part_ml, float* out, cudaStream_t s, int* status = nullptr, unsigned int* count = nullptr,
+                     const ActImage* img = nullptr);
+bool attn_fusable(int n_head, int n_kv, int hd, int act_type);
 // cos/sin pairs of one position delta for every rotated pair (head_dim <= 256).
 constexpr int kRotPairs = 128;
 struct RotTable {

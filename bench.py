@@ -111,6 +111,11 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def progress(msg: str) -> None:
+    """Phase marker on stderr (stdout carries only the JSON line)."""
+    print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def dist_init():
     """torch.distributed plumbing (gloo on the host) when launched by torchrun."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -411,8 +416,10 @@ def run_decode_ours(args, dist, rank, world, local):
     path = model_path("8b_q4k")
     t_write = 0.0
     if rank == 0 and not os.path.exists(path):
+        progress("writing the synthetic 8B GGUF")
         t_write = write_8b(b2, path)
     nccl_id, path = tp_share(dist, rank, world, b2.nccl_unique_id, path)
+    progress("loading")
     barrier(dist)
     t0 = time.perf_counter()
     model = b2.Model(path, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
@@ -421,6 +428,7 @@ def run_decode_ours(args, dist, rank, world, local):
     n_ctx = PROMPT + warm + CLOCK_LOAD_STEPS + args.steps + 8
     ctx = b2.Context(model, n_ctx=n_ctx, n_seq=BATCH)
     prompts = prompts_8b()
+    progress("prefill")
     # Prefill: each prompt through b2_decode (8-token steps), last logits -> first greedy token.
     barrier(dist)
     t0 = time.perf_counter()
@@ -430,6 +438,7 @@ def run_decode_ours(args, dist, rank, world, local):
         first.append(int(ctx.argmax()[0][-1]))
     t_prefill = dist_max(dist, time.perf_counter() - t0)
     seqs = np.arange(BATCH, dtype=np.int32)
+    progress(f"prefill done in {t_prefill:.1f} s; warm-up")
     # Warm-up steps (graph capture on the first), then the state the timed steps start from.
     ids = ctx.generate(first, warm, seq=seqs)
     start_tok = ids[-1].copy()
@@ -441,6 +450,7 @@ def run_decode_ours(args, dist, rank, world, local):
 
     e0, e1 = b2.Event(), b2.Event()
     barrier(dist)
+    progress("timed steps")
     with ClockSampler(local) as clk:
         ctx.generate(start_tok, CLOCK_LOAD_STEPS, seq=seqs)     # untimed load: clocks seen under work
         rewind()
@@ -459,6 +469,7 @@ def run_decode_ours(args, dist, rank, world, local):
 
     # e2e: the llama-style host loop through the C ABI (b2_decode with host
     # token/pos/seq arrays, b2_get_argmax back to the host) from the same state.
+    progress("e2e host loop")
     rewind()
     tok = start_tok.copy()
     e2e_ids = np.empty_like(gen)
@@ -478,6 +489,7 @@ def run_decode_ours(args, dist, rank, world, local):
     step_bytes = decode_weight_bytes(world) + decode_kv_bytes(ctx_lens, world) / args.steps
     step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
     ff_l = c["n_ff"] // world
+    progress("kernel roofline")
     g = time_gemv_shape(b2, b2.Q4_K, 2 * ff_l, c["n_embd"], BATCH, 64, 7)
     del ctx, model
     q40 = gemv_q4_0_measure(b2, 200) if rank == 0 else None
@@ -516,6 +528,7 @@ def run_decode_ours(args, dist, rank, world, local):
     if q40 is not None:
         out["q4_0_gemv"] = q40
     if rank == 0:
+        progress("cpu baseline")
         out["cpu_baseline"] = cpu_decode_baseline(path, args.cpu_seconds)
     barrier(dist)
     if rank == 0 and not args.keep_model:
@@ -780,7 +793,7 @@ def run_gemm_ours(args, dist, rank, world, local):
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
-    if rank == 0:
+    if rank == 0 and args.cpu_seconds > 0:
         nt = os.cpu_count() or 1
         per_tok, n = cpu_gemm_rate(q, x, args.cpu_seconds, None, nt)
         out["cpu_baseline"] = {"value": round(2 * GEMM_N * GEMM_K / per_tok / 1e12, 5), "unit": "TFLOP/s",

@@ -642,8 +642,9 @@ void orc_matmul_dev_strided(int wtype, const void* w, int64_t n_rows, size_t row
 
 /* Split-K decode attention in the device kernels' order: positions in chunks
  * of 128; per chunk and head, the score of a position is eight fmaf chains
- * over hd/8 consecutive dims each (chain i over dims [i·hd/8, (i+1)·hd/8)),
- * combined by the 8-lane butterfly (xor 4, 2, 1), times 1/sqrt(hd); m = the
+ * over hd/8 dims each (chain i over dims [i·B, i·B + B) then
+ * [hd/2 + i·B, hd/2 + i·B + B), B = hd/16), combined by the 8-lane
+ * butterfly (xor 4, 2, 1), times 1/sqrt(hd); m = the
  * chunk max; e = exp_dev(s − m); the chunk sum is ((W0 + W1) + W2) + W3, W_w
  * the 32-lane butterfly (xor 16..1) over positions 32w..32w+31 (0 past the
  * end); P·V per dim keeps four sums a_r of e·v by fmaf over the positions
@@ -661,7 +662,7 @@ static float butterfly(float* v, int n) {
 void orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc, int64_t kv_stride, int n_pos,
                          int n_heads, int n_kv_heads, int hd, float* out) {
     const int G = n_heads / n_kv_heads;
-    const int P = 128, DL = hd / 8;
+    const int P = 128, B = hd / 16;
     const float scale = 1.0f / sqrtf((float)hd);
     const int n_split = (n_pos + P - 1) / P;
     float* sc = (float*)malloc(sizeof(float) * P);
@@ -677,10 +678,13 @@ void orc_attn_decode_dev(const float* q, const uint16_t* kc, const uint16_t* vc,
             float m = -FLT_MAX;
             for (int i = 0; i < n; ++i) {
                 orc_fp16_to_fp32_row(kc + (size_t)(t0 + i) * kv_stride + (size_t)kvh * hd, kt, hd);
+                /* lane l: dims [B*l, B*l+B) then [hd/2 + B*l, hd/2 + B*l + B) */
                 float a[8];
                 for (int l = 0; l < 8; ++l) {
                     a[l] = 0.0f;
-                    for (int d = l * DL; d < (l + 1) * DL; ++d) a[l] = fmaf(qh[d], kt[d], a[l]);
+                    for (int j = 0; j < 2; ++j)
+                        for (int d = j * (hd / 2) + B * l; d < j * (hd / 2) + B * (l + 1); ++d)
+                            a[l] = fmaf(qh[d], kt[d], a[l]);
                 }
                 sc[i] = butterfly(a, 8) * scale;
                 m = fmaxf(m, sc[i]);

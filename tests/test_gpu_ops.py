@@ -105,6 +105,20 @@ def test_gemv_matches_oracle(t, n, k, n_tok):
     assert np.array_equal(_bits(got), _bits(O.gemv_dev(t, q, n, k, x))), "not bit-exact with the device order"
 
 
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("n,k", [(6144, 4096), (2048, 14336)])
+@pytest.mark.parametrize("n_tok", [1, 3, 8])
+def test_gemv_many_items_per_cta(t, n, k, n_tok):
+    """Enough rows that every CTA works several items, so the stage rings wrap
+    many times and the consumer sets run concurrently: bit-exact with the
+    device order."""
+    q = _weights(t, n, k, 41)
+    m = b2.QMatrix(t, q, n, k)
+    x = np.random.default_rng(n + k + n_tok).standard_normal((n_tok, k)).astype(np.float32)
+    got = m.gemv(x)
+    assert np.array_equal(_bits(got), _bits(O.gemv_dev(t, q, n, k, x))), "not bit-exact with the device order"
+
+
 def test_gemv_config1_q4_0_4096():
     """Q4_0 GEMV 4096x4096, batch 1: W N(0,0.02) seed 0, x N(0,1) seed 1."""
     n = k = 4096
