@@ -605,11 +605,12 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     }
     // Fused: the attention's last CTAs combine the chunks and quantize the O
     // projection's input image.
-    const bool fuse_o = fuse && attn_fusable(m->nh_l, m->nkv_l, hd, L.wo.m.type);
+    const bool fuse_attn = fuse && attn_combine_fusable(m->nh_l, m->nkv_l, hd, c->n_ctx);
+    const bool fuse_o = fuse_attn && attn_fusable(m->nh_l, m->nkv_l, hd, L.wo.m.type);
     const ActImage o_img = gemv_act_image(L.wo.m, n, c->act_img);
     if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->vc[l], c->st_d,
                                c->n_seq, c->n_ctx, c->part_o, c->part_ml, c->att, s, c->status,
-                               fuse ? c->attn_cnt : nullptr, fuse_o ? &o_img : nullptr)))
+                               fuse_attn ? c->attn_cnt : nullptr, fuse_o ? &o_img : nullptr)))
       return rc;
     if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
     {

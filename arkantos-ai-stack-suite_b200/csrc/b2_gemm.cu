@@ -17,20 +17,30 @@
 // reference's own sequence per super-block with explicitly rounded fp32
 // operations, so Y is bit-identical to the reference-order CPU matmul.
 //
-// Structure (one CTA per 128 weight rows x 64 tokens, 10 warps):
+// Structure (one CTA per 128 weight rows x 64 tokens, 18 warps):
 //   warp 0   TMA producer: per super-block the 16 Q4_K row tiles (1-D bulk
 //            copies of the tile layout), the four 64-k activation sub-tiles
 //            and the msum operand; the tile's activation scales once.
-//   warp 1   allocates TMEM (512 columns: two buffers of isum-half-0,
-//            isum-half-1, msum x 64 tokens) and issues the MMAs from one
-//            thread; tcgen05.commit releases operand stages and hands a
-//            finished super-block to the epilogue.
-//   warps 2-5  dequantize one row each into canonical K-major fp16 tiles
-//            (8x8 core matrices, no swizzle) and publish d, dmin.
-//   warps 6-9  epilogue: tcgen05.ld of their 32 TMEM lanes (rows), the
-//            per-super-block fp32 update for 64 tokens in registers, then Y.
+//   warp 1   allocates TMEM (512 columns: two accumulator buffers of
+//            isum-half-0 | isum-half-1 | msum x 64 tokens, a ring of three A
+//            sub-tiles and two msum A operands) and issues the MMAs from one
+//            thread, A from TMEM and B from shared memory (128-byte swizzled);
+//            tcgen05.commit releases stages and hands a finished super-block
+//            to the epilogue.
+//   warps 2-9  dequantize: warp w serves TMEM lanes 32*(w%4).. (one weight
+//            row per lane) and k-half (w-2)/4 of every 64-k sub-step; the
+//            values sc*q are formed with integer ops and one packed fp16
+//            subtract (1024 + v, exact below 1024) and stored into the A ring
+//            with tcgen05.st; they also publish d, dmin and the msum operand.
+//   warps 10-17  epilogue: warp w reads TMEM lanes 32*(w%4).. (rows) for
+//            token half (w-10)/4 and keeps the per-super-block fp32 update
+//            for its 32 tokens in registers (scalar, explicitly rounded
+//            operations), then Y.
 // Every wait is bounded; an expired wait records a status code and the
 // thread proceeds (results are then garbage, the kernel still ends).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "b2_common.cuh"
 #include "b2_quant.cuh"
 
@@ -40,15 +50,20 @@ namespace {
 constexpr int kMT = 128;            // weight rows per CTA (MMA M)
 constexpr int kNT = 64;             // tokens per CTA (MMA N)
 constexpr int kSubK = 64;           // k per A/B sub-tile (4 MMAs of K=16)
-constexpr int kRaw = 3, kARing = 4, kBRing = 4;
+constexpr int kRaw = 4, kARing = 3, kBGroups = 3;   // B ring: groups of the 4 sub-tiles of a super-block
 constexpr int kRawStage = 16 * 1152;          // 16 eight-row Q4_K tiles, one super-block
-constexpr int kASub = kMT * kSubK * 2;        // 16 KB
-constexpr int kBSub = kNT * kSubK * 2;        // 8 KB
-constexpr int kAm = kMT * 16 * 2;             // 4 KB
+constexpr int kBSub = kNT * kSubK * 2;        // 8 KB: 64 token rows x 128 B, 128-byte swizzled
+constexpr int kBGroup = 4 * kBSub;            // one super-block of B sub-tiles, one copy
+
 constexpr int kBm = kNT * 16 * 2;             // 2 KB
-constexpr int kThreads = 10 * 32;
+constexpr int kDqWarps = 8, kEpWarps = 8;
+constexpr int kThreads = (2 + kDqWarps + kEpWarps) * 32;
+constexpr int kDqThreads = kDqWarps * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kBufCols = 192;                 // isum0 | isum1 | msum, 64 columns each
+constexpr int kAcols = 32;                    // one A sub-tile in TMEM: 128 lanes x 64 fp16
+constexpr int kAcol0 = 2 * kBufCols;          // the A ring after the two accumulator buffers
+constexpr int kAmCol0 = kAcol0 + kARing * kAcols;   // two msum A operands (8 columns each)
 
 struct GemmP {
   const uint8_t* w;          // Q4_K tile layout
@@ -75,33 +90,91 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   d |= (uint64_t)1 << 46;   // descriptor version (sm_100)
   return d;                 // base offset 0, lbo mode 0, layout type 0 (no swizzle)
 }
+// K-major, 128-byte swizzle: rows of 128 bytes (64 fp16 of k), 16-byte chunk
+// c of row n stored at chunk c ^ (n % 8); 8-row groups 1024 bytes apart
+// (SBO); the atom starts 1024-byte aligned.  A K=16 step advances the start
+// address by 32 bytes (the hardware applies the swizzle to the address).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                    // LBO (unused for swizzled K-major): 16 bytes
+  d |= (uint64_t)(1024 >> 4) << 32;          // SBO: 8 rows x 128 bytes
+  d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                    // layout type: 128-byte swizzle
+  return d;
+}
+// Byte offset of (row n, k) in a 128-byte-swizzled K-major tile of 64-wide k.
+__host__ __device__ __forceinline__ uint32_t sw128_offset(int n, int k) {
+  return (uint32_t)n * 128u + ((uint32_t)((k >> 3) ^ (n & 7)) << 4) + (uint32_t)(k & 7) * 2u;
+}
+
 // Instruction descriptor: kind::f16, A and B fp16 K-major, D fp32, M=128, N=kNT.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kNT >> 3) << 17) |
                             ((uint32_t)(kMT >> 4) << 24);
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
-}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+// TMEM loads and stores are asynchronous on their registers until the
+// matching wait: each helper issues the access and its wait in one asm block,
+// so no register can be read or reused in between.
+// Three 8-column loads (isum0, isum1, msum of 8 tokens) of this warp's lanes.
+__device__ __forceinline__ void tmem_ld8x3(uint32_t t0, uint32_t t1, uint32_t t2, uint32_t (&a)[8], uint32_t (&b)[8],
+                                           uint32_t (&c)[8]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%24];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%25];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%26];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]),
+        "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]),
+        "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7])
+      : "r"(t0), "r"(t1), "r"(t2)
+      : "memory");
 }
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 8 columns of this warp's lanes, completed before return.
+__device__ __forceinline__ void tmem_st8_sync(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+// 16 columns of this warp's lanes, completed before return.
+__device__ __forceinline__ void tmem_st16_sync(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+// D = A x B with A from TMEM (128 lanes = rows, K=16 fp16 in 8 columns), B from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %3, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p;\n\t}\n"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(accumulate), "r"(kIdesc));
+}
+
+// Four 4-bit values (the low nibbles of the bytes of w) times sc as two
+// fp16x2 words: each 16-bit lane gets 0x6400 + n*sc = fp16(1024 + n*sc)
+// (exact, n*sc <= 945 < 1024), minus 1024 in fp16 = fp16(n*sc) exactly.
+__device__ __forceinline__ void nib4_to_h2(uint32_t w, uint32_t sc, uint32_t& h01, uint32_t& h23) {
+  const uint32_t m = w & 0x0F0F0F0Fu;
+  const uint32_t x0 = __byte_perm(m, 0u, 0x4140) * sc + 0x64006400u;   // bytes 0, 1 -> 16-bit lanes
+  const uint32_t x1 = __byte_perm(m, 0u, 0x4342) * sc + 0x64006400u;   // bytes 2, 3
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const __half2 r0 = __hsub2(*reinterpret_cast<const __half2*>(&x0), k1024);
+  const __half2 r1 = __hsub2(*reinterpret_cast<const __half2*>(&x1), k1024);
+  h01 = *reinterpret_cast<const uint32_t*>(&r0);
+  h23 = *reinterpret_cast<const uint32_t*>(&r1);
+}
 
 // Ring wait helpers: the n-th use (n >= 0) of a slot waits for parity n & 1
 // of its full barrier; a producer's n-th refill (n >= 1) waits for parity
@@ -119,6 +192,16 @@ __device__ __forceinline__ bool wait_full(uint64_t* bar, int64_t use, int* statu
 }
 __device__ __forceinline__ bool wait_empty(uint64_t* bar, int64_t use, int* status, int code, int* abort_flag) {
   return use == 0 || ring_wait(bar, (uint32_t)((use - 1) & 1), status, code, abort_flag);
+}
+
+// 3-D tiled TMA load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -151,7 +234,7 @@ __global__ void gemm_act_kernel(const float* __restrict__ x, int64_t x_stride, i
     const int tt = t / kNT, tr = t % kNT;
     // codes: k = sb*256 + 8*lane .. +7 -> sub-tile sb*4 + lane/8, k block lane%8
     uint8_t* bsub = bimg + ((int64_t)tt * nss + sb * 4 + lane / 8) * kBSub;
-    *reinterpret_cast<uint4*>(bsub + (tr / 8) * 1024 + (lane % 8) * 128 + (tr % 8) * 16) =
+    *reinterpret_cast<uint4*>(bsub + sw128_offset(tr, (lane % 8) * 8)) =
         make_uint4(pack_h2(q[0], q[1]), pack_h2(q[2], q[3]), pack_h2(q[4], q[5]), pack_h2(q[6], q[7]));
     // msum operand: bsum_j (32 values) = 64*bh + bl, bl in [0, 64)
     const int b32 = bs + __shfl_xor_sync(0xffffffffu, bs, 2);
@@ -167,17 +250,19 @@ __global__ void gemm_act_kernel(const float* __restrict__ x, int64_t x_stride, i
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+__global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p, const __grid_constant__ CUtensorMap wmap) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // the B ring needs 1024-byte alignment (128-byte swizzle atoms)
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int nsb = p.nu;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* raw_full = bars;                 // [3]
-  uint64_t* raw_empty = raw_full + kRaw;     // [3]
-  uint64_t* a_full = raw_empty + kRaw;       // [4]
-  uint64_t* a_empty = a_full + kARing;       // [4]
-  uint64_t* b_full = a_empty + kARing;       // [4]
-  uint64_t* b_empty = b_full + kBRing;       // [4]
-  uint64_t* am_full = b_empty + kBRing;      // [2]
+  uint64_t* raw_full = bars;                 // [kRaw]
+  uint64_t* raw_empty = raw_full + kRaw;     // [kRaw]
+  uint64_t* a_full = raw_empty + kRaw;       // [kARing]  A sub-tile written into TMEM
+  uint64_t* a_empty = a_full + kARing;       // [kARing]  ... and read by its MMAs
+  uint64_t* b_full = a_empty + kARing;       // [kBGroups]
+  uint64_t* b_empty = b_full + kBGroups;     // [kBGroups]
+  uint64_t* am_full = b_empty + kBGroups;    // [2]
   uint64_t* am_empty = am_full + 2;          // [2]
   uint64_t* bm_full = am_empty + 2;          // [2]
   uint64_t* bm_empty = bm_full + 2;          // [2]
@@ -189,11 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
   uint64_t* mma_done = dx_bar + 1;           // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 496);
   int* abort_flag = reinterpret_cast<int*>(smem + 500);
-  uint8_t* raw = smem + 512;
-  uint8_t* As = raw + kRaw * kRawStage;
-  uint8_t* Bs = As + kARing * kASub;
-  uint8_t* Ams = Bs + kBRing * kBSub;
-  uint8_t* Bms = Ams + 2 * kAm;
+  uint8_t* Bs = smem + 1024;
+  uint8_t* raw = Bs + kBGroups * kBGroup;
+  uint8_t* Bms = raw + kRaw * kRawStage;
   float* scl = reinterpret_cast<float*>(Bms + 2 * kBm);      // [2][128][2] d, dmin
   float* dxs = scl + 2 * kMT * 2;                             // [nsb][64]
 
@@ -207,25 +290,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRaw; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 128);
+      mbar_init(&raw_empty[i], kDqThreads);
     }
     for (int i = 0; i < kARing; ++i) {
-      mbar_init(&a_full[i], 128);
+      mbar_init(&a_full[i], kDqThreads);
       mbar_init(&a_empty[i], 1);
     }
-    for (int i = 0; i < kBRing; ++i) {
+    for (int i = 0; i < kBGroups; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&am_full[i], 128);
+      mbar_init(&am_full[i], kDqThreads);
       mbar_init(&am_empty[i], 1);
       mbar_init(&bm_full[i], 1);
       mbar_init(&bm_empty[i], 1);
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
-      mbar_init(&sc_full[i], 128);
-      mbar_init(&sc_empty[i], 128);
+      mbar_init(&acc_empty[i], kEpWarps * 32);
+      mbar_init(&sc_full[i], kDqThreads);
+      mbar_init(&sc_empty[i], kEpWarps * 32);
     }
     mbar_init(dx_bar, 1);
     mbar_init(mma_done, 1);
@@ -254,25 +337,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
       for (int s = 0; s < nsb; ++s) {
         const int rs = s % kRaw;
         if (!wait_empty(&raw_empty[rs], s / kRaw, p.status, 20, abort_flag)) break;
-        mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(tiles_here * 1152));
-        // unit s of tile t: slot (i = s % L) * S + (w = s / L) of the tile layout
+        // unit s of the CTA's 16 tiles: slot (i = s % L) * S + (w = s / L), one 3-D copy
+        // (tiles past the matrix are zero-filled and still counted)
+        mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)kRawStage);
         const int wr = s / p.L, ii = s - wr * p.L;
-        for (int t = 0; t < tiles_here; ++t)
-          bulk_g2s(raw + rs * kRawStage + t * 1152,
-                   p.w + (int64_t)(tile0 + t) * p.tile_bytes + (int64_t)(ii * p.S + wr) * p.slot_bytes, 1152,
-                   &raw_full[rs]);
+        tma_load_3d(raw + rs * kRawStage, &wmap, 0, ii * p.S + wr, tile0, &raw_full[rs]);
         ++n_raw;
-        bool ok = true;
-        for (int ss = 0; ss < 4 && ok; ++ss) {
-          const int idx = s * 4 + ss, bsl = idx % kBRing;
-          ok = wait_empty(&b_empty[bsl], idx / kBRing, p.status, 21, abort_flag);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&b_full[bsl], kBSub);
-          bulk_g2s(Bs + bsl * kBSub, p.bimg + ((int64_t)tok_tile * nsb * 4 + idx) * kBSub, kBSub, &b_full[bsl]);
-          ++n_b;
-        }
+        const int bg = s % kBGroups;
+        if (!wait_empty(&b_empty[bg], s / kBGroups, p.status, 21, abort_flag)) break;
+        mbar_arrive_expect_tx(&b_full[bg], kBGroup);
+        bulk_g2s(Bs + bg * kBGroup, p.bimg + ((int64_t)tok_tile * nsb * 4 + s * 4) * kBSub, kBGroup, &b_full[bg]);
+        ++n_b;
         const int ms = s % 2;
-        if (!ok || !wait_empty(&bm_empty[ms], s / 2, p.status, 22, abort_flag)) break;
+        if (!wait_empty(&bm_empty[ms], s / 2, p.status, 22, abort_flag)) break;
         mbar_arrive_expect_tx(&bm_full[ms], kBm);
         bulk_g2s(Bms + ms * kBm, p.bmimg + ((int64_t)tok_tile * nsb + s) * kBm, kBm, &bm_full[ms]);
         ++n_bm;
@@ -281,7 +358,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
       // last phase of each ring slot (immediate when the consumers saw them).
       mbar_wait_bounded(dx_bar, 0, p.status, 23);
       for (int u = max(0, n_raw - kRaw); u < n_raw; ++u) mbar_wait_bounded(&raw_full[u % kRaw], (u / kRaw) & 1, p.status, 23);
-      for (int u = max(0, n_b - kBRing); u < n_b; ++u) mbar_wait_bounded(&b_full[u % kBRing], (u / kBRing) & 1, p.status, 23);
+      for (int u = max(0, n_b - kBGroups); u < n_b; ++u)
+        mbar_wait_bounded(&b_full[u % kBGroups], (u / kBGroups) & 1, p.status, 23);
       for (int u = max(0, n_bm - 2); u < n_bm; ++u) mbar_wait_bounded(&bm_full[u % 2], (u / 2) & 1, p.status, 23);
     }
   } else if (warp == 1) {
@@ -291,29 +369,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
         const int b = s & 1;
         if (!wait_empty(&acc_empty[b], s / 2, p.status, 30, abort_flag)) break;
         tc_fence_after();
-        bool ok = true;
-        for (int ss = 0; ss < 4; ++ss) {
-          const int idx = s * 4 + ss, asl = idx % kARing, bsl = idx % kBRing;
-          ok = wait_full(&a_full[asl], idx / kARing, p.status, 31, abort_flag) &&
-               wait_full(&b_full[bsl], idx / kBRing, p.status, 32, abort_flag);
+        const int bg = s % kBGroups;
+        bool ok = wait_full(&b_full[bg], s / kBGroups, p.status, 32, abort_flag);
+        for (int ss = 0; ss < 4 && ok; ++ss) {
+          const int idx = s * 4 + ss, asl = idx % kARing;
+          ok = wait_full(&a_full[asl], idx / kARing, p.status, 31, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t acc = tmem + b * kBufCols + (ss / 2) * kNT;
-          const uint32_t abase = smem_u32(As + asl * kASub), bbase = smem_u32(Bs + bsl * kBSub);
+          const uint32_t abase = tmem + kAcol0 + asl * kAcols, bbase = smem_u32(Bs + bg * kBGroup + ss * kBSub);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(acc, smem_desc(abase + kk * 256, 128, 1024), smem_desc(bbase + kk * 256, 128, 1024),
-                     ((ss & 1) | kk) != 0);
+            umma_f16_ts(acc, abase + kk * 8, smem_desc_sw128(bbase + kk * 32), ((ss & 1) | kk) != 0);
           umma_commit(&a_empty[asl]);
-          umma_commit(&b_empty[bsl]);
         }
+        if (ok) umma_commit(&b_empty[bg]);
         const int ms = s % 2;
         if (!ok || !wait_full(&am_full[ms], s / 2, p.status, 33, abort_flag) ||
             !wait_full(&bm_full[ms], s / 2, p.status, 34, abort_flag))
           break;
         tc_fence_after();
-        umma_f16(tmem + b * kBufCols + 2 * kNT, smem_desc(smem_u32(Ams + ms * kAm), 128, 256),
-                 smem_desc(smem_u32(Bms + ms * kBm), 128, 256), 0u);
+        umma_f16_ts(tmem + b * kBufCols + 2 * kNT, tmem + kAmCol0 + ms * 8, smem_desc(smem_u32(Bms + ms * kBm), 128, 256),
+                    0u);
         umma_commit(&am_empty[ms]);
         umma_commit(&bm_empty[ms]);
         umma_commit(&acc_full[b]);
@@ -322,11 +399,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
       umma_commit(mma_done);
       mbar_wait_bounded(mma_done, 0, p.status, 35);
     }
-  } else if (warp < 6) {
-    // ---------------- dequantize: thread = one weight row ----------------
-    const int r = (warp - 2) * 32 + lane;
+  } else if (warp < 2 + kDqWarps) {
+    // ---------------- dequantize: lane = weight row of the warp's TMEM lane quarter ----------------
+    const int qd = warp & 3, kh = (warp - 2) >> 2;   // lane quarter, k-half of each sub-step
+    const int r = qd * 32 + lane;
     const int tl = r >> 3, g = r & 7;
     const bool live = r0 + r < p.n_rows;
+    const uint32_t tlane = (uint32_t)(qd * 32) << 16;
     for (int s = 0; s < nsb; ++s) {
       const int rs = s % kRaw;
       wait_full(&raw_full[rs], s / kRaw, p.status, 40, abort_flag);
@@ -364,50 +443,54 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
       // d, dmin for the epilogue
       const int sl2 = s % 2;
       wait_empty(&sc_empty[sl2], s / 2, p.status, 41, abort_flag);
-      scl[(sl2 * kMT + r) * 2] = h2f((uint16_t)(dd & 0xFFFFu));
-      scl[(sl2 * kMT + r) * 2 + 1] = h2f((uint16_t)(dd >> 16));
+      if (kh == 0) {
+        scl[(sl2 * kMT + r) * 2] = h2f((uint16_t)(dd & 0xFFFFu));
+        scl[(sl2 * kMT + r) * 2 + 1] = h2f((uint16_t)(dd >> 16));
+      }
       mbar_arrive(&sc_full[sl2]);
-      // A sub-tiles: sub-step ss = qs chunk pair ss: k 0..31 low nibbles (scale
-      // sc[2ss]), k 32..63 high nibbles (scale sc[2ss+1]) of its 32 bytes
+      // A sub-tile ss (k 64ss..64ss+63 of the super-block) = qs bytes
+      // 32ss..32ss+31: k-half 0 the low nibbles (scale sc[2ss]), k-half 1 the
+      // high nibbles (sc[2ss+1]); 16 TMEM columns of fp16 pairs per half.
 #pragma unroll
       for (int ss = 0; ss < 4; ++ss) {
         const int idx = s * 4 + ss, asl = idx % kARing;
-        wait_empty(&a_empty[asl], idx / kARing, p.status, 42, abort_flag);
-        uint8_t* arow = As + asl * kASub + (r >> 3) * 1024 + (r & 7) * 16;
+        const uint32_t scv = (uint32_t)sc[2 * ss + kh];
+        uint32_t h[16];
 #pragma unroll
-        for (int kb = 0; kb < 8; ++kb) {
-          const int hi = kb >> 2, scv = sc[2 * ss + hi];
-          const uint32_t w0 = qw[8 * ss + 2 * (kb & 3)], w1 = qw[8 * ss + 2 * (kb & 3) + 1];
-          const uint32_t n0 = hi ? (w0 >> 4) & 0x0F0F0F0Fu : w0 & 0x0F0F0F0Fu;
-          const uint32_t n1 = hi ? (w1 >> 4) & 0x0F0F0F0Fu : w1 & 0x0F0F0F0Fu;
-          uint4 o;
-          o.x = pack_h2((float)(((n0 >> 0) & 0xFF) * scv), (float)(((n0 >> 8) & 0xFF) * scv));
-          o.y = pack_h2((float)(((n0 >> 16) & 0xFF) * scv), (float)(((n0 >> 24) & 0xFF) * scv));
-          o.z = pack_h2((float)(((n1 >> 0) & 0xFF) * scv), (float)(((n1 >> 8) & 0xFF) * scv));
-          o.w = pack_h2((float)(((n1 >> 16) & 0xFF) * scv), (float)(((n1 >> 24) & 0xFF) * scv));
-          *reinterpret_cast<uint4*>(arow + kb * 128) = o;
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t w = kh ? (qw[8 * ss + i] >> 4) : qw[8 * ss + i];
+          nib4_to_h2(w, scv, h[2 * i], h[2 * i + 1]);
         }
-        fence_async_smem();
+        wait_empty(&a_empty[asl], idx / kARing, p.status, 42, abort_flag);
+        tc_fence_after();
+        tmem_st16_sync(tmem + tlane + kAcol0 + asl * kAcols + kh * 16, h);
+        tc_fence_before();
         mbar_arrive(&a_full[asl]);
       }
       // msum operand: (m_0..m_7 | m_0..m_7)
       const int ms = s % 2;
       wait_empty(&am_empty[ms], s / 2, p.status, 43, abort_flag);
-      uint8_t* am = Ams + ms * kAm + (r >> 3) * 256 + (r & 7) * 16;
-      const uint4 mv = make_uint4(pack_h2((float)mn[0], (float)mn[1]), pack_h2((float)mn[2], (float)mn[3]),
-                                  pack_h2((float)mn[4], (float)mn[5]), pack_h2((float)mn[6], (float)mn[7]));
-      *reinterpret_cast<uint4*>(am) = mv;
-      *reinterpret_cast<uint4*>(am + 128) = mv;
-      fence_async_smem();
+      if (kh == 0) {   // warp-uniform: warps 2-5 store the 8 columns of their lanes
+        uint32_t mv[8];
+        mv[0] = mv[4] = pack_h2((float)mn[0], (float)mn[1]);
+        mv[1] = mv[5] = pack_h2((float)mn[2], (float)mn[3]);
+        mv[2] = mv[6] = pack_h2((float)mn[4], (float)mn[5]);
+        mv[3] = mv[7] = pack_h2((float)mn[6], (float)mn[7]);
+        tc_fence_after();
+        tmem_st8_sync(tmem + tlane + kAmCol0 + ms * 8, mv);
+        tc_fence_before();
+      }
       mbar_arrive(&am_full[ms]);
     }
   } else {
-    // ---------------- epilogue: thread = one weight row (TMEM lane) ----------------
+    // ---------------- epilogue: thread = one weight row (TMEM lane), 32 of the 64 tokens ----------------
+    constexpr int NE = kNT / 2;                // tokens per epilogue thread
     const int qt = warp & 3;                   // TMEM lane quarter of this warp
+    const int eh = (warp - 2 - kDqWarps) >> 2; // token half
     const int r = qt * 32 + lane;
-    float out[kNT];
+    float2 out[NE / 2];
 #pragma unroll
-    for (int t = 0; t < kNT; ++t) out[t] = 0.0f;
+    for (int t = 0; t < NE / 2; ++t) out[t] = make_float2(0.0f, 0.0f);
     ring_wait(dx_bar, 0, p.status, 50, abort_flag);
     for (int s = 0; s < nsb; ++s) {
       const int b = s & 1, sl2 = s % 2;
@@ -416,23 +499,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
       wait_full(&sc_full[sl2], s / 2, p.status, 52, abort_flag);
       const float d = scl[(sl2 * kMT + r) * 2], dmin = scl[(sl2 * kMT + r) * 2 + 1];
       mbar_arrive(&sc_empty[sl2]);
-      const uint32_t tbase = tmem + ((uint32_t)(qt * 32) << 16) + b * kBufCols;
+      const uint32_t tbase = tmem + ((uint32_t)(qt * 32) << 16) + b * kBufCols + eh * NE;
+      const float2* dx2 = reinterpret_cast<const float2*>(dxs + s * kNT + eh * NE);
+      // 8 tokens per step
 #pragma unroll
-      for (int c = 0; c < kNT / 16; ++c) {
-        uint32_t a0[16], a1[16], am[16];
-        tmem_ld16(tbase + c * 16, a0);
-        tmem_ld16(tbase + kNT + c * 16, a1);
-        tmem_ld16(tbase + 2 * kNT + c * 16, am);
-        tmem_ld_wait();
+      for (int c = 0; c < NE / 8; ++c) {
+        uint32_t a0[8], a1[8], am[8];
+        tmem_ld8x3(tbase + c * 8, tbase + kNT + c * 8, tbase + 2 * kNT + c * 8, a0, a1, am);
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const float dx = dxs[s * kNT + c * 16 + t];
-          const float isum = __fadd_rn(__uint_as_float(a0[t]), __uint_as_float(a1[t]));
-          const float msum = __uint_as_float(am[t]);
-          float o = out[c * 16 + t];
-          o = __fadd_rn(o, __fmul_rn(__fmul_rn(d, dx), isum));
-          o = __fsub_rn(o, __fmul_rn(__fmul_rn(dmin, dx), msum));
-          out[c * 16 + t] = o;
+        for (int t = 0; t < 4; ++t) {
+          const float2 dx = dx2[c * 4 + t];
+          const float i0 = __fadd_rn(__uint_as_float(a0[2 * t]), __uint_as_float(a1[2 * t]));
+          const float i1 = __fadd_rn(__uint_as_float(a0[2 * t + 1]), __uint_as_float(a1[2 * t + 1]));
+          float2 o = out[c * 4 + t];
+          o.x = __fadd_rn(o.x, __fmul_rn(__fmul_rn(d, dx.x), i0));
+          o.y = __fadd_rn(o.y, __fmul_rn(__fmul_rn(d, dx.y), i1));
+          o.x = __fsub_rn(o.x, __fmul_rn(__fmul_rn(dmin, dx.x), __uint_as_float(am[2 * t])));
+          o.y = __fsub_rn(o.y, __fmul_rn(__fmul_rn(dmin, dx.y), __uint_as_float(am[2 * t + 1])));
+          out[c * 4 + t] = o;
         }
       }
       tc_fence_before();
@@ -441,9 +525,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
     const int64_t row = r0 + r;
     if (row < p.n_rows) {
 #pragma unroll
-      for (int t = 0; t < kNT; ++t) {
-        const int tok = tok_tile * kNT + t;
-        if (tok < p.n_tok) p.y[(int64_t)tok * p.n_rows + row] = out[t];
+      for (int t = 0; t < NE / 2; ++t) {
+        const int tok = tok_tile * kNT + eh * NE + 2 * t;
+        if (tok < p.n_tok) p.y[(int64_t)tok * p.n_rows + row] = out[t].x;
+        if (tok + 1 < p.n_tok) p.y[(int64_t)(tok + 1) * p.n_rows + row] = out[t].y;
       }
     }
   }
@@ -456,8 +541,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p) {
 }
 
 size_t gemm_smem_bytes(int nsb) {
-  return 512 + (size_t)kRaw * kRawStage + (size_t)kARing * kASub + (size_t)kBRing * kBSub + 2 * kAm + 2 * kBm +
+  return 1024 + 1024 + (size_t)kBGroups * kBGroup + (size_t)kRaw * kRawStage + 2 * kBm +
          (size_t)2 * kMT * 2 * 4 + (size_t)nsb * kNT * 4;
+}
+
+// The weight tensor map: the tile layout as [tiles][slots][144 x 8 bytes],
+// boxes of 16 tiles x 1 slot (one super-block of a CTA's 128 rows).
+int make_weight_map(const QMatrix& w, CUtensorMap* map) {
+  static PFN_cuTensorMapEncodeTiled encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) != cudaSuccess || !fn) {
+      set_error("gemm: cuTensorMapEncodeTiled unavailable");
+      return B2_ERR_CUDA;
+    }
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+  }
+  const cuuint64_t dims[3] = {144, (cuuint64_t)w.splits * w.ulen, (cuuint64_t)w.n_tiles};
+  const cuuint64_t strides[2] = {(cuuint64_t)w.slot_bytes, (cuuint64_t)w.tile_bytes};
+  const cuuint32_t box[3] = {144, 1, kMT / 8};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(w.data), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("gemm: weight tensor map rejected (CUresult %d)", (int)r);
+    return B2_ERR_CUDA;
+  }
+  return B2_OK;
 }
 
 }  // namespace
@@ -524,7 +636,10 @@ int launch_gemm(const QMatrix& w, const float* x, int64_t x_stride, int n_tok, f
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_q4k_kernel, p));
+  CUtensorMap wmap;
+  const int mrc = make_weight_map(w, &wmap);
+  if (mrc) return mrc;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_q4k_kernel, p, wmap));
   return B2_OK;
 }
 

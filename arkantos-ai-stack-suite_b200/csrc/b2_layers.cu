@@ -560,24 +560,46 @@ __global__ void __launch_bounds__(256, 3) attn_chunk_kernel(const float* __restr
   __syncthreads();
   if (!last_cta) return;
   __threadfence();
-  float* ob = reinterpret_cast<float*>(smem + 128);   // [G][HD] outputs of this kv head
+  // Chunk weights e_c = exp(m_c − M) per head (staged once), L = Σ_c e_c·l_c
+  // in chunk order, then out[d] = (Σ_c e_c·O_c[d]) · (1/L) — attn_combine's
+  // arithmetic, with the partials read from L2 eight chunks at a time.
+  float* ec = reinterpret_cast<float*>(smem + 128);   // [G][n_split] (0: chunk attended to nothing)
+  float* ob = ec + G * n_split;                        // [G][HD] outputs of this kv head
+  __shared__ float inv_l[G];
+  if (warp < G) {
+    const float* ml = part_ml + ((int64_t)b * n_head + hq0 + warp) * n_split * 2;
+    float M = -FLT_MAX;
+    for (int c = lane; c < n_split; c += 32) M = fmaxf(M, __ldcg(ml + 2 * c));
+    M = warp_max(M);
+    for (int c = lane; c < n_split; c += 32) {
+      const float lc = __ldcg(ml + 2 * c + 1);
+      ec[warp * n_split + c] = lc > 0.0f ? b2_expf(__fsub_rn(__ldcg(ml + 2 * c), M)) : 0.0f;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float L = 0.0f;
+      for (int c = 0; c < n_split; ++c) {
+        const float lc = __ldcg(ml + 2 * c + 1);
+        if (lc > 0.0f) L = __fadd_rn(L, __fmul_rn(ec[warp * n_split + c], lc));
+      }
+      inv_l[warp] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;   // L == 0: a query that attended to nothing
+    }
+  }
+  __syncthreads();
   for (int hd2 = tid; hd2 < G * HD; hd2 += blockDim.x) {
     const int h = hd2 / HD, d = hd2 - h * HD;
-    const float* ml = part_ml + ((int64_t)b * n_head + hq0 + h) * n_split * 2;
-    const float* pq = part_o + ((int64_t)b * n_head + hq0 + h) * n_split * HD;
-    float M = -FLT_MAX;
-    for (int c = 0; c < n_split; ++c) M = fmaxf(M, __ldcg(ml + 2 * c));
-    float L = 0.0f, v = 0.0f;
-    for (int c = 0; c < n_split; ++c) {
-      const float lc = __ldcg(ml + 2 * c + 1);
-      if (lc > 0.0f) {
-        const float ec = b2_expf(__fsub_rn(__ldcg(ml + 2 * c), M));
-        L = __fadd_rn(L, __fmul_rn(ec, lc));
-        v = __fadd_rn(v, __fmul_rn(ec, __ldcg(pq + (int64_t)c * HD + d)));
-      }
+    const float* pq = part_o + ((int64_t)b * n_head + hq0 + h) * n_split * HD + d;
+    const float* eh = ec + h * n_split;
+    float v = 0.0f;
+    for (int c0 = 0; c0 < n_split; c0 += 8) {
+      float pv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pv[j] = c0 + j < n_split ? __ldcg(pq + (int64_t)(c0 + j) * HD) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j < n_split && eh[c0 + j] != 0.0f) v = __fadd_rn(v, __fmul_rn(eh[c0 + j], pv[j]));
     }
-    const float invL = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;   // L == 0: a query that attended to nothing
-    const float o = __fmul_rn(v, invL);
+    const float o = __fmul_rn(v, inv_l[h]);
     fz.out[((int64_t)b * n_head + hq0 + h) * HD + d] = o;
     ob[hd2] = o;
   }
@@ -837,6 +859,13 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
 
 int attn_splits(int cap) { return (cap + kAttnP - 1) / kAttnP; }
 
+// The fused combine stages G*n_split chunk weights and G*hd outputs in the
+// K buffer of the last CTA.
+bool attn_combine_fusable(int n_head, int n_kv, int hd, int cap) {
+  const int G = n_head / n_kv;
+  return (size_t)G * (attn_splits(cap) + hd) * 4 <= (size_t)kAttnP * hd * 2;
+}
+
 bool attn_fusable(int n_head, int n_kv, int hd, int act_type) {
   const int G = n_head / n_kv;
   return (act_type == B2_Q4_K || act_type == B2_Q6_K) ? (G * hd) % 256 == 0 : (G * hd) % 32 == 0;
@@ -851,6 +880,7 @@ int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, co
   const float scale = 1.0f / sqrtf((float)hd);
   const dim3 grid(n_split, n_kv, n_tok);
   AttnFuse fz;
+  B2_CHECK_ARG(!count || attn_combine_fusable(n_head, n_kv, hd, cap), "attention: combine not fusable");
   if (count) {
     fz.count = count;
     fz.out = out;

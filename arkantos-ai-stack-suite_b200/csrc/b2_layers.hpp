@@ -35,11 +35,12 @@ int attn_splits(int cap);
 // With `count` ([n_tok][n_kv] zeroed counters, left zeroed) the combine runs
 // in the last CTA of each (query, kv head) instead of a second kernel, and
 // with `img` that CTA also quantizes its outputs into the O projection's
-// activation image (attn_fusable must hold).
+// activation image (attn_combine_fusable, and for img attn_fusable, must hold).
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                      const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* part_o,
                      float* part_ml, float* out, cudaStream_t s, int* status = nullptr, unsigned int* count = nullptr,
                      const ActImage* img = nullptr);
+bool attn_combine_fusable(int n_head, int n_kv, int hd, int cap);
 bool attn_fusable(int n_head, int n_kv, int hd, int act_type);
 // cos/sin pairs of one position delta for every rotated pair (head_dim <= 256).
 constexpr int kRotPairs = 128;
