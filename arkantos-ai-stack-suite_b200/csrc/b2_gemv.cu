@@ -971,7 +971,8 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.act_img = in_kernel ? nullptr : a.act_img;
   if (a.epilogue == EPI_ROPE_KV) p.rope = *a.rope;
   // Stages of P tiles x U unit steps of all S ranges.  mma: one tile pair per
-  // stage, U as large as fits ~16 KB, and whole rings of nss >= 2 slots for
+  // stage, U as large as fits ~20 KB (bulk copies of ~9 KB or more: smaller
+  // ones cost streaming bandwidth), and whole rings of nss >= 2 slots for
   // each of the nset consumer sets (smaller U, or the full shared memory,
   // where needed); dp4a: P = 8/S tiles, ~32 KB.  With small activations stay
   // within ~100 KB when that still gives the pipeline it needs, so that two
@@ -985,7 +986,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   int U = 0, ns = 0;
   size_t stage = 0;
   auto fit = [&](size_t cap_, int want_per_set) -> bool {
-    for (int u = std::min<int>(w.ulen, (int)std::max<size_t>(1, (mma ? 16 * 1024 : 32 * 1024) / step_b)); u >= 1;
+    for (int u = std::min<int>(w.ulen, (int)std::max<size_t>(1, (mma ? 20 * 1024 : 32 * 1024) / step_b)); u >= 1;
          --u) {
       const size_t st = step_b * u;
       if (fixed + st > cap_) continue;
