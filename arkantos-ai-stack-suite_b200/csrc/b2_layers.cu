@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(256, 3) attn_chunk_kernel(const float* __restr
   constexpr int P = kAttnP, B = HD / 16;
   constexpr int PAIRS = HD / 2;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);        // [0]: K rows, [1]: V rows
   uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);   // [P][HD]
   uint16_t* vs = ks + P * HD;                                 // [P][HD]
   float* qs = reinterpret_cast<float*>(vs + P * HD);          // [G][HD]
@@ -392,19 +392,24 @@ __global__ void __launch_bounds__(256, 3) attn_chunk_kernel(const float* __restr
     const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
     const int64_t base = ((int64_t)s * n_kv + kh) * cap;   // row of slot 0
     if (tid == 0) {
-      mbar_init(bar, 1);
+      mbar_init(&bar[0], 1);
+      mbar_init(&bar[1], 1);
       fence_mbar_init();
-      mbar_arrive_expect_tx(bar, (uint32_t)(2 * n * HD * 2));
-      // logical positions [t0, t0+n) as runs of consecutive slots
-      int p = t0;
-      while (p < t0 + n) {
-        const int64_t slot = kv_slot(sst, p, cap);
-        int len = t0 + n - p;
-        if (p < sst.n_keep) len = min(len, sst.n_keep - p);
-        else len = (int)min((int64_t)len, (int64_t)cap - slot);   // up to the end of the ring
-        bulk_g2s(ks + (p - t0) * HD, kc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
-        bulk_g2s(vs + (p - t0) * HD, vc + (base + slot) * HD, (uint32_t)(len * HD * 2), bar);
-        p += len;
+      mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * HD * 2));
+      mbar_arrive_expect_tx(&bar[1], (uint32_t)(n * HD * 2));
+      // logical positions [t0, t0+n) as runs of consecutive slots; all K
+      // runs first, so the scores can start while V is still arriving
+      for (int kv = 0; kv < 2; ++kv) {
+        int p = t0;
+        while (p < t0 + n) {
+          const int64_t slot = kv_slot(sst, p, cap);
+          int len = t0 + n - p;
+          if (p < sst.n_keep) len = min(len, sst.n_keep - p);
+          else len = (int)min((int64_t)len, (int64_t)cap - slot);   // up to the end of the ring
+          bulk_g2s((kv ? vs : ks) + (p - t0) * HD, (kv ? vc : kc) + (base + slot) * HD, (uint32_t)(len * HD * 2),
+                   &bar[kv]);
+          p += len;
+        }
       }
     }
     // q of the G heads into shared memory while the copies fly
@@ -413,7 +418,7 @@ __global__ void __launch_bounds__(256, 3) attn_chunk_kernel(const float* __restr
       for (int i = tid; i < G * HD / 4; i += blockDim.x) reinterpret_cast<float4*>(qs)[i] = qg[i];
     }
     __syncthreads();
-    mbar_wait_bounded(bar, 0, status, 5);
+    mbar_wait_bounded(&bar[0], 0, status, 5);
 
     // ---- scores: lane group grp of warp w takes positions w*16 + it*4 + grp, HG heads per pass ----
     {
@@ -503,6 +508,7 @@ __global__ void __launch_bounds__(256, 3) attn_chunk_kernel(const float* __restr
       }
     }
     __syncthreads();
+    mbar_wait_bounded(&bar[1], 0, status, 5);   // V, which landed while the scores ran
     // ---- P·V: warp (residue r, dim half), lane = dim pair; all heads per position ----
     float* pv = reinterpret_cast<float*>(ks);   // [4 residues][G][HD] partials, K is no longer needed
     {
