@@ -508,10 +508,11 @@ __device__ __forceinline__ void store_y(const GemvP& p, int t, int64_t row, floa
   *yp = p.epilogue == EPI_ACCUM ? __fadd_rn(*yp, v) : v;
 }
 
-// After every consumer thread of the CTA has stored: count the CTA; the last
-// CTA of the grid publishes the next epoch to every rank's flag.  Stores reach
-// peers before the count (fence.sys by each storing thread, then the CTA
-// barrier), and the count before the flags (fence.sys in the last CTA).
+// After every consumer thread of the CTA has stored (a CTA barrier): count
+// the CTA; the last CTA of the grid publishes the next epoch to every rank's
+// flag.  Stores reach peers before the count (the barrier, then this
+// thread's fence.sys), and the count before the flags (fence.sys in the last
+// CTA).
 __device__ __forceinline__ void signal_peers(const GemvP& p) {
   __threadfence_system();
   const unsigned int prev = atomicAdd(p.peer.done, 1u);
@@ -809,7 +810,10 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
     }
   }
   if (p.peer.n) {
-    __threadfence_system();   // this thread's peer stores, before the CTA is counted
+    // Every consumer thread's peer stores are ordered before the CTA barrier;
+    // the signalling thread's system-scope fence after it makes them all
+    // visible before the count (the grid-barrier pattern: barrier, then one
+    // thread's fence and atomic).
     consumer_sync(NW * 32);
     if (warp == 0 && lane == 0) signal_peers(p);
   }
