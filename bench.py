@@ -369,10 +369,11 @@ def prompts_8b() -> np.ndarray:
 
 def launches_per_step(n_layer: int) -> int:
     """Kernels of this library one decode step launches: embed; per layer
-    rmsnorm, QKV GEMV, rope+KV store, attention split + combine, O GEMV,
-    rmsnorm, gate|up GEMV (SwiGLU epilogue), down GEMV; then rmsnorm, head
-    GEMV and argmax.  NCCL's collective kernels are not counted."""
-    return 1 + 9 * n_layer + 3
+    RMSNorm (+ Q8 image), QKV GEMV (RoPE + KV store epilogue), attention
+    (combine + O image in its last CTAs), O GEMV, RMSNorm (+ image), gate|up
+    GEMV (SwiGLU epilogue), quantize (down input), down GEMV; then RMSNorm,
+    head GEMV and argmax.  No library collective runs in a step."""
+    return 1 + 8 * n_layer + 3
 
 
 def time_gemv_shape(b2, qtype: int, n: int, k: int, n_tok: int, steps: int, seed: int) -> dict:
@@ -539,18 +540,19 @@ def run_decode_ours(args, dist, rank, world, local):
     return out
 
 
-def cpu_decode_samples(path: str, n_samples: int | None, seconds: float | None, warm: int):
-    """Oracle decode of one token of the 8B model at context PROMPT, timed as
+def cpu_decode_samples(path: str, n_samples: int | None, seconds: float | None, warm: int, layers: int | None = None,
+                       ctx_len: int = PROMPT):
+    """Oracle decode of one token of a model at context ctx_len, timed as
     samples: one decoder layer per sample (cycling over all layers, so every
     layer's weights come from DRAM), plus embed+final norm+head samples.
     Returns (seconds per token extrapolated, samples, threads)."""
     from oracle import oracle as O
     nt = os.cpu_count() or 1
     m = O.Model(path)
-    m.init_cache(1, PROMPT + 8)
+    m.init_cache(1, ctx_len + 8)
     m.cache_fill(0x3C00)
     nl = m.n_layers
-    tok, pos = 17, PROMPT
+    tok, pos = 17, ctx_len
     t_layer, t_head = [], []
 
     def sample(i):
@@ -617,6 +619,106 @@ def run_decode_reference(args, dist, rank, world, local):
                                        f"embed+norm+head of one token at context {PROMPT}; tok/s = 1 / (32 x mean "
                                        f"layer + head); {n} samples in {wall:.0f} s"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ------------------------------------------------------------------------------------------
+# Workload: 1.1B Q4_0 decode, batch 1 (config 4)
+# ------------------------------------------------------------------------------------------
+LLAMA_1B = dict(n_layer=22, n_embd=2048, n_ff=5632, n_head=32, n_head_kv=4, n_vocab=32000, seed=5,
+                rope_theta=10000.0, n_ctx_train=2048)
+PROMPT_1B, GEN_1B = 128, 256
+
+
+def write_1b(b2, path: str) -> float:
+    t0 = time.perf_counter()
+    c = LLAMA_1B
+    b2.write_synthetic_llama(path + ".part", c["n_layer"], c["n_embd"], c["n_ff"], c["n_head"], c["n_head_kv"],
+                             c["n_vocab"], b2.Q4_0, embd_type=b2.Q4_0, out_type=b2.Q4_0, seed=c["seed"],
+                             rope_theta=c["rope_theta"], n_ctx_train=c["n_ctx_train"])
+    os.replace(path + ".part", path)
+    return time.perf_counter() - t0
+
+
+def weight_bytes_1b() -> int:
+    c = LLAMA_1B
+    d, ff, hd = c["n_embd"], c["n_ff"], c["n_embd"] // c["n_head"]
+    qkv = (c["n_head"] + 2 * c["n_head_kv"]) * hd
+    per_layer = q_bytes(2, qkv, d) + q_bytes(2, d, d) + q_bytes(2, 2 * ff, d) + q_bytes(2, d, ff)
+    return c["n_layer"] * per_layer + q_bytes(2, c["n_vocab"], d)
+
+
+def run_decode1b_ours(args, dist, rank, world, local):
+    """Config 4: 128-token prompt, then GEN_1B greedy steps of one sequence,
+    timed as one b2_generate call (device-side feedback) with CUDA events;
+    e2e is the host loop b2_decode + b2_get_argmax over the same steps."""
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    c = LLAMA_1B
+    path = model_path("1b_q4_0")
+    t_write = write_1b(b2, path) if rank == 0 and not os.path.exists(path) else 0.0
+    nccl_id, path = tp_share(dist, rank, world, b2.nccl_unique_id, path)
+    model = b2.Model(path, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    n_ctx = PROMPT_1B + 2 * GEN_1B + 16
+    ctx = b2.Context(model, n_ctx=n_ctx, n_seq=1)
+    prompt = np.random.default_rng(c["seed"]).integers(0, c["n_vocab"], PROMPT_1B).astype(np.int32)
+    ctx.decode(prompt, want_logits=2)
+    first = int(ctx.argmax()[0][-1])
+    steps = min(args.steps, GEN_1B)
+    warm = max(args.warmup, 3)
+    ctx.generate([first], warm, seq=[0])          # graph capture + warm-up
+    ctx.kv_seq_rm(0, PROMPT_1B, -1)
+    e0, e1 = b2.Event(), b2.Event()
+    barrier(dist)
+    with ClockSampler(local) as clk:
+        e0.record(ctx.stream)
+        gen = ctx.generate([first], steps, seq=[0])
+        e1.record(ctx.stream)
+        ctx.synchronize()
+    ms = dist_max(dist, e0.elapsed_ms(e1))
+    tok_s = steps / (ms * 1e-3)
+    ctx.kv_seq_rm(0, PROMPT_1B, -1)
+    tok, ids = first, []
+    barrier(dist)
+    t0 = time.perf_counter()
+    for k in range(steps):
+        ctx.decode([tok], pos=[PROMPT_1B + k], seq=[0], want_logits=1)
+        tok = int(ctx.argmax()[0][0])
+        ids.append(tok)
+    e2e_s = dist_max(dist, time.perf_counter() - t0)
+    peaks = measured_peaks()
+    hd = c["n_embd"] // c["n_head"]
+    kv_step = sum(c["n_layer"] * 2 * c["n_head_kv"] * hd * 2 * (PROMPT_1B + k + 1) for k in range(steps)) / steps
+    step_bytes = (weight_bytes_1b() + kv_step) / world
+    step_gbs = step_bytes / (ms / steps * 1e-3) / 1e9
+    out = {"metric": "decode tok/s (Llama-shape 1.1B Q4_0, batch 1)", "value": round(tok_s, 1), "unit": "tok/s",
+           "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": ms / steps, "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "q4_0 x q8_0 -> int32 -> f32, fp16 KV",
+           "data": "synthetic: random-init Llama 1.1B (N(0,0.02) seed 5) GGUF Q4_0; uniform random prompt ids",
+           "config": {"workload": "decode_1b_q4_0: 22 layers, d 2048, ffn 5632, 32/4 heads, hd 64, vocab 32000; "
+                                  "128-token prompt, greedy steps, batch 1 (config 4)",
+                      "global_batch": 1, "seq_len": PROMPT_1B, "parallelism": f"tp{world}",
+                      "l2": "inputs larger than L2 (0.62 GB of weights per step)"},
+           "roofline": {"bound": "hbm", "kernel": "decode step (weights + KV per token)",
+                        "achieved": round(step_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": round(step_gbs / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
+                        "algorithmic_bytes_per_launch": int(step_bytes)},
+           "e2e": {"value": round(steps / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 128,
+                   "greedy_ids_equal_device_loop": bool(np.array_equal(np.array(ids), gen.ravel()[:steps]))},
+           "gpu_launches": launches_per_step(c["n_layer"]) * steps, "clocks": clk.summary(),
+           "setup_s": {"write_gguf": round(t_write, 1)}}
+    del ctx, model
+    if rank == 0 and args.cpu_seconds > 0:
+        per_tok, n, nt = cpu_decode_samples(path, None, args.cpu_seconds, 2, layers=c["n_layer"], ctx_len=PROMPT_1B)
+        out["cpu_baseline"] = {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": nt, "kind": "port",
+                               "sample": f"{n} samples of one token at context {PROMPT_1B}: single decoder layers "
+                                         f"cycling over all {c['n_layer']} plus embed+norm+head"}
+    barrier(dist)
+    if rank == 0 and not args.keep_model:
+        try:
+            os.remove(path)
+        except OSError:
+            pass
+    return out
 
 
 # ------------------------------------------------------------------------------------------
@@ -847,6 +949,7 @@ def run_gemv_op(args, dist, rank, world, local):
 
 WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
              "gemv_q4_0": (run_gemv_ours, run_gemv_reference),
+             "decode_1b_q4_0": (run_decode1b_ours, None),
              "gemv_op": (run_gemv_op, None),
              "gemm_q4k": (run_gemm_ours, run_gemm_reference),
              "attn": (run_attn_ours, None)}
