@@ -338,7 +338,7 @@ class QMatrix:
 
     def gemm_device(self, x: DeviceBuffer, n_tok: int, y: DeviceBuffer, status: DeviceBuffer | None = None,
                     stream: int | None = None, workspace: DeviceBuffer | None = None) -> None:
-        """Tensor-core prefill GEMM (Q4_K): x fp32 [n_tok, k] -> y fp32 [n_tok, n_rows] on the device."""
+        """Tensor-core prefill GEMM (Q4_K or Q8_0 weights): x fp32 [n_tok, k] -> y fp32 [n_tok, n_rows] on the device."""
         check(lib.b2_gemm(self.h, x.ptr, n_tok, y.ptr, workspace.ptr if workspace else None,
                           workspace.nbytes if workspace else 0, status.ptr if status else None, stream), "gemm")
 

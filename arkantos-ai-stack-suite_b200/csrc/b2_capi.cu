@@ -297,7 +297,7 @@ int b2_gemm_workspace_bytes(const b2_qmatrix* w, int n_tok, size_t* bytes) {
 int b2_gemm(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* workspace, size_t workspace_bytes,
             int* status, void* stream) {
   B2_CHECK_ARG(w && x && y && n_tok >= 1, "gemm arguments");
-  B2_CHECK_ARG(w->m.type == B2_Q4_K, "b2_gemm takes Q4_K weights");
+  B2_CHECK_ARG(w->m.type == B2_Q4_K || w->m.type == B2_Q8_0, "b2_gemm takes Q4_K or Q8_0 weights");
   cudaStream_t s = as_stream(stream);
   const size_t need = gemm_act_image_bytes(w->m, n_tok);
   if (workspace) {

@@ -1,7 +1,8 @@
-// Prefill GEMM for Q4_K weights on the 5th-generation tensor cores:
-// Y[t][r] = Σ_super-blocks of W row r · Q8_K(X[t]) — the reference's
+// Prefill GEMMs for Q4_K and Q8_0 weights on the 5th-generation tensor cores:
+// Y[t][r] = Σ_(super-)blocks of W row r · Q8(X[t]) — the reference's
 // matmul_quantized (Singularity/src/core/cortex_a5_engine.cpp:997-1027) with
-// ggml's Q4_K x Q8_K dot, for many tokens at once.
+// ggml's Q4_K x Q8_K dot, or the Q8_0 x Q8_0 dot, for many tokens at once.
+// The Q4_K kernel comes first; the Q8_0 kernel (integer MMAs) follows it.
 //
 // Exactness.  Per 256-weight super-block the reference adds
 //   (d·dx)·isum  then subtracts  (dmin·dx)·msum,
@@ -540,13 +541,276 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p, co
   }
 }
 
+// ---- Q8_0 weights: the integer tensor-core path ----------------------------------------------
+// Per 32-weight block the reference adds (d_w·d_x)·sumi with sumi the exact
+// int32 dot of the codes (Singularity/tests/test_and_bench_a5.cpp:205-221).
+// A repacked Q8_0 slot is already two K-major 8x16-byte core matrices of the
+// tile's 8 rows (codes 0-15 at +0, 16-31 at +128, the fp16 scales at +256),
+// so a TMA copy of one slot per tile gives tcgen05.mma kind::i8 its A operand
+// as loaded: no dequantization.  One K=32 MMA per block writes that block's
+// sumi (int32) into its own 64 TMEM columns; the accumulators start at
+// 0x4B400000, so the result read back as fp32 is 12582912 + sumi exactly
+// (|sumi| <= 2^19) and one subtraction recovers (float)sumi.  The epilogue
+// then applies acc + (d_w·d_x)·sumi block by block in order, two tokens per
+// instruction with fma.rn.f32x2: a·b as fma(a, b, -0), a + b as fma(a, 1, b)
+// and the subtraction as fma(x, 1, -12582912) each round exactly as the
+// scalar operation, so Y is bit-identical to the reference-order matmul.
+// The constants 1, -0 and -12582912 arrive as kernel parameters: with
+// literal operands the compiler may turn such an fma back into a multiply or
+// an add and fuse the pair into one fma (one rounding instead of two), which
+// was measured to break the reference's rounding.
+//
+// Structure (one CTA per 128 weight rows x 64 tokens, 18 warps): warp 0
+// issues the copies of a group of 4 blocks per stage (16 slot tiles per
+// block, the codes and scales of the activations); warp 1 owns TMEM (two
+// buffers of 4 blocks x 64 columns) and issues the MMAs; warps 2-17 are the
+// epilogue, warp w reading TMEM lanes 32*(w%4).. for tokens 16*((w-2)/4)..,
+// and re-seeding the columns it has read before handing the buffer back.
+constexpr int kQ8G = 4;                             // blocks per group (one TMEM buffer)
+constexpr int kQ8Stages = 6;
+constexpr int kQ8A = (kMT / 8) * 272;               // 16 slots of one block
+constexpr int kQ8B = kNT * 32;                      // 64 tokens x 32 codes, core-matrix order
+constexpr int kQ8Dx = kNT * 4;
+constexpr int kQ8Stage = kQ8G * (kQ8A + kQ8B + kQ8Dx);
+constexpr int kQ8EpWarps = 16;
+constexpr int kQ8Threads = (2 + kQ8EpWarps) * 32;
+constexpr uint32_t kQ8Seed = 0x4B400000u;           // 12582912.0f
+constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kNT >> 3) << 17) |
+                              ((uint32_t)(kMT >> 4) << 24);   // s32 D, s8 A and B, K-major, M=128, N=kNT
+
+struct GemmQ8P {
+  int nb, S, L;
+  int64_t n_rows;
+  int n_tok;
+  const uint8_t* bimg;       // activation codes [tok tile][nb][kQ8B]
+  const float* dximg;        // activation scales [tok tile][nb][kNT]
+  float* y;                  // [n_tok][n_rows]
+  int* status;
+  float one, nzero, nseed;   // 1, -0, -12582912: opaque to the compiler (see above)
+};
+
+__device__ __forceinline__ void umma_i8_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %3, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %4, p;\n\t}\n"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(kIdescI8));
+}
+// 16 columns of this warp's lanes, loaded before return.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+// The same 32-bit value into 16 columns of this warp's lanes, completed before return.
+__device__ __forceinline__ void tmem_fill16_sync(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr), "r"(v)
+      : "memory");
+}
+// (d0, d1) = (a0·b0 + c0, a1·b1 + c1), each lane one correctly rounded fma.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rc;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// x fp32 [n_tok][k] -> Q8_0 codes in the B core-matrix order and the scales
+// (as fp32 of the fp16 scale); padded tokens are zero.  One warp per (token,
+// block), one value per lane, quantized like ref_quantize_row_q8_0.
+__global__ void gemm_act_q8_0_kernel(const float* __restrict__ x, int64_t x_stride, int n_tok, int n_tok_pad, int nb,
+                                     uint8_t* __restrict__ bimg, float* __restrict__ dximg) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)n_tok_pad * nb;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < total;
+       i += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int t = (int)(i / nb), b = (int)(i - (int64_t)t * nb);
+    uint32_t c = 0;
+    uint16_t d16 = 0;
+    if (t < n_tok) c = (uint8_t)quant_q8_0_lane(x[t * x_stride + (int64_t)b * 32 + lane], &d16);   // warp-uniform
+    const uint32_t w = c | (__shfl_down_sync(0xffffffffu, c, 1) << 8) | (__shfl_down_sync(0xffffffffu, c, 2) << 16) |
+                       (__shfl_down_sync(0xffffffffu, c, 3) << 24);
+    const int tt = t / kNT, tr = t % kNT;
+    uint8_t* blk = bimg + ((int64_t)tt * nb + b) * kQ8B;
+    if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(blk + (tr / 8) * 256 + (lane / 16) * 128 + (tr % 8) * 16 + (lane % 16)) = w;
+    if (lane == 0) dximg[((int64_t)tt * nb + b) * kNT + tr] = h2f(d16);
+  }
+}
+
+__global__ void __launch_bounds__(kQ8Threads, 1)
+    gemm_q8_0_kernel(const GemmQ8P p, const __grid_constant__ CUtensorMap wmap) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int nb = p.nb, ng = (nb + kQ8G - 1) / kQ8G;
+  uint64_t* st_full = reinterpret_cast<uint64_t*>(smem);   // [kQ8Stages]
+  uint64_t* st_empty = st_full + kQ8Stages;                 // [kQ8Stages] MMA commit + every epilogue thread
+  uint64_t* acc_full = st_empty + kQ8Stages;                // [2]
+  uint64_t* acc_empty = acc_full + 2;                       // [2] every epilogue thread (seeded)
+  uint64_t* mma_done = acc_empty + 2;                       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 496);
+  int* abort_flag = reinterpret_cast<int*>(smem + 500);
+  uint8_t* stages = smem + 1024;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_blk = blockIdx.x, tok_tile = blockIdx.y;
+  const int64_t r0 = (int64_t)row_blk * kMT;
+  const int tile0 = row_blk * (kMT / 8);
+  constexpr int kEpThreads = kQ8EpWarps * 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kQ8Stages; ++i) {
+      mbar_init(&st_full[i], 1);
+      mbar_init(&st_empty[i], 1 + kEpThreads);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpThreads);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      pdl_wait();   // the activation image comes from the previous kernel
+      int issued = 0;
+      for (int g = 0; g < ng; ++g) {
+        const int st = g % kQ8Stages, b0 = g * kQ8G, gb = min(kQ8G, nb - b0);
+        if (!wait_empty(&st_empty[st], g / kQ8Stages, p.status, 60, abort_flag)) break;
+        uint8_t* sp = stages + st * kQ8Stage;
+        mbar_arrive_expect_tx(&st_full[st], (uint32_t)(gb * (kQ8A + kQ8B + kQ8Dx)));
+        for (int j = 0; j < gb; ++j) {
+          const int u = b0 + j, wr = u / p.L, ii = u - wr * p.L;
+          tma_load_3d(sp + j * kQ8A, &wmap, 0, ii * p.S + wr, tile0, &st_full[st]);
+        }
+        const int64_t blk0 = (int64_t)tok_tile * nb + b0;
+        bulk_g2s(sp + kQ8G * kQ8A, p.bimg + blk0 * kQ8B, (uint32_t)(gb * kQ8B), &st_full[st]);
+        bulk_g2s(sp + kQ8G * (kQ8A + kQ8B), p.dximg + blk0 * kNT, (uint32_t)(gb * kQ8Dx), &st_full[st]);
+        ++issued;
+      }
+      // every copy issued has landed before the CTA may exit
+      for (int u = max(0, issued - kQ8Stages); u < issued; ++u)
+        mbar_wait_bounded(&st_full[u % kQ8Stages], (u / kQ8Stages) & 1, p.status, 61);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      for (int g = 0; g < ng; ++g) {
+        const int b = g & 1, st = g % kQ8Stages, gb = min(kQ8G, nb - g * kQ8G);
+        // phase u of acc_empty[b] completes when the epilogue has seeded the buffer for use u
+        if (!wait_full(&acc_empty[b], g / 2, p.status, 62, abort_flag)) break;
+        tc_fence_after();
+        if (!wait_full(&st_full[st], g / kQ8Stages, p.status, 63, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(stages + st * kQ8Stage), sb = sa + kQ8G * kQ8A;
+        for (int j = 0; j < gb; ++j)
+          umma_i8_ss(tmem + b * (kQ8G * kNT) + j * kNT, smem_desc(sa + j * kQ8A, 128, 272), smem_desc(sb + j * kQ8B, 128, 256),
+                     1u);
+        umma_commit(&st_empty[st]);
+        umma_commit(&acc_full[b]);
+      }
+      umma_commit(mma_done);
+      mbar_wait_bounded(mma_done, 0, p.status, 64);
+    }
+  } else {
+    // ---------------- epilogue: thread = one weight row (TMEM lane), 16 tokens ----------------
+    constexpr int NE = kNT / 4;
+    const int qt = warp & 3, eh = (warp - 2) >> 2;
+    const int r = qt * 32 + lane;
+    const uint32_t tl = tmem + ((uint32_t)(qt * 32) << 16) + eh * NE;
+    // seed both buffers, then hand them to the MMA issuer
+#pragma unroll
+    for (int c = 0; c < 2 * kQ8G; ++c) tmem_fill16_sync(tl + c * kNT, kQ8Seed);
+    tc_fence_before();
+    mbar_arrive(&acc_empty[0]);
+    mbar_arrive(&acc_empty[1]);
+    float2 out[NE / 2];
+#pragma unroll
+    for (int t = 0; t < NE / 2; ++t) out[t] = make_float2(0.0f, 0.0f);
+    const float2 one2 = make_float2(p.one, p.one), nz2 = make_float2(p.nzero, p.nzero),
+                 nseed2 = make_float2(p.nseed, p.nseed);
+    for (int g = 0; g < ng; ++g) {
+      const int b = g & 1, st = g % kQ8Stages, gb = min(kQ8G, nb - g * kQ8G);
+      wait_full(&acc_full[b], g / 2, p.status, 65, abort_flag);
+      tc_fence_after();
+      wait_full(&st_full[st], g / kQ8Stages, p.status, 66, abort_flag);   // complete already: orders the smem reads
+      const uint8_t* sp = stages + st * kQ8Stage;
+      for (int j = 0; j < gb; ++j) {
+        const float dw = h2f(*reinterpret_cast<const uint16_t*>(sp + j * kQ8A + (r >> 3) * 272 + 256 + (r & 7) * 2));
+        const float2 dw2 = make_float2(dw, dw);
+        const float4* dx4 = reinterpret_cast<const float4*>(sp + kQ8G * (kQ8A + kQ8B) + j * kQ8Dx) + eh * (NE / 4);
+        uint32_t v[16];
+        tmem_ld16(tl + b * (kQ8G * kNT) + j * kNT, v);
+#pragma unroll
+        for (int q4 = 0; q4 < NE / 4; ++q4) {
+          const float4 dx = dx4[q4];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int t2 = q4 * 2 + h;
+            const float2 sumi = fma2(make_float2(__uint_as_float(v[2 * t2]), __uint_as_float(v[2 * t2 + 1])), one2, nseed2);
+            const float2 dd = fma2(dw2, h ? make_float2(dx.z, dx.w) : make_float2(dx.x, dx.y), nz2);
+            out[t2] = fma2(fma2(dd, sumi, nz2), one2, out[t2]);
+          }
+        }
+      }
+      mbar_arrive(&st_empty[st]);
+#pragma unroll
+      for (int c = 0; c < kQ8G; ++c) tmem_fill16_sync(tl + b * (kQ8G * kNT) + c * kNT, kQ8Seed);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[b]);
+    }
+    const int64_t row = r0 + r;
+    if (row < p.n_rows) {
+#pragma unroll
+      for (int t = 0; t < NE / 2; ++t) {
+        const int tok = tok_tile * kNT + eh * NE + 2 * t;
+        if (tok < p.n_tok) p.y[(int64_t)tok * p.n_rows + row] = out[t].x;
+        if (tok + 1 < p.n_tok) p.y[(int64_t)(tok + 1) * p.n_rows + row] = out[t].y;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+size_t gemm_q8_0_smem_bytes() { return 1024 + 1024 + (size_t)kQ8Stages * kQ8Stage; }
+
 size_t gemm_smem_bytes(int nsb) {
   return 1024 + 1024 + (size_t)kBGroups * kBGroup + (size_t)kRaw * kRawStage + 2 * kBm +
          (size_t)2 * kMT * 2 * 4 + (size_t)nsb * kNT * 4;
 }
 
-// The weight tensor map: the tile layout as [tiles][slots][144 x 8 bytes],
-// boxes of 16 tiles x 1 slot (one super-block of a CTA's 128 rows).
+// The weight tensor map: the tile layout as [tiles][slots][slot_bytes / 8 x
+// 8 bytes], boxes of 16 tiles x 1 slot (one unit of a CTA's 128 rows).
 int make_weight_map(const QMatrix& w, CUtensorMap* map) {
   static PFN_cuTensorMapEncodeTiled encode = nullptr;
   if (!encode) {
@@ -558,9 +822,9 @@ int make_weight_map(const QMatrix& w, CUtensorMap* map) {
     }
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
   }
-  const cuuint64_t dims[3] = {144, (cuuint64_t)w.splits * w.ulen, (cuuint64_t)w.n_tiles};
+  const cuuint64_t dims[3] = {(cuuint64_t)w.slot_bytes / 8, (cuuint64_t)w.splits * w.ulen, (cuuint64_t)w.n_tiles};
   const cuuint64_t strides[2] = {(cuuint64_t)w.slot_bytes, (cuuint64_t)w.tile_bytes};
-  const cuuint32_t box[3] = {144, 1, kMT / 8};
+  const cuuint32_t box[3] = {(cuuint32_t)w.slot_bytes / 8, 1, kMT / 8};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(w.data), dims, strides, box,
                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -575,16 +839,73 @@ int make_weight_map(const QMatrix& w, CUtensorMap* map) {
 }  // namespace
 
 size_t gemm_act_image_bytes(const QMatrix& w, int n_tok) {
-  const int nsb = w.nu;
   const int tiles = (n_tok + kNT - 1) / kNT;
-  return (size_t)tiles * nsb * (4 * kBSub + kBm + kNT * 4);
+  if (w.type == B2_Q8_0) return (size_t)tiles * w.nu * (kQ8B + kQ8Dx);
+  return (size_t)tiles * w.nu * (4 * kBSub + kBm + kNT * 4);
 }
+
+namespace {
+int launch_gemm_q8_0(const QMatrix& w, const float* x, int64_t x_stride, int n_tok, float* y, uint8_t* img,
+                     int* status, cudaStream_t s) {
+  const int nb = w.nu;
+  const int tiles = (n_tok + kNT - 1) / kNT;
+  uint8_t* bimg = img;
+  float* dximg = reinterpret_cast<float*>(bimg + (size_t)tiles * nb * kQ8B);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  {
+    cudaLaunchConfig_t cfg = {};
+    const int64_t warps = (int64_t)tiles * kNT * nb;
+    cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>((warps * 32 + 255) / 256, 8 * sm_count())));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_act_q8_0_kernel, x, x_stride, n_tok, tiles * kNT, nb, bimg, dximg));
+  }
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = gemm_q8_0_smem_bytes();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    B2_CUDA_TRY(cudaFuncSetAttribute(gemm_q8_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set[dev] = true;
+  }
+  GemmQ8P p = {};
+  p.nb = nb;
+  p.S = w.splits;
+  p.L = w.ulen;
+  p.n_rows = w.n_rows;
+  p.n_tok = n_tok;
+  p.bimg = bimg;
+  p.dximg = dximg;
+  p.y = y;
+  p.status = status;
+  p.one = 1.0f;
+  p.nzero = -0.0f;
+  p.nseed = -12582912.0f;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((w.n_rows + kMT - 1) / kMT), (unsigned)tiles);
+  cfg.blockDim = dim3(kQ8Threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUtensorMap wmap;
+  const int mrc = make_weight_map(w, &wmap);
+  if (mrc) return mrc;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_q8_0_kernel, p, wmap));
+  return B2_OK;
+}
+}  // namespace
 
 int launch_gemm(const QMatrix& w, const float* x, int64_t x_stride, int n_tok, float* y, uint8_t* img, int* status,
                 cudaStream_t s) {
-  B2_CHECK_ARG(w.type == B2_Q4_K, "the tensor-core GEMM takes Q4_K weights");
+  B2_CHECK_ARG(w.type == B2_Q4_K || w.type == B2_Q8_0, "the tensor-core GEMM takes Q4_K or Q8_0 weights");
   B2_CHECK_ARG(n_tok >= 1 && x && y && img, "gemm arguments");
   B2_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && x_stride % 4 == 0, "x alignment");
+  if (w.type == B2_Q8_0) return launch_gemm_q8_0(w, x, x_stride, n_tok, y, img, status, s);
   const int nsb = w.nu;
   const size_t smem = gemm_smem_bytes(nsb);
   B2_CHECK_ARG(smem <= 227 * 1024, "k too large for the GEMM's shared memory");

@@ -18,6 +18,7 @@ Prints one JSON line (rank 0).  Workloads:
               seed 2 -> GGUF Q4_K, X fp32 [512x4096] N(0,1) seed 3, Y fp32
               [512x11008]; one step = one b2_gemm (activation quantize +
               tcgen05 GEMM) over rotating W copies (> 2x L2).
+  gemm_q8_0   The same GEMM with W -> GGUF Q8_0 (integer tcgen05 MMAs).
   gemv_q4_0   Q4_0 block-quantized GEMV, batch 1: W 4096x4096 N(0,0.02) seed 0
               -> GGUF Q4_0, x fp32[4096] N(0,1) seed 1 quantized to Q8_0 in the
               kernel, y fp32[4096].  One step = one GEMV; consecutive steps
@@ -807,23 +808,27 @@ GEMM_FLOP = 2 * GEMM_N * GEMM_K * GEMM_T
 GEMM_REF_TOKENS = 8          # tokens per reference-arm step (a bounded sample of the 512)
 
 
-def gemm_inputs(b2):
+GEMM_QTYPE = {"gemm_q4k": (12, "Q4_K", "q4_k x q8_k -> f16 exact integers -> f32 (TMEM)"),
+              "gemm_q8_0": (8, "Q8_0", "q8_0 x q8_0 -> s32 (TMEM) -> f32")}
+
+
+def gemm_inputs(b2, qt):
     w = b2.synth_normal(2, GEMM_N * GEMM_K, std=0.02).reshape(GEMM_N, GEMM_K)
-    q = b2.quantize_weights(b2.Q4_K, w)
+    q = b2.quantize_weights(qt, w)
     x = b2.synth_normal(3, GEMM_T * GEMM_K).reshape(GEMM_T, GEMM_K)
     return q, x
 
 
-def cpu_gemm_rate(q, x, seconds: float | None, n_tok: int | None, nt: int) -> tuple[float, int]:
+def cpu_gemm_rate(q, x, seconds: float | None, n_tok: int | None, nt: int, qt: int) -> tuple[float, int]:
     """Oracle (reference-order) matmul of whole tokens on nt host threads:
     returns (seconds per token, tokens done)."""
     from oracle import oracle as O
-    xq = O.quantize_act(O.Q4_K, x[:1])
-    O.matmul(O.Q4_K, q, GEMM_N, GEMM_K, xq[0], nt)
+    xq = O.quantize_act(qt, x[:1])
+    O.matmul(qt, q, GEMM_N, GEMM_K, xq[0], nt)
     n, t0 = 0, time.perf_counter()
     while (n_tok is not None and n < n_tok) or (seconds is not None and time.perf_counter() - t0 < seconds):
-        xq = O.quantize_act(O.Q4_K, x[n % GEMM_T:n % GEMM_T + 1])
-        O.matmul(O.Q4_K, q, GEMM_N, GEMM_K, xq[0], nt)
+        xq = O.quantize_act(qt, x[n % GEMM_T:n % GEMM_T + 1])
+        O.matmul(qt, q, GEMM_N, GEMM_K, xq[0], nt)
         n += 1
     return (time.perf_counter() - t0) / n, n
 
@@ -831,10 +836,11 @@ def cpu_gemm_rate(q, x, seconds: float | None, n_tok: int | None, nt: int) -> tu
 def run_gemm_ours(args, dist, rank, world, local):
     import b2gguf as b2
     b2.check(b2.lib.b2_set_device(local), "set_device")
-    q, x = gemm_inputs(b2)
+    qt, qname, qdtype = GEMM_QTYPE[args.workload]
+    q, x = gemm_inputs(b2, qt)
     wb = q.nbytes
     copies = max(2, -(-300_000_000 // wb))               # rotating W copies, > 2x L2
-    mats = [b2.QMatrix(b2.Q4_K, q, GEMM_N, GEMM_K) for _ in range(copies)]
+    mats = [b2.QMatrix(qt, q, GEMM_N, GEMM_K) for _ in range(copies)]
     xd = b2.DeviceBuffer.from_array(x)
     yd = b2.DeviceBuffer(GEMM_T * GEMM_N * 4)
     st = b2.DeviceBuffer.from_array(np.zeros(1, np.int32))
@@ -879,12 +885,12 @@ def run_gemm_ours(args, dist, rank, world, local):
     e2e_s = dist_max(dist, (time.perf_counter() - t0) / n_e2e)
     peaks = measured_peaks()
     out = {
-        "metric": "Q4_K prefill GEMM TFLOP/s (W 11008x4096, X 512x4096)",
+        "metric": f"{qname} prefill GEMM TFLOP/s (W 11008x4096, X 512x4096)",
         "value": round(tflops * world, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_k x q8_k -> f16 exact integers -> f32 (TMEM)",
-        "data": "synthetic: W N(0,0.02) seed 2 -> GGUF Q4_K; X N(0,1) seed 3",
-        "config": {"workload": "gemm_q4k 11008x4096 x 512 tokens (config 2)", "rotating_weight_copies": copies,
+        "vs_baseline": None, "dtype": qdtype,
+        "data": f"synthetic: W N(0,0.02) seed 2 -> GGUF {qname}; X N(0,1) seed 3",
+        "config": {"workload": f"{args.workload} 11008x4096 x 512 tokens (config 2)", "rotating_weight_copies": copies,
                    "l2": f"inputs larger than L2 ({copies} rotating W copies, {copies * wb / 1e6:.0f} MB)",
                    "replicas": world},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["bf16_tflops"],
@@ -897,10 +903,10 @@ def run_gemm_ours(args, dist, rank, world, local):
     }
     if rank == 0 and args.cpu_seconds > 0:
         nt = os.cpu_count() or 1
-        per_tok, n = cpu_gemm_rate(q, x, args.cpu_seconds, None, nt)
+        per_tok, n = cpu_gemm_rate(q, x, args.cpu_seconds, None, nt, qt)
         out["cpu_baseline"] = {"value": round(2 * GEMM_N * GEMM_K / per_tok / 1e12, 5), "unit": "TFLOP/s",
                                "cores": nt, "kind": "port",
-                               "sample": f"{n} tokens (Q8_K quantize + 11008 row vec_dots) in {args.cpu_seconds:.0f} s"}
+                               "sample": f"{n} tokens (activation quantize + 11008 row vec_dots) in {args.cpu_seconds:.0f} s"}
     return out
 
 
@@ -908,16 +914,17 @@ def run_gemm_reference(args, dist, rank, world, local):
     if rank != 0:
         return None
     import b2gguf as b2  # host-only helpers (quantizer, generator)
-    q, x = gemm_inputs(b2)
+    qt, qname, _ = GEMM_QTYPE[args.workload]
+    q, x = gemm_inputs(b2, qt)
     nt = os.cpu_count() or 1
-    cpu_gemm_rate(q, x, None, max(1, args.warmup), nt)
-    per_tok, n = cpu_gemm_rate(q, x, None, GEMM_REF_TOKENS * args.steps, nt)
+    cpu_gemm_rate(q, x, None, max(1, args.warmup), nt, qt)
+    per_tok, n = cpu_gemm_rate(q, x, None, GEMM_REF_TOKENS * args.steps, nt, qt)
     v = round(2 * GEMM_N * GEMM_K / per_tok / 1e12, 5)
-    return {"metric": "Q4_K prefill GEMM TFLOP/s (W 11008x4096, X 512x4096)", "value": v, "unit": "TFLOP/s",
+    return {"metric": f"{qname} prefill GEMM TFLOP/s (W 11008x4096, X 512x4096)", "value": v, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": per_tok * GEMM_REF_TOKENS * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_k x q8_k -> int32 -> f32", "data": "synthetic",
-            "config": {"workload": "gemm_q4k 11008x4096 x 512 tokens (config 2)"}, "impl": "reference",
+            "vs_baseline": None, "dtype": f"{qname.lower()} x q8 -> int32 -> f32", "data": "synthetic",
+            "config": {"workload": f"{args.workload} 11008x4096 x 512 tokens (config 2)"}, "impl": "reference",
             "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port",
                              "sample": f"{n} of the 512 tokens ({GEMM_REF_TOKENS} per step) on {nt} host threads"},
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -952,6 +959,7 @@ WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
              "decode_1b_q4_0": (run_decode1b_ours, None),
              "gemv_op": (run_gemv_op, None),
              "gemm_q4k": (run_gemm_ours, run_gemm_reference),
+             "gemm_q8_0": (run_gemm_ours, run_gemm_reference),
              "attn": (run_attn_ours, None)}
 
 

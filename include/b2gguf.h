@@ -161,9 +161,10 @@ B2_API int b2_gemm_workspace_bytes(const b2_qmatrix* w, int n_tok, size_t* bytes
 
 /* Prefill GEMM on the tensor cores (tcgen05, fp32 accumulation in TMEM),
  * the reference's matmul_quantized (Singularity/src/core/cortex_a5_engine.cpp:997-1027)
- * for any n_tok >= 1: y[t][r] = vec_dot(W row r, Q8_K(x[t])), super-blocks
+ * for any n_tok >= 1: y[t][r] = vec_dot(W row r, Q8_K(x[t])) for Q4_K
+ * weights, vec_dot(W row r, Q8_0(x[t])) for Q8_0 weights, (super-)blocks
  * added in order exactly as the CPU vec_dot adds them, so y is bit-identical
- * to the reference's per-row result.  Q4_K weights.  x fp32 [n_tok][k]
+ * to the reference's per-row result.  x fp32 [n_tok][k]
  * (16-byte aligned), y fp32 [n_tok][n_rows].  `workspace` (device, 16-byte
  * aligned, b2_gemm_workspace_bytes) may be NULL: the call then allocates
  * stream-ordered scratch.  `status` (device int, may be NULL) receives a
