@@ -120,6 +120,7 @@ struct b2_context {
   float *x = nullptr, *delta = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
   float *logits = nullptr, *part_o = nullptr, *part_ml = nullptr, *top = nullptr;
   unsigned int* attn_cnt = nullptr;   // [kStepMax][n_kv] arrival counters of the fused attention combine
+  uint32_t* argmax_scr = nullptr;     // vocabulary-slice partials and arrival counters of the argmax
   // [ids kStepMax | top-1, margin 2*kStepMax | status] in one allocation: one
   // D2H copy returns a step's greedy result and the device-wait status
   int32_t* res = nullptr;
@@ -493,6 +494,9 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   }
   if ((rc = dalloc(c, &c->attn_cnt, (size_t)T * m->nkv_l))) return rc;
   B2_CUDA_TRY(cudaMemset(c->attn_cnt, 0, (size_t)T * m->nkv_l * sizeof(unsigned int)));
+  static_assert(kStepMax <= kArgmaxTok, "argmax scratch sized for the step");
+  if ((rc = dalloc(c, &c->argmax_scr, argmax_scratch_words()))) return rc;
+  B2_CUDA_TRY(cudaMemset(c->argmax_scr, 0, argmax_scratch_words() * sizeof(uint32_t)));
   c->ids = c->res;
   c->top = reinterpret_cast<float*>(c->res + kStepMax);
   c->status = c->res + 3 * kStepMax;
@@ -676,7 +680,8 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     f.count = c->gen_count;
     f.cap = c->n_ctx;
   }
-  return launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s, f, tp ? &in_head : nullptr, c->status);
+  return launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s, f, tp ? &in_head : nullptr, c->status,
+                       c->argmax_scr);
 }
 
 int run_step(b2_context* c, int n, bool with_logits, bool feed = false) {

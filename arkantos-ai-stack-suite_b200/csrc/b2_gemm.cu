@@ -560,20 +560,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4k_kernel(const GemmP p, co
 // an add and fuse the pair into one fma (one rounding instead of two), which
 // was measured to break the reference's rounding.
 //
-// Structure (one CTA per 128 weight rows x 64 tokens, 18 warps): warp 0
-// issues the copies of a group of 4 blocks per stage (16 slot tiles per
-// block, the codes and scales of the activations); warp 1 owns TMEM (two
-// buffers of 4 blocks x 64 columns) and issues the MMAs; warps 2-17 are the
-// epilogue, warp w reading TMEM lanes 32*(w%4).. for tokens 16*((w-2)/4)..,
+// Structure (one CTA per 128 weight rows x 64 tokens, 10 warps, two CTAs per
+// SM so one's start-up and tail overlap the other's epilogue): warp 0 issues
+// the copies of a group of 2 blocks per stage (16 slot tiles per block, the
+// codes and scales of the activations); warp 1 owns 256 TMEM columns (two
+// buffers of 2 blocks x 64 columns) and issues the MMAs; warps 2-9 are the
+// epilogue, warp w reading TMEM lanes 32*(w%4).. for tokens 32*((w-2)/4)..,
 // and re-seeding the columns it has read before handing the buffer back.
-constexpr int kQ8G = 4;                             // blocks per group (one TMEM buffer)
+constexpr int kQ8G = 2;                             // blocks per group (one TMEM buffer)
 constexpr int kQ8Stages = 6;
 constexpr int kQ8A = (kMT / 8) * 272;               // 16 slots of one block
 constexpr int kQ8B = kNT * 32;                      // 64 tokens x 32 codes, core-matrix order
 constexpr int kQ8Dx = kNT * 4;
 constexpr int kQ8Stage = kQ8G * (kQ8A + kQ8B + kQ8Dx);
-constexpr int kQ8EpWarps = 16;
+constexpr int kQ8EpWarps = 8;
 constexpr int kQ8Threads = (2 + kQ8EpWarps) * 32;
+constexpr uint32_t kQ8TmemCols = 2 * kQ8G * kNT;
 constexpr uint32_t kQ8Seed = 0x4B400000u;           // 12582912.0f
 constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kNT >> 3) << 17) |
                               ((uint32_t)(kMT >> 4) << 24);   // s32 D, s8 A and B, K-major, M=128, N=kNT
@@ -596,20 +598,24 @@ __device__ __forceinline__ void umma_i8_ss(uint32_t tmem_d, uint64_t adesc, uint
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %4, p;\n\t}\n"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(kIdescI8));
 }
-// 16 columns of this warp's lanes, loaded before return.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+// 32 columns of this warp's lanes, loaded before return.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr)
       : "memory");
 }
-// The same 32-bit value into 16 columns of this warp's lanes, completed before return.
-__device__ __forceinline__ void tmem_fill16_sync(uint32_t taddr, uint32_t v) {
+// The same 32-bit value into 32 columns of this warp's lanes, completed before return.
+__device__ __forceinline__ void tmem_fill32_sync(uint32_t taddr, uint32_t v) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};\n\t"
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};\n\t"
       "tcgen05.wait::st.sync.aligned;" ::"r"(taddr), "r"(v)
       : "memory");
 }
@@ -649,7 +655,7 @@ __global__ void gemm_act_q8_0_kernel(const float* __restrict__ x, int64_t x_stri
   }
 }
 
-__global__ void __launch_bounds__(kQ8Threads, 1)
+__global__ void __launch_bounds__(kQ8Threads, 2)
     gemm_q8_0_kernel(const GemmQ8P p, const __grid_constant__ CUtensorMap wmap) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -684,7 +690,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+                 "r"(kQ8TmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -738,14 +744,14 @@ __global__ void __launch_bounds__(kQ8Threads, 1)
       mbar_wait_bounded(mma_done, 0, p.status, 64);
     }
   } else {
-    // ---------------- epilogue: thread = one weight row (TMEM lane), 16 tokens ----------------
-    constexpr int NE = kNT / 4;
+    // ---------------- epilogue: thread = one weight row (TMEM lane), 32 tokens ----------------
+    constexpr int NE = kNT / 2;
     const int qt = warp & 3, eh = (warp - 2) >> 2;
     const int r = qt * 32 + lane;
     const uint32_t tl = tmem + ((uint32_t)(qt * 32) << 16) + eh * NE;
     // seed both buffers, then hand them to the MMA issuer
 #pragma unroll
-    for (int c = 0; c < 2 * kQ8G; ++c) tmem_fill16_sync(tl + c * kNT, kQ8Seed);
+    for (int c = 0; c < 2 * kQ8G; ++c) tmem_fill32_sync(tl + c * kNT, kQ8Seed);
     tc_fence_before();
     mbar_arrive(&acc_empty[0]);
     mbar_arrive(&acc_empty[1]);
@@ -754,33 +760,38 @@ __global__ void __launch_bounds__(kQ8Threads, 1)
     for (int t = 0; t < NE / 2; ++t) out[t] = make_float2(0.0f, 0.0f);
     const float2 one2 = make_float2(p.one, p.one), nz2 = make_float2(p.nzero, p.nzero),
                  nseed2 = make_float2(p.nseed, p.nseed);
+    const int dw_off = (r >> 3) * 272 + 256 + (r & 7) * 2;
     for (int g = 0; g < ng; ++g) {
       const int b = g & 1, st = g % kQ8Stages, gb = min(kQ8G, nb - g * kQ8G);
       wait_full(&acc_full[b], g / 2, p.status, 65, abort_flag);
       tc_fence_after();
       wait_full(&st_full[st], g / kQ8Stages, p.status, 66, abort_flag);   // complete already: orders the smem reads
       const uint8_t* sp = stages + st * kQ8Stage;
-      for (int j = 0; j < gb; ++j) {
-        const float dw = h2f(*reinterpret_cast<const uint16_t*>(sp + j * kQ8A + (r >> 3) * 272 + 256 + (r & 7) * 2));
-        const float2 dw2 = make_float2(dw, dw);
-        const float4* dx4 = reinterpret_cast<const float4*>(sp + kQ8G * (kQ8A + kQ8B) + j * kQ8Dx) + eh * (NE / 4);
-        uint32_t v[16];
-        tmem_ld16(tl + b * (kQ8G * kNT) + j * kNT, v);
 #pragma unroll
-        for (int q4 = 0; q4 < NE / 4; ++q4) {
-          const float4 dx = dx4[q4];
+      for (int j = 0; j < kQ8G; ++j) {
+        if (j < gb) {
+          const float dw = h2f(*reinterpret_cast<const uint16_t*>(sp + j * kQ8A + dw_off));
+          const float2 dw2 = make_float2(dw, dw);
+          const float4* dx4 = reinterpret_cast<const float4*>(sp + kQ8G * (kQ8A + kQ8B) + j * kQ8Dx) + eh * (NE / 4);
+          uint32_t v[NE];
+          tmem_ld32(tl + b * (kQ8G * kNT) + j * kNT, v);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int t2 = q4 * 2 + h;
-            const float2 sumi = fma2(make_float2(__uint_as_float(v[2 * t2]), __uint_as_float(v[2 * t2 + 1])), one2, nseed2);
-            const float2 dd = fma2(dw2, h ? make_float2(dx.z, dx.w) : make_float2(dx.x, dx.y), nz2);
-            out[t2] = fma2(fma2(dd, sumi, nz2), one2, out[t2]);
+          for (int q4 = 0; q4 < NE / 4; ++q4) {
+            const float4 dx = dx4[q4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int t2 = q4 * 2 + h;
+              const float2 sumi =
+                  fma2(make_float2(__uint_as_float(v[2 * t2]), __uint_as_float(v[2 * t2 + 1])), one2, nseed2);
+              const float2 dd = fma2(dw2, h ? make_float2(dx.z, dx.w) : make_float2(dx.x, dx.y), nz2);
+              out[t2] = fma2(fma2(dd, sumi, nz2), one2, out[t2]);
+            }
           }
         }
       }
       mbar_arrive(&st_empty[st]);
 #pragma unroll
-      for (int c = 0; c < kQ8G; ++c) tmem_fill16_sync(tl + b * (kQ8G * kNT) + c * kNT, kQ8Seed);
+      for (int c = 0; c < kQ8G; ++c) tmem_fill32_sync(tl + b * (kQ8G * kNT) + c * kNT, kQ8Seed);
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
@@ -798,7 +809,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kQ8TmemCols) : "memory");
   }
 }
 

@@ -743,9 +743,24 @@ __global__ void kv_compact_kernel(uint16_t* __restrict__ kc, uint16_t* __restric
 // feed (device-side greedy loop) it also makes the id the next step's token of
 // row b, advances the row's position and appends the id to the row's output
 // list; the step's other kernels have finished reading tok/pos by then.
+// Each token's vocabulary is scanned by np CTAs (contiguous slices); the last
+// of them to finish (arrival counter) merges the slices' (top-1, top-2, id)
+// and writes the result.  The merge is order-independent: the top-1 is the
+// largest value with the lowest id, the top-2 the largest of the rest.
+// Top-1 / top-2 merge with the reference's tie rule (the lower index wins).
+__device__ __forceinline__ void top2_merge(float& v1, float& v2, int& i1, float a1, float a2, int ai) {
+  if (a1 > v1 || (a1 == v1 && ai < i1)) {
+    v2 = fmaxf(v1, a2);
+    v1 = a1;
+    i1 = ai;
+  } else {
+    v2 = fmaxf(v2, a1);
+  }
+}
+
 __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n_vocab, int v_local,
                               int32_t* __restrict__ ids, float* __restrict__ top, GreedyFeed feed, PeerIn in,
-                              int* status) {
+                              int* status, uint32_t* __restrict__ part, unsigned int* __restrict__ count) {
   pdl_wait();
   if (!feed.tok) pdl_launch_dependents();
   if (in.n) {   // the ranks' head shards arrive in the gather layout
@@ -755,17 +770,25 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n
     }
     __syncthreads();
   }
-  const int b = blockIdx.x;
+  // CTA (pi, b) scans vocabulary slice pi of token b: contiguous runs of the
+  // [shard][n_tok][v_local] gather layout, one run per shard it crosses.
+  const int b = blockIdx.y, np = gridDim.x, pi = blockIdx.x;
+  const int per = (n_vocab + np - 1) / np;
+  const int va = pi * per, vb = min(n_vocab, va + per);
   float v1 = -FLT_MAX, v2 = -FLT_MAX;
   int i1 = 0x7fffffff;
-  for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) {
-    const float x = __ldcg(logits + (int64_t)(v / v_local) * n_tok * v_local + (int64_t)b * v_local + v % v_local);
-    if (x > v1 || (x == v1 && v < i1)) {
-      v2 = v1;
-      v1 = x;
-      i1 = v;
-    } else if (x > v2) {
-      v2 = x;
+  for (int r = va / v_local; r * v_local < vb; ++r) {
+    const int a = max(va, r * v_local), e = min(vb, (r + 1) * v_local);
+    const float* row = logits + ((int64_t)r * n_tok + b) * v_local - (int64_t)r * v_local;   // indexed by v
+    for (int v = a + (int)threadIdx.x; v < e; v += blockDim.x) {
+      const float x = __ldcg(row + v);
+      if (x > v1 || (x == v1 && v < i1)) {
+        v2 = v1;
+        v1 = x;
+        i1 = v;
+      } else if (x > v2) {
+        v2 = x;
+      }
     }
   }
   __shared__ float s1[32], s2[32];
@@ -775,13 +798,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n
     const float a1 = __shfl_xor_sync(0xffffffffu, v1, o);
     const float a2 = __shfl_xor_sync(0xffffffffu, v2, o);
     const int ai = __shfl_xor_sync(0xffffffffu, i1, o);
-    if (a1 > v1 || (a1 == v1 && ai < i1)) {
-      v2 = fmaxf(v1, a2);
-      v1 = a1;
-      i1 = ai;
-    } else {
-      v2 = fmaxf(v2, a1);
-    }
+    top2_merge(v1, v2, i1, a1, a2, ai);
   }
   const int w = threadIdx.x >> 5;
   if ((threadIdx.x & 31) == 0) {
@@ -790,28 +807,37 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n
     si[w] = i1;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float b1 = s1[0], b2 = s2[0];
-    int bi = si[0];
-    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) {
-      if (s1[k] > b1 || (s1[k] == b1 && si[k] < bi)) {
-        b2 = fmaxf(b1, s2[k]);
-        b1 = s1[k];
-        bi = si[k];
-      } else {
-        b2 = fmaxf(b2, s1[k]);
-      }
-    }
-    ids[b] = bi;
-    top[2 * b] = b1;
-    top[2 * b + 1] = b1 - b2;
-    if (feed.tok) {
-      feed.tok[b] = bi;
-      feed.pos[b] += 1;
-      const int t = feed.count[b];
-      if (t < feed.cap) feed.out[(int64_t)t * n_tok + b] = bi;
-      feed.count[b] = t + 1;
-    }
+  if (threadIdx.x != 0) return;
+  float b1 = s1[0], b2 = s2[0];
+  int bi = si[0];
+  for (int k = 1; k < (int)(blockDim.x >> 5); ++k) top2_merge(b1, b2, bi, s1[k], s2[k], si[k]);
+  if (np > 1) {
+    // the last CTA of token b to finish merges the slices
+    uint32_t* pp = part + ((int64_t)b * np + pi) * 3;
+    pp[0] = __float_as_uint(b1);
+    pp[1] = __float_as_uint(b2);
+    pp[2] = (uint32_t)bi;
+    __threadfence();
+    if (atomicAdd(&count[b], 1u) != (unsigned int)(np - 1)) return;
+    __threadfence();
+    const uint32_t* p0 = part + (int64_t)b * np * 3;
+    b1 = __uint_as_float(__ldcg(p0));
+    b2 = __uint_as_float(__ldcg(p0 + 1));
+    bi = (int)__ldcg(p0 + 2);
+    for (int k = 1; k < np; ++k)
+      top2_merge(b1, b2, bi, __uint_as_float(__ldcg(p0 + 3 * k)), __uint_as_float(__ldcg(p0 + 3 * k + 1)),
+                 (int)__ldcg(p0 + 3 * k + 2));
+    count[b] = 0;   // ready for the next launch
+  }
+  ids[b] = bi;
+  top[2 * b] = b1;
+  top[2 * b + 1] = b1 - b2;
+  if (feed.tok) {
+    feed.tok[b] = bi;
+    feed.pos[b] += 1;
+    const int t = feed.count[b];
+    if (t < feed.cap) feed.out[(int64_t)t * n_tok + b] = bi;
+    feed.count[b] = t + 1;
   }
 }
 
@@ -943,9 +969,16 @@ int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, con
 }
 
 int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s,
-                  const GreedyFeed& feed, const PeerIn* in, int* status) {
-  return launch_pdl(argmax_kernel, dim3(n_tok), dim3(1024), 0, s, logits, n_tok, n_vocab, v_local, ids, top, feed,
-                    in ? *in : PeerIn{}, status);
+                  const GreedyFeed& feed, const PeerIn* in, int* status, uint32_t* scratch) {
+  // With scratch, each token's vocabulary is split over up to kArgmaxParts
+  // CTAs (the last one merges); without, one CTA per token.
+  const int np = scratch ? std::max(1, std::min(kArgmaxParts, n_vocab / 2048)) : 1;
+  B2_CHECK_ARG(n_tok >= 1 && n_tok <= kArgmaxTok, "argmax: too many tokens");
+  uint32_t* part = scratch;
+  unsigned int* count = scratch ? reinterpret_cast<unsigned int*>(scratch + (size_t)kArgmaxTok * kArgmaxParts * 3)
+                                : nullptr;
+  return launch_pdl(argmax_kernel, dim3(np, n_tok), dim3(np > 1 ? 256 : 1024), 0, s, logits, n_tok, n_vocab, v_local,
+                    ids, top, feed, in ? *in : PeerIn{}, status, part, count);
 }
 
 }  // namespace b2

@@ -59,7 +59,13 @@ struct GreedyFeed {
   int32_t* count = nullptr;  // [n_tok] ids appended so far
   int cap = 0;
 };
+// Greedy top-1 (lowest index on ties) and top-1 − top-2 margin per token.
+// `scratch` (argmax_scratch_words() words, zero before the first launch and
+// left zero by every launch) lets each token's scan spread over many CTAs.
+constexpr int kArgmaxParts = 64, kArgmaxTok = 8;
+constexpr size_t argmax_scratch_words() { return (size_t)kArgmaxTok * kArgmaxParts * 3 + kArgmaxTok; }
 int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s,
-                  const GreedyFeed& feed = GreedyFeed{}, const PeerIn* in = nullptr, int* status = nullptr);
+                  const GreedyFeed& feed = GreedyFeed{}, const PeerIn* in = nullptr, int* status = nullptr,
+                  uint32_t* scratch = nullptr);
 
 }  // namespace b2
