@@ -690,6 +690,11 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
             if (item * P + pp < p.n_tiles) tx += bytes;
           mbar_arrive_expect_tx(&full[sl], tx);
           uint8_t* sp = ring + (size_t)sl * p.stage_bytes;
+          if (ni == p.L && tx == (uint32_t)P * bytes) {
+            // whole tiles, all live: the P tiles are adjacent in memory, one copy
+            bulk_g2s(sp, p.w + item * P * p.tile_bytes, tx, &full[sl]);
+            continue;
+          }
           for (int pp = 0; pp < P; ++pp) {
             const int64_t tile = item * P + pp;
             if (tile < p.n_tiles)
@@ -975,10 +980,13 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.act_img = in_kernel ? nullptr : a.act_img;
   if (a.epilogue == EPI_ROPE_KV) p.rope = *a.rope;
   // Stages of P tiles x U unit steps of all S ranges.  mma: one tile pair per
-  // stage, U as large as fits ~20 KB (bulk copies of ~9 KB or more: smaller
-  // ones cost streaming bandwidth), and whole rings of nss >= 2 slots for
-  // each of the nset consumer sets (smaller U, or the full shared memory,
-  // where needed); dp4a: P = 8/S tiles, ~32 KB.  With small activations stay
+  // stage, U as large as fits (up to whole tiles: then the stage is one bulk
+  // copy of up to ~128 KB).  An SM's bulk copies are served at a near-fixed
+  // rate of copies, not bytes, so few large copies stream fastest: measured
+  // on the 8B shapes, whole-tile stages with one slot per consumer set beat
+  // ~18 KB stages with two slots per set (gate/up 26.3 -> 23.1 us, head 161
+  // -> 133 us).  Where whole tiles do not fit, the largest U that gives every
+  // set a slot.  dp4a: P = 8/S tiles, ~32 KB.  With small activations stay
   // within ~100 KB when that still gives the pipeline it needs, so that two
   // CTAs fit on an SM and the next launch's producer can stream while this
   // one drains.
@@ -990,7 +998,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   int U = 0, ns = 0;
   size_t stage = 0;
   auto fit = [&](size_t cap_, int want_per_set) -> bool {
-    for (int u = std::min<int>(w.ulen, (int)std::max<size_t>(1, (mma ? 20 * 1024 : 32 * 1024) / step_b)); u >= 1;
+    for (int u = std::min<int>(w.ulen, (int)std::max<size_t>(1, (mma ? 128 * 1024 : 32 * 1024) / step_b)); u >= 1;
          --u) {
       const size_t st = step_b * u;
       if (fixed + st > cap_) continue;
@@ -1005,8 +1013,8 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
     }
     return false;
   };
-  const bool ok_fit = (in_kernel && fit(100 * 1024, mma ? 2 : 3)) || fit((size_t)kSmemCap, 2) ||
-                      fit((size_t)kSmemCap, 1);
+  const bool ok_fit = (in_kernel && fit(100 * 1024, mma ? 2 : 3)) || (mma && fit((size_t)kSmemCap, 1)) ||
+                      fit((size_t)kSmemCap, 2) || fit((size_t)kSmemCap, 1);
   if (!ok_fit) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
