@@ -53,11 +53,11 @@ struct DevQ {
 
 // Uploads rows given by pointers to their first byte (all rows k values of
 // `type` starting at the slice's first column).
-int upload_rows(DevQ& q, int type, int64_t k, const std::vector<const uint8_t*>& rows) {
+int upload_rows(DevQ& q, int type, int64_t k, const std::vector<const uint8_t*>& rows, UploadStager* st) {
   q.m.type = type;
   q.m.n_rows = (int64_t)rows.size();
   q.m.k = k;
-  return upload_tiles(q.m, rows.data());
+  return upload_tiles(q.m, rows.data(), st);
 }
 
 struct Layer {
@@ -268,6 +268,9 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
   m->device_bytes += (int64_t)te->bytes;
   int rc = upload_f32(tn, d, &m->out_norm);
   if (rc) return rc;
+  // One pinned double-buffered stager for every weight matrix: repacking on
+  // the host overlaps the copies of the previous slab.
+  UploadStager stager;
   // Output head: vocabulary rows [r*v_l, (r+1)*v_l).
   m->out_type = to->type;
   if (!is_weight_type(to->type)) {
@@ -278,7 +281,7 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
     std::vector<const uint8_t*> rows;
     const size_t rb = row_bytes(to->type, d);
     for (int64_t i = 0; i < m->v_l; ++i) rows.push_back(to->data + (size_t)(r * (int64_t)m->v_l + i) * rb);
-    if ((rc = upload_rows(m->head, to->type, d, rows))) return rc;
+    if ((rc = upload_rows(m->head, to->type, d, rows, &stager))) return rc;
   }
   for (int l = 0; l < m->n_layer; ++l) {
     auto L = std::make_unique<Layer>();
@@ -304,7 +307,7 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
       for (int64_t i = 0; i < (int64_t)m->nh_l * hd; ++i) rows.push_back(wq->data + ((int64_t)r * m->nh_l * hd + i) * rb);
       for (int64_t i = 0; i < (int64_t)m->nkv_l * hd; ++i) rows.push_back(wk->data + ((int64_t)r * m->nkv_l * hd + i) * rb);
       for (int64_t i = 0; i < (int64_t)m->nkv_l * hd; ++i) rows.push_back(wv->data + ((int64_t)r * m->nkv_l * hd + i) * rb);
-      if ((rc = upload_rows(L->wqkv, wq->type, d, rows))) return rc;
+      if ((rc = upload_rows(L->wqkv, wq->type, d, rows, &stager))) return rc;
     }
     // O: all rows, input columns of this rank's heads.
     {
@@ -316,7 +319,7 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
       std::vector<const uint8_t*> rows;
       const size_t rb = row_bytes(wo->type, k_all), off = row_bytes(wo->type, r * k_l);
       for (int64_t i = 0; i < d; ++i) rows.push_back(wo->data + i * rb + off);
-      if ((rc = upload_rows(L->wo, wo->type, k_l, rows))) return rc;
+      if ((rc = upload_rows(L->wo, wo->type, k_l, rows, &stager))) return rc;
     }
     // gate/up interleaved (gate_i, up_i) for this rank's FFN features.
     {
@@ -326,7 +329,7 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
         rows.push_back(wg->data + ((int64_t)r * m->ff_l + i) * rb);
         rows.push_back(wu->data + ((int64_t)r * m->ff_l + i) * rb);
       }
-      if ((rc = upload_rows(L->wgu, wg->type, d, rows))) return rc;
+      if ((rc = upload_rows(L->wgu, wg->type, d, rows, &stager))) return rc;
     }
     // down: all rows, input columns of this rank's FFN features.
     {
@@ -337,14 +340,14 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
       std::vector<const uint8_t*> rows;
       const size_t rb = row_bytes(wd->type, m->n_ff), off = row_bytes(wd->type, (int64_t)r * m->ff_l);
       for (int64_t i = 0; i < d; ++i) rows.push_back(wd->data + i * rb + off);
-      if ((rc = upload_rows(L->wdown, wd->type, m->ff_l, rows))) return rc;
+      if ((rc = upload_rows(L->wdown, wd->type, m->ff_l, rows, &stager))) return rc;
     }
     for (const DevQ* q : {&L->wqkv, &L->wo, &L->wgu, &L->wdown}) m->device_bytes += q->m.bytes();
     m->device_bytes += 2 * d * 4;
     m->layers.push_back(std::move(L));
   }
   m->device_bytes += m->head.m.bytes();
-  return B2_OK;
+  return stager.finish();
 }
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }

@@ -77,10 +77,51 @@ void plan_qmatrix(QMatrix& m) {
   m.tile_bytes = (int64_t)m.splits * m.ulen * m.slot_bytes;
 }
 
-int upload_tiles(QMatrix& m, const uint8_t* const* rows) {
+UploadStager::~UploadStager() {
+  if (stream) cudaStreamSynchronize(stream);
+  for (int b = 0; b < 2; ++b) {
+    if (h[b]) cudaFreeHost(h[b]);
+    if (ev[b]) cudaEventDestroy(ev[b]);
+  }
+  if (stream) cudaStreamDestroy(stream);
+}
+
+int UploadStager::init(size_t per_buffer) {
+  if (!stream) {
+    B2_CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    for (int b = 0; b < 2; ++b) B2_CUDA_TRY(cudaEventCreateWithFlags(&ev[b], cudaEventDisableTiming));
+  }
+  if (per_buffer <= bytes) return B2_OK;
+  B2_CUDA_TRY(cudaStreamSynchronize(stream));
+  for (int b = 0; b < 2; ++b) {
+    if (h[b]) cudaFreeHost(h[b]);
+    h[b] = nullptr;
+  }
+  bytes = 0;
+  for (int b = 0; b < 2; ++b) {
+    const cudaError_t e = cudaMallocHost(&h[b], per_buffer);
+    if (e != cudaSuccess) {
+      set_error("upload staging: pinned allocation of %zu bytes: %s", per_buffer, cudaGetErrorString(e));
+      return B2_ERR_OOM;
+    }
+  }
+  bytes = per_buffer;
+  return B2_OK;
+}
+
+int UploadStager::finish() {
+  if (stream) B2_CUDA_TRY(cudaStreamSynchronize(stream));
+  return B2_OK;
+}
+
+int upload_tiles(QMatrix& m, const uint8_t* const* rows, UploadStager* st) {
   plan_qmatrix(m);
   cudaGetDevice(&m.device);
   m.data = nullptr;
+  UploadStager local;
+  if (!st) st = &local;
+  int rc = st->init(std::max<size_t>((size_t)64 << 20, (size_t)m.tile_bytes));
+  if (rc) return rc;
   const int64_t bytes = m.bytes();
   cudaError_t e = cudaMalloc(&m.data, (size_t)std::max<int64_t>(bytes, 16));
   if (e != cudaSuccess) {
@@ -88,36 +129,40 @@ int upload_tiles(QMatrix& m, const uint8_t* const* rows) {
     set_error("matrix upload: device allocation of %lld bytes: %s", (long long)bytes, cudaGetErrorString(e));
     return B2_ERR_OOM;
   }
-  // Slabs of whole tiles through a pinned staging buffer, tiles split over threads.
-  const int64_t slab = std::max<int64_t>(1, (int64_t)(64 << 20) / std::max<int64_t>(1, m.tile_bytes));
-  uint8_t* h = nullptr;
-  e = cudaMallocHost(&h, (size_t)(std::min(slab, m.n_tiles) * m.tile_bytes));
-  if (e != cudaSuccess) {
-    cudaFree(m.data);
-    m.data = nullptr;
-    set_error("matrix upload: pinned staging: %s", cudaGetErrorString(e));
-    return B2_ERR_OOM;
-  }
+  // Slabs of whole tiles, alternating between the two pinned buffers: a
+  // buffer is refilled once its previous copy has completed; the tiles of a
+  // slab are split over host threads.
+  const int64_t slab = std::max<int64_t>(1, (int64_t)st->bytes / std::max<int64_t>(1, m.tile_bytes));
   const int nt = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
-  int rc = B2_OK;
-  for (int64_t t0 = 0; t0 < m.n_tiles; t0 += slab) {
+  for (int64_t t0 = 0; t0 < m.n_tiles && rc == B2_OK; t0 += slab) {
     const int64_t t1 = std::min(m.n_tiles, t0 + slab), n = t1 - t0;
-    auto work = [&](int64_t a, int64_t b) {
-      if (b > a) repack_tiles_host(m, rows, a, b, h + (a - t0) * m.tile_bytes);
+    const int b = st->next;
+    st->next ^= 1;
+    e = cudaEventSynchronize(st->ev[b]);
+    if (e != cudaSuccess) {
+      set_error("matrix upload: staging wait: %s", cudaGetErrorString(e));
+      rc = B2_ERR_CUDA;
+      break;
+    }
+    uint8_t* h = st->h[b];
+    auto work = [&](int64_t a, int64_t c) {
+      if (c > a) repack_tiles_host(m, rows, a, c, h + (a - t0) * m.tile_bytes);
     };
     std::vector<std::thread> th;
     for (int t = 1; t < nt; ++t) th.emplace_back(work, t0 + n * t / nt, t0 + n * (t + 1) / nt);
     work(t0, t0 + n / nt);
     for (auto& x : th) x.join();
-    e = cudaMemcpy(m.data + t0 * m.tile_bytes, h, (size_t)(n * m.tile_bytes), cudaMemcpyHostToDevice);
+    e = cudaMemcpyAsync(m.data + t0 * m.tile_bytes, h, (size_t)(n * m.tile_bytes), cudaMemcpyHostToDevice,
+                        st->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(st->ev[b], st->stream);
     if (e != cudaSuccess) {
       set_error("matrix upload: copy: %s", cudaGetErrorString(e));
       rc = B2_ERR_CUDA;
-      break;
     }
   }
-  cudaFreeHost(h);
+  if (rc == B2_OK && st == &local) rc = st->finish();
   if (rc != B2_OK) {
+    st->finish();
     cudaFree(m.data);
     m.data = nullptr;
   }

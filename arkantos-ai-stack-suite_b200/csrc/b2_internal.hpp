@@ -158,9 +158,28 @@ void plan_qmatrix(QMatrix& m);
 // Repacks into host buffer `out` the tiles [t0, t1); row r's GGUF bytes are
 // at rows[r] (rows past n_rows are zero).
 void repack_tiles_host(const QMatrix& m, const uint8_t* const* rows, int64_t t0, int64_t t1, uint8_t* out);
+// Pinned, double-buffered staging for weight uploads: the host threads
+// repack one slab while the previous slab is copied to the device on the
+// stager's stream.  One stager serves a whole model load (pinning memory is
+// costly); finish() waits for every copy issued.
+struct UploadStager {
+  uint8_t* h[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  cudaStream_t stream = nullptr;
+  size_t bytes = 0;   // per buffer
+  int next = 0;
+  UploadStager() = default;
+  UploadStager(const UploadStager&) = delete;
+  UploadStager& operator=(const UploadStager&) = delete;
+  ~UploadStager();
+  int init(size_t per_buffer);
+  int finish();
+};
 // Plans m (type, n_rows, k set), allocates m.data on the current device and
-// uploads the repacked tiles; rows[r] points at row r's GGUF bytes.
-int upload_tiles(QMatrix& m, const uint8_t* const* rows);
+// uploads the repacked tiles; rows[r] points at row r's GGUF bytes.  With a
+// stager the copies may still be in flight on return (the stager's finish()
+// completes them); without one the call stages through its own and waits.
+int upload_tiles(QMatrix& m, const uint8_t* const* rows, UploadStager* st = nullptr);
 
 // ---- planar quantized activations (device) ---------------------------------------
 // B token rows of kp values: qs [B][kp] int8 (zero beyond k), d [B][kp/32]
