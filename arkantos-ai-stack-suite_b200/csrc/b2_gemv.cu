@@ -380,24 +380,23 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
       const uint4 xa = act_chunk16(trow, 2 * u), xb = act_chunk16(trow, 2 * u + 1);
       int s;
       if constexpr (WT == B2_Q4_0) {
-        s = dp4a_us(lo[0], xa.x, 0);
-        s = dp4a_us(lo[1], xa.y, s);
-        s = dp4a_us(lo[2], xa.z, s);
-        s = dp4a_us(lo[3], xa.w, s);
-        s = dp4a_us(hi[0], xb.x, s);
-        s = dp4a_us(hi[1], xb.y, s);
-        s = dp4a_us(hi[2], xb.z, s);
-        s = dp4a_us(hi[3], xb.w, s);
-        s -= 8 * (int)bss[t * p.nu + u];
+        int s0 = dp4a_us(lo[0], xa.x, 0), s1 = dp4a_us(hi[0], xb.x, 0);
+        s0 = dp4a_us(lo[1], xa.y, s0);
+        s1 = dp4a_us(hi[1], xb.y, s1);
+        s0 = dp4a_us(lo[2], xa.z, s0);
+        s1 = dp4a_us(hi[2], xb.z, s1);
+        s0 = dp4a_us(lo[3], xa.w, s0);
+        s1 = dp4a_us(hi[3], xb.w, s1);
+        s = s0 + s1 - 8 * (int)bss[t * p.nu + u];
       } else {
-        s = dp4a_ss(lo[0], xa.x, 0);
-        s = dp4a_ss(lo[1], xa.y, s);
-        s = dp4a_ss(lo[2], xa.z, s);
-        s = dp4a_ss(lo[3], xa.w, s);
-        s = dp4a_ss(hi[0], xb.x, s);
-        s = dp4a_ss(hi[1], xb.y, s);
-        s = dp4a_ss(hi[2], xb.z, s);
-        s = dp4a_ss(hi[3], xb.w, s);
+        int s0 = dp4a_ss(lo[0], xa.x, 0), s1 = dp4a_ss(hi[0], xb.x, 0);
+        s0 = dp4a_ss(lo[1], xa.y, s0);
+        s1 = dp4a_ss(hi[1], xb.y, s1);
+        s0 = dp4a_ss(lo[2], xa.z, s0);
+        s1 = dp4a_ss(hi[2], xb.z, s1);
+        s0 = dp4a_ss(lo[3], xa.w, s0);
+        s1 = dp4a_ss(hi[3], xb.w, s1);
+        s = s0 + s1;
       }
       acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, dxs[t * p.nu + u]), (float)s));
     }
@@ -793,6 +792,7 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
           // this stage holds units [ua, ub) of the warp's range; the four lane
           // groups take four consecutive units (residues 0..3) at once
           const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);
+#pragma unroll 4
           for (int u4 = ua & ~3; u4 < ub; u4 += 4) {
             const int u = u4 + dq;
             if (u >= ua && u < ub) dp4a_unit<WT, NB>(p, rbase + (size_t)(u - ua) * us, act, u, dg, dacc);
