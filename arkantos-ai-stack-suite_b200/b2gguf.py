@@ -81,6 +81,7 @@ def _bind() -> None:
         "b2_quantize_act": (_i, [_i, _vp, _i, _i64, _vp, _vp]),
         "b2_gemv": (_i, [_vp, _vp, _i, _vp, _vp]),
         "b2_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _sz, _vp, _vp]),
+        "b2_gemv_multi": (_i, [_vp, _i, _vp, _i, _vp, _vp]),
         "b2_gemm_workspace_bytes": (_i, [_vp, _i, _vp]),
         "b2_gemm_host": (_i, [_vp, _vp, _i, _vp]),
         "b2_gemv_host": (_i, [_vp, _vp, _i, _vp]),
@@ -307,6 +308,15 @@ def rope_table(theta: float, head_dim: int, p0: int, n_pos: int) -> np.ndarray:
 
 
 # ---- quantized matrices and single ops --------------------------------------------------------
+def gemv_multi(mats, x: "DeviceBuffer", n_tok: int, ys, stream: int | None = None) -> None:
+    """Several GEMVs of one type and shape over the same device input in one
+    launch (1-2 tokens): ys[i] = mats[i]·x, each bit-identical to gemv_device."""
+    n = len(mats)
+    hs = (ctypes.c_void_p * n)(*[m.h for m in mats])
+    yp = (ctypes.c_void_p * n)(*[y.ptr for y in ys])
+    check(lib.b2_gemv_multi(hs, n, x.ptr, n_tok, yp, stream), "gemv_multi")
+
+
 class QMatrix:
     """A GGUF tensor uploaded to the current device in the repacked layout."""
 

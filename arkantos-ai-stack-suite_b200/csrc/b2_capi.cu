@@ -264,6 +264,34 @@ int b2_quantize_act(int act_type, const float* x, int n_tok, int64_t k, void* bl
   return rc;
 }
 
+int b2_gemv_multi(const b2_qmatrix* const* w, int n_mat, const float* x, int n_tok, float* const* y, void* stream) {
+  B2_CHECK_ARG(w && x && y && n_mat >= 1 && n_mat <= 64 && n_tok >= 1 && n_tok <= 2, "gemv_multi arguments");
+  std::vector<const QMatrix*> ws((size_t)n_mat);
+  for (int i = 0; i < n_mat; ++i) {
+    B2_CHECK_ARG(w[i] && y[i], "gemv_multi: null matrix or output");
+    ws[(size_t)i] = &w[i]->m;
+  }
+  GemvArgs a = {};
+  a.w = ws[0];
+  a.x = x;
+  a.x_stride = w[0]->m.k;
+  a.n_tok = n_tok;
+  a.y = y[0];
+  a.y_stride = w[0]->m.n_rows;
+  a.epilogue = EPI_STORE;
+  a.n_mat = n_mat;
+  a.wlist = ws.data();
+  a.ylist = y;
+  cudaStream_t s = as_stream(stream);
+  if (!gemv_needs_image(w[0]->m, n_tok)) return launch_gemv(a, s);
+  B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&a.act_img), gemv_act_image_bytes(w[0]->m, n_tok), s));
+  const int rc = launch_gemv(a, s);
+  const cudaError_t e = cudaFreeAsync(a.act_img, s);
+  if (rc) return rc;
+  B2_CUDA_TRY(e);
+  return B2_OK;
+}
+
 int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stream) {
   B2_CHECK_ARG(w && x && y, "gemv arguments");
   GemvArgs a = {};

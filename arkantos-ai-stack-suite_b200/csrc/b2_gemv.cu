@@ -48,6 +48,7 @@ constexpr int kMaxTok = 8;
 constexpr int kDp4aMaxTok = 2;           // dp4a up to this many tokens, mma.sync above
 constexpr uint32_t kM4 = 0x0F0F0F0Fu;
 
+constexpr int kMaxMat = 64;          // matrices of one multi-matrix launch
 struct GemvP {
   const uint8_t* w;
   int type, nu, S, L, slot_bytes;
@@ -67,6 +68,12 @@ struct GemvP {
   int* status;
   PeerOut peer;
   RopeKvEpi rope;
+  // The matrices of the launch (same type and shape, one shared x): items
+  // run over matrix 0's, then matrix 1's, ...; wl[0] = w, yl[0] = y for one.
+  int n_mat;
+  int64_t ipm;            // items per matrix
+  const uint8_t* wl[kMaxMat];
+  float* yl[kMaxMat];
 };
 
 __device__ __forceinline__ void consumer_sync(int nthreads) {
@@ -497,13 +504,13 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
 
 // Output (token t, row) of the store / residual-add epilogues; with a
 // tensor-parallel exchange the value goes to this rank's slot of every rank.
-__device__ __forceinline__ void store_y(const GemvP& p, int t, int64_t row, float v) {
+__device__ __forceinline__ void store_y(const GemvP& p, float* y, int t, int64_t row, float v) {
   const int64_t off = t * p.y_stride + row;
   if (p.peer.n) {
     for (int j = 0; j < p.peer.n; ++j) p.peer.dst[j][off] = v;
     return;
   }
-  float* yp = p.y + off;
+  float* yp = y + off;
   *yp = p.epilogue == EPI_ACCUM ? __fadd_rn(*yp, v) : v;
 }
 
@@ -570,7 +577,7 @@ __device__ __forceinline__ void rope_kv_store(const RopeKvEpi& e, int t, int64_t
 }
 
 template <int NT>
-__device__ __forceinline__ void finish_tiles(const GemvP& p, const float* red, int64_t t0, int lane) {
+__device__ __forceinline__ void finish_tiles(const GemvP& p, const float* red, int64_t t0, int lane, float* y) {
   constexpr int R = 8 * NT;   // rows per item
   if (p.epilogue == EPI_ROPE_KV) {
     // R/2 row pairs x 8 tokens
@@ -607,7 +614,7 @@ __device__ __forceinline__ void finish_tiles(const GemvP& p, const float* red, i
     const int e = lane + 32 * k;
     const int t = e / R, rr = e % R;
     const int64_t row = t0 * 8 + rr;
-    if (t < p.n_tok && row < p.n_rows) store_y(p, t, row, range_total(red, p.S, R * 8, e));
+    if (t < p.n_tok && row < p.n_rows) store_y(p, y, t, row, range_total(red, p.S, R * 8, e));
   }
 }
 
@@ -651,7 +658,7 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
   // waits on a slot whose previous use (by the same set) is still in flight.
   // Set j works items j, j + NSET, ...; its local stage l is chunk l % n_ch of
   // its item l / n_ch and lives in slot j*nss + l % nss.
-  const int64_t n_items = (p.n_tiles + P - 1) / P;
+  const int64_t n_items = p.ipm * p.n_mat;
   const int64_t g0 = n_items * blockIdx.x / gridDim.x, g1 = n_items * (blockIdx.x + 1) / gridDim.x;
   const int n_ch = (p.L + p.U - 1) / p.U;   // stages per item
   const int nset = MODE == 0 ? min(NW / S, 8) : 1;
@@ -681,7 +688,9 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
           const int sl = j * nss + (int)(l % nss);
           const int64_t use = l / nss;
           if (use > 0 && !mbar_wait_bounded(&empty[sl], (uint32_t)((use - 1) & 1), p.status, 2)) return;
-          const int64_t item = g0 + i;
+          const int64_t gitem = g0 + i;
+          const int64_t mi = gitem / p.ipm, item = gitem - mi * p.ipm;   // matrix, item within it
+          const uint8_t* wm = p.wl[mi];
           const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
           const uint32_t bytes = (uint32_t)ni * S * p.slot_bytes;
           uint32_t tx = 0;
@@ -691,13 +700,13 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
           uint8_t* sp = ring + (size_t)sl * p.stage_bytes;
           if (ni == p.L && tx == (uint32_t)P * bytes) {
             // whole tiles, all live: the P tiles are adjacent in memory, one copy
-            bulk_g2s(sp, p.w + item * P * p.tile_bytes, tx, &full[sl]);
+            bulk_g2s(sp, wm + item * P * p.tile_bytes, tx, &full[sl]);
             continue;
           }
           for (int pp = 0; pp < P; ++pp) {
             const int64_t tile = item * P + pp;
             if (tile < p.n_tiles)
-              bulk_g2s(sp + pp * piece, p.w + tile * p.tile_bytes + (int64_t)i0 * S * p.slot_bytes, bytes, &full[sl]);
+              bulk_g2s(sp + pp * piece, wm + tile * p.tile_bytes + (int64_t)i0 * S * p.slot_bytes, bytes, &full[sl]);
           }
         }
       }
@@ -769,7 +778,7 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
       }
       if (S > 1) tile_sync(set, S * 32);
       else __syncwarp();
-      if (r == 0 && ok) finish_tiles<2>(p, red[it & 1] + set * S * 128, item * 2, lane);
+      if (r == 0 && ok) finish_tiles<2>(p, red[it & 1] + set * S * 128, item * 2, lane, p.y);
     }
   } else {
     const int slot_p = warp / S, r = warp % S;
@@ -778,7 +787,8 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
     float dacc[NB];    // partial sums [token] of residue dq
     int64_t st = 0;
     for (int64_t grp = g0; grp < g1; ++grp) {
-      const int64_t tile = grp * P + slot_p;
+      const int64_t mi = grp / p.ipm;   // matrix of this item
+      const int64_t tile = (grp - mi * p.ipm) * P + slot_p;
       const bool live = tile < p.n_tiles;
 #pragma unroll
       for (int t = 0; t < NB; ++t) dacc[t] = 0.0f;
@@ -811,7 +821,7 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
       }
       if (S > 1) tile_sync(slot_p, S * 32);
       else __syncwarp();
-      if (r == 0 && live && ok) finish_tiles<1>(p, red[grp & 1] + slot_p * S * 64, tile, lane);
+      if (r == 0 && live && ok) finish_tiles<1>(p, red[grp & 1] + slot_p * S * 64, tile, lane, p.yl[mi]);
     }
   }
   if (p.peer.n) {
@@ -944,6 +954,22 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   }
   GemvP p = {};
   p.w = w.data;
+  p.n_mat = a.n_mat;
+  if (a.n_mat == 1) {
+    p.wl[0] = w.data;
+    p.yl[0] = a.y;
+  } else {
+    B2_CHECK_ARG(a.n_mat >= 1 && a.n_mat <= kMaxMat && a.wlist && a.ylist, "multi-matrix GEMV: 1..64 matrices");
+    B2_CHECK_ARG(a.n_tok <= kDp4aMaxTok && a.epilogue == EPI_STORE && !(a.peer && a.peer->n > 0) && !a.image_ready,
+                 "multi-matrix GEMV: 1-2 tokens, plain store");
+    for (int i = 0; i < a.n_mat; ++i) {
+      const QMatrix& wi = *a.wlist[i];
+      B2_CHECK_ARG(wi.data && wi.type == w.type && wi.n_rows == w.n_rows && wi.k == w.k && a.ylist[i],
+                   "multi-matrix GEMV: matrices of one type and shape, an output each");
+      p.wl[i] = wi.data;
+      p.yl[i] = a.ylist[i];
+    }
+  }
   p.type = w.type;
   p.nu = w.nu;
   p.S = w.splits;
@@ -1013,8 +1039,9 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
     }
     return false;
   };
-  const bool ok_fit = (in_kernel && fit(100 * 1024, mma ? 2 : 3)) || (mma && fit((size_t)kSmemCap, 1)) ||
-                      fit((size_t)kSmemCap, 2) || fit((size_t)kSmemCap, 1);
+  // (A multi-matrix launch streams long enough that the deepest ring wins.)
+  const bool ok_fit = (in_kernel && a.n_mat == 1 && fit(100 * 1024, mma ? 2 : 3)) ||
+                      (mma && fit((size_t)kSmemCap, 1)) || fit((size_t)kSmemCap, 2) || fit((size_t)kSmemCap, 1);
   if (!ok_fit) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
@@ -1023,7 +1050,8 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.n_stages = ns;
   p.stage_bytes = (uint32_t)stage;
   const size_t smem = fixed + (size_t)ns * stage;
-  const int64_t items = (w.n_tiles + P - 1) / P;
+  p.ipm = (w.n_tiles + P - 1) / P;
+  const int64_t items = p.ipm * p.n_mat;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), items));
   if (!in_kernel && !a.image_ready) {
     const int qrc = launch_quantize_image(a.x, a.x_stride, a.n_tok, ag, s);

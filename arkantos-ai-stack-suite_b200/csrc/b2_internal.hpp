@@ -287,6 +287,11 @@ struct GemvArgs {
   const PeerOut* peer = nullptr;   // tensor-parallel exchange of the outputs (EPI_STORE only)
   const RopeKvEpi* rope = nullptr; // EPI_ROPE_KV targets
   bool image_ready = false;        // act_img already holds x quantized (x is not read)
+  // Several matrices of w's type and shape over the same x in one launch
+  // (1-2 tokens, plain store): wlist[i] -> ylist[i]; w = wlist[0].
+  int n_mat = 1;
+  const QMatrix* const* wlist = nullptr;
+  float* const* ylist = nullptr;
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 size_t gemv_act_image_bytes(const QMatrix& w, int n_tok);

@@ -23,7 +23,9 @@ Prints one JSON line (rank 0).  Workloads:
               -> GGUF Q4_0, x fp32[4096] N(0,1) seed 1 quantized to Q8_0 in the
               kernel, y fp32[4096].  One step = one GEMV; consecutive steps
               rotate over 48 distinct device copies of W (453 MB > 2x the
-              126 MB L2), so every step streams W from HBM.
+              126 MB L2), so every step streams W from HBM.  `value` runs the
+              K independent GEMVs 48 per b2_gemv_multi launch; "chain" times
+              the same K as one dependent b2_gemv launch each.
 The reference arm (--impl reference) times the CPU oracle (the reference's
 CPU arithmetic restated in C) on the same workload on the host cores.
 """
@@ -160,45 +162,75 @@ def gemv_inputs(b2):
     return q, x
 
 
-def run_gemv_ours(args, dist, rank, world, local):
-    import b2gguf as b2
-    b2.check(b2.lib.b2_set_device(local), "set_device")
+def gemv_q4_0_graphs(b2, steps: int):
+    """The config-1 timed region, K GEMVs over the rotating W copies with one
+    shared x, in two captured forms: `streamed`, the GEMVs in launches of up to
+    GEMV_COPIES independent matrices each (b2_gemv_multi: the weights stream
+    back to back through one pipeline); `chain`, one launch per GEMV, each
+    waiting on the previous one (b2_gemv).  Returns (graphs, stream, launches)."""
     q, x = gemv_inputs(b2)
     mats = [b2.QMatrix(b2.Q4_0, q, GEMV_N, GEMV_K) for _ in range(GEMV_COPIES)]
     xd = b2.DeviceBuffer.from_array(x)
-    yd = b2.DeviceBuffer(GEMV_N * 4)
+    ys = [b2.DeviceBuffer(GEMV_N * 4) for _ in range(GEMV_COPIES)]
     stream = b2.Stream()
 
-    def step(i, s):
-        mats[i % GEMV_COPIES].gemv_device(xd, 1, yd, s)
+    def streamed(s):
+        i = 0
+        while i < steps:
+            n = min(GEMV_COPIES, steps - i)
+            b2.gemv_multi(mats[:n], xd, 1, ys[:n], s)
+            i += n
 
-    for i in range(max(args.warmup, 3)):
-        step(i, stream.h)
+    def chain(s):
+        for i in range(steps):
+            mats[i % GEMV_COPIES].gemv_device(xd, 1, ys[0], s)
+
+    for f in (streamed, chain):
+        f(stream.h)
     stream.synchronize()
-    # The K timed steps are one captured CUDA graph, so host launch overhead
-    # does not leave the GPU idle between GEMVs.
-    graph = b2.Graph(stream, lambda s: [step(i, s) for i in range(args.steps)])
-    graph.launch()
+    graphs = {"streamed": b2.Graph(stream, streamed), "chain": b2.Graph(stream, chain)}
+    for g in graphs.values():
+        g.launch()
     stream.synchronize()
+    launches = {"streamed": -(-steps // GEMV_COPIES), "chain": steps}
+    return graphs, stream, launches, (q, x, mats, xd, ys)
+
+
+def time_graph(b2, g, stream) -> float:
     e0, e1 = b2.Event(), b2.Event()
+    e0.record(stream.h)
+    g.launch()
+    e1.record(stream.h)
+    stream.synchronize()
+    return e0.elapsed_ms(e1)
+
+
+def run_gemv_ours(args, dist, rank, world, local):
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    graphs, stream, launches, keep = gemv_q4_0_graphs(b2, args.steps)
+    q, x, mats = keep[0], keep[1], keep[2]
+    for _ in range(max(args.warmup, 3)):
+        for g in graphs.values():
+            g.launch()
+    stream.synchronize()
     barrier(dist)
     with ClockSampler(local) as clk:
         t_end = time.time() + 0.4           # untimed load so the sampler sees the clocks under work
         while time.time() < t_end:
-            graph.launch()
+            graphs["streamed"].launch()
             stream.synchronize()
-        e0.record(stream.h)
-        graph.launch()
-        e1.record(stream.h)
-        stream.synchronize()
+        ms_total = time_graph(b2, graphs["streamed"], stream)
+        ms_chain = time_graph(b2, graphs["chain"], stream)
         t_end = time.time() + 0.2
         while time.time() < t_end:
-            graph.launch()
+            graphs["streamed"].launch()
             stream.synchronize()
-    ms_total = e0.elapsed_ms(e1)
     ms_total = dist_max(dist, ms_total)
+    ms_chain = dist_max(dist, ms_chain)
     ms_step = ms_total / args.steps
     gbs = GEMV_BYTES * world / (ms_step * 1e-3) / 1e9
+    chain_gbs = GEMV_BYTES * world / (ms_chain / args.steps * 1e-3) / 1e9
 
     # e2e: host x in, host y out, through the C ABI call a host engine makes.
     mats_e2e = mats[:1]
@@ -228,15 +260,20 @@ def run_gemv_ours(args, dist, rank, world, local):
         "dtype": "q4_0 x q8_0 -> int32 -> f32",
         "data": "synthetic: W N(0,0.02) seed 0 -> GGUF Q4_0; x N(0,1) seed 1",
         "config": {"workload": "gemv_q4_0 4096x4096 batch 1 (config 1)", "rotating_weight_copies": GEMV_COPIES,
-                   "l2": "inputs larger than L2 (48 rotating W copies, 453 MB)", "replicas": world},
+                   "l2": "inputs larger than L2 (48 rotating W copies, 453 MB)", "replicas": world,
+                   "timed_region": f"K GEMVs of distinct W copies with one x, {GEMV_COPIES} per b2_gemv_multi launch"},
         "roofline": {"bound": "hbm", "achieved": round(GEMV_BYTES / (ms_step * 1e-3) / 1e9, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(GEMV_BYTES / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                      "traffic": None, "peak_src": peaks["src"],
-                     "algorithmic_bytes_per_launch": GEMV_BYTES},
+                     "algorithmic_bytes_per_launch": GEMV_BYTES * GEMV_COPIES,
+                     "algorithmic_bytes_per_gemv": GEMV_BYTES},
+        "chain": {"value": round(chain_gbs, 1), "unit": "GB/s", "frac": round(chain_gbs / world / peaks["hbm_gbs"], 4),
+                  "ms_per_gemv": ms_chain / args.steps,
+                  "note": "one b2_gemv launch per GEMV, each waiting on the previous (programmatic dependent launch)"},
         "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": GEMV_K * 4,
                 "d2h_bytes_per_step": GEMV_N * 4},
-        "gpu_launches": args.steps,
+        "gpu_launches": launches["streamed"],
         "clocks": clk.summary(),
     }
     if rank == 0:
@@ -246,28 +283,23 @@ def run_gemv_ours(args, dist, rank, world, local):
 
 def gemv_q4_0_measure(b2, steps: int) -> dict:
     """Config-1 Q4_0 GEMV (the metric's second half) on the current device:
-    CUDA-event time of `steps` GEMVs captured in one graph over rotating copies."""
-    q, x = gemv_inputs(b2)
-    mats = [b2.QMatrix(b2.Q4_0, q, GEMV_N, GEMV_K) for _ in range(GEMV_COPIES)]
-    xd = b2.DeviceBuffer.from_array(x)
-    yd = b2.DeviceBuffer(GEMV_N * 4)
-    stream = b2.Stream()
-    for i in range(GEMV_COPIES):
-        mats[i].gemv_device(xd, 1, yd, stream.h)
-    graph = b2.Graph(stream, lambda s: [mats[i % GEMV_COPIES].gemv_device(xd, 1, yd, s) for i in range(steps)])
-    graph.launch()
+    CUDA-event time of `steps` GEMVs captured in one graph over rotating
+    copies, streamed (b2_gemv_multi) and as a dependent chain (b2_gemv)."""
+    graphs, stream, _, keep = gemv_q4_0_graphs(b2, steps)
+    for g in graphs.values():
+        g.launch()
     stream.synchronize()
-    e0, e1 = b2.Event(), b2.Event()
-    e0.record(stream.h)
-    graph.launch()
-    e1.record(stream.h)
-    stream.synchronize()
-    ms = e0.elapsed_ms(e1) / steps
+    ms = time_graph(b2, graphs["streamed"], stream) / steps
+    ms_chain = time_graph(b2, graphs["chain"], stream) / steps
     gbs = GEMV_BYTES / (ms * 1e-3) / 1e9
+    chain_gbs = GEMV_BYTES / (ms_chain * 1e-3) / 1e9
     peaks = measured_peaks()
     return {"metric": "Q4_0 GEMV HBM GB/s (4096x4096, batch 1)", "value": round(gbs, 1), "unit": "GB/s",
             "frac": round(gbs / peaks["hbm_gbs"], 4), "peak": peaks["hbm_gbs"], "ms_per_gemv": ms,
-            "algorithmic_bytes_per_launch": GEMV_BYTES, "launches": steps}
+            "algorithmic_bytes_per_gemv": GEMV_BYTES, "launches": -(-steps // GEMV_COPIES),
+            "form": f"{GEMV_COPIES} independent GEMVs per b2_gemv_multi launch",
+            "chain": {"value": round(chain_gbs, 1), "frac": round(chain_gbs / peaks["hbm_gbs"], 4),
+                      "ms_per_gemv": ms_chain, "form": "one b2_gemv launch per GEMV"}}
 
 
 def cpu_gemv_baseline(q, x, seconds: float) -> dict:

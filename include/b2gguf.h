@@ -156,6 +156,17 @@ B2_API int b2_quantize_act(int act_type, const float* x, int n_tok, int64_t k, v
  * Q8_K for Q4_K/Q6_K).  x fp32 [n_tok][k], y fp32 [n_tok][n_rows]. */
 B2_API int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stream);
 
+/* Several GEMVs over one input in one launch: y[i] = W[i]·x for n_mat
+ * (1..64) matrices of one type and shape, 1-2 tokens; each y[i] (device,
+ * [n_tok][n_rows]) is bit-identical to b2_gemv(W[i], x, ...).  The matrices
+ * stream back to back through one pipeline, with no dependency wait between
+ * them: the form for independent projections of one input, as the
+ * reference's q/k/v matmuls on the same quantized row
+ * (Singularity/src/core/cortex_a5_engine.cpp:1129-1131).  `w` and `y` are
+ * host arrays of handles and device pointers. */
+B2_API int b2_gemv_multi(const b2_qmatrix* const* w, int n_mat, const float* x, int n_tok, float* const* y,
+                         void* stream);
+
 /* Device scratch b2_gemm needs for n_tok tokens (the quantized activations). */
 B2_API int b2_gemm_workspace_bytes(const b2_qmatrix* w, int n_tok, size_t* bytes);
 

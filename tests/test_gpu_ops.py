@@ -119,6 +119,38 @@ def test_gemv_many_items_per_cta(t, n, k, n_tok):
     assert np.array_equal(_bits(got), _bits(O.gemv_dev(t, q, n, k, x))), "not bit-exact with the device order"
 
 
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("n,k,n_tok,n_mat", [(4096, 4096, 1, 5), (200, 2048, 2, 3), (8, 512, 1, 64),
+                                             (1000, 1024, 2, 2), (2048, 14336, 1, 2)])
+def test_gemv_multi_matches_single(t, n, k, n_tok, n_mat):
+    """One launch over several matrices (distinct weights, shared x): every
+    output bit-identical to that matrix's own GEMV, and in the device order."""
+    mats, qs = [], []
+    for i in range(n_mat):
+        q = _weights(t, n, k, 100 + i)
+        qs.append(q)
+        mats.append(b2.QMatrix(t, q, n, k))
+    x = np.random.default_rng(n + k + n_mat).standard_normal((n_tok, k)).astype(np.float32)
+    xd = b2.DeviceBuffer.from_array(x)
+    ys = [b2.DeviceBuffer(n_tok * n * 4) for _ in range(n_mat)]
+    b2.gemv_multi(mats, xd, n_tok, ys)
+    for i in (0, n_mat // 2, n_mat - 1):
+        got = ys[i].download(np.float32).reshape(n_tok, n)
+        assert np.array_equal(_bits(got), _bits(mats[i].gemv(x))), f"matrix {i} differs from its own GEMV"
+        assert np.array_equal(_bits(got), _bits(O.gemv_dev(t, qs[i], n, k, x))), f"matrix {i}: not the device order"
+
+
+def test_gemv_multi_rejects_mixed_shapes_and_batches():
+    a = b2.QMatrix(b2.Q4_0, _weights(b2.Q4_0, 64, 256, 1), 64, 256)
+    c = b2.QMatrix(b2.Q4_0, _weights(b2.Q4_0, 72, 256, 2), 72, 256)
+    xd = b2.DeviceBuffer.from_array(np.zeros((3, 256), np.float32))
+    ys = [b2.DeviceBuffer(3 * 72 * 4) for _ in range(2)]
+    with pytest.raises(Exception):
+        b2.gemv_multi([a, c], xd, 1, ys)
+    with pytest.raises(Exception):
+        b2.gemv_multi([a, a], xd, 3, ys)
+
+
 def test_gemv_config1_q4_0_4096():
     """Q4_0 GEMV 4096x4096, batch 1: W N(0,0.02) seed 0, x N(0,1) seed 1."""
     n = k = 4096
