@@ -309,7 +309,7 @@ def cpu_gemv_baseline(q, x, seconds: float) -> dict:
     O.matmul(O.Q4_0, q, GEMV_N, GEMV_K, xq, nt)
     n = 0
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
+    while n == 0 or time.perf_counter() - t0 < seconds:
         xq = O.quantize_q8_0(x)[0]
         O.matmul(O.Q4_0, q, GEMV_N, GEMV_K, xq, nt)
         n += 1
