@@ -674,6 +674,12 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
       const int64_t items_here = g1 - g0;
       const int64_t max_local = ((items_here + nset - 1) / nset) * n_ch;
       bool act_sent = p.act_img == nullptr;
+      // l = blk * n_ch + ch = use * nss + ring_pos, kept as counters: one
+      // thread issues every stage, so no division (64-bit ones are long
+      // software sequences) sits between a freed slot and its refill.
+      int64_t blk = 0, use = 0;
+      int ch = 0, ring_pos = 0;
+      int64_t mi = p.n_mat > 1 ? g0 / p.ipm : 0;   // matrix cursor (several matrices: one set, items ascend)
       for (int64_t l = 0; l < max_local; ++l) {
         if (l == nss && !act_sent) {
           pdl_wait();
@@ -682,14 +688,13 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
           act_sent = true;
         }
         for (int j = 0; j < nset; ++j) {
-          const int64_t i = j + (int64_t)nset * (l / n_ch);   // item index within the CTA's run
+          const int64_t i = j + (int64_t)nset * blk;   // item index within the CTA's run
           if (i >= items_here) continue;
-          const int ch = (int)(l % n_ch);
-          const int sl = j * nss + (int)(l % nss);
-          const int64_t use = l / nss;
+          const int sl = j * nss + ring_pos;
           if (use > 0 && !mbar_wait_bounded(&empty[sl], (uint32_t)((use - 1) & 1), p.status, 2)) return;
           const int64_t gitem = g0 + i;
-          const int64_t mi = gitem / p.ipm, item = gitem - mi * p.ipm;   // matrix, item within it
+          while (p.n_mat > 1 && (mi + 1) * p.ipm <= gitem) ++mi;
+          const int64_t item = gitem - mi * p.ipm;   // item within matrix mi
           const uint8_t* wm = p.wl[mi];
           const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
           const uint32_t bytes = (uint32_t)ni * S * p.slot_bytes;
@@ -708,6 +713,14 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
             if (tile < p.n_tiles)
               bulk_g2s(sp + pp * piece, wm + tile * p.tile_bytes + (int64_t)i0 * S * p.slot_bytes, bytes, &full[sl]);
           }
+        }
+        if (++ch == n_ch) {
+          ch = 0;
+          ++blk;
+        }
+        if (++ring_pos == nss) {
+          ring_pos = 0;
+          ++use;
         }
       }
       if (!act_sent) {
@@ -743,6 +756,8 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
     const int set = warp / S, r = warp % S;
     const int g = lane >> 2, q = lane & 3;      // D rows g, g+8; tokens 2q, 2q+1
     int it = 0;
+    int ring_pos = 0;      // this set's local stage modulo nss, and its ring pass parity
+    uint32_t ph = 0;
     // (with S = 1 only the first 8 of the 16 warps form sets; the rest idle)
     for (int64_t i = set; set < nset && g0 + i < g1; i += nset, ++it) {
       const int64_t item = g0 + i;
@@ -750,9 +765,12 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
 #pragma unroll
       for (int a = 0; a < 4; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.0f;
       for (int ch = 0; ch < n_ch; ++ch) {
-        const int64_t lst = (int64_t)it * n_ch + ch;   // this set's local stage
-        const int s = set * nss + (int)(lst % nss);
-        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)(lst / nss) & 1u, p.status, 1);
+        const int s = set * nss + ring_pos;   // local stage it*n_ch + ch of this set
+        if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
+        if (++ring_pos == nss) {
+          ring_pos = 0;
+          ph ^= 1u;
+        }
         const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
         const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);   // units of this stage in range r
         if (ok) {
@@ -785,17 +803,22 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
     const int dg = lane & 7, dq = lane >> 3;    // tile row dg, unit residue dq
     constexpr int NB = MODE;
     float dacc[NB];    // partial sums [token] of residue dq
-    int64_t st = 0;
+    int ring_pos = 0;      // stage counter modulo ns, and the ring pass parity
+    uint32_t ph = 0;
+    int64_t mi = p.n_mat > 1 ? g0 / p.ipm : 0;   // matrix cursor
     for (int64_t grp = g0; grp < g1; ++grp) {
-      const int64_t mi = grp / p.ipm;   // matrix of this item
+      while (p.n_mat > 1 && (mi + 1) * p.ipm <= grp) ++mi;
       const int64_t tile = (grp - mi * p.ipm) * P + slot_p;
       const bool live = tile < p.n_tiles;
 #pragma unroll
       for (int t = 0; t < NB; ++t) dacc[t] = 0.0f;
-      for (int ch = 0; ch < n_ch; ++ch, ++st) {
-        const int s = (int)(st % ns);
-        const uint32_t ph = (uint32_t)(st / ns) & 1u;
+      for (int ch = 0; ch < n_ch; ++ch) {
+        const int s = ring_pos;
         if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
+        if (++ring_pos == ns) {
+          ring_pos = 0;
+          ph ^= 1u;
+        }
         const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
         if (ok && live) {
           const uint8_t* rbase = ring + (size_t)s * p.stage_bytes + slot_p * piece + (size_t)r * p.slot_bytes;
