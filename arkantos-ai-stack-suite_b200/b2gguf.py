@@ -419,7 +419,8 @@ class ModelParams(ctypes.Structure):
 
 
 class ContextParams(ctypes.Structure):
-    _fields_ = [("n_ctx", ctypes.c_int32), ("n_seq_max", ctypes.c_int32), ("use_graph", ctypes.c_int32)]
+    _fields_ = [("n_ctx", ctypes.c_int32), ("n_seq_max", ctypes.c_int32), ("use_graph", ctypes.c_int32),
+                ("prefill_gemm", ctypes.c_int32)]
 
 
 def nccl_unique_id() -> bytes:
@@ -458,9 +459,10 @@ class Model:
 
 
 class Context:
-    def __init__(self, model: Model, n_ctx: int = 4096, n_seq: int = 1, use_graph: bool = True):
+    def __init__(self, model: Model, n_ctx: int = 4096, n_seq: int = 1, use_graph: bool = True,
+                 prefill_gemm: bool = True):
         self.model = model
-        p = ContextParams(n_ctx, n_seq, 1 if use_graph else 0)
+        p = ContextParams(n_ctx, n_seq, 1 if use_graph else 0, 1 if prefill_gemm else 0)
         h = ctypes.c_void_p()
         check(lib.b2_context_create(model.h, ctypes.byref(p), ctypes.byref(h)), "context_create")
         self.h = h.value

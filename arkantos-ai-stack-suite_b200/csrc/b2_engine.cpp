@@ -129,6 +129,16 @@ struct b2_context {
   // device-side greedy loop: [n_ctx][kStepMax] generated ids, per-row counts
   int32_t *gen_out = nullptr, *gen_count = nullptr;
   uint8_t* act_img = nullptr;   // quantized activations of the GEMV being run
+  // Prefill through the tensor-core GEMMs: chunks of up to pf_cap tokens,
+  // buffers allocated at the first long enough prompt.
+  bool prefill_gemm = true;
+  int pf_cap = 0;
+  int32_t* pf_in = nullptr;     // [tok | pos | seq] x pf_cap
+  int32_t* pf_in_h = nullptr;   // pinned staging of pf_in
+  cudaEvent_t pf_ev = nullptr;  // the staging's last copy
+  float *pf_x = nullptr, *pf_xn = nullptr, *pf_delta = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
+  float *pf_att = nullptr, *pf_gu = nullptr, *pf_h = nullptr, *pf_part_o = nullptr, *pf_part_ml = nullptr;
+  uint8_t* pf_ws = nullptr;     // GEMM activation images
   // last decode
   int last_n = 0;
   bool last_logits = false;
@@ -162,6 +172,8 @@ b2_context::~b2_context() {
   if (xbuf) cudaFree(xbuf);
   for (void* p : allocs) cudaFree(p);
   if (in_h) cudaFreeHost(in_h);
+  if (pf_in_h) cudaFreeHost(pf_in_h);
+  if (pf_ev) cudaEventDestroy(pf_ev);
   for (auto& e : in_ev)
     if (e) cudaEventDestroy(e);
   if (stream) cudaStreamDestroy(stream);
@@ -449,6 +461,7 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   c->n_ctx = p->n_ctx;
   c->n_seq = p->n_seq_max;
   c->use_graph = p->use_graph != 0;
+  c->prefill_gemm = p->prefill_gemm != 0;
   B2_CUDA_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   const int hd = m->head_dim, d = m->n_embd;
   const size_t kv = (size_t)c->n_seq * m->nkv_l * c->n_ctx * hd;
@@ -720,6 +733,105 @@ int check_status(b2_context* c) {
   return B2_OK;
 }
 
+// ---- prefill through the tensor-core GEMMs ------------------------------------------------
+// A long prompt's tokens (all but the last kStepMax of a b2_decode call) go
+// through the layers in chunks of up to pf_cap tokens: every projection is
+// one tensor-core GEMM over the chunk (Q4_K or Q8_0 weights, the reference's
+// row order), RoPE + KV store, the split-K attention and SwiGLU run as in the
+// unfused decode step.  Only the KV cache leaves a chunk: the tokens that
+// need logits take the decode step afterwards.
+constexpr int kPrefillMin = 64;              // tokens worth a GEMM pass
+constexpr int kPrefillCapMax = 512;
+constexpr size_t kPrefillBudget = (size_t)384 << 20;
+
+bool gemm_type(int t) { return t == B2_Q4_K || t == B2_Q8_0; }
+
+bool prefill_eligible(const b2_context* c) {
+  const b2_model* m = c->model;
+  if (!c->prefill_gemm || c->eval_cb || m->tp_size != 1) return false;
+  for (const auto& L : m->layers)
+    if (!gemm_type(L->wqkv.m.type) || !gemm_type(L->wo.m.type) || !gemm_type(L->wgu.m.type) ||
+        !gemm_type(L->wdown.m.type))
+      return false;
+  return true;
+}
+
+int prefill_alloc(b2_context* c) {
+  if (c->pf_cap) return B2_OK;
+  b2_model* m = c->model;
+  const int d = m->n_embd, hd = m->head_dim, qkv_w = (m->nh_l + 2 * m->nkv_l) * hd, nq = m->nh_l * hd;
+  const int n_split = attn_splits(c->n_ctx);
+  const size_t per_tok = 4 * ((size_t)3 * d + qkv_w + 2 * (size_t)nq + 3 * (size_t)m->ff_l +
+                              (size_t)m->nh_l * n_split * (hd + 2) + 3);
+  const int cap = (int)std::max<size_t>(kPrefillMin, std::min<size_t>(kPrefillCapMax, kPrefillBudget / per_tok));
+  int rc;
+  if ((rc = dalloc(c, &c->pf_in, (size_t)3 * cap)) || (rc = dalloc(c, &c->pf_x, (size_t)cap * d)) ||
+      (rc = dalloc(c, &c->pf_xn, (size_t)cap * d)) || (rc = dalloc(c, &c->pf_delta, (size_t)cap * d)) ||
+      (rc = dalloc(c, &c->pf_qkv, (size_t)cap * qkv_w)) || (rc = dalloc(c, &c->pf_q, (size_t)cap * nq)) ||
+      (rc = dalloc(c, &c->pf_att, (size_t)cap * nq)) || (rc = dalloc(c, &c->pf_gu, (size_t)cap * 2 * m->ff_l)) ||
+      (rc = dalloc(c, &c->pf_h, (size_t)cap * m->ff_l)) ||
+      (rc = dalloc(c, &c->pf_part_o, (size_t)cap * m->nh_l * n_split * hd)) ||
+      (rc = dalloc(c, &c->pf_part_ml, (size_t)cap * m->nh_l * n_split * 2)))
+    return rc;
+  size_t ws = 0;
+  for (const auto& L : m->layers)
+    for (const DevQ* q : {&L->wqkv, &L->wo, &L->wgu, &L->wdown}) ws = std::max(ws, gemm_act_image_bytes(q->m, cap));
+  if ((rc = dalloc(c, &c->pf_ws, ws))) return rc;
+  B2_CUDA_TRY(cudaMallocHost(&c->pf_in_h, (size_t)3 * cap * sizeof(int32_t)));
+  B2_CUDA_TRY(cudaEventCreateWithFlags(&c->pf_ev, cudaEventDisableTiming));
+  c->pf_cap = cap;
+  return B2_OK;
+}
+
+// One chunk of nt tokens staged in pf_in: the layers up to the KV cache.
+int enqueue_prefill_chunk(b2_context* c, int nt) {
+  b2_model* m = c->model;
+  cudaStream_t s = c->stream;
+  const int d = m->n_embd, hd = m->head_dim, nq = m->nh_l * hd;
+  const int32_t *tok = c->pf_in, *pos = c->pf_in + c->pf_cap, *seq = c->pf_in + 2 * c->pf_cap;
+  int rc = launch_embed(tok, nt, m->n_vocab, m->embd_type, m->embd, m->embd_row_bytes, d, c->pf_x, s);
+  for (int l = 0; l < m->n_layer && rc == B2_OK; ++l) {
+    const Layer& L = *m->layers[l];
+    if ((rc = launch_add_rmsnorm(c->pf_x, l ? c->pf_delta : nullptr, L.attn_norm, c->pf_xn, nt, d, m->eps, s,
+                                 nullptr, c->status)) ||
+        (rc = launch_gemm(L.wqkv.m, c->pf_xn, d, nt, c->pf_qkv, c->pf_ws, c->status, s)) ||
+        (rc = launch_rope_kv(c->pf_qkv, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->rope, c->pf_q, c->kc[l], c->vc[l],
+                             c->st_d, c->n_seq, c->n_ctx, s)) ||
+        (rc = launch_attention(c->pf_q, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->kc[l], c->vc[l], c->st_d, c->n_seq,
+                               c->n_ctx, c->pf_part_o, c->pf_part_ml, c->pf_att, s, c->status)) ||
+        (rc = launch_gemm(L.wo.m, c->pf_att, nq, nt, c->pf_delta, c->pf_ws, c->status, s)) ||
+        (rc = launch_add_rmsnorm(c->pf_x, c->pf_delta, L.ffn_norm, c->pf_xn, nt, d, m->eps, s, nullptr,
+                                 c->status)) ||
+        (rc = launch_gemm(L.wgu.m, c->pf_xn, d, nt, c->pf_gu, c->pf_ws, c->status, s)) ||
+        (rc = launch_swiglu_pairs(c->pf_gu, nt, m->ff_l, c->pf_h, s)) ||
+        (rc = launch_gemm(L.wdown.m, c->pf_h, m->ff_l, nt, c->pf_delta, c->pf_ws, c->status, s)))
+      break;
+  }
+  return rc;
+}
+
+// Tokens [0, np) of a validated decode call through the GEMM chunks.
+int prefill_gemm_tokens(b2_context* c, const int32_t* tokens, const std::vector<int32_t>& pv,
+                        const std::vector<int32_t>& sv, int np) {
+  int rc = prefill_alloc(c);
+  if (rc) return rc;
+  const int cap = c->pf_cap;
+  for (int j0 = 0; j0 < np; j0 += cap) {
+    if (c->abort_cb && c->abort_cb(c->abort_user)) return B2_ABORTED;
+    const int nt = std::min(cap, np - j0);
+    B2_CUDA_TRY(cudaEventSynchronize(c->pf_ev));   // the staging's previous copy has been read
+    for (int i = 0; i < nt; ++i) {
+      c->pf_in_h[i] = tokens[j0 + i];
+      c->pf_in_h[cap + i] = pv[j0 + i];
+      c->pf_in_h[2 * cap + i] = sv[j0 + i];
+    }
+    B2_CUDA_TRY(cudaMemcpyAsync(c->pf_in, c->pf_in_h, (size_t)3 * cap * 4, cudaMemcpyHostToDevice, c->stream));
+    B2_CUDA_TRY(cudaEventRecord(c->pf_ev, c->stream));
+    if ((rc = enqueue_prefill_chunk(c, nt))) return rc;
+  }
+  return B2_OK;
+}
+
 int decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32_t* seq, int n, int want_logits) {
   b2_model* m = c->model;
   B2_CUDA_TRY(cudaSetDevice(m->device));
@@ -743,12 +855,22 @@ int decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32
     pv[i] = p;
     sv[i] = s;
   }
-  // Steps of up to kStepMax tokens; a step never holds two tokens of one
-  // sequence out of order (they are consecutive and written before the
-  // step's attention reads them).
+  // A long prompt: all but the last kStepMax tokens through the GEMM chunks
+  // (no logits are asked of them), the rest through the decode step.
   int i0 = 0;
   c->last_n = 0;
   c->last_logits = false;
+  {
+    const int np = n - std::min(n, kStepMax);
+    if (want_logits != 1 && np >= kPrefillMin && prefill_eligible(c)) {
+      const int rc = prefill_gemm_tokens(c, tokens, pv, sv, np);
+      if (rc) return rc;
+      i0 = np;
+    }
+  }
+  // Steps of up to kStepMax tokens; a step never holds two tokens of one
+  // sequence out of order (they are consecutive and written before the
+  // step's attention reads them).
   while (i0 < n) {
     if (c->abort_cb && c->abort_cb(c->abort_user)) return B2_ABORTED;
     const int k = std::min(kStepMax, n - i0);
@@ -951,6 +1073,7 @@ void b2_context_default_params(b2_context_params* p) {
   p->n_ctx = 4096;
   p->n_seq_max = 1;
   p->use_graph = 1;
+  p->prefill_gemm = 1;
 }
 
 int b2_context_create(b2_model* m, const b2_context_params* params, b2_context** out) {

@@ -968,6 +968,25 @@ int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, con
   return B2_OK;
 }
 
+// SwiGLU over (gate, up) row pairs, as the GEMV's SwiGLU epilogue computes
+// it: h[t][f] = silu(gu[t][2f]) * gu[t][2f+1], the same rounded operations.
+__global__ void swiglu_pairs_kernel(const float* __restrict__ gu, int64_t n_tok, int ff, float* __restrict__ h) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t total = n_tok * ff;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / ff, f = i - t * ff;
+    const float2 v = *reinterpret_cast<const float2*>(gu + t * 2 * ff + 2 * f);
+    h[i] = __fmul_rn(__fdiv_rn(v.x, __fadd_rn(1.0f, b2_expf(-v.x))), v.y);
+  }
+}
+
+int launch_swiglu_pairs(const float* gu, int n_tok, int ff, float* h, cudaStream_t s) {
+  const int64_t total = (int64_t)n_tok * ff;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8 * kSMs));
+  return launch_pdl(swiglu_pairs_kernel, dim3(grid), dim3(256), 0, s, gu, (int64_t)n_tok, ff, h);
+}
+
 int launch_argmax(const float* logits, int n_tok, int n_vocab, int v_local, int32_t* ids, float* top, cudaStream_t s,
                   const GreedyFeed& feed, const PeerIn* in, int* status, uint32_t* scratch) {
   // With scratch, each token's vocabulary is split over up to kArgmaxParts

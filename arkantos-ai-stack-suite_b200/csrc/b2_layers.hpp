@@ -41,6 +41,9 @@ int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, co
                      float* part_ml, float* out, cudaStream_t s, int* status = nullptr, unsigned int* count = nullptr,
                      const ActImage* img = nullptr);
 bool attn_combine_fusable(int n_head, int n_kv, int hd, int cap);
+// h [n_tok][ff] = silu(gate) * up over the (gate, up) row pairs of gu
+// [n_tok][2 ff], with the arithmetic of the GEMV's SwiGLU epilogue.
+int launch_swiglu_pairs(const float* gu, int n_tok, int ff, float* h, cudaStream_t s);
 bool attn_fusable(int n_head, int n_kv, int hd, int act_type);
 // cos/sin pairs of one position delta for every rotated pair (head_dim <= 256).
 constexpr int kRotPairs = 128;

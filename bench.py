@@ -443,6 +443,23 @@ def tp_share(dist, rank: int, world: int, make_id, path: str):
     return obj[0], obj[1]
 
 
+def prefill_report(c, t_prefill: float, world: int, peaks: dict) -> dict:
+    """Config-5 prefill (8 prompts x 2048 tokens, one b2_decode call each):
+    wall time, and the projections' FLOP rate against the tensor roofline."""
+    d, ff, hd = c["n_embd"], c["n_ff"], c["n_embd"] // c["n_head"]
+    per_layer = (c["n_head"] + 2 * c["n_head_kv"]) * hd * d + d * d + 3 * ff * d
+    flop = 2.0 * c["n_layer"] * per_layer * BATCH * PROMPT
+    tflops = flop / t_prefill / 1e12
+    return {"tok_s": round(BATCH * PROMPT / t_prefill, 1), "seconds": round(t_prefill, 2),
+            "projection_tflop": round(flop / 1e12, 1), "projection_tflop_s": round(tflops, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1), "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s per GPU", "frac": round(tflops / world / peaks["bf16_tflops"], 4),
+                         "peak_src": peaks["src"] + " bf16 burst"},
+            "path": ("all but the last 8 tokens of each prompt through the tensor-core GEMM chunks" if world == 1
+                     else "decode GEMV steps of 8 tokens (tensor-parallel)"),
+            "timing": "host wall clock around the 8 b2_decode calls and their argmax reads"}
+
+
 def run_decode_ours(args, dist, rank, world, local):
     import b2gguf as b2
     b2.check(b2.lib.b2_set_device(local), "set_device")
@@ -558,6 +575,7 @@ def run_decode_ours(args, dist, rank, world, local):
         "clocks": clk.summary(),
         "setup_s": {"write_gguf": round(t_write, 1), "load": round(t_load, 1), "prefill": round(t_prefill, 1)},
         "prefill_tok_s": round(BATCH * PROMPT / t_prefill, 1),
+        "prefill": prefill_report(c, t_prefill, world, peaks),
     }
     if q40 is not None:
         out["q4_0_gemv"] = q40

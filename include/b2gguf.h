@@ -322,6 +322,14 @@ typedef struct b2_context_params {
     int32_t n_ctx;        /* KV positions per sequence (llama n_ctx) */
     int32_t n_seq_max;    /* concurrent sequences (decode batch) */
     int32_t use_graph;    /* replay each decode step as a CUDA graph */
+    int32_t prefill_gemm; /* long prompts through the tensor-core GEMMs (default 1): a b2_decode
+                             call of n tokens that asks no logits of its first n - 8, with
+                             n - 8 >= 64, runs those first tokens through the layers in chunks
+                             whose projections are tensor-core GEMMs, when every layer's
+                             projections are Q4_K or Q8_0 and the model is not tensor-parallel.
+                             Their projections then sum in the reference's row order (the
+                             CPU matmul_quantized's) instead of the decode GEMV's tile order;
+                             the last 8 tokens take the decode step. */
 } b2_context_params;
 
 /* llama_context_default_params / llama_init_from_model

@@ -137,7 +137,9 @@ int  orc_model_forward_range(orc_model* m, int seq, int32_t token, int pos, int 
                              int n_threads);
 /* KV shift on one sequence: drop [p0, p1), re-rotate K of [p1, n_past). */
 int  orc_model_kv_shift(orc_model* m, int seq, int p0, int p1, int n_past);
-/* 1: evaluate in the GPU kernels' order (orc_*_dev), 0: the reference's. */
+/* 1: evaluate in the GPU kernels' order (orc_*_dev), 0: the reference's;
+ * 2: the GPU kernels' order except the projections, which take the
+ * reference's row order (orc_matmul), as the tensor-core prefill GEMMs do. */
 void orc_model_set_device_order(orc_model* m, int on);
 /* Emulates tp tensor-parallel ranks in device order: attention-out and
  * FFN-down become per-rank column-slice partials summed in rank order (every

@@ -275,8 +275,10 @@ class Model:
         (self.n_layers, self.dim, self.hidden, self.n_heads, self.n_kv, self.vocab,
          self.head_dim, self.ctx_len, self.wtype, self.embd_type, self.out_type, _) = [int(v) for v in info]
 
-    def set_device_order(self, on: bool = True) -> None:
-        lib.orc_model_set_device_order(self.h, 1 if on else 0)
+    def set_device_order(self, on: bool = True, gemm_projections: bool = False) -> None:
+        """GPU kernels' order (on), optionally with the projections in the
+        reference's row order, as the tensor-core prefill GEMMs compute them."""
+        lib.orc_model_set_device_order(self.h, (2 if gemm_projections else 1) if on else 0)
 
     def init_cache(self, n_seq: int, n_ctx: int) -> None:
         if lib.orc_model_init_cache(self.h, n_seq, n_ctx) != 0:

@@ -48,7 +48,9 @@ struct orc_model {
     float* rope;
     orc_tap_fn tap;
     void* tap_user;
-    int device_order;   /* 1: evaluate in the GPU kernels' order (bit-exact check) */
+    int device_order;   /* 1: evaluate in the GPU kernels' order (bit-exact check); 2: the same
+                           with the projections in the reference's row order, as the
+                           tensor-core prefill GEMMs compute them */
     int tp;             /* tensor-parallel ranks emulated by the row-sharded projections */
     float* part;        /* [tp][dim] partial outputs */
 };
@@ -305,7 +307,7 @@ static void proj_mode(orc_model* m, const orc_tensor* w, const float* x, float* 
     const int k = (int)w->ne[0];
     if (orc_vec_dot_type(w->type) == ORC_Q8_K) orc_quantize_row_q8_k(x, m->xq, k);
     else orc_quantize_row_q8_0(x, m->xq, k);
-    if (m->device_order) orc_matmul_dev(w->type, w->data, w->ne[1], k, m->xq, y, swiglu, nt);
+    if (m->device_order == 1) orc_matmul_dev(w->type, w->data, w->ne[1], k, m->xq, y, swiglu, nt);
     else orc_matmul(w->type, w->data, w->ne[1], k, m->xq, y, nt);
 }
 static void proj(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) { proj_mode(m, w, x, y, nt, 0); }
@@ -315,7 +317,7 @@ static void proj(orc_model* m, const orc_tensor* w, const float* x, float* y, in
  * them; the partials are summed in rank order, y = ((p0 + p1) + p2) + ...,
  * which is the reduction the GPU ranks perform after exchanging partials. */
 static void proj_reduce(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) {
-    if (m->tp <= 1 || !m->device_order) { proj(m, w, x, y, nt); return; }
+    if (m->tp <= 1 || m->device_order != 1) { proj(m, w, x, y, nt); return; }
     const int k = (int)w->ne[0], n = (int)w->ne[1], kl = k / m->tp;
     const int at = orc_vec_dot_type(w->type);
     if (at == ORC_Q8_K) orc_quantize_row_q8_k(x, m->xq, k);

@@ -51,6 +51,43 @@ def oracle_run(path, n_seq, n_ctx):
     return m
 
 
+@pytest.mark.parametrize("n_seq,prefill_gemm", [(1, True), (2, True), (1, False)])
+def test_long_prompt_prefill_bit_exact(model_file, n_seq, prefill_gemm):
+    """A prompt long enough for the tensor-core prefill: all but the last 8
+    tokens of the call go through the GEMM chunks when the layers are Q4_K or
+    Q8_0 (the Q4_0 model, and prefill_gemm off, keep the decode step).  The
+    last token's logits and the greedy steps after it are bit-exact with the
+    oracle in the GPU kernels' order, with reference-order projections for
+    the tokens that went through the GEMMs."""
+    rng = np.random.default_rng(3)
+    n_ctx = 192
+    om = O.Model(model_file)
+    om.init_cache(n_seq, n_ctx)
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=n_ctx, n_seq=n_seq, prefill_gemm=prefill_gemm)
+    per = 90 // n_seq
+    toks = rng.integers(0, om.vocab, (per, n_seq))
+    order = [(int(toks[p, s]), p, s) for p in range(per) for s in range(n_seq)]   # sequences interleaved
+    n = len(order)
+    ctx.decode([t for t, _, _ in order], pos=[p for _, p, _ in order], seq=[s for _, _, s in order],
+               want_logits=2)
+    got = ctx.logits(-1)
+    gemm = prefill_gemm and om.wtype in (b2.Q4_K, b2.Q8_0)
+    for i, (t, p, s) in enumerate(order):
+        om.set_device_order(True, gemm_projections=gemm and i < n - 8)
+        want = om.forward(s, t, p, logits=(i == n - 1))
+    assert_same(got, want, "long prompt")
+    om.set_device_order(True)
+    s_last, pos = order[-1][2], order[-1][1] + 1
+    for step in range(3):
+        tok = int(np.argmax(want))
+        ctx.decode([tok], pos=[pos], seq=[s_last], want_logits=1)
+        got = ctx.logits(0)
+        want = om.forward(s_last, tok, pos)
+        pos += 1
+        assert_same(got, want, f"decode step {step} after the long prompt")
+
+
 @pytest.mark.parametrize("use_graph", [True, False])
 def test_prefill_and_greedy_decode_bit_exact(model_file, use_graph):
     rng = np.random.default_rng(0)
