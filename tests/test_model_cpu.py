@@ -66,3 +66,25 @@ def test_oracle_layer_range_forward_composes(tiny_gguf):
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     b.cache_fill(0x3C00)
     assert np.all(np.isfinite(b.forward(0, 5, 3)))
+
+
+@pytest.mark.parametrize("gemm_projections", [False, True])
+def test_oracle_projection_order_modes(tiny_gguf, gemm_projections):
+    """The oracle's GPU-order mode computes a projection in the decode GEMV's
+    tile order; with gemm_projections (the order of the tensor-core prefill)
+    the same projection takes the reference's row order, while the rest of
+    the forward stays in the GPU's order."""
+    m = O.Model(tiny_gguf)
+    m.set_device_order(True, gemm_projections=gemm_projections)
+    m.init_cache(1, 16)
+    taps = {}
+    m.set_tap(lambda name, layer, a: taps.__setitem__((name, layer), a))
+    m.forward(0, 7, 0, logits=False)
+    names = {t.name: t for t in gguf.GGUFReader(tiny_gguf).tensors}
+    wd = np.ascontiguousarray(names["blk.0.ffn_down.weight"].data).view(np.uint8)   # k = 768: three units
+    xq = O.quantize_act(O.Q4_K, taps[("ffn_act", 0)][None, :])[0]
+    ref = O.matmul(O.Q4_K, wd, 256, 768, xq)
+    dev = O.matmul_dev(O.Q4_K, wd, 256, 768, xq)
+    assert not np.array_equal(ref.view(np.uint32), dev.view(np.uint32))   # the two orders differ here
+    want = ref if gemm_projections else dev
+    assert np.array_equal(taps[("ffn_out", 0)].view(np.uint32), want.view(np.uint32))
