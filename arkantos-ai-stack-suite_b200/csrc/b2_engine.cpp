@@ -864,8 +864,16 @@ int decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32
     const int np = n - std::min(n, kStepMax);
     if (want_logits != 1 && np >= kPrefillMin && prefill_eligible(c)) {
       const int rc = prefill_gemm_tokens(c, tokens, pv, sv, np);
-      if (rc) return rc;
-      i0 = np;
+      if (rc == B2_ERR_OOM && c->pf_cap == 0) {
+        // no room for the chunk buffers: this context keeps the decode step
+        // for long prompts (nothing was enqueued)
+        cudaGetLastError();
+        c->prefill_gemm = false;
+      } else if (rc) {
+        return rc;
+      } else {
+        i0 = np;
+      }
     }
   }
   // Steps of up to kStepMax tokens; a step never holds two tokens of one
