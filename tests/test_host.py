@@ -1,5 +1,7 @@
 """Host-side checks (no GPU): the library loads and exports every declared
 entry point, and its host helpers agree with the oracle."""
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -46,3 +48,11 @@ def test_error_reporting_on_bad_arguments():
         b2.quantize_weights(b2.Q4_0, np.zeros((2, 33), np.float32))
     with pytest.raises(b2.B2Error):
         b2.quantize_weights(99, np.zeros((2, 32), np.float32))
+
+
+def test_context_default_params():
+    """llama_context_default_params' counterpart: 4096 positions, one
+    sequence, graph replay and the tensor-core prefill on."""
+    p = b2.ContextParams()
+    b2.lib.b2_context_default_params(ctypes.byref(p))
+    assert (p.n_ctx, p.n_seq_max, p.use_graph, p.prefill_gemm) == (4096, 1, 1, 1)
