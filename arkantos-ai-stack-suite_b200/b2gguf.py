@@ -114,6 +114,12 @@ def _bind() -> None:
         "b2_kv_seq_pos_max": (_i, [_vp, ctypes.c_int32, _vp]),
         "b2_set_abort_callback": (_i, [_vp, _vp, _vp]),
         "b2_set_eval_callback": (_i, [_vp, _vp, _vp]),
+        "b2_n_ctx": (_i, [_vp, _vp]),
+        "b2_flag_wait": (_i, [_vp, _i, _u64, _vp, _vp]),
+        "b2_memory_can_shift": (_i, [_vp, _vp]),
+        "b2_state_seq_get_size": (_i, [_vp, ctypes.c_int32, _vp]),
+        "b2_state_seq_get_data": (_i, [_vp, ctypes.c_int32, _vp, _sz, _vp]),
+        "b2_state_seq_set_data": (_i, [_vp, ctypes.c_int32, _vp, _sz, _vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -536,6 +542,43 @@ class Context:
         v = ctypes.c_int32()
         check(lib.b2_kv_seq_pos_max(self.h, seq, ctypes.byref(v)), "kv_seq_pos_max")
         return v.value
+
+    def n_ctx(self) -> int:
+        v = ctypes.c_int32()
+        check(lib.b2_n_ctx(self.h, ctypes.byref(v)), "n_ctx")
+        return v.value
+
+    def can_shift(self) -> bool:
+        v = ctypes.c_int32()
+        check(lib.b2_memory_can_shift(self.h, ctypes.byref(v)), "memory_can_shift")
+        return bool(v.value)
+
+    def state_seq_get(self, seq: int) -> bytes:
+        """Snapshot of one sequence's KV state (llama_state_seq_get_data)."""
+        n = ctypes.c_size_t()
+        check(lib.b2_state_seq_get_size(self.h, seq, ctypes.byref(n)), "state_seq_get_size")
+        buf = ctypes.create_string_buffer(n.value)
+        w = ctypes.c_size_t()
+        check(lib.b2_state_seq_get_data(self.h, seq, buf, n.value, ctypes.byref(w)), "state_seq_get_data")
+        return buf.raw[:w.value]
+
+    def state_seq_set(self, seq: int, data: bytes) -> int:
+        """Restores a snapshot into sequence seq (llama_state_seq_set_data); returns bytes read."""
+        r = ctypes.c_size_t()
+        check(lib.b2_state_seq_set_data(self.h, seq, data, len(data), ctypes.byref(r)), "state_seq_set_data")
+        return r.value
+
+    def set_abort_callback(self, fn) -> None:
+        """fn() -> bool polled between decode steps; True stops the call with status 2 (llama abort callback)."""
+        if fn is None:
+            self._abort = None
+            check(lib.b2_set_abort_callback(self.h, None, None), "set_abort_callback")
+            return
+        self._abort = self.ABORT(lambda user: 1 if fn() else 0)
+        check(lib.b2_set_abort_callback(self.h, ctypes.cast(self._abort, ctypes.c_void_p), None),
+              "set_abort_callback")
+
+    ABORT = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
 
     def free(self) -> None:
         if getattr(self, "h", None):

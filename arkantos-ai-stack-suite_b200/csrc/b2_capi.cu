@@ -474,4 +474,10 @@ int b2_kv_shift_k(uint16_t* k_cache, int seq, int n_kv, int head_dim, int cap, i
   return launch_kv_shift(k_cache, n_kv, head_dim, seq, st, cap, p_begin, p_end, cs, as_stream(stream));
 }
 
+int b2_flag_wait(const uint64_t* flags, int n, uint64_t target, int* status, void* stream) {
+  B2_CHECK_ARG(flags && status && n > 0, "flag_wait arguments");
+  return launch_flag_wait(reinterpret_cast<const unsigned long long*>(flags), n, (unsigned long long)target, status,
+                          as_stream(stream));
+}
+
 }  // extern "C"

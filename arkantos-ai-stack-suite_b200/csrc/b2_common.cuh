@@ -93,6 +93,7 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
 // caller then proceeds on whatever the buffers hold, so a lost peer ends the
 // step with an error status instead of hanging the GPU).
 constexpr uint64_t kPeerWaitNs = 2000000000ull;
+constexpr int kPeerWaitStatus = 3;   // status code of an expired exchange wait
 __device__ __forceinline__ bool wait_peer_flags(const unsigned long long* flags, int n, unsigned long long target,
                                                 int* status, int code) {
   // after one expiry in this step the others give up at once (a lost peer

@@ -227,6 +227,21 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
     return B2_ERR_FORMAT;
   }
   const GgufFile& g = m->gguf;
+  // The forward implemented here is Llama's (adjacent-pair RoPE, no
+  // projection biases).  Any other architecture, or a Llama file carrying
+  // biases, would load and silently compute the wrong function: refuse it.
+  {
+    const std::string arch = g.get_str("general.architecture", "");
+    if (arch != "llama") {
+      set_error("model load: architecture '%s' unsupported (llama only)", arch.c_str());
+      return B2_ERR_UNSUPPORTED;
+    }
+    for (const GgufTensor& t : g.tensors)
+      if (t.name.size() > 5 && t.name.compare(t.name.size() - 5, 5, ".bias") == 0) {
+        set_error("model load: bias tensor %s unsupported", t.name.c_str());
+        return B2_ERR_UNSUPPORTED;
+      }
+  }
   m->n_layer = (int)g.get_int(".block_count", 0);
   m->n_embd = (int)g.get_int(".embedding_length", 0);
   m->n_ff = (int)g.get_int(".feed_forward_length", 0);
@@ -764,6 +779,10 @@ int prefill_alloc(b2_context* c) {
   const size_t per_tok = 4 * ((size_t)3 * d + qkv_w + 2 * (size_t)nq + 3 * (size_t)m->ff_l +
                               (size_t)m->nh_l * n_split * (hd + 2) + 3);
   const int cap = (int)std::max<size_t>(kPrefillMin, std::min<size_t>(kPrefillCapMax, kPrefillBudget / per_tok));
+  size_t ws = 0;
+  for (const auto& L : m->layers)
+    for (const DevQ* q : {&L->wqkv, &L->wo, &L->wgu, &L->wdown}) ws = std::max(ws, gemm_act_image_bytes(q->m, cap));
+  const size_t n_before = c->allocs.size();
   int rc;
   if ((rc = dalloc(c, &c->pf_in, (size_t)3 * cap)) || (rc = dalloc(c, &c->pf_x, (size_t)cap * d)) ||
       (rc = dalloc(c, &c->pf_xn, (size_t)cap * d)) || (rc = dalloc(c, &c->pf_delta, (size_t)cap * d)) ||
@@ -771,12 +790,17 @@ int prefill_alloc(b2_context* c) {
       (rc = dalloc(c, &c->pf_att, (size_t)cap * nq)) || (rc = dalloc(c, &c->pf_gu, (size_t)cap * 2 * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_h, (size_t)cap * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_part_o, (size_t)cap * m->nh_l * n_split * hd)) ||
-      (rc = dalloc(c, &c->pf_part_ml, (size_t)cap * m->nh_l * n_split * 2)))
+      (rc = dalloc(c, &c->pf_part_ml, (size_t)cap * m->nh_l * n_split * 2)) || (rc = dalloc(c, &c->pf_ws, ws))) {
+    // A context short of memory keeps none of the chunk buffers: free the
+    // ones this call took (nothing has been enqueued on them).
+    for (size_t i = n_before; i < c->allocs.size(); ++i) cudaFree(c->allocs[i]);
+    c->allocs.resize(n_before);
+    c->pf_in = nullptr;
+    c->pf_x = c->pf_xn = c->pf_delta = c->pf_qkv = c->pf_q = c->pf_att = c->pf_gu = c->pf_h = nullptr;
+    c->pf_part_o = c->pf_part_ml = nullptr;
+    c->pf_ws = nullptr;
     return rc;
-  size_t ws = 0;
-  for (const auto& L : m->layers)
-    for (const DevQ* q : {&L->wqkv, &L->wo, &L->wgu, &L->wdown}) ws = std::max(ws, gemm_act_image_bytes(q->m, cap));
-  if ((rc = dalloc(c, &c->pf_ws, ws))) return rc;
+  }
   B2_CUDA_TRY(cudaMallocHost(&c->pf_in_h, (size_t)3 * cap * sizeof(int32_t)));
   B2_CUDA_TRY(cudaEventCreateWithFlags(&c->pf_ev, cudaEventDisableTiming));
   c->pf_cap = cap;
@@ -990,6 +1014,54 @@ int kv_shift(b2_context* c, int s, int p0, int p1) {
   if (rc) return rc;
   c->n_past[s] = n_past - nd;
   B2_CUDA_TRY(cudaMemcpyAsync(c->st_d + s, &st, sizeof(KvSeqState), cudaMemcpyHostToDevice, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return B2_OK;
+}
+
+// Sequence-state snapshot (llama_state_seq_get_data / set_data): the
+// sequence's fp16 K and V rows of this rank's KV heads in logical position
+// order, behind a header that names the shape they belong to.
+struct SeqStateHeader {
+  char magic[8];          // "B2KVSEQ"
+  uint32_t version;       // 1
+  int32_t n_layer, n_kv, head_dim, n_pos, kv_type, tp_rank, tp_size;
+  int32_t reserved[6];
+};
+static_assert(sizeof(SeqStateHeader) == 64, "snapshot header size");
+constexpr char kSeqMagic[8] = {'B', '2', 'K', 'V', 'S', 'E', 'Q', 0};
+
+size_t seq_state_bytes(const b2_context* c, int n_pos) {
+  const b2_model* m = c->model;
+  return sizeof(SeqStateHeader) + (size_t)m->n_layer * 2 * m->nkv_l * n_pos * m->head_dim * 2;
+}
+
+// Copies logical positions [0, n_pos) of sequence s between the cache and
+// host memory: per layer K then V, each [n_kv][n_pos][head_dim].  The ring
+// maps a position range to at most three contiguous slot runs; each run is
+// one strided copy over the KV heads.
+int seq_state_copy(b2_context* c, int s, int n_pos, uint8_t* host, bool to_host) {
+  const b2_model* m = c->model;
+  const KvSeqState st = to_host ? c->st[s] : KvSeqState{0, 0};
+  const size_t row = (size_t)m->head_dim * 2, cap = (size_t)c->n_ctx;
+  for (int l = 0; l < m->n_layer; ++l)
+    for (int kv = 0; kv < 2; ++kv) {
+      uint16_t* base = (kv ? c->vc[l] : c->kc[l]) + (size_t)s * m->nkv_l * cap * m->head_dim;
+      uint8_t* h = host + ((size_t)l * 2 + kv) * m->nkv_l * n_pos * row;
+      for (int p = 0; p < n_pos;) {
+        const int64_t slot = kv_slot(st, p, c->n_ctx);
+        int len = 1;
+        while (p + len < n_pos && kv_slot(st, p + len, c->n_ctx) == slot + len) ++len;
+        uint8_t* dev = reinterpret_cast<uint8_t*>(base) + (size_t)slot * row;
+        uint8_t* hp = h + (size_t)p * row;
+        if (to_host)
+          B2_CUDA_TRY(cudaMemcpy2DAsync(hp, (size_t)n_pos * row, dev, cap * row, (size_t)len * row, m->nkv_l,
+                                        cudaMemcpyDeviceToHost, c->stream));
+        else
+          B2_CUDA_TRY(cudaMemcpy2DAsync(dev, cap * row, hp, (size_t)n_pos * row, (size_t)len * row, m->nkv_l,
+                                        cudaMemcpyHostToDevice, c->stream));
+        p += len;
+      }
+    }
   B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
   return B2_OK;
 }
@@ -1231,6 +1303,102 @@ int b2_kv_seq_add(b2_context* c, int32_t seq, int32_t p0, int32_t p1, int32_t de
 int b2_kv_seq_pos_max(b2_context* c, int32_t seq, int32_t* pos) {
   B2_CHECK_ARG(c && pos && seq >= 0 && seq < c->n_seq, "kv_seq_pos_max arguments");
   *pos = c->n_past[seq] - 1;
+  return B2_OK;
+}
+
+int b2_n_ctx(const b2_context* c, int32_t* n_ctx) {
+  B2_CHECK_ARG(c && n_ctx, "n_ctx arguments");
+  *n_ctx = c->n_ctx;
+  return B2_OK;
+}
+
+int b2_memory_can_shift(const b2_context* c, int32_t* can_shift) {
+  B2_CHECK_ARG(c && can_shift, "memory_can_shift arguments");
+  *can_shift = 1;   // the fp16 ring cache re-rotates K in place for any shift
+  return B2_OK;
+}
+
+int b2_state_seq_get_size(b2_context* c, int32_t seq, size_t* size) {
+  B2_CHECK_ARG(c && size && seq >= 0 && seq < c->n_seq, "state_seq_get_size arguments");
+  *size = seq_state_bytes(c, c->n_past[seq]);
+  return B2_OK;
+}
+
+int b2_state_seq_get_data(b2_context* c, int32_t seq, void* dst, size_t size, size_t* written) {
+  B2_CHECK_ARG(c && dst && seq >= 0 && seq < c->n_seq, "state_seq_get_data arguments");
+  if (written) *written = 0;
+  for (const auto& p : pending_for(c))
+    if (p.p0 >= 0) {
+      set_error("state_seq_get_data: a KV removal is waiting for its position shift (b2_kv_seq_add)");
+      return B2_ERR_INVALID;
+    }
+  const b2_model* m = c->model;
+  const int n_pos = c->n_past[seq];
+  const size_t need = seq_state_bytes(c, n_pos);
+  if (size < need) {
+    set_error("state_seq_get_data: %zu bytes given, the state of sequence %d takes %zu", size, seq, need);
+    return B2_ERR_INVALID;
+  }
+  B2_CUDA_TRY(cudaSetDevice(m->device));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  SeqStateHeader h = {};
+  memcpy(h.magic, kSeqMagic, 8);
+  h.version = 1;
+  h.n_layer = m->n_layer;
+  h.n_kv = m->nkv_l;
+  h.head_dim = m->head_dim;
+  h.n_pos = n_pos;
+  h.kv_type = B2_F16;
+  h.tp_rank = m->tp_rank;
+  h.tp_size = m->tp_size;
+  memcpy(dst, &h, sizeof h);
+  const int rc = seq_state_copy(c, seq, n_pos, static_cast<uint8_t*>(dst) + sizeof h, true);
+  if (rc) return rc;
+  if (written) *written = need;
+  return check_status(c);
+}
+
+int b2_state_seq_set_data(b2_context* c, int32_t seq, const void* src, size_t size, size_t* read) {
+  B2_CHECK_ARG(c && src && seq >= 0 && seq < c->n_seq, "state_seq_set_data arguments");
+  if (read) *read = 0;
+  const b2_model* m = c->model;
+  SeqStateHeader h;
+  if (size < sizeof h) {
+    set_error("state_seq_set_data: %zu bytes, shorter than the header", size);
+    return B2_ERR_FORMAT;
+  }
+  memcpy(&h, src, sizeof h);
+  if (memcmp(h.magic, kSeqMagic, 8) != 0 || h.version != 1) {
+    set_error("state_seq_set_data: not a sequence-state snapshot of this library");
+    return B2_ERR_FORMAT;
+  }
+  if (h.n_layer != m->n_layer || h.n_kv != m->nkv_l || h.head_dim != m->head_dim || h.kv_type != B2_F16 ||
+      h.tp_rank != m->tp_rank || h.tp_size != m->tp_size) {
+    set_error("state_seq_set_data: snapshot of another model shape or rank (%d layers, %d kv heads, hd %d, "
+              "rank %d/%d)", h.n_layer, h.n_kv, h.head_dim, h.tp_rank, h.tp_size);
+    return B2_ERR_FORMAT;
+  }
+  if (h.n_pos < 0 || h.n_pos > c->n_ctx) {
+    set_error("state_seq_set_data: %d positions, the context holds %d", h.n_pos, c->n_ctx);
+    return B2_NO_KV_SLOT;
+  }
+  const size_t need = seq_state_bytes(c, h.n_pos);
+  if (size < need) {
+    set_error("state_seq_set_data: %zu bytes, the snapshot declares %zu", size, need);
+    return B2_ERR_FORMAT;
+  }
+  B2_CUDA_TRY(cudaSetDevice(m->device));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  // The restored sequence starts a fresh ring: positions in slots 0..n_pos-1.
+  pending_for(c)[seq] = Pending{};
+  const int rc = seq_state_copy(c, seq, h.n_pos, const_cast<uint8_t*>(static_cast<const uint8_t*>(src)) + sizeof h,
+                                false);
+  if (rc) return rc;
+  c->st[seq] = KvSeqState{0, 0};
+  c->n_past[seq] = h.n_pos;
+  B2_CUDA_TRY(cudaMemcpyAsync(c->st_d + seq, &c->st[seq], sizeof(KvSeqState), cudaMemcpyHostToDevice, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (read) *read = need;
   return B2_OK;
 }
 

@@ -314,6 +314,10 @@ int launch_act_to_blocks(const ActQ& a, int64_t k, void* blocks, cudaStream_t s)
 int launch_block_dots(const QMatrix& w, const ActQ& a, int64_t row, int32_t* out_i, int32_t* out_m,
                       cudaStream_t s);
 int launch_dequantize(const QMatrix& w, float* dst, cudaStream_t s);
+// The exchange's bounded wait on its own: *status = kPeerWaitStatus when the
+// flags did not all reach `target` within the wait bound.
+int launch_flag_wait(const unsigned long long* flags, int n, unsigned long long target, int* status,
+                     cudaStream_t s);
 
 // Multiprocessor count of the current device (cached per device).
 int sm_count();

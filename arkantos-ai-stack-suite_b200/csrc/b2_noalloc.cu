@@ -8,9 +8,13 @@
 // until the process exits.  The caller still passes q, the caches and out.
 // The array's device address is taken with cudaGetSymbolAddress the first
 // time the entry point runs on a device (with that device current), so that
-// first call should come before any stream capture.  All calls share the
-// array: calls whose work overlaps on the GPU (different streams, or other
-// threads) race on it and must be serialized by the caller.
+// first call should come before any stream capture.  A call on a stream that
+// is not capturing looks the address up again, so a device reset
+// (cudaDeviceReset, which reloads the module) between calls is picked up; a
+// call under capture uses the address seen last, and a reset between that
+// lookup and the capture leaves it stale.  All calls share the array: calls
+// whose work overlaps on the GPU (different streams, or other threads) race
+// on it and must be serialized by the caller.
 #include <mutex>
 
 #include "b2_common.cuh"
@@ -28,16 +32,19 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 std::mutex g_mu;
 void* g_addr[kMaxDevices] = {};
 
-// Device address of g_scratch on the current device, looked up once.
-int scratch_address(void** out) {
+// Device address of g_scratch on the current device: looked up on every
+// call outside stream capture, cached for calls under capture.
+int scratch_address(cudaStream_t stream, void** out) {
   int dev = 0;
   B2_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) {
     set_error("attn_decode_noalloc: device ordinal %d beyond %d", dev, kMaxDevices);
     return B2_ERR_UNSUPPORTED;
   }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  B2_CUDA_TRY(cudaStreamIsCapturing(stream, &cap));
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_addr[dev]) {
+  if (cap == cudaStreamCaptureStatusNone || !g_addr[dev]) {
     void* p = nullptr;
     B2_CUDA_TRY(cudaGetSymbolAddress(&p, g_scratch));
     g_addr[dev] = p;
@@ -71,7 +78,7 @@ extern "C" int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, c
     return B2_ERR_INVALID;
   }
   void* base = nullptr;
-  const int rc = scratch_address(&base);
+  const int rc = scratch_address(static_cast<cudaStream_t>(stream), &base);
   if (rc) return rc;
   uint8_t* b = static_cast<uint8_t*>(base);
   // Every partial is rewritten by the call; sequence ids and positions are

@@ -206,7 +206,19 @@ __global__ void dequantize_kernel(QMatrix m, float* dst) {
 
 int grid_for(int64_t n, int block) { return (int)std::min<int64_t>((n + block - 1) / block, 1 << 30); }
 
+// One thread runs the tensor-parallel exchange's bounded flag wait.
+__global__ void flag_wait_kernel(const unsigned long long* flags, int n, unsigned long long target, int* status) {
+  wait_peer_flags(flags, n, target, status, kPeerWaitStatus);
+}
+
 }  // namespace
+
+int launch_flag_wait(const unsigned long long* flags, int n, unsigned long long target, int* status,
+                     cudaStream_t s) {
+  flag_wait_kernel<<<1, 1, 0, s>>>(flags, n, target, status);
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
 
 int launch_quantize_act(int act_type, const float* x, int64_t x_stride, int n_tok, int64_t k, ActQ& out,
                         cudaStream_t s) {

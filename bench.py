@@ -460,6 +460,14 @@ def prefill_report(c, t_prefill: float, world: int, peaks: dict) -> dict:
             "timing": "host wall clock around the 8 b2_decode calls and their argmax reads"}
 
 
+def decode_config(world: int) -> dict:
+    """The config-5 workload as both arms report it."""
+    return {"workload": "decode_8b_q4k: 32 layers, d 4096, ffn 14336, 32/8 heads, hd 128, vocab 128256, "
+                        "theta 5e5; batch 8 x 2048-token prompts, greedy steps (config 5)",
+            "global_batch": BATCH, "seq_len": PROMPT, "parallelism": f"tp{world}",
+            "l2": f"inputs larger than L2 ({decode_weight_bytes(world) / 1e9:.2f} GB of weights per rank per step)"}
+
+
 def run_decode_ours(args, dist, rank, world, local):
     import b2gguf as b2
     b2.check(b2.lib.b2_set_device(local), "set_device")
@@ -557,11 +565,7 @@ def run_decode_ours(args, dist, rank, world, local):
         "vs_baseline": None,
         "dtype": "q4_k/q6_k x q8_k -> int32 -> f32, fp16 KV",
         "data": "synthetic: random-init Llama 8B (N(0,0.02) seed 6) GGUF Q4_K + Q6_K head; uniform random prompt ids",
-        "config": {"workload": "decode_8b_q4k: 32 layers, d 4096, ffn 14336, 32/8 heads, hd 128, vocab 128256, "
-                               "theta 5e5; batch 8 x 2048-token prompts, greedy steps (config 5)",
-                   "global_batch": BATCH, "seq_len": PROMPT, "parallelism": f"tp{world}",
-                   "l2": f"inputs larger than L2 ({decode_weight_bytes(world) / 1e9:.2f} GB of weights per rank per step)",
-                   "context_at_start": p_start, "timed_region": "b2_generate: K greedy steps, device-side feedback"},
+        "config": decode_config(world),
         "roofline": {"bound": "hbm", "kernel": f"gemv Q4_K batch 8, {2 * ff_l}x{c['n_embd']} (ffn gate|up)",
                      "achieved": round(g["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(g["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
@@ -571,6 +575,8 @@ def run_decode_ours(args, dist, rank, world, local):
                           "note": "weights + fp16 KV read per rank per step / device time per step"},
         "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 3 * BATCH * 4,
                 "d2h_bytes_per_step": 32 * 4, "greedy_ids_equal_device_loop": bool(np.array_equal(e2e_ids, gen))},
+        "timed_region": "b2_generate: K greedy steps, device-side feedback",
+        "context_at_start": p_start,
         "gpu_launches": launches_per_step(c["n_layer"]) * args.steps,
         "clocks": clk.summary(),
         "setup_s": {"write_gguf": round(t_write, 1), "load": round(t_load, 1), "prefill": round(t_prefill, 1)},
@@ -592,7 +598,7 @@ def run_decode_ours(args, dist, rank, world, local):
 
 
 def cpu_decode_samples(path: str, n_samples: int | None, seconds: float | None, warm: int, layers: int | None = None,
-                       ctx_len: int = PROMPT):
+                       ctx_len: int = PROMPT, with_time: bool = False):
     """Oracle decode of one token of a model at context ctx_len, timed as
     samples: one decoder layer per sample (cycling over all layers, so every
     layer's weights come from DRAM), plus embed+final norm+head samples.
@@ -607,7 +613,7 @@ def cpu_decode_samples(path: str, n_samples: int | None, seconds: float | None, 
     t_layer, t_head = [], []
 
     def sample(i):
-        j = i % (nl + 1)
+        j = (i + nl) % (nl + 1)      # the head first, then layers 0..nl-1, cycling
         t0 = time.perf_counter()
         if j == nl:
             m.forward_range(0, tok, pos, 0, 0, logits=True, n_threads=nt)
@@ -617,7 +623,7 @@ def cpu_decode_samples(path: str, n_samples: int | None, seconds: float | None, 
             t_layer.append(time.perf_counter() - t0)
 
     for i in range(warm):
-        sample(nl - i % 2)           # head and last layer: page the mapping in
+        sample(0 if i % 2 == 0 else nl)   # head and last layer: page the mapping in
     t_layer.clear()
     t_head.clear()
     i, t_start = 0, time.perf_counter()
@@ -628,10 +634,12 @@ def cpu_decode_samples(path: str, n_samples: int | None, seconds: float | None, 
             break
         sample(i)
         i += 1
-    if not t_head:
-        sample(nl)
+    if not t_layer:
+        sample(1)
+        i += 1
+    timed = float(np.sum(t_layer) + np.sum(t_head))
     per_tok = nl * float(np.mean(t_layer)) + float(np.mean(t_head))
-    return per_tok, i, nt
+    return (per_tok, i, nt, timed) if with_time else (per_tok, i, nt)
 
 
 def cpu_decode_baseline(path: str, seconds: float) -> dict:
@@ -642,15 +650,30 @@ def cpu_decode_baseline(path: str, seconds: float) -> dict:
                       f"token by token, so batch 8 does not change tok/s)"}
 
 
+def write_8b_cpu_arm(path: str) -> None:
+    """The config-5 model file for the CPU reference arm, written by the
+    oracle's numpy GGUF writer (same shapes and block types; random valid
+    blocks), so the arm's process loads no product library."""
+    from oracle import synth_gguf as S
+    c = LLAMA_8B
+    S.write_llama(path + ".part", c["n_layer"], c["n_embd"], c["n_ff"], c["n_head"], c["n_head_kv"], c["n_vocab"],
+                  S.Q4_K, S.Q4_K, S.Q6_K, c["seed"], rope_theta=c["rope_theta"], n_ctx_train=c["n_ctx_train"])
+    os.replace(path + ".part", path)
+
+
 def run_decode_reference(args, dist, rank, world, local):
+    """The reference's CPU decode path (the oracle port) on the host cores.
+    A step is one timed sample: one decoder layer of one token (cycling over
+    all 32) or embed + norm + head.  ms_per_step is the mean sample time the
+    run measured; value is the tok/s those samples extrapolate to (one token
+    = 32 layer samples + 1 head sample)."""
     if rank != 0:
         return None
-    import b2gguf as b2  # host-only: the synthetic GGUF writer
-    path = model_path("8b_q4k")
+    path = model_path("8b_q4k_cpu")
     if not os.path.exists(path):
-        write_8b(b2, path)
+        write_8b_cpu_arm(path)
     t0 = time.perf_counter()
-    per_tok, n, nt = cpu_decode_samples(path, args.steps, None, args.warmup)
+    per_tok, n, nt, timed_s = cpu_decode_samples(path, args.steps, None, args.warmup, with_time=True)
     wall = time.perf_counter() - t0
     if not args.keep_model:
         try:
@@ -659,16 +682,17 @@ def run_decode_reference(args, dist, rank, world, local):
             pass
     v = round(1.0 / per_tok, 4)
     return {"metric": "decode tok/s (Llama-shape 8B Q4_K, batch 8)", "value": v, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_tok * BATCH * 1e3,
+            "steps": n, "warmup": args.warmup, "ms_per_step": timed_s / n * 1e3,
+            "value_kind": "extrapolated: 1 / (32 x mean layer sample + mean head sample) per token",
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "q4_k/q6_k x q8_k -> int32 -> f32, fp16 KV", "data": "synthetic",
-            "config": {"workload": "decode_8b_q4k (config 5)", "global_batch": BATCH, "seq_len": PROMPT,
-                       "parallelism": "host cores"},
+            "dtype": "q4_k/q6_k x q8_k -> int32 -> f32, fp16 KV",
+            "data": "synthetic: Llama 8B shapes, Q4_K layers + Q6_K head with random valid blocks (oracle writer)",
+            "config": decode_config(world),
             "impl": "reference",
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": nt, "kind": "port",
                              "sample": f"each step one sample: a single decoder layer (cycling over all 32) or "
-                                       f"embed+norm+head of one token at context {PROMPT}; tok/s = 1 / (32 x mean "
-                                       f"layer + head); {n} samples in {wall:.0f} s"},
+                                       f"embed+norm+head of one token at context {PROMPT}; {n} samples timed in "
+                                       f"{timed_s:.1f} s ({wall:.0f} s with warm-up)"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 

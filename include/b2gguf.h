@@ -250,8 +250,10 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
  * n_q·n_head·ceil(cap/128)·(head_dim+2)·4 bytes within the array (larger
  * requests return B2_ERR_INVALID).  The first
  * call on a device looks up the array's address (call it once before any
- * stream capture).  Calls share the array: calls that overlap on the GPU
- * race and must be serialized by the caller. */
+ * stream capture); calls outside capture look it up again, so a device reset
+ * between calls is picked up, while a call under capture uses the address
+ * seen last.  Calls share the array: calls that overlap on the GPU race and
+ * must be serialized by the caller. */
 #define B2_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
 #define B2_NOALLOC_MAX_QUERIES 64
 B2_API int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
@@ -264,6 +266,17 @@ B2_API int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, const
  * stream-ordered, no host synchronization. */
 B2_API int b2_kv_shift_k(uint16_t* k_cache, int seq, int n_kv, int head_dim, int cap, int p_begin, int p_end,
                          int delta, float theta, void* stream);
+
+/* The tensor-parallel exchange's bounded device wait on its own.  No
+ * llama.cpp counterpart.  One device thread waits until every flag of
+ * flags[0..n) (device uint64) reaches `target`, for at most 2 s of wall
+ * time; on expiry it stores B2_WAIT_EXPIRED in *status (device int) and
+ * returns, so the stream stays usable and the caller reads the status
+ * instead of finding a hung GPU.  The same wait guards every exchange of a
+ * tensor-parallel decode step (a lost peer ends the step with
+ * B2_ERR_TIMEOUT). */
+#define B2_WAIT_EXPIRED 3
+B2_API int b2_flag_wait(const uint64_t* flags, int n, uint64_t target, int* status, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* GGUF model files                                                           */
@@ -377,6 +390,27 @@ B2_API int b2_kv_clear(b2_context* c);
 B2_API int b2_kv_seq_rm(b2_context* c, int32_t seq, int32_t p0, int32_t p1);
 B2_API int b2_kv_seq_add(b2_context* c, int32_t seq, int32_t p0, int32_t p1, int32_t delta);
 B2_API int b2_kv_seq_pos_max(b2_context* c, int32_t seq, int32_t* pos);
+
+/* llama_n_ctx (Milda/src/engine.cpp:1236): KV positions per sequence. */
+B2_API int b2_n_ctx(const b2_context* c, int32_t* n_ctx);
+/* llama_memory_can_shift (Milda/src/engine.cpp:1655, 2126): 1 — the cache
+ * re-rotates K in place for the seq_rm + seq_add shift. */
+B2_API int b2_memory_can_shift(const b2_context* c, int32_t* can_shift);
+
+/* Sequence-state snapshot and restore: llama_state_seq_get_size /
+ * get_data / set_data (Milda/src/engine.cpp:1487-1492 pins the system
+ * prompt's state, :1701-1705 restores it; Sutra/src/llm_backends.cpp:2572-2580
+ * caches a prefix).  The snapshot holds the sequence's positions
+ * [0, pos_max] — this rank's KV heads, fp16 K and V per layer in position
+ * order — behind a 64-byte header naming the model shape and rank.
+ * get_size: bytes the snapshot of `seq` takes now.  get_data: writes it to
+ * dst (size >= get_size) and sets *written.  set_data: replaces sequence
+ * `seq` (any id of this context) with the snapshot; *read = bytes consumed.
+ * A snapshot of another shape or rank is refused with B2_ERR_FORMAT, one
+ * longer than n_ctx with B2_NO_KV_SLOT.  Synchronous. */
+B2_API int b2_state_seq_get_size(b2_context* c, int32_t seq, size_t* size);
+B2_API int b2_state_seq_get_data(b2_context* c, int32_t seq, void* dst, size_t size, size_t* written);
+B2_API int b2_state_seq_set_data(b2_context* c, int32_t seq, const void* src, size_t size, size_t* read);
 
 /* Intermediate-tensor callback, the analogue of llama.cpp's cb_eval context
  * parameter: when set, decode steps run without graph replay and after each

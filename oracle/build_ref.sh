@@ -1,12 +1,14 @@
 #!/usr/bin/env bash
 # Builds the reference's own scalar reference ops from their sources where
 # they lie under the reference checkout into oracle/_ref/libsingularity_ref.so.
-# Test infrastructure only.  Skips (exit 0) when the reference is absent.
+# Test infrastructure only.  The reference checkout's root comes from the
+# first argument or B2_REFERENCE_ROOT; with neither, or when the sources are
+# not there, the script skips (exit 0).
 set -euo pipefail
 here="$(cd "$(dirname "$0")" && pwd)"
-ref="${B2_REFERENCE_ROOT:-/root/reference}"
+ref="${1:-${B2_REFERENCE_ROOT:-}}"
 out="$here/_ref"
-if [ ! -f "$ref/Singularity/tests/test_and_bench_a5.cpp" ]; then
+if [ -z "$ref" ] || [ ! -f "$ref/Singularity/tests/test_and_bench_a5.cpp" ]; then
     echo "build_ref: reference sources not present; skipping"
     exit 0
 fi

@@ -198,3 +198,34 @@ def test_reference_fuzz_replay_on_gpu():
         want = O.gemv(t, q, rows, k, x[:8])
         errs = [rel_error(a, b) for a, b in zip(got.ravel(), want.ravel())]
         assert max(errs) <= 1e-4
+
+
+def test_expired_flag_wait_reports_status_and_device_stays_usable():
+    """The exchange's bounded wait, run on flags that nothing raises: the
+    kernel gives up after its wall-clock bound (2 s), stores the expiry
+    status and returns; the stream and the context keep working.  With the
+    flags raised the same wait returns at once with no status."""
+    import time
+
+    flags = b2.DeviceBuffer.from_array(np.zeros(2, np.uint64))
+    status = b2.DeviceBuffer.from_array(np.zeros(1, np.int32))
+    t0 = time.perf_counter()
+    b2.check(b2.lib.b2_flag_wait(flags.ptr, 2, 1, status.ptr, None), "flag_wait")
+    b2.check(b2.lib.b2_stream_synchronize(None), "sync")
+    waited = time.perf_counter() - t0
+    assert int(status.download(np.int32)[0]) == 3          # B2_WAIT_EXPIRED
+    assert 1.5 < waited < 30.0, waited
+    flags.upload(np.array([1, 5], np.uint64))
+    status.zero()
+    t0 = time.perf_counter()
+    b2.check(b2.lib.b2_flag_wait(flags.ptr, 2, 1, status.ptr, None), "flag_wait")
+    b2.check(b2.lib.b2_stream_synchronize(None), "sync")
+    assert int(status.download(np.int32)[0]) == 0
+    assert time.perf_counter() - t0 < 1.0
+    # the device still computes correctly
+    rng = np.random.default_rng(9)
+    n, k = 64, 256
+    q = b2.quantize_weights(b2.Q8_0, (rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    y = b2.QMatrix(b2.Q8_0, q, n, k).gemv(x)
+    assert np.array_equal(_bits(y), _bits(O.gemv_dev(O.Q8_0, q, n, k, x)))

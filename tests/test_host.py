@@ -56,3 +56,51 @@ def test_context_default_params():
     p = b2.ContextParams()
     b2.lib.b2_context_default_params(ctypes.byref(p))
     assert (p.n_ctx, p.n_seq_max, p.use_graph, p.prefill_gemm) == (4096, 1, 1, 1)
+
+
+def _write_small_llama(path):
+    b2.write_synthetic_llama(str(path), 1, 64, 128, 2, 1, 64, b2.Q8_0, embd_type=b2.Q8_0, out_type=b2.Q8_0, seed=3)
+    return path.read_bytes()
+
+
+def _load_rc(path) -> int:
+    h = ctypes.c_void_p()
+    rc = b2.lib.b2_model_load(str(path).encode(), None, ctypes.byref(h))
+    assert not h.value, "a refused model must not hand out a handle"
+    return rc
+
+
+def test_model_load_refuses_other_architectures(tmp_path):
+    """A Qwen2 (or any non-Llama) file would load and compute the wrong
+    function (NeoX RoPE, projection biases): the loader refuses it before any
+    device work, as llama_model_load_from_file returns null on an unusable
+    file (Milda/src/engine.cpp:920-934)."""
+    raw = _write_small_llama(tmp_path / "llama.gguf")
+    qwen = tmp_path / "qwen2.gguf"
+    qwen.write_bytes(raw.replace(b"llama", b"qwen2"))     # architecture and its key prefix
+    assert _load_rc(qwen) == -6
+    assert "qwen2" in b2.lib.b2_last_error().decode()
+
+
+def test_model_load_refuses_bias_tensors(tmp_path):
+    raw = _write_small_llama(tmp_path / "llama.gguf")
+    name = b"blk.0.ffn_up.weight"
+    assert raw.count(name) == 1
+    biased = tmp_path / "bias.gguf"
+    biased.write_bytes(raw.replace(name, b"blk.0.ffn_up.w.bias"))   # same length: only the name changes
+    assert _load_rc(biased) == -6
+    assert "bias" in b2.lib.b2_last_error().decode()
+
+
+@pytest.mark.parametrize("cut", [0, 3, 24, 200, "data"])
+def test_model_load_refuses_truncated_or_corrupt_files(tmp_path, cut):
+    raw = _write_small_llama(tmp_path / "llama.gguf")
+    bad = tmp_path / "bad.gguf"
+    if cut == "data":
+        bad.write_bytes(raw[: len(raw) - 1000])          # tensor data cut short
+    else:
+        bad.write_bytes(raw[:cut])                       # header cut short
+    assert _load_rc(bad) == -4
+    bad.write_bytes(b"GGUX" + raw[4:])                   # wrong magic
+    assert _load_rc(bad) == -4
+    assert _load_rc(tmp_path / "missing.gguf") == -4

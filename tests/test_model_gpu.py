@@ -236,3 +236,66 @@ def test_device_greedy_generate_bit_exact(model_file, use_graph):
     assert rc == b2.NO_KV_SLOT
     with pytest.raises(b2.B2Error):
         ctx.generate([1, 2], 2, seq=[0, 0])          # repeated sequence
+
+
+def test_state_snapshot_restore_bit_exact(model_file):
+    """Milda pins its system prompt's state after the first prefill
+    (llama_state_seq_get_data, Milda/src/engine.cpp:1487-1492) and restores
+    it when partial removal is refused (:1701-1705): after clear + restore
+    the next step's logits equal the ones computed before, bit for bit, in
+    the same sequence or in another one; a snapshot taken after an in-place
+    shift (ring cache) restores the shifted state."""
+    rng = np.random.default_rng(5)
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=64, n_seq=2)
+    assert ctx.n_ctx() == 64 and ctx.can_shift()
+    prompt = rng.integers(0, gm.n_vocab, 21).tolist()
+    ctx.decode(prompt, want_logits=0)
+    snap = ctx.state_seq_get(0)
+    ctx.decode([7], pos=[21], want_logits=1)
+    ref = ctx.logits(0)
+    ctx.decode([9, 10, 11], want_logits=0)              # the conversation moves on
+    ctx.kv_clear()
+    assert ctx.state_seq_set(0, snap) == len(snap)
+    assert ctx.kv_pos_max(0) == 20
+    ctx.decode([7], pos=[21], want_logits=1)
+    assert_same(ctx.logits(0), ref, "restored into its own sequence")
+    assert ctx.state_seq_set(1, snap) == len(snap)    # Sutra's prefix cache: into another sequence
+    ctx.decode([7], pos=[21], seq=[1], want_logits=1)
+    assert_same(ctx.logits(0), ref, "restored into another sequence")
+    # shift, snapshot the ring, restore into the other sequence
+    ctx.kv_seq_rm(0, 4, 12)
+    ctx.kv_seq_add(0, 12, -1, -8)
+    shifted = ctx.state_seq_get(0)
+    ctx.decode([3], pos=[14], seq=[0], want_logits=1)
+    ref2 = ctx.logits(0)
+    ctx.state_seq_set(1, shifted)
+    ctx.decode([3], pos=[14], seq=[1], want_logits=1)
+    assert_same(ctx.logits(0), ref2, "shifted state restored")
+    with pytest.raises(b2.B2Error):
+        ctx.state_seq_set(0, b"B2KVSEQ\0" + snap[8:40])   # truncated
+    with pytest.raises(b2.B2Error):
+        ctx.state_seq_set(0, b"XXXXXXXX" + snap[8:])      # not a snapshot
+    small = b2.Context(gm, n_ctx=16, n_seq=1)
+    assert b2.lib.b2_state_seq_set_data(small.h, 0, snap, len(snap), None) == b2.NO_KV_SLOT
+
+
+def test_abort_callback_stops_decode_and_generate(model_file):
+    """llama_set_abort_callback (Sutra/src/llm_backends.cpp:3017): a callback
+    that asks to stop ends b2_decode / b2_generate with status 2 (Sutra maps
+    it to Cancelled), and the context stays usable."""
+    gm = b2.Model(model_file)
+    ctx = b2.Context(gm, n_ctx=64, n_seq=1)
+    calls = []
+    stop = {"now": False}
+    ctx.set_abort_callback(lambda: calls.append(1) or stop["now"])
+    ctx.decode([1, 2, 3], want_logits=2)
+    assert calls, "the callback is polled"
+    stop["now"] = True
+    assert b2.lib.b2_decode(ctx.h, np.array([4], np.int32).ctypes.data, None, None, 1, 1) == b2.ABORTED
+    out = np.zeros(4, np.int32)
+    assert b2.lib.b2_generate(ctx.h, np.array([4], np.int32).ctypes.data, None, 1, 4, out.ctypes.data) == b2.ABORTED
+    assert ctx.kv_pos_max(0) == 2
+    ctx.set_abort_callback(None)
+    ctx.decode([4], want_logits=1)
+    assert np.all(np.isfinite(ctx.logits(0)))
