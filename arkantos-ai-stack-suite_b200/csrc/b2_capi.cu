@@ -453,13 +453,22 @@ int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_ca
                "attn_decode arguments");
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
   cudaStream_t s = as_stream(stream);
-  const int n_split = attn_splits(cap);
-  const size_t po = (size_t)n_q * n_head * n_split * head_dim, pm = (size_t)n_q * n_head * n_split * 2;
+  // scores / probabilities, then the arrival counters (zeroed here)
+  const size_t nsc = attn_scratch_floats(n_q, n_head, cap);
+  const size_t ncnt = (size_t)n_q * n_kv;
   void* scratch = nullptr;
-  B2_CUDA_TRY(cudaMallocAsync(&scratch, (po + pm) * 4, s));
-  float* part_o = static_cast<float*>(scratch);
-  const int rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap,
-                                  part_o, part_o + po, out, s);
+  B2_CUDA_TRY(cudaMallocAsync(&scratch, (nsc + ncnt) * 4, s));
+  float* scores = static_cast<float*>(scratch);
+  unsigned int* count = reinterpret_cast<unsigned int*>(scores + nsc);
+  int rc = B2_OK;
+  const cudaError_t e = cudaMemsetAsync(count, 0, ncnt * 4, s);
+  if (e != cudaSuccess) {
+    set_error("attn_decode: %s", cudaGetErrorString(e));
+    rc = B2_ERR_CUDA;
+  } else {
+    rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap, scores,
+                          count, out, s);
+  }
   cudaFreeAsync(scratch, s);
   return rc;
 }

@@ -21,6 +21,23 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Launches kern with programmatic stream serialization when PDL is on.
+template <typename K, typename... Args>
+int launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
+  return B2_OK;
+}
+
 // ---- mbarrier -----------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -179,6 +196,51 @@ __device__ __forceinline__ float b2_expf(float x) {
   }
   const float s1 = __int_as_float((ni + 127) << 23);
   return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
+// exp(x) in fp32 with the results of the host C library's expf (glibc 2.28+,
+// the table-driven algorithm published with ARM's optimized-routines):
+// x·32/ln2 = k + r with k rounded to an integer through the 1.5·2^52 shift,
+// 2^(k/32) from a 32-entry table of 2^(i/32) (rounded to double, with the
+// exponent field pre-biased by i·2^47), 2^(r/32) by a cubic, all in double,
+// then one rounding to float.  r is formed with one fused multiply-add, the
+// form the library's FMA build evaluates; the whole float range was compared
+// against the host library bit for bit.  The reference's CPU path
+// (ref_softmax_f32, Singularity/tests/test_and_bench_a5.cpp:260-278, and the
+// SiLU of the forward) calls expf, so kernels that must reproduce it bit for
+// bit use this.
+__constant__ static const unsigned long long kExp2Tab32[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+__device__ __forceinline__ float b2_expf_ref(float x) {
+  if (!(x == x)) return x;
+  if (x > 88.7228394f) return __int_as_float(0x7f800000);
+  if (x < -103.972084f) return 0.0f;
+  const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0, shift = 0x1.8p+52;
+  const double c0 = 0x1.c6af84b912394p-5 / 32768.0, c1 = 0x1.ebfce50fac4f3p-3 / 1024.0,
+               c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+  const double xd = (double)x;
+  double kd = __dadd_rn(__dmul_rn(inv_ln2_n, xd), shift);
+  const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+  kd = __dsub_rn(kd, shift);
+  const double r = __fma_rn(inv_ln2_n, xd, -kd);
+  const double s = __longlong_as_double((long long)(kExp2Tab32[ki & 31] + (ki << 47)));
+  const double z = __dadd_rn(__dmul_rn(c0, r), c1);
+  const double r2 = __dmul_rn(r, r);
+  double y = __dadd_rn(__dmul_rn(c2, r), 1.0);
+  y = __dadd_rn(__dmul_rn(z, r2), y);
+  return __double2float_rn(__dmul_rn(y, s));
+}
+
+// silu(g)·u in the reference's order: (g / (1 + expf(-g))) · u.
+__device__ __forceinline__ float silu_mul_ref(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, b2_expf_ref(-g))), u);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -118,8 +118,8 @@ struct b2_context {
   int in_slot = 0;
   // step buffers
   float *x = nullptr, *delta = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
-  float *logits = nullptr, *part_o = nullptr, *part_ml = nullptr, *top = nullptr;
-  unsigned int* attn_cnt = nullptr;   // [kStepMax][n_kv] arrival counters of the fused attention combine
+  float *logits = nullptr, *scores = nullptr, *top = nullptr;   // scores: attention [kStepMax][n_head][n_ctx]
+  unsigned int* attn_cnt = nullptr;   // [kStepMax][n_kv] arrival counters of the attention's softmax
   uint32_t* argmax_scr = nullptr;     // vocabulary-slice partials and arrival counters of the argmax
   // [ids kStepMax | top-1, margin 2*kStepMax | status] in one allocation: one
   // D2H copy returns a step's greedy result and the device-wait status
@@ -137,7 +137,8 @@ struct b2_context {
   int32_t* pf_in_h = nullptr;   // pinned staging of pf_in
   cudaEvent_t pf_ev = nullptr;  // the staging's last copy
   float *pf_x = nullptr, *pf_xn = nullptr, *pf_delta = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
-  float *pf_att = nullptr, *pf_gu = nullptr, *pf_h = nullptr, *pf_part_o = nullptr, *pf_part_ml = nullptr;
+  float *pf_att = nullptr, *pf_gu = nullptr, *pf_h = nullptr, *pf_scores = nullptr;
+  unsigned int* pf_attn_cnt = nullptr;
   uint8_t* pf_ws = nullptr;     // GEMM activation images
   // last decode
   int last_n = 0;
@@ -505,15 +506,13 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   for (auto& e : c->in_ev) B2_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   if ((rc = prepare_gemv_kernels())) return rc;
   const int T = kStepMax;
-  const int n_split = attn_splits(c->n_ctx);
   if ((rc = dalloc(c, &c->x, (size_t)T * d)) || (rc = dalloc(c, &c->delta, (size_t)T * d)) ||
       (rc = dalloc(c, &c->xn, (size_t)T * d)) ||
       (rc = dalloc(c, &c->qkv, (size_t)T * (m->nh_l + 2 * m->nkv_l) * hd)) ||
       (rc = dalloc(c, &c->q, (size_t)T * m->nh_l * hd)) || (rc = dalloc(c, &c->att, (size_t)T * m->nh_l * hd)) ||
       (rc = dalloc(c, &c->h, (size_t)T * m->ff_l)) ||
       (m->tp_size == 1 && (rc = dalloc(c, &c->logits, (size_t)T * m->n_vocab))) ||
-      (rc = dalloc(c, &c->part_o, (size_t)T * m->nh_l * n_split * hd)) ||
-      (rc = dalloc(c, &c->part_ml, (size_t)T * m->nh_l * n_split * 2)) || (rc = dalloc(c, &c->res, kResWords)) ||
+      (rc = dalloc(c, &c->scores, attn_scratch_floats(T, m->nh_l, c->n_ctx))) || (rc = dalloc(c, &c->res, kResWords)) ||
       (rc = dalloc(c, &c->gen_out, (size_t)c->n_ctx * T)) || (rc = dalloc(c, &c->gen_count, T)))
     return rc;
   {
@@ -638,14 +637,8 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
         return rc;
       if ((rc = tap("q_rope", l, c->q, (int64_t)n * m->nh_l * hd))) return rc;
     }
-    // Fused: the attention's last CTAs combine the chunks and quantize the O
-    // projection's input image.
-    const bool fuse_attn = fuse && attn_combine_fusable(m->nh_l, m->nkv_l, hd, c->n_ctx);
-    const bool fuse_o = fuse_attn && attn_fusable(m->nh_l, m->nkv_l, hd, L.wo.m.type);
-    const ActImage o_img = gemv_act_image(L.wo.m, n, c->act_img);
     if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->vc[l], c->st_d,
-                               c->n_seq, c->n_ctx, c->part_o, c->part_ml, c->att, s, c->status,
-                               fuse_attn ? c->attn_cnt : nullptr, fuse_o ? &o_img : nullptr)))
+                               c->n_seq, c->n_ctx, c->scores, c->attn_cnt, c->att, s, c->status)))
       return rc;
     if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
     {
@@ -660,7 +653,6 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
       a.status = c->status;
       a.act_img = c->act_img;
       a.peer = tp ? &out_o : nullptr;
-      a.image_ready = fuse_o;
       if ((rc = launch_gemv(a, s))) return rc;
     }
     if (!tp && (rc = tap("attn_proj", l, c->delta, (int64_t)n * d))) return rc;
@@ -775,9 +767,8 @@ int prefill_alloc(b2_context* c) {
   if (c->pf_cap) return B2_OK;
   b2_model* m = c->model;
   const int d = m->n_embd, hd = m->head_dim, qkv_w = (m->nh_l + 2 * m->nkv_l) * hd, nq = m->nh_l * hd;
-  const int n_split = attn_splits(c->n_ctx);
   const size_t per_tok = 4 * ((size_t)3 * d + qkv_w + 2 * (size_t)nq + 3 * (size_t)m->ff_l +
-                              (size_t)m->nh_l * n_split * (hd + 2) + 3);
+                              attn_scratch_floats(1, m->nh_l, c->n_ctx) + m->nkv_l + 3);
   const int cap = (int)std::max<size_t>(kPrefillMin, std::min<size_t>(kPrefillCapMax, kPrefillBudget / per_tok));
   size_t ws = 0;
   for (const auto& L : m->layers)
@@ -789,18 +780,20 @@ int prefill_alloc(b2_context* c) {
       (rc = dalloc(c, &c->pf_qkv, (size_t)cap * qkv_w)) || (rc = dalloc(c, &c->pf_q, (size_t)cap * nq)) ||
       (rc = dalloc(c, &c->pf_att, (size_t)cap * nq)) || (rc = dalloc(c, &c->pf_gu, (size_t)cap * 2 * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_h, (size_t)cap * m->ff_l)) ||
-      (rc = dalloc(c, &c->pf_part_o, (size_t)cap * m->nh_l * n_split * hd)) ||
-      (rc = dalloc(c, &c->pf_part_ml, (size_t)cap * m->nh_l * n_split * 2)) || (rc = dalloc(c, &c->pf_ws, ws))) {
+      (rc = dalloc(c, &c->pf_scores, attn_scratch_floats(cap, m->nh_l, c->n_ctx))) ||
+      (rc = dalloc(c, &c->pf_attn_cnt, (size_t)cap * m->nkv_l)) || (rc = dalloc(c, &c->pf_ws, ws))) {
     // A context short of memory keeps none of the chunk buffers: free the
     // ones this call took (nothing has been enqueued on them).
     for (size_t i = n_before; i < c->allocs.size(); ++i) cudaFree(c->allocs[i]);
     c->allocs.resize(n_before);
     c->pf_in = nullptr;
     c->pf_x = c->pf_xn = c->pf_delta = c->pf_qkv = c->pf_q = c->pf_att = c->pf_gu = c->pf_h = nullptr;
-    c->pf_part_o = c->pf_part_ml = nullptr;
+    c->pf_scores = nullptr;
+    c->pf_attn_cnt = nullptr;
     c->pf_ws = nullptr;
     return rc;
   }
+  B2_CUDA_TRY(cudaMemset(c->pf_attn_cnt, 0, (size_t)cap * m->nkv_l * sizeof(unsigned int)));
   B2_CUDA_TRY(cudaMallocHost(&c->pf_in_h, (size_t)3 * cap * sizeof(int32_t)));
   B2_CUDA_TRY(cudaEventCreateWithFlags(&c->pf_ev, cudaEventDisableTiming));
   c->pf_cap = cap;
@@ -822,7 +815,7 @@ int enqueue_prefill_chunk(b2_context* c, int nt) {
         (rc = launch_rope_kv(c->pf_qkv, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->rope, c->pf_q, c->kc[l], c->vc[l],
                              c->st_d, c->n_seq, c->n_ctx, s)) ||
         (rc = launch_attention(c->pf_q, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->kc[l], c->vc[l], c->st_d, c->n_seq,
-                               c->n_ctx, c->pf_part_o, c->pf_part_ml, c->pf_att, s, c->status)) ||
+                               c->n_ctx, c->pf_scores, c->pf_attn_cnt, c->pf_att, s, c->status)) ||
         (rc = launch_gemm(L.wo.m, c->pf_att, nq, nt, c->pf_delta, c->pf_ws, c->status, s)) ||
         (rc = launch_add_rmsnorm(c->pf_x, c->pf_delta, L.ffn_norm, c->pf_xn, nt, d, m->eps, s, nullptr,
                                  c->status)) ||

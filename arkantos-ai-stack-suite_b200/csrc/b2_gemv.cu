@@ -4,105 +4,77 @@
 // ref_vec_dot_q4_0_q8_0 / _q8_0_q8_0 (Singularity/tests/test_and_bench_a5.cpp:184-221)
 // and, for K-quants, ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K.
 //
-// Weights are in the tile layout (8-row tiles, S unit ranges per row, see
-// QMatrix).  One CTA per SM takes a contiguous run of items: tile pairs
-// (16 rows) for the mma kernels, groups of P = 8/S tiles for dp4a.
-//   * the last warp is the producer: lane 0 streams each stage — for every
-//     tile of the item the next U unit slots of all its ranges, one
-//     contiguous cp.async.bulk (1-D TMA) per tile — into a ring of
-//     shared-memory stages completing on full[] mbarriers.  It starts before
-//     the grid dependency resolves, so weights stream while the previous
-//     kernel drains (PDL).
-//   * the activations are quantized (bit-exact with the reference's
-//     quantizers) either by every CTA into shared memory (small inputs) or
-//     once per launch by a small kernel into an image of the shared-memory
-//     layout that the producer copies in after the grid dependency resolves.
-//   * integer dots are exact: for 1-2 tokens with dp4a (8 warps; warp = tile
-//     of the group x range, lane = tile row x unit residue mod 4); for 3-8
-//     tokens with int8 mma.sync m16n8k32 (m16n8k16 for Q6_K's 16-weight
-//     groups) with the tile pair's 16 weight rows as M and the tokens as N
-//     (16 warps in sets of S; a set works one tile pair, a warp one range of
-//     it for all four unit residues).  Each unit's integer sums are scaled in
-//     fp32 as the reference does, into four partial sums by unit residue mod
-//     4; a range's sum is (a0 + a1) + (a2 + a3) and the S ranges of a row are
-//     added in order through shared memory — one order for every batch size
-//     (restated by the oracle's orc_tile_row_dot).
+// Summation order: the reference's.  Every output y[t][r] is the left fold
+// over the row's units in order, sumf = ((0 + p_0) + p_1) + ... (Q4_K:
+// ((sumf + a_u) − b_u) per unit), where each unit's terms are the exact
+// integer block sums scaled exactly as the CPU vec_dot scales them.  So every
+// output is bit-identical to the reference's per-row result.
+//
+// Weights are in the tile layout (8-row tiles, units in order, see QMatrix).
+// A CTA takes a contiguous run of tiles; its warps own tiles round-robin and
+// fold each tile's rows through all units themselves, so no cross-warp
+// reduction or barrier sits in the main loop.  Every warp streams its own
+// tiles: lane 0 issues 1-D bulk copies (cp.async.bulk, no multicast) of U
+// consecutive unit slots into the warp's ring of stages, each completing on
+// its own mbarrier, and refills a stage as soon as the warp has read it.  The
+// first stages are issued before the grid dependency resolves, so with
+// programmatic dependent launch a GEMV's weights stream while the previous
+// kernel finishes.
+//   * activations are quantized bit-exactly with the reference's quantizers,
+//     either by the CTA itself into shared memory (small inputs) or once per
+//     launch by a producer kernel into an image that one bulk copy brings in;
+//   * 1-2 tokens: dp4a, lane = tile row g (lane & 7) x unit residue j
+//     (lane >> 3); the four lanes of a row exchange their unit terms by
+//     shuffles and all fold them in unit order;
+//   * 3-8 tokens: int8 mma.sync (m16n8k32; m16n8k16 for Q6_K's 16-weight
+//     groups) with the tokens as M (rows 8-15 zero) and the tile's 8 weight
+//     rows as N; lane 4g+q folds (token g, rows 2q and 2q+1);
 //   * epilogue: store, residual add, SwiGLU over interleaved gate/up rows,
-//     or the tensor-parallel exchange into every rank's gather buffer.
-// Every mbarrier wait is bounded; a warp whose wait expires records a status
-// code and runs to the end without waiting or computing, so the named
-// barriers stay matched and the CTA always exits.
+//     RoPE + fp16 KV store over the fused QKV rows, or the tensor-parallel
+//     exchange into every rank's gather buffer.
+// Every mbarrier wait is bounded: a warp whose wait expires records a status
+// code, stops computing and issuing, waits (bounded) for the copies it still
+// has in flight, and the CTA always exits.
 #include "b2_common.cuh"
 #include "b2_quant.cuh"
 
 namespace b2 {
 namespace {
 
-// Consumer warps: 16 for the mma kernels, 8 for the dp4a kernels; plus one
-// producer.
-constexpr int kMaxNCW = 16;
-constexpr int ncw_for(int mode) { return mode == 0 ? 16 : 8; }
-constexpr int kMaxStages = 16;
-constexpr int kBarBytes = 512;           // full[kMaxStages], empty[kMaxStages], act, padded
+constexpr int kMaxWarps = 16;
+constexpr int kMaxStages = 8;            // ring stages per warp
+constexpr int kHdrBytes = 1152;          // full[kMaxWarps][kMaxStages], act barrier, padding
 constexpr int kMaxTok = 8;
 constexpr int kDp4aMaxTok = 2;           // dp4a up to this many tokens, mma.sync above
 constexpr uint32_t kM4 = 0x0F0F0F0Fu;
 
 constexpr int kMaxMat = 64;          // matrices of one multi-matrix launch
 struct GemvP {
-  const uint8_t* w;
-  int type, nu, S, L, slot_bytes;
+  int type, nu, slot_bytes;
   int64_t tile_bytes, n_rows, n_tiles, k;
-  int n_tok, n_act_tok;   // tokens computed; token rows quantized into shared memory (8 for mma)
+  int n_tok;
   const float* x;
   int64_t x_stride;
-  float* y;
   int64_t y_stride;
   int epilogue;
-  int U, n_stages;
-  uint32_t stage_bytes;   // P tiles x U x S slots
-  int kq;                 // activation row bytes (k rounded up to 128)
-  uint32_t off_dx, off_bs, act_bytes;   // activation carve-up (bytes from the activation base)
-  const uint8_t* act_img; // the quantized activations in that carve-up (global), or null:
-                          // the consumers quantize x into shared memory themselves
+  int U, n_ch, n_stages;   // units per stage, stages per tile, ring stages per warp
+  uint32_t stage_bytes;    // U * slot_bytes
+  int kq;                  // activation row stride in bytes
+  uint32_t off_dx, off_bs, act_bytes, act_region;   // activation carve-up and its shared-memory size
+  const uint8_t* act_img;  // the quantized activations (global), or null: the CTA quantizes x itself
   int* status;
   PeerOut peer;
   RopeKvEpi rope;
-  // The matrices of the launch (same type and shape, one shared x): items
-  // run over matrix 0's, then matrix 1's, ...; wl[0] = w, yl[0] = y for one.
+  // The matrices of the launch (same type and shape, one shared x): tiles
+  // run over matrix 0's, then matrix 1's, ...
   int n_mat;
-  int64_t ipm;            // items per matrix
+  int64_t tpm;             // tiles per matrix
   const uint8_t* wl[kMaxMat];
   float* yl[kMaxMat];
 };
 
-__device__ __forceinline__ void consumer_sync(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-}
-// The S warps of tile slot p (barrier ids 2..9).
-__device__ __forceinline__ void tile_sync(int p, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(2 + p), "r"(nthreads) : "memory");
-}
-
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-
-// Activation image (global and in shared memory): the ActImage carve-up,
-// stored by store_q8k_unit / store_q8_0_block (b2_quant.cuh).
-__device__ __forceinline__ void act_frag16(const uint8_t* trow, int u, int g, int q, uint32_t (&a)[16]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint4 v = lds128(trow + u * 256 + (((4 * i + q) + 4 * (g & 1)) & 15) * 16);
-    a[4 * i] = v.x;
-    a[4 * i + 1] = v.y;
-    a[4 * i + 2] = v.z;
-    a[4 * i + 3] = v.w;
-  }
-}
-__device__ __forceinline__ uint2 act_frag2(const uint8_t* trow, int u, int g, int q) {
-  return *reinterpret_cast<const uint2*>(trow + (u >> 2) * 128 + ((((u & 3) * 4 + q) + 4 * (g & 3)) & 15) * 8);
-}
-__device__ __forceinline__ uint4 act_chunk16(const uint8_t* trow, int c) { return lds128(trow + c * 16); }
 
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
   int d;
@@ -111,27 +83,25 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 }
 __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
-// Rows-as-M forms: D[16x8] = A[16xK] (weight rows of a tile pair) * B[Kx8]
-// (k x tokens).  d[0..3] = (row g, token 2q), (row g, 2q+1), (row g+8, 2q),
-// (row g+8, 2q+1) for lane = 4g + q.
-__device__ __forceinline__ void mma16_k32_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
+// Tokens-as-M forms: D[16x8] = A[16xK] (token rows 0..7, rows 8..15 zero)
+// * B[Kx8] (k x the tile's weight rows).  With a1 = a3 = 0, lane 4g+q gets
+// d[0] = (token g, row 2q), d[1] = (token g, row 2q+1).
+__device__ __forceinline__ void mma_k32_s8u8(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
 }
-__device__ __forceinline__ void mma16_k32_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_k32_s8s8(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
 }
-__device__ __forceinline__ void mma16_k16_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+__device__ __forceinline__ void mma_k16_s8u8(int (&d)[4], uint32_t a0, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+               : "r"(a0), "r"(0), "r"(b0), "r"(0));
 }
 
 __device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)((w >> (8 * b)) & 0xFFu); }
@@ -146,69 +116,69 @@ __device__ __forceinline__ void q4k_scales(uint32_t s0, uint32_t s1, uint32_t s2
   sh = (s2 & kM4) | ((s0 >> 2) & 0x30303030u);
   mh = ((s2 >> 4) & kM4) | ((s1 >> 2) & 0x30303030u);
 }
+// Σ_j m_j · bsum_j over the 8 32-groups (bq: 8 int16 group sums of one token).
+__device__ __forceinline__ int q4k_msum(const uint4& bq, uint32_t ml, uint32_t mh) {
+  int m = __dp2a_lo((int)bq.x, (int)ml, 0);
+  m = __dp2a_hi((int)bq.y, (int)ml, m);
+  m = __dp2a_lo((int)bq.z, (int)mh, m);
+  return __dp2a_hi((int)bq.w, (int)mh, m);
+}
 
 // ---- activation image ------------------------------------------------------------------
-// fp32 x [n_tok][k] -> the image: codes, the fp32 scale of every unit, and the
-// block sums the unit terms need (Q4_0: per 32; Q4_K: per 32 as pairs of
-// Q8_K sums; Q6_K: Q8_K's per 16).  Token rows n_tok..n_act_tok-1 are zero.
-// Threads tid of nthreads (a multiple of 32) share the work; img is global
-// memory (the quantize kernel) or the GEMV's shared memory.
+// fp32 x [n_tok][k] -> the image (ActImage carve-up, codes in natural order):
+// codes, the fp32 scale of every unit, and the block sums the unit terms
+// need (Q4_0: per 32; Q4_K: per 32 as pairs of Q8_K sums; Q6_K: Q8_K's per
+// 16).  Threads tid of nthreads (a multiple of 32) share the work; img is
+// global memory (the quantize kernel) or the GEMV's shared memory.
 __device__ void quantize_image(const float* __restrict__ x, int64_t x_stride, int n_tok, const ActImage& img,
                                int64_t tid, int64_t nthreads) {
   const int nu = img.nu;
   if (img.type == B2_Q4_0 || img.type == B2_Q8_0) {
     // One 32-value block per thread: eight float4 loads in flight, then the
     // reference quantizer on registers.
-    for (int64_t i = tid; i < (int64_t)img.n_act_tok * nu; i += nthreads) {
+    for (int64_t i = tid; i < (int64_t)n_tok * nu; i += nthreads) {
       const int t = (int)(i / nu), b = (int)(i - (int64_t)t * nu);
       uint32_t w[8];
       int sum = 0;
-      float dq = 0.0f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) w[j] = 0;
-      if (t < n_tok) {
-        const float4* src = reinterpret_cast<const float4*>(x + t * x_stride + (int64_t)b * 32);
-        float v[32];
+      const float4* src = reinterpret_cast<const float4*>(x + t * x_stride + (int64_t)b * 32);
+      float v[32];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 f = __ldg(src + j);
-          v[4 * j] = f.x;
-          v[4 * j + 1] = f.y;
-          v[4 * j + 2] = f.z;
-          v[4 * j + 3] = f.w;
-        }
-        float amax = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-        const float d = __fmul_rn(amax, 1.0f / 127.0f);
-        const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float sc = __fmul_rn(v[j], id);
-          const float tt = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
-          int q = __float2int_rz(tt);
-          q = q < -127 ? -127 : (q > 127 ? 127 : q);
-          sum += q;
-          w[j >> 2] |= ((uint32_t)(uint8_t)q) << (8 * (j & 3));
-        }
-        dq = h2f(f2h_rn(d));
+      for (int j = 0; j < 8; ++j) {
+        const float4 f = __ldg(src + j);
+        v[4 * j] = f.x;
+        v[4 * j + 1] = f.y;
+        v[4 * j + 2] = f.z;
+        v[4 * j + 3] = f.w;
       }
-      store_q8_0_block(img, t, b, w, dq, sum);
+      float amax = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+      const float d = __fmul_rn(amax, 1.0f / 127.0f);
+      const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float sc = __fmul_rn(v[j], id);
+        const float tt = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
+        int q = __float2int_rz(tt);
+        q = q < -127 ? -127 : (q > 127 ? 127 : q);
+        sum += q;
+        w[j >> 2] |= ((uint32_t)(uint8_t)q) << (8 * (j & 3));
+      }
+      store_q8_0_block(img, t, b, w, h2f(f2h_rn(d)), sum);
     }
   } else {
     // One 256-value super-block per warp, 8 values per lane.
     const int lane = threadIdx.x & 31;
-    for (int64_t i = tid >> 5; i < (int64_t)img.n_act_tok * nu; i += nthreads >> 5) {
+    for (int64_t i = tid >> 5; i < (int64_t)n_tok * nu; i += nthreads >> 5) {
       const int t = (int)(i / nu), b = (int)(i - (int64_t)t * nu);
-      int8_t q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      int8_t q[8];
       int bs = 0;
-      float d = 0.0f;
-      if (t < n_tok) {   // warp-uniform
-        const float4* src = reinterpret_cast<const float4*>(x + t * x_stride + (int64_t)b * 256 + lane * 8);
-        const float4 f0 = __ldg(src), f1 = __ldg(src + 1);
-        const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-        d = quant_q8_k_lane(v, q, &bs);
-      }
+      const float4* src = reinterpret_cast<const float4*>(x + t * x_stride + (int64_t)b * 256 + lane * 8);
+      const float4 f0 = __ldg(src), f1 = __ldg(src + 1);
+      const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+      const float d = quant_q8_k_lane(v, q, &bs);
       store_q8k_unit(img, t, b, q, d, bs);
     }
   }
@@ -221,146 +191,12 @@ __global__ void quantize_image_kernel(const float* __restrict__ x, int64_t x_str
                  (int64_t)gridDim.x * blockDim.x);
 }
 
-// ---- mma path: one unit of a 16-row tile pair for tokens 0..7 ------------------------------
-// sa, sb: the unit's slot in tile a (rows 0..7 -> D rows 0..7) and tile b
-// (D rows 8..15).  Lane 4g + q holds outputs i = 2*tb + e: tile row g of
-// tile tb (0: a, 1: b) for token 2q + e.  Each output's fp32 update is the
-// reference's per-unit sequence.
-template <int WT>
-__device__ __forceinline__ void mma2_unit(const GemvP& p, const uint8_t* sa, const uint8_t* sb, const uint8_t* act,
-                                          int u, int g, int q, float (&acc)[4]) {
-  const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
-  const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
-  const float dx0 = dxs[(2 * q) * p.nu + u], dx1 = dxs[(2 * q + 1) * p.nu + u];
-  const uint8_t* trow = act + g * p.kq;   // B column g = token g
-  if constexpr (WT == B2_Q4_0) {
-    const uint32_t wa = lds32(sa + 16 * g + 4 * q), wb = lds32(sb + 16 * g + 4 * q);
-    const uint2 b = act_frag2(trow, u, g, q);
-    int c[4];
-    mma16_k32_u8s8(c, wa & kM4, wb & kM4, (wa >> 4) & kM4, (wb >> 4) & kM4, b.x, b.y);
-    const int corr0 = 8 * (int)bss[(2 * q) * p.nu + u], corr1 = 8 * (int)bss[(2 * q + 1) * p.nu + u];
-    const float da = h2f(*reinterpret_cast<const uint16_t*>(sa + 128 + 2 * g));
-    const float db = h2f(*reinterpret_cast<const uint16_t*>(sb + 128 + 2 * g));
-    acc[0] = __fadd_rn(acc[0], __fmul_rn(__fmul_rn(da, dx0), (float)(c[0] - corr0)));
-    acc[1] = __fadd_rn(acc[1], __fmul_rn(__fmul_rn(da, dx1), (float)(c[1] - corr1)));
-    acc[2] = __fadd_rn(acc[2], __fmul_rn(__fmul_rn(db, dx0), (float)(c[2] - corr0)));
-    acc[3] = __fadd_rn(acc[3], __fmul_rn(__fmul_rn(db, dx1), (float)(c[3] - corr1)));
-  } else if constexpr (WT == B2_Q8_0) {
-    const uint2 b = act_frag2(trow, u, g, q);
-    int c[4];
-    mma16_k32_s8s8(c, lds32(sa + 16 * g + 4 * q), lds32(sb + 16 * g + 4 * q), lds32(sa + 128 + 16 * g + 4 * q),
-                   lds32(sb + 128 + 16 * g + 4 * q), b.x, b.y);
-    const float da = h2f(*reinterpret_cast<const uint16_t*>(sa + 256 + 2 * g));
-    const float db = h2f(*reinterpret_cast<const uint16_t*>(sb + 256 + 2 * g));
-    acc[0] = __fadd_rn(acc[0], __fmul_rn(__fmul_rn(da, dx0), (float)c[0]));
-    acc[1] = __fadd_rn(acc[1], __fmul_rn(__fmul_rn(da, dx1), (float)c[1]));
-    acc[2] = __fadd_rn(acc[2], __fmul_rn(__fmul_rn(db, dx0), (float)c[2]));
-    acc[3] = __fadd_rn(acc[3], __fmul_rn(__fmul_rn(db, dx1), (float)c[3]));
-  } else if constexpr (WT == B2_Q4_K) {
-    const uint4 ma = lds128(sa + 1024 + 16 * g), mb = lds128(sb + 1024 + 16 * g);
-    uint32_t sla, mla, sha, mha, slb, mlb, shb, mhb;
-    q4k_scales(ma.y, ma.z, ma.w, sla, mla, sha, mha);
-    q4k_scales(mb.y, mb.z, mb.w, slb, mlb, shb, mhb);
-    const uint8_t* qa = sa + 128 * g;
-    const uint8_t* qb = sb + 128 * g;
-    uint32_t af[16];
-    act_frag16(trow, u, g, q, af);
-    int is[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int jc = 0; jc < 4; ++jc) {
-      const uint32_t wa0 = lds32(qa + 16 * ((2 * jc + g) & 7) + 4 * q);
-      const uint32_t wa1 = lds32(qa + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
-      const uint32_t wb0 = lds32(qb + 16 * ((2 * jc + g) & 7) + 4 * q);
-      const uint32_t wb1 = lds32(qb + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int j = 2 * jc + h;
-        int c[4];
-        if (h == 0)
-          mma16_k32_u8s8(c, wa0 & kM4, wb0 & kM4, wa1 & kM4, wb1 & kM4, af[2 * j], af[2 * j + 1]);
-        else
-          mma16_k32_u8s8(c, (wa0 >> 4) & kM4, (wb0 >> 4) & kM4, (wa1 >> 4) & kM4, (wb1 >> 4) & kM4, af[2 * j],
-                         af[2 * j + 1]);
-        const int sa_j = j < 4 ? ubyte(sla, j) : ubyte(sha, j - 4);
-        const int sb_j = j < 4 ? ubyte(slb, j) : ubyte(shb, j - 4);
-        is[0] += sa_j * c[0];
-        is[1] += sa_j * c[1];
-        is[2] += sb_j * c[2];
-        is[3] += sb_j * c[3];
-      }
-    }
-    const uint4 b0 = lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q) * p.nu + u) * 8));
-    const uint4 b1 = lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q + 1) * p.nu + u) * 8));
-    auto msum = [](const uint4& bq, uint32_t ml, uint32_t mh) {
-      int m = __dp2a_lo((int)bq.x, (int)ml, 0);
-      m = __dp2a_hi((int)bq.y, (int)ml, m);
-      m = __dp2a_lo((int)bq.z, (int)mh, m);
-      return __dp2a_hi((int)bq.w, (int)mh, m);
-    };
-    const int ms[4] = {msum(b0, mla, mha), msum(b1, mla, mha), msum(b0, mlb, mhb), msum(b1, mlb, mhb)};
-    const float dd[2] = {h2f((uint16_t)(ma.x & 0xFFFFu)), h2f((uint16_t)(mb.x & 0xFFFFu))};
-    const float dm[2] = {h2f((uint16_t)(ma.x >> 16)), h2f((uint16_t)(mb.x >> 16))};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float dx = (i & 1) ? dx1 : dx0;
-      acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dd[i >> 1], dx), (float)is[i]));
-      acc[i] = __fsub_rn(acc[i], __fmul_rn(__fmul_rn(dm[i >> 1], dx), (float)ms[i]));
-    }
-  } else {  // Q6_K: 16 groups of 16 weights, m16n8k16
-    const uint8_t* qla = sa + 128 * g;
-    const uint8_t* qlb = sb + 128 * g;
-    const uint8_t* qha = sa + 1024 + 64 * g;
-    const uint8_t* qhb = sb + 1024 + 64 * g;
-    const uint4 sca = lds128(sa + 1536 + 16 * g), scb = lds128(sb + 1536 + 16 * g);
-    const uint32_t swa[4] = {sca.x, sca.y, sca.z, sca.w}, swb[4] = {scb.x, scb.y, scb.z, scb.w};
-    const int16_t* bs0 = bss + ((2 * q) * p.nu + u) * 16;
-    const int16_t* bs1 = bss + ((2 * q + 1) * p.nu + u) * 16;
-    uint32_t af[16];
-    act_frag16(trow, u, g, q, af);
-    int is[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        // qh word of l = 16*hf + 4q.. of half hh; ql words of quartiles a = 0/2 (lo/hi nibble of
-        // chunk 4hh + hf) and a = 1/3 (chunk 4hh + 2 + hf)
-        const uint32_t ha = lds32(qha + 16 * ((2 * hh + hf + g) & 3) + 4 * q);
-        const uint32_t hb = lds32(qhb + 16 * ((2 * hh + hf + g) & 3) + 4 * q);
-#pragma unroll
-        for (int a1 = 0; a1 < 2; ++a1) {
-          const uint32_t la = lds32(qla + 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q);
-          const uint32_t lb = lds32(qlb + 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q);
-#pragma unroll
-          for (int nh = 0; nh < 2; ++nh) {
-            const int a = a1 + 2 * nh;          // quartile of the half
-            const int i = hh * 8 + a * 2 + hf;  // 16-weight group of the super-block
-            const uint32_t va = (nh ? (la >> 4) & kM4 : la & kM4) | (((ha >> (2 * a)) & 0x03030303u) << 4);
-            const uint32_t vb = (nh ? (lb >> 4) & kM4 : lb & kM4) | (((hb >> (2 * a)) & 0x03030303u) << 4);
-            int c[4];
-            mma16_k16_u8s8(c, va, vb, af[i]);
-            const int o0 = 32 * (int)bs0[i], o1 = 32 * (int)bs1[i];
-            const int s_a = sbyte(swa[i >> 2], i & 3), s_b = sbyte(swb[i >> 2], i & 3);
-            is[0] += s_a * (c[0] - o0);
-            is[1] += s_a * (c[1] - o1);
-            is[2] += s_b * (c[2] - o0);
-            is[3] += s_b * (c[3] - o1);
-          }
-        }
-      }
-    }
-    const float da = h2f(*reinterpret_cast<const uint16_t*>(sa + 1664 + 2 * g));
-    const float db = h2f(*reinterpret_cast<const uint16_t*>(sb + 1664 + 2 * g));
-    acc[0] = __fadd_rn(acc[0], __fmul_rn(__fmul_rn(da, dx0), (float)is[0]));
-    acc[1] = __fadd_rn(acc[1], __fmul_rn(__fmul_rn(da, dx1), (float)is[1]));
-    acc[2] = __fadd_rn(acc[2], __fmul_rn(__fmul_rn(db, dx0), (float)is[2]));
-    acc[3] = __fadd_rn(acc[3], __fmul_rn(__fmul_rn(db, dx1), (float)is[3]));
-  }
-}
-
-// ---- dp4a path: one unit, tile row g, tokens 0..B-1 -----------------------------------------
+// ---- dp4a path: the terms of one unit u, tile row g, tokens 0..B-1 ---------------------------
+// pa[t] is the unit's product (d_w·d_x)·isum; for Q4_K pb[t] is the min term
+// (dmin·d_x)·msum, subtracted after pa is added.
 template <int WT, int B>
-__device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, int g,
-                                          float (&acc)[B]) {
+__device__ __forceinline__ void dp4a_terms(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, int g,
+                                           float (&pa)[B], float (&pb)[B]) {
   const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
   const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
   if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
@@ -383,8 +219,8 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
     }
 #pragma unroll
     for (int t = 0; t < B; ++t) {
-      const uint8_t* trow = act + t * p.kq;
-      const uint4 xa = act_chunk16(trow, 2 * u), xb = act_chunk16(trow, 2 * u + 1);
+      const uint8_t* xr = act + t * p.kq + u * 32;
+      const uint4 xa = lds128(xr), xb = lds128(xr + 16);
       int s;
       if constexpr (WT == B2_Q4_0) {
         int s0 = dp4a_us(lo[0], xa.x, 0), s1 = dp4a_us(hi[0], xb.x, 0);
@@ -405,7 +241,8 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
         s1 = dp4a_ss(hi[3], xb.w, s1);
         s = s0 + s1;
       }
-      acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, dxs[t * p.nu + u]), (float)s));
+      pa[t] = __fmul_rn(__fmul_rn(dw, dxs[t * p.nu + u]), (float)s);
+      pb[t] = 0.0f;
     }
   } else if constexpr (WT == B2_Q4_K) {
     const uint4 meta = lds128(sl + 1024 + 16 * g);
@@ -425,10 +262,8 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
       const int s_hi = jc < 2 ? ubyte(sl4, 2 * jc + 1) : ubyte(sh4, 2 * jc - 3);
 #pragma unroll
       for (int t = 0; t < B; ++t) {
-        const uint8_t* trow = act + t * p.kq;
-        const int c0 = u * 16 + 4 * jc;   // the 64 activation bytes of this 32-byte qs pair
-        const uint4 x0 = act_chunk16(trow, c0), x1 = act_chunk16(trow, c0 + 1);
-        const uint4 x2 = act_chunk16(trow, c0 + 2), x3 = act_chunk16(trow, c0 + 3);
+        const uint8_t* xr = act + t * p.kq + u * 256 + 64 * jc;   // the 64 codes of this 32-byte qs pair
+        const uint4 x0 = lds128(xr), x1 = lds128(xr + 16), x2 = lds128(xr + 32), x3 = lds128(xr + 48);
         const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
         const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
         int dl = 0, dh = 0;
@@ -442,14 +277,10 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
     }
 #pragma unroll
     for (int t = 0; t < B; ++t) {
-      const uint4 b32 = lds128(reinterpret_cast<const uint8_t*>(bss + (t * p.nu + u) * 8));
-      int m = __dp2a_lo((int)b32.x, (int)ml4, 0);
-      m = __dp2a_hi((int)b32.y, (int)ml4, m);
-      m = __dp2a_lo((int)b32.z, (int)mh4, m);
-      m = __dp2a_hi((int)b32.w, (int)mh4, m);
+      const int m = q4k_msum(lds128(reinterpret_cast<const uint8_t*>(bss + (t * p.nu + u) * 8)), ml4, mh4);
       const float dx = dxs[t * p.nu + u];
-      acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dd, dx), (float)is[t]));
-      acc[t] = __fsub_rn(acc[t], __fmul_rn(__fmul_rn(dm, dx), (float)m));
+      pa[t] = __fmul_rn(__fmul_rn(dd, dx), (float)is[t]);
+      pb[t] = __fmul_rn(__fmul_rn(dm, dx), (float)m);
     }
   } else {  // Q6_K
     const uint8_t* qlr = sl + 128 * g;
@@ -480,8 +311,8 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
           const int s0 = sbyte(scw[g0 >> 2], g0 & 3), s1 = sbyte(scw[(g0 + 1) >> 2], (g0 + 1) & 3);
 #pragma unroll
           for (int t = 0; t < B; ++t) {
-            const uint8_t* trow = act + t * p.kq;
-            const uint4 xa = act_chunk16(trow, u * 16 + g0), xb = act_chunk16(trow, u * 16 + g0 + 1);
+            const uint8_t* xr = act + t * p.kq + u * 256 + 16 * g0;
+            const uint4 xa = lds128(xr), xb = lds128(xr + 16);
             int d0 = dp4a_us(v[0], xa.x, 0);
             d0 = dp4a_us(v[1], xa.y, d0);
             d0 = dp4a_us(v[2], xa.z, d0);
@@ -497,8 +328,109 @@ __device__ __forceinline__ void dp4a_unit(const GemvP& p, const uint8_t* sl, con
       }
     }
 #pragma unroll
-    for (int t = 0; t < B; ++t)
-      acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(d6, dxs[t * p.nu + u]), (float)is[t]));
+    for (int t = 0; t < B; ++t) {
+      pa[t] = __fmul_rn(__fmul_rn(d6, dxs[t * p.nu + u]), (float)is[t]);
+      pb[t] = 0.0f;
+    }
+  }
+}
+
+// ---- mma path: the terms of one unit u for (token g, rows 2q and 2q+1) -----------------------
+// a[r] / b[r] as in dp4a_terms for row 2q + r.  Tokens at or past n_tok feed
+// zero codes (their outputs are never stored).
+template <int WT>
+__device__ __forceinline__ void mma_terms(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, int g, int q,
+                                          bool live, float (&a)[2], float (&b)[2]) {
+  const float dx = live ? reinterpret_cast<const float*>(act + p.off_dx)[g * p.nu + u] : 0.0f;
+  const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
+  const uint8_t* xr = act + g * p.kq;
+  if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
+    const uint8_t* xb = xr + u * 32;
+    const uint32_t a0 = live ? lds32(xb + 4 * q) : 0u, a2 = live ? lds32(xb + 16 + 4 * q) : 0u;
+    int c[4];
+    uint32_t dw2;
+    if constexpr (WT == B2_Q4_0) {
+      const uint32_t w = lds32(sl + 16 * g + 4 * q);
+      mma_k32_s8u8(c, a0, a2, w & kM4, (w >> 4) & kM4);
+      const int corr = live ? 8 * (int)bss[g * p.nu + u] : 0;
+      c[0] -= corr;
+      c[1] -= corr;
+      dw2 = lds32(sl + 128 + 4 * q);
+    } else {
+      mma_k32_s8s8(c, a0, a2, lds32(sl + 16 * g + 4 * q), lds32(sl + 128 + 16 * g + 4 * q));
+      dw2 = lds32(sl + 256 + 4 * q);
+    }
+    const float d0 = h2f((uint16_t)(dw2 & 0xFFFFu)), d1 = h2f((uint16_t)(dw2 >> 16));
+    a[0] = __fmul_rn(__fmul_rn(d0, dx), (float)c[0]);
+    a[1] = __fmul_rn(__fmul_rn(d1, dx), (float)c[1]);
+    b[0] = b[1] = 0.0f;
+  } else if constexpr (WT == B2_Q4_K) {
+    const uint4 m0 = lds128(sl + 1024 + 32 * q), m1 = lds128(sl + 1024 + 32 * q + 16);   // rows 2q, 2q+1
+    uint32_t sl0, ml0, sh0, mh0, sl1, ml1, sh1, mh1;
+    q4k_scales(m0.y, m0.z, m0.w, sl0, ml0, sh0, mh0);
+    q4k_scales(m1.y, m1.z, m1.w, sl1, ml1, sh1, mh1);
+    const uint8_t* qrow = sl + 128 * g;          // B column g = weight row g of the tile
+    const uint8_t* xu = xr + u * 256;
+    int is0 = 0, is1 = 0;
+#pragma unroll
+    for (int jc = 0; jc < 4; ++jc) {
+      const uint32_t w0 = lds32(qrow + 16 * ((2 * jc + g) & 7) + 4 * q);
+      const uint32_t w1 = lds32(qrow + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * jc + h;                 // 32-weight group
+        const uint32_t a0 = live ? lds32(xu + 32 * j + 4 * q) : 0u;
+        const uint32_t a2 = live ? lds32(xu + 32 * j + 16 + 4 * q) : 0u;
+        int c[4];
+        if (h == 0) mma_k32_s8u8(c, a0, a2, w0 & kM4, w1 & kM4);
+        else mma_k32_s8u8(c, a0, a2, (w0 >> 4) & kM4, (w1 >> 4) & kM4);
+        is0 += (j < 4 ? ubyte(sl0, j) : ubyte(sh0, j - 4)) * c[0];
+        is1 += (j < 4 ? ubyte(sl1, j) : ubyte(sh1, j - 4)) * c[1];
+      }
+    }
+    const uint4 bq = live ? lds128(reinterpret_cast<const uint8_t*>(bss + (g * p.nu + u) * 8)) : make_uint4(0, 0, 0, 0);
+    const int ms0 = q4k_msum(bq, ml0, mh0), ms1 = q4k_msum(bq, ml1, mh1);
+    const float dd0 = h2f((uint16_t)(m0.x & 0xFFFFu)), dm0 = h2f((uint16_t)(m0.x >> 16));
+    const float dd1 = h2f((uint16_t)(m1.x & 0xFFFFu)), dm1 = h2f((uint16_t)(m1.x >> 16));
+    a[0] = __fmul_rn(__fmul_rn(dd0, dx), (float)is0);
+    b[0] = __fmul_rn(__fmul_rn(dm0, dx), (float)ms0);
+    a[1] = __fmul_rn(__fmul_rn(dd1, dx), (float)is1);
+    b[1] = __fmul_rn(__fmul_rn(dm1, dx), (float)ms1);
+  } else {  // Q6_K: 16 groups of 16 weights, m16n8k16
+    const uint8_t* qlr = sl + 128 * g;
+    const uint8_t* qhr = sl + 1024 + 64 * g;
+    const uint4 sc0 = lds128(sl + 1536 + 32 * q), sc1 = lds128(sl + 1536 + 32 * q + 16);   // rows 2q, 2q+1
+    const uint32_t sw0[4] = {sc0.x, sc0.y, sc0.z, sc0.w}, sw1[4] = {sc1.x, sc1.y, sc1.z, sc1.w};
+    const int16_t* bs = bss + (g * p.nu + u) * 16;
+    const uint8_t* xu = xr + u * 256;
+    int is0 = 0, is1 = 0;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint32_t hw = lds32(qhr + 16 * ((2 * hh + hf + g) & 3) + 4 * q);
+#pragma unroll
+        for (int a1 = 0; a1 < 2; ++a1) {
+          const uint32_t lw = lds32(qlr + 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q);
+#pragma unroll
+          for (int nh = 0; nh < 2; ++nh) {
+            const int aq = a1 + 2 * nh;          // quartile of the half
+            const int i = hh * 8 + aq * 2 + hf;  // 16-weight group of the super-block
+            const uint32_t v = (nh ? (lw >> 4) & kM4 : lw & kM4) | (((hw >> (2 * aq)) & 0x03030303u) << 4);
+            const uint32_t a0 = live ? lds32(xu + 16 * i + 4 * q) : 0u;
+            int c[4];
+            mma_k16_s8u8(c, a0, v);
+            const int o = live ? 32 * (int)bs[i] : 0;
+            is0 += sbyte(sw0[i >> 2], i & 3) * (c[0] - o);
+            is1 += sbyte(sw1[i >> 2], i & 3) * (c[1] - o);
+          }
+        }
+      }
+    }
+    const uint32_t dw2 = lds32(sl + 1664 + 4 * q);
+    a[0] = __fmul_rn(__fmul_rn(h2f((uint16_t)(dw2 & 0xFFFFu)), dx), (float)is0);
+    a[1] = __fmul_rn(__fmul_rn(h2f((uint16_t)(dw2 >> 16)), dx), (float)is1);
+    b[0] = b[1] = 0.0f;
   }
 }
 
@@ -514,11 +446,10 @@ __device__ __forceinline__ void store_y(const GemvP& p, float* y, int t, int64_t
   *yp = p.epilogue == EPI_ACCUM ? __fadd_rn(*yp, v) : v;
 }
 
-// After every consumer thread of the CTA has stored (a CTA barrier): count
-// the CTA; the last CTA of the grid publishes the next epoch to every rank's
-// flag.  Stores reach peers before the count (the barrier, then this
-// thread's fence.sys), and the count before the flags (fence.sys in the last
-// CTA).
+// After every thread of the CTA has stored (a CTA barrier): count the CTA;
+// the last CTA of the grid publishes the next epoch to every rank's flag.
+// Stores reach peers before the count (the barrier, then this thread's
+// fence.sys), and the count before the flags (fence.sys in the last CTA).
 __device__ __forceinline__ void signal_peers(const GemvP& p) {
   __threadfence_system();
   const unsigned int prev = atomicAdd(p.peer.done, 1u);
@@ -531,18 +462,6 @@ __device__ __forceinline__ void signal_peers(const GemvP& p) {
   }
 }
 
-// Sum of the S range partials of output e, ranges added in order.  red
-// holds S blocks of `stride` floats (block r: range r).
-__device__ __forceinline__ float range_total(const float* red, int S, int stride, int e) {
-  float v = red[e];
-  for (int r = 1; r < S; ++r) v = __fadd_rn(v, red[r * stride + e]);
-  return v;
-}
-
-// Writes the outputs of `nt` consecutive 8-row tiles starting at tile t0 from
-// red (S blocks of nt*64 floats, element e = token*(8*nt) + tile_row), one
-// warp: store / residual add / peer store, or SwiGLU over (gate, up) row
-// pairs of a tile.
 // The fused QKV epilogue for one (token, row pair): see RopeKvEpi.
 __device__ __forceinline__ void rope_kv_store(const RopeKvEpi& e, int t, int64_t row, float x0, float x1) {
   const int s = e.seq[t], ps = e.pos[t];
@@ -576,166 +495,85 @@ __device__ __forceinline__ void rope_kv_store(const RopeKvEpi& e, int t, int64_t
   }
 }
 
-template <int NT>
-__device__ __forceinline__ void finish_tiles(const GemvP& p, const float* red, int64_t t0, int lane, float* y) {
-  constexpr int R = 8 * NT;   // rows per item
+// Epilogue of one (token, row pair) (rows r0 = 2f and r0 + 1 of the
+// output; for SwiGLU the pair is (gate_f, up_f)).
+__device__ __forceinline__ void emit_pair(const GemvP& p, float* y, int t, int64_t r0, float v0, float v1) {
   if (p.epilogue == EPI_ROPE_KV) {
-    // R/2 row pairs x 8 tokens
-#pragma unroll
-    for (int k = 0; k < (R / 2 * 8 + 31) / 32; ++k) {
-      const int e = lane + 32 * k;
-      if (e >= R / 2 * 8) break;
-      const int t = e / (R / 2), f = e % (R / 2);
-      const int64_t row = t0 * 8 + 2 * f;
-      if (t < p.n_tok && row < p.n_rows)
-        rope_kv_store(p.rope, t, row, range_total(red, p.S, R * 8, t * R + 2 * f),
-                      range_total(red, p.S, R * 8, t * R + 2 * f + 1));
-    }
-    return;
-  }
-  if (p.epilogue == EPI_SWIGLU) {
-    // R/2 features x 8 tokens: feature f = rows (2f, 2f+1)
-#pragma unroll
-    for (int k = 0; k < (R / 2 * 8 + 31) / 32; ++k) {
-      const int e = lane + 32 * k;
-      if (e >= R / 2 * 8) break;
-      const int t = e / (R / 2), f = e % (R / 2);
-      const int64_t row = t0 * 8 + 2 * f;
-      if (t < p.n_tok && row < p.n_rows) {
-        const float gs = range_total(red, p.S, R * 8, t * R + 2 * f);
-        const float us = range_total(red, p.S, R * 8, t * R + 2 * f + 1);
-        p.y[t * p.y_stride + row / 2] = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, b2_expf(-gs))), us);
-      }
-    }
-    return;
-  }
-#pragma unroll
-  for (int k = 0; k < R * 8 / 32; ++k) {
-    const int e = lane + 32 * k;
-    const int t = e / R, rr = e % R;
-    const int64_t row = t0 * 8 + rr;
-    if (t < p.n_tok && row < p.n_rows) store_y(p, y, t, row, range_total(red, p.S, R * 8, e));
+    if (r0 < p.n_rows) rope_kv_store(p.rope, t, r0, v0, v1);
+  } else if (p.epilogue == EPI_SWIGLU) {
+    if (r0 < p.n_rows) y[t * p.y_stride + r0 / 2] = silu_mul_ref(v0, v1);
+  } else {
+    if (r0 < p.n_rows) store_y(p, y, t, r0, v0);
+    if (r0 + 1 < p.n_rows) store_y(p, y, t, r0 + 1, v1);
   }
 }
 
-// MODE 0 (3..8 tokens, int8 mma.sync, weight rows as the M dimension): items
-// are tile pairs (16 rows).  The 16 consumer warps form NSET = 16/S sets of S
-// warps; set j works items j, j + NSET, ... of the CTA's run, warp r of a set
-// one unit range of the pair for all four residues.  A stage holds one item's
-// next U units of all ranges, so the sets consume the ring concurrently.
-// MODES 1, 2 (dp4a over 1-2 tokens): items are P = 8/S tiles; all 8 consumer
-// warps (tile w/S, range w%S) work every stage.
-template <int WT, int MODE>
-__global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const GemvP p) {
-  constexpr int NW = ncw_for(MODE);        // consumer warps
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kMaxStages;
-  uint64_t* act_bar = empty + kMaxStages;
-  uint8_t* ring = smem + kBarBytes;
-  uint8_t* act = ring + (size_t)p.n_stages * p.stage_bytes;
-  // mma: [iteration parity][set][range][token*16 + pair row]; dp4a: [group parity][tile slot][range][token*8 + row]
-  __shared__ float red[2][kMaxNCW * 128];
+// The warp's stage sequence: tile i of its list (tile t0 + warp + i*NW of the
+// CTA's run [t0, t1)), chunk ch of n_ch, in ring slot l % n_stages.
+struct WarpStream {
+  int64_t t0, t1, tile;    // next tile to issue
+  int ch;                  // next chunk of that tile to issue
+  int64_t issued;          // stages issued so far
+};
 
+__device__ __forceinline__ void issue_stage(const GemvP& p, WarpStream& ws, int nw, uint8_t* ring, uint64_t* full) {
+  const int s = (int)(ws.issued % p.n_stages);
+  const int64_t mi = p.n_mat > 1 ? ws.tile / p.tpm : 0;
+  const int64_t tl = ws.tile - mi * p.tpm;
+  const int u0 = ws.ch * p.U;
+  const uint32_t bytes = (uint32_t)min(p.U, p.nu - u0) * (uint32_t)p.slot_bytes;
+  mbar_arrive_expect_tx(&full[s], bytes);
+  bulk_g2s(ring + (size_t)s * p.stage_bytes, p.wl[mi] + tl * p.tile_bytes + (int64_t)u0 * p.slot_bytes, bytes,
+           &full[s]);
+  ++ws.issued;
+  if (++ws.ch == p.n_ch) {
+    ws.ch = 0;
+    ws.tile += nw;
+  }
+}
+
+// MODE 0: 3..8 tokens on int8 mma.sync; MODES 1, 2: dp4a over 1 or 2 tokens.
+template <int WT, int MODE>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ns = p.n_stages;
-  const int S = p.S;
-  const int P = MODE == 0 ? 2 : 8 / S;   // tiles per item
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < ns; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], MODE == 0 ? S : NW);
-    }
-    mbar_init(act_bar, 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * kMaxStages;
+  uint64_t* act_bar = reinterpret_cast<uint64_t*>(smem) + kMaxWarps * kMaxStages;
+  uint8_t* act = smem + kHdrBytes;
+  uint8_t* ring = act + p.act_region + (size_t)warp * p.n_stages * p.stage_bytes;
+
+  if (lane == 0) {
+    for (int s = 0; s < p.n_stages; ++s) mbar_init(&full[s], 1);
+    if (warp == 0) mbar_init(act_bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  // Items of this CTA (contiguous, balanced) and the stage sequence.  The
-  // consumer sets (MODE 0: NSET sets; dp4a: one) each own a ring of nss =
-  // ns/NSET consecutive slots and take their stages in order, so a set never
-  // waits on a slot whose previous use (by the same set) is still in flight.
-  // Set j works items j, j + NSET, ...; its local stage l is chunk l % n_ch of
-  // its item l / n_ch and lives in slot j*nss + l % nss.
-  const int64_t n_items = p.ipm * p.n_mat;
-  const int64_t g0 = n_items * blockIdx.x / gridDim.x, g1 = n_items * (blockIdx.x + 1) / gridDim.x;
-  const int n_ch = (p.L + p.U - 1) / p.U;   // stages per item
-  const int nset = MODE == 0 ? min(NW / S, 8) : 1;
-  const int nss = ns / nset;
-  const uint32_t piece = (uint32_t)p.U * S * p.slot_bytes;   // one tile's part of a stage
+  // This CTA's tiles (contiguous, balanced); this warp's: every nw-th.
+  const int64_t n_tiles = p.tpm * p.n_mat;
+  WarpStream ws;
+  ws.t0 = n_tiles * blockIdx.x / gridDim.x;
+  ws.t1 = n_tiles * (blockIdx.x + 1) / gridDim.x;
+  ws.tile = ws.t0 + warp;
+  ws.ch = 0;
+  ws.issued = 0;
+  const int64_t my_tiles = ws.tile < ws.t1 ? (ws.t1 - ws.tile + nw - 1) / nw : 0;
+  const int64_t n_stages_total = my_tiles * p.n_ch;
+  // Weights do not depend on the previous kernel: fill the ring now.
+  if (lane == 0)
+    while (ws.issued < n_stages_total && ws.issued < p.n_stages) issue_stage(p, ws, nw, ring, full);
+  __syncwarp();
 
-  if (warp == NW) {
-    // ---------------- producer ----------------
-    // Stages go out round-robin over the sets by local stage; the first nss
-    // of every set need no free slot.  Once those are out and the previous
-    // kernel (the activation quantizer) has finished, the image.
-    if (lane == 0) {
-      const int64_t items_here = g1 - g0;
-      const int64_t max_local = ((items_here + nset - 1) / nset) * n_ch;
-      bool act_sent = p.act_img == nullptr;
-      // l = blk * n_ch + ch = use * nss + ring_pos, kept as counters: one
-      // thread issues every stage, so no division (64-bit ones are long
-      // software sequences) sits between a freed slot and its refill.
-      int64_t blk = 0, use = 0;
-      int ch = 0, ring_pos = 0;
-      int64_t mi = p.n_mat > 1 ? g0 / p.ipm : 0;   // matrix cursor (several matrices: one set, items ascend)
-      for (int64_t l = 0; l < max_local; ++l) {
-        if (l == nss && !act_sent) {
-          pdl_wait();
-          mbar_arrive_expect_tx(act_bar, p.act_bytes);
-          bulk_g2s(act, p.act_img, p.act_bytes, act_bar);
-          act_sent = true;
-        }
-        for (int j = 0; j < nset; ++j) {
-          const int64_t i = j + (int64_t)nset * blk;   // item index within the CTA's run
-          if (i >= items_here) continue;
-          const int sl = j * nss + ring_pos;
-          if (use > 0 && !mbar_wait_bounded(&empty[sl], (uint32_t)((use - 1) & 1), p.status, 2)) return;
-          const int64_t gitem = g0 + i;
-          while (p.n_mat > 1 && (mi + 1) * p.ipm <= gitem) ++mi;
-          const int64_t item = gitem - mi * p.ipm;   // item within matrix mi
-          const uint8_t* wm = p.wl[mi];
-          const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
-          const uint32_t bytes = (uint32_t)ni * S * p.slot_bytes;
-          uint32_t tx = 0;
-          for (int pp = 0; pp < P; ++pp)
-            if (item * P + pp < p.n_tiles) tx += bytes;
-          mbar_arrive_expect_tx(&full[sl], tx);
-          uint8_t* sp = ring + (size_t)sl * p.stage_bytes;
-          if (ni == p.L && tx == (uint32_t)P * bytes) {
-            // whole tiles, all live: the P tiles are adjacent in memory, one copy
-            bulk_g2s(sp, wm + item * P * p.tile_bytes, tx, &full[sl]);
-            continue;
-          }
-          for (int pp = 0; pp < P; ++pp) {
-            const int64_t tile = item * P + pp;
-            if (tile < p.n_tiles)
-              bulk_g2s(sp + pp * piece, wm + tile * p.tile_bytes + (int64_t)i0 * S * p.slot_bytes, bytes, &full[sl]);
-          }
-        }
-        if (++ch == n_ch) {
-          ch = 0;
-          ++blk;
-        }
-        if (++ring_pos == nss) {
-          ring_pos = 0;
-          ++use;
-        }
-      }
-      if (!act_sent) {
-        pdl_wait();
-        mbar_arrive_expect_tx(act_bar, p.act_bytes);
-        bulk_g2s(act, p.act_img, p.act_bytes, act_bar);
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
+  // Activations: after the grid dependency resolves.
   pdl_wait();
   bool ok = true;
   if (p.act_img) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(act_bar, p.act_bytes);
+      bulk_g2s(act, p.act_img, p.act_bytes, act_bar);
+    }
     ok = mbar_wait_bounded(act_bar, 0, p.status, 3);
   } else {
     ActImage ai;
@@ -743,122 +581,116 @@ __global__ void __launch_bounds__((ncw_for(MODE) + 1) * 32, 1) gemv_kernel(const
     ai.kq = p.kq;
     ai.nu = p.nu;
     ai.type = p.type;
-    ai.n_act_tok = p.n_act_tok;
-    ai.mma = MODE == 0;
+    ai.n_act_tok = p.n_tok;
     ai.off_dx = p.off_dx;
     ai.off_bs = p.off_bs;
-    quantize_image(p.x, p.x_stride, p.n_tok, ai, warp * 32 + lane, NW * 32);
-    consumer_sync(NW * 32);
+    quantize_image(p.x, p.x_stride, p.n_tok, ai, threadIdx.x, blockDim.x);
+    __syncthreads();
   }
-  const size_t us = (size_t)S * p.slot_bytes;   // slot stride between consecutive units of a range
 
-  if constexpr (MODE == 0) {
-    const int set = warp / S, r = warp % S;
-    const int g = lane >> 2, q = lane & 3;      // D rows g, g+8; tokens 2q, 2q+1
-    int it = 0;
-    int ring_pos = 0;      // this set's local stage modulo nss, and its ring pass parity
-    uint32_t ph = 0;
-    // (with S = 1 only the first 8 of the 16 warps form sets; the rest idle)
-    for (int64_t i = set; set < nset && g0 + i < g1; i += nset, ++it) {
-      const int64_t item = g0 + i;
-      float acc[4][4];   // [unit residue][output]
-#pragma unroll
-      for (int a = 0; a < 4; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.0f;
-      for (int ch = 0; ch < n_ch; ++ch) {
-        const int s = set * nss + ring_pos;   // local stage it*n_ch + ch of this set
-        if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
-        if (++ring_pos == nss) {
-          ring_pos = 0;
-          ph ^= 1u;
-        }
-        const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
-        const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);   // units of this stage in range r
+  int64_t consumed = 0;
+  for (int64_t it = 0; it < my_tiles; ++it) {
+    const int64_t tile = ws.t0 + warp + it * nw;
+    const int64_t mi = p.n_mat > 1 ? tile / p.tpm : 0;
+    const int64_t tl = tile - mi * p.tpm;
+    float* y = p.yl[mi];
+    if constexpr (MODE == 0) {
+      const int g = lane >> 2, q = lane & 3;   // token g, rows 2q and 2q+1
+      const bool live = g < p.n_tok;
+      float acc[2] = {0.0f, 0.0f};
+      for (int ch = 0; ch < p.n_ch; ++ch, ++consumed) {
+        const int s = (int)(consumed % p.n_stages);
+        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1);
         if (ok) {
-          const uint8_t* sa = ring + (size_t)s * p.stage_bytes + (size_t)r * p.slot_bytes;
-          const uint8_t* sb = sa + piece;
-          for (int u4 = ua & ~3; u4 < ub; u4 += 4) {
-#pragma unroll
-            for (int a = 0; a < 4; ++a) {
-              const int u = u4 + a;
-              if (u >= ua && u < ub) mma2_unit<WT>(p, sa + (u - ua) * us, sb + (u - ua) * us, act, u, g, q, acc[a]);
+          const uint8_t* st = ring + (size_t)s * p.stage_bytes;
+          const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
+          for (int u = u0; u < u1; ++u) {
+            float a[2], b[2];
+            mma_terms<WT>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, q, live, a, b);
+            acc[0] = __fadd_rn(acc[0], a[0]);
+            acc[1] = __fadd_rn(acc[1], a[1]);
+            if constexpr (WT == B2_Q4_K) {
+              acc[0] = __fsub_rn(acc[0], b[0]);
+              acc[1] = __fsub_rn(acc[1], b[1]);
             }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-      }
-      // range partial (a0 + a1) + (a2 + a3) into red[it&1][set][r][token*16 + row]
-      float* rw = red[it & 1] + (set * S + r) * 128;
-#pragma unroll
-      for (int o = 0; o < 4; ++o) {
-        const float v = __fadd_rn(__fadd_rn(acc[0][o], acc[1][o]), __fadd_rn(acc[2][o], acc[3][o]));
-        rw[(2 * q + (o & 1)) * 16 + g + 8 * (o >> 1)] = v;
-      }
-      if (S > 1) tile_sync(set, S * 32);
-      else __syncwarp();
-      if (r == 0 && ok) finish_tiles<2>(p, red[it & 1] + set * S * 128, item * 2, lane, p.y);
-    }
-  } else {
-    const int slot_p = warp / S, r = warp % S;
-    const int dg = lane & 7, dq = lane >> 3;    // tile row dg, unit residue dq
-    constexpr int NB = MODE;
-    float dacc[NB];    // partial sums [token] of residue dq
-    int ring_pos = 0;      // stage counter modulo ns, and the ring pass parity
-    uint32_t ph = 0;
-    int64_t mi = p.n_mat > 1 ? g0 / p.ipm : 0;   // matrix cursor
-    for (int64_t grp = g0; grp < g1; ++grp) {
-      while (p.n_mat > 1 && (mi + 1) * p.ipm <= grp) ++mi;
-      const int64_t tile = (grp - mi * p.ipm) * P + slot_p;
-      const bool live = tile < p.n_tiles;
-#pragma unroll
-      for (int t = 0; t < NB; ++t) dacc[t] = 0.0f;
-      for (int ch = 0; ch < n_ch; ++ch) {
-        const int s = ring_pos;
-        if (ok) ok = mbar_wait_bounded(&full[s], ph, p.status, 1);
-        if (++ring_pos == ns) {
-          ring_pos = 0;
-          ph ^= 1u;
+        if (lane == 0 && ok && ws.issued < n_stages_total) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_stage(p, ws, nw, ring, full);
         }
-        const int i0 = ch * p.U, ni = min(p.U, p.L - i0);
-        if (ok && live) {
-          const uint8_t* rbase = ring + (size_t)s * p.stage_bytes + slot_p * piece + (size_t)r * p.slot_bytes;
-          // this stage holds units [ua, ub) of the warp's range; the four lane
-          // groups take four consecutive units (residues 0..3) at once
-          const int ua = r * p.L + i0, ub = min(ua + ni, p.nu);
-#pragma unroll 4
-          for (int u4 = ua & ~3; u4 < ub; u4 += 4) {
-            const int u = u4 + dq;
-            if (u >= ua && u < ub) dp4a_unit<WT, NB>(p, rbase + (size_t)(u - ua) * us, act, u, dg, dacc);
+      }
+      if (ok && live) emit_pair(p, y, g, tl * 8 + 2 * q, acc[0], acc[1]);
+    } else {
+      constexpr int NB = MODE;
+      const int g = lane & 7, j = lane >> 3;   // tile row g, unit residue j
+      float acc[NB];
+#pragma unroll
+      for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
+      for (int ch = 0; ch < p.n_ch; ++ch, ++consumed) {
+        const int s = (int)(consumed % p.n_stages);
+        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1);
+        if (ok) {
+          const uint8_t* st = ring + (size_t)s * p.stage_bytes;
+          const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
+          for (int u4 = u0; u4 < u1; u4 += 4) {
+            const int u = u4 + j;
+            float pa[NB], pb[NB];
+            if (u < u1) {
+              dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa, pb);
+            } else {
+#pragma unroll
+              for (int t = 0; t < NB; ++t) pa[t] = pb[t] = 0.0f;
+            }
+            // the row's units u4, u4+1, ... in order, from lanes g, g+8, ...
+            const int n_in = min(4, u1 - u4);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              if (jj < n_in) {
+#pragma unroll
+                for (int t = 0; t < NB; ++t) {
+                  acc[t] = __fadd_rn(acc[t], __shfl_sync(0xffffffffu, pa[t], g + 8 * jj));
+                  if constexpr (WT == B2_Q4_K) acc[t] = __fsub_rn(acc[t], __shfl_sync(0xffffffffu, pb[t], g + 8 * jj));
+                }
+              }
+            }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0 && ok && ws.issued < n_stages_total) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_stage(p, ws, nw, ring, full);
+        }
       }
-      // (a0 + a1) + (a2 + a3): residues dq and dq^1 are 8 lanes apart, dq and dq^2 16
-      float* rw = red[grp & 1] + (slot_p * S + r) * 64;
+      float other[NB];
 #pragma unroll
-      for (int t = 0; t < NB; ++t) {
-        float v = __fadd_rn(dacc[t], __shfl_xor_sync(0xffffffffu, dacc[t], 8));
-        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 16));
-        if (dq == 0) rw[t * 8 + dg] = v;
+      for (int t = 0; t < NB; ++t) other[t] = __shfl_xor_sync(0xffffffffu, acc[t], 1);   // row g ^ 1
+      if (ok && j < NB) {
+        const int64_t row = tl * 8 + g;
+        if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
+          if ((g & 1) == 0) emit_pair(p, y, j, row, acc[j], other[j]);
+        } else if (row < p.n_rows) {
+          store_y(p, y, j, row, acc[j]);
+        }
       }
-      if (S > 1) tile_sync(slot_p, S * 32);
-      else __syncwarp();
-      if (r == 0 && live && ok) finish_tiles<1>(p, red[grp & 1] + slot_p * S * 64, tile, lane, p.yl[mi]);
     }
   }
+  // A warp that stopped early waits (bounded) for the copies it still has in flight.
+  if (!ok && lane == 0) {
+    for (int64_t l = consumed; l < ws.issued; ++l)
+      mbar_wait_bounded(&full[l % p.n_stages], (uint32_t)((l / p.n_stages) & 1), nullptr, 0);
+  }
   if (p.peer.n) {
-    // Every consumer thread's peer stores are ordered before the CTA barrier;
-    // the signalling thread's system-scope fence after it makes them all
-    // visible before the count (the grid-barrier pattern: barrier, then one
-    // thread's fence and atomic).
-    consumer_sync(NW * 32);
-    if (warp == 0 && lane == 0) signal_peers(p);
+    // Every thread's peer stores are ordered before the CTA barrier; the
+    // signalling thread's system-scope fence after it makes them all visible
+    // before the count (the grid-barrier pattern).
+    __syncthreads();
+    if (threadIdx.x == 0) signal_peers(p);
   }
 }
 
-// 227 KB opt-in per block, less the kernel's static shared memory.
-constexpr int kSmemCap = 227 * 1024 - (int)sizeof(float) * 2 * kMaxNCW * 128 - 1024;
+constexpr int kSmemCap = 227 * 1024;
 
 template <int WT, int MODE>
 int set_attr() {
@@ -875,10 +707,10 @@ int set_attr_all() {
 }
 
 template <int WT, int MODE>
-int launch_t(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
+int launch_t(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3((ncw_for(MODE) + 1) * 32);
+  cfg.blockDim = dim3(nw * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -891,15 +723,15 @@ int launch_t(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
 }
 
 template <int WT>
-int launch_w(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
-  if (p.n_tok > kDp4aMaxTok) return launch_t<WT, 0>(p, grid, smem, s);
-  if (p.n_tok == 1) return launch_t<WT, 1>(p, grid, smem, s);
-  return launch_t<WT, 2>(p, grid, smem, s);
+int launch_w(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
+  if (p.n_tok > kDp4aMaxTok) return launch_t<WT, 0>(p, grid, nw, smem, s);
+  if (p.n_tok == 1) return launch_t<WT, 1>(p, grid, nw, smem, s);
+  return launch_t<WT, 2>(p, grid, nw, smem, s);
 }
 
 int launch_quantize_image(const float* x, int64_t x_stride, int n_tok, const ActImage& g, cudaStream_t s) {
   const bool k_quant = g.type == B2_Q4_K || g.type == B2_Q6_K;
-  const int64_t work = (int64_t)g.n_act_tok * g.nu * (k_quant ? 32 : 1);   // threads wanted
+  const int64_t work = (int64_t)n_tok * g.nu * (k_quant ? 32 : 1);   // threads wanted
   const int block = 256;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + block - 1) / block, 4 * sm_count()));
   cudaLaunchConfig_t cfg = {};
@@ -915,21 +747,25 @@ int launch_quantize_image(const float* x, int64_t x_stride, int n_tok, const Act
   return B2_OK;
 }
 
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
 }  // namespace
 
-// Carve-up of the activation image for w at n_tok tokens.
+// Carve-up of the activation image for w at n_tok tokens: codes [n_tok][kq]
+// in natural order (kq = k rounded up to 128, plus 16 bytes so that the
+// token rows of one mma fragment load fall on different banks), fp32 unit
+// scales [n_tok][nu], int16 block sums [n_tok][nu][nb].
 ActImage gemv_act_image(const QMatrix& w, int n_tok, uint8_t* img) {
   ActImage g;
   g.img = img;
   g.type = w.type;
   g.nu = w.nu;
-  g.mma = n_tok > kDp4aMaxTok;
-  g.n_act_tok = g.mma ? kMaxTok : n_tok;
-  g.kq = (int)((w.k + 127) / 128 * 128);
+  g.n_act_tok = n_tok;
+  g.kq = (int)((w.k + 127) / 128 * 128 + 16);
   const int bs_per_unit = w.type == B2_Q4_0 ? 1 : w.type == B2_Q4_K ? 8 : w.type == B2_Q6_K ? 16 : 0;
-  const size_t qs_b = (size_t)g.n_act_tok * g.kq;
-  const size_t dx_b = ((size_t)g.n_act_tok * w.nu * 4 + 15) / 16 * 16;
-  const size_t bs_b = ((size_t)g.n_act_tok * w.nu * bs_per_unit * 2 + 15) / 16 * 16;
+  const size_t qs_b = (size_t)n_tok * g.kq;
+  const size_t dx_b = align_up((size_t)n_tok * w.nu * 4, 16);
+  const size_t bs_b = align_up((size_t)n_tok * w.nu * bs_per_unit * 2, 16);
   g.off_dx = (uint32_t)qs_b;
   g.off_bs = (uint32_t)(qs_b + dx_b);
   g.bytes = (uint32_t)(qs_b + dx_b + bs_b);
@@ -962,7 +798,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   B2_CHECK_ARG(a.n_tok >= 1 && a.n_tok <= kMaxTok, "n_tok must be in [1, 8]");
   B2_CHECK_ARG(a.image_ready || a.x != nullptr, "x");
   B2_CHECK_ARG(a.epilogue == EPI_ROPE_KV ? a.rope != nullptr : a.y != nullptr, "outputs");
-  B2_CHECK_ARG(w.data != nullptr && w.nu > 0, "matrix");
+  B2_CHECK_ARG(w.data != nullptr && w.nu > 0 && w.splits == 1, "matrix");
   B2_CHECK_ARG(a.epilogue != EPI_SWIGLU || (w.n_rows % 2) == 0, "SwiGLU needs (gate, up) row pairs");
   B2_CHECK_ARG(a.image_ready || ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride % 4) == 0),
                "x must be 16-byte aligned with a stride of whole float4s");
@@ -976,7 +812,6 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
                  "RoPE/KV epilogue arguments");
   }
   GemvP p = {};
-  p.w = w.data;
   p.n_mat = a.n_mat;
   if (a.n_mat == 1) {
     p.wl[0] = w.data;
@@ -995,18 +830,14 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   }
   p.type = w.type;
   p.nu = w.nu;
-  p.S = w.splits;
-  p.L = w.ulen;
   p.slot_bytes = w.slot_bytes;
   p.tile_bytes = w.tile_bytes;
   p.n_rows = w.n_rows;
   p.n_tiles = w.n_tiles;
   p.k = w.k;
   p.n_tok = a.n_tok;
-  p.n_act_tok = a.n_tok > kDp4aMaxTok ? kMaxTok : a.n_tok;
   p.x = a.x;
   p.x_stride = a.x_stride;
-  p.y = a.y;
   p.y_stride = a.y_stride;
   p.epilogue = a.epilogue;
   p.status = a.status;
@@ -1022,69 +853,60 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.off_dx = ag.off_dx;
   p.off_bs = ag.off_bs;
   p.act_bytes = ag.bytes;
+  p.act_region = (uint32_t)align_up(ag.bytes, 128);
   // Small activations are quantized by each CTA itself (no extra kernel and
   // no dependency on a shared image between consecutive launches); large ones
   // once, into the image every CTA copies.
   const bool in_kernel = !a.image_ready && !gemv_needs_image(w, a.n_tok);
   p.act_img = in_kernel ? nullptr : a.act_img;
   if (a.epilogue == EPI_ROPE_KV) p.rope = *a.rope;
-  // Stages of P tiles x U unit steps of all S ranges.  mma: one tile pair per
-  // stage, U as large as fits (up to whole tiles: then the stage is one bulk
-  // copy of up to ~128 KB).  An SM's bulk copies are served at a near-fixed
-  // rate of copies, not bytes, so few large copies stream fastest: measured
-  // on the 8B shapes, whole-tile stages with one slot per consumer set beat
-  // ~18 KB stages with two slots per set (gate/up 26.3 -> 23.1 us, head 161
-  // -> 133 us).  Where whole tiles do not fit, the largest U that gives every
-  // set a slot.  dp4a: P = 8/S tiles, ~32 KB.  With small activations stay
-  // within ~100 KB when that still gives the pipeline it needs, so that two
-  // CTAs fit on an SM and the next launch's producer can stream while this
-  // one drains.
-  const bool mma = a.n_tok > kDp4aMaxTok;
-  const int P = mma ? 2 : 8 / w.splits;
-  const int nset = mma ? std::min(16 / w.splits, 8) : 1;
-  const size_t step_b = (size_t)P * w.splits * w.slot_bytes;
-  const size_t fixed = kBarBytes + p.act_bytes;
-  int U = 0, ns = 0;
-  size_t stage = 0;
-  auto fit = [&](size_t cap_, int want_per_set) -> bool {
-    for (int u = std::min<int>(w.ulen, (int)std::max<size_t>(1, (mma ? 128 * 1024 : 32 * 1024) / step_b)); u >= 1;
-         --u) {
-      const size_t st = step_b * u;
-      if (fixed + st > cap_) continue;
-      int n = (int)std::min<size_t>(kMaxStages, (cap_ - fixed) / st);
-      n = n / nset * nset;
-      if (n >= want_per_set * nset) {
-        U = u;
-        ns = n;
-        stage = st;
-        return true;
-      }
-    }
-    return false;
-  };
-  // (A multi-matrix launch streams long enough that the deepest ring wins.)
-  const bool ok_fit = (in_kernel && a.n_mat == 1 && fit(100 * 1024, mma ? 2 : 3)) ||
-                      (mma && fit((size_t)kSmemCap, 1)) || fit((size_t)kSmemCap, 2) || fit((size_t)kSmemCap, 1);
-  if (!ok_fit) {
+  // Geometry.  One CTA per SM over a contiguous run of tiles; as many warps
+  // as the run has tiles (up to 8), so every warp streams and folds its own.
+  // Each warp's ring gets an equal share of the shared memory left after the
+  // activations: with small activations about 110 KB in all, so that two
+  // CTAs fit on an SM and the next launch's weights stream while this one
+  // finishes.  A stage is as many unit slots as fit half the share (the
+  // whole tile when it fits the share: one bulk copy per tile).
+  p.tpm = w.n_tiles;
+  const int64_t n_tiles = p.tpm * p.n_mat;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), n_tiles));
+  const int64_t per_cta = (n_tiles + grid - 1) / grid;
+  const int nw = (int)std::max<int64_t>(1, std::min<int64_t>(8, per_cta));
+  const size_t cap = in_kernel && a.n_mat == 1 ? (size_t)110 * 1024 : (size_t)kSmemCap;
+  const size_t fixed = kHdrBytes + p.act_region;
+  if (fixed + (size_t)nw * w.slot_bytes > cap) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
   }
+  const size_t share = (cap - fixed) / nw;
+  const bool dp4a = a.n_tok <= kDp4aMaxTok;
+  const int64_t tiles_per_warp = (per_cta + nw - 1) / nw;
+  int U;
+  if ((size_t)w.tile_bytes <= share && (tiles_per_warp <= 1 || (size_t)w.tile_bytes * 2 <= share)) {
+    U = w.nu;   // whole tiles
+  } else {
+    U = (int)std::max<size_t>(1, std::min<size_t>(w.nu, share / 2 / w.slot_bytes));
+    if (dp4a && U < w.nu) U = std::max(4, U / 4 * 4);   // the dp4a fold takes units four at a time
+  }
+  const size_t stage = (size_t)U * w.slot_bytes;
+  if (stage > share) {
+    set_error("gemv: no stage of unit slots fits for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
+    return B2_ERR_UNSUPPORTED;
+  }
   p.U = U;
-  p.n_stages = ns;
+  p.n_ch = (w.nu + U - 1) / U;
+  p.n_stages = (int)std::max<size_t>(1, std::min<size_t>(kMaxStages, share / stage));
   p.stage_bytes = (uint32_t)stage;
-  const size_t smem = fixed + (size_t)ns * stage;
-  p.ipm = (w.n_tiles + P - 1) / P;
-  const int64_t items = p.ipm * p.n_mat;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), items));
+  const size_t smem = fixed + (size_t)nw * p.n_stages * stage;
   if (!in_kernel && !a.image_ready) {
     const int qrc = launch_quantize_image(a.x, a.x_stride, a.n_tok, ag, s);
     if (qrc) return qrc;
   }
   switch (w.type) {
-    case B2_Q4_0: return launch_w<B2_Q4_0>(p, grid, smem, s);
-    case B2_Q8_0: return launch_w<B2_Q8_0>(p, grid, smem, s);
-    case B2_Q4_K: return launch_w<B2_Q4_K>(p, grid, smem, s);
-    case B2_Q6_K: return launch_w<B2_Q6_K>(p, grid, smem, s);
+    case B2_Q4_0: return launch_w<B2_Q4_0>(p, grid, nw, smem, s);
+    case B2_Q8_0: return launch_w<B2_Q8_0>(p, grid, nw, smem, s);
+    case B2_Q4_K: return launch_w<B2_Q4_K>(p, grid, nw, smem, s);
+    case B2_Q6_K: return launch_w<B2_Q6_K>(p, grid, nw, smem, s);
   }
   set_error("gemv: unsupported weight type %d", w.type);
   return B2_ERR_UNSUPPORTED;

@@ -55,19 +55,19 @@ inline int act_type_for(int wtype) { return (wtype == B2_Q4_K || wtype == B2_Q6_
 // ---- tiled quantized matrix (device) ---------------------------------------------
 // W is [n_rows x k] in GGUF units along k: 32-weight blocks (Q4_0, Q8_0) or
 // 256-weight super-blocks (Q4_K, Q6_K), nu units per row.  On upload the rows
-// are grouped into tiles of 8 (the last tile zero-padded) and each row's
-// units into S = tile_splits(type, k) ranges of L = ceil(nu / S) units (range
-// w holds units [w*L, min((w+1)*L, nu))).  A tile is S*L unit slots; slot
-// i*S + w carries unit w*L + i of the tile's 8 rows (zeros past nu), so the
-// i-th units of all ranges are adjacent and the next few i of a tile are one
-// contiguous bulk copy.  Within a slot the 8 rows' unit bytes are moved into
-// planes, row g of each plane at g * (plane row bytes); planes of 64 or 128 B
-// per row have row g's 16-byte chunks rotated by g, so the GEMV's per-row
-// shared-memory reads hit distinct banks.  Bytes are those of the GGUF input.
+// are grouped into tiles of 8 (the last tile zero-padded); a tile is nu unit
+// slots in unit order, slot u carrying unit u of the tile's 8 rows, so any
+// run of a tile's units is one contiguous bulk copy.  Within a slot the 8
+// rows' unit bytes are moved into planes, row g of each plane at g * (plane
+// row bytes); planes of 64 or 128 B per row have row g's 16-byte chunks
+// rotated by g, so per-row shared-memory reads hit distinct banks.  Bytes
+// are those of the GGUF input.
 //   Q4_0  144 B: qs 8x16 @0,  d 8x2 @128
 //   Q8_0  272 B: qs[0:16] 8x16 @0, qs[16:32] 8x16 @128, d 8x2 @256
 //   Q4_K 1152 B: qs 8x128 @0 (rotated), d|dmin|scales 8x16 @1024
 //   Q6_K 1680 B: ql 8x128 @0 (rotated), qh 8x64 @1024 (rotated), scales 8x16 @1536, d 8x2 @1664
+// (splits/ulen describe the slot order: S ranges of L units, slot i*S + w =
+// unit w*L + i; the layout uploaded here is S = 1, L = nu, i.e. unit order.)
 #if defined(__CUDACC__)
 #define B2_HD __host__ __device__
 #else
@@ -92,14 +92,8 @@ B2_HD inline int gguf_unit_bytes(int type) {
 B2_HD inline int tile_slot_bytes(int type) {
   return type == B2_Q4_0 ? 144 : type == B2_Q8_0 ? 272 : type == B2_Q4_K ? 1152 : type == B2_Q6_K ? 1680 : 0;
 }
-// Ranges per row: the largest power of two <= 8 that leaves >= 4 units per
-// range (the four interleaved partial sums of a range each get a unit).
-B2_HD inline int tile_splits(int type, int64_t k) {
-  const int64_t nu = k / unit_elems(type);
-  int s = 1;
-  while (s < 8 && 2 * s * 4 <= nu) s *= 2;
-  return s;
-}
+// Slot-order ranges per row of the uploaded layout: one (units in order).
+B2_HD inline int tile_splits(int type, int64_t k) { return 1; }
 // Byte offset of (tile, unit u) in the matrix data.
 B2_HD inline int64_t slot_offset(const QMatrix& m, int64_t tile, int u) {
   const int w = u / m.ulen, i = u - w * m.ulen;
@@ -239,13 +233,13 @@ struct RopeKvEpi {
 };
 
 // Where a GEMV's quantized activations live: the image carve-up of
-// gemv_act_image(w, n_tok) — codes [n_act_tok][kq] (fragment order for the
-// mma kernels, natural order for dp4a), fp32 scales per (token, unit), int16
-// block sums per (token, unit).  Producers other than the GEMV's own
-// quantizer (the fused RMSNorm) write it through the same store helpers.
+// gemv_act_image(w, n_tok) — codes [n_act_tok][kq] in natural order, fp32
+// scales per (token, unit), int16 block sums per (token, unit).  Producers
+// other than the GEMV's own quantizer (the fused RMSNorm, the attention's
+// last CTAs) write it through the same store helpers.
 struct ActImage {
   uint8_t* img = nullptr;
-  int kq = 0, nu = 0, type = 0, n_act_tok = 0, mma = 0;
+  int kq = 0, nu = 0, type = 0, n_act_tok = 0;
   uint32_t off_dx = 0, off_bs = 0, bytes = 0;
 };
 

@@ -293,384 +293,6 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_
   }
 }
 
-// ---- split-K decode attention ----------------------------------------------------------------
-// CTA (chunk, kv head, query): positions [chunk*128, chunk*128+128) ∩ [0, pos+1)
-// of the query's sequence, for the G query heads sharing the kv head.  The
-// chunk's K and V rows are brought into shared memory by cp.async.bulk (1-D
-// TMA; a chunk crossing the ring's seam or the pinned prefix is up to three
-// copies) while q goes to shared memory; then, per head:
-//   scores: lane i of an 8-lane group holds dims [B*i, B*i+B) and
-//     [HD/2 + B*i, HD/2 + B*i + B) (B = HD/16) of q and k (16-byte rows of a
-//     position per group, so the K reads are bank-conflict free); an fmaf
-//     chain over its dims in that order, a butterfly over the 8 lanes (xor 4,
-//     2, 1), times 1/sqrt(HD).  Each lane group scores 4 positions against
-//     all G heads at once (q from shared memory, packed f32x2 FMAs);
-//   m = the chunk's max; e = exp(s − m); the chunk sum l = ((W0 + W1) + W2) + W3
-//     with W_w the 32-lane butterfly (xor 16..1) of e over positions 32w..32w+31;
-//   P·V: output dim d keeps four sums a_r of e·v over the positions i with
-//     i mod 4 == r (fmaf chains in position order; warp r of a dim half takes
-//     them, one position for all heads at a time), then (a0 + a1) + (a2 + a3).
-// Writes the unnormalised partial output with its max and sum.  With
-// fz.count, the last CTA of each (query, kv head) to finish also combines the
-// chunks (attn_combine's arithmetic) into fz.out and, with fz.img, quantizes
-// those G·HD outputs into the O projection's activation image.  Every wait is
-// bounded; a query outside the cache attends to nothing.
-constexpr int kAttnP = 128;
-struct AttnFuse {
-  unsigned int* count = nullptr;   // [n_tok][n_kv] arrivals, zero between launches (null: separate combine)
-  float* out = nullptr;            // [n_tok][n_head][hd]
-  ActImage img;                    // O projection image (img.img null: none)
-};
-
-// Two fp32 FMAs in one instruction (fma.rn.f32x2): each lane is rounded like fmaf.
-__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%0, %1};\n\t"
-      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
-      "mov.b64 {%0, %1}, rc;\n\t}"
-      : "+f"(d0), "+f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
-// B fp16 values at p (16-byte aligned for B = 8, 8-byte for B = 4) -> fp32.
-template <int B>
-__device__ __forceinline__ void ld_half_row(const uint16_t* p, float (&f)[B]) {
-  if constexpr (B == 8) {
-    const uint4 w = *reinterpret_cast<const uint4*>(p);
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      f[2 * e] = h2f((uint16_t)(ww[e] & 0xFFFFu));
-      f[2 * e + 1] = h2f((uint16_t)(ww[e] >> 16));
-    }
-  } else {
-    const uint2 w = *reinterpret_cast<const uint2*>(p);
-    f[0] = h2f((uint16_t)(w.x & 0xFFFFu));
-    f[1] = h2f((uint16_t)(w.x >> 16));
-    f[2] = h2f((uint16_t)(w.y & 0xFFFFu));
-    f[3] = h2f((uint16_t)(w.y >> 16));
-  }
-}
-
-template <int HD, int G>
-__global__ void __launch_bounds__(256, 3) attn_chunk_kernel(const float* __restrict__ q, int n_head, int n_kv,
-                                                            const int32_t* __restrict__ pos,
-                                                            const int32_t* __restrict__ seq,
-                                                            const uint16_t* __restrict__ kc,
-                                                            const uint16_t* __restrict__ vc,
-                                                            const KvSeqState* __restrict__ st, int n_seq, int cap,
-                                                            float scale, float* __restrict__ part_o,
-                                                            float* __restrict__ part_ml, int n_split, int* status,
-                                                            AttnFuse fz) {
-  constexpr int P = kAttnP, B = HD / 16;
-  constexpr int PAIRS = HD / 2;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);        // [0]: K rows, [1]: V rows
-  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);   // [P][HD]
-  uint16_t* vs = ks + P * HD;                                 // [P][HD]
-  float* qs = reinterpret_cast<float*>(vs + P * HD);          // [G][HD]
-  float* sc = qs + G * HD;                                    // [P][G]: scores, then e
-  __shared__ float mh[G], lh[G], wred[G][4];
-  __shared__ unsigned int last_cta;
-  pdl_wait();
-  pdl_launch_dependents();
-  const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
-  const int s = seq[b], pb = pos[b];
-  const int n_pos = (s >= 0 && s < n_seq && pb >= 0 && pb < cap) ? pb + 1 : 0;
-  const int t0 = chunk * P, n = min(P, n_pos - t0);
-  const int hq0 = kh * G;
-  float* po = part_o + (((int64_t)b * n_head + hq0) * n_split + chunk) * HD;
-  float* pml = part_ml + (((int64_t)b * n_head + hq0) * n_split + chunk) * 2;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (n <= 0) {
-    for (int i = tid; i < G * HD; i += blockDim.x) po[(int64_t)(i / HD) * n_split * HD + i % HD] = 0.0f;
-    if (tid < G) {
-      pml[(int64_t)tid * n_split * 2 + 0] = -FLT_MAX;
-      pml[(int64_t)tid * n_split * 2 + 1] = 0.0f;
-    }
-  } else {
-    const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
-    const int64_t base = ((int64_t)s * n_kv + kh) * cap;   // row of slot 0
-    if (tid == 0) {
-      mbar_init(&bar[0], 1);
-      mbar_init(&bar[1], 1);
-      fence_mbar_init();
-      mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * HD * 2));
-      mbar_arrive_expect_tx(&bar[1], (uint32_t)(n * HD * 2));
-      // logical positions [t0, t0+n) as runs of consecutive slots; all K
-      // runs first, so the scores can start while V is still arriving
-      for (int kv = 0; kv < 2; ++kv) {
-        int p = t0;
-        while (p < t0 + n) {
-          const int64_t slot = kv_slot(sst, p, cap);
-          int len = t0 + n - p;
-          if (p < sst.n_keep) len = min(len, sst.n_keep - p);
-          else len = (int)min((int64_t)len, (int64_t)cap - slot);   // up to the end of the ring
-          bulk_g2s((kv ? vs : ks) + (p - t0) * HD, (kv ? vc : kc) + (base + slot) * HD, (uint32_t)(len * HD * 2),
-                   &bar[kv]);
-          p += len;
-        }
-      }
-    }
-    // q of the G heads into shared memory while the copies fly
-    {
-      const float4* qg = reinterpret_cast<const float4*>(q + ((int64_t)b * n_head + hq0) * HD);
-      for (int i = tid; i < G * HD / 4; i += blockDim.x) reinterpret_cast<float4*>(qs)[i] = qg[i];
-    }
-    __syncthreads();
-    mbar_wait_bounded(&bar[0], 0, status, 5);
-
-    // ---- scores: lane group grp of warp w takes positions w*16 + it*4 + grp, HG heads per pass ----
-    {
-      constexpr int HG = G < 4 ? G : 4;
-      const int li = lane & 7, grp = lane >> 3;
-#pragma unroll 1
-      for (int hb = 0; hb < G; hb += HG) {
-        float acc[4][HG];
-#pragma unroll
-        for (int it = 0; it < 4; ++it)
-#pragma unroll
-          for (int h = 0; h < HG; ++h) acc[it][h] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int d0 = j * (HD / 2) + B * li;
-          float qv[HG][B];
-#pragma unroll
-          for (int h = 0; h < HG; ++h)
-#pragma unroll
-            for (int d = 0; d < B; d += 4) {
-              const float4 v = *reinterpret_cast<const float4*>(qs + (hb + h) * HD + d0 + d);
-              qv[h][d] = v.x;
-              qv[h][d + 1] = v.y;
-              qv[h][d + 2] = v.z;
-              qv[h][d + 3] = v.w;
-            }
-#pragma unroll
-          for (int it = 0; it < 4; ++it) {
-            const int i = warp * 16 + it * 4 + grp;
-            float kf[B];
-            if (i < n) {
-              ld_half_row<B>(ks + i * HD + d0, kf);
-            } else {
-#pragma unroll
-              for (int d = 0; d < B; ++d) kf[d] = 0.0f;
-            }
-#pragma unroll
-            for (int d = 0; d < B; ++d) {
-              if constexpr (HG == 1) {
-                acc[it][0] = fmaf(qv[0][d], kf[d], acc[it][0]);
-              } else {
-#pragma unroll
-                for (int h = 0; h < HG; h += 2)
-                  ffma2(acc[it][h], acc[it][h + 1], qv[h][d], qv[h + 1][d], kf[d], kf[d]);
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-          const int i = warp * 16 + it * 4 + grp;
-#pragma unroll
-          for (int h = 0; h < HG; ++h) {
-            float a = acc[it][h];
-            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
-            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
-            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-            if (li == h && i < n) sc[i * G + hb + h] = __fmul_rn(a, scale);
-          }
-        }
-      }
-    }
-    __syncthreads();
-    // ---- max, exp and the chunk sum: 128 threads per head, 2 heads per round ----
-#pragma unroll 1
-    for (int h0 = 0; h0 < G; h0 += 2) {
-      const int h = h0 + (tid >> 7), w = (tid >> 5) & 3, i = tid & 127;
-      const bool act = h < G;
-      float v = (act && i < n) ? sc[i * G + h] : -FLT_MAX;
-      v = warp_max(v);
-      if (act && lane == 0) wred[h][w] = v;
-      __syncthreads();
-      const float m = act ? fmaxf(fmaxf(wred[h][0], wred[h][1]), fmaxf(wred[h][2], wred[h][3])) : 0.0f;
-      float e = 0.0f;
-      if (act && i < n) {
-        e = b2_expf(__fsub_rn(sc[i * G + h], m));
-        sc[i * G + h] = e;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, o));
-      __syncthreads();   // every wred max read before the sums reuse it
-      if (act && lane == 0) wred[h][w] = e;
-      __syncthreads();
-      if (act && i == 0) {
-        mh[h] = m;
-        lh[h] = __fadd_rn(__fadd_rn(__fadd_rn(wred[h][0], wred[h][1]), wred[h][2]), wred[h][3]);
-      }
-    }
-    __syncthreads();
-    mbar_wait_bounded(&bar[1], 0, status, 5);   // V, which landed while the scores ran
-    // ---- P·V: warp (residue r, dim half), lane = dim pair; all heads per position ----
-    float* pv = reinterpret_cast<float*>(ks);   // [4 residues][G][HD] partials, K is no longer needed
-    {
-      const int r = warp & 3, pr = (warp >> 2) * 32 + lane;
-      if (pr < PAIRS) {
-        float acc[G][2];
-#pragma unroll
-        for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0.0f;
-        for (int i = r; i < n; i += 4) {
-          const uint32_t vv = *reinterpret_cast<const uint32_t*>(vs + i * HD + 2 * pr);
-          const float v0 = h2f((uint16_t)(vv & 0xFFFFu)), v1 = h2f((uint16_t)(vv >> 16));
-          float e[G];
-#pragma unroll
-          for (int h = 0; h < G; h += (G >= 4 ? 4 : 1)) {
-            if constexpr (G >= 4) {
-              const float4 e4 = *reinterpret_cast<const float4*>(sc + i * G + h);
-              e[h] = e4.x;
-              e[h + 1] = e4.y;
-              e[h + 2] = e4.z;
-              e[h + 3] = e4.w;
-            } else {
-              e[h] = sc[i * G + h];
-            }
-          }
-#pragma unroll
-          for (int h = 0; h < G; ++h) ffma2(acc[h][0], acc[h][1], e[h], e[h], v0, v1);
-        }
-        __syncwarp();
-#pragma unroll
-        for (int h = 0; h < G; ++h)
-          *reinterpret_cast<float2*>(pv + (r * G + h) * HD + 2 * pr) = make_float2(acc[h][0], acc[h][1]);
-      }
-    }
-    __syncthreads();
-    for (int hd2 = tid; hd2 < G * HD; hd2 += blockDim.x) {
-      const int h = hd2 / HD, d = hd2 - h * HD;
-      const float a0 = pv[(0 * G + h) * HD + d], a1 = pv[(1 * G + h) * HD + d];
-      const float a2 = pv[(2 * G + h) * HD + d], a3 = pv[(3 * G + h) * HD + d];
-      po[(int64_t)h * n_split * HD + d] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
-    }
-    if (tid < G) {
-      pml[(int64_t)tid * n_split * 2 + 0] = mh[tid];
-      pml[(int64_t)tid * n_split * 2 + 1] = lh[tid];
-    }
-  }
-  if (fz.count == nullptr) return;
-  // ---- the last CTA of this (query, kv head) combines the chunks ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    unsigned int* cnt = fz.count + (int64_t)b * n_kv + kh;
-    last_cta = atomicAdd(cnt, 1u) == (unsigned int)(n_split - 1);
-    if (last_cta) *cnt = 0u;   // ready for the next launch
-  }
-  __syncthreads();
-  if (!last_cta) return;
-  __threadfence();
-  // Chunk weights e_c = exp(m_c − M) per head (staged once), L = Σ_c e_c·l_c
-  // in chunk order, then out[d] = (Σ_c e_c·O_c[d]) · (1/L) — attn_combine's
-  // arithmetic, with the partials read from L2 eight chunks at a time.
-  float* ec = reinterpret_cast<float*>(smem + 128);   // [G][n_split] (0: chunk attended to nothing)
-  float* ob = ec + G * n_split;                        // [G][HD] outputs of this kv head
-  __shared__ float inv_l[G];
-  if (warp < G) {
-    const float* ml = part_ml + ((int64_t)b * n_head + hq0 + warp) * n_split * 2;
-    float M = -FLT_MAX;
-    for (int c = lane; c < n_split; c += 32) M = fmaxf(M, __ldcg(ml + 2 * c));
-    M = warp_max(M);
-    for (int c = lane; c < n_split; c += 32) {
-      const float lc = __ldcg(ml + 2 * c + 1);
-      ec[warp * n_split + c] = lc > 0.0f ? b2_expf(__fsub_rn(__ldcg(ml + 2 * c), M)) : 0.0f;
-    }
-    __syncwarp();
-    if (lane == 0) {
-      float L = 0.0f;
-      for (int c = 0; c < n_split; ++c) {
-        const float lc = __ldcg(ml + 2 * c + 1);
-        if (lc > 0.0f) L = __fadd_rn(L, __fmul_rn(ec[warp * n_split + c], lc));
-      }
-      inv_l[warp] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;   // L == 0: a query that attended to nothing
-    }
-  }
-  __syncthreads();
-  for (int hd2 = tid; hd2 < G * HD; hd2 += blockDim.x) {
-    const int h = hd2 / HD, d = hd2 - h * HD;
-    const float* pq = part_o + ((int64_t)b * n_head + hq0 + h) * n_split * HD + d;
-    const float* eh = ec + h * n_split;
-    float v = 0.0f;
-    for (int c0 = 0; c0 < n_split; c0 += 8) {
-      float pv[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) pv[j] = c0 + j < n_split ? __ldcg(pq + (int64_t)(c0 + j) * HD) : 0.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (c0 + j < n_split && eh[c0 + j] != 0.0f) v = __fadd_rn(v, __fmul_rn(eh[c0 + j], pv[j]));
-    }
-    const float o = __fmul_rn(v, inv_l[h]);
-    fz.out[((int64_t)b * n_head + hq0 + h) * HD + d] = o;
-    ob[hd2] = o;
-  }
-  if (fz.img.img == nullptr) return;
-  __syncthreads();
-  // quantize the G*HD outputs (columns [hq0*HD, (hq0+G)*HD) of the O input row)
-  const int col0 = hq0 * HD;
-  if (fz.img.type == B2_Q4_K || fz.img.type == B2_Q6_K) {
-    // one 256-value unit per warp, 8 values per lane
-    for (int u = warp; u < G * HD / 256; u += blockDim.x / 32) {
-      float v8[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v8[j] = ob[u * 256 + lane * 8 + j];
-      int8_t q8[8];
-      int bs = 0;
-      const float d = quant_q8_k_lane(v8, q8, &bs);
-      store_q8k_unit(fz.img, b, col0 / 256 + u, q8, d, bs);
-    }
-  } else {
-    // one 32-value block per thread (ref_quantize_row_q8_0)
-    for (int u = tid; u < G * HD / 32; u += blockDim.x) {
-      float amax = 0.0f;
-      for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(ob[u * 32 + j]));
-      const float d = __fmul_rn(amax, 1.0f / 127.0f);
-      const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
-      uint32_t w8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      int sum = 0;
-      for (int j = 0; j < 32; ++j) {
-        const float scv = __fmul_rn(ob[u * 32 + j], id);
-        const float tt = scv >= 0.0f ? __fadd_rn(scv, 0.5f) : __fsub_rn(scv, 0.5f);
-        int qv = __float2int_rz(tt);
-        qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
-        sum += qv;
-        w8[j >> 2] |= ((uint32_t)(uint8_t)qv) << (8 * (j & 3));
-      }
-      store_q8_0_block(fz.img, b, col0 / 32 + u, w8, h2f(f2h_rn(d)), sum);
-    }
-  }
-}
-
-// Combines the chunks of one query head: M = max m_s, L = Σ_s e^(m_s−M)·l_s,
-// out = (Σ_s e^(m_s−M)·O_s) · (1/L), chunks in order, each step one rounded
-// operation.
-__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_head,
-                                    int hd, int n_split, float* __restrict__ out) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const int h = blockIdx.x, b = blockIdx.y;
-  const float* ml = part_ml + ((int64_t)b * n_head + h) * n_split * 2;
-  const float* po = part_o + ((int64_t)b * n_head + h) * n_split * hd;
-  float M = -FLT_MAX;
-  for (int s = 0; s < n_split; ++s) M = fmaxf(M, ml[2 * s]);
-  float L = 0.0f;
-  for (int s = 0; s < n_split; ++s)
-    if (ml[2 * s + 1] > 0.0f) L = __fadd_rn(L, __fmul_rn(b2_expf(__fsub_rn(ml[2 * s], M)), ml[2 * s + 1]));
-  const float invL = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;   // L == 0: a query that attended to nothing
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float v = 0.0f;
-    for (int s = 0; s < n_split; ++s)
-      if (ml[2 * s + 1] > 0.0f)
-        v = __fadd_rn(v, __fmul_rn(b2_expf(__fsub_rn(ml[2 * s], M)), po[(int64_t)s * hd + d]));
-    out[((int64_t)b * n_head + h) * hd + d] = __fmul_rn(v, invL);
-  }
-}
-
 // ---- KV shift ----------------------------------------------------------------------------
 // Rotates K rows of logical positions [p_begin, p_end) of sequence s (slots
 // computed with the state before the shift) by the angle table of the
@@ -841,22 +463,6 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n
   }
 }
 
-template <typename K, typename... Args>
-int launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
-  return B2_OK;
-}
-
 }  // namespace
 
 int launch_embed(const int32_t* tokens, int n_tok, int n_vocab, int type, const uint8_t* table, int64_t row_bytes,
@@ -889,65 +495,6 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
                     st, n_seq, cap);
 }
 
-int attn_splits(int cap) { return (cap + kAttnP - 1) / kAttnP; }
-
-// The fused combine stages G*n_split chunk weights and G*hd outputs in the
-// K buffer of the last CTA.
-bool attn_combine_fusable(int n_head, int n_kv, int hd, int cap) {
-  const int G = n_head / n_kv;
-  return (size_t)G * (attn_splits(cap) + hd) * 4 <= (size_t)kAttnP * hd * 2;
-}
-
-bool attn_fusable(int n_head, int n_kv, int hd, int act_type) {
-  const int G = n_head / n_kv;
-  return (act_type == B2_Q4_K || act_type == B2_Q6_K) ? (G * hd) % 256 == 0 : (G * hd) % 32 == 0;
-}
-
-int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* part_o,
-                     float* part_ml, float* out, cudaStream_t s, int* status, unsigned int* count,
-                     const ActImage* img) {
-  const int G = n_head / n_kv;
-  const int n_split = attn_splits(cap);
-  const float scale = 1.0f / sqrtf((float)hd);
-  const dim3 grid(n_split, n_kv, n_tok);
-  AttnFuse fz;
-  B2_CHECK_ARG(!count || attn_combine_fusable(n_head, n_kv, hd, cap), "attention: combine not fusable");
-  if (count) {
-    fz.count = count;
-    fz.out = out;
-    if (img) {
-      B2_CHECK_ARG(attn_fusable(n_head, n_kv, hd, img->type) && img->img, "attention: image not fusable");
-      fz.img = *img;
-    }
-  }
-  int rc = B2_ERR_UNSUPPORTED;
-#define B2_ATTN_CASE(HDV, GV)                                                                                       \
-  if (hd == HDV && G == GV) {                                                                                       \
-    const size_t sm = 128 + (size_t)2 * kAttnP * HDV * 2 + (size_t)GV * HDV * 4 + (size_t)GV * kAttnP * 4;          \
-    B2_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<HDV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
-                                     (int)sm));                                                                     \
-    rc = launch_pdl(attn_chunk_kernel<HDV, GV>, grid, dim3(256), sm, s, q, n_head, n_kv, pos, seq, kc, vc, st,      \
-                    n_seq, cap, scale, part_o, part_ml, n_split, status, fz);                                       \
-  }
-  B2_ATTN_CASE(128, 1)
-  B2_ATTN_CASE(128, 2)
-  B2_ATTN_CASE(128, 4)
-  B2_ATTN_CASE(128, 8)
-  B2_ATTN_CASE(64, 1)
-  B2_ATTN_CASE(64, 2)
-  B2_ATTN_CASE(64, 4)
-  B2_ATTN_CASE(64, 8)
-#undef B2_ATTN_CASE
-  if (rc == B2_ERR_UNSUPPORTED) {
-    set_error("attention: unsupported head_dim %d / group %d", hd, G);
-    return rc;
-  }
-  if (rc != B2_OK || count) return rc;
-  return launch_pdl(attn_combine_kernel, dim3(n_head, n_tok), dim3(hd), 0, s, (const float*)part_o,
-                    (const float*)part_ml, n_head, hd, n_split, out);
-}
-
 int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
                     const RotTable& cs, cudaStream_t s) {
   B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
@@ -969,7 +516,8 @@ int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, con
 }
 
 // SwiGLU over (gate, up) row pairs, as the GEMV's SwiGLU epilogue computes
-// it: h[t][f] = silu(gu[t][2f]) * gu[t][2f+1], the same rounded operations.
+// it: h[t][f] = silu(gu[t][2f]) * gu[t][2f+1] in the reference's order
+// (silu_mul_ref).
 __global__ void swiglu_pairs_kernel(const float* __restrict__ gu, int64_t n_tok, int ff, float* __restrict__ h) {
   pdl_wait();
   pdl_launch_dependents();
@@ -977,7 +525,7 @@ __global__ void swiglu_pairs_kernel(const float* __restrict__ gu, int64_t n_tok,
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / ff, f = i - t * ff;
     const float2 v = *reinterpret_cast<const float2*>(gu + t * 2 * ff + 2 * f);
-    h[i] = __fmul_rn(__fdiv_rn(v.x, __fadd_rn(1.0f, b2_expf(-v.x))), v.y);
+    h[i] = silu_mul_ref(v.x, v.y);
   }
 }
 

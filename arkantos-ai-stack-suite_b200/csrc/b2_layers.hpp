@@ -23,28 +23,20 @@ bool add_rmsnorm_q_supported(int n, int act_type);
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                    const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int n_seq, int cap,
                    cudaStream_t s);
-// Split-K attention: positions are cut into chunks of P, one CTA per (chunk,
-// kv head, query); part_o [n_tok][n_head][n_split][hd], part_ml
-// [n_tok][n_head][n_split][2] hold the partial results (scratch).
-// Split-K decode attention in chunks of 128 positions (attn_splits(cap)
-// partials per query head in part_o [n_tok][n_head][n_split][hd] and
-// part_ml [.][.][n_split][2]), then the combine.  Queries whose sequence id
+// Decode attention in the reference's order (b2_attn.cu): q fp32
+// [n_tok][n_head][hd] against the fp16 caches [n_seq][n_kv][cap][hd], out
+// fp32 [n_tok][n_head][hd].  `scores` is scratch of attn_scratch_floats
+// floats; `count` is [n_tok][n_kv] counters that must be zero before the
+// first launch and are left zero by every launch.  Queries whose sequence id
 // is outside [0, n_seq) or whose position is outside [0, cap) read nothing
 // and produce zero outputs.  st may be null (plain layout).
-int attn_splits(int cap);
-// With `count` ([n_tok][n_kv] zeroed counters, left zeroed) the combine runs
-// in the last CTA of each (query, kv head) instead of a second kernel, and
-// with `img` that CTA also quantizes its outputs into the O projection's
-// activation image (attn_combine_fusable, and for img attn_fusable, must hold).
+size_t attn_scratch_floats(int n_tok, int n_head, int cap);
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* part_o,
-                     float* part_ml, float* out, cudaStream_t s, int* status = nullptr, unsigned int* count = nullptr,
-                     const ActImage* img = nullptr);
-bool attn_combine_fusable(int n_head, int n_kv, int hd, int cap);
+                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scores,
+                     unsigned int* count, float* out, cudaStream_t s, int* status = nullptr);
 // h [n_tok][ff] = silu(gate) * up over the (gate, up) row pairs of gu
 // [n_tok][2 ff], with the arithmetic of the GEMV's SwiGLU epilogue.
 int launch_swiglu_pairs(const float* gu, int n_tok, int ff, float* h, cudaStream_t s);
-bool attn_fusable(int n_head, int n_kv, int hd, int act_type);
 // cos/sin pairs of one position delta for every rotated pair (head_dim <= 256).
 constexpr int kRotPairs = 128;
 struct RotTable {

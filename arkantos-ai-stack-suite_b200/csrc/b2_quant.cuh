@@ -77,15 +77,8 @@ __device__ __forceinline__ float quant_q8_k_lane(const float v[8], int8_t q[8], 
 }
 
 // ---- stores into a GEMV activation image (ActImage carve-up) -------------------------------
-// Codes of token t start at t*kq.  For the dp4a kernels they are in natural
-// order; for the mma kernels each token's codes are stored in fragment order:
-//   Q8_K (256-value units, 64 words w): the 16 words thread q of a warp
-//     needs, idx = 2j + h <-> word 8j + 4h + q, sit in 16-byte chunks i = idx/4
-//     at physical chunk ((4i + q) + 4*(t & 1)) & 15 of the unit's 256 bytes;
-//   Q8_0 (32-value blocks): words q and q+4 of block u are one 8-byte slot,
-//     slot ((u & 3)*4 + q + 4*(t & 3)) & 15 of the 128 bytes of blocks u & ~3.
-// The rotations by token spread the 8 tokens of a fragment load over all
-// banks.
+// Codes of token t start at t*kq, in natural order (unit u of Q8_K at
+// u*256, block b of Q8_0 at b*32).
 
 // One Q8_K unit b of token t, called by a whole warp (lane = 8-value group):
 // codes q[8] of the lane, scale d, and the lane's 16-group sum bs (valid on
@@ -98,18 +91,7 @@ __device__ __forceinline__ void store_q8k_unit(const ActImage& a, int t, int b, 
   const uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
                       ((uint32_t)(uint8_t)q[7] << 24);
   uint8_t* unit = a.img + (int64_t)t * a.kq + (int64_t)b * 256;
-  if (a.mma) {
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      const int wi = 2 * lane + h2;   // word 8j + 4h + q of the unit
-      const int j = wi >> 3, h = (wi >> 2) & 1, qq = wi & 3;
-      const int idx = 2 * j + h;
-      *reinterpret_cast<uint32_t*>(unit + ((((idx >> 2) * 4 + qq) + 4 * (t & 1)) & 15) * 16 + (idx & 3) * 4) =
-          h2 ? w1 : w0;
-    }
-  } else {
-    *reinterpret_cast<uint2*>(unit + lane * 8) = make_uint2(w0, w1);
-  }
+  *reinterpret_cast<uint2*>(unit + lane * 8) = make_uint2(w0, w1);
   float* dxs = reinterpret_cast<float*>(a.img + a.off_dx);
   int16_t* bss = reinterpret_cast<int16_t*>(a.img + a.off_bs);
   if (lane == 0) dxs[t * a.nu + b] = d;
@@ -126,15 +108,8 @@ __device__ __forceinline__ void store_q8k_unit(const ActImage& a, int t, int b, 
 __device__ __forceinline__ void store_q8_0_block(const ActImage& a, int t, int b, const uint32_t (&w)[8], float dq,
                                                  int sum) {
   uint8_t* trow = a.img + (int64_t)t * a.kq;
-  if (a.mma) {
-    uint8_t* base = trow + (b >> 2) * 128;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<uint2*>(base + ((((b & 3) * 4 + q) + 4 * (t & 3)) & 15) * 8) = make_uint2(w[q], w[q + 4]);
-  } else {
-    *reinterpret_cast<uint4*>(trow + b * 32) = make_uint4(w[0], w[1], w[2], w[3]);
-    *reinterpret_cast<uint4*>(trow + b * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
-  }
+  *reinterpret_cast<uint4*>(trow + b * 32) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(trow + b * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
   reinterpret_cast<float*>(a.img + a.off_dx)[t * a.nu + b] = dq;
   if (a.type == B2_Q4_0) reinterpret_cast<int16_t*>(a.img + a.off_bs)[t * a.nu + b] = (int16_t)sum;
 }

@@ -400,13 +400,15 @@ def prompts_8b() -> np.ndarray:
     return rng.integers(0, LLAMA_8B["n_vocab"], (BATCH, PROMPT)).astype(np.int32)
 
 
-def launches_per_step(n_layer: int) -> int:
+def launches_per_step(n_layer: int, small_o: bool = False) -> int:
     """Kernels of this library one decode step launches: embed; per layer
     RMSNorm (+ Q8 image), QKV GEMV (RoPE + KV store epilogue), attention
-    (combine + O image in its last CTAs), O GEMV, RMSNorm (+ image), gate|up
-    GEMV (SwiGLU epilogue), quantize (down input), down GEMV; then RMSNorm,
-    head GEMV and argmax.  No library collective runs in a step."""
-    return 1 + 8 * n_layer + 3
+    scores (+ softmax in the last CTAs), attention P.V, quantize (O input;
+    none when the O input is small enough for the GEMV to quantize it
+    itself), O GEMV, RMSNorm (+ image), gate|up GEMV (SwiGLU epilogue),
+    quantize (down input), down GEMV; then RMSNorm, head GEMV and argmax.
+    No library collective runs in a step."""
+    return 1 + (9 if small_o else 10) * n_layer + 3
 
 
 def time_gemv_shape(b2, qtype: int, n: int, k: int, n_tok: int, steps: int, seed: int) -> dict:
@@ -585,6 +587,16 @@ def run_decode_ours(args, dist, rank, world, local):
     }
     if q40 is not None:
         out["q4_0_gemv"] = q40
+    if world == 1 and not args.skip_1b:
+        progress("config-4 decode (1.1B Q4_0, batch 1)")
+        sub = argparse.Namespace(**vars(args))
+        sub.steps = min(args.steps, GEN_1B)
+        sub.cpu_seconds = min(args.cpu_seconds, 5.0)
+        d1 = run_decode1b_ours(sub, None, 0, 1, local)
+        out["decode_1b_q4_0"] = {k: d1[k] for k in ("metric", "value", "unit", "steps", "ms_per_step", "roofline",
+                                                     "e2e", "gpu_launches", "clocks") if k in d1}
+        if "cpu_baseline" in d1:
+            out["decode_1b_q4_0"]["cpu_baseline"] = d1["cpu_baseline"]
     if rank == 0:
         progress("cpu baseline")
         out["cpu_baseline"] = cpu_decode_baseline(path, args.cpu_seconds)
@@ -779,7 +791,7 @@ def run_decode1b_ours(args, dist, rank, world, local):
                         "algorithmic_bytes_per_launch": int(step_bytes)},
            "e2e": {"value": round(steps / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 128,
                    "greedy_ids_equal_device_loop": bool(np.array_equal(np.array(ids), gen.ravel()[:steps]))},
-           "gpu_launches": launches_per_step(c["n_layer"]) * steps, "clocks": clk.summary(),
+           "gpu_launches": launches_per_step(c["n_layer"], small_o=True) * steps, "clocks": clk.summary(),
            "setup_s": {"write_gguf": round(t_write, 1)}}
     del ctx, model
     if rank == 0 and args.cpu_seconds > 0:
@@ -1046,6 +1058,7 @@ def main():
     ap.add_argument("--workload", default="decode_8b_q4k", choices=sorted(WORKLOADS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--keep-model", action="store_true", help="keep the synthetic GGUF file after the run")
+    ap.add_argument("--skip-1b", action="store_true", help="decode_8b_q4k: leave out the 1.1B Q4_0 (config 4) line")
     ap.add_argument("--attn-batch", type=int, default=None, help="attn: one batch size (default 1, 4 and 16)")
     ap.add_argument("--profile-range", action="store_true",
                     help="open the profiler range around the timed decode steps only")

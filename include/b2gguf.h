@@ -228,14 +228,16 @@ B2_API int b2_rope_kv_store(const float* qkv, int n_tok, int n_seq, int n_head, 
                             const int32_t* pos, const int32_t* seq, const float* rope, float* q_out,
                             uint16_t* k_cache, uint16_t* v_cache, int cap, void* stream);
 
-/* Decode attention over the fp16 cache (cortex_a5_engine.cpp:1205-1254),
- * split-K over positions: query i attends to positions 0..pos[i] of sequence
- * seq[i] with its n_head/n_kv grouped heads.  q fp32 [n_q][n_head][hd],
- * out fp32 [n_q][n_head][hd]; caches as above ([n_seq][n_kv][cap][hd]).  A
- * query whose sequence id is outside [0, n_seq) or position outside
- * [0, cap) reads nothing and gets a zero row.  Partial results go to
- * stream-ordered scratch allocated by the call; no host synchronization, so
- * the call can be captured into a CUDA graph. */
+/* Decode attention over the fp16 cache (cortex_a5_engine.cpp:1205-1254) in
+ * the reference's order: query i attends to positions 0..pos[i] of sequence
+ * seq[i] with its n_head/n_kv grouped heads; scores, softmax (expf as the
+ * host C library computes it) and the weighted V sum are the reference's
+ * sequential fp32 operations, so the output is bit-identical to its CPU
+ * result.  q fp32 [n_q][n_head][hd], out fp32 [n_q][n_head][hd]; caches as
+ * above ([n_seq][n_kv][cap][hd]).  A query whose sequence id is outside
+ * [0, n_seq) or position outside [0, cap) reads nothing and gets a zero
+ * row.  Scores go to stream-ordered scratch allocated by the call; no host
+ * synchronization, so the call can be captured into a CUDA graph. */
 B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
                           const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv, int head_dim, int cap,
                           float* out, void* stream);
@@ -244,11 +246,11 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
  * run (a host that gives the library a fixed device-memory budget at
  * start-up, or a real-time decode loop that must not pay an allocation's
  * latency or risk its failure mid-turn).  No counterpart in the reference.
- * Same arguments and results as b2_attn_decode; the split-K partials live in
- * one static device array of B2_NOALLOC_SCRATCH_BYTES that every GPU loading
- * the library holds until exit.  Limits: n_q <= B2_NOALLOC_MAX_QUERIES and
- * n_q·n_head·ceil(cap/128)·(head_dim+2)·4 bytes within the array (larger
- * requests return B2_ERR_INVALID).  The first
+ * Same arguments and results as b2_attn_decode; the scores and the arrival
+ * counters live in one static device array of B2_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading the library holds until exit.  Limits: n_q <=
+ * B2_NOALLOC_MAX_QUERIES and n_q·n_head·cap·4 bytes (+ n_q·n_kv counters)
+ * within the array (larger requests return B2_ERR_INVALID).  The first
  * call on a device looks up the array's address (call it once before any
  * stream capture); calls outside capture look it up again, so a device reset
  * between calls is picked up, while a call under capture uses the address

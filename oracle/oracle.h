@@ -80,6 +80,8 @@ void orc_rope_table(float theta, int head_dim, int p0, int n_pos, float* out);
  * n_threads POSIX threads.  xq is Q8_0 for Q4_0/Q8_0 weights and Q8_K for
  * Q4_K/Q6_K weights.  row_bytes is the GGUF row size. */
 void orc_matmul(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int n_threads);
+void orc_matmul_strided(int wtype, const void* w, int64_t n_rows, size_t row_stride, int k, const void* xq, float* y,
+                        int n_threads);
 
 /* Activation type the reference's CPU dot pairs with each weight type. */
 int orc_vec_dot_type(int wtype);

@@ -294,7 +294,10 @@ class Model:
         return out
 
     def set_tp(self, tp: int) -> None:
-        """Device-order forward as `tp` tensor-parallel ranks compute it."""
+        """The forward as `tp` tensor-parallel ranks compute it: attention-out
+        and FFN-down as per-rank column-slice partials (each in the reference's
+        block order, or the tile order in device-order mode) summed in rank
+        order."""
         if lib.orc_model_set_tp(self.h, tp) != 0:
             raise ValueError(f"model does not split over {tp} ranks")
 

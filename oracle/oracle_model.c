@@ -312,20 +312,24 @@ static void proj_mode(orc_model* m, const orc_tensor* w, const float* x, float* 
 }
 static void proj(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) { proj_mode(m, w, x, y, nt, 0); }
 
-/* Attention-out and FFN-down under tensor parallelism (device order): rank r
- * owns input columns [r*k/tp, (r+1)*k/tp) and produces a partial output over
- * them; the partials are summed in rank order, y = ((p0 + p1) + p2) + ...,
+/* Attention-out and FFN-down under tensor parallelism: rank r owns input
+ * columns [r*k/tp, (r+1)*k/tp) and produces a partial output over them (in
+ * the reference's order over its blocks, or the tile order of device-order
+ * mode); the partials are summed in rank order, y = ((p0 + p1) + p2) + ...,
  * which is the reduction the GPU ranks perform after exchanging partials. */
 static void proj_reduce(orc_model* m, const orc_tensor* w, const float* x, float* y, int nt) {
-    if (m->tp <= 1 || m->device_order != 1) { proj(m, w, x, y, nt); return; }
+    if (m->tp <= 1 || m->device_order == 2) { proj(m, w, x, y, nt); return; }
     const int k = (int)w->ne[0], n = (int)w->ne[1], kl = k / m->tp;
     const int at = orc_vec_dot_type(w->type);
     if (at == ORC_Q8_K) orc_quantize_row_q8_k(x, m->xq, k);
     else orc_quantize_row_q8_0(x, m->xq, k);
     const size_t rb = orc_row_bytes(w->type, k);
-    for (int r = 0; r < m->tp; ++r)
-        orc_matmul_dev_strided(w->type, w->data + orc_row_bytes(w->type, r * kl), n, rb, kl,
-                               (const uint8_t*)m->xq + orc_row_bytes(at, r * kl), m->part + (size_t)r * n, 0, nt);
+    for (int r = 0; r < m->tp; ++r) {
+        const uint8_t* ws = w->data + orc_row_bytes(w->type, r * kl);
+        const void* xs = (const uint8_t*)m->xq + orc_row_bytes(at, r * kl);
+        if (m->device_order == 1) orc_matmul_dev_strided(w->type, ws, n, rb, kl, xs, m->part + (size_t)r * n, 0, nt);
+        else orc_matmul_strided(w->type, ws, n, rb, kl, xs, m->part + (size_t)r * n, nt);
+    }
     for (int i = 0; i < n; ++i) {
         float s = m->part[i];
         for (int r = 1; r < m->tp; ++r) s = s + m->part[(size_t)r * n + i];

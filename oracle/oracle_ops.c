@@ -760,12 +760,19 @@ static void* mm_worker(void* arg) {
 }
 
 void orc_matmul(int wtype, const void* w, int64_t n_rows, int k, const void* xq, float* y, int n_threads) {
+    orc_matmul_strided(wtype, w, n_rows, orc_row_bytes(wtype, k), k, xq, y, n_threads);
+}
+
+/* orc_matmul over rows row_stride bytes apart (a column slice of a wider
+ * matrix: its rows start row_stride bytes apart and hold k values). */
+void orc_matmul_strided(int wtype, const void* w, int64_t n_rows, size_t row_stride, int k, const void* xq, float* y,
+                        int n_threads) {
     if (n_threads < 1) n_threads = 1;
     if (n_threads > 256) n_threads = 256;
     if ((int64_t)n_threads > n_rows) n_threads = (int)n_rows;
     mm_job jobs[256];
     pthread_t th[256];
-    const size_t rb = orc_row_bytes(wtype, k);
+    const size_t rb = row_stride;
     for (int t = 0; t < n_threads; ++t) {
         jobs[t].wtype = wtype;
         jobs[t].w = (const uint8_t*)w;

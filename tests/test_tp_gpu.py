@@ -2,9 +2,9 @@
 
 The ranks exchange the attention-out / FFN-down partial outputs and the
 head's logit shards through peer memory and sum the partials in rank order,
-so the result is deterministic and the oracle reproduces it: its forward in
-the kernels' order with the same two column-slice partials per row-split
-projection (orc_model_set_tp).  Both ranks' logits must equal the oracle's
+so the result is deterministic and the oracle reproduces it: its
+reference-order forward with the same two column-slice partials per
+row-split projection, each slice in block order (orc_model_set_tp).  Both ranks' logits must equal the oracle's
 bit for bit, prefill and greedy steps, host loop and device loop alike."""
 import os
 import subprocess
@@ -67,7 +67,6 @@ def test_tp2_bit_exact_with_oracle(tmp_path, name):
                               _bits(res[1][key]) if res[1][key].dtype == np.float32 else res[1][key]), key
 
     om = O.Model(path)
-    om.set_device_order(True)
     om.set_tp(2)
     om.init_cache(2, 64)
     for p, t in enumerate(W.PROMPT):
