@@ -8,28 +8,33 @@
 // every multiply and add a separately rounded fp32 operation, expf the host
 // library's (b2_expf_ref), so every output is bit-identical to the
 // reference's CPU result.  The sums are sequential chains; the work is laid
-// out so that as many chains as possible run side by side.
+// out so that as many chains as possible run side by side and no chain
+// waits on global-memory latency.
+//
+// Scratch per (query, kv head) group: the scores S [G][capS] (capS = cap
+// rounded up to 4) and the probabilities P [capS][GP] (GP = max(G, 4)).
 //
 // Two kernels:
 //   * attn_scores_kernel: one CTA per (128-position chunk, kv head, query).
-//     The chunk's K rows arrive by 1-D bulk copies (one per row, into rows
-//     padded by 16 bytes so the per-thread row reads do not collide on
-//     banks) while q goes to shared memory;
-//     thread t scores position t against the G query heads of the group
-//     (G chains over the dims, two heads per packed f32x2 multiply and add)
-//     and writes s_t to the score buffer.  The last CTA of each (query, kv
-//     head) to finish then runs the softmax of those G heads over all
-//     positions: the maximum, e_t (three warps compute a chunk of e while
-//     lanes 0..G-1 of warp 0 add the previous chunk into the sums, double
-//     buffered), 1/l, and p_t written back over the scores.
+//     The chunk's K rows arrive by 1-D bulk copies (one per run of
+//     consecutive cache slots: the pinned prefix, the ring's tail, its head)
+//     while q goes to shared memory; thread t scores position t against the
+//     G query heads of the group (G chains over the dims, two heads per
+//     packed f32x2 operation) and writes s_t.  The last CTA of each (query,
+//     kv head) to finish runs the softmax of those G heads: windows of the
+//     score rows come into shared memory by bulk copies, the maximum and
+//     e_t are computed there by all threads, lanes 0..G-1 add e_t in
+//     position order, and p_t = e_t·(1/l) goes to P.
 //   * attn_pv_kernel: one CTA per (slice of 64/G dims, kv head, query).  A
-//     loader warp stages p_t (as pairs) and the V slice (converted to fp32)
-//     for chunks of up to 128 positions into three buffers; the chain warp's lane
+//     loader warp brings each chunk of up to 128 positions in with one 2-D
+//     tensor copy of the V slice and one bulk copy of the P rows, then turns
+//     V into fp32 and p_t into (p_t, p_t) pairs; the chain warp's lane
 //     (head, dim pair) runs out += p_t·v_t over the positions in order with
-//     packed f32x2 multiplies and adds.  Launched with programmatic dependent
-//     launch, it prefetches its V rows into L2 while the scores finish.
+//     packed f32x2 operations.
 // Queries whose sequence id or position is outside the cache attend to
 // nothing and get zero outputs.  Every wait is bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <float.h>
 
 #include "b2_common.cuh"
@@ -38,8 +43,15 @@
 namespace b2 {
 namespace {
 
-constexpr int kScoreP = 128;     // positions per scores CTA (one per thread)
-constexpr int kSoftCh = 512;     // positions per softmax chunk
+constexpr int kScoreP = 128;          // positions per scores CTA (one per thread)
+constexpr int kWinFloats = 8192;      // softmax window: G x W floats in shared memory
+constexpr int kPvCh = 128;            // positions per P.V chunk
+constexpr int kPvStages = 4;
+
+__host__ __device__ constexpr int gp_of(int g) { return g < 4 ? 4 : g; }
+__host__ __device__ inline int cap_s(int cap) { return (cap + 3) & ~3; }
+// floats of one (query, kv head) group: S [G][capS] then P [capS][GP]
+__host__ __device__ inline int64_t group_floats(int g, int cap) { return (int64_t)cap_s(cap) * (g + gp_of(g)); }
 
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
   uint64_t r;
@@ -73,11 +85,21 @@ __device__ __forceinline__ int query_positions(const int32_t* pos, const int32_t
   return (s >= 0 && s < n_seq && p >= 0 && p < cap) ? p + 1 : 0;
 }
 
-// Named barriers of the softmax's double buffer: full[buf] = 1 + buf,
-// empty[buf] = 3 + buf, each over the CTA's 128 threads.
-__device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-__device__ __forceinline__ void bar_arrive(int id, int n) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+// A run of logical positions starting at p that sit in consecutive cache
+// slots: within the pinned prefix, or within the ring up to its end.
+struct SlotRun {
+  int p, len;
+  int64_t slot;
+};
+__device__ __forceinline__ SlotRun slot_run(const KvSeqState& st, int p, int end, int cap, int max_len) {
+  SlotRun r;
+  r.p = p;
+  r.slot = kv_slot(st, p, cap);
+  int len = min(max_len, end - p);
+  if (p < st.n_keep) len = min(len, st.n_keep - p);
+  else len = (int)min((int64_t)len, (int64_t)cap - r.slot);
+  r.len = len;
+  return r;
 }
 
 template <int HD, int G>
@@ -90,13 +112,16 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
                                                               unsigned int* __restrict__ count, int* status,
                                                               float one, float neg_zero) {
   constexpr int P = kScoreP;
-  constexpr int NP = (G + 1) / 2;                     // head pairs (the last one half used when G is odd)
+  constexpr int NP = (G + 1) / 2;              // head pairs (the last one half used when G is odd)
+  constexpr int GP = gp_of(G);
+  constexpr int W = (kWinFloats / G) & ~3;     // softmax window positions
+  constexpr int KB = P * HD * 2;               // K rows of the chunk
+  constexpr int RB = KB > kWinFloats * 4 ? KB : kWinFloats * 4;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  constexpr int KS = HD * 2 + 16;                     // K row stride in bytes (bank skew)
-  uint8_t* ks = smem + 128;                                      // [P] rows of KS bytes
-  uint64_t* qs = reinterpret_cast<uint64_t*>(ks + P * KS);       // [HD][NP]: (q_2j[i], q_2j+1[i])
-  float* ebuf = reinterpret_cast<float*>(qs + HD * NP);          // softmax: [2][G][kSoftCh]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);    // [0] K rows, [1] softmax windows
+  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);   // [P][HD] (scores phase)
+  float* ws = reinterpret_cast<float*>(smem + 128);         // [G][W] (softmax phase, same bytes)
+  uint64_t* qs = reinterpret_cast<uint64_t*>(smem + 128 + RB);   // [HD][NP]: (q_2j[i], q_2j+1[i])
   __shared__ float mh[4][G];
   __shared__ float inv_l[G];
   __shared__ unsigned int last_cta;
@@ -110,16 +135,22 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = chunk * P, n = min(P, n_pos - t0);
   const int hq0 = kh * G;
-  float* srow = sbuf + ((int64_t)b * n_head + hq0) * cap;   // head g's scores at srow + g * cap
+  const int capS = cap_s(cap);
+  float* grp = sbuf + ((int64_t)b * n_kv + kh) * group_floats(G, cap);
+  float* srow = grp;                           // head g's scores at srow + g * capS
+  float* prow = grp + (int64_t)G * capS;       // position t's probabilities at prow + t * GP
   const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
   if (tid == 0) {
     mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * HD * 2));
-    // one bulk copy per position, into rows of KS bytes
     const int64_t base = ((int64_t)s * n_kv + kh) * cap;
-    for (int p = t0; p < t0 + n; ++p)
-      bulk_g2s(ks + (p - t0) * KS, kc + (base + kv_slot(sst, p, cap)) * HD, (uint32_t)(HD * 2), &bar[0]);
+    for (int p = t0; p < t0 + n;) {
+      const SlotRun r = slot_run(sst, p, t0 + n, cap, P);
+      bulk_g2s(ks + (p - t0) * HD, kc + (base + r.slot) * HD, (uint32_t)(r.len * HD * 2), &bar[0]);
+      p += r.len;
+    }
   }
   // q of the G heads, as head pairs, while the copies fly
   {
@@ -134,11 +165,10 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   __syncthreads();
   bool ok = mbar_wait_bounded(&bar[0], 0, status, 5);
   if (ok && tid < n) {
-    // the row of position t0 + tid (the KS stride puts the 8 rows of a
-    // quarter warp on different banks), then the chains in dim order
+    // the row of position t0 + tid, then the chains in dim order
     constexpr int NPc = HD / 8;
     const Ones k2{pack2(one, one), pack2(neg_zero, neg_zero)};
-    const uint8_t* rp = ks + tid * KS;
+    const uint8_t* rp = reinterpret_cast<const uint8_t*>(ks + tid * HD);
     uint64_t acc[NP];
 #pragma unroll
     for (int j = 0; j < NP; ++j) acc[j] = 0ull;   // (+0, +0)
@@ -160,8 +190,8 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
     for (int j = 0; j < NP; ++j) {
       float lo, hi;
       unpack2(acc[j], lo, hi);
-      srow[(int64_t)(2 * j) * cap + t] = __fmul_rn(lo, scale);
-      if (2 * j + 1 < G) srow[(int64_t)(2 * j + 1) * cap + t] = __fmul_rn(hi, scale);
+      srow[(int64_t)(2 * j) * capS + t] = __fmul_rn(lo, scale);
+      if (2 * j + 1 < G) srow[(int64_t)(2 * j + 1) * capS + t] = __fmul_rn(hi, scale);
     }
   }
   // The last CTA of this (query, kv head) runs the softmax over all positions.
@@ -175,163 +205,230 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   __syncthreads();
   if (!last_cta) return;
   __threadfence();
+  const int n_win = (n_pos + W - 1) / W;
+  uint32_t round = 0;
+  // Brings window w of the G score rows into ws [G][W] (a bulk copy per row;
+  // rows start on 16 bytes and the length rounds up to 4 floats inside capS).
+  auto load_window = [&](int w) -> bool {
+    const int p0 = w * W, len = min(W, n_pos - p0), len4 = (len + 3) & ~3;
+    __syncthreads();   // every thread is done with the previous window
+    if (tid == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(&bar[1], (uint32_t)(G * len4 * 4));
+      for (int g = 0; g < G; ++g) bulk_g2s(ws + g * W, srow + (int64_t)g * capS + p0, (uint32_t)(len4 * 4), &bar[1]);
+    }
+    const bool r = mbar_wait_bounded(&bar[1], round & 1, status, 9);
+    ++round;
+    return r;
+  };
   // m: any order (a maximum)
-  {
-    float m[G];
+  float mg[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) m[g] = -FLT_MAX;
-    for (int t = tid; t < n_pos; t += P) {
+  for (int g = 0; g < G; ++g) mg[g] = -FLT_MAX;
+  for (int w = 0; w < n_win && ok; ++w) {
+    ok = load_window(w);
+    const int len = min(W, n_pos - w * W);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float v = __ldcg(srow + (int64_t)g * cap + t);
-        if (v > m[g]) m[g] = v;
+    for (int g = 0; g < G; ++g)
+      for (int t = tid; t < len; t += P) {
+        const float v = ws[g * W + t];
+        if (v > mg[g]) mg[g] = v;
       }
-    }
+  }
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+  for (int g = 0; g < G; ++g) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
-      if (lane == 0) mh[warp][g] = m[g];
-    }
+    for (int o = 16; o > 0; o >>= 1) mg[g] = fmaxf(mg[g], __shfl_xor_sync(0xffffffffu, mg[g], o));
+    if (lane == 0) mh[warp][g] = mg[g];
   }
   __syncthreads();
-  if (tid < G) mh[0][tid] = fmaxf(fmaxf(mh[0][tid], mh[1][tid]), fmaxf(mh[2][tid], mh[3][tid]));
-  __syncthreads();
-  const float* mg = mh[0];
-  // e_t by warps 1..3 into the double buffer (and over the scores); the sums
-  // by lanes 0..G-1 of warp 0, positions in order.
-  const int n_sc = (n_pos + kSoftCh - 1) / kSoftCh;
-  if (warp == 0) {
-    float l = 0.0f;
-    for (int c = 0; c < n_sc; ++c) {
-      const int buf = c & 1, len = min(kSoftCh, n_pos - c * kSoftCh);
-      bar_sync(1 + buf, P);   // full
-      if (lane < G) {
-        const float* e = ebuf + (buf * G + lane) * kSoftCh;
-        int i = 0;
-        for (; i + 4 <= len; i += 4) {
-          const float4 v = *reinterpret_cast<const float4*>(e + i);
-          l = __fadd_rn(l, v.x);
-          l = __fadd_rn(l, v.y);
-          l = __fadd_rn(l, v.z);
-          l = __fadd_rn(l, v.w);
-        }
-        for (; i < len; ++i) l = __fadd_rn(l, e[i]);
+#pragma unroll
+  for (int g = 0; g < G; ++g) mg[g] = fmaxf(fmaxf(mh[0][g], mh[1][g]), fmaxf(mh[2][g], mh[3][g]));
+  // e_t in the window (all threads), then the sums in position order (lanes 0..G-1)
+  float l = 0.0f;
+  for (int w = 0; w < n_win && ok; ++w) {
+    if (n_win > 1) ok = load_window(w);
+    const int len = min(W, n_pos - w * W);
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      for (int t = tid; t < len; t += P) ws[g * W + t] = b2_expf_ref(__fsub_rn(ws[g * W + t], mg[g]));
+    __syncthreads();
+    if (tid < G) {
+      const float* e = ws + tid * W;
+      int i = 0;
+      for (; i + 4 <= len; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(e + i);
+        l = __fadd_rn(l, v.x);
+        l = __fadd_rn(l, v.y);
+        l = __fadd_rn(l, v.z);
+        l = __fadd_rn(l, v.w);
       }
-      __syncwarp();
-      bar_arrive(3 + buf, P);   // empty
+      for (; i < len; ++i) l = __fadd_rn(l, e[i]);
     }
-    if (lane < G) inv_l[lane] = __fdiv_rn(1.0f, l);
-  } else {
-    const int ptid = tid - 32;   // 96 producer threads
-    for (int c = 0; c < n_sc; ++c) {
-      const int buf = c & 1, base = c * kSoftCh, len = min(kSoftCh, n_pos - base);
-      if (c >= 2) bar_sync(3 + buf, P);   // the chain has read this buffer
-      for (int i = ptid; i < G * kSoftCh; i += P - 32) {
-        const int g = i / kSoftCh, j = i - g * kSoftCh;
-        if (j < len) {
-          float* sp = srow + (int64_t)g * cap + base + j;
-          const float e = b2_expf_ref(__fsub_rn(__ldcg(sp), mg[g]));
-          ebuf[(buf * G + g) * kSoftCh + j] = e;
-          *sp = e;
-        }
-      }
-      bar_arrive(1 + buf, P);   // full
-    }
-    // pair the chain's releases of the last two chunks
-    for (int c = max(0, n_sc - 2); c < n_sc; ++c) bar_sync(3 + (c & 1), P);
   }
+  if (tid < G) inv_l[tid] = __fdiv_rn(1.0f, l);
   __syncthreads();
-  // p_t = e_t · (1/l) over the scores
-  for (int i = tid; i < G * n_pos; i += P) {
-    const int g = i / n_pos, t = i - g * n_pos;
-    float* sp = srow + (int64_t)g * cap + t;
-    *sp = __fmul_rn(__ldcg(sp), inv_l[g]);
+  // p_t = e_t · (1/l) into P [t][GP]
+  for (int w = 0; w < n_win && ok; ++w) {
+    const int p0 = w * W, len = min(W, n_pos - p0);
+    if (n_win > 1) {
+      ok = load_window(w);
+      __syncthreads();
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        for (int t = tid; t < len; t += P) ws[g * W + t] = b2_expf_ref(__fsub_rn(ws[g * W + t], mg[g]));
+      __syncthreads();
+    }
+    for (int i = tid; i < len * G; i += P) {
+      const int t = i / G, g = i - t * G;
+      prow[(int64_t)(p0 + t) * GP + g] = __fmul_rn(ws[g * W + t], inv_l[g]);
+    }
   }
 }
 
-// out[b][h][d] for the dims [slice*DS, slice*DS+DS) of the G heads of one kv head.
+// 2-D tiled TMA load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+template <int G>
+__host__ __device__ constexpr size_t pv_stage_bytes(int ds) {
+  // raw V (fp16) | raw P [CH][GP] | V fp32 | P pairs [CH][G]
+  return (size_t)kPvCh * ds * 2 + (size_t)kPvCh * gp_of(G) * 4 + (size_t)kPvCh * ds * 4 + (size_t)kPvCh * G * 8;
+}
+
+// out[b][h][d] for the dims [slice*DS, slice*DS+DS) of the G heads of one kv
+// head.  Warp 1: lane 0 issues each chunk's V rows (one 2-D tensor copy of
+// kPvCh rows x DS dims from the first slot of a run) and P rows (one bulk
+// copy) into a raw stage; the warp converts V to fp32 and P to (p, p)
+// pairs.  Warp 0: lane (head g, dim pair j) runs out += p_t·v_t over the
+// positions in order.
 template <int HD, int G>
 __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__ pos, const int32_t* __restrict__ seq,
-                                                     const uint16_t* __restrict__ vc,
+                                                     const __grid_constant__ CUtensorMap vmap,
                                                      const KvSeqState* __restrict__ st, int n_seq, int n_head,
-                                                     int n_kv, int cap, const float* __restrict__ pbuf,
-                                                     float* __restrict__ out, float one, float neg_zero) {
+                                                     int n_kv, int cap, const float* __restrict__ sbuf,
+                                                     float* __restrict__ out, int* status, float one, float neg_zero) {
   constexpr int DS = 64 / G;            // dims of the slice: G heads x DS/2 pairs = 32 chain lanes
-  constexpr int CH = (2048 / DS) < 128 ? (2048 / DS) : 128;   // positions per chunk
-  constexpr int NBUF = 3;               // chunks in flight (barrier ids 1..3 full, 4..6 empty)
-  constexpr int PST = CH + 4;           // pairs per head row (bank skew)
-  constexpr int PIECES = DS / 8;        // 16-byte pieces of fp16 per position
+  constexpr int CH = kPvCh, NS = kPvStages;
+  constexpr int GP = gp_of(G);
   static_assert(HD % DS == 0 && DS % 8 == 0, "slice");
-  __shared__ __align__(16) uint64_t pp[NBUF][G][PST];   // (p_t, p_t)
-  __shared__ __align__(16) float vv[NBUF][CH][DS];       // V slice, fp32
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);   // [NS] raw stage landed
+  uint64_t* conv = full + NS;                           // [NS] converted
+  uint64_t* empty = conv + NS;                          // [NS] chain done with the stage
+  constexpr size_t SB = pv_stage_bytes<G>(DS);
+  uint8_t* stages = smem + 128;
   const int slice = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&conv[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
   const int s_q = seq[b], p_q = pos[b];
   const int n_pos = (s_q >= 0 && s_q < n_seq && p_q >= 0 && p_q < cap) ? p_q + 1 : 0;
   const KvSeqState sst = (n_pos && st) ? st[s_q] : KvSeqState{0, 0};
-  const int64_t vbase = n_pos ? ((int64_t)s_q * n_kv + kh) * cap : 0;
+  const int row0 = n_pos ? (s_q * n_kv + kh) * cap : 0;   // tensor-map row of slot 0
   const int d0 = slice * DS;
-  // V does not depend on the scores: bring this slice's rows towards L2 now.
-  if (warp == 1) {
-    for (int t = lane; t < n_pos; t += 32) {
-      const uint16_t* src = vc + (vbase + kv_slot(sst, t, cap)) * HD + d0;
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
-    }
-  }
   pdl_wait();
   pdl_launch_dependents();
-  const float* prow = pbuf + ((int64_t)b * n_head + kh * G) * cap;
-  const int n_c = (n_pos + CH - 1) / CH;
+  const float* prow = sbuf + ((int64_t)b * n_kv + kh) * group_floats(G, cap) + (int64_t)G * cap_s(cap);
+  bool ok = true;
   if (warp == 1) {
-    // loader: chunk c into buffer c % NBUF once the chain has released it
-    for (int c = 0; c < n_c; ++c) {
-      const int buf = c % NBUF, base = c * CH, len = min(CH, n_pos - base);
-      if (c >= NBUF) bar_sync(4 + buf, 64);
-#pragma unroll 4
-      for (int i = lane; i < len * PIECES; i += 32) {
-        const int t = i / PIECES, pc = i - t * PIECES;
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(vc + (vbase + kv_slot(sst, base + t, cap)) * HD + d0 +
-                                                              8 * pc));
-        const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
-        float* dst = &vv[buf][t][8 * pc];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          dst[2 * e] = h2f((uint16_t)(w4[e] & 0xFFFFu));
-          dst[2 * e + 1] = h2f((uint16_t)(w4[e] >> 16));
+    int p_iss = 0, c_iss = 0;
+    auto issue = [&](int si) {
+      const SlotRun r = slot_run(sst, p_iss, n_pos, cap, CH);
+      uint8_t* sp = stages + si * SB;
+      mbar_arrive_expect_tx(&full[si], (uint32_t)(CH * DS * 2 + r.len * GP * 4));
+      tma_load_2d(sp, &vmap, d0, row0 + (int)r.slot, &full[si]);
+      bulk_g2s(sp + CH * DS * 2, prow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
+      p_iss += r.len;
+      ++c_iss;
+    };
+    if (lane == 0)
+      while (p_iss < n_pos && c_iss < NS) issue(c_iss % NS);
+    __syncwarp();
+    int p = 0;
+    for (int c = 0; p < n_pos; ++c) {
+      const int si = c % NS;
+      const int len = slot_run(sst, p, n_pos, cap, CH).len;
+      if (ok) ok = mbar_wait_bounded(&full[si], (uint32_t)((c / NS) & 1), status, 6);
+      if (ok && c >= NS) ok = mbar_wait_bounded(&empty[si], (uint32_t)(((c / NS) - 1) & 1), status, 7);
+      if (ok) {
+        uint8_t* sp = stages + si * SB;
+        const uint32_t* rv = reinterpret_cast<const uint32_t*>(sp);
+        const float* rp = reinterpret_cast<const float*>(sp + CH * DS * 2);
+        float* fv = reinterpret_cast<float*>(sp + CH * DS * 2 + CH * GP * 4);
+        uint64_t* fp = reinterpret_cast<uint64_t*>(sp + CH * DS * 2 + CH * GP * 4 + CH * DS * 4);
+        for (int i = lane; i < len * DS / 2; i += 32) {
+          const uint32_t w2 = rv[i];
+          fv[2 * i] = h2f((uint16_t)(w2 & 0xFFFFu));
+          fv[2 * i + 1] = h2f((uint16_t)(w2 >> 16));
+        }
+        for (int i = lane; i < len * G; i += 32) {
+          const int t = i / G, g = i - t * G;
+          const float pv = rp[t * GP + g];
+          fp[i] = pack2(pv, pv);
         }
       }
-#pragma unroll 4
-      for (int i = lane; i < G * len; i += 32) {
-        const int g = i / len, t = i - g * len;
-        const float pv = __ldcg(prow + (int64_t)g * cap + base + t);
-        pp[buf][g][t] = pack2(pv, pv);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&conv[si]);
+        if (ok && p_iss < n_pos) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue(si);
+        }
       }
-      bar_arrive(1 + buf, 64);
+      __syncwarp();
+      p += len;
     }
-    // complete the chain's releases of the last NBUF chunks
-    for (int c = max(0, n_c - NBUF); c < n_c; ++c) bar_sync(4 + c % NBUF, 64);
+    // copies still in flight after a failed wait: wait for them (bounded)
+    if (!ok && lane == 0) {
+      int pp = 0;
+      for (int c = 0; pp < p_iss; ++c) {
+        const int si = c % NS;
+        pp += slot_run(sst, pp, n_pos, cap, CH).len;
+        mbar_wait_bounded(&full[si], (uint32_t)((c / NS) & 1), nullptr, 0);
+      }
+    }
     return;
   }
   // chain warp: lane = (head g, dim pair j)
   const int g = lane / (DS / 2), j = lane - g * (DS / 2);
   const Ones k2{pack2(one, one), pack2(neg_zero, neg_zero)};
   uint64_t acc = 0ull;
-  for (int c = 0; c < n_c; ++c) {
-    const int buf = c % NBUF, len = min(CH, n_pos - c * CH);
-    bar_sync(1 + buf, 64);
-    const uint64_t* pr = &pp[buf][g][0];
-    int t = 0;
-    for (; t + 2 <= len; t += 2) {
-      const ulonglong2 p2 = *reinterpret_cast<const ulonglong2*>(pr + t);
-      const uint64_t v0 = *reinterpret_cast<const uint64_t*>(&vv[buf][t][2 * j]);
-      const uint64_t v1 = *reinterpret_cast<const uint64_t*>(&vv[buf][t + 1][2 * j]);
-      acc = mul_add2(acc, p2.x, v0, k2);
-      acc = mul_add2(acc, p2.y, v1, k2);
+  int p = 0;
+  for (int c = 0; p < n_pos; ++c) {
+    const int si = c % NS;
+    const int len = slot_run(sst, p, n_pos, cap, CH).len;
+    if (ok) ok = mbar_wait_bounded(&conv[si], (uint32_t)((c / NS) & 1), status, 8);
+    if (ok) {
+      const uint8_t* sp = stages + si * SB;
+      const float* vr = reinterpret_cast<const float*>(sp + CH * DS * 2 + CH * GP * 4) + 2 * j;
+      const uint64_t* pr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4 + CH * DS * 4) + g;
+      int t = 0;
+      for (; t + 2 <= len; t += 2) {
+        const uint64_t p0 = pr[t * G], p1 = pr[(t + 1) * G];
+        const uint64_t v0 = *reinterpret_cast<const uint64_t*>(vr + t * DS);
+        const uint64_t v1 = *reinterpret_cast<const uint64_t*>(vr + (t + 1) * DS);
+        acc = mul_add2(acc, p0, v0, k2);
+        acc = mul_add2(acc, p1, v1, k2);
+      }
+      if (t < len) acc = mul_add2(acc, pr[t * G], *reinterpret_cast<const uint64_t*>(vr + t * DS), k2);
     }
-    if (t < len) acc = mul_add2(acc, pr[t], *reinterpret_cast<const uint64_t*>(&vv[buf][t][2 * j]), k2);
     __syncwarp();
-    bar_arrive(4 + buf, 64);
+    if (lane == 0) mbar_arrive(&empty[si]);
+    p += len;
   }
   float o0, o1;
   unpack2(acc, o0, o1);
@@ -340,29 +437,66 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
   op[1] = o1;
 }
 
+// The V cache as a 2-D tensor [n_seq*n_kv*cap rows][hd] of fp16, boxes of
+// kPvCh rows x ds dims.
+int make_v_map(const uint16_t* vc, int64_t n_rows, int hd, int ds, CUtensorMap* map) {
+  static PFN_cuTensorMapEncodeTiled encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) != cudaSuccess || !fn) {
+      set_error("attention: cuTensorMapEncodeTiled unavailable");
+      return B2_ERR_CUDA;
+    }
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)n_rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)ds, (cuuint32_t)kPvCh};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(vc), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("attention: V tensor map rejected (CUresult %d)", (int)r);
+    return B2_ERR_CUDA;
+  }
+  return B2_OK;
+}
+
 template <int HD, int G>
 int launch_hd_g(const float* q, int n_tok, int n_head, int n_kv, const int32_t* pos, const int32_t* seq,
                 const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scores,
                 unsigned int* count, float* out, cudaStream_t s, int* status) {
   constexpr int NP = (G + 1) / 2;
-  const size_t sm = 128 + (size_t)kScoreP * (HD * 2 + 16) + (size_t)HD * NP * 8 + (size_t)2 * G * kSoftCh * 4;
+  constexpr int DS = 64 / G;
+  constexpr size_t KB = (size_t)kScoreP * HD * 2, RB = KB > kWinFloats * 4 ? KB : (size_t)kWinFloats * 4;
+  const size_t sm = 128 + RB + (size_t)HD * NP * 8;
   B2_CUDA_TRY(cudaFuncSetAttribute(attn_scores_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   const float scale = 1.0f / sqrtf((float)HD);
   int rc = launch_pdl(attn_scores_kernel<HD, G>, dim3((cap + kScoreP - 1) / kScoreP, n_kv, n_tok), dim3(kScoreP), sm,
                       s, q, n_head, n_kv, pos, seq, kc, st, n_seq, cap, scale, scores, count, status, 1.0f, -0.0f);
   if (rc) return rc;
-  return launch_pdl(attn_pv_kernel<HD, G>, dim3(HD / (64 / G), n_kv, n_tok), dim3(64), 0, s, pos, seq, vc, st, n_seq,
-                    n_head, n_kv, cap, (const float*)scores, out, 1.0f, -0.0f);
+  CUtensorMap vmap;
+  if ((rc = make_v_map(vc, (int64_t)n_seq * n_kv * cap, HD, DS, &vmap))) return rc;
+  const size_t smv = 128 + (size_t)kPvStages * pv_stage_bytes<G>(DS);
+  B2_CUDA_TRY(cudaFuncSetAttribute(attn_pv_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smv));
+  return launch_pdl(attn_pv_kernel<HD, G>, dim3(HD / DS, n_kv, n_tok), dim3(64), smv, s, pos, seq, vmap, st, n_seq,
+                    n_head, n_kv, cap, (const float*)scores, out, status, 1.0f, -0.0f);
 }
 
 }  // namespace
 
-size_t attn_scratch_floats(int n_tok, int n_head, int cap) { return (size_t)n_tok * n_head * cap; }
+size_t attn_scratch_floats(int n_tok, int n_head, int n_kv, int cap) {
+  const int G = n_kv > 0 ? n_head / n_kv : 1;
+  return (size_t)n_tok * n_kv * (size_t)group_floats(G, cap);
+}
 
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                      const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scores,
                      unsigned int* count, float* out, cudaStream_t s, int* status) {
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0 && scores && count && out && cap > 0, "attention arguments");
+  B2_CHECK_ARG((reinterpret_cast<uintptr_t>(scores) & 15) == 0, "attention scratch must be 16-byte aligned");
   const int G = n_head / n_kv;
 #define B2_ATTN_CASE(HDV, GV) \
   if (hd == HDV && G == GV)   \

@@ -454,7 +454,7 @@ int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_ca
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
   cudaStream_t s = as_stream(stream);
   // scores / probabilities, then the arrival counters (zeroed here)
-  const size_t nsc = attn_scratch_floats(n_q, n_head, cap);
+  const size_t nsc = attn_scratch_floats(n_q, n_head, n_kv, cap);
   const size_t ncnt = (size_t)n_q * n_kv;
   void* scratch = nullptr;
   B2_CUDA_TRY(cudaMallocAsync(&scratch, (nsc + ncnt) * 4, s));

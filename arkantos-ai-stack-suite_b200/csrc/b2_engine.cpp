@@ -512,7 +512,7 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
       (rc = dalloc(c, &c->q, (size_t)T * m->nh_l * hd)) || (rc = dalloc(c, &c->att, (size_t)T * m->nh_l * hd)) ||
       (rc = dalloc(c, &c->h, (size_t)T * m->ff_l)) ||
       (m->tp_size == 1 && (rc = dalloc(c, &c->logits, (size_t)T * m->n_vocab))) ||
-      (rc = dalloc(c, &c->scores, attn_scratch_floats(T, m->nh_l, c->n_ctx))) || (rc = dalloc(c, &c->res, kResWords)) ||
+      (rc = dalloc(c, &c->scores, attn_scratch_floats(T, m->nh_l, m->nkv_l, c->n_ctx))) || (rc = dalloc(c, &c->res, kResWords)) ||
       (rc = dalloc(c, &c->gen_out, (size_t)c->n_ctx * T)) || (rc = dalloc(c, &c->gen_count, T)))
     return rc;
   {
@@ -768,7 +768,7 @@ int prefill_alloc(b2_context* c) {
   b2_model* m = c->model;
   const int d = m->n_embd, hd = m->head_dim, qkv_w = (m->nh_l + 2 * m->nkv_l) * hd, nq = m->nh_l * hd;
   const size_t per_tok = 4 * ((size_t)3 * d + qkv_w + 2 * (size_t)nq + 3 * (size_t)m->ff_l +
-                              attn_scratch_floats(1, m->nh_l, c->n_ctx) + m->nkv_l + 3);
+                              attn_scratch_floats(1, m->nh_l, m->nkv_l, c->n_ctx) + m->nkv_l + 3);
   const int cap = (int)std::max<size_t>(kPrefillMin, std::min<size_t>(kPrefillCapMax, kPrefillBudget / per_tok));
   size_t ws = 0;
   for (const auto& L : m->layers)
@@ -780,7 +780,7 @@ int prefill_alloc(b2_context* c) {
       (rc = dalloc(c, &c->pf_qkv, (size_t)cap * qkv_w)) || (rc = dalloc(c, &c->pf_q, (size_t)cap * nq)) ||
       (rc = dalloc(c, &c->pf_att, (size_t)cap * nq)) || (rc = dalloc(c, &c->pf_gu, (size_t)cap * 2 * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_h, (size_t)cap * m->ff_l)) ||
-      (rc = dalloc(c, &c->pf_scores, attn_scratch_floats(cap, m->nh_l, c->n_ctx))) ||
+      (rc = dalloc(c, &c->pf_scores, attn_scratch_floats(cap, m->nh_l, m->nkv_l, c->n_ctx))) ||
       (rc = dalloc(c, &c->pf_attn_cnt, (size_t)cap * m->nkv_l)) || (rc = dalloc(c, &c->pf_ws, ws))) {
     // A context short of memory keeps none of the chunk buffers: free the
     // ones this call took (nothing has been enqueued on them).

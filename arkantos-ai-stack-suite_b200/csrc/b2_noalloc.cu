@@ -68,7 +68,7 @@ extern "C" int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, c
     return B2_ERR_INVALID;
   }
   // [scores / probabilities][arrival counters]
-  const size_t sc_bytes = attn_scratch_floats(n_q, n_head, cap) * sizeof(float);
+  const size_t sc_bytes = attn_scratch_floats(n_q, n_head, n_kv, cap) * sizeof(float);
   const size_t cnt_off = (sc_bytes + 255) / 256 * 256;
   const size_t cnt_bytes = (size_t)n_q * n_kv * sizeof(unsigned int);
   if (cnt_off + cnt_bytes > kScratchBytes) {

@@ -249,14 +249,16 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
  * Same arguments and results as b2_attn_decode; the scores and the arrival
  * counters live in one static device array of B2_NOALLOC_SCRATCH_BYTES that
  * every GPU loading the library holds until exit.  Limits: n_q <=
- * B2_NOALLOC_MAX_QUERIES and n_q·n_head·cap·4 bytes (+ n_q·n_kv counters)
- * within the array (larger requests return B2_ERR_INVALID).  The first
+ * B2_NOALLOC_MAX_QUERIES and the scores and probabilities, n_q·n_kv·capS·
+ * (G + max(G, 4))·4 bytes with G = n_head/n_kv and capS = cap rounded up to
+ * 4 (2·n_q·n_head·cap·4 for G >= 4), plus n_q·n_kv counters, within the
+ * array (larger requests return B2_ERR_INVALID).  The first
  * call on a device looks up the array's address (call it once before any
  * stream capture); calls outside capture look it up again, so a device reset
  * between calls is picked up, while a call under capture uses the address
  * seen last.  Calls share the array: calls that overlap on the GPU race and
  * must be serialized by the caller. */
-#define B2_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+#define B2_NOALLOC_SCRATCH_BYTES (32 * 1024 * 1024)
 #define B2_NOALLOC_MAX_QUERIES 64
 B2_API int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
                                   const int32_t* pos, const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv,

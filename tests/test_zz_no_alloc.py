@@ -43,7 +43,7 @@ def test_noalloc_attention_matches_allocating_entry_point_twice(n_q, cap, n_head
 
 
 def test_noalloc_attention_rejects_oversize_requests():
-    n_q, n_head, n_kv, hd, cap = 64, 32, 8, 128, 8192      # 64·32·64·130·4 bytes (~68 MB) > the built-in scratch
+    n_q, n_head, n_kv, hd, cap = 64, 32, 8, 128, 8192      # 2·64·32·8192·4 bytes (~134 MB) > the built-in scratch
     q = np.zeros((n_q, n_head * hd), np.float32)
     kc = np.zeros((1, n_kv, cap, hd), np.uint16)
     pos = np.zeros(n_q, np.int32)
