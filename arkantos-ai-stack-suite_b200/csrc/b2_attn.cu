@@ -7,30 +7,34 @@
 //   p_t = e_t · (1/l);  out_i = Σ_t p_t·v_ti (positions in order)
 // every multiply and add a separately rounded fp32 operation, expf the host
 // library's (b2_expf_ref), so every output is bit-identical to the
-// reference's CPU result.  The sums are sequential chains; the work is laid
-// out so that as many chains as possible run side by side and no chain
-// waits on global-memory latency.
+// reference's CPU result.  The sums over positions are sequential chains:
+// the work is laid out so that as many chains as possible run side by side,
+// every chain reads shared memory that was filled ahead of it, and nothing
+// but the chains themselves is serial.
 //
-// Scratch per (query, kv head) group: the scores S [G][capS] (capS = cap
-// rounded up to 4) and the probabilities P [capS][GP] (GP = max(G, 4)).
+// Scratch per (query, kv head) group, in floats: the scores S [G][capS]
+// (capS = cap rounded up to 4), the exponentials E [capS][GP] (GP = max(G,
+// 4): one 16-byte-aligned row per position), and the chunk maxima M [G][nchS]
+// (nchS = the number of 128-position chunks rounded up to 4).
 //
-// Two kernels:
+// Three kernels:
 //   * attn_scores_kernel: one CTA per (128-position chunk, kv head, query).
 //     The chunk's K rows arrive by 1-D bulk copies (one per run of
 //     consecutive cache slots: the pinned prefix, the ring's tail, its head)
 //     while q goes to shared memory; thread t scores position t against the
-//     G query heads of the group (G chains over the dims, two heads per
-//     packed f32x2 operation) and writes s_t.  The last CTA of each (query,
-//     kv head) to finish runs the softmax of those G heads: windows of the
-//     score rows come into shared memory by bulk copies, the maximum and
-//     e_t are computed there by all threads, lanes 0..G-1 add e_t in
-//     position order, and p_t = e_t·(1/l) goes to P.
-//   * attn_pv_kernel: one CTA per (slice of 64/G dims, kv head, query).  A
-//     loader warp brings each chunk of up to 128 positions in with one 2-D
-//     tensor copy of the V slice and one bulk copy of the P rows, then turns
-//     V into fp32 and p_t into (p_t, p_t) pairs; the chain warp's lane
-//     (head, dim pair) runs out += p_t·v_t over the positions in order with
-//     packed f32x2 operations.
+//     G query heads (two heads per packed f32x2 operation) and writes s_t;
+//     the CTA writes the chunk's maximum per head.
+//   * attn_exp_kernel: one CTA per (chunk, kv head, query): m from the chunk
+//     maxima (a maximum: any order), then e_t = expf(s_t − m) for every
+//     position of the chunk and head into E.
+//   * attn_pv_kernel: one CTA per (slice of 64/G dims, kv head, query).
+//     First lanes 0..G-1 add e_t in position order (windows of E arrive by
+//     bulk copies, in parts the chain starts on as each lands) and take
+//     1/l.  Then a loader warp brings each chunk of up to 128 positions in
+//     with one 2-D tensor copy of the V slice and one bulk copy of the E
+//     rows, turns V into fp32 and forms (p_t, p_t) = e_t·(1/l); the chain
+//     warp's lane (head, dim pair) runs out += p_t·v_t over the positions in
+//     order with packed f32x2 operations.
 // Queries whose sequence id or position is outside the cache attend to
 // nothing and get zero outputs.  Every wait is bounded.
 #include <cuda.h>
@@ -43,15 +47,20 @@
 namespace b2 {
 namespace {
 
-constexpr int kScoreP = 128;          // positions per scores CTA (one per thread)
-constexpr int kWinFloats = 8192;      // softmax window: G x W floats in shared memory
+constexpr int kScoreP = 128;          // positions per scores / exp CTA (one per thread)
 constexpr int kPvCh = 128;            // positions per P.V chunk
-constexpr int kPvStages = 4;
+constexpr int kPvStagesMax = 8;            // P.V stages per CTA: as many as the CTAs per SM leave room for
+constexpr int kSumParts = 4;          // bulk copies (and mbarriers) per window of the sum
 
 __host__ __device__ constexpr int gp_of(int g) { return g < 4 ? 4 : g; }
 __host__ __device__ inline int cap_s(int cap) { return (cap + 3) & ~3; }
-// floats of one (query, kv head) group: S [G][capS] then P [capS][GP]
-__host__ __device__ inline int64_t group_floats(int g, int cap) { return (int64_t)cap_s(cap) * (g + gp_of(g)); }
+__host__ __device__ inline int nch_s(int cap) { return ((cap + kScoreP - 1) / kScoreP + 3) & ~3; }
+// floats of one (query, kv head) group: S [G][capS], E [capS][GP], M [G][nchS]
+__host__ __device__ inline int64_t group_floats(int g, int cap) {
+  return (int64_t)cap_s(cap) * (g + gp_of(g)) + (int64_t)g * nch_s(cap);
+}
+__host__ __device__ inline int64_t e_offset(int g, int cap) { return (int64_t)g * cap_s(cap); }
+__host__ __device__ inline int64_t m_offset(int g, int cap) { return (int64_t)cap_s(cap) * (g + gp_of(g)); }
 
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
   uint64_t r;
@@ -108,23 +117,16 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
                                                               const int32_t* __restrict__ seq,
                                                               const uint16_t* __restrict__ kc,
                                                               const KvSeqState* __restrict__ st, int n_seq, int cap,
-                                                              float scale, float* __restrict__ sbuf,
-                                                              unsigned int* __restrict__ count, int* status,
+                                                              float scale, float* __restrict__ sbuf, int* status,
                                                               float one, float neg_zero) {
   constexpr int P = kScoreP;
   constexpr int NP = (G + 1) / 2;              // head pairs (the last one half used when G is odd)
-  constexpr int GP = gp_of(G);
-  constexpr int W = (kWinFloats / G) & ~3;     // softmax window positions
   constexpr int KB = P * HD * 2;               // K rows of the chunk
-  constexpr int RB = KB > kWinFloats * 4 ? KB : kWinFloats * 4;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);    // [0] K rows, [1] softmax windows
-  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);   // [P][HD] (scores phase)
-  float* ws = reinterpret_cast<float*>(smem + 128);         // [G][W] (softmax phase, same bytes)
-  uint64_t* qs = reinterpret_cast<uint64_t*>(smem + 128 + RB);   // [HD][NP]: (q_2j[i], q_2j+1[i])
-  __shared__ float mh[4][G];
-  __shared__ float inv_l[G];
-  __shared__ unsigned int last_cta;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);        // [P][HD]
+  uint64_t* qs = reinterpret_cast<uint64_t*>(smem + 128 + KB);   // [HD][NP]: (q_2j[i], q_2j+1[i])
+  __shared__ float mh[P / 32][G];
   pdl_wait();
   pdl_launch_dependents();
   const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -138,11 +140,10 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   const int capS = cap_s(cap);
   float* grp = sbuf + ((int64_t)b * n_kv + kh) * group_floats(G, cap);
   float* srow = grp;                           // head g's scores at srow + g * capS
-  float* prow = grp + (int64_t)G * capS;       // position t's probabilities at prow + t * GP
+  float* mrow = grp + m_offset(G, cap);        // head g's chunk maxima at mrow + g * nchS
   const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
   if (tid == 0) {
     mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * HD * 2));
     const int64_t base = ((int64_t)s * n_kv + kh) * cap;
@@ -163,7 +164,10 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
     }
   }
   __syncthreads();
-  bool ok = mbar_wait_bounded(&bar[0], 0, status, 5);
+  const bool ok = mbar_wait_bounded(&bar[0], 0, status, 5);
+  float sc[2 * NP];
+#pragma unroll
+  for (int j = 0; j < 2 * NP; ++j) sc[j] = -FLT_MAX;
   if (ok && tid < n) {
     // the row of position t0 + tid, then the chains in dim order
     constexpr int NPc = HD / 8;
@@ -190,100 +194,77 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
     for (int j = 0; j < NP; ++j) {
       float lo, hi;
       unpack2(acc[j], lo, hi);
-      srow[(int64_t)(2 * j) * capS + t] = __fmul_rn(lo, scale);
-      if (2 * j + 1 < G) srow[(int64_t)(2 * j + 1) * capS + t] = __fmul_rn(hi, scale);
+      sc[2 * j] = __fmul_rn(lo, scale);
+      sc[2 * j + 1] = __fmul_rn(hi, scale);
+      srow[(int64_t)(2 * j) * capS + t] = sc[2 * j];
+      if (2 * j + 1 < G) srow[(int64_t)(2 * j + 1) * capS + t] = sc[2 * j + 1];
     }
   }
-  // The last CTA of this (query, kv head) runs the softmax over all positions.
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const unsigned int prev = atomicAdd(&count[b * n_kv + kh], 1u);
-    last_cta = prev == (unsigned int)(n_ch - 1);
-    if (last_cta) count[b * n_kv + kh] = 0u;   // ready for the next launch
-  }
-  __syncthreads();
-  if (!last_cta) return;
-  __threadfence();
-  const int n_win = (n_pos + W - 1) / W;
-  uint32_t round = 0;
-  // Brings window w of the G score rows into ws [G][W] (a bulk copy per row;
-  // rows start on 16 bytes and the length rounds up to 4 floats inside capS).
-  auto load_window = [&](int w) -> bool {
-    const int p0 = w * W, len = min(W, n_pos - p0), len4 = (len + 3) & ~3;
-    __syncthreads();   // every thread is done with the previous window
-    if (tid == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive_expect_tx(&bar[1], (uint32_t)(G * len4 * 4));
-      for (int g = 0; g < G; ++g) bulk_g2s(ws + g * W, srow + (int64_t)g * capS + p0, (uint32_t)(len4 * 4), &bar[1]);
-    }
-    const bool r = mbar_wait_bounded(&bar[1], round & 1, status, 9);
-    ++round;
-    return r;
-  };
-  // m: any order (a maximum)
-  float mg[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) mg[g] = -FLT_MAX;
-  for (int w = 0; w < n_win && ok; ++w) {
-    ok = load_window(w);
-    const int len = min(W, n_pos - w * W);
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-      for (int t = tid; t < len; t += P) {
-        const float v = ws[g * W + t];
-        if (v > mg[g]) mg[g] = v;
-      }
-  }
+  // the chunk's maximum per head (a maximum: any order)
 #pragma unroll
   for (int g = 0; g < G; ++g) {
+    float v = sc[g];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mg[g] = fmaxf(mg[g], __shfl_xor_sync(0xffffffffu, mg[g], o));
-    if (lane == 0) mh[warp][g] = mg[g];
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) mh[warp][g] = v;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float v = mh[0][tid];
+#pragma unroll
+    for (int w = 1; w < P / 32; ++w) v = fmaxf(v, mh[w][tid]);
+    mrow[(int64_t)tid * nch_s(cap) + chunk] = v;
+  }
+}
+
+// e_t = expf(s_t − m) for the chunk's positions, m the maximum over all the
+// chunk maxima of the head.
+template <int G>
+__global__ void __launch_bounds__(kScoreP) attn_exp_kernel(const int32_t* __restrict__ pos,
+                                                           const int32_t* __restrict__ seq, int n_seq, int n_kv,
+                                                           int cap, float* __restrict__ sbuf) {
+  constexpr int P = kScoreP, GP = gp_of(G);
+  __shared__ unsigned long long tab[32];
+  __shared__ float mh[P / 32][G];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  int s;
+  const int n_pos = query_positions(pos, seq, b, n_seq, cap, &s);
+  const int n_ch = (n_pos + P - 1) / P;
+  if (chunk >= n_ch) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  exp_table_to_smem(tab, tid, P);
+  float* grp = sbuf + ((int64_t)b * n_kv + kh) * group_floats(G, cap);
+  const float* srow = grp;
+  float* erow = grp + e_offset(G, cap);
+  const float* mrow = grp + m_offset(G, cap);
+  const int capS = cap_s(cap), nchS = nch_s(cap);
+  float mg[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float v = -FLT_MAX;
+    for (int c = tid; c < n_ch; c += P) v = fmaxf(v, mrow[g * nchS + c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) mh[warp][g] = v;
   }
   __syncthreads();
 #pragma unroll
-  for (int g = 0; g < G; ++g) mg[g] = fmaxf(fmaxf(mh[0][g], mh[1][g]), fmaxf(mh[2][g], mh[3][g]));
-  // e_t in the window (all threads), then the sums in position order (lanes 0..G-1)
-  float l = 0.0f;
-  for (int w = 0; w < n_win && ok; ++w) {
-    if (n_win > 1) ok = load_window(w);
-    const int len = min(W, n_pos - w * W);
-    __syncthreads();
+  for (int g = 0; g < G; ++g) {
+    float v = mh[0][g];
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-      for (int t = tid; t < len; t += P) ws[g * W + t] = b2_expf_ref(__fsub_rn(ws[g * W + t], mg[g]));
-    __syncthreads();
-    if (tid < G) {
-      const float* e = ws + tid * W;
-      int i = 0;
-      for (; i + 4 <= len; i += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(e + i);
-        l = __fadd_rn(l, v.x);
-        l = __fadd_rn(l, v.y);
-        l = __fadd_rn(l, v.z);
-        l = __fadd_rn(l, v.w);
-      }
-      for (; i < len; ++i) l = __fadd_rn(l, e[i]);
-    }
+    for (int w = 1; w < P / 32; ++w) v = fmaxf(v, mh[w][g]);
+    mg[g] = v;
   }
-  if (tid < G) inv_l[tid] = __fdiv_rn(1.0f, l);
-  __syncthreads();
-  // p_t = e_t · (1/l) into P [t][GP]
-  for (int w = 0; w < n_win && ok; ++w) {
-    const int p0 = w * W, len = min(W, n_pos - p0);
-    if (n_win > 1) {
-      ok = load_window(w);
-      __syncthreads();
+  const int t = chunk * P + tid;
+  if (t < n_pos) {
+    float e[GP];
 #pragma unroll
-      for (int g = 0; g < G; ++g)
-        for (int t = tid; t < len; t += P) ws[g * W + t] = b2_expf_ref(__fsub_rn(ws[g * W + t], mg[g]));
-      __syncthreads();
-    }
-    for (int i = tid; i < len * G; i += P) {
-      const int t = i / G, g = i - t * G;
-      prow[(int64_t)(p0 + t) * GP + g] = __fmul_rn(ws[g * W + t], inv_l[g]);
-    }
+    for (int g = 0; g < GP; ++g) e[g] = g < G ? b2_expf_ref(__fsub_rn(srow[(int64_t)g * capS + t], mg[g]), tab) : 0.0f;
+    float4* dst = reinterpret_cast<float4*>(erow + (int64_t)t * GP);
+#pragma unroll
+    for (int v = 0; v < GP / 4; ++v) dst[v] = make_float4(e[4 * v], e[4 * v + 1], e[4 * v + 2], e[4 * v + 3]);
   }
 }
 
@@ -296,34 +277,77 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Rows of the converted stage hold kPvChP = kPvCh + 2 pairs: 16 bytes of
+// padding per row put the rows that the chain lanes read side by side on
+// different banks.
+constexpr int kPvChP = kPvCh + 2;
 template <int G>
 __host__ __device__ constexpr size_t pv_stage_bytes(int ds) {
-  // raw V (fp16) | raw P [CH][GP] | V fp32 | P pairs [CH][G]
-  return (size_t)kPvCh * ds * 2 + (size_t)kPvCh * gp_of(G) * 4 + (size_t)kPvCh * ds * 4 + (size_t)kPvCh * G * 8;
+  // raw V [CH][ds] fp16 | raw E [CH][GP] | V pairs [ds/2][CHP] | (p, p) pairs [G][CHP],
+  // rounded up to 128 bytes (the tensor copy's destination alignment)
+  return ((size_t)kPvCh * ds * 2 + (size_t)kPvCh * gp_of(G) * 4 + (size_t)(ds / 2) * kPvChP * 8 +
+          (size_t)G * kPvChP * 8 + 127) / 128 * 128;
+}
+__device__ __forceinline__ uint64_t u64_of(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+
+// l = Σ_t e_t in position order for lane g < G, over rows e[t * GP + g] of
+// shared memory: the next 16 values are read while the current 16 are added,
+// so no add waits on a load.
+template <int GP>
+__device__ __forceinline__ float sum_run(const float* e, int a, int b, float l) {
+  const int n16 = a + ((b - a) & ~15);
+  float cur[16], nxt[16];
+  if (n16 > a) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) cur[k] = e[(a + k) * GP];
+  }
+  for (int i = a; i < n16; i += 16) {
+    if (i + 16 < n16) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) nxt[k] = e[(i + 16 + k) * GP];
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) l = __fadd_rn(l, cur[k]);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) cur[k] = nxt[k];
+  }
+  for (int i = n16; i < b; ++i) l = __fadd_rn(l, e[i * GP]);
+  return l;
 }
 
 // out[b][h][d] for the dims [slice*DS, slice*DS+DS) of the G heads of one kv
-// head.  Warp 1: lane 0 issues each chunk's V rows (one 2-D tensor copy of
-// kPvCh rows x DS dims from the first slot of a run) and P rows (one bulk
-// copy) into a raw stage; the warp converts V to fp32 and P to (p, p)
-// pairs.  Warp 0: lane (head g, dim pair j) runs out += p_t·v_t over the
-// positions in order.
+// head.  Sum phase: warp 1's lane 0 copies windows of E into the stage
+// memory, in kSumParts parts on their own mbarriers, and warp 0's lanes
+// 0..G-1 add them in position order.  P.V phase: warp 1 issues each chunk's
+// V rows (one 2-D tensor copy of kPvCh rows x DS dims from the first slot of
+// a run) and E rows (one bulk copy) into a raw stage, converts V to fp32 and
+// forms (p, p) = e·(1/l) pairs; warp 0's lane (head g, dim pair j) runs out
+// += p_t·v_t over the positions in order.
 template <int HD, int G>
 __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__ pos, const int32_t* __restrict__ seq,
                                                      const __grid_constant__ CUtensorMap vmap,
                                                      const KvSeqState* __restrict__ st, int n_seq, int n_head,
                                                      int n_kv, int cap, const float* __restrict__ sbuf,
-                                                     float* __restrict__ out, int* status, float one, float neg_zero) {
+                                                     float* __restrict__ out, int* status, int n_stages, float one,
+                                                     float neg_zero) {
   constexpr int DS = 64 / G;            // dims of the slice: G heads x DS/2 pairs = 32 chain lanes
-  constexpr int CH = kPvCh, NS = kPvStages;
+  constexpr int CH = kPvCh;
+  const int NS = n_stages;
   constexpr int GP = gp_of(G);
   static_assert(HD % DS == 0 && DS % 8 == 0, "slice");
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);   // [NS] raw stage landed
-  uint64_t* conv = full + NS;                           // [NS] converted
-  uint64_t* empty = conv + NS;                          // [NS] chain done with the stage
+  uint64_t* conv = full + kPvStagesMax;                 // [NS] converted
+  uint64_t* empty = conv + kPvStagesMax;                // [NS] chain done with the stage
+  uint64_t* part = empty + kPvStagesMax;                // [kSumParts] window parts of the sum
+  float* inv_l = reinterpret_cast<float*>(part + kSumParts);   // [G]
   constexpr size_t SB = pv_stage_bytes<G>(DS);
-  uint8_t* stages = smem + 128;
+  const int WA = (int)(NS * SB / (GP * 4)) & ~3;        // positions per window of the sum
+  uint8_t* stages = smem + 256;
   const int slice = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -332,6 +356,7 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
       mbar_init(&conv[i], 1);
       mbar_init(&empty[i], 1);
     }
+    for (int i = 0; i < kSumParts; ++i) mbar_init(&part[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -342,8 +367,43 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
   const int d0 = slice * DS;
   pdl_wait();
   pdl_launch_dependents();
-  const float* prow = sbuf + ((int64_t)b * n_kv + kh) * group_floats(G, cap) + (int64_t)G * cap_s(cap);
+  const float* erow = sbuf + ((int64_t)b * n_kv + kh) * group_floats(G, cap) + e_offset(G, cap);
   bool ok = true;
+
+  // ---- sum phase ----
+  float l = 0.0f;
+  for (int w0 = 0, wi = 0; w0 < n_pos; w0 += WA, ++wi) {
+    const int len = min(WA, n_pos - w0), len4 = (len + 3) & ~3;
+    const int plen = ((len + kSumParts - 1) / kSumParts + 3) & ~3;
+    __syncthreads();   // the previous window is consumed
+    if (warp == 1 && lane == 0 && ok) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int i = 0; i < kSumParts && i * plen < len; ++i) {
+        const int a = i * plen, n4 = min(plen, len4 - a);
+        mbar_arrive_expect_tx(&part[i], (uint32_t)(n4 * GP * 4));
+        bulk_g2s(stages + (size_t)a * GP * 4, erow + (int64_t)(w0 + a) * GP, (uint32_t)(n4 * GP * 4), &part[i]);
+      }
+    }
+    if (warp == 0 && lane < G) {
+      const float* e = reinterpret_cast<const float*>(stages) + lane;
+      for (int i = 0; i < kSumParts && i * plen < len; ++i) {
+        if (ok) ok = mbar_wait_bounded(&part[i], (uint32_t)(wi & 1), status, 10);
+        if (ok) l = sum_run<GP>(e, i * plen, min(i * plen + plen, len), l);
+      }
+    }
+    ok = __syncthreads_and(ok);
+    if (!ok) {
+      // copies of this window still in flight: wait for them (bounded)
+      if (warp == 1 && lane == 0)
+        for (int i = 0; i < kSumParts && i * plen < len; ++i) mbar_wait_bounded(&part[i], (uint32_t)(wi & 1), nullptr, 0);
+      break;
+    }
+  }
+  if (warp == 0 && lane < G) inv_l[lane] = __fdiv_rn(1.0f, l);
+  __syncthreads();
+  if (!ok) return;
+
+  // ---- P.V phase ----
   if (warp == 1) {
     int p_iss = 0, c_iss = 0;
     auto issue = [&](int si) {
@@ -351,13 +411,18 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
       uint8_t* sp = stages + si * SB;
       mbar_arrive_expect_tx(&full[si], (uint32_t)(CH * DS * 2 + r.len * GP * 4));
       tma_load_2d(sp, &vmap, d0, row0 + (int)r.slot, &full[si]);
-      bulk_g2s(sp + CH * DS * 2, prow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
+      bulk_g2s(sp + CH * DS * 2, erow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
       p_iss += r.len;
       ++c_iss;
     };
-    if (lane == 0)
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       while (p_iss < n_pos && c_iss < NS) issue(c_iss % NS);
+    }
     __syncwarp();
+    float inv[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) inv[g] = inv_l[g];
     int p = 0;
     for (int c = 0; p < n_pos; ++c) {
       const int si = c % NS;
@@ -366,19 +431,32 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
       if (ok && c >= NS) ok = mbar_wait_bounded(&empty[si], (uint32_t)(((c / NS) - 1) & 1), status, 7);
       if (ok) {
         uint8_t* sp = stages + si * SB;
-        const uint32_t* rv = reinterpret_cast<const uint32_t*>(sp);
-        const float* rp = reinterpret_cast<const float*>(sp + CH * DS * 2);
-        float* fv = reinterpret_cast<float*>(sp + CH * DS * 2 + CH * GP * 4);
-        uint64_t* fp = reinterpret_cast<uint64_t*>(sp + CH * DS * 2 + CH * GP * 4 + CH * DS * 4);
-        for (int i = lane; i < len * DS / 2; i += 32) {
-          const uint32_t w2 = rv[i];
-          fv[2 * i] = h2f((uint16_t)(w2 & 0xFFFFu));
-          fv[2 * i + 1] = h2f((uint16_t)(w2 >> 16));
-        }
-        for (int i = lane; i < len * G; i += 32) {
-          const int t = i / G, g = i - t * G;
-          const float pv = rp[t * GP + g];
-          fp[i] = pack2(pv, pv);
+        const uint4* rv = reinterpret_cast<const uint4*>(sp);                 // [CH][DS/8] raw V
+        const float4* re = reinterpret_cast<const float4*>(sp + CH * DS * 2);  // [CH][GP/4] raw E
+        uint64_t* vp = reinterpret_cast<uint64_t*>(sp + CH * DS * 2 + CH * GP * 4);   // [DS/2][CHP]
+        uint64_t* pp = vp + (DS / 2) * kPvChP;                                       // [G][CHP]
+        // lane t owns positions t, t + 32, ...: its V row becomes DS/2 pairs
+        // and its E row G pairs (p, p) = e·(1/l)
+        for (int t = lane; t < len; t += 32) {
+#pragma unroll
+          for (int c = 0; c < DS / 8; ++c) {
+            const uint4 w = rv[t * (DS / 8) + c];
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              vp[(4 * c + k) * kPvChP + t] = pack2(h2f((uint16_t)(ww[k] & 0xFFFFu)), h2f((uint16_t)(ww[k] >> 16)));
+          }
+#pragma unroll
+          for (int c = 0; c < GP / 4; ++c) {
+            const float4 e = re[t * (GP / 4) + c];
+            const float ev[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (4 * c + k < G) {
+                const float pv = __fmul_rn(ev[k], inv[4 * c + k]);
+                pp[(4 * c + k) * kPvChP + t] = pack2(pv, pv);
+              }
+          }
         }
       }
       __syncwarp();
@@ -414,17 +492,41 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
     if (ok) ok = mbar_wait_bounded(&conv[si], (uint32_t)((c / NS) & 1), status, 8);
     if (ok) {
       const uint8_t* sp = stages + si * SB;
-      const float* vr = reinterpret_cast<const float*>(sp + CH * DS * 2 + CH * GP * 4) + 2 * j;
-      const uint64_t* pr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4 + CH * DS * 4) + g;
-      int t = 0;
-      for (; t + 2 <= len; t += 2) {
-        const uint64_t p0 = pr[t * G], p1 = pr[(t + 1) * G];
-        const uint64_t v0 = *reinterpret_cast<const uint64_t*>(vr + t * DS);
-        const uint64_t v1 = *reinterpret_cast<const uint64_t*>(vr + (t + 1) * DS);
-        acc = mul_add2(acc, p0, v0, k2);
-        acc = mul_add2(acc, p1, v1, k2);
+      const uint64_t* vr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4) + j * kPvChP;
+      const uint64_t* pr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4) +
+                           (DS / 2) * kPvChP + g * kPvChP;
+      // positions in groups of 8, two per 16-byte load: the next group's
+      // (p, v) are read while the current group's chain runs, so no step
+      // waits on a shared-memory load
+      const int len8 = len & ~7;
+      uint4 cp[4], cv[4], np_[4], nv[4];
+      if (len8 > 0) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          cp[k] = *reinterpret_cast<const uint4*>(pr + 2 * k);
+          cv[k] = *reinterpret_cast<const uint4*>(vr + 2 * k);
+        }
       }
-      if (t < len) acc = mul_add2(acc, pr[t * G], *reinterpret_cast<const uint64_t*>(vr + t * DS), k2);
+      for (int t = 0; t < len8; t += 8) {
+        if (t + 8 < len8) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            np_[k] = *reinterpret_cast<const uint4*>(pr + t + 8 + 2 * k);
+            nv[k] = *reinterpret_cast<const uint4*>(vr + t + 8 + 2 * k);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc = mul_add2(acc, u64_of(cp[k].x, cp[k].y), u64_of(cv[k].x, cv[k].y), k2);
+          acc = mul_add2(acc, u64_of(cp[k].z, cp[k].w), u64_of(cv[k].z, cv[k].w), k2);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          cp[k] = np_[k];
+          cv[k] = nv[k];
+        }
+      }
+      for (int t = len8; t < len; ++t) acc = mul_add2(acc, pr[t], vr[t], k2);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[si]);
@@ -466,23 +568,31 @@ int make_v_map(const uint16_t* vc, int64_t n_rows, int hd, int ds, CUtensorMap* 
 
 template <int HD, int G>
 int launch_hd_g(const float* q, int n_tok, int n_head, int n_kv, const int32_t* pos, const int32_t* seq,
-                const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scores,
-                unsigned int* count, float* out, cudaStream_t s, int* status) {
+                const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scratch,
+                float* out, cudaStream_t s, int* status) {
   constexpr int NP = (G + 1) / 2;
   constexpr int DS = 64 / G;
-  constexpr size_t KB = (size_t)kScoreP * HD * 2, RB = KB > kWinFloats * 4 ? KB : (size_t)kWinFloats * 4;
-  const size_t sm = 128 + RB + (size_t)HD * NP * 8;
+  const size_t sm = 128 + (size_t)kScoreP * HD * 2 + (size_t)HD * NP * 8;
   B2_CUDA_TRY(cudaFuncSetAttribute(attn_scores_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   const float scale = 1.0f / sqrtf((float)HD);
-  int rc = launch_pdl(attn_scores_kernel<HD, G>, dim3((cap + kScoreP - 1) / kScoreP, n_kv, n_tok), dim3(kScoreP), sm,
-                      s, q, n_head, n_kv, pos, seq, kc, st, n_seq, cap, scale, scores, count, status, 1.0f, -0.0f);
+  const dim3 chunks((cap + kScoreP - 1) / kScoreP, n_kv, n_tok);
+  int rc = launch_pdl(attn_scores_kernel<HD, G>, chunks, dim3(kScoreP), sm, s, q, n_head, n_kv, pos, seq, kc, st, n_seq,
+                      cap, scale, scratch, status, 1.0f, -0.0f);
+  if (rc) return rc;
+  rc = launch_pdl(attn_exp_kernel<G>, chunks, dim3(kScoreP), 0, s, pos, seq, n_seq, n_kv, cap, scratch);
   if (rc) return rc;
   CUtensorMap vmap;
   if ((rc = make_v_map(vc, (int64_t)n_seq * n_kv * cap, HD, DS, &vmap))) return rc;
-  const size_t smv = 128 + (size_t)kPvStages * pv_stage_bytes<G>(DS);
+  // Stages: as many as fit when the grid's CTAs are spread evenly over the
+  // SMs (more stages keep more V in flight and make the sum's windows longer).
+  const int64_t ctas = (int64_t)(HD / DS) * n_kv * n_tok;
+  const int per_sm = (int)std::min<int64_t>(4, std::max<int64_t>(1, (ctas + sm_count() - 1) / sm_count()));
+  const size_t sb = pv_stage_bytes<G>(DS);
+  const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvStagesMax, ((size_t)227 * 1024 / per_sm - 1024 - 256) / sb));
+  const size_t smv = 256 + (size_t)ns * sb;
   B2_CUDA_TRY(cudaFuncSetAttribute(attn_pv_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smv));
   return launch_pdl(attn_pv_kernel<HD, G>, dim3(HD / DS, n_kv, n_tok), dim3(64), smv, s, pos, seq, vmap, st, n_seq,
-                    n_head, n_kv, cap, (const float*)scores, out, status, 1.0f, -0.0f);
+                    n_head, n_kv, cap, (const float*)scratch, out, status, ns, 1.0f, -0.0f);
 }
 
 }  // namespace
@@ -493,14 +603,14 @@ size_t attn_scratch_floats(int n_tok, int n_head, int n_kv, int cap) {
 }
 
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scores,
-                     unsigned int* count, float* out, cudaStream_t s, int* status) {
-  B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0 && scores && count && out && cap > 0, "attention arguments");
-  B2_CHECK_ARG((reinterpret_cast<uintptr_t>(scores) & 15) == 0, "attention scratch must be 16-byte aligned");
+                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scratch,
+                     float* out, cudaStream_t s, int* status) {
+  B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0 && scratch && out && cap > 0, "attention arguments");
+  B2_CHECK_ARG((reinterpret_cast<uintptr_t>(scratch) & 15) == 0, "attention scratch must be 16-byte aligned");
   const int G = n_head / n_kv;
 #define B2_ATTN_CASE(HDV, GV) \
   if (hd == HDV && G == GV)   \
-    return launch_hd_g<HDV, GV>(q, n_tok, n_head, n_kv, pos, seq, kc, vc, st, n_seq, cap, scores, count, out, s, status);
+    return launch_hd_g<HDV, GV>(q, n_tok, n_head, n_kv, pos, seq, kc, vc, st, n_seq, cap, scratch, out, s, status);
   B2_ATTN_CASE(128, 1)
   B2_ATTN_CASE(128, 2)
   B2_ATTN_CASE(128, 4)

@@ -453,22 +453,11 @@ int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_ca
                "attn_decode arguments");
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
   cudaStream_t s = as_stream(stream);
-  // scores / probabilities, then the arrival counters (zeroed here)
-  const size_t nsc = attn_scratch_floats(n_q, n_head, n_kv, cap);
-  const size_t ncnt = (size_t)n_q * n_kv;
+  // scores, exponentials and chunk maxima (no initialisation needed)
   void* scratch = nullptr;
-  B2_CUDA_TRY(cudaMallocAsync(&scratch, (nsc + ncnt) * 4, s));
-  float* scores = static_cast<float*>(scratch);
-  unsigned int* count = reinterpret_cast<unsigned int*>(scores + nsc);
-  int rc = B2_OK;
-  const cudaError_t e = cudaMemsetAsync(count, 0, ncnt * 4, s);
-  if (e != cudaSuccess) {
-    set_error("attn_decode: %s", cudaGetErrorString(e));
-    rc = B2_ERR_CUDA;
-  } else {
-    rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap, scores,
-                          count, out, s);
-  }
+  B2_CUDA_TRY(cudaMallocAsync(&scratch, attn_scratch_floats(n_q, n_head, n_kv, cap) * 4, s));
+  const int rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap,
+                                  static_cast<float*>(scratch), out, s);
   cudaFreeAsync(scratch, s);
   return rc;
 }

@@ -218,7 +218,10 @@ __constant__ static const unsigned long long kExp2Tab32[32] = {
     0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
     0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
     0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
-__device__ __forceinline__ float b2_expf_ref(float x) {
+// tab: kExp2Tab32 itself, or a copy of it in shared memory (exp_table_to_smem):
+// the lanes of a warp index the table with different k, which the constant
+// cache serves one address at a time and shared memory in one access.
+__device__ __forceinline__ float b2_expf_ref(float x, const unsigned long long* tab) {
   if (!(x == x)) return x;
   if (x > 88.7228394f) return __int_as_float(0x7f800000);
   if (x < -103.972084f) return 0.0f;
@@ -230,7 +233,7 @@ __device__ __forceinline__ float b2_expf_ref(float x) {
   const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
   kd = __dsub_rn(kd, shift);
   const double r = __fma_rn(inv_ln2_n, xd, -kd);
-  const double s = __longlong_as_double((long long)(kExp2Tab32[ki & 31] + (ki << 47)));
+  const double s = __longlong_as_double((long long)(tab[ki & 31] + (ki << 47)));
   const double z = __dadd_rn(__dmul_rn(c0, r), c1);
   const double r2 = __dmul_rn(r, r);
   double y = __dadd_rn(__dmul_rn(c2, r), 1.0);
@@ -239,6 +242,12 @@ __device__ __forceinline__ float b2_expf_ref(float x) {
 }
 
 // silu(g)·u in the reference's order: (g / (1 + expf(-g))) · u.
+__device__ __forceinline__ float b2_expf_ref(float x) { return b2_expf_ref(x, kExp2Tab32); }
+// Copies the table into tab[32] of shared memory (threads tid of n); the
+// caller synchronizes before the first use.
+__device__ __forceinline__ void exp_table_to_smem(unsigned long long* tab, int tid, int n) {
+  for (int i = tid; i < 32; i += n) tab[i] = kExp2Tab32[i];
+}
 __device__ __forceinline__ float silu_mul_ref(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, b2_expf_ref(-g))), u);
 }

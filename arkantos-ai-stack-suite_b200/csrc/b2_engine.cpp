@@ -118,8 +118,7 @@ struct b2_context {
   int in_slot = 0;
   // step buffers
   float *x = nullptr, *delta = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
-  float *logits = nullptr, *scores = nullptr, *top = nullptr;   // scores: attention [kStepMax][n_head][n_ctx]
-  unsigned int* attn_cnt = nullptr;   // [kStepMax][n_kv] arrival counters of the attention's softmax
+  float *logits = nullptr, *scores = nullptr, *top = nullptr;   // scores: the attention's scratch for kStepMax queries
   uint32_t* argmax_scr = nullptr;     // vocabulary-slice partials and arrival counters of the argmax
   // [ids kStepMax | top-1, margin 2*kStepMax | status] in one allocation: one
   // D2H copy returns a step's greedy result and the device-wait status
@@ -138,7 +137,6 @@ struct b2_context {
   cudaEvent_t pf_ev = nullptr;  // the staging's last copy
   float *pf_x = nullptr, *pf_xn = nullptr, *pf_delta = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
   float *pf_att = nullptr, *pf_gu = nullptr, *pf_h = nullptr, *pf_scores = nullptr;
-  unsigned int* pf_attn_cnt = nullptr;
   uint8_t* pf_ws = nullptr;     // GEMM activation images
   // last decode
   int last_n = 0;
@@ -522,8 +520,6 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
       for (int n = 1; n <= T; ++n) img = std::max(img, gemv_act_image_bytes(q->m, n));
     if ((rc = dalloc(c, &c->act_img, img))) return rc;
   }
-  if ((rc = dalloc(c, &c->attn_cnt, (size_t)T * m->nkv_l))) return rc;
-  B2_CUDA_TRY(cudaMemset(c->attn_cnt, 0, (size_t)T * m->nkv_l * sizeof(unsigned int)));
   static_assert(kStepMax <= kArgmaxTok, "argmax scratch sized for the step");
   if ((rc = dalloc(c, &c->argmax_scr, argmax_scratch_words()))) return rc;
   B2_CUDA_TRY(cudaMemset(c->argmax_scr, 0, argmax_scratch_words() * sizeof(uint32_t)));
@@ -638,7 +634,7 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
       if ((rc = tap("q_rope", l, c->q, (int64_t)n * m->nh_l * hd))) return rc;
     }
     if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->vc[l], c->st_d,
-                               c->n_seq, c->n_ctx, c->scores, c->attn_cnt, c->att, s, c->status)))
+                               c->n_seq, c->n_ctx, c->scores, c->att, s, c->status)))
       return rc;
     if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
     {
@@ -768,7 +764,7 @@ int prefill_alloc(b2_context* c) {
   b2_model* m = c->model;
   const int d = m->n_embd, hd = m->head_dim, qkv_w = (m->nh_l + 2 * m->nkv_l) * hd, nq = m->nh_l * hd;
   const size_t per_tok = 4 * ((size_t)3 * d + qkv_w + 2 * (size_t)nq + 3 * (size_t)m->ff_l +
-                              attn_scratch_floats(1, m->nh_l, m->nkv_l, c->n_ctx) + m->nkv_l + 3);
+                              attn_scratch_floats(1, m->nh_l, m->nkv_l, c->n_ctx) + 3);
   const int cap = (int)std::max<size_t>(kPrefillMin, std::min<size_t>(kPrefillCapMax, kPrefillBudget / per_tok));
   size_t ws = 0;
   for (const auto& L : m->layers)
@@ -781,7 +777,7 @@ int prefill_alloc(b2_context* c) {
       (rc = dalloc(c, &c->pf_att, (size_t)cap * nq)) || (rc = dalloc(c, &c->pf_gu, (size_t)cap * 2 * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_h, (size_t)cap * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_scores, attn_scratch_floats(cap, m->nh_l, m->nkv_l, c->n_ctx))) ||
-      (rc = dalloc(c, &c->pf_attn_cnt, (size_t)cap * m->nkv_l)) || (rc = dalloc(c, &c->pf_ws, ws))) {
+      (rc = dalloc(c, &c->pf_ws, ws))) {
     // A context short of memory keeps none of the chunk buffers: free the
     // ones this call took (nothing has been enqueued on them).
     for (size_t i = n_before; i < c->allocs.size(); ++i) cudaFree(c->allocs[i]);
@@ -789,11 +785,9 @@ int prefill_alloc(b2_context* c) {
     c->pf_in = nullptr;
     c->pf_x = c->pf_xn = c->pf_delta = c->pf_qkv = c->pf_q = c->pf_att = c->pf_gu = c->pf_h = nullptr;
     c->pf_scores = nullptr;
-    c->pf_attn_cnt = nullptr;
     c->pf_ws = nullptr;
     return rc;
   }
-  B2_CUDA_TRY(cudaMemset(c->pf_attn_cnt, 0, (size_t)cap * m->nkv_l * sizeof(unsigned int)));
   B2_CUDA_TRY(cudaMallocHost(&c->pf_in_h, (size_t)3 * cap * sizeof(int32_t)));
   B2_CUDA_TRY(cudaEventCreateWithFlags(&c->pf_ev, cudaEventDisableTiming));
   c->pf_cap = cap;
@@ -815,7 +809,7 @@ int enqueue_prefill_chunk(b2_context* c, int nt) {
         (rc = launch_rope_kv(c->pf_qkv, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->rope, c->pf_q, c->kc[l], c->vc[l],
                              c->st_d, c->n_seq, c->n_ctx, s)) ||
         (rc = launch_attention(c->pf_q, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->kc[l], c->vc[l], c->st_d, c->n_seq,
-                               c->n_ctx, c->pf_scores, c->pf_attn_cnt, c->pf_att, s, c->status)) ||
+                               c->n_ctx, c->pf_scores, c->pf_att, s, c->status)) ||
         (rc = launch_gemm(L.wo.m, c->pf_att, nq, nt, c->pf_delta, c->pf_ws, c->status, s)) ||
         (rc = launch_add_rmsnorm(c->pf_x, c->pf_delta, L.ffn_norm, c->pf_xn, nt, d, m->eps, s, nullptr,
                                  c->status)) ||

@@ -11,15 +11,20 @@
 // output is bit-identical to the reference's per-row result.
 //
 // Weights are in the tile layout (8-row tiles, units in order, see QMatrix).
-// A CTA takes a contiguous run of tiles; its warps own tiles round-robin and
-// fold each tile's rows through all units themselves, so no cross-warp
-// reduction or barrier sits in the main loop.  Every warp streams its own
-// tiles: lane 0 issues 1-D bulk copies (cp.async.bulk, no multicast) of U
-// consecutive unit slots into the warp's ring of stages, each completing on
-// its own mbarrier, and refills a stage as soon as the warp has read it.  The
-// first stages are issued before the grid dependency resolves, so with
-// programmatic dependent launch a GEMV's weights stream while the previous
-// kernel finishes.
+// A CTA takes a contiguous run of items (a tile for 1-2 tokens, a pair of
+// tiles for 3-8).  With many items per CTA its warps own items round-robin
+// and fold each item's rows through all units themselves; with few (at most
+// kKsMaxItems) each item gets a group of S warps that split its units in
+// chunks: a warp computes its chunk's unit terms, then takes the running sums
+// from the warp of the previous chunk (a shared-memory slot and an mbarrier),
+// adds its terms in unit order and passes the sums on, so the fold keeps the
+// reference's order while up to 16 warps stream and compute.  Every warp
+// streams its own chunks: lane 0 issues 1-D bulk copies (cp.async.bulk, no
+// multicast) of U consecutive unit slots into the warp's ring of stages,
+// each completing on its own mbarrier, and refills a stage as soon as the
+// warp has read it.  The first stages are issued before the grid dependency
+// resolves, so with programmatic dependent launch a GEMV's weights stream
+// while the previous kernel finishes.
 //   * activations are quantized bit-exactly with the reference's quantizers,
 //     either by the CTA itself into shared memory (small inputs) or once per
 //     launch by a producer kernel into an image that one bulk copy brings in;
@@ -27,14 +32,17 @@
 //     (lane >> 3); the four lanes of a row exchange their unit terms by
 //     shuffles and all fold them in unit order;
 //   * 3-8 tokens: int8 mma.sync (m16n8k32; m16n8k16 for Q6_K's 16-weight
-//     groups) with the tokens as M (rows 8-15 zero) and the tile's 8 weight
-//     rows as N; lane 4g+q folds (token g, rows 2q and 2q+1);
+//     groups) with the 16 rows of a tile pair as M (tile A's row g as row g,
+//     tile B's as row g + 8) and the tokens as N; lane 4g+q folds rows g of
+//     both tiles for tokens 2q and 2q+1;
 //   * epilogue: store, residual add, SwiGLU over interleaved gate/up rows,
 //     RoPE + fp16 KV store over the fused QKV rows, or the tensor-parallel
 //     exchange into every rank's gather buffer.
 // Every mbarrier wait is bounded: a warp whose wait expires records a status
 // code, stops computing and issuing, waits (bounded) for the copies it still
 // has in flight, and the CTA always exits.
+#include <stdlib.h>
+
 #include "b2_common.cuh"
 #include "b2_quant.cuh"
 
@@ -43,9 +51,14 @@ namespace {
 
 constexpr int kMaxWarps = 16;
 constexpr int kMaxStages = 8;            // ring stages per warp
-constexpr int kHdrBytes = 1152;          // full[kMaxWarps][kMaxStages], act barrier, padding
+constexpr int kHdrBytes = 1280;          // full[kMaxWarps][kMaxStages], act barrier, turn[kMaxWarps], padding
 constexpr int kMaxTok = 8;
 constexpr int kDp4aMaxTok = 2;           // dp4a up to this many tokens, mma.sync above
+constexpr int kKsMaxItems = 8;           // items per CTA up to which the warps of a group split each item
+constexpr int kKsPairUnits = 2;          // units per chunk of a split tile pair
+// 4-unit groups per chunk of a split dp4a tile (two for Q4_K at 2 tokens,
+// whose unit terms take the most registers)
+__host__ __device__ constexpr int ks_dp4a_groups(int type, int n_tok) { return type == B2_Q4_K && n_tok == 2 ? 2 : 4; }
 constexpr uint32_t kM4 = 0x0F0F0F0Fu;
 
 constexpr int kMaxMat = 64;          // matrices of one multi-matrix launch
@@ -57,8 +70,12 @@ struct GemvP {
   int64_t x_stride;
   int64_t y_stride;
   int epilogue;
-  int U, n_ch, n_stages;   // units per stage, stages per tile, ring stages per warp
-  uint32_t stage_bytes;    // U * slot_bytes
+  int U, n_ch, n_stages;   // units per stage, stages per item, ring stages per warp
+  int ipt;                 // tiles per item: 1, or 2 (the rows-as-M pairs of MODE 3)
+  int S;                   // warps per item (split items, KS), else 1
+  uint32_t tok_bytes;      // the groups' slots for passing sums (KS)
+  uint32_t half_bytes;     // U * slot_bytes: one tile's share of a stage
+  uint32_t stage_bytes;    // ipt * half_bytes
   int kq;                  // activation row stride in bytes
   uint32_t off_dx, off_bs, act_bytes, act_region;   // activation carve-up and its shared-memory size
   const uint8_t* act_img;  // the quantized activations (global), or null: the CTA quantizes x itself
@@ -83,25 +100,27 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 }
 __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
-// Tokens-as-M forms: D[16x8] = A[16xK] (token rows 0..7, rows 8..15 zero)
-// * B[Kx8] (k x the tile's weight rows).  With a1 = a3 = 0, lane 4g+q gets
-// d[0] = (token g, row 2q), d[1] = (token g, row 2q+1).
-__device__ __forceinline__ void mma_k32_s8u8(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+// Rows-as-M forms: D[16x8] = A[16xK] (weight row g of tile A as row g, of
+// tile B as row g + 8) * B[Kx8] (k x tokens).  Lane 4g+q gets d[0] = (row
+// gA, token 2q), d[1] = (gA, 2q+1), d[2] = (gB, 2q), d[3] = (gB, 2q+1).
+__device__ __forceinline__ void mma_k32_u8s8_rows(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                  uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
-__device__ __forceinline__ void mma_k32_s8s8(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_k32_s8s8_rows(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                  uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
-__device__ __forceinline__ void mma_k16_s8u8(int (&d)[4], uint32_t a0, uint32_t b0) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+__device__ __forceinline__ void mma_k16_u8s8_rows(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-               : "r"(a0), "r"(0), "r"(b0), "r"(0));
+               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
 
 __device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)((w >> (8 * b)) & 0xFFu); }
@@ -335,102 +354,133 @@ __device__ __forceinline__ void dp4a_terms(const GemvP& p, const uint8_t* sl, co
   }
 }
 
-// ---- mma path: the terms of one unit u for (token g, rows 2q and 2q+1) -----------------------
-// a[r] / b[r] as in dp4a_terms for row 2q + r.  Tokens at or past n_tok feed
-// zero codes (their outputs are never stored).
+// ---- rows-as-M path: the terms of one unit u of two tiles for lane 4g+q ---------------------
+// i = 2·(tile B) + (token 2q+1): a[i] / b[i] as in dp4a_terms for row g of
+// tile A (i = 0, 1) or of tile B (i = 2, 3) and token 2q (i even) or 2q+1.
+// The B fragment is token g's codes; tokens at or past n_tok feed zeros.
 template <int WT>
-__device__ __forceinline__ void mma_terms(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, int g, int q,
-                                          bool live, float (&a)[2], float (&b)[2]) {
-  const float dx = live ? reinterpret_cast<const float*>(act + p.off_dx)[g * p.nu + u] : 0.0f;
+__device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa, const uint8_t* sb,
+                                               const uint8_t* act, int u, int g, int q, float (&a)[4],
+                                               float (&b)[4]) {
+  const bool lg = g < p.n_tok, l0 = 2 * q < p.n_tok, l1 = 2 * q + 1 < p.n_tok;
+  const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
   const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
+  const float dx0 = l0 ? dxs[(2 * q) * p.nu + u] : 0.0f, dx1 = l1 ? dxs[(2 * q + 1) * p.nu + u] : 0.0f;
   const uint8_t* xr = act + g * p.kq;
   if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
     const uint8_t* xb = xr + u * 32;
-    const uint32_t a0 = live ? lds32(xb + 4 * q) : 0u, a2 = live ? lds32(xb + 16 + 4 * q) : 0u;
+    const uint32_t b0 = lg ? lds32(xb + 4 * q) : 0u, b1 = lg ? lds32(xb + 16 + 4 * q) : 0u;
     int c[4];
-    uint32_t dw2;
+    float dA, dB;
     if constexpr (WT == B2_Q4_0) {
-      const uint32_t w = lds32(sl + 16 * g + 4 * q);
-      mma_k32_s8u8(c, a0, a2, w & kM4, (w >> 4) & kM4);
-      const int corr = live ? 8 * (int)bss[g * p.nu + u] : 0;
-      c[0] -= corr;
-      c[1] -= corr;
-      dw2 = lds32(sl + 128 + 4 * q);
+      const uint32_t wa = lds32(sa + 16 * g + 4 * q), wb = lds32(sb + 16 * g + 4 * q);
+      mma_k32_u8s8_rows(c, wa & kM4, wb & kM4, (wa >> 4) & kM4, (wb >> 4) & kM4, b0, b1);
+      const int k0 = l0 ? 8 * (int)bss[(2 * q) * p.nu + u] : 0, k1 = l1 ? 8 * (int)bss[(2 * q + 1) * p.nu + u] : 0;
+      c[0] -= k0;
+      c[1] -= k1;
+      c[2] -= k0;
+      c[3] -= k1;
+      dA = h2f(*reinterpret_cast<const uint16_t*>(sa + 128 + 2 * g));
+      dB = h2f(*reinterpret_cast<const uint16_t*>(sb + 128 + 2 * g));
     } else {
-      mma_k32_s8s8(c, a0, a2, lds32(sl + 16 * g + 4 * q), lds32(sl + 128 + 16 * g + 4 * q));
-      dw2 = lds32(sl + 256 + 4 * q);
+      mma_k32_s8s8_rows(c, lds32(sa + 16 * g + 4 * q), lds32(sb + 16 * g + 4 * q), lds32(sa + 128 + 16 * g + 4 * q),
+                        lds32(sb + 128 + 16 * g + 4 * q), b0, b1);
+      dA = h2f(*reinterpret_cast<const uint16_t*>(sa + 256 + 2 * g));
+      dB = h2f(*reinterpret_cast<const uint16_t*>(sb + 256 + 2 * g));
     }
-    const float d0 = h2f((uint16_t)(dw2 & 0xFFFFu)), d1 = h2f((uint16_t)(dw2 >> 16));
-    a[0] = __fmul_rn(__fmul_rn(d0, dx), (float)c[0]);
-    a[1] = __fmul_rn(__fmul_rn(d1, dx), (float)c[1]);
-    b[0] = b[1] = 0.0f;
+    a[0] = __fmul_rn(__fmul_rn(dA, dx0), (float)c[0]);
+    a[1] = __fmul_rn(__fmul_rn(dA, dx1), (float)c[1]);
+    a[2] = __fmul_rn(__fmul_rn(dB, dx0), (float)c[2]);
+    a[3] = __fmul_rn(__fmul_rn(dB, dx1), (float)c[3]);
+    b[0] = b[1] = b[2] = b[3] = 0.0f;
   } else if constexpr (WT == B2_Q4_K) {
-    const uint4 m0 = lds128(sl + 1024 + 32 * q), m1 = lds128(sl + 1024 + 32 * q + 16);   // rows 2q, 2q+1
-    uint32_t sl0, ml0, sh0, mh0, sl1, ml1, sh1, mh1;
-    q4k_scales(m0.y, m0.z, m0.w, sl0, ml0, sh0, mh0);
-    q4k_scales(m1.y, m1.z, m1.w, sl1, ml1, sh1, mh1);
-    const uint8_t* qrow = sl + 128 * g;          // B column g = weight row g of the tile
+    const uint4 ma = lds128(sa + 1024 + 16 * g), mb = lds128(sb + 1024 + 16 * g);
+    uint32_t slA, mlA, shA, mhA, slB, mlB, shB, mhB;
+    q4k_scales(ma.y, ma.z, ma.w, slA, mlA, shA, mhA);
+    q4k_scales(mb.y, mb.z, mb.w, slB, mlB, shB, mhB);
+    const uint8_t* qa = sa + 128 * g;
+    const uint8_t* qb = sb + 128 * g;
     const uint8_t* xu = xr + u * 256;
-    int is0 = 0, is1 = 0;
+    int is[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int jc = 0; jc < 4; ++jc) {
-      const uint32_t w0 = lds32(qrow + 16 * ((2 * jc + g) & 7) + 4 * q);
-      const uint32_t w1 = lds32(qrow + 16 * ((2 * jc + 1 + g) & 7) + 4 * q);
+      const int c0 = 16 * ((2 * jc + g) & 7) + 4 * q, c1 = 16 * ((2 * jc + 1 + g) & 7) + 4 * q;
+      const uint32_t w0a = lds32(qa + c0), w1a = lds32(qa + c1), w0b = lds32(qb + c0), w1b = lds32(qb + c1);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int j = 2 * jc + h;                 // 32-weight group
-        const uint32_t a0 = live ? lds32(xu + 32 * j + 4 * q) : 0u;
-        const uint32_t a2 = live ? lds32(xu + 32 * j + 16 + 4 * q) : 0u;
+        const int j = 2 * jc + h;   // 32-weight group
+        const uint32_t b0 = lg ? lds32(xu + 32 * j + 4 * q) : 0u, b1 = lg ? lds32(xu + 32 * j + 16 + 4 * q) : 0u;
+        const int sh = 4 * h;
         int c[4];
-        if (h == 0) mma_k32_s8u8(c, a0, a2, w0 & kM4, w1 & kM4);
-        else mma_k32_s8u8(c, a0, a2, (w0 >> 4) & kM4, (w1 >> 4) & kM4);
-        is0 += (j < 4 ? ubyte(sl0, j) : ubyte(sh0, j - 4)) * c[0];
-        is1 += (j < 4 ? ubyte(sl1, j) : ubyte(sh1, j - 4)) * c[1];
+        mma_k32_u8s8_rows(c, (w0a >> sh) & kM4, (w0b >> sh) & kM4, (w1a >> sh) & kM4, (w1b >> sh) & kM4, b0, b1);
+        const int sA = j < 4 ? ubyte(slA, j) : ubyte(shA, j - 4);
+        const int sB = j < 4 ? ubyte(slB, j) : ubyte(shB, j - 4);
+        is[0] += sA * c[0];
+        is[1] += sA * c[1];
+        is[2] += sB * c[2];
+        is[3] += sB * c[3];
       }
     }
-    const uint4 bq = live ? lds128(reinterpret_cast<const uint8_t*>(bss + (g * p.nu + u) * 8)) : make_uint4(0, 0, 0, 0);
-    const int ms0 = q4k_msum(bq, ml0, mh0), ms1 = q4k_msum(bq, ml1, mh1);
-    const float dd0 = h2f((uint16_t)(m0.x & 0xFFFFu)), dm0 = h2f((uint16_t)(m0.x >> 16));
-    const float dd1 = h2f((uint16_t)(m1.x & 0xFFFFu)), dm1 = h2f((uint16_t)(m1.x >> 16));
-    a[0] = __fmul_rn(__fmul_rn(dd0, dx), (float)is0);
-    b[0] = __fmul_rn(__fmul_rn(dm0, dx), (float)ms0);
-    a[1] = __fmul_rn(__fmul_rn(dd1, dx), (float)is1);
-    b[1] = __fmul_rn(__fmul_rn(dm1, dx), (float)ms1);
+    const uint4 z4 = make_uint4(0, 0, 0, 0);
+    const uint4 bq0 = l0 ? lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q) * p.nu + u) * 8)) : z4;
+    const uint4 bq1 = l1 ? lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q + 1) * p.nu + u) * 8)) : z4;
+    const int ms[4] = {q4k_msum(bq0, mlA, mhA), q4k_msum(bq1, mlA, mhA), q4k_msum(bq0, mlB, mhB),
+                       q4k_msum(bq1, mlB, mhB)};
+    const float ddA = h2f((uint16_t)(ma.x & 0xFFFFu)), dmA = h2f((uint16_t)(ma.x >> 16));
+    const float ddB = h2f((uint16_t)(mb.x & 0xFFFFu)), dmB = h2f((uint16_t)(mb.x >> 16));
+    const float dd[4] = {ddA, ddA, ddB, ddB}, dm[4] = {dmA, dmA, dmB, dmB}, dx[4] = {dx0, dx1, dx0, dx1};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a[i] = __fmul_rn(__fmul_rn(dd[i], dx[i]), (float)is[i]);
+      b[i] = __fmul_rn(__fmul_rn(dm[i], dx[i]), (float)ms[i]);
+    }
   } else {  // Q6_K: 16 groups of 16 weights, m16n8k16
-    const uint8_t* qlr = sl + 128 * g;
-    const uint8_t* qhr = sl + 1024 + 64 * g;
-    const uint4 sc0 = lds128(sl + 1536 + 32 * q), sc1 = lds128(sl + 1536 + 32 * q + 16);   // rows 2q, 2q+1
-    const uint32_t sw0[4] = {sc0.x, sc0.y, sc0.z, sc0.w}, sw1[4] = {sc1.x, sc1.y, sc1.z, sc1.w};
-    const int16_t* bs = bss + (g * p.nu + u) * 16;
+    const uint8_t* qla = sa + 128 * g;
+    const uint8_t* qlb = sb + 128 * g;
+    const uint8_t* qha = sa + 1024 + 64 * g;
+    const uint8_t* qhb = sb + 1024 + 64 * g;
+    const uint4 sca = lds128(sa + 1536 + 16 * g), scb = lds128(sb + 1536 + 16 * g);
+    const uint32_t swa[4] = {sca.x, sca.y, sca.z, sca.w}, swb[4] = {scb.x, scb.y, scb.z, scb.w};
+    const int16_t* bs0 = bss + ((2 * q) * p.nu + u) * 16;
+    const int16_t* bs1 = bss + ((2 * q + 1) * p.nu + u) * 16;
     const uint8_t* xu = xr + u * 256;
-    int is0 = 0, is1 = 0;
+    int is[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const uint32_t hw = lds32(qhr + 16 * ((2 * hh + hf + g) & 3) + 4 * q);
+        const int ch = 16 * ((2 * hh + hf + g) & 3) + 4 * q;
+        const uint32_t hwa = lds32(qha + ch), hwb = lds32(qhb + ch);
 #pragma unroll
         for (int a1 = 0; a1 < 2; ++a1) {
-          const uint32_t lw = lds32(qlr + 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q);
+          const int cl = 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q;
+          const uint32_t lwa = lds32(qla + cl), lwb = lds32(qlb + cl);
 #pragma unroll
           for (int nh = 0; nh < 2; ++nh) {
             const int aq = a1 + 2 * nh;          // quartile of the half
             const int i = hh * 8 + aq * 2 + hf;  // 16-weight group of the super-block
-            const uint32_t v = (nh ? (lw >> 4) & kM4 : lw & kM4) | (((hw >> (2 * aq)) & 0x03030303u) << 4);
-            const uint32_t a0 = live ? lds32(xu + 16 * i + 4 * q) : 0u;
+            const uint32_t va = ((lwa >> (4 * nh)) & kM4) | (((hwa >> (2 * aq)) & 0x03030303u) << 4);
+            const uint32_t vb = ((lwb >> (4 * nh)) & kM4) | (((hwb >> (2 * aq)) & 0x03030303u) << 4);
+            const uint32_t b0 = lg ? lds32(xu + 16 * i + 4 * q) : 0u;
             int c[4];
-            mma_k16_s8u8(c, a0, v);
-            const int o = live ? 32 * (int)bs[i] : 0;
-            is0 += sbyte(sw0[i >> 2], i & 3) * (c[0] - o);
-            is1 += sbyte(sw1[i >> 2], i & 3) * (c[1] - o);
+            mma_k16_u8s8_rows(c, va, vb, b0);
+            const int o0 = l0 ? 32 * (int)bs0[i] : 0, o1 = l1 ? 32 * (int)bs1[i] : 0;
+            const int sA = sbyte(swa[i >> 2], i & 3), sB = sbyte(swb[i >> 2], i & 3);
+            is[0] += sA * (c[0] - o0);
+            is[1] += sA * (c[1] - o1);
+            is[2] += sB * (c[2] - o0);
+            is[3] += sB * (c[3] - o1);
           }
         }
       }
     }
-    const uint32_t dw2 = lds32(sl + 1664 + 4 * q);
-    a[0] = __fmul_rn(__fmul_rn(h2f((uint16_t)(dw2 & 0xFFFFu)), dx), (float)is0);
-    a[1] = __fmul_rn(__fmul_rn(h2f((uint16_t)(dw2 >> 16)), dx), (float)is1);
-    b[0] = b[1] = 0.0f;
+    const float dA = h2f(*reinterpret_cast<const uint16_t*>(sa + 1664 + 2 * g));
+    const float dB = h2f(*reinterpret_cast<const uint16_t*>(sb + 1664 + 2 * g));
+    a[0] = __fmul_rn(__fmul_rn(dA, dx0), (float)is[0]);
+    a[1] = __fmul_rn(__fmul_rn(dA, dx1), (float)is[1]);
+    a[2] = __fmul_rn(__fmul_rn(dB, dx0), (float)is[2]);
+    a[3] = __fmul_rn(__fmul_rn(dB, dx1), (float)is[3]);
+    b[0] = b[1] = b[2] = b[3] = 0.0f;
   }
 }
 
@@ -508,62 +558,109 @@ __device__ __forceinline__ void emit_pair(const GemvP& p, float* y, int t, int64
   }
 }
 
-// The warp's stage sequence: tile i of its list (tile t0 + warp + i*NW of the
-// CTA's run [t0, t1)), chunk ch of n_ch, in ring slot l % n_stages.
+// The warp's stage sequence.  Warp w is split s = w % S of group r = w / S
+// (R = nw / S groups): the group takes items t0 + r, t0 + r + R, ... of the
+// CTA's run [t0, t1), the warp chunks s, s + S, ... < n_ch of each (U units
+// per chunk), in ring slot l % n_stages.  An item is a tile, or with ipt = 2
+// the tile pair (2·item, 2·item + 1) whose chunk copies land in the two
+// halves of a stage (a missing second tile of an odd count is not copied;
+// its rows are never stored).
 struct WarpStream {
-  int64_t t0, t1, tile;    // next tile to issue
-  int ch;                  // next chunk of that tile to issue
+  int64_t tile;            // next item to issue
+  int ch;                  // next chunk of that item to issue
   int64_t issued;          // stages issued so far
 };
 
-__device__ __forceinline__ void issue_stage(const GemvP& p, WarpStream& ws, int nw, uint8_t* ring, uint64_t* full) {
+__device__ __forceinline__ void issue_stage(const GemvP& p, WarpStream& ws, int split, int n_groups, int S,
+                                            uint8_t* ring, uint64_t* full) {
   const int s = (int)(ws.issued % p.n_stages);
-  const int64_t mi = p.n_mat > 1 ? ws.tile / p.tpm : 0;
-  const int64_t tl = ws.tile - mi * p.tpm;
   const int u0 = ws.ch * p.U;
   const uint32_t bytes = (uint32_t)min(p.U, p.nu - u0) * (uint32_t)p.slot_bytes;
-  mbar_arrive_expect_tx(&full[s], bytes);
-  bulk_g2s(ring + (size_t)s * p.stage_bytes, p.wl[mi] + tl * p.tile_bytes + (int64_t)u0 * p.slot_bytes, bytes,
-           &full[s]);
+  uint8_t* dst = ring + (size_t)s * p.stage_bytes;
+  if (p.ipt == 2) {
+    const int64_t ta = 2 * ws.tile;
+    const bool two = ta + 1 < p.tpm;
+    mbar_arrive_expect_tx(&full[s], two ? 2 * bytes : bytes);
+    const uint8_t* src = p.wl[0] + ta * p.tile_bytes + (int64_t)u0 * p.slot_bytes;
+    bulk_g2s(dst, src, bytes, &full[s]);
+    if (two) bulk_g2s(dst + p.half_bytes, src + p.tile_bytes, bytes, &full[s]);
+  } else {
+    const int64_t mi = p.n_mat > 1 ? ws.tile / p.tpm : 0;
+    const int64_t tl = ws.tile - mi * p.tpm;
+    mbar_arrive_expect_tx(&full[s], bytes);
+    bulk_g2s(dst, p.wl[mi] + tl * p.tile_bytes + (int64_t)u0 * p.slot_bytes, bytes, &full[s]);
+  }
   ++ws.issued;
-  if (++ws.ch == p.n_ch) {
-    ws.ch = 0;
-    ws.tile += nw;
+  ws.ch += S;
+  if (ws.ch >= p.n_ch) {
+    ws.ch = split;
+    ws.tile += n_groups;
   }
 }
 
-// MODE 0: 3..8 tokens on int8 mma.sync; MODES 1, 2: dp4a over 1 or 2 tokens.
-template <int WT, int MODE>
+// Split items (KS): the sums of an item pass from the warp of chunk c to the
+// warp of chunk c + 1 through the group's slot of shared memory, so every
+// output is still the left fold over its units in order.  A warp computes
+// its chunk's unit terms into registers and refills the stage before it
+// waits for the incoming sums; then it adds its terms in unit order and
+// passes the sums on (or, for the last chunk, runs the epilogue).  A warp
+// whose wait expired still passes the sums on, so the rest of the ring
+// ends without waiting out its own limits.
+__device__ __forceinline__ bool receive_sums(uint64_t* turn, uint32_t& n_rx, const float* slot, int lane, int n,
+                                             float* acc, bool ok, int* status) {
+  if (ok) ok = mbar_wait_bounded(turn, n_rx & 1, status, 2);
+  ok = __all_sync(0xffffffffu, ok);
+  ++n_rx;
+  if (ok)
+    for (int i = 0; i < n; ++i) acc[i] = slot[lane * 4 + i];
+  return ok;
+}
+__device__ __forceinline__ void pass_sums(uint64_t* next_turn, float* slot, int lane, int n, const float* acc) {
+  for (int i = 0; i < n; ++i) slot[lane * 4 + i] = acc[i];
+  __syncwarp();   // every lane's sums before the arrive (release) of lane 0
+  if (lane == 0) mbar_arrive(next_turn);
+}
+
+// MODES 1, 2: dp4a over 1 or 2 tokens; MODE 3: 3..8 tokens on int8
+// mma.sync with the 16 rows of a tile pair as M.  KS: the S warps of a group
+// split every item's chunks; otherwise a warp folds all units of its items.
+template <int WT, int MODE, bool KS>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * kMaxStages;
   uint64_t* act_bar = reinterpret_cast<uint64_t*>(smem) + kMaxWarps * kMaxStages;
-  uint8_t* act = smem + kHdrBytes;
+  uint64_t* turn = act_bar + 1;   // [kMaxWarps]: the sums arrived for this warp (KS)
+  float* sums = reinterpret_cast<float*>(smem + kHdrBytes);   // [R][32 lanes][4] (KS)
+  uint8_t* act = smem + kHdrBytes + p.tok_bytes;
   uint8_t* ring = act + p.act_region + (size_t)warp * p.n_stages * p.stage_bytes;
+  const int S = KS ? p.S : 1;
+  const int R = nw / S, grp = warp / S, split = warp - grp * S;
+  float* slot = sums + grp * 128;
 
   if (lane == 0) {
     for (int s = 0; s < p.n_stages; ++s) mbar_init(&full[s], 1);
+    if (KS) mbar_init(&turn[warp], 1);
     if (warp == 0) mbar_init(act_bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  // This CTA's tiles (contiguous, balanced); this warp's: every nw-th.
-  const int64_t n_tiles = p.tpm * p.n_mat;
+  // This CTA's items (contiguous, balanced); this group's: every R-th.
+  const int64_t n_items = MODE == 3 ? (p.tpm + 1) / 2 : p.tpm * p.n_mat;
+  const int64_t t0 = n_items * blockIdx.x / gridDim.x, t1 = n_items * (blockIdx.x + 1) / gridDim.x;
   WarpStream ws;
-  ws.t0 = n_tiles * blockIdx.x / gridDim.x;
-  ws.t1 = n_tiles * (blockIdx.x + 1) / gridDim.x;
-  ws.tile = ws.t0 + warp;
-  ws.ch = 0;
+  ws.tile = t0 + grp;
+  ws.ch = split;
   ws.issued = 0;
-  const int64_t my_tiles = ws.tile < ws.t1 ? (ws.t1 - ws.tile + nw - 1) / nw : 0;
-  const int64_t n_stages_total = my_tiles * p.n_ch;
+  const int64_t my_items = (grp < R && ws.tile < t1) ? (t1 - ws.tile + R - 1) / R : 0;
+  const int64_t my_chunks = split < p.n_ch ? (p.n_ch - split + S - 1) / S : 0;
+  const int64_t n_stages_total = my_items * my_chunks;
   // Weights do not depend on the previous kernel: fill the ring now.
   if (lane == 0)
-    while (ws.issued < n_stages_total && ws.issued < p.n_stages) issue_stage(p, ws, nw, ring, full);
+    while (ws.issued < n_stages_total && ws.issued < p.n_stages) issue_stage(p, ws, split, R, S, ring, full);
   __syncwarp();
 
   // Activations: after the grid dependency resolves.
@@ -587,91 +684,203 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
     quantize_image(p.x, p.x_stride, p.n_tok, ai, threadIdx.x, blockDim.x);
     __syncthreads();
   }
+  ok = __all_sync(0xffffffffu, ok);
 
   int64_t consumed = 0;
-  for (int64_t it = 0; it < my_tiles; ++it) {
-    const int64_t tile = ws.t0 + warp + it * nw;
+  uint32_t n_rx = 0;   // sums received (KS)
+  const bool last_split = !KS || ((p.n_ch - 1) % S == split);   // this warp ends every item
+  for (int64_t it = 0; it < my_items; ++it) {
+    const int64_t tile = t0 + grp + it * R;
     const int64_t mi = p.n_mat > 1 ? tile / p.tpm : 0;
     const int64_t tl = tile - mi * p.tpm;
     float* y = p.yl[mi];
-    if constexpr (MODE == 0) {
-      const int g = lane >> 2, q = lane & 3;   // token g, rows 2q and 2q+1
-      const bool live = g < p.n_tok;
-      float acc[2] = {0.0f, 0.0f};
-      for (int ch = 0; ch < p.n_ch; ++ch, ++consumed) {
+    if constexpr (MODE == 3) {
+      const int g = lane >> 2, q = lane & 3;   // rows g of tiles 2·tile and 2·tile+1, tokens 2q and 2q+1
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int64_t kc = 0; kc < my_chunks; ++kc, ++consumed) {
+        const int ch = split + (int)kc * S;
         const int s = (int)(consumed % p.n_stages);
-        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1);
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1));
+        const uint8_t* st = ring + (size_t)s * p.stage_bytes;
+        const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
+        if constexpr (!KS) {
+          if (ok) {
+            for (int u = u0; u < u1; ++u) {
+              const uint8_t* sa = st + (size_t)(u - u0) * p.slot_bytes;
+              float a[4], b[4];
+              mma_pair_terms<WT>(p, sa, sa + p.half_bytes, act, u, g, q, a, b);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                acc[i] = __fadd_rn(acc[i], a[i]);
+                if constexpr (WT == B2_Q4_K) acc[i] = __fsub_rn(acc[i], b[i]);
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0 && ok && ws.issued < n_stages_total) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_stage(p, ws, split, R, S, ring, full);
+          }
+        } else {
+          constexpr int UM = kKsPairUnits;
+          float ta[UM][4], tb[UM][4];
+          if (ok) {
+#pragma unroll
+            for (int i = 0; i < UM; ++i)
+              if (u0 + i < u1) {
+                const uint8_t* sa = st + (size_t)i * p.slot_bytes;
+                mma_pair_terms<WT>(p, sa, sa + p.half_bytes, act, u0 + i, g, q, ta[i], tb[i]);
+              }
+          }
+          __syncwarp();
+          if (lane == 0 && ok && ws.issued < n_stages_total) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_stage(p, ws, split, R, S, ring, full);
+          }
+          if (ch > 0) {
+            ok = receive_sums(&turn[warp], n_rx, slot, lane, 4, acc, ok, p.status);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = 0.0f;
+          }
+          if (ok) {
+#pragma unroll
+            for (int k = 0; k < UM; ++k)
+              if (u0 + k < u1) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  acc[i] = __fadd_rn(acc[i], ta[k][i]);
+                  if constexpr (WT == B2_Q4_K) acc[i] = __fsub_rn(acc[i], tb[k][i]);
+                }
+              }
+          }
+          if (ch + 1 < p.n_ch) pass_sums(&turn[grp * S + (ch + 1) % S], slot, lane, 4, acc);
+        }
+      }
+      if (last_split) {
+        float other[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) other[i] = __shfl_xor_sync(0xffffffffu, acc[i], 4);   // row g ^ 1
         if (ok) {
-          const uint8_t* st = ring + (size_t)s * p.stage_bytes;
-          const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
-          for (int u = u0; u < u1; ++u) {
-            float a[2], b[2];
-            mma_terms<WT>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, q, live, a, b);
-            acc[0] = __fadd_rn(acc[0], a[0]);
-            acc[1] = __fadd_rn(acc[1], a[1]);
-            if constexpr (WT == B2_Q4_K) {
-              acc[0] = __fsub_rn(acc[0], b[0]);
-              acc[1] = __fsub_rn(acc[1], b[1]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int t = 2 * q + (i & 1);
+            const int64_t row = (2 * tile + (i >> 1)) * 8 + g;
+            if (t >= p.n_tok) continue;
+            if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
+              if ((g & 1) == 0) emit_pair(p, y, t, row, acc[i], other[i]);
+            } else if (row < p.n_rows) {
+              store_y(p, y, t, row, acc[i]);
             }
           }
         }
-        __syncwarp();
-        if (lane == 0 && ok && ws.issued < n_stages_total) {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          issue_stage(p, ws, nw, ring, full);
-        }
       }
-      if (ok && live) emit_pair(p, y, g, tl * 8 + 2 * q, acc[0], acc[1]);
     } else {
       constexpr int NB = MODE;
       const int g = lane & 7, j = lane >> 3;   // tile row g, unit residue j
       float acc[NB];
 #pragma unroll
       for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
-      for (int ch = 0; ch < p.n_ch; ++ch, ++consumed) {
+      for (int64_t kc = 0; kc < my_chunks; ++kc, ++consumed) {
+        const int ch = split + (int)kc * S;
         const int s = (int)(consumed % p.n_stages);
-        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1);
-        if (ok) {
-          const uint8_t* st = ring + (size_t)s * p.stage_bytes;
-          const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
-          for (int u4 = u0; u4 < u1; u4 += 4) {
-            const int u = u4 + j;
-            float pa[NB], pb[NB];
-            if (u < u1) {
-              dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa, pb);
-            } else {
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1));
+        const uint8_t* st = ring + (size_t)s * p.stage_bytes;
+        const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
+        if constexpr (!KS) {
+          if (ok) {
+            for (int u4 = u0; u4 < u1; u4 += 4) {
+              const int u = u4 + j;
+              float pa[NB], pb[NB];
+              if (u < u1) {
+                dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa, pb);
+              } else {
 #pragma unroll
-              for (int t = 0; t < NB; ++t) pa[t] = pb[t] = 0.0f;
-            }
-            // the row's units u4, u4+1, ... in order, from lanes g, g+8, ...
-            const int n_in = min(4, u1 - u4);
+                for (int t = 0; t < NB; ++t) pa[t] = pb[t] = 0.0f;
+              }
+              // the row's units u4, u4+1, ... in order, from lanes g, g+8, ...
+              const int n_in = min(4, u1 - u4);
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              if (jj < n_in) {
+              for (int jj = 0; jj < 4; ++jj) {
+                if (jj < n_in) {
 #pragma unroll
-                for (int t = 0; t < NB; ++t) {
-                  acc[t] = __fadd_rn(acc[t], __shfl_sync(0xffffffffu, pa[t], g + 8 * jj));
-                  if constexpr (WT == B2_Q4_K) acc[t] = __fsub_rn(acc[t], __shfl_sync(0xffffffffu, pb[t], g + 8 * jj));
+                  for (int t = 0; t < NB; ++t) {
+                    acc[t] = __fadd_rn(acc[t], __shfl_sync(0xffffffffu, pa[t], g + 8 * jj));
+                    if constexpr (WT == B2_Q4_K) acc[t] = __fsub_rn(acc[t], __shfl_sync(0xffffffffu, pb[t], g + 8 * jj));
+                  }
                 }
               }
             }
           }
-        }
-        __syncwarp();
-        if (lane == 0 && ok && ws.issued < n_stages_total) {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          issue_stage(p, ws, nw, ring, full);
+          __syncwarp();
+          if (lane == 0 && ok && ws.issued < n_stages_total) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_stage(p, ws, split, R, S, ring, full);
+          }
+        } else {
+          constexpr int GM = ks_dp4a_groups(WT, NB);
+          float pa[GM][NB], pb[GM][NB];
+#pragma unroll
+          for (int k = 0; k < GM; ++k) {
+            const int u = u0 + 4 * k + j;
+            if (ok && u < u1) {
+              dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa[k], pb[k]);
+            } else {
+#pragma unroll
+              for (int t = 0; t < NB; ++t) pa[k][t] = pb[k][t] = 0.0f;
+            }
+          }
+          __syncwarp();
+          if (lane == 0 && ok && ws.issued < n_stages_total) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_stage(p, ws, split, R, S, ring, full);
+          }
+          if (ch > 0) {
+            ok = receive_sums(&turn[warp], n_rx, slot, lane, NB, acc, ok, p.status);
+          } else {
+#pragma unroll
+            for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
+          }
+          if (ok) {
+#pragma unroll
+            for (int k = 0; k < GM; ++k) {
+              const int u4 = u0 + 4 * k;
+              const int n_in = min(4, u1 - u4);
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                if (jj < n_in) {
+#pragma unroll
+                  for (int t = 0; t < NB; ++t) {
+                    acc[t] = __fadd_rn(acc[t], __shfl_sync(0xffffffffu, pa[k][t], g + 8 * jj));
+                    if constexpr (WT == B2_Q4_K)
+                      acc[t] = __fsub_rn(acc[t], __shfl_sync(0xffffffffu, pb[k][t], g + 8 * jj));
+                  }
+                }
+              }
+            }
+          }
+          if (ch + 1 < p.n_ch) pass_sums(&turn[grp * S + (ch + 1) % S], slot, lane, NB, acc);
         }
       }
-      float other[NB];
+      if (last_split) {
+        float other[NB];
 #pragma unroll
-      for (int t = 0; t < NB; ++t) other[t] = __shfl_xor_sync(0xffffffffu, acc[t], 1);   // row g ^ 1
-      if (ok && j < NB) {
-        const int64_t row = tl * 8 + g;
-        if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
-          if ((g & 1) == 0) emit_pair(p, y, j, row, acc[j], other[j]);
-        } else if (row < p.n_rows) {
-          store_y(p, y, j, row, acc[j]);
+        for (int t = 0; t < NB; ++t) other[t] = __shfl_xor_sync(0xffffffffu, acc[t], 1);   // row g ^ 1
+        // lane (g, j < NB) stores token j (selected without indexing the register arrays)
+        float mine = acc[0], theirs = other[0];
+#pragma unroll
+        for (int t = 1; t < NB; ++t)
+          if (j == t) {
+            mine = acc[t];
+            theirs = other[t];
+          }
+        if (ok && j < NB) {
+          const int64_t row = tl * 8 + g;
+          if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
+            if ((g & 1) == 0) emit_pair(p, y, j, row, mine, theirs);
+          } else if (row < p.n_rows) {
+            store_y(p, y, j, row, mine);
+          }
         }
       }
     }
@@ -692,21 +901,24 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
 
 constexpr int kSmemCap = 227 * 1024;
 
-template <int WT, int MODE>
+template <int WT, int MODE, bool KS>
 int set_attr() {
-  B2_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<WT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap));
+  B2_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<WT, MODE, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap));
   return B2_OK;
 }
 
 template <int WT>
 int set_attr_all() {
-  int rc = set_attr<WT, 0>();
-  if (!rc) rc = set_attr<WT, 1>();
-  if (!rc) rc = set_attr<WT, 2>();
+  int rc = set_attr<WT, 1, false>();
+  if (!rc) rc = set_attr<WT, 2, false>();
+  if (!rc) rc = set_attr<WT, 3, false>();
+  if (!rc) rc = set_attr<WT, 1, true>();
+  if (!rc) rc = set_attr<WT, 2, true>();
+  if (!rc) rc = set_attr<WT, 3, true>();
   return rc;
 }
 
-template <int WT, int MODE>
+template <int WT, int MODE, bool KS>
 int launch_t(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -718,15 +930,20 @@ int launch_t(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<WT, MODE>, p));
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<WT, MODE, KS>, p));
   return B2_OK;
+}
+
+template <int WT, bool KS>
+int launch_k(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
+  if (p.ipt == 2) return launch_t<WT, 3, KS>(p, grid, nw, smem, s);
+  if (p.n_tok == 1) return launch_t<WT, 1, KS>(p, grid, nw, smem, s);
+  return launch_t<WT, 2, KS>(p, grid, nw, smem, s);
 }
 
 template <int WT>
 int launch_w(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
-  if (p.n_tok > kDp4aMaxTok) return launch_t<WT, 0>(p, grid, nw, smem, s);
-  if (p.n_tok == 1) return launch_t<WT, 1>(p, grid, nw, smem, s);
-  return launch_t<WT, 2>(p, grid, nw, smem, s);
+  return p.S > 1 ? launch_k<WT, true>(p, grid, nw, smem, s) : launch_k<WT, false>(p, grid, nw, smem, s);
 }
 
 int launch_quantize_image(const float* x, int64_t x_stride, int n_tok, const ActImage& g, cudaStream_t s) {
@@ -860,35 +1077,78 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   const bool in_kernel = !a.image_ready && !gemv_needs_image(w, a.n_tok);
   p.act_img = in_kernel ? nullptr : a.act_img;
   if (a.epilogue == EPI_ROPE_KV) p.rope = *a.rope;
-  // Geometry.  One CTA per SM over a contiguous run of tiles; as many warps
-  // as the run has tiles (up to 8), so every warp streams and folds its own.
-  // Each warp's ring gets an equal share of the shared memory left after the
-  // activations: with small activations about 110 KB in all, so that two
-  // CTAs fit on an SM and the next launch's weights stream while this one
-  // finishes.  A stage is as many unit slots as fit half the share (the
-  // whole tile when it fits the share: one bulk copy per tile).
+  // Geometry.  One CTA per SM over a contiguous run of items: 8-row tiles
+  // for 1-2 tokens, tile pairs for 3..8 (one rows-as-M mma covers 16 rows x
+  // 8 tokens).  With more than kKsMaxItems items per CTA every warp folds
+  // whole items (up to 8 warps, 16 with pairs); with fewer, the CTA runs one
+  // group of S warps per item and the S warps split the item's units in
+  // chunks of U (KS), so that up to 16 warps stream and compute even when
+  // the CTA has one or two items.  Each warp's ring gets an equal share of
+  // the shared memory left after the activations; with small activations
+  // and at most 8 warps that is about 110 KB in all, so that two CTAs fit
+  // on an SM and the next launch's weights stream while this one finishes.
   p.tpm = w.n_tiles;
-  const int64_t n_tiles = p.tpm * p.n_mat;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), n_tiles));
-  const int64_t per_cta = (n_tiles + grid - 1) / grid;
-  const int nw = (int)std::max<int64_t>(1, std::min<int64_t>(8, per_cta));
-  const size_t cap = in_kernel && a.n_mat == 1 ? (size_t)110 * 1024 : (size_t)kSmemCap;
-  const size_t fixed = kHdrBytes + p.act_region;
-  if (fixed + (size_t)nw * w.slot_bytes > cap) {
+  const int sms = sm_count();
+  const bool pairs = a.n_tok > kDp4aMaxTok;
+  p.ipt = pairs ? 2 : 1;
+  const int64_t n_items = pairs ? (w.n_tiles + 1) / 2 : p.tpm * p.n_mat;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, n_items));
+  const int64_t per_cta = (n_items + grid - 1) / grid;
+  const int gran = pairs ? 1 : 4;   // units that one step of the fold takes
+  int S = 1, nw, U = 0;
+  static const int ks_warps = getenv("B2_GEMV_KS_WARPS") ? atoi(getenv("B2_GEMV_KS_WARPS")) : kMaxWarps;   // TUNING PROBE
+  if (per_cta <= kKsMaxItems) {
+    const int64_t n_gran = (w.nu + gran - 1) / gran;
+    S = (int)std::min<int64_t>(ks_warps / per_cta, n_gran);
+    if (S >= 2) {
+      const int64_t per_warp = (n_gran + S - 1) / S;
+      U = gran * (int)std::min<int64_t>(pairs ? kKsPairUnits : ks_dp4a_groups(w.type, a.n_tok), per_warp);
+      S = (int)std::min<int64_t>(S, (w.nu + U - 1) / U);   // every warp gets a chunk
+    }
+    if (S < 2) S = 1;
+  }
+  const size_t item_slot = (size_t)p.ipt * w.slot_bytes, item_bytes = (size_t)p.ipt * w.tile_bytes;
+  // Split items: the chunk shrinks to what fits the warp's share of shared
+  // memory (two stages where possible); where not even one fold step fits,
+  // the item gets fewer warps.
+  size_t cap = 0, fixed = 0;
+  while (S > 1) {
+    nw = (int)per_cta * S;
+    p.tok_bytes = (uint32_t)per_cta * 32 * 4 * 4;
+    cap = in_kernel && a.n_mat == 1 && nw <= 8 ? (size_t)110 * 1024 : (size_t)kSmemCap;
+    fixed = kHdrBytes + p.tok_bytes + p.act_region;
+    const size_t share = fixed < cap ? (cap - fixed) / nw : 0;
+    const int two = (int)(share / 2 / item_slot) / gran * gran, one = (int)(share / item_slot) / gran * gran;
+    if (one >= gran) {
+      U = std::min(U, two >= gran ? two : one);
+      S = (int)std::min<int64_t>(S, (w.nu + U - 1) / U);
+      nw = (int)per_cta * S;
+      break;
+    }
+    --S;
+  }
+  p.S = S;
+  if (S <= 1) {
+    nw = (int)std::max<int64_t>(1, std::min<int64_t>(pairs ? 16 : 8, per_cta));
+    p.tok_bytes = 0;
+    cap = in_kernel && a.n_mat == 1 && nw <= 8 ? (size_t)110 * 1024 : (size_t)kSmemCap;
+    fixed = kHdrBytes + p.act_region;
+  }
+  if (fixed >= cap || (S <= 1 && fixed + (size_t)nw * item_slot > cap)) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
   }
   const size_t share = (cap - fixed) / nw;
-  const bool dp4a = a.n_tok <= kDp4aMaxTok;
-  const int64_t tiles_per_warp = (per_cta + nw - 1) / nw;
-  int U;
-  if ((size_t)w.tile_bytes <= share && (tiles_per_warp <= 1 || (size_t)w.tile_bytes * 2 <= share)) {
-    U = w.nu;   // whole tiles
-  } else {
-    U = (int)std::max<size_t>(1, std::min<size_t>(w.nu, share / 2 / w.slot_bytes));
-    if (dp4a && U < w.nu) U = std::max(4, U / 4 * 4);   // the dp4a fold takes units four at a time
+  if (S == 1) {
+    const int64_t items_per_warp = (per_cta + nw - 1) / nw;
+    if (item_bytes <= share && (items_per_warp <= 1 || item_bytes * 2 <= share)) {
+      U = w.nu;   // whole items
+    } else {
+      U = (int)std::max<size_t>(1, std::min<size_t>(w.nu, share / 2 / item_slot));
+      if (!pairs && U < w.nu) U = std::max(4, U / 4 * 4);   // the dp4a fold takes units four at a time
+    }
   }
-  const size_t stage = (size_t)U * w.slot_bytes;
+  const size_t stage = (size_t)U * item_slot;
   if (stage > share) {
     set_error("gemv: no stage of unit slots fits for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
@@ -896,6 +1156,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.U = U;
   p.n_ch = (w.nu + U - 1) / U;
   p.n_stages = (int)std::max<size_t>(1, std::min<size_t>(kMaxStages, share / stage));
+  p.half_bytes = (uint32_t)((size_t)U * w.slot_bytes);
   p.stage_bytes = (uint32_t)stage;
   const size_t smem = fixed + (size_t)nw * p.n_stages * stage;
   if (!in_kernel && !a.image_ready) {

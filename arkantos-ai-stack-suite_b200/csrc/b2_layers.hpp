@@ -25,15 +25,15 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
                    cudaStream_t s);
 // Decode attention in the reference's order (b2_attn.cu): q fp32
 // [n_tok][n_head][hd] against the fp16 caches [n_seq][n_kv][cap][hd], out
-// fp32 [n_tok][n_head][hd].  `scores` is scratch of attn_scratch_floats
-// floats (16-byte aligned); `count` is [n_tok][n_kv] counters that must be zero before the
-// first launch and are left zero by every launch.  Queries whose sequence id
-// is outside [0, n_seq) or whose position is outside [0, cap) read nothing
-// and produce zero outputs.  st may be null (plain layout).
+// fp32 [n_tok][n_head][hd].  `scratch` holds attn_scratch_floats floats
+// (16-byte aligned) of scores, exponentials and chunk maxima; it needs no
+// initialisation.  Queries whose sequence id is outside [0, n_seq) or whose
+// position is outside [0, cap) read nothing and produce zero outputs.  st
+// may be null (plain layout).
 size_t attn_scratch_floats(int n_tok, int n_head, int n_kv, int cap);
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scores,
-                     unsigned int* count, float* out, cudaStream_t s, int* status = nullptr);
+                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scratch,
+                     float* out, cudaStream_t s, int* status = nullptr);
 // h [n_tok][ff] = silu(gate) * up over the (gate, up) row pairs of gu
 // [n_tok][2 ff], with the arithmetic of the GEMV's SwiGLU epilogue.
 int launch_swiglu_pairs(const float* gu, int n_tok, int ff, float* h, cudaStream_t s);

@@ -3,7 +3,7 @@
 // device-memory budget at start-up, and real-time decode loops that must not
 // take an allocation's latency or risk its failure in the middle of a turn.
 //
-// The attention's scores and arrival counters live in one file-scope
+// The attention's scratch (scores, exponentials, chunk maxima) lives in one file-scope
 // __device__ array of B2_NOALLOC_SCRATCH_BYTES; every GPU that loads the
 // library holds that array until the process exits.  The caller still passes q, the caches and out.
 // The array's device address is taken with cudaGetSymbolAddress the first
@@ -26,7 +26,6 @@ namespace {
 constexpr size_t kScratchBytes = (size_t)B2_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
 
-// [scores / probabilities][arrival counters]
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 std::mutex g_mu;
@@ -67,24 +66,17 @@ extern "C" int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, c
     set_error("attn_decode_noalloc: n_q=%d outside [1, %d]", n_q, B2_NOALLOC_MAX_QUERIES);
     return B2_ERR_INVALID;
   }
-  // [scores / probabilities][arrival counters]
   const size_t sc_bytes = attn_scratch_floats(n_q, n_head, n_kv, cap) * sizeof(float);
-  const size_t cnt_off = (sc_bytes + 255) / 256 * 256;
-  const size_t cnt_bytes = (size_t)n_q * n_kv * sizeof(unsigned int);
-  if (cnt_off + cnt_bytes > kScratchBytes) {
+  if (sc_bytes > kScratchBytes) {
     set_error("attn_decode_noalloc: %d queries x %d heads x %d positions need %zu scratch bytes, "
               "more than the %zu built in",
-              n_q, n_head, cap, cnt_off + cnt_bytes, kScratchBytes);
+              n_q, n_head, cap, sc_bytes, kScratchBytes);
     return B2_ERR_INVALID;
   }
   void* base = nullptr;
   const int rc = scratch_address(static_cast<cudaStream_t>(stream), &base);
   if (rc) return rc;
-  uint8_t* b = static_cast<uint8_t*>(base);
-  // The counters must start at zero (a previous call leaves them zero, but a
-  // call that failed part-way may not); the scores are rewritten by the call.
-  B2_CUDA_TRY(cudaMemsetAsync(b + cnt_off, 0, cnt_bytes, static_cast<cudaStream_t>(stream)));
+  // every value the kernels read is written earlier in the same call
   return launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap,
-                          reinterpret_cast<float*>(b), reinterpret_cast<unsigned int*>(b + cnt_off), out,
-                          static_cast<cudaStream_t>(stream));
+                          static_cast<float*>(base), out, static_cast<cudaStream_t>(stream));
 }

@@ -246,13 +246,14 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
  * run (a host that gives the library a fixed device-memory budget at
  * start-up, or a real-time decode loop that must not pay an allocation's
  * latency or risk its failure mid-turn).  No counterpart in the reference.
- * Same arguments and results as b2_attn_decode; the scores and the arrival
- * counters live in one static device array of B2_NOALLOC_SCRATCH_BYTES that
- * every GPU loading the library holds until exit.  Limits: n_q <=
- * B2_NOALLOC_MAX_QUERIES and the scores and probabilities, n_q·n_kv·capS·
- * (G + max(G, 4))·4 bytes with G = n_head/n_kv and capS = cap rounded up to
- * 4 (2·n_q·n_head·cap·4 for G >= 4), plus n_q·n_kv counters, within the
- * array (larger requests return B2_ERR_INVALID).  The first
+ * Same arguments and results as b2_attn_decode; the scratch (scores,
+ * exponentials, chunk maxima) lives in one static device array of
+ * B2_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit.  Limits: n_q <= B2_NOALLOC_MAX_QUERIES and the scratch,
+ * n_q·n_kv·(capS·(G + max(G, 4)) + G·nchS)·4 bytes with G = n_head/n_kv,
+ * capS = cap rounded up to 4 and nchS = ceil(cap/128) rounded up to 4
+ * (about 2·n_q·n_head·cap·4 for G >= 4), within the array (larger requests
+ * return B2_ERR_INVALID).  The first
  * call on a device looks up the array's address (call it once before any
  * stream capture); calls outside capture look it up again, so a device reset
  * between calls is picked up, while a call under capture uses the address

@@ -110,9 +110,25 @@ def test_gemv_matches_oracle(t, n, k, n_tok):
 @pytest.mark.parametrize("n,k", [(6144, 4096), (2048, 14336)])
 @pytest.mark.parametrize("n_tok", [1, 3, 8])
 def test_gemv_many_items_per_cta(t, n, k, n_tok):
-    """Enough rows that every warp works several tiles, so the stage rings
-    wrap many times: bit-exact with the reference order."""
+    """A few items per SM: the warps of a group split each item's units and
+    pass the partial sums on in unit order, with several chunks per warp so
+    that the stage rings wrap: bit-exact with the reference order."""
     q = _weights(t, n, k, 41)
+    m = b2.QMatrix(t, q, n, k)
+    x = np.random.default_rng(n + k + n_tok).standard_normal((n_tok, k)).astype(np.float32)
+    got = m.gemv(x)
+    assert np.array_equal(_bits(got), _bits(O.gemv(t, q, n, k, x))), "not bit-exact with the reference order"
+
+
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("n,k,n_tok", [(9480, 1024, 1), (9480, 1024, 2), (19000, 1024, 3), (19000, 1024, 5),
+                                       (18945, 2048, 7), (28672, 4096, 8)])
+def test_gemv_whole_items(t, n, k, n_tok):
+    """More than eight items per SM: every warp folds whole items (8-row
+    tiles for 1-2 tokens; for 3..8 tokens tile pairs, the 16 rows of two
+    tiles as the M of one rows-as-M mma, an odd tile count leaving the last
+    pair one tile short).  Bit-exact with the reference order."""
+    q = _weights(t, n, k, 43)
     m = b2.QMatrix(t, q, n, k)
     x = np.random.default_rng(n + k + n_tok).standard_normal((n_tok, k)).astype(np.float32)
     got = m.gemv(x)

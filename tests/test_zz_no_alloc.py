@@ -1,13 +1,15 @@
 """The allocation-free decode attention entry point, for callers that cannot
 allocate device memory while they run (a fixed device-memory budget handed
 to the library at start-up, or a real-time decode loop that must not pay an
-allocation's latency).  It must give the same result as b2_attn_decode —
-the attention tests' bar is bit-identity with the kernel's evaluation order,
-so the two entry points must agree bit for bit — on two calls in a row, the
-second with new inputs over the shared static scratch, and must refuse
-requests larger than its built-in scratch.  This file is collected last."""
+allocation's latency).  It must give the same result as b2_attn_decode,
+bit for bit, and the reference's order (the oracle) for the first query, on
+two calls in a row, the second with new inputs over the shared static
+scratch, and must refuse requests larger than its built-in scratch.  This
+file is collected last."""
 import numpy as np
 import pytest
+
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -40,10 +42,14 @@ def test_noalloc_attention_matches_allocating_entry_point_twice(n_q, cap, n_head
         want = _run(b2.lib.b2_attn_decode, q, kc, vc, pos, seq, n_head, n_kv, hd, cap)
         got = _run(b2.lib.b2_attn_decode_noalloc, q, kc, vc, pos, seq, n_head, n_kv, hd, cap)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"call {call} differs"
+        # query 0 (sequence 0) against the reference's order
+        ref = O.attn_decode(q[0], kc[0].transpose(1, 0, 2).reshape(cap, n_kv * hd), vc[0].transpose(1, 0, 2).reshape(
+            cap, n_kv * hd), int(pos[0]) + 1, n_head, n_kv, hd)
+        assert np.array_equal(got[0].view(np.uint32), ref.view(np.uint32)), f"call {call}: not the reference order"
 
 
 def test_noalloc_attention_rejects_oversize_requests():
-    n_q, n_head, n_kv, hd, cap = 64, 32, 8, 128, 8192      # 2·64·32·8192·4 bytes (~134 MB) > the built-in scratch
+    n_q, n_head, n_kv, hd, cap = 64, 32, 8, 128, 8192      # 64·8·(8192·8 + 4·64)·4 bytes (~134 MB) > 32 MiB
     q = np.zeros((n_q, n_head * hd), np.float32)
     kc = np.zeros((1, n_kv, cap, hd), np.uint16)
     pos = np.zeros(n_q, np.int32)
