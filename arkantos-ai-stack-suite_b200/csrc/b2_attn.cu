@@ -142,14 +142,21 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   float* srow = grp;                           // head g's scores at srow + g * capS
   float* mrow = grp + m_offset(G, cap);        // head g's chunk maxima at mrow + g * nchS
   const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
-  if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    fence_mbar_init();
-    mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * HD * 2));
+  if (warp == 0) {
+    // one lane per run of consecutive slots (at most three): a bulk copy
+    // costs its issuing thread a few hundred cycles, copies from different
+    // lanes overlap
+    if (lane == 0) {
+      mbar_init(&bar[0], 1);
+      fence_mbar_init();
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * HD * 2));
     const int64_t base = ((int64_t)s * n_kv + kh) * cap;
-    for (int p = t0; p < t0 + n;) {
+    int p = t0;
+    for (int r_i = 0; p < t0 + n; ++r_i) {
       const SlotRun r = slot_run(sst, p, t0 + n, cap, P);
-      bulk_g2s(ks + (p - t0) * HD, kc + (base + r.slot) * HD, (uint32_t)(r.len * HD * 2), &bar[0]);
+      if (lane == r_i) bulk_g2s(ks + (p - t0) * HD, kc + (base + r.slot) * HD, (uint32_t)(r.len * HD * 2), &bar[0]);
       p += r.len;
     }
   }
@@ -376,13 +383,11 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
     const int len = min(WA, n_pos - w0), len4 = (len + 3) & ~3;
     const int plen = ((len + kSumParts - 1) / kSumParts + 3) & ~3;
     __syncthreads();   // the previous window is consumed
-    if (warp == 1 && lane == 0 && ok) {
+    if (warp == 1 && lane < kSumParts && lane * plen < len && ok) {   // lane i copies part i
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      for (int i = 0; i < kSumParts && i * plen < len; ++i) {
-        const int a = i * plen, n4 = min(plen, len4 - a);
-        mbar_arrive_expect_tx(&part[i], (uint32_t)(n4 * GP * 4));
-        bulk_g2s(stages + (size_t)a * GP * 4, erow + (int64_t)(w0 + a) * GP, (uint32_t)(n4 * GP * 4), &part[i]);
-      }
+      const int a = lane * plen, n4 = min(plen, len4 - a);
+      mbar_arrive_expect_tx(&part[lane], (uint32_t)(n4 * GP * 4));
+      bulk_g2s(stages + (size_t)a * GP * 4, erow + (int64_t)(w0 + a) * GP, (uint32_t)(n4 * GP * 4), &part[lane]);
     }
     if (warp == 0 && lane < G) {
       const float* e = reinterpret_cast<const float*>(stages) + lane;
@@ -405,20 +410,24 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
 
   // ---- P.V phase ----
   if (warp == 1) {
+    // Every lane keeps the issue position; lane 0 copies a chunk's V rows,
+    // lane 1 its E rows (a bulk copy costs its issuing thread a few hundred
+    // cycles, copies from different lanes overlap).
     int p_iss = 0, c_iss = 0;
     auto issue = [&](int si) {
       const SlotRun r = slot_run(sst, p_iss, n_pos, cap, CH);
       uint8_t* sp = stages + si * SB;
-      mbar_arrive_expect_tx(&full[si], (uint32_t)(CH * DS * 2 + r.len * GP * 4));
-      tma_load_2d(sp, &vmap, d0, row0 + (int)r.slot, &full[si]);
-      bulk_g2s(sp + CH * DS * 2, erow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[si], (uint32_t)(CH * DS * 2 + r.len * GP * 4));
+        tma_load_2d(sp, &vmap, d0, row0 + (int)r.slot, &full[si]);
+      } else if (lane == 1) {
+        bulk_g2s(sp + CH * DS * 2, erow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
+      }
       p_iss += r.len;
       ++c_iss;
     };
-    if (lane == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      while (p_iss < n_pos && c_iss < NS) issue(c_iss % NS);
-    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    while (p_iss < n_pos && c_iss < NS) issue(c_iss % NS);
     __syncwarp();
     float inv[G];
 #pragma unroll
@@ -460,12 +469,10 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
         }
       }
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&conv[si]);
-        if (ok && p_iss < n_pos) {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          issue(si);
-        }
+      if (lane == 0) mbar_arrive(&conv[si]);
+      if (ok && p_iss < n_pos) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(si);
       }
       __syncwarp();
       p += len;

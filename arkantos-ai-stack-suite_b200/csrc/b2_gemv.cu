@@ -51,7 +51,12 @@ namespace {
 
 constexpr int kMaxWarps = 16;
 constexpr int kMaxStages = 8;            // ring stages per warp
-constexpr int kHdrBytes = 1280;          // full[kMaxWarps][kMaxStages], act barrier, turn[kMaxWarps], padding
+// Shared memory header: full[kMaxWarps][kMaxStages] mbarriers (per warp, or per
+// group with split items), the activation mbarrier, turn[kMaxWarps], the
+// split groups' used[kMaxWarps][kMaxStages] counters and issued[kMaxWarps].
+constexpr int kUsedOff = (kMaxWarps * kMaxStages + 1 + kMaxWarps) * 8;
+constexpr int kIssuedOff = kUsedOff + kMaxWarps * kMaxStages * 4;
+constexpr int kHdrBytes = (kIssuedOff + kMaxWarps * 4 + 127) / 128 * 128;
 constexpr int kMaxTok = 8;
 constexpr int kDp4aMaxTok = 2;           // dp4a up to this many tokens, mma.sync above
 constexpr int kKsMaxItems = 8;           // items per CTA up to which the warps of a group split each item
@@ -71,10 +76,11 @@ struct GemvP {
   int64_t y_stride;
   int epilogue;
   int U, n_ch, n_stages;   // units per stage, stages per item, ring stages per warp
+  int Ug;                  // units per group stage (split items)
   int ipt;                 // tiles per item: 1, or 2 (the rows-as-M pairs of MODE 3)
   int S;                   // warps per item (split items, KS), else 1
   uint32_t tok_bytes;      // the groups' slots for passing sums (KS)
-  uint32_t half_bytes;     // U * slot_bytes: one tile's share of a stage
+  uint32_t half_bytes;     // one tile's share of a stage: U (Ug with split items) unit slots
   uint32_t stage_bytes;    // ipt * half_bytes
   int kq;                  // activation row stride in bytes
   uint32_t off_dx, off_bs, act_bytes, act_region;   // activation carve-up and its shared-memory size
@@ -357,25 +363,28 @@ __device__ __forceinline__ void dp4a_terms(const GemvP& p, const uint8_t* sl, co
 // ---- rows-as-M path: the terms of one unit u of two tiles for lane 4g+q ---------------------
 // i = 2·(tile B) + (token 2q+1): a[i] / b[i] as in dp4a_terms for row g of
 // tile A (i = 0, 1) or of tile B (i = 2, 3) and token 2q (i even) or 2q+1.
-// The B fragment is token g's codes; tokens at or past n_tok feed zeros.
+// The B fragment is token g's codes.  Tokens at or past n_tok read the last
+// token's data instead: a column of the mma only feeds the outputs of its own
+// token, and those outputs are never stored.
 template <int WT>
 __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa, const uint8_t* sb,
                                                const uint8_t* act, int u, int g, int q, float (&a)[4],
                                                float (&b)[4]) {
-  const bool lg = g < p.n_tok, l0 = 2 * q < p.n_tok, l1 = 2 * q + 1 < p.n_tok;
+  const int last = p.n_tok - 1;
+  const int tg = min(g, last), t0 = min(2 * q, last), t1 = min(2 * q + 1, last);
   const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
   const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
-  const float dx0 = l0 ? dxs[(2 * q) * p.nu + u] : 0.0f, dx1 = l1 ? dxs[(2 * q + 1) * p.nu + u] : 0.0f;
-  const uint8_t* xr = act + g * p.kq;
+  const float dx0 = dxs[t0 * p.nu + u], dx1 = dxs[t1 * p.nu + u];
+  const uint8_t* xr = act + tg * p.kq;
   if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
     const uint8_t* xb = xr + u * 32;
-    const uint32_t b0 = lg ? lds32(xb + 4 * q) : 0u, b1 = lg ? lds32(xb + 16 + 4 * q) : 0u;
+    const uint32_t b0 = lds32(xb + 4 * q), b1 = lds32(xb + 16 + 4 * q);
     int c[4];
     float dA, dB;
     if constexpr (WT == B2_Q4_0) {
       const uint32_t wa = lds32(sa + 16 * g + 4 * q), wb = lds32(sb + 16 * g + 4 * q);
       mma_k32_u8s8_rows(c, wa & kM4, wb & kM4, (wa >> 4) & kM4, (wb >> 4) & kM4, b0, b1);
-      const int k0 = l0 ? 8 * (int)bss[(2 * q) * p.nu + u] : 0, k1 = l1 ? 8 * (int)bss[(2 * q + 1) * p.nu + u] : 0;
+      const int k0 = 8 * (int)bss[t0 * p.nu + u], k1 = 8 * (int)bss[t1 * p.nu + u];
       c[0] -= k0;
       c[1] -= k1;
       c[2] -= k0;
@@ -409,7 +418,7 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int j = 2 * jc + h;   // 32-weight group
-        const uint32_t b0 = lg ? lds32(xu + 32 * j + 4 * q) : 0u, b1 = lg ? lds32(xu + 32 * j + 16 + 4 * q) : 0u;
+        const uint32_t b0 = lds32(xu + 32 * j + 4 * q), b1 = lds32(xu + 32 * j + 16 + 4 * q);
         const int sh = 4 * h;
         int c[4];
         mma_k32_u8s8_rows(c, (w0a >> sh) & kM4, (w0b >> sh) & kM4, (w1a >> sh) & kM4, (w1b >> sh) & kM4, b0, b1);
@@ -421,9 +430,8 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
         is[3] += sB * c[3];
       }
     }
-    const uint4 z4 = make_uint4(0, 0, 0, 0);
-    const uint4 bq0 = l0 ? lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q) * p.nu + u) * 8)) : z4;
-    const uint4 bq1 = l1 ? lds128(reinterpret_cast<const uint8_t*>(bss + ((2 * q + 1) * p.nu + u) * 8)) : z4;
+    const uint4 bq0 = lds128(reinterpret_cast<const uint8_t*>(bss + (t0 * p.nu + u) * 8));
+    const uint4 bq1 = lds128(reinterpret_cast<const uint8_t*>(bss + (t1 * p.nu + u) * 8));
     const int ms[4] = {q4k_msum(bq0, mlA, mhA), q4k_msum(bq1, mlA, mhA), q4k_msum(bq0, mlB, mhB),
                        q4k_msum(bq1, mlB, mhB)};
     const float ddA = h2f((uint16_t)(ma.x & 0xFFFFu)), dmA = h2f((uint16_t)(ma.x >> 16));
@@ -441,8 +449,8 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
     const uint8_t* qhb = sb + 1024 + 64 * g;
     const uint4 sca = lds128(sa + 1536 + 16 * g), scb = lds128(sb + 1536 + 16 * g);
     const uint32_t swa[4] = {sca.x, sca.y, sca.z, sca.w}, swb[4] = {scb.x, scb.y, scb.z, scb.w};
-    const int16_t* bs0 = bss + ((2 * q) * p.nu + u) * 16;
-    const int16_t* bs1 = bss + ((2 * q + 1) * p.nu + u) * 16;
+    const int16_t* bs0 = bss + (t0 * p.nu + u) * 16;
+    const int16_t* bs1 = bss + (t1 * p.nu + u) * 16;
     const uint8_t* xu = xr + u * 256;
     int is[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -461,10 +469,10 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
             const int i = hh * 8 + aq * 2 + hf;  // 16-weight group of the super-block
             const uint32_t va = ((lwa >> (4 * nh)) & kM4) | (((hwa >> (2 * aq)) & 0x03030303u) << 4);
             const uint32_t vb = ((lwb >> (4 * nh)) & kM4) | (((hwb >> (2 * aq)) & 0x03030303u) << 4);
-            const uint32_t b0 = lg ? lds32(xu + 16 * i + 4 * q) : 0u;
+            const uint32_t b0 = lds32(xu + 16 * i + 4 * q);
             int c[4];
             mma_k16_u8s8_rows(c, va, vb, b0);
-            const int o0 = l0 ? 32 * (int)bs0[i] : 0, o1 = l1 ? 32 * (int)bs1[i] : 0;
+            const int o0 = 32 * (int)bs0[i], o1 = 32 * (int)bs1[i];
             const int sA = sbyte(swa[i >> 2], i & 3), sB = sbyte(swb[i >> 2], i & 3);
             is[0] += sA * (c[0] - o0);
             is[1] += sA * (c[1] - o1);
@@ -558,54 +566,96 @@ __device__ __forceinline__ void emit_pair(const GemvP& p, float* y, int t, int64
   }
 }
 
-// The warp's stage sequence.  Warp w is split s = w % S of group r = w / S
-// (R = nw / S groups): the group takes items t0 + r, t0 + r + R, ... of the
-// CTA's run [t0, t1), the warp chunks s, s + S, ... < n_ch of each (U units
-// per chunk), in ring slot l % n_stages.  An item is a tile, or with ipt = 2
-// the tile pair (2·item, 2·item + 1) whose chunk copies land in the two
-// halves of a stage (a missing second tile of an odd count is not copied;
-// its rows are never stored).
-struct WarpStream {
-  int64_t tile;            // next item to issue
-  int ch;                  // next chunk of that item to issue
-  int64_t issued;          // stages issued so far
-};
+// Whole items (S = 1): warp w takes items t0 + w, t0 + w + nw, ... of the
+// CTA's run [t0, t1), chunk ch of n_ch of each (U units per chunk), through
+// its own ring of stages, slot l % n_stages.  An item is a tile, or with
+// ipt = 2 the tile pair (2·item, 2·item + 1) whose chunk copies land in the
+// two halves of a stage (a missing second tile of an odd count is not
+// copied; its rows are never stored).
 
-__device__ __forceinline__ void issue_stage(const GemvP& p, WarpStream& ws, int split, int n_groups, int S,
-                                            uint8_t* ring, uint64_t* full) {
-  const int s = (int)(ws.issued % p.n_stages);
-  const int u0 = ws.ch * p.U;
-  const uint32_t bytes = (uint32_t)min(p.U, p.nu - u0) * (uint32_t)p.slot_bytes;
-  uint8_t* dst = ring + (size_t)s * p.stage_bytes;
+// A bulk copy costs its issuing thread about 300 cycles whatever its size,
+// while copies issued by different lanes overlap, so a stage's copies (and
+// the stages of a ring fill) go out from different lanes.  Part `part` of a
+// stage: part 0 arms the barrier with the whole stage's bytes and copies
+// tile A's units [u0, u0 + n) of item `item`; part 1 copies tile B's (pairs;
+// not for a missing second tile of an odd count, whose rows are never
+// stored).  The barrier's transaction count may run ahead of the arming; the
+// phase cannot complete before the arming arrival.
+__device__ __forceinline__ void copy_part(const GemvP& p, int64_t item, int u0, int n, uint32_t half, uint8_t* dst,
+                                          uint64_t* bar, int part) {
+  const uint32_t bytes = (uint32_t)n * (uint32_t)p.slot_bytes;
   if (p.ipt == 2) {
-    const int64_t ta = 2 * ws.tile;
+    const int64_t ta = 2 * item;
     const bool two = ta + 1 < p.tpm;
-    mbar_arrive_expect_tx(&full[s], two ? 2 * bytes : bytes);
     const uint8_t* src = p.wl[0] + ta * p.tile_bytes + (int64_t)u0 * p.slot_bytes;
-    bulk_g2s(dst, src, bytes, &full[s]);
-    if (two) bulk_g2s(dst + p.half_bytes, src + p.tile_bytes, bytes, &full[s]);
-  } else {
-    const int64_t mi = p.n_mat > 1 ? ws.tile / p.tpm : 0;
-    const int64_t tl = ws.tile - mi * p.tpm;
-    mbar_arrive_expect_tx(&full[s], bytes);
-    bulk_g2s(dst, p.wl[mi] + tl * p.tile_bytes + (int64_t)u0 * p.slot_bytes, bytes, &full[s]);
-  }
-  ++ws.issued;
-  ws.ch += S;
-  if (ws.ch >= p.n_ch) {
-    ws.ch = split;
-    ws.tile += n_groups;
+    if (part == 0) {
+      mbar_arrive_expect_tx(bar, two ? 2 * bytes : bytes);
+      bulk_g2s(dst, src, bytes, bar);
+    } else if (two) {
+      bulk_g2s(dst + half, src + p.tile_bytes, bytes, bar);
+    }
+  } else if (part == 0) {
+    const int64_t mi = p.n_mat > 1 ? item / p.tpm : 0;
+    const int64_t tl = item - mi * p.tpm;
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_g2s(dst, p.wl[mi] + tl * p.tile_bytes + (int64_t)u0 * p.slot_bytes, bytes, bar);
   }
 }
 
-// Split items (KS): the sums of an item pass from the warp of chunk c to the
-// warp of chunk c + 1 through the group's slot of shared memory, so every
-// output is still the left fold over its units in order.  A warp computes
-// its chunk's unit terms into registers and refills the stage before it
-// waits for the incoming sums; then it adds its terms in unit order and
-// passes the sums on (or, for the last chunk, runs the epilogue).  A warp
-// whose wait expired still passes the sums on, so the rest of the ring
-// ends without waiting out its own limits.
+// Stage l of a whole-items warp: item item0 + (l / n_ch)·nw, chunk l % n_ch,
+// slot l % n_stages; lanes [l·ipt, l·ipt + ipt) of `lane0` onwards issue it.
+__device__ __forceinline__ void issue_stage(const GemvP& p, int64_t item0, int64_t l, int nw, uint8_t* ring,
+                                            uint64_t* full, int part) {
+  const int s = (int)(l % p.n_stages);
+  const int64_t it = l / p.n_ch;
+  const int u0 = (int)(l - it * p.n_ch) * p.U;
+  copy_part(p, item0 + it * nw, u0, min(p.U, p.nu - u0), p.half_bytes, ring + (size_t)s * p.stage_bytes, &full[s],
+            part);
+}
+
+// Split items (KS): the S warps of a group share one item and one ring of
+// stages of Ug units (both tiles of a pair: one bulk copy per tile and
+// stage, so that few, large copies carry the weights).  Warp s of the group
+// takes chunks s, s + S, ... of U units; chunk c lies in stage c / (Ug / U).
+// The last warp to finish with a stage refills it (an acq_rel counter per
+// stage slot), so no warp waits for another to release a stage.
+__device__ __forceinline__ void issue_gstage(const GemvP& p, int64_t item, int k, uint8_t* ring, uint64_t* full,
+                                             int* issued, int part) {
+  const int slot = k % p.n_stages, u0 = k * p.Ug;
+  copy_part(p, item, u0, min(p.Ug, p.nu - u0), p.half_bytes, ring + (size_t)slot * p.stage_bytes, &full[slot], part);
+  if (part == 0) atomicAdd(issued, 1);
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel(unsigned int* a, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(smem_u32(a)), "r"(v) : "memory");
+  return old;
+}
+// After the warp has read chunk c (stage k): count it, and if it was the
+// stage's last chunk, refill the slot with stage k + n_stages (lanes 0 and 1
+// for the two tiles of a pair).
+__device__ __forceinline__ void release_chunk(const GemvP& p, int64_t item, int k, int cps, int n_gst,
+                                              unsigned int* used, uint8_t* ring, uint64_t* full, int* issued,
+                                              bool ok, int lane) {
+  __syncwarp();
+  int refill = 0;
+  if (lane == 0) {
+    const int slot = k % p.n_stages;
+    const unsigned int prev = atom_add_acq_rel(&used[slot], 1u);
+    refill = prev == (unsigned int)((k / p.n_stages + 1) * cps - 1) && ok && k + p.n_stages < n_gst;
+    if (refill) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  refill = __shfl_sync(0xffffffffu, refill, 0);
+  if (refill && lane < p.ipt) issue_gstage(p, item, k + p.n_stages, ring, full, issued, lane);
+}
+
+// The running sums of a split item pass from the warp of chunk c to the warp
+// of chunk c + 1 through the group's slot of shared memory, so every output
+// is still the left fold over its units in order.  A warp computes its
+// chunk's unit terms into registers and releases the stage before it waits
+// for the incoming sums; then it adds its terms in unit order and passes the
+// sums on (or, for the last chunk, runs the epilogue).  A warp whose wait
+// expired still passes the sums on, so the rest of the ring ends without
+// waiting out its own limits.
 __device__ __forceinline__ bool receive_sums(uint64_t* turn, uint32_t& n_rx, const float* slot, int lane, int n,
                                              float* acc, bool ok, int* status) {
   if (ok) ok = mbar_wait_bounded(turn, n_rx & 1, status, 2);
@@ -621,26 +671,97 @@ __device__ __forceinline__ void pass_sums(uint64_t* next_turn, float* slot, int 
   if (lane == 0) mbar_arrive(next_turn);
 }
 
+// Epilogue of tile pair `item` for lane 4g+q (MODE 3): rows g of both tiles,
+// tokens 2q and 2q+1.
+__device__ __forceinline__ void pair_epilogue(const GemvP& p, float* y, int64_t item, int g, int q, const float (&acc)[4],
+                                              bool ok) {
+  float other[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) other[i] = __shfl_xor_sync(0xffffffffu, acc[i], 4);   // row g ^ 1
+  if (!ok) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = 2 * q + (i & 1);
+    const int64_t row = (2 * item + (i >> 1)) * 8 + g;
+    if (t >= p.n_tok) continue;
+    if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
+      if ((g & 1) == 0) emit_pair(p, y, t, row, acc[i], other[i]);
+    } else if (row < p.n_rows) {
+      store_y(p, y, t, row, acc[i]);
+    }
+  }
+}
+
+// Epilogue of tile tl for lane (g, j) (dp4a modes): lanes j < NB store token j
+// of row g (the token selected without indexing the register arrays).
+template <int NB>
+__device__ __forceinline__ void tile_epilogue(const GemvP& p, float* y, int64_t tl, int g, int j, const float (&acc)[NB],
+                                              bool ok) {
+  float other[NB];
+#pragma unroll
+  for (int t = 0; t < NB; ++t) other[t] = __shfl_xor_sync(0xffffffffu, acc[t], 1);   // row g ^ 1
+  float mine = acc[0], theirs = other[0];
+#pragma unroll
+  for (int t = 1; t < NB; ++t)
+    if (j == t) {
+      mine = acc[t];
+      theirs = other[t];
+    }
+  if (ok && j < NB) {
+    const int64_t row = tl * 8 + g;
+    if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
+      if ((g & 1) == 0) emit_pair(p, y, j, row, mine, theirs);
+    } else if (row < p.n_rows) {
+      store_y(p, y, j, row, mine);
+    }
+  }
+}
+
+// The row's units u4, u4+1, ... (fewer than 4 at the end) in order, from
+// lanes g, g+8, ... (dp4a modes).
+template <int WT, int NB>
+__device__ __forceinline__ void fold4(float (&acc)[NB], const float (&pa)[NB], const float (&pb)[NB], int n_in, int g) {
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    if (jj < n_in) {
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+        acc[t] = __fadd_rn(acc[t], __shfl_sync(0xffffffffu, pa[t], g + 8 * jj));
+        if constexpr (WT == B2_Q4_K) acc[t] = __fsub_rn(acc[t], __shfl_sync(0xffffffffu, pb[t], g + 8 * jj));
+      }
+    }
+  }
+}
+
 // MODES 1, 2: dp4a over 1 or 2 tokens; MODE 3: 3..8 tokens on int8
 // mma.sync with the 16 rows of a tile pair as M.  KS: the S warps of a group
-// split every item's chunks; otherwise a warp folds all units of its items.
+// split one item; otherwise every warp folds whole items.
 template <int WT, int MODE, bool KS>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * kMaxStages;
-  uint64_t* act_bar = reinterpret_cast<uint64_t*>(smem) + kMaxWarps * kMaxStages;
-  uint64_t* turn = act_bar + 1;   // [kMaxWarps]: the sums arrived for this warp (KS)
-  float* sums = reinterpret_cast<float*>(smem + kHdrBytes);   // [R][32 lanes][4] (KS)
-  uint8_t* act = smem + kHdrBytes + p.tok_bytes;
-  uint8_t* ring = act + p.act_region + (size_t)warp * p.n_stages * p.stage_bytes;
   const int S = KS ? p.S : 1;
   const int R = nw / S, grp = warp / S, split = warp - grp * S;
+  const int ring_id = KS ? grp : warp;   // the group's ring (KS) or the warp's own
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem) + ring_id * kMaxStages;
+  uint64_t* act_bar = reinterpret_cast<uint64_t*>(smem) + kMaxWarps * kMaxStages;
+  uint64_t* turn = act_bar + 1;   // [kMaxWarps]: the sums arrived for this warp (KS)
+  unsigned int* used = reinterpret_cast<unsigned int*>(smem + kUsedOff) + grp * kMaxStages;   // KS
+  int* issued_g = reinterpret_cast<int*>(smem + kIssuedOff) + grp;                            // KS
+  float* sums = reinterpret_cast<float*>(smem + kHdrBytes);   // [R][32 lanes][4] (KS)
+  uint8_t* act = smem + kHdrBytes + p.tok_bytes;
+  uint8_t* ring = act + p.act_region + (size_t)ring_id * p.n_stages * p.stage_bytes;
   float* slot = sums + grp * 128;
 
   if (lane == 0) {
-    for (int s = 0; s < p.n_stages; ++s) mbar_init(&full[s], 1);
+    if (!KS || split == 0) {
+      for (int s = 0; s < p.n_stages; ++s) mbar_init(&full[s], 1);
+      if (KS) {
+        for (int s = 0; s < p.n_stages; ++s) used[s] = 0u;
+        *issued_g = 0;
+      }
+    }
     if (KS) mbar_init(&turn[warp], 1);
     if (warp == 0) mbar_init(act_bar, 1);
     fence_mbar_init();
@@ -648,19 +769,29 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
   __syncthreads();
   pdl_launch_dependents();
 
-  // This CTA's items (contiguous, balanced); this group's: every R-th.
+  // This CTA's items (contiguous, balanced).
   const int64_t n_items = MODE == 3 ? (p.tpm + 1) / 2 : p.tpm * p.n_mat;
   const int64_t t0 = n_items * blockIdx.x / gridDim.x, t1 = n_items * (blockIdx.x + 1) / gridDim.x;
-  WarpStream ws;
-  ws.tile = t0 + grp;
-  ws.ch = split;
-  ws.issued = 0;
-  const int64_t my_items = (grp < R && ws.tile < t1) ? (t1 - ws.tile + R - 1) / R : 0;
-  const int64_t my_chunks = split < p.n_ch ? (p.n_ch - split + S - 1) / S : 0;
-  const int64_t n_stages_total = my_items * my_chunks;
-  // Weights do not depend on the previous kernel: fill the ring now.
-  if (lane == 0)
-    while (ws.issued < n_stages_total && ws.issued < p.n_stages) issue_stage(p, ws, split, R, S, ring, full);
+  // KS: the group's one item; otherwise the warp's items, every nw-th.
+  const int64_t item0 = t0 + (KS ? grp : warp);
+  const int64_t my_items = KS ? (grp < R && item0 < t1 ? 1 : 0) : (item0 < t1 ? (t1 - item0 + nw - 1) / nw : 0);
+  const int my_chunks = KS ? (split < p.n_ch ? (p.n_ch - split + S - 1) / S : 0) : p.n_ch;
+  const int cps = KS ? p.Ug / p.U : 1;               // chunks per group stage
+  const int n_gst = KS ? (p.nu + p.Ug - 1) / p.Ug : 0;
+  const int64_t n_stages_total = KS ? 0 : my_items * p.n_ch;
+  // Weights do not depend on the previous kernel: fill the ring now, one
+  // stage per lane (two lanes per stage for pairs).
+  int64_t issued = 0;   // whole items: stages issued so far (every lane keeps the count)
+  {
+    const int st_lane = lane / p.ipt, part = lane - st_lane * p.ipt;
+    if constexpr (KS) {
+      if (my_items && split == 0 && st_lane < n_gst && st_lane < p.n_stages)
+        issue_gstage(p, item0, st_lane, ring, full, issued_g, part);
+    } else {
+      issued = min(n_stages_total, (int64_t)p.n_stages);
+      if (st_lane < issued) issue_stage(p, item0, st_lane, nw, ring, full, part);
+    }
+  }
   __syncwarp();
 
   // Activations: after the grid dependency resolves.
@@ -686,24 +817,23 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
   }
   ok = __all_sync(0xffffffffu, ok);
 
-  int64_t consumed = 0;
-  uint32_t n_rx = 0;   // sums received (KS)
-  const bool last_split = !KS || ((p.n_ch - 1) % S == split);   // this warp ends every item
+  int64_t consumed = 0;   // stages consumed (whole items)
+  uint32_t n_rx = 0;      // sums received (KS)
+  const bool last_split = !KS || ((p.n_ch - 1) % S == split);   // this warp ends the item
   for (int64_t it = 0; it < my_items; ++it) {
-    const int64_t tile = t0 + grp + it * R;
-    const int64_t mi = p.n_mat > 1 ? tile / p.tpm : 0;
-    const int64_t tl = tile - mi * p.tpm;
+    const int64_t item = item0 + it * nw;   // KS: one item
+    const int64_t mi = p.n_mat > 1 ? item / p.tpm : 0;
+    const int64_t tl = item - mi * p.tpm;
     float* y = p.yl[mi];
     if constexpr (MODE == 3) {
-      const int g = lane >> 2, q = lane & 3;   // rows g of tiles 2·tile and 2·tile+1, tokens 2q and 2q+1
+      const int g = lane >> 2, q = lane & 3;   // rows g of tiles 2·item and 2·item+1, tokens 2q and 2q+1
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int64_t kc = 0; kc < my_chunks; ++kc, ++consumed) {
-        const int ch = split + (int)kc * S;
-        const int s = (int)(consumed % p.n_stages);
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1));
-        const uint8_t* st = ring + (size_t)s * p.stage_bytes;
-        const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
+      for (int kc = 0; kc < my_chunks; ++kc) {
         if constexpr (!KS) {
+          const int s = (int)(consumed % p.n_stages);
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1));
+          const uint8_t* st = ring + (size_t)s * p.stage_bytes;
+          const int u0 = kc * p.U, u1 = min(u0 + p.U, p.nu);
           if (ok) {
             for (int u = u0; u < u1; ++u) {
               const uint8_t* sa = st + (size_t)(u - u0) * p.slot_bytes;
@@ -717,12 +847,20 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
             }
           }
           __syncwarp();
-          if (lane == 0 && ok && ws.issued < n_stages_total) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_stage(p, ws, split, R, S, ring, full);
+          if (ok && issued < n_stages_total) {
+            if (lane < p.ipt) {
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              issue_stage(p, item0, issued, nw, ring, full, lane);
+            }
+            ++issued;
           }
+          ++consumed;
         } else {
           constexpr int UM = kKsPairUnits;
+          const int ch = split + kc * S, k = ch / cps, sl = k % p.n_stages;
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[sl], (uint32_t)((k / p.n_stages) & 1), p.status, 1));
+          const uint8_t* st = ring + (size_t)sl * p.stage_bytes + (size_t)(ch - k * cps) * p.U * p.slot_bytes;
+          const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
           float ta[UM][4], tb[UM][4];
           if (ok) {
 #pragma unroll
@@ -732,11 +870,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
                 mma_pair_terms<WT>(p, sa, sa + p.half_bytes, act, u0 + i, g, q, ta[i], tb[i]);
               }
           }
-          __syncwarp();
-          if (lane == 0 && ok && ws.issued < n_stages_total) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_stage(p, ws, split, R, S, ring, full);
-          }
+          release_chunk(p, item, k, cps, n_gst, used, ring, full, issued_g, ok, lane);
           if (ch > 0) {
             ok = receive_sums(&turn[warp], n_rx, slot, lane, 4, acc, ok, p.status);
           } else {
@@ -745,49 +879,31 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
           }
           if (ok) {
 #pragma unroll
-            for (int k = 0; k < UM; ++k)
-              if (u0 + k < u1) {
+            for (int kk = 0; kk < UM; ++kk)
+              if (u0 + kk < u1) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                  acc[i] = __fadd_rn(acc[i], ta[k][i]);
-                  if constexpr (WT == B2_Q4_K) acc[i] = __fsub_rn(acc[i], tb[k][i]);
+                  acc[i] = __fadd_rn(acc[i], ta[kk][i]);
+                  if constexpr (WT == B2_Q4_K) acc[i] = __fsub_rn(acc[i], tb[kk][i]);
                 }
               }
           }
           if (ch + 1 < p.n_ch) pass_sums(&turn[grp * S + (ch + 1) % S], slot, lane, 4, acc);
         }
       }
-      if (last_split) {
-        float other[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) other[i] = __shfl_xor_sync(0xffffffffu, acc[i], 4);   // row g ^ 1
-        if (ok) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int t = 2 * q + (i & 1);
-            const int64_t row = (2 * tile + (i >> 1)) * 8 + g;
-            if (t >= p.n_tok) continue;
-            if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
-              if ((g & 1) == 0) emit_pair(p, y, t, row, acc[i], other[i]);
-            } else if (row < p.n_rows) {
-              store_y(p, y, t, row, acc[i]);
-            }
-          }
-        }
-      }
+      if (last_split) pair_epilogue(p, y, item, g, q, acc, ok);
     } else {
       constexpr int NB = MODE;
       const int g = lane & 7, j = lane >> 3;   // tile row g, unit residue j
       float acc[NB];
 #pragma unroll
       for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
-      for (int64_t kc = 0; kc < my_chunks; ++kc, ++consumed) {
-        const int ch = split + (int)kc * S;
-        const int s = (int)(consumed % p.n_stages);
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1));
-        const uint8_t* st = ring + (size_t)s * p.stage_bytes;
-        const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
+      for (int kc = 0; kc < my_chunks; ++kc) {
         if constexpr (!KS) {
+          const int s = (int)(consumed % p.n_stages);
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)((consumed / p.n_stages) & 1), p.status, 1));
+          const uint8_t* st = ring + (size_t)s * p.stage_bytes;
+          const int u0 = kc * p.U, u1 = min(u0 + p.U, p.nu);
           if (ok) {
             for (int u4 = u0; u4 < u1; u4 += 4) {
               const int u = u4 + j;
@@ -798,43 +914,36 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
 #pragma unroll
                 for (int t = 0; t < NB; ++t) pa[t] = pb[t] = 0.0f;
               }
-              // the row's units u4, u4+1, ... in order, from lanes g, g+8, ...
-              const int n_in = min(4, u1 - u4);
-#pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                if (jj < n_in) {
-#pragma unroll
-                  for (int t = 0; t < NB; ++t) {
-                    acc[t] = __fadd_rn(acc[t], __shfl_sync(0xffffffffu, pa[t], g + 8 * jj));
-                    if constexpr (WT == B2_Q4_K) acc[t] = __fsub_rn(acc[t], __shfl_sync(0xffffffffu, pb[t], g + 8 * jj));
-                  }
-                }
-              }
+              fold4<WT, NB>(acc, pa, pb, min(4, u1 - u4), g);
             }
           }
           __syncwarp();
-          if (lane == 0 && ok && ws.issued < n_stages_total) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_stage(p, ws, split, R, S, ring, full);
+          if (ok && issued < n_stages_total) {
+            if (lane < p.ipt) {
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              issue_stage(p, item0, issued, nw, ring, full, lane);
+            }
+            ++issued;
           }
+          ++consumed;
         } else {
           constexpr int GM = ks_dp4a_groups(WT, NB);
+          const int ch = split + kc * S, k = ch / cps, sl = k % p.n_stages;
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[sl], (uint32_t)((k / p.n_stages) & 1), p.status, 1));
+          const uint8_t* st = ring + (size_t)sl * p.stage_bytes + (size_t)(ch - k * cps) * p.U * p.slot_bytes;
+          const int u0 = ch * p.U, u1 = min(u0 + p.U, p.nu);
           float pa[GM][NB], pb[GM][NB];
 #pragma unroll
-          for (int k = 0; k < GM; ++k) {
-            const int u = u0 + 4 * k + j;
+          for (int kk = 0; kk < GM; ++kk) {
+            const int u = u0 + 4 * kk + j;
             if (ok && u < u1) {
-              dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa[k], pb[k]);
+              dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa[kk], pb[kk]);
             } else {
 #pragma unroll
-              for (int t = 0; t < NB; ++t) pa[k][t] = pb[k][t] = 0.0f;
+              for (int t = 0; t < NB; ++t) pa[kk][t] = pb[kk][t] = 0.0f;
             }
           }
-          __syncwarp();
-          if (lane == 0 && ok && ws.issued < n_stages_total) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_stage(p, ws, split, R, S, ring, full);
-          }
+          release_chunk(p, item, k, cps, n_gst, used, ring, full, issued_g, ok, lane);
           if (ch > 0) {
             ok = receive_sums(&turn[warp], n_rx, slot, lane, NB, acc, ok, p.status);
           } else {
@@ -843,52 +952,30 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
           }
           if (ok) {
 #pragma unroll
-            for (int k = 0; k < GM; ++k) {
-              const int u4 = u0 + 4 * k;
-              const int n_in = min(4, u1 - u4);
-#pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                if (jj < n_in) {
-#pragma unroll
-                  for (int t = 0; t < NB; ++t) {
-                    acc[t] = __fadd_rn(acc[t], __shfl_sync(0xffffffffu, pa[k][t], g + 8 * jj));
-                    if constexpr (WT == B2_Q4_K)
-                      acc[t] = __fsub_rn(acc[t], __shfl_sync(0xffffffffu, pb[k][t], g + 8 * jj));
-                  }
-                }
-              }
+            for (int kk = 0; kk < GM; ++kk) {
+              const int u4 = u0 + 4 * kk;
+              if (u4 < u1) fold4<WT, NB>(acc, pa[kk], pb[kk], min(4, u1 - u4), g);
             }
           }
           if (ch + 1 < p.n_ch) pass_sums(&turn[grp * S + (ch + 1) % S], slot, lane, NB, acc);
         }
       }
-      if (last_split) {
-        float other[NB];
-#pragma unroll
-        for (int t = 0; t < NB; ++t) other[t] = __shfl_xor_sync(0xffffffffu, acc[t], 1);   // row g ^ 1
-        // lane (g, j < NB) stores token j (selected without indexing the register arrays)
-        float mine = acc[0], theirs = other[0];
-#pragma unroll
-        for (int t = 1; t < NB; ++t)
-          if (j == t) {
-            mine = acc[t];
-            theirs = other[t];
-          }
-        if (ok && j < NB) {
-          const int64_t row = tl * 8 + g;
-          if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
-            if ((g & 1) == 0) emit_pair(p, y, j, row, mine, theirs);
-          } else if (row < p.n_rows) {
-            store_y(p, y, j, row, mine);
-          }
-        }
-      }
+      if (last_split) tile_epilogue<NB>(p, y, tl, g, j, acc, ok);
     }
   }
-  // A warp that stopped early waits (bounded) for the copies it still has in flight.
-  if (!ok && lane == 0) {
-    for (int64_t l = consumed; l < ws.issued; ++l)
-      mbar_wait_bounded(&full[l % p.n_stages], (uint32_t)((l / p.n_stages) & 1), nullptr, 0);
+  // Copies still in flight after a failed wait: wait for them (bounded).
+  if constexpr (KS) {
+    const bool any_fail = __syncthreads_or(!ok);
+    if (any_fail && my_items && split == 0 && lane == 0) {
+      const int n_iss = *issued_g;
+      for (int k = max(0, n_iss - p.n_stages); k < n_iss; ++k)
+        mbar_wait_bounded(&full[k % p.n_stages], (uint32_t)((k / p.n_stages) & 1), nullptr, 0);
+    }
+  } else {
+    if (!ok && lane == 0) {
+      for (int64_t l = consumed; l < issued; ++l)
+        mbar_wait_bounded(&full[l % p.n_stages], (uint32_t)((l / p.n_stages) & 1), nullptr, 0);
+    }
   }
   if (p.peer.n) {
     // Every thread's peer stores are ordered before the CTA barrier; the
@@ -1108,37 +1195,53 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
     if (S < 2) S = 1;
   }
   const size_t item_slot = (size_t)p.ipt * w.slot_bytes, item_bytes = (size_t)p.ipt * w.tile_bytes;
-  // Split items: the chunk shrinks to what fits the warp's share of shared
-  // memory (two stages where possible); where not even one fold step fits,
-  // the item gets fewer warps.
+  // Split items: the group's stages hold the whole item where it fits the
+  // group's share of shared memory, else as many whole chunk rounds (S
+  // chunks of U units) as fit twice; where not even that fits, the chunk and
+  // then the number of warps shrink.
   size_t cap = 0, fixed = 0;
+  int Ug = 0;
   while (S > 1) {
     nw = (int)per_cta * S;
     p.tok_bytes = (uint32_t)per_cta * 32 * 4 * 4;
     cap = in_kernel && a.n_mat == 1 && nw <= 8 ? (size_t)110 * 1024 : (size_t)kSmemCap;
     fixed = kHdrBytes + p.tok_bytes + p.act_region;
-    const size_t share = fixed < cap ? (cap - fixed) / nw : 0;
-    const int two = (int)(share / 2 / item_slot) / gran * gran, one = (int)(share / item_slot) / gran * gran;
-    if (one >= gran) {
-      U = std::min(U, two >= gran ? two : one);
-      S = (int)std::min<int64_t>(S, (w.nu + U - 1) / U);
-      nw = (int)per_cta * S;
+    const size_t share_g = fixed < cap ? (cap - fixed) / per_cta : 0;
+    const int n_ch = (w.nu + U - 1) / U;
+    if ((size_t)n_ch * U * item_slot <= share_g) {
+      Ug = n_ch * U;   // the whole item in one stage
+      break;
+    }
+    const int fit = (int)(share_g / 2 / item_slot);   // units per stage with two stages
+    if (fit >= S * U) {
+      Ug = fit / (S * U) * (S * U);
+      break;
+    }
+    const int u_fit = fit / S / gran * gran;
+    if (u_fit >= gran) {
+      U = u_fit;
+      Ug = S * U;
       break;
     }
     --S;
   }
-  p.S = S;
-  if (S <= 1) {
+  if (S > 1) {
+    S = (int)std::min<int64_t>(S, (w.nu + U - 1) / U);   // every warp gets a chunk
+    nw = (int)per_cta * S;
+  } else {
+    S = 1;
     nw = (int)std::max<int64_t>(1, std::min<int64_t>(pairs ? 16 : 8, per_cta));
     p.tok_bytes = 0;
     cap = in_kernel && a.n_mat == 1 && nw <= 8 ? (size_t)110 * 1024 : (size_t)kSmemCap;
     fixed = kHdrBytes + p.act_region;
   }
-  if (fixed >= cap || (S <= 1 && fixed + (size_t)nw * item_slot > cap)) {
+  p.S = S;
+  if (fixed >= cap || (S == 1 && fixed + (size_t)nw * item_slot > cap)) {
     set_error("gemv: shared memory too small for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
   }
-  const size_t share = (cap - fixed) / nw;
+  const int n_rings = S > 1 ? (int)per_cta : nw;   // rings: one per group (split items) or per warp
+  const size_t share = (cap - fixed) / n_rings;
   if (S == 1) {
     const int64_t items_per_warp = (per_cta + nw - 1) / nw;
     if (item_bytes <= share && (items_per_warp <= 1 || item_bytes * 2 <= share)) {
@@ -1147,18 +1250,20 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
       U = (int)std::max<size_t>(1, std::min<size_t>(w.nu, share / 2 / item_slot));
       if (!pairs && U < w.nu) U = std::max(4, U / 4 * 4);   // the dp4a fold takes units four at a time
     }
+    Ug = U;
   }
-  const size_t stage = (size_t)U * item_slot;
+  const size_t stage = (size_t)Ug * item_slot;
   if (stage > share) {
     set_error("gemv: no stage of unit slots fits for n_tok=%d k=%lld", a.n_tok, (long long)w.k);
     return B2_ERR_UNSUPPORTED;
   }
   p.U = U;
+  p.Ug = Ug;
   p.n_ch = (w.nu + U - 1) / U;
   p.n_stages = (int)std::max<size_t>(1, std::min<size_t>(kMaxStages, share / stage));
-  p.half_bytes = (uint32_t)((size_t)U * w.slot_bytes);
+  p.half_bytes = (uint32_t)((size_t)Ug * w.slot_bytes);
   p.stage_bytes = (uint32_t)stage;
-  const size_t smem = fixed + (size_t)nw * p.n_stages * stage;
+  const size_t smem = fixed + (size_t)n_rings * p.n_stages * stage;
   if (!in_kernel && !a.image_ready) {
     const int qrc = launch_quantize_image(a.x, a.x_stride, a.n_tok, ag, s);
     if (qrc) return qrc;
