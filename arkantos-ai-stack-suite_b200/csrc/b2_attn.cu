@@ -80,6 +80,17 @@ __device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
 struct Ones {
   uint64_t one, neg_zero;
 };
+// The two halves of mul_add2: p = a·b (rounded), acc + p (rounded).
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b, const Ones& k) {
+  uint64_t p;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(a), "l"(b), "l"(k.neg_zero));
+  return p;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t acc, uint64_t p, const Ones& k) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(p), "l"(k.one), "l"(acc));
+  return r;
+}
 __device__ __forceinline__ uint64_t mul_add2(uint64_t acc, uint64_t a, uint64_t b, const Ones& k) {
   uint64_t p, r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(a), "l"(b), "l"(k.neg_zero));
@@ -302,27 +313,41 @@ __device__ __forceinline__ uint64_t u64_of(uint32_t lo, uint32_t hi) {
 }
 
 // l = Σ_t e_t in position order for lane g < G, over rows e[t * GP + g] of
-// shared memory: the next 16 values are read while the current 16 are added,
-// so no add waits on a load.
+// shared memory.  Two buffers of 16 values take turns: the next 16 are read
+// while the current 16 are added (a warp issues in order: each read sits
+// between two adds, in the latency of the chain), and no register copies
+// sit between the adds.
 template <int GP>
 __device__ __forceinline__ float sum_run(const float* e, int a, int b, float l) {
-  const int n16 = a + ((b - a) & ~15);
-  float cur[16], nxt[16];
-  if (n16 > a) {
+  const int n32 = a + ((b - a) & ~31);
+  float A[16], B[16];
+  if (n32 > a) {
 #pragma unroll
-    for (int k = 0; k < 16; ++k) cur[k] = e[(a + k) * GP];
+    for (int k = 0; k < 16; ++k) A[k] = e[(a + k) * GP];
   }
-  for (int i = a; i < n16; i += 16) {
-    if (i + 16 < n16) {
+  for (int i = a; i < n32; i += 32) {
+    // each add followed by the read of the value 16 ahead, so the reads
+    // issue in the adds' latency
 #pragma unroll
-      for (int k = 0; k < 16; ++k) nxt[k] = e[(i + 16 + k) * GP];
+    for (int k = 0; k < 16; ++k) {
+      B[k] = e[(i + 16 + k) * GP];
+      l = __fadd_rn(l, A[k]);
     }
+    const int in = i + 32 < n32 ? i + 32 : i;   // the last trip re-reads in range
 #pragma unroll
-    for (int k = 0; k < 16; ++k) l = __fadd_rn(l, cur[k]);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) cur[k] = nxt[k];
+    for (int k = 0; k < 16; ++k) {
+      A[k] = e[(in + k) * GP];
+      l = __fadd_rn(l, B[k]);
+    }
   }
-  for (int i = n16; i < b; ++i) l = __fadd_rn(l, e[i * GP]);
+  // the last (fewer than 32) values: all reads first, then the adds
+  const int rem = b - n32;
+  float T[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) T[k] = k < rem ? e[(n32 + k) * GP] : 0.0f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k)
+    if (k < rem) l = __fadd_rn(l, T[k]);
   return l;
 }
 
@@ -502,38 +527,59 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
       const uint64_t* vr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4) + j * kPvChP;
       const uint64_t* pr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4) +
                            (DS / 2) * kPvChP + g * kPvChP;
-      // positions in groups of 8, two per 16-byte load: the next group's
-      // (p, v) are read while the current group's chain runs, so no step
-      // waits on a shared-memory load
-      const int len8 = len & ~7;
-      uint4 cp[4], cv[4], np_[4], nv[4];
-      if (len8 > 0) {
+      // positions in groups of 8, two per 16-byte load, in two buffers that
+      // take turns: the next group's (p, v) are read while the current
+      // group's chain runs, with no register copies between the steps
+      const int len16 = len & ~15;
+      uint4 ap[4], av[4], bp[4], bv[4];
+      if (len16 > 0) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          cp[k] = *reinterpret_cast<const uint4*>(pr + 2 * k);
-          cv[k] = *reinterpret_cast<const uint4*>(vr + 2 * k);
+          ap[k] = *reinterpret_cast<const uint4*>(pr + 2 * k);
+          av[k] = *reinterpret_cast<const uint4*>(vr + 2 * k);
         }
       }
-      for (int t = 0; t < len8; t += 8) {
-        if (t + 8 < len8) {
+      for (int t = 0; t < len16; t += 16) {
+        // the 8 products of the group first, then the 8 adds in position
+        // order with the next group's reads between them
+        uint64_t pa[8];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            np_[k] = *reinterpret_cast<const uint4*>(pr + t + 8 + 2 * k);
-            nv[k] = *reinterpret_cast<const uint4*>(vr + t + 8 + 2 * k);
-          }
+        for (int k = 0; k < 4; ++k) {
+          pa[2 * k] = mul2(u64_of(ap[k].x, ap[k].y), u64_of(av[k].x, av[k].y), k2);
+          pa[2 * k + 1] = mul2(u64_of(ap[k].z, ap[k].w), u64_of(av[k].z, av[k].w), k2);
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          acc = mul_add2(acc, u64_of(cp[k].x, cp[k].y), u64_of(cv[k].x, cv[k].y), k2);
-          acc = mul_add2(acc, u64_of(cp[k].z, cp[k].w), u64_of(cv[k].z, cv[k].w), k2);
+          bp[k] = *reinterpret_cast<const uint4*>(pr + t + 8 + 2 * k);
+          bv[k] = *reinterpret_cast<const uint4*>(vr + t + 8 + 2 * k);
+          acc = add2(acc, pa[2 * k], k2);
+          acc = add2(acc, pa[2 * k + 1], k2);
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          cp[k] = np_[k];
-          cv[k] = nv[k];
+          pa[2 * k] = mul2(u64_of(bp[k].x, bp[k].y), u64_of(bv[k].x, bv[k].y), k2);
+          pa[2 * k + 1] = mul2(u64_of(bp[k].z, bp[k].w), u64_of(bv[k].z, bv[k].w), k2);
+        }
+        const int tn = t + 16 < len16 ? t + 16 : t;   // the last trip re-reads in range
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          ap[k] = *reinterpret_cast<const uint4*>(pr + tn + 2 * k);
+          av[k] = *reinterpret_cast<const uint4*>(vr + tn + 2 * k);
+          acc = add2(acc, pa[2 * k], k2);
+          acc = add2(acc, pa[2 * k + 1], k2);
         }
       }
-      for (int t = len8; t < len; ++t) acc = mul_add2(acc, pr[t], vr[t], k2);
+      // the last (fewer than 16) positions: all reads first, then the steps
+      const int rem = len - len16;
+      uint64_t tp[16], tv[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        tp[k] = k < rem ? pr[len16 + k] : 0ull;
+        tv[k] = k < rem ? vr[len16 + k] : 0ull;
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (k < rem) acc = mul_add2(acc, tp[k], tv[k], k2);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[si]);

@@ -944,6 +944,18 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
             }
           }
           release_chunk(p, item, k, cps, n_gst, used, ring, full, issued_g, ok, lane);
+          // every lane of row g gathers the row's unit terms before the sums
+          // arrive, so only the adds remain on the ring's path
+          float sa[GM][4][NB], sb[GM][4][NB];
+#pragma unroll
+          for (int kk = 0; kk < GM; ++kk)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+              for (int t = 0; t < NB; ++t) {
+                sa[kk][jj][t] = __shfl_sync(0xffffffffu, pa[kk][t], g + 8 * jj);
+                if constexpr (WT == B2_Q4_K) sb[kk][jj][t] = __shfl_sync(0xffffffffu, pb[kk][t], g + 8 * jj);
+              }
           if (ch > 0) {
             ok = receive_sums(&turn[warp], n_rx, slot, lane, NB, acc, ok, p.status);
           } else {
@@ -952,10 +964,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
           }
           if (ok) {
 #pragma unroll
-            for (int kk = 0; kk < GM; ++kk) {
-              const int u4 = u0 + 4 * kk;
-              if (u4 < u1) fold4<WT, NB>(acc, pa[kk], pb[kk], min(4, u1 - u4), g);
-            }
+            for (int kk = 0; kk < GM; ++kk)
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj)
+                if (u0 + 4 * kk + jj < u1) {
+#pragma unroll
+                  for (int t = 0; t < NB; ++t) {
+                    acc[t] = __fadd_rn(acc[t], sa[kk][jj][t]);
+                    if constexpr (WT == B2_Q4_K) acc[t] = __fsub_rn(acc[t], sb[kk][jj][t]);
+                  }
+                }
           }
           if (ch + 1 < p.n_ch) pass_sums(&turn[grp * S + (ch + 1) % S], slot, lane, NB, acc);
         }
