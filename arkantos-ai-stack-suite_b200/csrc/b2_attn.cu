@@ -194,17 +194,35 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
     uint64_t acc[NP];
 #pragma unroll
     for (int j = 0; j < NP; ++j) acc[j] = 0ull;   // (+0, +0)
-#pragma unroll
+    // 16 dims per trip (the body stays small enough for the instruction
+    // cache); a half2 of K turns into two floats at once, and one 16-byte
+    // read brings two head pairs of q
+#pragma unroll 2
     for (int c = 0; c < NPc; ++c) {
       const uint4 rc = *reinterpret_cast<const uint4*>(rp + 16 * c);
       const uint32_t w4[4] = {rc.x, rc.y, rc.z, rc.w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float kv = h2f((uint16_t)((w4[e >> 1] >> (16 * (e & 1))) & 0xFFFFu));
-        const uint64_t kk = pack2(kv, kv);
-        const int d = 8 * c + e;
+      for (int e2 = 0; e2 < 4; ++e2) {
+        const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&w4[e2]));
+        const float kv2[2] = {kf.x, kf.y};
 #pragma unroll
-        for (int j = 0; j < NP; ++j) acc[j] = mul_add2(acc[j], qs[d * NP + j], kk, k2);
+        for (int h = 0; h < 2; ++h) {
+          const int d = 8 * c + 2 * e2 + h;
+          const uint64_t kk = pack2(kv2[h], kv2[h]);
+          uint64_t qv[NP];
+          if constexpr (NP == 1) {
+            qv[0] = qs[d];
+          } else {
+#pragma unroll
+            for (int i = 0; i < NP; i += 2) {
+              const uint4 v = *reinterpret_cast<const uint4*>(qs + d * NP + i);
+              qv[i] = ((uint64_t)v.y << 32) | v.x;
+              qv[i + 1] = ((uint64_t)v.w << 32) | v.z;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < NP; ++j) acc[j] = mul_add2(acc[j], qv[j], kk, k2);
+        }
       }
     }
     const int t = t0 + tid;
@@ -364,7 +382,8 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
                                                      const __grid_constant__ CUtensorMap vmap,
                                                      const KvSeqState* __restrict__ st, int n_seq, int n_head,
                                                      int n_kv, int cap, const float* __restrict__ sbuf,
-                                                     float* __restrict__ out, int* status, int n_stages, float one,
+                                                     float* __restrict__ out, int* status, int n_stages, int wa,
+                                                     float one,
                                                      float neg_zero) {
   constexpr int DS = 64 / G;            // dims of the slice: G heads x DS/2 pairs = 32 chain lanes
   constexpr int CH = kPvCh;
@@ -378,7 +397,7 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
   uint64_t* part = empty + kPvStagesMax;                // [kSumParts] window parts of the sum
   float* inv_l = reinterpret_cast<float*>(part + kSumParts);   // [G]
   constexpr size_t SB = pv_stage_bytes<G>(DS);
-  const int WA = (int)(NS * SB / (GP * 4)) & ~3;        // positions per window of the sum
+  const int WA = wa;                                    // positions per window of the sum (a multiple of 4)
   uint8_t* stages = smem + 256;
   const int slice = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -636,16 +655,22 @@ int launch_hd_g(const float* q, int n_tok, int n_head, int n_kv, const int32_t* 
   if (rc) return rc;
   CUtensorMap vmap;
   if ((rc = make_v_map(vc, (int64_t)n_seq * n_kv * cap, HD, DS, &vmap))) return rc;
-  // Stages: as many as fit when the grid's CTAs are spread evenly over the
-  // SMs (more stages keep more V in flight and make the sum's windows longer).
+  // Shared memory per CTA: what the grid leaves when its CTAs are spread
+  // evenly over the SMs.  It holds up to kPvStagesMax stages of the P.V
+  // phase, and in the sum phase a window of E rows: the whole context where
+  // it fits (one copy round instead of several).
   const int64_t ctas = (int64_t)(HD / DS) * n_kv * n_tok;
   const int per_sm = (int)std::min<int64_t>(4, std::max<int64_t>(1, (ctas + sm_count() - 1) / sm_count()));
+  const size_t budget = (size_t)227 * 1024 / per_sm - 1024 - 256;
   const size_t sb = pv_stage_bytes<G>(DS);
-  const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvStagesMax, ((size_t)227 * 1024 / per_sm - 1024 - 256) / sb));
-  const size_t smv = 256 + (size_t)ns * sb;
+  const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvStagesMax, budget / sb));
+  const size_t e_all = (size_t)cap_s(cap) * gp_of(G) * 4;
+  const size_t area = std::max((size_t)ns * sb, std::min(budget, e_all) / 128 * 128);
+  const int wa = (int)(area / (gp_of(G) * 4)) & ~3;
+  const size_t smv = 256 + area;
   B2_CUDA_TRY(cudaFuncSetAttribute(attn_pv_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smv));
   return launch_pdl(attn_pv_kernel<HD, G>, dim3(HD / DS, n_kv, n_tok), dim3(64), smv, s, pos, seq, vmap, st, n_seq,
-                    n_head, n_kv, cap, (const float*)scratch, out, status, ns, 1.0f, -0.0f);
+                    n_head, n_kv, cap, (const float*)scratch, out, status, ns, wa, 1.0f, -0.0f);
 }
 
 }  // namespace
