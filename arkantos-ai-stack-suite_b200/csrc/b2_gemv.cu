@@ -365,26 +365,53 @@ __device__ __forceinline__ void dp4a_terms(const GemvP& p, const uint8_t* sl, co
 // tile A (i = 0, 1) or of tile B (i = 2, 3) and token 2q (i even) or 2q+1.
 // The B fragment is token g's codes.  Tokens at or past n_tok read the last
 // token's data instead: a column of the mma only feeds the outputs of its own
-// token, and those outputs are never stored.
-template <int WT>
-__device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa, const uint8_t* sb,
-                                               const uint8_t* act, int u, int g, int q, float (&a)[4],
-                                               float (&b)[4]) {
+// token, and those outputs are never stored.  Everything that depends only
+// on the lane is worked out once per warp (PairLane), so a unit costs its
+// reads, the integer work and the reference's float updates.
+struct PairLane {
+  const uint8_t* x;      // token g's codes + 4q (the B fragment's column and k offset)
+  const float* dx0;      // unit scales of tokens 2q and 2q+1
+  const float* dx1;
+  const int16_t* bs0;    // block sums of tokens 2q and 2q+1
+  const int16_t* bs1;
+  int rot[8];            // 16·((c + g) mod 8) + 4q: the lane's word of 16-byte chunk c of row g (Q4_K qs, Q6_K ql)
+  int roth[4];           // 16·((c + g) mod 4) + 4q (Q6_K qh)
+  int g, q4;             // row g, 4q
+};
+__device__ __forceinline__ PairLane pair_lane(const GemvP& p, const uint8_t* act, int g, int q) {
+  PairLane L;
   const int last = p.n_tok - 1;
   const int tg = min(g, last), t0 = min(2 * q, last), t1 = min(2 * q + 1, last);
-  const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
-  const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
-  const float dx0 = dxs[t0 * p.nu + u], dx1 = dxs[t1 * p.nu + u];
-  const uint8_t* xr = act + tg * p.kq;
+  const int nb = p.type == B2_Q4_0 ? 1 : p.type == B2_Q4_K ? 8 : p.type == B2_Q6_K ? 16 : 0;
+  L.x = act + tg * p.kq + 4 * q;
+  L.dx0 = reinterpret_cast<const float*>(act + p.off_dx) + t0 * p.nu;
+  L.dx1 = reinterpret_cast<const float*>(act + p.off_dx) + t1 * p.nu;
+  L.bs0 = reinterpret_cast<const int16_t*>(act + p.off_bs) + t0 * p.nu * nb;
+  L.bs1 = reinterpret_cast<const int16_t*>(act + p.off_bs) + t1 * p.nu * nb;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) L.rot[c] = 16 * ((c + g) & 7) + 4 * q;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) L.roth[c] = 16 * ((c + g) & 3) + 4 * q;
+  L.g = g;
+  L.q4 = 4 * q;
+  return L;
+}
+
+template <int WT>
+__device__ __forceinline__ void mma_pair_terms(const PairLane& L, const uint8_t* sa, const uint8_t* sb, int u,
+                                               float (&a)[4], float (&b)[4]) {
+  const int g = L.g;
+  const float dx0 = L.dx0[u], dx1 = L.dx1[u];
   if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
-    const uint8_t* xb = xr + u * 32;
-    const uint32_t b0 = lds32(xb + 4 * q), b1 = lds32(xb + 16 + 4 * q);
+    const uint8_t* xb = L.x + u * 32;
+    const uint32_t b0 = lds32(xb), b1 = lds32(xb + 16);
+    const int q4 = L.q4;
     int c[4];
     float dA, dB;
     if constexpr (WT == B2_Q4_0) {
-      const uint32_t wa = lds32(sa + 16 * g + 4 * q), wb = lds32(sb + 16 * g + 4 * q);
+      const uint32_t wa = lds32(sa + 16 * g + q4), wb = lds32(sb + 16 * g + q4);
       mma_k32_u8s8_rows(c, wa & kM4, wb & kM4, (wa >> 4) & kM4, (wb >> 4) & kM4, b0, b1);
-      const int k0 = 8 * (int)bss[t0 * p.nu + u], k1 = 8 * (int)bss[t1 * p.nu + u];
+      const int k0 = 8 * (int)L.bs0[u], k1 = 8 * (int)L.bs1[u];
       c[0] -= k0;
       c[1] -= k1;
       c[2] -= k0;
@@ -392,8 +419,8 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
       dA = h2f(*reinterpret_cast<const uint16_t*>(sa + 128 + 2 * g));
       dB = h2f(*reinterpret_cast<const uint16_t*>(sb + 128 + 2 * g));
     } else {
-      mma_k32_s8s8_rows(c, lds32(sa + 16 * g + 4 * q), lds32(sb + 16 * g + 4 * q), lds32(sa + 128 + 16 * g + 4 * q),
-                        lds32(sb + 128 + 16 * g + 4 * q), b0, b1);
+      mma_k32_s8s8_rows(c, lds32(sa + 16 * g + q4), lds32(sb + 16 * g + q4), lds32(sa + 128 + 16 * g + q4),
+                        lds32(sb + 128 + 16 * g + q4), b0, b1);
       dA = h2f(*reinterpret_cast<const uint16_t*>(sa + 256 + 2 * g));
       dB = h2f(*reinterpret_cast<const uint16_t*>(sb + 256 + 2 * g));
     }
@@ -409,16 +436,16 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
     q4k_scales(mb.y, mb.z, mb.w, slB, mlB, shB, mhB);
     const uint8_t* qa = sa + 128 * g;
     const uint8_t* qb = sb + 128 * g;
-    const uint8_t* xu = xr + u * 256;
+    const uint8_t* xu = L.x + u * 256;
     int is[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int jc = 0; jc < 4; ++jc) {
-      const int c0 = 16 * ((2 * jc + g) & 7) + 4 * q, c1 = 16 * ((2 * jc + 1 + g) & 7) + 4 * q;
+      const int c0 = L.rot[2 * jc], c1 = L.rot[2 * jc + 1];
       const uint32_t w0a = lds32(qa + c0), w1a = lds32(qa + c1), w0b = lds32(qb + c0), w1b = lds32(qb + c1);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int j = 2 * jc + h;   // 32-weight group
-        const uint32_t b0 = lds32(xu + 32 * j + 4 * q), b1 = lds32(xu + 32 * j + 16 + 4 * q);
+        const uint32_t b0 = lds32(xu + 32 * j), b1 = lds32(xu + 32 * j + 16);
         const int sh = 4 * h;
         int c[4];
         mma_k32_u8s8_rows(c, (w0a >> sh) & kM4, (w0b >> sh) & kM4, (w1a >> sh) & kM4, (w1b >> sh) & kM4, b0, b1);
@@ -430,8 +457,8 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
         is[3] += sB * c[3];
       }
     }
-    const uint4 bq0 = lds128(reinterpret_cast<const uint8_t*>(bss + (t0 * p.nu + u) * 8));
-    const uint4 bq1 = lds128(reinterpret_cast<const uint8_t*>(bss + (t1 * p.nu + u) * 8));
+    const uint4 bq0 = lds128(reinterpret_cast<const uint8_t*>(L.bs0 + u * 8));
+    const uint4 bq1 = lds128(reinterpret_cast<const uint8_t*>(L.bs1 + u * 8));
     const int ms[4] = {q4k_msum(bq0, mlA, mhA), q4k_msum(bq1, mlA, mhA), q4k_msum(bq0, mlB, mhB),
                        q4k_msum(bq1, mlB, mhB)};
     const float ddA = h2f((uint16_t)(ma.x & 0xFFFFu)), dmA = h2f((uint16_t)(ma.x >> 16));
@@ -449,19 +476,19 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
     const uint8_t* qhb = sb + 1024 + 64 * g;
     const uint4 sca = lds128(sa + 1536 + 16 * g), scb = lds128(sb + 1536 + 16 * g);
     const uint32_t swa[4] = {sca.x, sca.y, sca.z, sca.w}, swb[4] = {scb.x, scb.y, scb.z, scb.w};
-    const int16_t* bs0 = bss + (t0 * p.nu + u) * 16;
-    const int16_t* bs1 = bss + (t1 * p.nu + u) * 16;
-    const uint8_t* xu = xr + u * 256;
+    const int16_t* bs0 = L.bs0 + u * 16;
+    const int16_t* bs1 = L.bs1 + u * 16;
+    const uint8_t* xu = L.x + u * 256;
     int is[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const int ch = 16 * ((2 * hh + hf + g) & 3) + 4 * q;
+        const int ch = L.roth[2 * hh + hf];
         const uint32_t hwa = lds32(qha + ch), hwb = lds32(qhb + ch);
 #pragma unroll
         for (int a1 = 0; a1 < 2; ++a1) {
-          const int cl = 16 * ((4 * hh + 2 * a1 + hf + g) & 7) + 4 * q;
+          const int cl = L.rot[4 * hh + 2 * a1 + hf];
           const uint32_t lwa = lds32(qla + cl), lwb = lds32(qlb + cl);
 #pragma unroll
           for (int nh = 0; nh < 2; ++nh) {
@@ -469,7 +496,7 @@ __device__ __forceinline__ void mma_pair_terms(const GemvP& p, const uint8_t* sa
             const int i = hh * 8 + aq * 2 + hf;  // 16-weight group of the super-block
             const uint32_t va = ((lwa >> (4 * nh)) & kM4) | (((hwa >> (2 * aq)) & 0x03030303u) << 4);
             const uint32_t vb = ((lwb >> (4 * nh)) & kM4) | (((hwb >> (2 * aq)) & 0x03030303u) << 4);
-            const uint32_t b0 = lds32(xu + 16 * i + 4 * q);
+            const uint32_t b0 = lds32(xu + 16 * i);
             int c[4];
             mma_k16_u8s8_rows(c, va, vb, b0);
             const int o0 = 32 * (int)bs0[i], o1 = 32 * (int)bs1[i];
@@ -827,6 +854,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
     float* y = p.yl[mi];
     if constexpr (MODE == 3) {
       const int g = lane >> 2, q = lane & 3;   // rows g of tiles 2·item and 2·item+1, tokens 2q and 2q+1
+      const PairLane PL = pair_lane(p, act, g, q);
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int kc = 0; kc < my_chunks; ++kc) {
         if constexpr (!KS) {
@@ -835,15 +863,24 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
           const uint8_t* st = ring + (size_t)s * p.stage_bytes;
           const int u0 = kc * p.U, u1 = min(u0 + p.U, p.nu);
           if (ok) {
-            for (int u = u0; u < u1; ++u) {
-              const uint8_t* sa = st + (size_t)(u - u0) * p.slot_bytes;
-              float a[4], b[4];
-              mma_pair_terms<WT>(p, sa, sa + p.half_bytes, act, u, g, q, a, b);
+            // two units at a time: both units' terms, then the adds in order
+            for (int ub = u0; ub < u1; ub += 2) {
+              float a[2][4], b[2][4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                acc[i] = __fadd_rn(acc[i], a[i]);
-                if constexpr (WT == B2_Q4_K) acc[i] = __fsub_rn(acc[i], b[i]);
-              }
+              for (int k = 0; k < 2; ++k)
+                if (ub + k < u1) {
+                  const uint8_t* sa = st + (size_t)(ub + k - u0) * p.slot_bytes;
+                  mma_pair_terms<WT>(PL, sa, sa + p.half_bytes, ub + k, a[k], b[k]);
+                }
+#pragma unroll
+              for (int k = 0; k < 2; ++k)
+                if (ub + k < u1) {
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    acc[i] = __fadd_rn(acc[i], a[k][i]);
+                    if constexpr (WT == B2_Q4_K) acc[i] = __fsub_rn(acc[i], b[k][i]);
+                  }
+                }
             }
           }
           __syncwarp();
@@ -867,7 +904,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
             for (int i = 0; i < UM; ++i)
               if (u0 + i < u1) {
                 const uint8_t* sa = st + (size_t)i * p.slot_bytes;
-                mma_pair_terms<WT>(p, sa, sa + p.half_bytes, act, u0 + i, g, q, ta[i], tb[i]);
+                mma_pair_terms<WT>(PL, sa, sa + p.half_bytes, u0 + i, ta[i], tb[i]);
               }
           }
           release_chunk(p, item, k, cps, n_gst, used, ring, full, issued_g, ok, lane);
@@ -905,16 +942,43 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
           const uint8_t* st = ring + (size_t)s * p.stage_bytes;
           const int u0 = kc * p.U, u1 = min(u0 + p.U, p.nu);
           if (ok) {
-            for (int u4 = u0; u4 < u1; u4 += 4) {
-              const int u = u4 + j;
-              float pa[NB], pb[NB];
-              if (u < u1) {
-                dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa, pb);
-              } else {
+            // GM groups of 4 units at a time: all their terms, then all the
+            // shuffles, then the adds in unit order (a warp issues in order,
+            // so a fold right after its own terms would wait on them)
+            constexpr int GM = ks_dp4a_groups(WT, NB);
+            for (int ub = u0; ub < u1; ub += 4 * GM) {
+              float pa[GM][NB], pb[GM][NB];
 #pragma unroll
-                for (int t = 0; t < NB; ++t) pa[t] = pb[t] = 0.0f;
+              for (int kk = 0; kk < GM; ++kk) {
+                const int u = ub + 4 * kk + j;
+                if (u < u1) {
+                  dp4a_terms<WT, NB>(p, st + (size_t)(u - u0) * p.slot_bytes, act, u, g, pa[kk], pb[kk]);
+                } else {
+#pragma unroll
+                  for (int t = 0; t < NB; ++t) pa[kk][t] = pb[kk][t] = 0.0f;
+                }
               }
-              fold4<WT, NB>(acc, pa, pb, min(4, u1 - u4), g);
+              float sa[GM][4][NB], sb[GM][4][NB];
+#pragma unroll
+              for (int kk = 0; kk < GM; ++kk)
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+                  for (int t = 0; t < NB; ++t) {
+                    sa[kk][jj][t] = __shfl_sync(0xffffffffu, pa[kk][t], g + 8 * jj);
+                    if constexpr (WT == B2_Q4_K) sb[kk][jj][t] = __shfl_sync(0xffffffffu, pb[kk][t], g + 8 * jj);
+                  }
+#pragma unroll
+              for (int kk = 0; kk < GM; ++kk)
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj)
+                  if (ub + 4 * kk + jj < u1) {
+#pragma unroll
+                    for (int t = 0; t < NB; ++t) {
+                      acc[t] = __fadd_rn(acc[t], sa[kk][jj][t]);
+                      if constexpr (WT == B2_Q4_K) acc[t] = __fsub_rn(acc[t], sb[kk][jj][t]);
+                    }
+                  }
             }
           }
           __syncwarp();
