@@ -153,6 +153,9 @@ def barrier(dist):
 GEMV_N = GEMV_K = 4096
 GEMV_COPIES = 48
 GEMV_BYTES = GEMV_N * GEMV_K // 32 * 18 + GEMV_K * 4 + GEMV_N * 4   # 9 469 952
+# DRAM bytes of one Q4_K 28672x4096 batch-8 GEMV launch (the FFN gate|up at
+# TP1) as ncu measured them: dram__bytes_read.sum + dram__bytes_write.sum.
+GATE_UP_TRAFFIC = 66_165_248 + 117_760
 
 
 def gemv_inputs(b2):
@@ -570,7 +573,11 @@ def run_decode_ours(args, dist, rank, world, local):
         "config": decode_config(world),
         "roofline": {"bound": "hbm", "kernel": f"gemv Q4_K batch 8, {2 * ff_l}x{c['n_embd']} (ffn gate|up)",
                      "achieved": round(g["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(g["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
+                     "frac": round(g["gbs"] / peaks["hbm_gbs"], 4),
+                     "traffic": GATE_UP_TRAFFIC if world == 1 else None,
+                     "traffic_src": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                    "(profiles/gemv_kernel_q4k_28672x4096_b8.md); the TP shards are other shapes",
+                     "peak_src": peaks["src"],
                      "algorithmic_bytes_per_launch": g["bytes"], "ms_per_launch": g["ms"]},
         "step_roofline": {"achieved": round(step_gbs, 1), "unit": "GB/s", "frac": round(step_gbs / peaks["hbm_gbs"], 4),
                           "algorithmic_bytes_per_step": int(step_bytes),
