@@ -1265,10 +1265,9 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   const int64_t per_cta = (n_items + grid - 1) / grid;
   const int gran = pairs ? 1 : 4;   // units that one step of the fold takes
   int S = 1, nw, U = 0;
-  static const int ks_warps = getenv("B2_GEMV_KS_WARPS") ? atoi(getenv("B2_GEMV_KS_WARPS")) : kMaxWarps;   // TUNING PROBE
   if (per_cta <= kKsMaxItems) {
     const int64_t n_gran = (w.nu + gran - 1) / gran;
-    S = (int)std::min<int64_t>(ks_warps / per_cta, n_gran);
+    S = (int)std::min<int64_t>(kMaxWarps / per_cta, n_gran);
     if (S >= 2) {
       const int64_t per_warp = (n_gran + S - 1) / S;
       U = gran * (int)std::min<int64_t>(pairs ? kKsPairUnits : ks_dp4a_groups(w.type, a.n_tok), per_warp);
