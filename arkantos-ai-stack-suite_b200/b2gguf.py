@@ -93,6 +93,10 @@ def _bind() -> None:
         "b2_attn_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
         "b2_attn_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
         "b2_kv_shift_k": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
+        "b2_kv_row_bytes": (ctypes.c_int64, [_i, _i]),
+        "b2_rope_kv_store_typed": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _vp]),
+        "b2_attn_decode_typed": (_i, [_vp, _vp, _i, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
+        "b2_kv_shift_k_typed": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
         "b2_model_default_params": (None, [_vp]),
         "b2_nccl_unique_id": (_i, [_vp]),
         "b2_model_load": (_i, [ctypes.c_char_p, _vp, _vp]),
@@ -426,7 +430,7 @@ class ModelParams(ctypes.Structure):
 
 class ContextParams(ctypes.Structure):
     _fields_ = [("n_ctx", ctypes.c_int32), ("n_seq_max", ctypes.c_int32), ("use_graph", ctypes.c_int32),
-                ("prefill_gemm", ctypes.c_int32)]
+                ("prefill_gemm", ctypes.c_int32), ("type_k", ctypes.c_int32), ("type_v", ctypes.c_int32)]
 
 
 def nccl_unique_id() -> bytes:
@@ -466,9 +470,9 @@ class Model:
 
 class Context:
     def __init__(self, model: Model, n_ctx: int = 4096, n_seq: int = 1, use_graph: bool = True,
-                 prefill_gemm: bool = True):
+                 prefill_gemm: bool = True, type_k: int = F16, type_v: int = F16):
         self.model = model
-        p = ContextParams(n_ctx, n_seq, 1 if use_graph else 0, 1 if prefill_gemm else 0)
+        p = ContextParams(n_ctx, n_seq, 1 if use_graph else 0, 1 if prefill_gemm else 0, type_k, type_v)
         h = ctypes.c_void_p()
         check(lib.b2_context_create(model.h, ctypes.byref(p), ctypes.byref(h)), "context_create")
         self.h = h.value

@@ -35,6 +35,15 @@
 //     rows, turns V into fp32 and forms (p_t, p_t) = e_t·(1/l); the chain
 //     warp's lane (head, dim pair) runs out += p_t·v_t over the positions in
 //     order with packed f32x2 operations.
+// Q8_0 caches (llama.cpp's cache type that Milda asks for by default,
+// Milda/src/engine.cpp:74-87, 1195-1196): rows of hd int8 codes then the
+// hd/32 fp16 block scales (kv_row_bytes).  With a Q8_0 K the CTA quantizes
+// its G query heads to Q8_0 (ref_quantize_row_q8_0) and thread t scores its
+// position with the reference's Q8_0·Q8_0 block dot (dp4a block sums, then
+// sumf += (d_k·d_q)·sumi in block order) times 1/sqrt(hd).  With a Q8_0 V
+// the loader brings the slice's codes and the rows' scale words with two
+// 2-D tensor copies and converts code·scale (exact in fp32) into the same
+// fp32 pairs the chain reads.
 // Queries whose sequence id or position is outside the cache attend to
 // nothing and get zero outputs.  Every wait is bounded.
 #include <cuda.h>
@@ -43,6 +52,7 @@
 
 #include "b2_common.cuh"
 #include "b2_layers.hpp"
+#include "b2_quant.cuh"
 
 namespace b2 {
 namespace {
@@ -122,21 +132,34 @@ __device__ __forceinline__ SlotRun slot_run(const KvSeqState& st, int p, int end
   return r;
 }
 
-template <int HD, int G>
+// Shared memory of a scores CTA: barrier, the chunk's K rows, then q (fp16
+// K: head pairs [HD][NP] of 8 bytes; Q8_0 K: the G heads' Q8_0 codes [G][HD]
+// and scales [G][HD/32] as fp32).
+template <int HD, int G, int KT>
+__host__ __device__ constexpr size_t scores_smem_bytes() {
+  return 128 + (size_t)kScoreP * kv_row_bytes(KT, HD) +
+         (KT == B2_Q8_0 ? (size_t)G * HD + (size_t)G * (HD / 32) * 4 : (size_t)HD * ((G + 1) / 2) * 8);
+}
+
+template <int HD, int G, int KT>
 __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __restrict__ q, int n_head, int n_kv,
                                                               const int32_t* __restrict__ pos,
                                                               const int32_t* __restrict__ seq,
-                                                              const uint16_t* __restrict__ kc,
+                                                              const uint8_t* __restrict__ kc,
                                                               const KvSeqState* __restrict__ st, int n_seq, int cap,
                                                               float scale, float* __restrict__ sbuf, int* status,
                                                               float one, float neg_zero) {
   constexpr int P = kScoreP;
   constexpr int NP = (G + 1) / 2;              // head pairs (the last one half used when G is odd)
-  constexpr int KB = P * HD * 2;               // K rows of the chunk
+  constexpr int RB = (int)kv_row_bytes(KT, HD);
+  constexpr int KB = P * RB;                   // K rows of the chunk
+  constexpr int NB = HD / 32;                  // Q8_0 blocks per row
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + 128);        // [P][HD]
-  uint64_t* qs = reinterpret_cast<uint64_t*>(smem + 128 + KB);   // [HD][NP]: (q_2j[i], q_2j+1[i])
+  uint8_t* ks = smem + 128;                                      // [P][RB]
+  uint64_t* qs = reinterpret_cast<uint64_t*>(smem + 128 + KB);   // fp16 K: [HD][NP]: (q_2j[i], q_2j+1[i])
+  int8_t* qq = reinterpret_cast<int8_t*>(smem + 128 + KB);       // Q8_0 K: codes [G][HD]
+  float* qd = reinterpret_cast<float*>(smem + 128 + KB + G * HD);   // Q8_0 K: scales [G][NB]
   __shared__ float mh[P / 32][G];
   pdl_wait();
   pdl_launch_dependents();
@@ -162,18 +185,27 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
       fence_mbar_init();
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * HD * 2));
+    if (lane == 0) mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * RB));
     const int64_t base = ((int64_t)s * n_kv + kh) * cap;
     int p = t0;
     for (int r_i = 0; p < t0 + n; ++r_i) {
       const SlotRun r = slot_run(sst, p, t0 + n, cap, P);
-      if (lane == r_i) bulk_g2s(ks + (p - t0) * HD, kc + (base + r.slot) * HD, (uint32_t)(r.len * HD * 2), &bar[0]);
+      if (lane == r_i) bulk_g2s(ks + (p - t0) * RB, kc + (base + r.slot) * RB, (uint32_t)(r.len * RB), &bar[0]);
       p += r.len;
     }
   }
-  // q of the G heads, as head pairs, while the copies fly
-  {
-    const float* qg = q + ((int64_t)b * n_head + hq0) * HD;
+  // q of the G heads while the copies fly: head pairs for fp16 K; for Q8_0
+  // K each head quantized to Q8_0 (one warp per 32-value block), the dot
+  // type that pairs with a Q8_0 K row
+  const float* qg = q + ((int64_t)b * n_head + hq0) * HD;
+  if constexpr (KT == B2_Q8_0) {
+    for (int blk = warp; blk < G * NB; blk += P / 32) {
+      uint16_t d16;
+      const int8_t c = quant_q8_0_lane(qg[blk * 32 + lane], &d16);
+      qq[blk * 32 + lane] = c;
+      if (lane == 0) qd[blk] = h2f(d16);
+    }
+  } else {
     for (int i = tid; i < HD * NP; i += P) {
       const int d = i / NP, j = i - d * NP;
       const float lo = qg[(2 * j) * HD + d];
@@ -186,11 +218,47 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   float sc[2 * NP];
 #pragma unroll
   for (int j = 0; j < 2 * NP; ++j) sc[j] = -FLT_MAX;
-  if (ok && tid < n) {
+  if constexpr (KT == B2_Q8_0) {
+    if (ok && tid < n) {
+      // the Q8_0·Q8_0 block dot of ref_vec_dot_q8_0_q8_0
+      // (Singularity/tests/test_and_bench_a5.cpp:205-221): exact block sums,
+      // then sumf += (d_k·d_q)·sumi over the blocks in order
+      const uint8_t* rp = ks + tid * RB;
+      float sumf[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) sumf[g] = 0.0f;
+#pragma unroll
+      for (int bi = 0; bi < NB; ++bi) {
+        const uint4 k0 = *reinterpret_cast<const uint4*>(rp + bi * 32);
+        const uint4 k1 = *reinterpret_cast<const uint4*>(rp + bi * 32 + 16);
+        const float dk = h2f(*reinterpret_cast<const uint16_t*>(rp + HD + 2 * bi));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const uint4 q0 = *reinterpret_cast<const uint4*>(qq + g * HD + bi * 32);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(qq + g * HD + bi * 32 + 16);
+          int si = __dp4a((int)k0.x, (int)q0.x, 0);
+          si = __dp4a((int)k0.y, (int)q0.y, si);
+          si = __dp4a((int)k0.z, (int)q0.z, si);
+          si = __dp4a((int)k0.w, (int)q0.w, si);
+          si = __dp4a((int)k1.x, (int)q1.x, si);
+          si = __dp4a((int)k1.y, (int)q1.y, si);
+          si = __dp4a((int)k1.z, (int)q1.z, si);
+          si = __dp4a((int)k1.w, (int)q1.w, si);
+          sumf[g] = __fadd_rn(sumf[g], __fmul_rn(__fmul_rn(dk, qd[g * NB + bi]), (float)si));
+        }
+      }
+      const int t = t0 + tid;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sc[g] = __fmul_rn(sumf[g], scale);
+        srow[(int64_t)g * capS + t] = sc[g];
+      }
+    }
+  } else if (ok && tid < n) {
     // the row of position t0 + tid, then the chains in dim order
     constexpr int NPc = HD / 8;
     const Ones k2{pack2(one, one), pack2(neg_zero, neg_zero)};
-    const uint8_t* rp = reinterpret_cast<const uint8_t*>(ks + tid * HD);
+    const uint8_t* rp = ks + tid * RB;
     uint64_t acc[NP];
 #pragma unroll
     for (int j = 0; j < NP; ++j) acc[j] = 0ull;   // (+0, +0)
@@ -317,11 +385,21 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 // padding per row put the rows that the chain lanes read side by side on
 // different banks.
 constexpr int kPvChP = kPvCh + 2;
-template <int G>
+// Bytes of a Q8_0 V slice's codes per row: the slice's ds bytes, at least
+// 16 (a tensor copy's smallest inner box), starting at the slice's first dim
+// rounded down to 16.
+__host__ __device__ constexpr int pv_code_bytes(int ds) { return ds < 16 ? 16 : ds; }
+// Raw V rows of a stage: fp16 [CH][ds]; Q8_0 codes [CH][pv_code_bytes] then
+// the rows' scale words [CH][8] (16 bytes: the hd/32 scales and padding).
+template <int VT>
+__host__ __device__ constexpr size_t pv_rawv_bytes(int ds) {
+  return VT == B2_Q8_0 ? (size_t)kPvCh * (pv_code_bytes(ds) + 16) : (size_t)kPvCh * ds * 2;
+}
+template <int G, int VT>
 __host__ __device__ constexpr size_t pv_stage_bytes(int ds) {
-  // raw V [CH][ds] fp16 | raw E [CH][GP] | V pairs [ds/2][CHP] | (p, p) pairs [G][CHP],
+  // raw V | raw E [CH][GP] | V pairs [ds/2][CHP] | (p, p) pairs [G][CHP],
   // rounded up to 128 bytes (the tensor copy's destination alignment)
-  return ((size_t)kPvCh * ds * 2 + (size_t)kPvCh * gp_of(G) * 4 + (size_t)(ds / 2) * kPvChP * 8 +
+  return (pv_rawv_bytes<VT>(ds) + (size_t)kPvCh * gp_of(G) * 4 + (size_t)(ds / 2) * kPvChP * 8 +
           (size_t)G * kPvChP * 8 + 127) / 128 * 128;
 }
 __device__ __forceinline__ uint64_t u64_of(uint32_t lo, uint32_t hi) {
@@ -377,9 +455,10 @@ __device__ __forceinline__ float sum_run(const float* e, int a, int b, float l) 
 // a run) and E rows (one bulk copy) into a raw stage, converts V to fp32 and
 // forms (p, p) = e·(1/l) pairs; warp 0's lane (head g, dim pair j) runs out
 // += p_t·v_t over the positions in order.
-template <int HD, int G>
+template <int HD, int G, int VT>
 __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__ pos, const int32_t* __restrict__ seq,
                                                      const __grid_constant__ CUtensorMap vmap,
+                                                     const __grid_constant__ CUtensorMap smap,
                                                      const KvSeqState* __restrict__ st, int n_seq, int n_head,
                                                      int n_kv, int cap, const float* __restrict__ sbuf,
                                                      float* __restrict__ out, int* status, int n_stages, int wa,
@@ -396,7 +475,9 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
   uint64_t* empty = conv + kPvStagesMax;                // [NS] chain done with the stage
   uint64_t* part = empty + kPvStagesMax;                // [kSumParts] window parts of the sum
   float* inv_l = reinterpret_cast<float*>(part + kSumParts);   // [G]
-  constexpr size_t SB = pv_stage_bytes<G>(DS);
+  constexpr size_t SB = pv_stage_bytes<G, VT>(DS);
+  constexpr int RAWV = (int)pv_rawv_bytes<VT>(DS);
+  constexpr int DSL = pv_code_bytes(DS);
   const int WA = wa;                                    // positions per window of the sum (a multiple of 4)
   uint8_t* stages = smem + 256;
   const int slice = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -462,10 +543,13 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
       const SlotRun r = slot_run(sst, p_iss, n_pos, cap, CH);
       uint8_t* sp = stages + si * SB;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[si], (uint32_t)(CH * DS * 2 + r.len * GP * 4));
-        tma_load_2d(sp, &vmap, d0, row0 + (int)r.slot, &full[si]);
+        mbar_arrive_expect_tx(&full[si], (uint32_t)(RAWV + r.len * GP * 4));
+        tma_load_2d(sp, &vmap, VT == B2_Q8_0 ? (d0 & ~15) : d0, row0 + (int)r.slot, &full[si]);
       } else if (lane == 1) {
-        bulk_g2s(sp + CH * DS * 2, erow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
+        bulk_g2s(sp + RAWV, erow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
+      } else if (VT == B2_Q8_0 && lane == 2) {
+        // the rows' scale words: 8 fp16 from byte HD of each row
+        tma_load_2d(sp + CH * DSL, &smap, HD / 2, row0 + (int)r.slot, &full[si]);
       }
       p_iss += r.len;
       ++c_iss;
@@ -484,20 +568,38 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
       if (ok && c >= NS) ok = mbar_wait_bounded(&empty[si], (uint32_t)(((c / NS) - 1) & 1), status, 7);
       if (ok) {
         uint8_t* sp = stages + si * SB;
-        const uint4* rv = reinterpret_cast<const uint4*>(sp);                 // [CH][DS/8] raw V
-        const float4* re = reinterpret_cast<const float4*>(sp + CH * DS * 2);  // [CH][GP/4] raw E
-        uint64_t* vp = reinterpret_cast<uint64_t*>(sp + CH * DS * 2 + CH * GP * 4);   // [DS/2][CHP]
-        uint64_t* pp = vp + (DS / 2) * kPvChP;                                       // [G][CHP]
+        const float4* re = reinterpret_cast<const float4*>(sp + RAWV);  // [CH][GP/4] raw E
+        uint64_t* vp = reinterpret_cast<uint64_t*>(sp + RAWV + CH * GP * 4);   // [DS/2][CHP]
+        uint64_t* pp = vp + (DS / 2) * kPvChP;                                // [G][CHP]
         // lane t owns positions t, t + 32, ...: its V row becomes DS/2 pairs
         // and its E row G pairs (p, p) = e·(1/l)
         for (int t = lane; t < len; t += 32) {
+          if constexpr (VT == B2_Q8_0) {
+            // code · block scale, exact in fp32 (ggml's dequantize_row_q8_0)
+            const uint8_t* rc = sp + t * DSL + (d0 & 15);
+            const uint16_t* rs = reinterpret_cast<const uint16_t*>(sp + CH * DSL) + t * 8;
 #pragma unroll
-          for (int c = 0; c < DS / 8; ++c) {
-            const uint4 w = rv[t * (DS / 8) + c];
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+            for (int c = 0; c < DS / 8; ++c) {
+              const uint2 w = *reinterpret_cast<const uint2*>(rc + 8 * c);
+              const float d = h2f(rs[(d0 + 8 * c) >> 5]);
+              const uint32_t ww[2] = {w.x, w.y};
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              vp[(4 * c + k) * kPvChP + t] = pack2(h2f((uint16_t)(ww[k] & 0xFFFFu)), h2f((uint16_t)(ww[k] >> 16)));
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t h = ww[k >> 1] >> (16 * (k & 1));
+                vp[(4 * c + k) * kPvChP + t] =
+                    pack2(__fmul_rn((float)(int8_t)(h & 0xFFu), d), __fmul_rn((float)(int8_t)(h >> 8), d));
+              }
+            }
+          } else {
+            const uint4* rv = reinterpret_cast<const uint4*>(sp);   // [CH][DS/8] raw V
+#pragma unroll
+            for (int c = 0; c < DS / 8; ++c) {
+              const uint4 w = rv[t * (DS / 8) + c];
+              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                vp[(4 * c + k) * kPvChP + t] = pack2(h2f((uint16_t)(ww[k] & 0xFFFFu)), h2f((uint16_t)(ww[k] >> 16)));
+            }
           }
 #pragma unroll
           for (int c = 0; c < GP / 4; ++c) {
@@ -543,9 +645,8 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
     if (ok) ok = mbar_wait_bounded(&conv[si], (uint32_t)((c / NS) & 1), status, 8);
     if (ok) {
       const uint8_t* sp = stages + si * SB;
-      const uint64_t* vr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4) + j * kPvChP;
-      const uint64_t* pr = reinterpret_cast<const uint64_t*>(sp + CH * DS * 2 + CH * GP * 4) +
-                           (DS / 2) * kPvChP + g * kPvChP;
+      const uint64_t* vr = reinterpret_cast<const uint64_t*>(sp + RAWV + CH * GP * 4) + j * kPvChP;
+      const uint64_t* pr = reinterpret_cast<const uint64_t*>(sp + RAWV + CH * GP * 4) + (DS / 2) * kPvChP + g * kPvChP;
       // positions in groups of 8, two per 16-byte load, in two buffers that
       // take turns: the next group's (p, v) are read while the current
       // group's chain runs, with no register copies between the steps
@@ -611,9 +712,11 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
   op[1] = o1;
 }
 
-// The V cache as a 2-D tensor [n_seq*n_kv*cap rows][hd] of fp16, boxes of
-// kPvCh rows x ds dims.
-int make_v_map(const uint16_t* vc, int64_t n_rows, int hd, int ds, CUtensorMap* map) {
+// The V cache as 2-D tensors over its rows ([n_seq*n_kv*cap rows]), boxes of
+// kPvCh rows: fp16 rows of hd values, ds-dim boxes; Q8_0 rows as bytes
+// (boxes of pv_code_bytes(ds) codes) and as 16-bit words (boxes of the 8
+// scale words from byte hd).  For fp16 `smap` is a copy of `vmap`.
+int make_v_maps(const void* vc, int vt, int64_t n_rows, int hd, int ds, CUtensorMap* vmap, CUtensorMap* smap) {
   static PFN_cuTensorMapEncodeTiled encode = nullptr;
   if (!encode) {
     void* fn = nullptr;
@@ -624,37 +727,48 @@ int make_v_map(const uint16_t* vc, int64_t n_rows, int hd, int ds, CUtensorMap* 
     }
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
   }
-  const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)n_rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)ds, (cuuint32_t)kPvCh};
+  const cuuint64_t rb = (cuuint64_t)kv_row_bytes(vt, hd);
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(vc), dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("attention: V tensor map rejected (CUresult %d)", (int)r);
-    return B2_ERR_CUDA;
+  auto enc = [&](CUtensorMap* map, CUtensorMapDataType dt, cuuint64_t inner, cuuint32_t box_inner) -> int {
+    const cuuint64_t dims[2] = {inner, (cuuint64_t)n_rows};
+    const cuuint64_t strides[1] = {rb};
+    const cuuint32_t box[2] = {box_inner, (cuuint32_t)kPvCh};
+    const CUresult r = encode(map, dt, 2, const_cast<void*>(vc), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("attention: V tensor map rejected (CUresult %d)", (int)r);
+      return B2_ERR_CUDA;
+    }
+    return B2_OK;
+  };
+  int rc;
+  if (vt == B2_Q8_0) {
+    if ((rc = enc(vmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, (cuuint32_t)pv_code_bytes(ds)))) return rc;
+    return enc(smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, rb / 2, 8);
   }
+  if ((rc = enc(vmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, (cuuint64_t)hd, (cuuint32_t)ds))) return rc;
+  *smap = *vmap;
   return B2_OK;
 }
 
-template <int HD, int G>
+template <int HD, int G, int KT, int VT>
 int launch_hd_g(const float* q, int n_tok, int n_head, int n_kv, const int32_t* pos, const int32_t* seq,
-                const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scratch,
-                float* out, cudaStream_t s, int* status) {
-  constexpr int NP = (G + 1) / 2;
+                const void* kc, const void* vc, const KvSeqState* st, int n_seq, int cap, float* scratch, float* out,
+                cudaStream_t s, int* status) {
   constexpr int DS = 64 / G;
-  const size_t sm = 128 + (size_t)kScoreP * HD * 2 + (size_t)HD * NP * 8;
-  B2_CUDA_TRY(cudaFuncSetAttribute(attn_scores_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  const size_t sm = scores_smem_bytes<HD, G, KT>();
+  B2_CUDA_TRY(
+      cudaFuncSetAttribute(attn_scores_kernel<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   const float scale = 1.0f / sqrtf((float)HD);
   const dim3 chunks((cap + kScoreP - 1) / kScoreP, n_kv, n_tok);
-  int rc = launch_pdl(attn_scores_kernel<HD, G>, chunks, dim3(kScoreP), sm, s, q, n_head, n_kv, pos, seq, kc, st, n_seq,
-                      cap, scale, scratch, status, 1.0f, -0.0f);
+  int rc = launch_pdl(attn_scores_kernel<HD, G, KT>, chunks, dim3(kScoreP), sm, s, q, n_head, n_kv, pos, seq,
+                      static_cast<const uint8_t*>(kc), st, n_seq, cap, scale, scratch, status, 1.0f, -0.0f);
   if (rc) return rc;
   rc = launch_pdl(attn_exp_kernel<G>, chunks, dim3(kScoreP), 0, s, pos, seq, n_seq, n_kv, cap, scratch);
   if (rc) return rc;
-  CUtensorMap vmap;
-  if ((rc = make_v_map(vc, (int64_t)n_seq * n_kv * cap, HD, DS, &vmap))) return rc;
+  CUtensorMap vmap, smap;
+  if ((rc = make_v_maps(vc, VT, (int64_t)n_seq * n_kv * cap, HD, DS, &vmap, &smap))) return rc;
   // Shared memory per CTA: what the grid leaves when its CTAs are spread
   // evenly over the SMs.  It holds up to kPvStagesMax stages of the P.V
   // phase, and in the sum phase a window of E rows: the whole context where
@@ -662,15 +776,32 @@ int launch_hd_g(const float* q, int n_tok, int n_head, int n_kv, const int32_t* 
   const int64_t ctas = (int64_t)(HD / DS) * n_kv * n_tok;
   const int per_sm = (int)std::min<int64_t>(4, std::max<int64_t>(1, (ctas + sm_count() - 1) / sm_count()));
   const size_t budget = (size_t)227 * 1024 / per_sm - 1024 - 256;
-  const size_t sb = pv_stage_bytes<G>(DS);
+  const size_t sb = pv_stage_bytes<G, VT>(DS);
   const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvStagesMax, budget / sb));
   const size_t e_all = (size_t)cap_s(cap) * gp_of(G) * 4;
   const size_t area = std::max((size_t)ns * sb, std::min(budget, e_all) / 128 * 128);
   const int wa = (int)(area / (gp_of(G) * 4)) & ~3;
   const size_t smv = 256 + area;
-  B2_CUDA_TRY(cudaFuncSetAttribute(attn_pv_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smv));
-  return launch_pdl(attn_pv_kernel<HD, G>, dim3(HD / DS, n_kv, n_tok), dim3(64), smv, s, pos, seq, vmap, st, n_seq,
-                    n_head, n_kv, cap, (const float*)scratch, out, status, ns, wa, 1.0f, -0.0f);
+  B2_CUDA_TRY(cudaFuncSetAttribute(attn_pv_kernel<HD, G, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smv));
+  return launch_pdl(attn_pv_kernel<HD, G, VT>, dim3(HD / DS, n_kv, n_tok), dim3(64), smv, s, pos, seq, vmap, smap, st,
+                    n_seq, n_head, n_kv, cap, (const float*)scratch, out, status, ns, wa, 1.0f, -0.0f);
+}
+
+template <int HD, int G>
+int launch_types(const float* q, int n_tok, int n_head, int n_kv, const int32_t* pos, const int32_t* seq,
+                 const void* kc, int kt, const void* vc, int vt, const KvSeqState* st, int n_seq, int cap,
+                 float* scratch, float* out, cudaStream_t s, int* status) {
+#define B2_ATTN_TYPES(KT, VT)                                                                                    \
+  if (kt == KT && vt == VT)                                                                                      \
+    return launch_hd_g<HD, G, KT, VT>(q, n_tok, n_head, n_kv, pos, seq, kc, vc, st, n_seq, cap, scratch, out, s, \
+                                      status);
+  B2_ATTN_TYPES(B2_F16, B2_F16)
+  B2_ATTN_TYPES(B2_F16, B2_Q8_0)
+  B2_ATTN_TYPES(B2_Q8_0, B2_F16)
+  B2_ATTN_TYPES(B2_Q8_0, B2_Q8_0)
+#undef B2_ATTN_TYPES
+  set_error("attention: KV cache types %d / %d (F16 or Q8_0)", kt, vt);
+  return B2_ERR_INVALID;
 }
 
 }  // namespace
@@ -681,14 +812,15 @@ size_t attn_scratch_floats(int n_tok, int n_head, int n_kv, int cap) {
 }
 
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scratch,
-                     float* out, cudaStream_t s, int* status) {
+                     const void* kc, int kt, const void* vc, int vt, const KvSeqState* st, int n_seq, int cap,
+                     float* scratch, float* out, cudaStream_t s, int* status) {
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0 && scratch && out && cap > 0, "attention arguments");
   B2_CHECK_ARG((reinterpret_cast<uintptr_t>(scratch) & 15) == 0, "attention scratch must be 16-byte aligned");
   const int G = n_head / n_kv;
 #define B2_ATTN_CASE(HDV, GV) \
   if (hd == HDV && G == GV)   \
-    return launch_hd_g<HDV, GV>(q, n_tok, n_head, n_kv, pos, seq, kc, vc, st, n_seq, cap, scratch, out, s, status);
+    return launch_types<HDV, GV>(q, n_tok, n_head, n_kv, pos, seq, kc, kt, vc, vt, st, n_seq, cap, scratch, out, s, \
+                                 status);
   B2_ATTN_CASE(128, 1)
   B2_ATTN_CASE(128, 2)
   B2_ATTN_CASE(128, 4)

@@ -436,40 +436,65 @@ int b2_rmsnorm(float* x, const float* delta, const float* w, float* out, int n_r
   return launch_add_rmsnorm(x, delta, w, out, n_rows, n, eps, as_stream(stream));
 }
 
+int64_t b2_kv_row_bytes(int type, int head_dim) {
+  return kv_type_ok(type) && head_dim > 0 ? kv_row_bytes(type, head_dim) : 0;
+}
+
+int b2_rope_kv_store_typed(const float* qkv, int n_tok, int n_seq, int n_head, int n_kv, int head_dim,
+                           const int32_t* pos, const int32_t* seq, const float* rope, float* q_out, void* k_cache,
+                           int type_k, void* v_cache, int type_v, int cap, void* stream) {
+  B2_CHECK_ARG(qkv && pos && seq && rope && q_out && k_cache && v_cache && n_tok > 0 && n_seq > 0 && cap > 0,
+               "rope_kv_store arguments");
+  B2_CHECK_ARG(head_dim % 32 == 0 && n_head > 0 && n_kv > 0, "head shape (head_dim a multiple of 32)");
+  return launch_rope_kv(qkv, n_tok, n_head, n_kv, head_dim, pos, seq, rope, q_out, k_cache, type_k, v_cache, type_v,
+                        nullptr, n_seq, cap, as_stream(stream));
+}
+
 int b2_rope_kv_store(const float* qkv, int n_tok, int n_seq, int n_head, int n_kv, int head_dim, const int32_t* pos,
                      const int32_t* seq, const float* rope, float* q_out, uint16_t* k_cache, uint16_t* v_cache, int cap,
                      void* stream) {
-  B2_CHECK_ARG(qkv && pos && seq && rope && q_out && k_cache && v_cache && n_tok > 0 && n_seq > 0 && cap > 0,
-               "rope_kv_store arguments");
-  B2_CHECK_ARG(head_dim % 2 == 0 && n_head > 0 && n_kv > 0, "head shape");
-  return launch_rope_kv(qkv, n_tok, n_head, n_kv, head_dim, pos, seq, rope, q_out, k_cache, v_cache, nullptr, n_seq, cap,
-                        as_stream(stream));
+  return b2_rope_kv_store_typed(qkv, n_tok, n_seq, n_head, n_kv, head_dim, pos, seq, rope, q_out, k_cache, B2_F16,
+                                v_cache, B2_F16, cap, stream);
+}
+
+int b2_attn_decode_typed(const float* q, const void* k_cache, int type_k, const void* v_cache, int type_v,
+                         const int32_t* pos, const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv,
+                         int head_dim, int cap, float* out, void* stream) {
+  B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && n_q > 0 && n_seq > 0 && cap > 0,
+               "attn_decode arguments");
+  B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
+  B2_CHECK_ARG(kv_type_ok(type_k) && kv_type_ok(type_v), "KV cache types must be B2_F16 or B2_Q8_0");
+  cudaStream_t s = as_stream(stream);
+  // scores, exponentials and chunk maxima (no initialisation needed)
+  void* scratch = nullptr;
+  B2_CUDA_TRY(cudaMallocAsync(&scratch, attn_scratch_floats(n_q, n_head, n_kv, cap) * 4, s));
+  const int rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, type_k, v_cache, type_v, nullptr,
+                                  n_seq, cap, static_cast<float*>(scratch), out, s);
+  cudaFreeAsync(scratch, s);
+  return rc;
 }
 
 int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
                    const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv, int head_dim, int cap, float* out,
                    void* stream) {
-  B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && n_q > 0 && n_seq > 0 && cap > 0,
-               "attn_decode arguments");
-  B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
-  cudaStream_t s = as_stream(stream);
-  // scores, exponentials and chunk maxima (no initialisation needed)
-  void* scratch = nullptr;
-  B2_CUDA_TRY(cudaMallocAsync(&scratch, attn_scratch_floats(n_q, n_head, n_kv, cap) * 4, s));
-  const int rc = launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap,
-                                  static_cast<float*>(scratch), out, s);
-  cudaFreeAsync(scratch, s);
-  return rc;
+  return b2_attn_decode_typed(q, k_cache, B2_F16, v_cache, B2_F16, pos, seq, n_q, n_seq, n_head, n_kv, head_dim, cap,
+                              out, stream);
+}
+
+int b2_kv_shift_k_typed(void* k_cache, int type_k, int seq, int n_kv, int head_dim, int cap, int p_begin, int p_end,
+                        int delta, float theta, void* stream) {
+  B2_CHECK_ARG(k_cache && seq >= 0 && p_begin >= 0 && p_end <= cap && head_dim % 32 == 0 && head_dim <= 2 * kRotPairs,
+               "kv_shift_k arguments");
+  B2_CHECK_ARG(kv_type_ok(type_k), "KV cache type must be B2_F16 or B2_Q8_0");
+  RotTable cs;
+  rope_table(theta, head_dim, delta, 1, cs.cs);
+  const KvSeqState st{0, 0};
+  return launch_kv_shift(k_cache, type_k, n_kv, head_dim, seq, st, cap, p_begin, p_end, cs, as_stream(stream));
 }
 
 int b2_kv_shift_k(uint16_t* k_cache, int seq, int n_kv, int head_dim, int cap, int p_begin, int p_end, int delta,
                   float theta, void* stream) {
-  B2_CHECK_ARG(k_cache && seq >= 0 && p_begin >= 0 && p_end <= cap && head_dim % 2 == 0 && head_dim <= 2 * kRotPairs,
-               "kv_shift_k arguments");
-  RotTable cs;
-  rope_table(theta, head_dim, delta, 1, cs.cs);
-  const KvSeqState st{0, 0};
-  return launch_kv_shift(k_cache, n_kv, head_dim, seq, st, cap, p_begin, p_end, cs, as_stream(stream));
+  return b2_kv_shift_k_typed(k_cache, B2_F16, seq, n_kv, head_dim, cap, p_begin, p_end, delta, theta, stream);
 }
 
 int b2_flag_wait(const uint64_t* flags, int n, uint64_t target, int* status, void* stream) {

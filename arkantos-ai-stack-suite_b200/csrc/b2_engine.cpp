@@ -103,8 +103,10 @@ struct b2_context {
   b2_model* model = nullptr;
   int n_ctx = 0, n_seq = 0;
   cudaStream_t stream = nullptr;
-  // KV ring per layer: [n_seq][nkv_l][n_ctx][head_dim] fp16
-  std::vector<uint16_t*> kc, vc;
+  // KV ring per layer: [n_seq][nkv_l][n_ctx] rows of the cache types
+  // (kv_row_bytes: fp16, or Q8_0 codes + block scales)
+  std::vector<uint8_t*> kc, vc;
+  int type_k = B2_F16, type_v = B2_F16;
   b2::KvSeqState* st_d = nullptr;
   std::vector<b2::KvSeqState> st;
   std::vector<int> n_past;
@@ -478,14 +480,17 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   c->prefill_gemm = p->prefill_gemm != 0;
   B2_CUDA_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   const int hd = m->head_dim, d = m->n_embd;
-  const size_t kv = (size_t)c->n_seq * m->nkv_l * c->n_ctx * hd;
+  c->type_k = p->type_k;
+  c->type_v = p->type_v;
+  const size_t rows = (size_t)c->n_seq * m->nkv_l * c->n_ctx;
+  const size_t kb = rows * kv_row_bytes(c->type_k, hd), vb = rows * kv_row_bytes(c->type_v, hd);
   c->kc.resize(m->n_layer);
   c->vc.resize(m->n_layer);
   int rc;
   for (int l = 0; l < m->n_layer; ++l) {
-    if ((rc = dalloc(c, &c->kc[l], kv)) || (rc = dalloc(c, &c->vc[l], kv))) return rc;
-    B2_CUDA_TRY(cudaMemset(c->kc[l], 0, kv * 2));
-    B2_CUDA_TRY(cudaMemset(c->vc[l], 0, kv * 2));
+    if ((rc = dalloc(c, &c->kc[l], kb)) || (rc = dalloc(c, &c->vc[l], vb))) return rc;
+    B2_CUDA_TRY(cudaMemset(c->kc[l], 0, kb));
+    B2_CUDA_TRY(cudaMemset(c->vc[l], 0, vb));
   }
   c->st.assign(c->n_seq, KvSeqState{0, 0});
   c->n_past.assign(c->n_seq, 0);
@@ -602,16 +607,25 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     return launch_gemv(a, s);
   };
   const int qkv_w = (m->nh_l + 2 * m->nkv_l) * hd;
+  // The QKV GEMV's RoPE epilogue stores fp16 K/V; a Q8_0 cache is written by
+  // the RoPE + store kernel, which quantizes each 32-value block.
+  const bool f16_kv = c->type_k == B2_F16 && c->type_v == B2_F16;
   for (int l = 0; l < m->n_layer; ++l) {
     Layer& L = *m->layers[l];
-    if (fuse) {
+    if (fuse && !f16_kv) {
+      if ((rc = norm_gemv(l ? c->delta : nullptr, L.attn_norm, tp && l ? &in_down : nullptr, L.wqkv, c->qkv, qkv_w,
+                          EPI_STORE, nullptr)) ||
+          (rc = launch_rope_kv(c->qkv, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->rope, c->q, c->kc[l],
+                               c->type_k, c->vc[l], c->type_v, c->st_d, c->n_seq, c->n_ctx, s)))
+        return rc;
+    } else if (fuse) {
       RopeKvEpi rk;
       rk.pos = c->pos_d;
       rk.seq = c->seq_d;
       rk.rope = c->rope;
       rk.q_out = c->q;
-      rk.kc = c->kc[l];
-      rk.vc = c->vc[l];
+      rk.kc = reinterpret_cast<uint16_t*>(c->kc[l]);
+      rk.vc = reinterpret_cast<uint16_t*>(c->vc[l]);
       rk.st = c->st_d;
       rk.n_head = m->nh_l;
       rk.n_kv = m->nkv_l;
@@ -629,12 +643,12 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
       if ((rc = gemv(L.wqkv, c->xn, d, c->qkv, qkv_w, EPI_STORE))) return rc;
       if ((rc = tap("qkv", l, c->qkv, (int64_t)n * qkv_w))) return rc;
       if ((rc = launch_rope_kv(c->qkv, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->rope, c->q, c->kc[l],
-                               c->vc[l], c->st_d, c->n_seq, c->n_ctx, s)))
+                               c->type_k, c->vc[l], c->type_v, c->st_d, c->n_seq, c->n_ctx, s)))
         return rc;
       if ((rc = tap("q_rope", l, c->q, (int64_t)n * m->nh_l * hd))) return rc;
     }
-    if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->vc[l], c->st_d,
-                               c->n_seq, c->n_ctx, c->scores, c->att, s, c->status)))
+    if ((rc = launch_attention(c->q, n, m->nh_l, m->nkv_l, hd, c->pos_d, c->seq_d, c->kc[l], c->type_k, c->vc[l],
+                               c->type_v, c->st_d, c->n_seq, c->n_ctx, c->scores, c->att, s, c->status)))
       return rc;
     if ((rc = tap("attn_out", l, c->att, (int64_t)n * m->nh_l * hd))) return rc;
     {
@@ -806,10 +820,10 @@ int enqueue_prefill_chunk(b2_context* c, int nt) {
     if ((rc = launch_add_rmsnorm(c->pf_x, l ? c->pf_delta : nullptr, L.attn_norm, c->pf_xn, nt, d, m->eps, s,
                                  nullptr, c->status)) ||
         (rc = launch_gemm(L.wqkv.m, c->pf_xn, d, nt, c->pf_qkv, c->pf_ws, c->status, s)) ||
-        (rc = launch_rope_kv(c->pf_qkv, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->rope, c->pf_q, c->kc[l], c->vc[l],
-                             c->st_d, c->n_seq, c->n_ctx, s)) ||
-        (rc = launch_attention(c->pf_q, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->kc[l], c->vc[l], c->st_d, c->n_seq,
-                               c->n_ctx, c->pf_scores, c->pf_att, s, c->status)) ||
+        (rc = launch_rope_kv(c->pf_qkv, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->rope, c->pf_q, c->kc[l], c->type_k,
+                             c->vc[l], c->type_v, c->st_d, c->n_seq, c->n_ctx, s)) ||
+        (rc = launch_attention(c->pf_q, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->kc[l], c->type_k, c->vc[l],
+                               c->type_v, c->st_d, c->n_seq, c->n_ctx, c->pf_scores, c->pf_att, s, c->status)) ||
         (rc = launch_gemm(L.wo.m, c->pf_att, nq, nt, c->pf_delta, c->pf_ws, c->status, s)) ||
         (rc = launch_add_rmsnorm(c->pf_x, c->pf_delta, L.ffn_norm, c->pf_xn, nt, d, m->eps, s, nullptr,
                                  c->status)) ||
@@ -990,13 +1004,13 @@ int kv_shift(b2_context* c, int s, int p0, int p1) {
   int rc = B2_OK;
   if (p0 == st.n_keep) {
     for (int l = 0; l < m->n_layer && !rc; ++l)
-      rc = launch_kv_shift(c->kc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p1, n_past, cs, c->stream);
+      rc = launch_kv_shift(c->kc[l], c->type_k, m->nkv_l, m->head_dim, s, st, c->n_ctx, p1, n_past, cs, c->stream);
     const int ring = c->n_ctx - st.n_keep;
     st.ring_head = ring > 0 ? (st.ring_head + nd) % ring : 0;
   } else {
     for (int l = 0; l < m->n_layer && !rc; ++l)
-      rc = launch_kv_compact(c->kc[l], c->vc[l], m->nkv_l, m->head_dim, s, st, c->n_ctx, p0, p1, n_past - p1, cs,
-                             c->stream);
+      rc = launch_kv_compact(c->kc[l], c->type_k, c->vc[l], c->type_v, m->nkv_l, m->head_dim, s, st, c->n_ctx, p0,
+                             p1, n_past - p1, cs, c->stream);
   }
   if (rc) return rc;
   c->n_past[s] = n_past - nd;
@@ -1006,39 +1020,45 @@ int kv_shift(b2_context* c, int s, int p0, int p1) {
 }
 
 // Sequence-state snapshot (llama_state_seq_get_data / set_data): the
-// sequence's fp16 K and V rows of this rank's KV heads in logical position
-// order, behind a header that names the shape they belong to.
+// sequence's K and V rows of this rank's KV heads in logical position order
+// (rows in the cache types' storage), behind a header that names the shape
+// and cache types they belong to.
 struct SeqStateHeader {
   char magic[8];          // "B2KVSEQ"
-  uint32_t version;       // 1
-  int32_t n_layer, n_kv, head_dim, n_pos, kv_type, tp_rank, tp_size;
-  int32_t reserved[6];
+  uint32_t version;       // 2
+  int32_t n_layer, n_kv, head_dim, n_pos, type_k, tp_rank, tp_size, type_v;
+  int32_t reserved[5];
 };
+constexpr uint32_t kSeqVersion = 2;
 static_assert(sizeof(SeqStateHeader) == 64, "snapshot header size");
 constexpr char kSeqMagic[8] = {'B', '2', 'K', 'V', 'S', 'E', 'Q', 0};
 
 size_t seq_state_bytes(const b2_context* c, int n_pos) {
   const b2_model* m = c->model;
-  return sizeof(SeqStateHeader) + (size_t)m->n_layer * 2 * m->nkv_l * n_pos * m->head_dim * 2;
+  return sizeof(SeqStateHeader) + (size_t)m->n_layer * m->nkv_l * n_pos *
+                                      (size_t)(kv_row_bytes(c->type_k, m->head_dim) +
+                                               kv_row_bytes(c->type_v, m->head_dim));
 }
 
 // Copies logical positions [0, n_pos) of sequence s between the cache and
-// host memory: per layer K then V, each [n_kv][n_pos][head_dim].  The ring
+// host memory: per layer K then V, each [n_kv][n_pos] rows.  The ring
 // maps a position range to at most three contiguous slot runs; each run is
 // one strided copy over the KV heads.
 int seq_state_copy(b2_context* c, int s, int n_pos, uint8_t* host, bool to_host) {
   const b2_model* m = c->model;
   const KvSeqState st = to_host ? c->st[s] : KvSeqState{0, 0};
-  const size_t row = (size_t)m->head_dim * 2, cap = (size_t)c->n_ctx;
+  const size_t krow = kv_row_bytes(c->type_k, m->head_dim), vrow = kv_row_bytes(c->type_v, m->head_dim);
+  const size_t cap = (size_t)c->n_ctx;
   for (int l = 0; l < m->n_layer; ++l)
     for (int kv = 0; kv < 2; ++kv) {
-      uint16_t* base = (kv ? c->vc[l] : c->kc[l]) + (size_t)s * m->nkv_l * cap * m->head_dim;
-      uint8_t* h = host + ((size_t)l * 2 + kv) * m->nkv_l * n_pos * row;
+      const size_t row = kv ? vrow : krow;
+      uint8_t* base = (kv ? c->vc[l] : c->kc[l]) + (size_t)s * m->nkv_l * cap * row;
+      uint8_t* h = host + (size_t)l * m->nkv_l * n_pos * (krow + vrow) + (kv ? (size_t)m->nkv_l * n_pos * krow : 0);
       for (int p = 0; p < n_pos;) {
         const int64_t slot = kv_slot(st, p, c->n_ctx);
         int len = 1;
         while (p + len < n_pos && kv_slot(st, p + len, c->n_ctx) == slot + len) ++len;
-        uint8_t* dev = reinterpret_cast<uint8_t*>(base) + (size_t)slot * row;
+        uint8_t* dev = base + (size_t)slot * row;
         uint8_t* hp = h + (size_t)p * row;
         if (to_host)
           B2_CUDA_TRY(cudaMemcpy2DAsync(hp, (size_t)n_pos * row, dev, cap * row, (size_t)len * row, m->nkv_l,
@@ -1141,6 +1161,8 @@ void b2_context_default_params(b2_context_params* p) {
   p->n_seq_max = 1;
   p->use_graph = 1;
   p->prefill_gemm = 1;
+  p->type_k = B2_F16;
+  p->type_v = B2_F16;
 }
 
 int b2_context_create(b2_model* m, const b2_context_params* params, b2_context** out) {
@@ -1150,6 +1172,7 @@ int b2_context_create(b2_model* m, const b2_context_params* params, b2_context**
   b2_context_default_params(&p);
   if (params) p = *params;
   B2_CHECK_ARG(p.n_ctx > 0 && p.n_seq_max > 0, "n_ctx and n_seq_max must be positive");
+  B2_CHECK_ARG(kv_type_ok(p.type_k) && kv_type_ok(p.type_v), "type_k / type_v must be B2_F16 or B2_Q8_0");
   b2_context* c = new (std::nothrow) b2_context;
   if (!c) return B2_ERR_OOM;
   int rc;
@@ -1301,7 +1324,7 @@ int b2_n_ctx(const b2_context* c, int32_t* n_ctx) {
 
 int b2_memory_can_shift(const b2_context* c, int32_t* can_shift) {
   B2_CHECK_ARG(c && can_shift, "memory_can_shift arguments");
-  *can_shift = 1;   // the fp16 ring cache re-rotates K in place for any shift
+  *can_shift = 1;   // the ring cache re-rotates K in place (fp16 or Q8_0) for any shift
   return B2_OK;
 }
 
@@ -1330,12 +1353,13 @@ int b2_state_seq_get_data(b2_context* c, int32_t seq, void* dst, size_t size, si
   B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
   SeqStateHeader h = {};
   memcpy(h.magic, kSeqMagic, 8);
-  h.version = 1;
+  h.version = kSeqVersion;
   h.n_layer = m->n_layer;
   h.n_kv = m->nkv_l;
   h.head_dim = m->head_dim;
   h.n_pos = n_pos;
-  h.kv_type = B2_F16;
+  h.type_k = c->type_k;
+  h.type_v = c->type_v;
   h.tp_rank = m->tp_rank;
   h.tp_size = m->tp_size;
   memcpy(dst, &h, sizeof h);
@@ -1355,14 +1379,15 @@ int b2_state_seq_set_data(b2_context* c, int32_t seq, const void* src, size_t si
     return B2_ERR_FORMAT;
   }
   memcpy(&h, src, sizeof h);
-  if (memcmp(h.magic, kSeqMagic, 8) != 0 || h.version != 1) {
+  if (memcmp(h.magic, kSeqMagic, 8) != 0 || h.version != kSeqVersion) {
     set_error("state_seq_set_data: not a sequence-state snapshot of this library");
     return B2_ERR_FORMAT;
   }
-  if (h.n_layer != m->n_layer || h.n_kv != m->nkv_l || h.head_dim != m->head_dim || h.kv_type != B2_F16 ||
-      h.tp_rank != m->tp_rank || h.tp_size != m->tp_size) {
-    set_error("state_seq_set_data: snapshot of another model shape or rank (%d layers, %d kv heads, hd %d, "
-              "rank %d/%d)", h.n_layer, h.n_kv, h.head_dim, h.tp_rank, h.tp_size);
+  if (h.n_layer != m->n_layer || h.n_kv != m->nkv_l || h.head_dim != m->head_dim || h.type_k != c->type_k ||
+      h.type_v != c->type_v || h.tp_rank != m->tp_rank || h.tp_size != m->tp_size) {
+    set_error("state_seq_set_data: snapshot of another model shape, cache type or rank (%d layers, %d kv heads, "
+              "hd %d, K/V types %d/%d, rank %d/%d)", h.n_layer, h.n_kv, h.head_dim, h.type_k, h.type_v, h.tp_rank,
+              h.tp_size);
     return B2_ERR_FORMAT;
   }
   if (h.n_pos < 0 || h.n_pos > c->n_ctx) {

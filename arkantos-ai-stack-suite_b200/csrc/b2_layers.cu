@@ -2,7 +2,8 @@
 // forward_token (Singularity/src/core/cortex_a5_engine.cpp:1029-1293):
 //   embed         token row dequantization (:1066-1105)
 //   add_rmsnorm   residual add fused with RMSNorm (:1121, :1259-1266, :1284-1287)
-//   rope_kv       RoPE on q/k (adjacent pairs, :1187-1192) + fp16 K/V store (:1195-1203)
+//   rope_kv       RoPE on q/k (adjacent pairs, :1187-1192) + K/V store (:1195-1203) into an
+//                 fp16 or Q8_0 cache (llama.cpp cache types, Milda/src/engine.cpp:74-87)
 //   attn_split / attn_combine
 //                 split-K GQA decode attention over the fp16 cache (:1205-1254)
 //   kv_shift      in-place K re-rotation for Milda's KV shift (Milda/src/engine.cpp:1642-1675)
@@ -253,10 +254,53 @@ __global__ void add_rmsnorm_q_kernel(float* __restrict__ x, const float* __restr
 }
 
 // ---- RoPE + KV store -------------------------------------------------------------------------
+// Cache rows (one kv head at one slot) in the cache type's storage
+// (kv_row_bytes): fp16 values, or Q8_0 as hd int8 codes then the hd/32 fp16
+// block scales (quantized as ref_quantize_row_q8_0,
+// Singularity/tests/test_and_bench_a5.cpp:223-245).
+__device__ __forceinline__ uint8_t* kv_row(uint8_t* c, int type, int hd, int s, int n_kv, int kh, int cap,
+                                           int64_t slot) {
+  return c + (((int64_t)s * n_kv + kh) * cap + slot) * kv_row_bytes(type, hd);
+}
+// Value i of a row (fp16, or Q8_0 code · block scale: exact in fp32).
+template <int T>
+__device__ __forceinline__ float kv_load(const uint8_t* row, int hd, int i) {
+  if constexpr (T == B2_Q8_0) {
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(row + hd + 2 * (i >> 5)));
+    return __fmul_rn((float)(int8_t)row[i], d);
+  } else {
+    return h2f(reinterpret_cast<const uint16_t*>(row)[i]);
+  }
+}
+// Stores value i of a row; for Q8_0 the whole warp stores one 32-value block
+// (lane = value i % 32), the block's scale from lane 0.
+template <int T>
+__device__ __forceinline__ void kv_store(uint8_t* row, int hd, int i, float y) {
+  if constexpr (T == B2_Q8_0) {
+    uint16_t d16;
+    const int8_t q = quant_q8_0_lane(y, &d16);
+    row[i] = (uint8_t)q;
+    if ((threadIdx.x & 31) == 0) *reinterpret_cast<uint16_t*>(row + hd + 2 * (i >> 5)) = d16;
+  } else {
+    reinterpret_cast<uint16_t*>(row)[i] = f2h_rn(y);
+  }
+}
+// Adjacent-pair rotation of value i, from its own value x and its pair
+// partner's (lane i ^ 1): x0·c − x1·s for even i, x0·s + x1·c for odd i.
+__device__ __forceinline__ float rotate_lane(float x, int i, const float* cs) {
+  const float other = __shfl_xor_sync(0xffffffffu, x, 1);
+  const int pr = i & ~1;
+  const float c = cs[pr], sn = cs[pr + 1];
+  const float x0 = (i & 1) ? other : x, x1 = (i & 1) ? x : other;
+  return (i & 1) ? __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)) : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+}
 
+// One CTA per token: q heads rotated into q_out; K heads rotated and V heads
+// stored into the caches, one warp per 32-value block (hd % 32 == 0).
+template <int KT, int VT>
 __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_kv, int hd, const int32_t* __restrict__ pos,
                                const int32_t* __restrict__ seq, const float* __restrict__ rope, float* __restrict__ q_out,
-                               uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, const KvSeqState* __restrict__ st,
+                               uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, const KvSeqState* __restrict__ st,
                                int n_seq, int cap) {
   pdl_wait();
   pdl_launch_dependents();
@@ -271,87 +315,93 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_
   const float* cs = rope + (int64_t)p * hd;
   const int64_t slot = kv_slot(st ? st[s] : KvSeqState{0, 0}, p, cap);
   const int half = hd / 2;
-  for (int i = threadIdx.x; i < (n_head + n_kv) * half; i += blockDim.x) {
+  for (int i = threadIdx.x; i < n_head * half; i += blockDim.x) {
     const int h = i / half, pr = i - h * half;
     const float x0 = src[h * hd + 2 * pr], x1 = src[h * hd + 2 * pr + 1];
     const float c = cs[2 * pr], sn = cs[2 * pr + 1];
-    const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-    const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-    if (h < n_head) {
-      q_out[(int64_t)b * n_head * hd + h * hd + 2 * pr] = y0;
-      q_out[(int64_t)b * n_head * hd + h * hd + 2 * pr + 1] = y1;
-    } else {
-      const int kh = h - n_head;
-      uint16_t* dst = kc + (((int64_t)s * n_kv + kh) * cap + slot) * hd + 2 * pr;
-      dst[0] = f2h_rn(y0);
-      dst[1] = f2h_rn(y1);
-    }
+    q_out[(int64_t)b * n_head * hd + h * hd + 2 * pr] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    q_out[(int64_t)b * n_head * hd + h * hd + 2 * pr + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
   }
-  for (int i = threadIdx.x; i < n_kv * hd; i += blockDim.x) {
-    const int kh = i / hd, d = i - kh * hd;
-    vc[(((int64_t)s * n_kv + kh) * cap + slot) * hd + d] = f2h_rn(src[(n_head + n_kv) * hd + i]);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n_warps = blockDim.x >> 5;
+  const int nb = hd / 32;
+  for (int blk = warp; blk < 2 * n_kv * nb; blk += n_warps) {
+    const bool is_v = blk >= n_kv * nb;
+    const int kh = (blk - (is_v ? n_kv * nb : 0)) / nb;
+    const int i = (blk % nb) * 32 + lane;
+    if (!is_v) {
+      const float y = rotate_lane(src[(n_head + kh) * hd + i], i, cs);
+      kv_store<KT>(kv_row(kc, KT, hd, s, n_kv, kh, cap, slot), hd, i, y);
+    } else {
+      kv_store<VT>(kv_row(vc, VT, hd, s, n_kv, kh, cap, slot), hd, i, src[(n_head + n_kv + kh) * hd + i]);
+    }
   }
 }
 
 // ---- KV shift ----------------------------------------------------------------------------
 // Rotates K rows of logical positions [p_begin, p_end) of sequence s (slots
 // computed with the state before the shift) by the angle table of the
-// position delta, in place: fp16 -> fp32 -> rotate -> fp16 (RNE).  The table
-// comes by value (no upload, so the call is stream-ordered and capturable).
-__global__ void kv_shift_kernel(uint16_t* __restrict__ kc, int n_kv, int hd, int s, KvSeqState stt, int cap, int p_begin,
+// position delta, in place: value -> fp32 -> rotate -> the cache type's
+// storage (fp16 RNE, or Q8_0 requantized per block).  One warp per 32-value
+// block.  The table comes by value (no upload, so the call is
+// stream-ordered and capturable).
+template <int KT>
+__global__ void kv_shift_kernel(uint8_t* __restrict__ kc, int n_kv, int hd, int s, KvSeqState stt, int cap, int p_begin,
                                 int p_end, RotTable rt) {
   __shared__ float cs[2 * kRotPairs];
   for (int i = threadIdx.x; i < hd; i += blockDim.x) cs[i] = rt.cs[i];
   __syncthreads();
-  const int half = hd / 2;
-  const int64_t total = (int64_t)(p_end - p_begin) * n_kv * half;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int pr = (int)(i % half);
-    const int kh = (int)((i / half) % n_kv);
-    const int p = p_begin + (int)(i / ((int64_t)half * n_kv));
-    const int64_t slot = kv_slot(stt, p, cap);
-    uint16_t* row = kc + (((int64_t)s * n_kv + kh) * cap + slot) * hd;
-    const float x0 = h2f(row[2 * pr]), x1 = h2f(row[2 * pr + 1]);
-    const float c = cs[2 * pr], sn = cs[2 * pr + 1];
-    row[2 * pr] = f2h_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-    row[2 * pr + 1] = f2h_rn(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+  const int nb = hd / 32, lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)(p_end - p_begin) * n_kv * nb;
+  const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_w = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t w = w0; w < total; w += n_w) {
+    const int bi = (int)(w % nb);
+    const int kh = (int)((w / nb) % n_kv);
+    const int p = p_begin + (int)(w / ((int64_t)nb * n_kv));
+    uint8_t* row = kv_row(kc, KT, hd, s, n_kv, kh, cap, kv_slot(stt, p, cap));
+    const int i = bi * 32 + lane;
+    const float y = rotate_lane(kv_load<KT>(row, hd, i), i, cs);
+    __syncwarp();
+    kv_store<KT>(row, hd, i, y);
   }
 }
 
 // Moves K/V rows of logical [src0, src0+n) to logical [dst0, dst0+n) of one
 // sequence (dst0 < src0, processed in ascending order by a single CTA per
-// head so overlapping ranges move safely), rotating K by cs (delta table).
-__global__ void kv_compact_kernel(uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int n_kv, int hd, int s,
+// head so overlapping ranges move safely), rotating K by cs (delta table)
+// and storing it back in the cache type's storage.  hd threads, one value
+// each.
+template <int KT, int VT>
+__global__ void kv_compact_kernel(uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, int n_kv, int hd, int s,
                                   KvSeqState stt, int cap, int dst0, int src0, int n, RotTable rt) {
   __shared__ float cs[2 * kRotPairs];
   for (int i = threadIdx.x; i < hd; i += blockDim.x) cs[i] = rt.cs[i];
   __syncthreads();
-  const int kh = blockIdx.x;
-  const int half = hd / 2;
+  const int kh = blockIdx.x, i = threadIdx.x;
+  const int vb = (int)kv_row_bytes(VT, hd);
   for (int t = 0; t < n; ++t) {
     const int64_t ss = kv_slot(stt, src0 + t, cap), ds = kv_slot(stt, dst0 + t, cap);
-    uint16_t* ksrc = kc + (((int64_t)s * n_kv + kh) * cap + ss) * hd;
-    uint16_t* kdst = kc + (((int64_t)s * n_kv + kh) * cap + ds) * hd;
-    uint16_t* vsrc = vc + (((int64_t)s * n_kv + kh) * cap + ss) * hd;
-    uint16_t* vdst = vc + (((int64_t)s * n_kv + kh) * cap + ds) * hd;
-    float y0 = 0.f, y1 = 0.f;
-    uint16_t vv0 = 0, vv1 = 0;
-    if (threadIdx.x < half) {
-      const int pr = threadIdx.x;
-      const float x0 = h2f(ksrc[2 * pr]), x1 = h2f(ksrc[2 * pr + 1]);
-      const float c = cs[2 * pr], sn = cs[2 * pr + 1];
-      y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-      y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-      vv0 = vsrc[2 * pr];
-      vv1 = vsrc[2 * pr + 1];
+    const uint8_t* ksrc = kv_row(kc, KT, hd, s, n_kv, kh, cap, ss);
+    uint8_t* kdst = kv_row(kc, KT, hd, s, n_kv, kh, cap, ds);
+    const uint8_t* vsrc = kv_row(vc, VT, hd, s, n_kv, kh, cap, ss);
+    uint8_t* vdst = kv_row(vc, VT, hd, s, n_kv, kh, cap, ds);
+    const float y = rotate_lane(kv_load<KT>(ksrc, hd, i), i, cs);
+    // the V row moves as bytes: 2 per value for fp16, codes then scales for Q8_0
+    uint16_t v0 = 0;
+    uint8_t v1 = 0;
+    if constexpr (VT == B2_Q8_0) {
+      v1 = vsrc[i];
+      if (i < (vb - hd) / 2) v0 = reinterpret_cast<const uint16_t*>(vsrc + hd)[i];
+    } else {
+      v0 = reinterpret_cast<const uint16_t*>(vsrc)[i];
     }
     __syncthreads();
-    if (threadIdx.x < half) {
-      const int pr = threadIdx.x;
-      kdst[2 * pr] = f2h_rn(y0);
-      kdst[2 * pr + 1] = f2h_rn(y1);
-      vdst[2 * pr] = vv0;
-      vdst[2 * pr + 1] = vv1;
+    kv_store<KT>(kdst, hd, i, y);
+    if constexpr (VT == B2_Q8_0) {
+      vdst[i] = v1;
+      if (i < (vb - hd) / 2) reinterpret_cast<uint16_t*>(vdst + hd)[i] = v0;
+    } else {
+      reinterpret_cast<uint16_t*>(vdst)[i] = v0;
     }
     __syncthreads();
   }
@@ -489,28 +539,53 @@ int launch_add_rmsnorm_q(float* x, const float* delta, const float* w, float* ou
 }
 
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                   const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int n_seq, int cap,
-                   cudaStream_t s) {
-  return launch_pdl(rope_kv_kernel, dim3(n_tok), dim3(256), 0, s, qkv, n_head, n_kv, hd, pos, seq, rope, q_out, kc, vc,
-                    st, n_seq, cap);
+                   const float* rope, float* q_out, void* kc, int kt, void* vc, int vt, const KvSeqState* st, int n_seq,
+                   int cap, cudaStream_t s) {
+  B2_CHECK_ARG(kv_type_ok(kt) && kv_type_ok(vt), "KV cache types must be F16 or Q8_0");
+  B2_CHECK_ARG(hd % 32 == 0, "head_dim must be a multiple of 32");
+  uint8_t* k8 = static_cast<uint8_t*>(kc);
+  uint8_t* v8 = static_cast<uint8_t*>(vc);
+#define B2_ROPE_KV(KT, VT)                                                                                           \
+  if (kt == KT && vt == VT)                                                                                          \
+    return launch_pdl(rope_kv_kernel<KT, VT>, dim3(n_tok), dim3(256), 0, s, qkv, n_head, n_kv, hd, pos, seq, rope, \
+                      q_out, k8, v8, st, n_seq, cap);
+  B2_ROPE_KV(B2_F16, B2_F16)
+  B2_ROPE_KV(B2_F16, B2_Q8_0)
+  B2_ROPE_KV(B2_Q8_0, B2_F16)
+  B2_ROPE_KV(B2_Q8_0, B2_Q8_0)
+#undef B2_ROPE_KV
+  return B2_ERR_INVALID;
 }
 
-int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
+int launch_kv_shift(void* kc, int kt, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
                     const RotTable& cs, cudaStream_t s) {
   B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
+  B2_CHECK_ARG(hd % 32 == 0 && kv_type_ok(kt), "KV shift: head_dim % 32 and an F16 or Q8_0 cache");
   if (p_end <= p_begin) return B2_OK;
-  const int64_t total = (int64_t)(p_end - p_begin) * n_kv * (hd / 2);
-  const int grid = (int)std::min<int64_t>((total + 255) / 256, 4 * kSMs);
-  kv_shift_kernel<<<grid, 256, 0, s>>>(kc, n_kv, hd, seq, st, cap, p_begin, p_end, cs);
+  const int64_t warps = (int64_t)(p_end - p_begin) * n_kv * (hd / 32);
+  const int grid = (int)std::min<int64_t>((warps + 7) / 8, 4 * kSMs);
+  uint8_t* k8 = static_cast<uint8_t*>(kc);
+  if (kt == B2_Q8_0) kv_shift_kernel<B2_Q8_0><<<grid, 256, 0, s>>>(k8, n_kv, hd, seq, st, cap, p_begin, p_end, cs);
+  else kv_shift_kernel<B2_F16><<<grid, 256, 0, s>>>(k8, n_kv, hd, seq, st, cap, p_begin, p_end, cs);
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
 }
 
-int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int dst0,
-                      int src0, int n, const RotTable& cs, cudaStream_t s) {
+int launch_kv_compact(void* kc, int kt, void* vc, int vt, int n_kv, int hd, int seq, const KvSeqState& st, int cap,
+                      int dst0, int src0, int n, const RotTable& cs, cudaStream_t s) {
   B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
+  B2_CHECK_ARG(hd % 32 == 0 && kv_type_ok(kt) && kv_type_ok(vt), "KV compact: head_dim % 32, F16 or Q8_0 caches");
   if (n <= 0) return B2_OK;
-  kv_compact_kernel<<<n_kv, std::max(32, hd / 2), 0, s>>>(kc, vc, n_kv, hd, seq, st, cap, dst0, src0, n, cs);
+  uint8_t* k8 = static_cast<uint8_t*>(kc);
+  uint8_t* v8 = static_cast<uint8_t*>(vc);
+#define B2_COMPACT(KT, VT)                                                                                       \
+  if (kt == KT && vt == VT)                                                                                      \
+    kv_compact_kernel<KT, VT><<<n_kv, hd, 0, s>>>(k8, v8, n_kv, hd, seq, st, cap, dst0, src0, n, cs);
+  B2_COMPACT(B2_F16, B2_F16)
+  B2_COMPACT(B2_F16, B2_Q8_0)
+  B2_COMPACT(B2_Q8_0, B2_F16)
+  B2_COMPACT(B2_Q8_0, B2_Q8_0)
+#undef B2_COMPACT
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
 }

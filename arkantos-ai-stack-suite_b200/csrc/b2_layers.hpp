@@ -20,11 +20,17 @@ int launch_add_rmsnorm(float* x, const float* delta, const float* w, float* out,
 int launch_add_rmsnorm_q(float* x, const float* delta, const float* w, float* out, int n_tok, int n, float eps,
                          const ActImage& img, cudaStream_t s, const PeerIn* in = nullptr, int* status = nullptr);
 bool add_rmsnorm_q_supported(int n, int act_type);
+// KV cache rows: one kv head's hd values at one slot, [n_seq][n_kv][cap]
+// rows per cache.  F16: hd fp16 values.  Q8_0: hd int8 codes, then the hd/32
+// fp16 block scales, padded to a multiple of 16 bytes (so every row, and
+// every run of rows, starts 16-byte aligned for bulk and tensor copies).
+__host__ __device__ constexpr int64_t kv_row_bytes(int type, int hd) { return type == B2_Q8_0 ? hd + 16 : 2 * hd; }
+inline bool kv_type_ok(int type) { return type == B2_F16 || type == B2_Q8_0; }
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                   const float* rope, float* q_out, uint16_t* kc, uint16_t* vc, const KvSeqState* st, int n_seq, int cap,
-                   cudaStream_t s);
+                   const float* rope, float* q_out, void* kc, int kt, void* vc, int vt, const KvSeqState* st, int n_seq,
+                   int cap, cudaStream_t s);
 // Decode attention in the reference's order (b2_attn.cu): q fp32
-// [n_tok][n_head][hd] against the fp16 caches [n_seq][n_kv][cap][hd], out
+// [n_tok][n_head][hd] against the caches (rows as above, types kt / vt), out
 // fp32 [n_tok][n_head][hd].  `scratch` holds attn_scratch_floats floats
 // (16-byte aligned) of scores, exponentials and chunk maxima; it needs no
 // initialisation.  Queries whose sequence id is outside [0, n_seq) or whose
@@ -32,8 +38,8 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
 // may be null (plain layout).
 size_t attn_scratch_floats(int n_tok, int n_head, int n_kv, int cap);
 int launch_attention(const float* q, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
-                     const uint16_t* kc, const uint16_t* vc, const KvSeqState* st, int n_seq, int cap, float* scratch,
-                     float* out, cudaStream_t s, int* status = nullptr);
+                     const void* kc, int kt, const void* vc, int vt, const KvSeqState* st, int n_seq, int cap,
+                     float* scratch, float* out, cudaStream_t s, int* status = nullptr);
 // h [n_tok][ff] = silu(gate) * up over the (gate, up) row pairs of gu
 // [n_tok][2 ff], with the arithmetic of the GEMV's SwiGLU epilogue.
 int launch_swiglu_pairs(const float* gu, int n_tok, int ff, float* h, cudaStream_t s);
@@ -42,10 +48,10 @@ constexpr int kRotPairs = 128;
 struct RotTable {
   float cs[2 * kRotPairs];
 };
-int launch_kv_shift(uint16_t* kc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
+int launch_kv_shift(void* kc, int kt, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
                     const RotTable& cs, cudaStream_t s);
-int launch_kv_compact(uint16_t* kc, uint16_t* vc, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int dst0,
-                      int src0, int n, const RotTable& cs, cudaStream_t s);
+int launch_kv_compact(void* kc, int kt, void* vc, int vt, int n_kv, int hd, int seq, const KvSeqState& st, int cap,
+                      int dst0, int src0, int n, const RotTable& cs, cudaStream_t s);
 // Device-side greedy loop: argmax ids become the next step's tokens.
 struct GreedyFeed {
   int32_t* tok = nullptr;    // [n_tok] next step's tokens (null: no feed)

@@ -77,6 +77,6 @@ extern "C" int b2_attn_decode_noalloc(const float* q, const uint16_t* k_cache, c
   const int rc = scratch_address(static_cast<cudaStream_t>(stream), &base);
   if (rc) return rc;
   // every value the kernels read is written earlier in the same call
-  return launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, v_cache, nullptr, n_seq, cap,
-                          static_cast<float*>(base), out, static_cast<cudaStream_t>(stream));
+  return launch_attention(q, n_q, n_head, n_kv, head_dim, pos, seq, k_cache, B2_F16, v_cache, B2_F16, nullptr, n_seq,
+                          cap, static_cast<float*>(base), out, static_cast<cudaStream_t>(stream));
 }

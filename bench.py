@@ -369,12 +369,45 @@ def decode_weight_bytes(world: int = 1) -> int:
     return (c["n_layer"] * layer + head) // world
 
 
-def decode_kv_bytes(ctx_lens, world: int = 1) -> int:
-    """fp16 K and V bytes the attention of one step reads on one rank: per sequence
-    and layer 2 x (n_kv heads x head_dim) x 2 B x the positions attended."""
+def decode_kv_bytes(ctx_lens, world: int = 1, row_bytes: int | None = None) -> int:
+    """K and V bytes the attention of one step reads on one rank: per sequence
+    and layer 2 x n_kv heads x the bytes of a cached row (fp16: 2 x head_dim;
+    Q8_0: head_dim + 16) x the positions attended."""
     c = LLAMA_8B
-    kv = c["n_head_kv"] * (c["n_embd"] // c["n_head"])
-    return sum(c["n_layer"] * 2 * kv * 2 * int(n) for n in ctx_lens) // world
+    hd = c["n_embd"] // c["n_head"]
+    rb = 2 * hd if row_bytes is None else row_bytes
+    return sum(c["n_layer"] * 2 * c["n_head_kv"] * rb * int(n) for n in ctx_lens) // world
+
+
+def decode_q8_0_cache(b2, dist, model, args, warm: int, world: int) -> dict:
+    """The same batch-8 greedy decode (b2_generate, CUDA events, max over
+    ranks) over a Q8_0 K and V cache, Milda's default cache types: the
+    prompts are prefilled into a fresh context of that type first."""
+    n_ctx = PROMPT + warm + args.steps + 8
+    ctx = b2.Context(model, n_ctx=n_ctx, n_seq=BATCH, type_k=b2.Q8_0, type_v=b2.Q8_0)
+    prompts = prompts_8b()
+    first = []
+    for s in range(BATCH):
+        ctx.decode(prompts[s], pos=np.arange(PROMPT), seq=np.full(PROMPT, s), want_logits=2)
+        first.append(int(ctx.argmax()[0][-1]))
+    seqs = np.arange(BATCH, dtype=np.int32)
+    ids = ctx.generate(first, warm, seq=seqs)
+    e0, e1 = b2.Event(), b2.Event()
+    barrier(dist)
+    e0.record(ctx.stream)
+    ctx.generate(ids[-1].copy(), args.steps, seq=seqs)
+    e1.record(ctx.stream)
+    ctx.synchronize()
+    ms_total = dist_max(dist, e0.elapsed_ms(e1))
+    ms_step = ms_total / args.steps
+    p_start = PROMPT + warm
+    ctx_lens = [p_start + k + 1 for k in range(args.steps) for _ in range(BATCH)]
+    kv = decode_kv_bytes(ctx_lens, world, int(b2.lib.b2_kv_row_bytes(b2.Q8_0, LLAMA_8B["n_embd"] // LLAMA_8B["n_head"])))
+    del ctx
+    return {"metric": "decode tok/s (Llama-shape 8B Q4_K, batch 8, Q8_0 K and V cache)",
+            "value": round(BATCH * args.steps / (ms_total * 1e-3), 1), "unit": "tok/s", "steps": args.steps,
+            "ms_per_step": ms_step, "kv_bytes_per_step": int(kv / args.steps),
+            "timed_region": "b2_generate: K greedy steps, device-side feedback"}
 
 
 def model_path(tag: str) -> str:
@@ -555,7 +588,10 @@ def run_decode_ours(args, dist, rank, world, local):
     ff_l = c["n_ff"] // world
     progress("kernel roofline")
     g = time_gemv_shape(b2, b2.Q4_K, 2 * ff_l, c["n_embd"], BATCH, 64, 7)
-    del ctx, model
+    del ctx
+    progress("decode over a Q8_0 KV cache")
+    q8kv = decode_q8_0_cache(b2, dist, model, args, warm, world)
+    del model
     q40 = gemv_q4_0_measure(b2, 200) if rank == 0 else None
     out = {
         "metric": "decode tok/s (Llama-shape 8B Q4_K, batch 8)",
@@ -592,6 +628,7 @@ def run_decode_ours(args, dist, rank, world, local):
         "prefill_tok_s": round(BATCH * PROMPT / t_prefill, 1),
         "prefill": prefill_report(c, t_prefill, world, peaks),
     }
+    out["decode_q8_0_kv"] = q8kv
     if q40 is not None:
         out["q4_0_gemv"] = q40
     if world == 1 and not args.skip_1b:
@@ -821,15 +858,24 @@ def run_decode1b_ours(args, dist, rank, world, local):
 ATTN_HEADS, ATTN_KV, ATTN_HD, ATTN_CTX = 32, 8, 128, 4096
 
 
-def attn_measure(b2, n_seq: int, steps: int) -> dict:
-    """CUDA-event time of b2_attn_decode (one query per sequence at position
-    ctx-1, all ctx positions attended) over rotating KV copies larger than L2,
-    and of the shift that drops the first 1024 positions and re-ropes K."""
+def attn_measure(b2, n_seq: int, steps: int, kv_type: int = 1) -> dict:
+    """CUDA-event time of b2_attn_decode_typed (one query per sequence at
+    position ctx-1, all ctx positions attended) over rotating KV copies
+    larger than L2, and of the shift that drops the first 1024 positions and
+    re-ropes K.  kv_type: B2_F16 (1) or B2_Q8_0 (8) for both caches; Q8_0
+    rows hold random codes and a fixed block scale."""
     rng = np.random.default_rng(4)
-    per_seq = ATTN_KV * ATTN_CTX * ATTN_HD            # fp16 values per sequence per cache
-    kv_bytes = 2 * 2 * per_seq * n_seq
+    rb = int(b2.lib.b2_kv_row_bytes(kv_type, ATTN_HD))   # bytes per cached row (one kv head, one position)
+    rows = ATTN_KV * ATTN_CTX * n_seq
+    kv_bytes = 2 * rows * rb
     copies = max(1, -(-300_000_000 // kv_bytes))
-    kv = rng.standard_normal(per_seq * n_seq, dtype=np.float32).astype(np.float16).view(np.uint16)
+    if kv_type == b2.F16:
+        kv = rng.standard_normal(rows * ATTN_HD, dtype=np.float32).astype(np.float16).view(np.uint8)
+    else:
+        kv = np.zeros((rows, rb), np.uint8)
+        kv[:, :ATTN_HD] = rng.integers(-127, 128, (rows, ATTN_HD), dtype=np.int8).view(np.uint8)
+        kv[:, ATTN_HD:ATTN_HD + ATTN_HD // 16] = np.frombuffer(np.float16(0.01).tobytes() * (ATTN_HD // 32), np.uint8)
+        kv = kv.ravel()
     ks = [b2.DeviceBuffer.from_array(kv) for _ in range(copies)]
     vs = [b2.DeviceBuffer.from_array(kv[::-1].copy()) for _ in range(copies)]
     q = b2.DeviceBuffer.from_array(rng.standard_normal((n_seq, ATTN_HEADS * ATTN_HD), dtype=np.float32))
@@ -839,8 +885,9 @@ def attn_measure(b2, n_seq: int, steps: int) -> dict:
     stream = b2.Stream()
 
     def one(i, s):
-        b2.check(b2.lib.b2_attn_decode(q.ptr, ks[i % copies].ptr, vs[i % copies].ptr, pos.ptr, seq.ptr, n_seq,
-                                       n_seq, ATTN_HEADS, ATTN_KV, ATTN_HD, ATTN_CTX, out.ptr, s), "attn_decode")
+        b2.check(b2.lib.b2_attn_decode_typed(q.ptr, ks[i % copies].ptr, kv_type, vs[i % copies].ptr, kv_type, pos.ptr,
+                                             seq.ptr, n_seq, n_seq, ATTN_HEADS, ATTN_KV, ATTN_HD, ATTN_CTX, out.ptr, s),
+                 "attn_decode")
 
     for i in range(2 * copies):
         one(i, stream.h)
@@ -857,8 +904,8 @@ def attn_measure(b2, n_seq: int, steps: int) -> dict:
     # KV shift: positions [1024, 4096) of every sequence rotated by -1024 (K read + write)
     def shift(i, s):
         for sq in range(n_seq):
-            b2.check(b2.lib.b2_kv_shift_k(ks[i % copies].ptr, sq, ATTN_KV, ATTN_HD, ATTN_CTX, 1024, ATTN_CTX, -1024,
-                                          10000.0, s), "kv_shift_k")
+            b2.check(b2.lib.b2_kv_shift_k_typed(ks[i % copies].ptr, kv_type, sq, ATTN_KV, ATTN_HD, ATTN_CTX, 1024,
+                                                ATTN_CTX, -1024, 10000.0, s), "kv_shift_k")
     shift(0, stream.h)
     sg = b2.Graph(stream, lambda s: [shift(i, s) for i in range(max(1, steps // 4))])
     sg.launch()
@@ -868,8 +915,8 @@ def attn_measure(b2, n_seq: int, steps: int) -> dict:
     e1.record(stream.h)
     stream.synchronize()
     ms_shift = e0.elapsed_ms(e1) / max(1, steps // 4)
-    shift_bytes = n_seq * 2 * (ATTN_CTX - 1024) * ATTN_KV * ATTN_HD * 2
-    return {"batch": n_seq, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes, "copies": copies,
+    shift_bytes = n_seq * 2 * (ATTN_CTX - 1024) * ATTN_KV * rb
+    return {"batch": n_seq, "kv_type": "q8_0" if kv_type == b2.Q8_0 else "f16", "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes, "copies": copies,
             "shift_ms": ms_shift, "shift_gbs": shift_bytes / (ms_shift * 1e-3) / 1e9, "shift_bytes": shift_bytes}
 
 
@@ -878,6 +925,8 @@ def run_attn_ours(args, dist, rank, world, local):
     b2.check(b2.lib.b2_set_device(local), "set_device")
     batches = (1, 4, 16) if args.attn_batch is None else (args.attn_batch,)
     res = [attn_measure(b2, n, args.steps) for n in batches]
+    # Milda's default cache type (Q8_0 K and V), the same batches
+    res_q8 = [attn_measure(b2, n, args.steps, b2.Q8_0) for n in batches]
     peaks = measured_peaks()
     big = res[-1]
     return {"metric": "decode attention HBM GB/s (32 q / 8 kv heads, hd 128, ctx 4096, fp16 KV)",
@@ -890,7 +939,8 @@ def run_attn_ours(args, dist, rank, world, local):
                          "frac": round(big["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
                          "algorithmic_bytes_per_launch": big["bytes"]},
             "batches": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()} for r in res],
-            "gpu_launches": args.steps * 2}
+            "batches_q8_0": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()} for r in res_q8],
+            "gpu_launches": args.steps * 3}
 
 
 # ------------------------------------------------------------------------------------------

@@ -242,6 +242,29 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
                           const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv, int head_dim, int cap,
                           float* out, void* stream);
 
+/* KV caches of either type (B2_F16 or B2_Q8_0; llama.cpp's cache types,
+ * Milda/src/engine.cpp:74-87).  Rows of one kv head at one slot,
+ * [n_seq][n_kv][cap] rows per cache, b2_kv_row_bytes(type, head_dim) bytes
+ * each: B2_F16 head_dim fp16 values; B2_Q8_0 head_dim int8 codes followed by
+ * the head_dim/32 fp16 block scales, padded to head_dim + 16 bytes.
+ * Storing quantizes each 32-value block as ref_quantize_row_q8_0
+ * (Singularity/tests/test_and_bench_a5.cpp:223-245).  Attention over a Q8_0
+ * K quantizes each query head to Q8_0 and scores position t as
+ * ref_vec_dot_q8_0_q8_0 (:205-221) of the K row and the query, times
+ * 1/sqrt(hd); over a Q8_0 V it sums p_t·(d·q) with the dequantized values
+ * (exact in fp32); everything else as b2_attn_decode.  The shift
+ * dequantizes, rotates and re-quantizes K.  head_dim a multiple of 32.
+ * b2_kv_row_bytes returns 0 for other types. */
+B2_API int64_t b2_kv_row_bytes(int type, int head_dim);
+B2_API int b2_rope_kv_store_typed(const float* qkv, int n_tok, int n_seq, int n_head, int n_kv, int head_dim,
+                                  const int32_t* pos, const int32_t* seq, const float* rope, float* q_out,
+                                  void* k_cache, int type_k, void* v_cache, int type_v, int cap, void* stream);
+B2_API int b2_attn_decode_typed(const float* q, const void* k_cache, int type_k, const void* v_cache, int type_v,
+                                const int32_t* pos, const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv,
+                                int head_dim, int cap, float* out, void* stream);
+B2_API int b2_kv_shift_k_typed(void* k_cache, int type_k, int seq, int n_kv, int head_dim, int cap, int p_begin,
+                               int p_end, int delta, float theta, void* stream);
+
 /* b2_attn_decode for callers that cannot allocate device memory while they
  * run (a host that gives the library a fixed device-memory budget at
  * start-up, or a real-time decode loop that must not pay an allocation's
@@ -348,10 +371,19 @@ typedef struct b2_context_params {
                              Their projections then sum in the reference's row order (the
                              CPU matmul_quantized's) instead of the decode GEMV's tile order;
                              the last 8 tokens take the decode step. */
+    int32_t type_k;       /* K cache type (llama_context_params.type_k, set from Milda's
+                             cache_type_k at Milda/src/engine.cpp:1195): B2_F16 (default) or
+                             B2_Q8_0 */
+    int32_t type_v;       /* V cache type (type_v, :1196): B2_F16 (default) or B2_Q8_0 */
 } b2_context_params;
 
 /* llama_context_default_params / llama_init_from_model
- * (Milda/src/engine.cpp:1180-1206): fp16 KV cache. */
+ * (Milda/src/engine.cpp:1180-1206): fp16 KV cache by default.  A Q8_0 cache
+ * (Milda's default cache_type_k / cache_type_v, Milda/include/milda/engine.hpp:85-86)
+ * stores each row's 32-value blocks with the reference's Q8_0 quantizer and
+ * attends as llama.cpp does over such a cache: the query quantized to Q8_0
+ * and scored with the Q8_0·Q8_0 block dot, V rows dequantized (d·q), the
+ * softmax and sums as for fp16 (see b2_attn_decode_typed). */
 B2_API void b2_context_default_params(b2_context_params* p);
 B2_API int  b2_context_create(b2_model* m, const b2_context_params* params, b2_context** out);
 B2_API int  b2_context_free(b2_context* c);   /* llama_free */
@@ -406,12 +438,14 @@ B2_API int b2_memory_can_shift(const b2_context* c, int32_t* can_shift);
  * get_data / set_data (Milda/src/engine.cpp:1487-1492 pins the system
  * prompt's state, :1701-1705 restores it; Sutra/src/llm_backends.cpp:2572-2580
  * caches a prefix).  The snapshot holds the sequence's positions
- * [0, pos_max] — this rank's KV heads, fp16 K and V per layer in position
- * order — behind a 64-byte header naming the model shape and rank.
+ * [0, pos_max] — this rank's KV heads, K and V rows per layer in position
+ * order, in the cache types' storage — behind a 64-byte header naming the
+ * model shape, the cache types and the rank.
  * get_size: bytes the snapshot of `seq` takes now.  get_data: writes it to
  * dst (size >= get_size) and sets *written.  set_data: replaces sequence
  * `seq` (any id of this context) with the snapshot; *read = bytes consumed.
- * A snapshot of another shape or rank is refused with B2_ERR_FORMAT, one
+ * A snapshot of another shape, cache type or rank is refused with
+ * B2_ERR_FORMAT, one
  * longer than n_ctx with B2_NO_KV_SLOT.  Synchronous. */
 B2_API int b2_state_seq_get_size(b2_context* c, int32_t seq, size_t* size);
 B2_API int b2_state_seq_get_data(b2_context* c, int32_t seq, void* dst, size_t size, size_t* written);

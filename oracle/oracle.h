@@ -98,6 +98,23 @@ void orc_attn_decode(const float* q, const uint16_t* kc, const uint16_t* vc, int
 void orc_kv_shift_k(uint16_t* kc, int64_t kv_stride, int n_pos, int n_kv_heads, int hd,
                     int delta, float theta);
 
+/* Quantized KV cache (llama.cpp cache types; Milda's default is Q8_0 K and
+ * V).  Rows hold hd values of one kv head in the type's storage: fp16, or
+ * ggml Q8_0 blocks.  A row is stored with the type's quantizer (Q8_0:
+ * orc_quantize_row_q8_0).  Attention: with a Q8_0 K the query head is
+ * quantized to Q8_0 and scored with orc_vec_dot_q8_0_q8_0 (times 1/√hd);
+ * V rows are dequantized before the weighted sum; softmax and summation
+ * order as orc_attn_decode.  Row (t, kvh) at base + t*stride + kvh*row
+ * bytes; strides in bytes.  The shift dequantizes, rotates as
+ * orc_kv_shift_k and stores back with the type's quantizer. */
+void orc_kv_store_row(int type, const float* x, void* row, int n);
+void orc_kv_store_rows(int type, const float* x, void* rows, int64_t n_rows, int n);
+void orc_attn_decode_typed(const float* q, const void* kc, int ktype, size_t k_stride, const void* vc,
+                           int vtype, size_t v_stride, int n_pos, int n_heads, int n_kv_heads, int hd,
+                           float* out);
+void orc_kv_shift_k_typed(void* kc, int ktype, size_t k_stride, int n_pos, int n_kv_heads, int hd, int delta,
+                          float theta);
+
 /* ---- Device-order arithmetic (the GPU kernels' evaluation order) ---- */
 float orc_expf_dev(float x);
 void  orc_silu_mul_dev(float* hb, const float* hb2, int n);
@@ -121,8 +138,11 @@ orc_model* orc_model_open(const char* path);   /* mmap a GGUF file */
 orc_model* orc_model_from_memory(const void* data, size_t size);
 void       orc_model_free(orc_model* m);
 int        orc_model_info(const orc_model* m, int32_t* out, int n_out);
-/* Per-sequence fp16 KV cache of n_ctx positions. */
+/* Per-sequence KV cache of n_ctx positions (fp16 unless set otherwise). */
 int  orc_model_init_cache(orc_model* m, int n_seq, int n_ctx);
+/* K and V cache types (ORC_F16 or ORC_Q8_0); re-creates an existing cache
+ * empty.  Returns -1 for other types. */
+int  orc_model_set_kv_types(orc_model* m, int ktype, int vtype);
 /* Sets every cached K and V value to the fp16 `bits` (touches the pages, so
  * timed attention reads real memory rather than never-written zero pages). */
 void orc_model_cache_fill(orc_model* m, uint16_t bits);

@@ -59,6 +59,12 @@ def _load() -> ctypes.CDLL:
         "orc_matmul": (None, [_i, _vp, ctypes.c_int64, _i, _vp, _vp, _i]),
         "orc_attn_decode": (None, [_vp, _vp, _vp, ctypes.c_int64, _i, _i, _i, _i, _vp]),
         "orc_kv_shift_k": (None, [_vp, ctypes.c_int64, _i, _i, _i, _i, _f]),
+        "orc_kv_store_row": (None, [_i, _vp, _vp, _i]),
+        "orc_kv_store_rows": (None, [_i, _vp, _vp, ctypes.c_int64, _i]),
+        "orc_attn_decode_typed": (None, [_vp, _vp, _i, ctypes.c_size_t, _vp, _i, ctypes.c_size_t, _i, _i, _i, _i,
+                                         _vp]),
+        "orc_kv_shift_k_typed": (None, [_vp, _i, ctypes.c_size_t, _i, _i, _i, _i, _f]),
+        "orc_model_set_kv_types": (_i, [_vp, _i, _i]),
         "orc_model_open": (_vp, [ctypes.c_char_p]),
         "orc_model_from_memory": (_vp, [_vp, ctypes.c_size_t]),
         "orc_model_free": (None, [_vp]),
@@ -258,6 +264,36 @@ def kv_shift_k(kc: np.ndarray, n_pos: int, n_kv: int, hd: int, delta: int, theta
     return kc
 
 
+def kv_store_rows(t: int, x: np.ndarray) -> np.ndarray:
+    """Cache rows in type t's storage (F16 bits or Q8_0 blocks) as bytes:
+    x [..., n] fp32 -> uint8 [..., row_bytes(t, n)]."""
+    x = np.ascontiguousarray(x, np.float32)
+    n = x.shape[-1]
+    rows = x.reshape(-1, n)
+    out = np.zeros((rows.shape[0], row_bytes(t, n)), np.uint8)
+    lib.orc_kv_store_rows(t, _p(rows), _p(out), rows.shape[0], n)
+    return out.reshape(x.shape[:-1] + (out.shape[-1],))
+
+
+def attn_decode_typed(q: np.ndarray, kc: np.ndarray, ktype: int, vc: np.ndarray, vtype: int, n_pos: int,
+                      n_heads: int, n_kv: int, hd: int) -> np.ndarray:
+    """q: [n_heads*hd] fp32; kc / vc: uint8 [n_pos, n_kv * row_bytes(type, hd)]."""
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(kc, np.uint8).reshape(n_pos, -1)
+    vc = np.ascontiguousarray(vc, np.uint8).reshape(n_pos, -1)
+    out = np.zeros(n_heads * hd, np.float32)
+    lib.orc_attn_decode_typed(_p(q), _p(kc), ktype, kc.shape[1], _p(vc), vtype, vc.shape[1], n_pos, n_heads, n_kv,
+                              hd, _p(out))
+    return out
+
+
+def kv_shift_k_typed(kc: np.ndarray, ktype: int, n_pos: int, n_kv: int, hd: int, delta: int,
+                     theta: float) -> np.ndarray:
+    kc = np.array(kc, np.uint8, copy=True, order="C").reshape(n_pos, -1)
+    lib.orc_kv_shift_k_typed(_p(kc), ktype, kc.shape[1], n_pos, n_kv, hd, delta, theta)
+    return kc
+
+
 class Model:
     """Oracle Llama forward over a GGUF file or buffer."""
 
@@ -279,6 +315,11 @@ class Model:
         """GPU kernels' order (on), optionally with the projections in the
         reference's row order, as the tensor-core prefill GEMMs compute them."""
         lib.orc_model_set_device_order(self.h, (2 if gemm_projections else 1) if on else 0)
+
+    def set_kv_types(self, ktype: int, vtype: int) -> None:
+        """K and V cache types (F16 or Q8_0); an existing cache restarts empty."""
+        if lib.orc_model_set_kv_types(self.h, ktype, vtype) != 0:
+            raise ValueError(f"oracle: unsupported cache types {ktype}/{vtype}")
 
     def init_cache(self, n_seq: int, n_ctx: int) -> None:
         if lib.orc_model_init_cache(self.h, n_seq, n_ctx) != 0:

@@ -42,7 +42,8 @@ struct orc_model {
     orc_layer* layers;
     /* runtime */
     int n_seq, n_ctx;
-    uint16_t *kc, *vc; /* [seq][layer][pos][kv_dim] */
+    uint8_t *kc, *vc;  /* [seq][layer][pos][kv_dim], rows in the cache types' storage */
+    int ktype, vtype;  /* ORC_F16 (default) or ORC_Q8_0 */
     float *x, *xb, *xb2, *q, *k, *v, *hb, *hb2;
     void* xq;
     float* rope;
@@ -56,6 +57,13 @@ struct orc_model {
 };
 
 void orc_model_set_device_order(orc_model* m, int on) { m->device_order = on; }
+
+int orc_model_set_kv_types(orc_model* m, int ktype, int vtype) {
+    if ((ktype != ORC_F16 && ktype != ORC_Q8_0) || (vtype != ORC_F16 && vtype != ORC_Q8_0)) return -1;
+    m->ktype = ktype;
+    m->vtype = vtype;
+    return m->kc ? orc_model_init_cache(m, m->n_seq, m->n_ctx) : 0;
+}
 
 int orc_model_set_tp(orc_model* m, int tp) {
     if (tp < 1 || m->n_heads % tp || m->n_kv % tp || m->hidden % tp || m->vocab % tp) return -1;
@@ -229,6 +237,7 @@ static int parse(orc_model* m) {
 
 orc_model* orc_model_from_memory(const void* data, size_t size) {
     orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
+    m->ktype = m->vtype = ORC_F16;
     m->base = (const uint8_t*)data;
     m->size = size;
     if (parse(m) != 0) {
@@ -275,9 +284,9 @@ int orc_model_init_cache(orc_model* m, int n_seq, int n_ctx) {
     free(m->kc); free(m->vc); free(m->rope);
     m->n_seq = n_seq;
     m->n_ctx = n_ctx;
-    const size_t n = (size_t)n_seq * m->n_layers * n_ctx * kv_dim;
-    m->kc = (uint16_t*)calloc(n, 2);
-    m->vc = (uint16_t*)calloc(n, 2);
+    const size_t n = (size_t)n_seq * m->n_layers * n_ctx;
+    m->kc = (uint8_t*)calloc(n, orc_row_bytes(m->ktype, kv_dim));
+    m->vc = (uint8_t*)calloc(n, orc_row_bytes(m->vtype, kv_dim));
     m->rope = (float*)malloc(sizeof(float) * (size_t)n_ctx * m->head_dim);
     orc_rope_table(m->theta, m->head_dim, 0, n_ctx, m->rope);
     const int big = m->dim > m->hidden ? m->dim : m->hidden;
@@ -295,9 +304,24 @@ int orc_model_init_cache(orc_model* m, int n_seq, int n_ctx) {
     return (m->kc && m->vc) ? 0 : -1;
 }
 
+/* fp16 rows take `bits` in every value; Q8_0 rows take `bits` as every
+ * block's scale and 1 as every code. */
+static void cache_fill_rows(uint8_t* c, int type, size_t n_vals, uint16_t bits) {
+    if (type == ORC_Q8_0) {
+        for (size_t b = 0; b < n_vals / 32; ++b) {
+            uint8_t* blk = c + b * ORC_Q8_0_BYTES;
+            memcpy(blk, &bits, 2);
+            memset(blk + 2, 1, 32);
+        }
+    } else {
+        for (size_t i = 0; i < n_vals; ++i) memcpy(c + 2 * i, &bits, 2);
+    }
+}
+
 void orc_model_cache_fill(orc_model* m, uint16_t bits) {
     const size_t n = (size_t)m->n_seq * m->n_layers * m->n_ctx * m->head_dim * m->n_kv;
-    for (size_t i = 0; i < n; ++i) { m->kc[i] = bits; m->vc[i] = bits; }
+    cache_fill_rows(m->kc, m->ktype, n, bits);
+    cache_fill_rows(m->vc, m->vtype, n, bits);
 }
 
 /* matmul_quantized with the activation quantized for the weight's dot type
@@ -350,7 +374,8 @@ int orc_model_forward_range(orc_model* m, int seq, int32_t token, int pos, int l
         l0 = 0;
     }
     const float* cs = m->rope + (size_t)pos * hd;
-    const size_t seq_stride = (size_t)m->n_layers * m->n_ctx * kv_dim;
+    const size_t krb = orc_row_bytes(m->ktype, kv_dim), vrb = orc_row_bytes(m->vtype, kv_dim);
+    const int typed = m->ktype != ORC_F16 || m->vtype != ORC_F16;
     const int nl = l1 < m->n_layers ? l1 : m->n_layers;
     for (int l = l0; l < nl; ++l) {
         const orc_layer* L = &m->layers[l];
@@ -365,12 +390,19 @@ int orc_model_forward_range(orc_model* m, int seq, int32_t token, int pos, int l
         orc_rope_pairs(m->q, cs, hd, m->n_heads);                                     /* :1187 */
         orc_rope_pairs(m->k, cs, hd, nkv);
         TAP("q_rope", l, m->q, dim);
-        uint16_t* kc = m->kc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
-        uint16_t* vc = m->vc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
-        orc_fp32_to_fp16_row(m->k, kc + (size_t)pos * kv_dim, kv_dim);                /* :1195 */
-        orc_fp32_to_fp16_row(m->v, vc + (size_t)pos * kv_dim, kv_dim);
-        if (m->device_order) orc_attn_decode_dev(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);
-        else orc_attn_decode(m->q, kc, vc, kv_dim, pos + 1, m->n_heads, nkv, hd, m->xb);   /* :1205 */
+        const size_t cache_row = ((size_t)seq * m->n_layers + l) * m->n_ctx;
+        uint8_t* kc = m->kc + cache_row * krb;
+        uint8_t* vc = m->vc + cache_row * vrb;
+        orc_kv_store_row(m->ktype, m->k, kc + (size_t)pos * krb, kv_dim);             /* :1195 */
+        orc_kv_store_row(m->vtype, m->v, vc + (size_t)pos * vrb, kv_dim);
+        if (typed)
+            orc_attn_decode_typed(m->q, kc, m->ktype, krb, vc, m->vtype, vrb, pos + 1, m->n_heads, nkv, hd, m->xb);
+        else if (m->device_order)
+            orc_attn_decode_dev(m->q, (const uint16_t*)kc, (const uint16_t*)vc, kv_dim, pos + 1, m->n_heads, nkv,
+                                hd, m->xb);
+        else
+            orc_attn_decode(m->q, (const uint16_t*)kc, (const uint16_t*)vc, kv_dim, pos + 1, m->n_heads, nkv, hd,
+                            m->xb);                                                   /* :1205 */
         TAP("attn_out", l, m->xb, dim);
         proj_reduce(m, &L->wo, m->xb, m->xb2, nt);                                    /* :1256 */
         TAP("attn_proj", l, m->xb2, dim);
@@ -413,14 +445,20 @@ int orc_model_hidden(const orc_model* m, float* out, int n) {
 int orc_model_kv_shift(orc_model* m, int seq, int p0, int p1, int n_past) {
     if (!m->kc || p0 < 0 || p1 < p0 || n_past < p1 || n_past > m->n_ctx) return -1;
     const int kv_dim = m->head_dim * m->n_kv;
-    const size_t seq_stride = (size_t)m->n_layers * m->n_ctx * kv_dim;
+    const size_t krb = orc_row_bytes(m->ktype, kv_dim), vrb = orc_row_bytes(m->vtype, kv_dim);
     const int n_move = n_past - p1;
     for (int l = 0; l < m->n_layers; ++l) {
-        uint16_t* kc = m->kc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
-        uint16_t* vc = m->vc + seq * seq_stride + (size_t)l * m->n_ctx * kv_dim;
-        memmove(kc + (size_t)p0 * kv_dim, kc + (size_t)p1 * kv_dim, (size_t)n_move * kv_dim * 2);
-        memmove(vc + (size_t)p0 * kv_dim, vc + (size_t)p1 * kv_dim, (size_t)n_move * kv_dim * 2);
-        orc_kv_shift_k(kc + (size_t)p0 * kv_dim, kv_dim, n_move, m->n_kv, m->head_dim, -(p1 - p0), m->theta);
+        const size_t cache_row = ((size_t)seq * m->n_layers + l) * m->n_ctx;
+        uint8_t* kc = m->kc + cache_row * krb;
+        uint8_t* vc = m->vc + cache_row * vrb;
+        memmove(kc + (size_t)p0 * krb, kc + (size_t)p1 * krb, (size_t)n_move * krb);
+        memmove(vc + (size_t)p0 * vrb, vc + (size_t)p1 * vrb, (size_t)n_move * vrb);
+        if (m->ktype == ORC_F16)
+            orc_kv_shift_k((uint16_t*)(kc + (size_t)p0 * krb), kv_dim, n_move, m->n_kv, m->head_dim, -(p1 - p0),
+                           m->theta);
+        else
+            orc_kv_shift_k_typed(kc + (size_t)p0 * krb, m->ktype, krb, n_move, m->n_kv, m->head_dim, -(p1 - p0),
+                                 m->theta);
     }
     return 0;
 }

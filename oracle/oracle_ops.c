@@ -852,3 +852,102 @@ void orc_kv_shift_k(uint16_t* kc, int64_t kv_stride, int n_pos, int n_kv_heads, 
     }
     free(cs);
 }
+
+/* ------------------------------------------------------------------------ */
+/* Quantized KV cache (llama.cpp cache types)                                */
+/* ------------------------------------------------------------------------ */
+
+/* Milda asks llama.cpp for a Q8_0 K and V cache by default
+ * (Milda/include/milda/engine.hpp:85-86, mapped at Milda/src/engine.cpp:74-87
+ * and set at :1195-1196) with flash attention on (engine.hpp:91,
+ * engine.cpp:1197).  llama.cpp (absent from the reference tree) stores each
+ * cached row with its type's quantizer, pairs a quantized K row with the
+ * query quantized to the K type's dot type (Q8_0 for Q8_0 K) and scores with
+ * that type's block dot, and dequantizes V rows (d·q) before the weighted
+ * sum.  Restated here with the reference's own ops: Q8_0 quantization and
+ * the Q8_0·Q8_0 dot of Singularity/tests/test_and_bench_a5.cpp:205-245, the
+ * Q8_0 dequantization of Singularity/src/core/cortex_a5_engine.cpp:1090-1105,
+ * and the softmax and order of the fp16 attention above
+ * (cortex_a5_engine.cpp:1205-1254). */
+
+static size_t kv_row_bytes(int type, int hd) { return orc_row_bytes(type, hd); }
+
+void orc_kv_store_row(int type, const float* x, void* row, int n) {
+    if (type == ORC_Q8_0) orc_quantize_row_q8_0(x, row, n);
+    else orc_fp32_to_fp16_row(x, (uint16_t*)row, n);
+}
+
+void orc_kv_store_rows(int type, const float* x, void* rows, int64_t n_rows, int n) {
+    const size_t rb = kv_row_bytes(type, n);
+    for (int64_t r = 0; r < n_rows; ++r) orc_kv_store_row(type, x + (size_t)r * n, (uint8_t*)rows + (size_t)r * rb, n);
+}
+
+void orc_attn_decode_typed(const float* q, const void* kc, int ktype, size_t k_stride, const void* vc,
+                           int vtype, size_t v_stride, int n_pos, int n_heads, int n_kv_heads, int hd,
+                           float* out) {
+    int gqa = 1;
+    while (gqa * n_kv_heads < n_heads) ++gqa;
+    const float att_scale = 1.0f / sqrtf((float)hd);
+    const size_t krb = kv_row_bytes(ktype, hd), vrb = kv_row_bytes(vtype, hd);
+    const uint8_t* kb = (const uint8_t*)kc;
+    const uint8_t* vb = (const uint8_t*)vc;
+    float* att = (float*)malloc(sizeof(float) * (size_t)(n_pos > 0 ? n_pos : 1));
+    float* tmp = (float*)malloc(sizeof(float) * (size_t)hd);
+    blk_q8_0* qq = (blk_q8_0*)malloc(sizeof(blk_q8_0) * (size_t)(hd / 32));
+    for (int h = 0; h < n_heads; ++h) {
+        int kvh = h / gqa;
+        if (kvh > n_kv_heads - 1) kvh = n_kv_heads - 1;
+        const float* qh = q + (size_t)h * hd;
+        if (ktype == ORC_Q8_0) orc_quantize_row_q8_0(qh, qq, hd);
+        for (int t = 0; t < n_pos; ++t) {
+            const uint8_t* krow = kb + (size_t)t * k_stride + (size_t)kvh * krb;
+            float score = 0.0f;
+            if (ktype == ORC_Q8_0) {
+                score = orc_vec_dot_q8_0_q8_0(hd, krow, qq);
+            } else {
+                orc_fp16_to_fp32_row((const uint16_t*)krow, tmp, hd);
+                for (int i = 0; i < hd; ++i) score += qh[i] * tmp[i];
+            }
+            att[t] = score * att_scale;
+        }
+        if (n_pos > 0) orc_softmax(att, att, n_pos);
+        float* oh = out + (size_t)h * hd;
+        for (int i = 0; i < hd; ++i) oh[i] = 0.0f;
+        for (int t = 0; t < n_pos; ++t) {
+            orc_dequantize_row(vtype, vb + (size_t)t * v_stride + (size_t)kvh * vrb, tmp, hd);
+            const float a = att[t];
+            for (int i = 0; i < hd; ++i) oh[i] += a * tmp[i];
+        }
+    }
+    free(qq);
+    free(tmp);
+    free(att);
+}
+
+/* The KV shift's K re-rotation on a typed cache: each kept row is
+ * dequantized, rotated by the delta angle as in orc_kv_shift_k and stored
+ * back with the type's quantizer (llama.cpp rotates a quantized K through an
+ * fp32 copy and writes it back through the type's quantizer). */
+void orc_kv_shift_k_typed(void* kc, int ktype, size_t k_stride, int n_pos, int n_kv_heads, int hd, int delta,
+                          float theta) {
+    float* cs = (float*)malloc(sizeof(float) * (size_t)hd);
+    float* x = (float*)malloc(sizeof(float) * (size_t)hd);
+    float* y = (float*)malloc(sizeof(float) * (size_t)hd);
+    const size_t rb = kv_row_bytes(ktype, hd);
+    orc_rope_table(theta, hd, delta, 1, cs);
+    for (int t = 0; t < n_pos; ++t) {
+        for (int h = 0; h < n_kv_heads; ++h) {
+            uint8_t* row = (uint8_t*)kc + (size_t)t * k_stride + (size_t)h * rb;
+            orc_dequantize_row(ktype, row, x, hd);
+            for (int i = 0; i < hd; i += 2) {
+                const float c = cs[i], s = cs[i + 1];
+                y[i] = x[i] * c - x[i + 1] * s;
+                y[i + 1] = x[i] * s + x[i + 1] * c;
+            }
+            orc_kv_store_row(ktype, y, row, hd);
+        }
+    }
+    free(y);
+    free(x);
+    free(cs);
+}

@@ -52,10 +52,21 @@ def test_error_reporting_on_bad_arguments():
 
 def test_context_default_params():
     """llama_context_default_params' counterpart: 4096 positions, one
-    sequence, graph replay and the tensor-core prefill on."""
+    sequence, graph replay and the tensor-core prefill on, fp16 K and V
+    caches."""
     p = b2.ContextParams()
     b2.lib.b2_context_default_params(ctypes.byref(p))
     assert (p.n_ctx, p.n_seq_max, p.use_graph, p.prefill_gemm) == (4096, 1, 1, 1)
+    assert (p.type_k, p.type_v) == (b2.F16, b2.F16)
+
+
+def test_kv_row_bytes():
+    """Cache rows: fp16 values, or Q8_0 codes + block scales padded to
+    head_dim + 16 bytes; other types are refused (0)."""
+    assert b2.lib.b2_kv_row_bytes(b2.F16, 128) == 256
+    assert b2.lib.b2_kv_row_bytes(b2.Q8_0, 128) == 144
+    assert b2.lib.b2_kv_row_bytes(b2.Q8_0, 64) == 80
+    assert b2.lib.b2_kv_row_bytes(b2.Q4_K, 128) == 0
 
 
 def _write_small_llama(path):
