@@ -111,6 +111,14 @@ def _bind() -> None:
         "b2_get_logits": (_i, [_vp, ctypes.c_int32, _vp, _i64]),
         "b2_get_argmax": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32]),
         "b2_generate": (_i, [_vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp]),
+        "b2_sampler_default_params": (None, [_vp]),
+        "b2_sampler_create": (_i, [_vp, _vp, _vp]),
+        "b2_sampler_free": (_i, [_vp]),
+        "b2_sampler_reset": (_i, [_vp]),
+        "b2_sampler_accept": (_i, [_vp, ctypes.c_int32]),
+        "b2_sampler_sample": (_i, [_vp, ctypes.c_int32, _vp]),
+        "b2_sampler_sample_logits": (_i, [_vp, _vp, ctypes.c_int32, _vp]),
+        "b2_generate_sampled": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp]),
         "b2_synchronize_context": (_i, [_vp]),
         "b2_kv_clear": (_i, [_vp]),
         "b2_kv_seq_rm": (_i, [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
@@ -468,6 +476,53 @@ class Model:
         self.free()
 
 
+class SamplerParams(ctypes.Structure):
+    _fields_ = [("penalty_last_n", ctypes.c_int32), ("penalty_repeat", ctypes.c_float),
+                ("penalty_freq", ctypes.c_float), ("penalty_present", ctypes.c_float), ("top_k", ctypes.c_int32),
+                ("top_p", ctypes.c_float), ("min_p", ctypes.c_float), ("temperature", ctypes.c_float),
+                ("seed", ctypes.c_uint32)]
+
+
+class Sampler:
+    """A sampler chain on a context's GPU (Milda's rebuild_sampler chain);
+    keyword arguments override Milda's defaults."""
+
+    def __init__(self, ctx, **kw):
+        p = SamplerParams()
+        lib.b2_sampler_default_params(ctypes.byref(p))
+        for k, v in kw.items():
+            setattr(p, k, v)
+        self.params = p
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        check(lib.b2_sampler_create(ctx.h, ctypes.byref(p), ctypes.byref(h)), "sampler_create")
+        self.h = h.value
+
+    def sample(self, idx: int = -1) -> int:
+        t = ctypes.c_int32()
+        check(lib.b2_sampler_sample(self.h, idx, ctypes.byref(t)), "sampler_sample")
+        return t.value
+
+    def sample_logits(self, logits_dev, n_vocab: int) -> int:
+        t = ctypes.c_int32()
+        check(lib.b2_sampler_sample_logits(self.h, logits_dev, n_vocab, ctypes.byref(t)), "sampler_sample_logits")
+        return t.value
+
+    def accept(self, tok: int) -> None:
+        check(lib.b2_sampler_accept(self.h, tok), "sampler_accept")
+
+    def reset(self) -> None:
+        check(lib.b2_sampler_reset(self.h), "sampler_reset")
+
+    def free(self) -> None:
+        if getattr(self, "h", None):
+            lib.b2_sampler_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.free()
+
+
 class Context:
     def __init__(self, model: Model, n_ctx: int = 4096, n_seq: int = 1, use_graph: bool = True,
                  prefill_gemm: bool = True, type_k: int = F16, type_v: int = F16):
@@ -511,6 +566,18 @@ class Context:
         out = np.zeros((max(n_steps, 1), f.size), np.int32)
         rc = lib.b2_generate(self.h, ptr(f), ptr(ss) if ss is not None else None, f.size, n_steps, ptr(out))
         check(rc, "generate")
+        self.last_n = f.size
+        return out[:n_steps]
+
+    def generate_sampled(self, samplers, first, n_steps: int, seq=None) -> np.ndarray:
+        """Sampled continuation on the device (row i drawn by samplers[i]): ids [n_steps, n]."""
+        f = np.ascontiguousarray(first, np.int32).ravel()
+        ss = None if seq is None else np.ascontiguousarray(seq, np.int32)
+        arr = (ctypes.c_void_p * len(samplers))(*[s.h for s in samplers])
+        out = np.zeros((max(n_steps, 1), f.size), np.int32)
+        rc = lib.b2_generate_sampled(self.h, arr, ptr(f), ptr(ss) if ss is not None else None, f.size, n_steps,
+                                     ptr(out))
+        check(rc, "generate_sampled")
         self.last_n = f.size
         return out[:n_steps]
 

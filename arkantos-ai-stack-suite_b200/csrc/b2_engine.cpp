@@ -34,6 +34,7 @@
 #include "b2_gguf.hpp"
 #include "b2_internal.hpp"
 #include "b2_layers.hpp"
+#include "b2_sampler.hpp"
 
 namespace b2 {
 
@@ -146,6 +147,10 @@ struct b2_context {
   // graphs per (n_tok, with_logits)
   cudaGraphExec_t graphs[b2::kStepMax + 1][2] = {};
   cudaGraphExec_t gen_graphs[b2::kStepMax + 1] = {};
+  cudaGraphExec_t samp_graphs[b2::kStepMax + 1] = {};   // device loop with the sampler chain
+  // sampler chain (allocated at the first sampler on this context)
+  b2::SamplerDev** samp_d = nullptr;          // [kStepMax] the rows' samplers during a sampled loop
+  unsigned long long* samp_keys = nullptr;   // candidate keys of the selecting CTAs
   bool use_graph = true;
   b2_abort_callback abort_cb = nullptr;
   void* abort_user = nullptr;
@@ -161,12 +166,24 @@ struct b2_context {
   ~b2_context();
 };
 
+// One sampler chain (llama_sampler of Milda's chain) bound to a context:
+// its parameters and initial state on the host, its state on the context's
+// device.
+struct b2_sampler {
+  b2_context* ctx = nullptr;
+  b2::SamplerDev host;                 // parameters + the fresh state
+  b2::SamplerDev* dev = nullptr;       // device state
+  b2::SamplerDev** self = nullptr;     // device array { dev } for single-row sampling
+};
+
 b2_context::~b2_context() {
   if (model) cudaSetDevice(model->device);
   for (auto& row : graphs)
     for (auto& g : row)
       if (g) cudaGraphExecDestroy(g);
   for (auto& g : gen_graphs)
+    if (g) cudaGraphExecDestroy(g);
+  for (auto& g : samp_graphs)
     if (g) cudaGraphExecDestroy(g);
   for (size_t j = 0; j < peer_xbuf.size(); ++j)
     if (peer_xbuf[j] && peer_xbuf[j] != xbuf) cudaIpcCloseMemHandle(peer_xbuf[j]);
@@ -538,7 +555,7 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
 
 // One device step over n tokens already staged in tok_d/pos_d/seq_d.  With
 // `feed`, the step ends by writing its argmax ids back as the next tokens.
-int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
+int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false, bool sampled = false) {
   b2_model* m = c->model;
   cudaStream_t s = c->stream;
   const int d = m->n_embd, hd = m->head_dim;
@@ -713,16 +730,23 @@ int enqueue_step(b2_context* c, int n, bool with_logits, bool feed = false) {
     f.count = c->gen_count;
     f.cap = c->n_ctx;
   }
-  return launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s, f, tp ? &in_head : nullptr, c->status,
-                       c->argmax_scr);
+  if (!sampled)
+    return launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s, f, tp ? &in_head : nullptr, c->status,
+                         c->argmax_scr);
+  // the argmax (which also waits for the ranks' head shards), then the
+  // rows' sampler chains, which feed the next step
+  if ((rc = launch_argmax(c->logits, n, m->n_vocab, m->v_l, c->ids, c->top, s, GreedyFeed{}, tp ? &in_head : nullptr,
+                          c->status, c->argmax_scr)))
+    return rc;
+  return launch_sample(c->logits, n, 0, n, m->n_vocab, m->v_l, c->samp_d, c->ids, f, c->samp_keys, s);
 }
 
-int run_step(b2_context* c, int n, bool with_logits, bool feed = false) {
-  if (!c->use_graph || c->eval_cb) return enqueue_step(c, n, with_logits, feed);
-  cudaGraphExec_t& g = feed ? c->gen_graphs[n] : c->graphs[n][with_logits ? 1 : 0];
+int run_step(b2_context* c, int n, bool with_logits, bool feed = false, bool sampled = false) {
+  if (!c->use_graph || c->eval_cb) return enqueue_step(c, n, with_logits, feed, sampled);
+  cudaGraphExec_t& g = sampled ? c->samp_graphs[n] : feed ? c->gen_graphs[n] : c->graphs[n][with_logits ? 1 : 0];
   if (!g) {
     B2_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    const int rc = enqueue_step(c, n, with_logits, feed);
+    const int rc = enqueue_step(c, n, with_logits, feed, sampled);
     cudaGraph_t graph = nullptr;
     const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
     if (rc) {
@@ -935,7 +959,8 @@ int decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32
 // Greedy generation with the loop on the device: step t feeds every row the
 // argmax of step t-1 (step 0 feeds `first`), so consecutive steps are graph
 // replays with no host round trip.  The ids come back in one copy at the end.
-int generate(b2_context* c, const int32_t* first, const int32_t* seq, int n, int n_steps, int32_t* out) {
+int generate(b2_context* c, const int32_t* first, const int32_t* seq, int n, int n_steps, int32_t* out,
+             b2_sampler* const* samplers = nullptr) {
   b2_model* m = c->model;
   B2_CUDA_TRY(cudaSetDevice(m->device));
   B2_CHECK_ARG(first && out && n > 0 && n <= kStepMax && n_steps >= 0, "generate arguments");
@@ -954,6 +979,23 @@ int generate(b2_context* c, const int32_t* first, const int32_t* seq, int n, int
       return B2_ERR_INVALID;
     }
     if (c->n_past[s] + n_steps > c->n_ctx) return B2_NO_KV_SLOT;
+  }
+  if (samplers) {
+    std::vector<SamplerDev*> sp(kStepMax, nullptr);
+    for (int i = 0; i < n; ++i) {
+      if (!samplers[i] || samplers[i]->ctx != c) {
+        set_error("generate: row %d has no sampler of this context", i);
+        return B2_ERR_INVALID;
+      }
+      for (int j = 0; j < i; ++j)
+        if (samplers[j] == samplers[i]) {
+          set_error("generate: rows %d and %d share one sampler", j, i);
+          return B2_ERR_INVALID;
+        }
+      sp[i] = samplers[i]->dev;
+    }
+    B2_CUDA_TRY(cudaMemcpyAsync(c->samp_d, sp.data(), kStepMax * sizeof(SamplerDev*), cudaMemcpyHostToDevice,
+                                c->stream));
   }
   if (n_steps == 0) return B2_OK;
   const int slot = c->in_slot;
@@ -974,7 +1016,7 @@ int generate(b2_context* c, const int32_t* first, const int32_t* seq, int n, int
       rc = B2_ABORTED;
       break;
     }
-    if ((rc = run_step(c, n, true, true))) return rc;
+    if ((rc = run_step(c, n, true, true, samplers != nullptr))) return rc;
   }
   if (done > 0) {
     B2_CUDA_TRY(cudaMemcpyAsync(out, c->gen_out, (size_t)done * n * 4, cudaMemcpyDeviceToHost, c->stream));
@@ -1224,6 +1266,133 @@ int b2_generate(b2_context* c, const int32_t* first, const int32_t* seq, int32_t
       return B2_ERR_INVALID;
     }
   return generate(c, first, seq, n, n_steps, out);
+}
+
+void b2_sampler_default_params(b2_sampler_params* p) {
+  if (!p) return;
+  // Milda's configuration defaults (Milda/include/milda/engine.hpp:79-84) and
+  // its penalty window of 64 (Milda/src/engine.cpp:1354-1355)
+  p->penalty_last_n = 64;
+  p->penalty_repeat = 1.08f;
+  p->penalty_freq = 0.0f;
+  p->penalty_present = 0.0f;
+  p->top_k = 40;
+  p->top_p = 0.90f;
+  p->min_p = 0.05f;
+  p->temperature = 0.75f;
+  p->seed = 42u;
+}
+
+int b2_sampler_create(b2_context* c, const b2_sampler_params* p, b2_sampler** out) {
+  B2_CHECK_ARG(c && p && out, "sampler_create arguments");
+  *out = nullptr;
+  B2_CHECK_ARG(p->penalty_last_n >= 0 && p->penalty_last_n <= kSampRing, "penalty_last_n must be in [0, 256]");
+  B2_CHECK_ARG(p->temperature <= 0.0f || (p->top_k >= 1 && p->top_k <= kSampTopKMax),
+               "a sampling chain (temperature > 0) needs top_k in [1, 256] on the device");
+  B2_CHECK_ARG(p->penalty_repeat > 0.0f, "penalty_repeat must be positive");
+  if (c->model->n_vocab > kSampParts * kSampSlice) {
+    set_error("sampler: vocabularies of up to %d entries are sampled on the device", kSampParts * kSampSlice);
+    return B2_ERR_UNSUPPORTED;
+  }
+  B2_CUDA_TRY(cudaSetDevice(c->model->device));
+  if (!c->samp_d) {
+    int rc;
+    if ((rc = dalloc(c, &c->samp_d, kStepMax)) || (rc = dalloc(c, &c->samp_keys, sampler_scratch_keys()))) return rc;
+  }
+  b2_sampler* sm = new (std::nothrow) b2_sampler;
+  if (!sm) return B2_ERR_OOM;
+  sm->ctx = c;
+  SamplerDev& h = sm->host;
+  memset(&h, 0, sizeof h);
+  h.last_n = p->penalty_last_n;
+  h.rep = p->penalty_repeat;
+  h.freq = p->penalty_freq;
+  h.pres = p->penalty_present;
+  h.top_k = p->top_k;
+  h.top_p = p->top_p;
+  h.min_p = p->min_p;
+  h.logf_min_p = p->min_p > 0.0f ? logf(p->min_p) : 0.0f;
+  h.temp = p->temperature;
+  h.seed = p->seed;
+  sampler_init_state(&h);
+  if (cudaMalloc(&sm->dev, sizeof(SamplerDev)) != cudaSuccess ||
+      cudaMalloc(&sm->self, sizeof(SamplerDev*)) != cudaSuccess) {
+    cudaFree(sm->dev);
+    delete sm;
+    set_error("sampler_create: device allocation failed");
+    return B2_ERR_OOM;
+  }
+  B2_CUDA_TRY(cudaMemcpyAsync(sm->dev, &h, sizeof h, cudaMemcpyHostToDevice, c->stream));
+  B2_CUDA_TRY(cudaMemcpyAsync(sm->self, &sm->dev, sizeof(SamplerDev*), cudaMemcpyHostToDevice, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  *out = sm;
+  return B2_OK;
+}
+
+int b2_sampler_free(b2_sampler* sm) {
+  if (!sm) return B2_OK;
+  cudaSetDevice(sm->ctx->model->device);
+  cudaStreamSynchronize(sm->ctx->stream);
+  cudaFree(sm->dev);
+  cudaFree(sm->self);
+  delete sm;
+  return B2_OK;
+}
+
+int b2_sampler_reset(b2_sampler* sm) {
+  B2_CHECK_ARG(sm, "sampler");
+  B2_CUDA_TRY(cudaSetDevice(sm->ctx->model->device));
+  SamplerDev& h = sm->host;
+  sampler_init_state(&h);
+  B2_CUDA_TRY(cudaMemcpyAsync(sm->dev, &h, sizeof h, cudaMemcpyHostToDevice, sm->ctx->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(sm->ctx->stream));
+  return B2_OK;
+}
+
+int b2_sampler_accept(b2_sampler* sm, int32_t token) {
+  B2_CHECK_ARG(sm && token >= 0 && token < kSampParts * kSampSlice, "sampler_accept arguments");
+  B2_CUDA_TRY(cudaSetDevice(sm->ctx->model->device));
+  return launch_sampler_accept(sm->dev, token, sm->ctx->stream);
+}
+
+int b2_sampler_sample(b2_sampler* sm, int32_t idx, int32_t* token) {
+  B2_CHECK_ARG(sm && token, "sampler_sample arguments");
+  b2_context* c = sm->ctx;
+  B2_CHECK_ARG(c->last_logits, "the last decode computed no logits");
+  if (idx < 0) idx += c->last_n;
+  B2_CHECK_ARG(idx >= 0 && idx < c->last_n, "logits row out of range");
+  B2_CUDA_TRY(cudaSetDevice(c->model->device));
+  const b2_model* m = c->model;
+  int rc = launch_sample(c->logits, c->last_n, idx, 1, m->n_vocab, m->v_l, sm->self, c->ids, GreedyFeed{},
+                         c->samp_keys, c->stream);
+  if (rc) return rc;
+  B2_CUDA_TRY(cudaMemcpyAsync(c->res_h, c->ids + idx, 4, cudaMemcpyDeviceToHost, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  *token = c->res_h[0];
+  return B2_OK;
+}
+
+int b2_sampler_sample_logits(b2_sampler* sm, const float* logits, int32_t n_vocab, int32_t* token) {
+  B2_CHECK_ARG(sm && logits && token && n_vocab > 0, "sampler_sample_logits arguments");
+  b2_context* c = sm->ctx;
+  B2_CUDA_TRY(cudaSetDevice(c->model->device));
+  int rc = launch_sample(logits, 1, 0, 1, n_vocab, n_vocab, sm->self, c->ids, GreedyFeed{}, c->samp_keys, c->stream);
+  if (rc) return rc;
+  B2_CUDA_TRY(cudaMemcpyAsync(c->res_h, c->ids, 4, cudaMemcpyDeviceToHost, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  *token = c->res_h[0];
+  return B2_OK;
+}
+
+int b2_generate_sampled(b2_context* c, b2_sampler* const* samplers, const int32_t* first, const int32_t* seq,
+                        int32_t n, int32_t n_steps, int32_t* out) {
+  B2_CHECK_ARG(c && samplers, "generate_sampled arguments");
+  for (const auto& p : pending_for(c))
+    if (p.p0 >= 0) {
+      set_error("generate: a KV removal is waiting for its position shift (b2_kv_seq_add)");
+      return B2_ERR_INVALID;
+    }
+  return generate(c, first, seq, n, n_steps, out, samplers);
 }
 
 int b2_get_logits(b2_context* c, int32_t i, float* out, int64_t n) {

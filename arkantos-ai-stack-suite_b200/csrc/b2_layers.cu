@@ -341,28 +341,77 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int n_head, int n_
 // Rotates K rows of logical positions [p_begin, p_end) of sequence s (slots
 // computed with the state before the shift) by the angle table of the
 // position delta, in place: value -> fp32 -> rotate -> the cache type's
-// storage (fp16 RNE, or Q8_0 requantized per block).  One warp per 32-value
-// block.  The table comes by value (no upload, so the call is
-// stream-ordered and capturable).
+// storage (fp16 RNE, or Q8_0 requantized per block as
+// ref_quantize_row_q8_0).  Each thread takes 4 consecutive values (two
+// rotation pairs): one 8-byte fp16 load and store, or one 4-byte code word,
+// with the 8 threads of a 32-value block sharing its maximum by shuffles.
+// The table comes by value (no upload, so the call is stream-ordered and
+// capturable).
 template <int KT>
 __global__ void kv_shift_kernel(uint8_t* __restrict__ kc, int n_kv, int hd, int s, KvSeqState stt, int cap, int p_begin,
                                 int p_end, RotTable rt) {
   __shared__ float cs[2 * kRotPairs];
   for (int i = threadIdx.x; i < hd; i += blockDim.x) cs[i] = rt.cs[i];
   __syncthreads();
-  const int nb = hd / 32, lane = threadIdx.x & 31;
-  const int64_t total = (int64_t)(p_end - p_begin) * n_kv * nb;
-  const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t n_w = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t w = w0; w < total; w += n_w) {
-    const int bi = (int)(w % nb);
-    const int kh = (int)((w / nb) % n_kv);
-    const int p = p_begin + (int)(w / ((int64_t)nb * n_kv));
-    uint8_t* row = kv_row(kc, KT, hd, s, n_kv, kh, cap, kv_slot(stt, p, cap));
-    const int i = bi * 32 + lane;
-    const float y = rotate_lane(kv_load<KT>(row, hd, i), i, cs);
-    __syncwarp();
-    kv_store<KT>(row, hd, i, y);
+  const int qpr = hd / 4;                               // threads per row (16 or 32: whole 8-lane groups)
+  const int total = (p_end - p_begin) * n_kv * qpr;     // multiple of 16
+  const int lane = threadIdx.x & 31;
+  const int stride = gridDim.x * blockDim.x;
+  // warp-uniform trip count: every lane of a warp runs every trip (shuffles)
+  for (int base = (blockIdx.x * blockDim.x + threadIdx.x) & ~31; base < total; base += stride) {
+    const int q = base + lane;
+    const bool on = q < total;
+    const int row = on ? q / qpr : 0, i = (q - row * qpr) * 4;
+    const int kh = row % n_kv, p = p_begin + row / n_kv;
+    uint8_t* rp = kv_row(kc, KT, hd, s, n_kv, kh, cap, on ? kv_slot(stt, p, cap) : 0);
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (KT == B2_Q8_0) {
+      if (on) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(rp + i);
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(rp + hd + 2 * (i >> 5)));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = __fmul_rn((float)(int8_t)(w >> (8 * k)), d);
+      }
+    } else if (on) {
+      const uint2 w = *reinterpret_cast<const uint2*>(rp + 2 * i);
+      x[0] = h2f((uint16_t)(w.x & 0xFFFFu));
+      x[1] = h2f((uint16_t)(w.x >> 16));
+      x[2] = h2f((uint16_t)(w.y & 0xFFFFu));
+      x[3] = h2f((uint16_t)(w.y >> 16));
+    }
+    float y[4];
+#pragma unroll
+    for (int k = 0; k < 4; k += 2) {
+      const float c = cs[(i + k) & (2 * kRotPairs - 1)], sn = cs[(i + k + 1) & (2 * kRotPairs - 1)];
+      y[k] = __fsub_rn(__fmul_rn(x[k], c), __fmul_rn(x[k + 1], sn));
+      y[k + 1] = __fadd_rn(__fmul_rn(x[k], sn), __fmul_rn(x[k + 1], c));
+    }
+    if constexpr (KT == B2_Q8_0) {
+      // the block's 32 values sit on 8 consecutive lanes
+      float amax = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float d = __fmul_rn(amax, 1.0f / 127.0f);
+      const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+      uint32_t w = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float sc = __fmul_rn(y[k], id);
+        const float t = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
+        int c = __float2int_rz(t);
+        c = c < -127 ? -127 : (c > 127 ? 127 : c);
+        w |= (uint32_t)(uint8_t)(int8_t)c << (8 * k);
+      }
+      if (on) {
+        *reinterpret_cast<uint32_t*>(rp + i) = w;
+        if ((i & 31) == 0) *reinterpret_cast<uint16_t*>(rp + hd + 2 * (i >> 5)) = f2h_rn(d);
+      }
+    } else if (on) {
+      uint2 w;
+      w.x = (uint32_t)f2h_rn(y[0]) | ((uint32_t)f2h_rn(y[1]) << 16);
+      w.y = (uint32_t)f2h_rn(y[2]) | ((uint32_t)f2h_rn(y[3]) << 16);
+      *reinterpret_cast<uint2*>(rp + 2 * i) = w;
+    }
   }
 }
 
@@ -562,8 +611,9 @@ int launch_kv_shift(void* kc, int kt, int n_kv, int hd, int seq, const KvSeqStat
   B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
   B2_CHECK_ARG(hd % 32 == 0 && kv_type_ok(kt), "KV shift: head_dim % 32 and an F16 or Q8_0 cache");
   if (p_end <= p_begin) return B2_OK;
-  const int64_t warps = (int64_t)(p_end - p_begin) * n_kv * (hd / 32);
-  const int grid = (int)std::min<int64_t>((warps + 7) / 8, 4 * kSMs);
+  const int64_t quads = (int64_t)(p_end - p_begin) * n_kv * (hd / 4);
+  B2_CHECK_ARG(quads < (int64_t)1 << 30, "KV shift range too large");
+  const int grid = (int)std::min<int64_t>((quads + 255) / 256, 4 * kSMs);
   uint8_t* k8 = static_cast<uint8_t*>(kc);
   if (kt == B2_Q8_0) kv_shift_kernel<B2_Q8_0><<<grid, 256, 0, s>>>(k8, n_kv, hd, seq, st, cap, p_begin, p_end, cs);
   else kv_shift_kernel<B2_F16><<<grid, 256, 0, s>>>(k8, n_kv, hd, seq, st, cap, p_begin, p_end, cs);

@@ -924,15 +924,17 @@ def run_attn_ours(args, dist, rank, world, local):
     import b2gguf as b2
     b2.check(b2.lib.b2_set_device(local), "set_device")
     batches = (1, 4, 16) if args.attn_batch is None else (args.attn_batch,)
-    res = [attn_measure(b2, n, args.steps) for n in batches]
+    res = [attn_measure(b2, n, args.steps) for n in batches] if args.attn_kv != "q8_0" else []
     # Milda's default cache type (Q8_0 K and V), the same batches
-    res_q8 = [attn_measure(b2, n, args.steps, b2.Q8_0) for n in batches]
+    res_q8 = [attn_measure(b2, n, args.steps, b2.Q8_0) for n in batches] if args.attn_kv != "f16" else []
     peaks = measured_peaks()
-    big = res[-1]
-    return {"metric": "decode attention HBM GB/s (32 q / 8 kv heads, hd 128, ctx 4096, fp16 KV)",
+    big = (res or res_q8)[-1]
+    kvn = "fp16" if big["kv_type"] == "f16" else "Q8_0"
+    return {"metric": f"decode attention HBM GB/s (32 q / 8 kv heads, hd 128, ctx 4096, {kvn} KV)",
             "value": round(big["gbs"] * world, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 2,
             "ms_per_step": big["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp16 KV, fp32 math", "data": "synthetic: q, k, v N(0,1) fp16, seed 4",
+            "dtype": f"{kvn} KV, fp32 math",
+            "data": "synthetic, seed 4: q N(0,1); fp16 K, V N(0,1); Q8_0 K, V uniform codes, block scale 0.01",
             "config": {"workload": f"attn_decode batch {big['batch']}, ctx 4096 (config 3); all batches in 'batches'",
                        "l2": "inputs larger than L2 (rotating KV copies)"},
             "roofline": {"bound": "hbm", "achieved": round(big["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -1117,6 +1119,8 @@ def main():
     ap.add_argument("--keep-model", action="store_true", help="keep the synthetic GGUF file after the run")
     ap.add_argument("--skip-1b", action="store_true", help="decode_8b_q4k: leave out the 1.1B Q4_0 (config 4) line")
     ap.add_argument("--attn-batch", type=int, default=None, help="attn: one batch size (default 1, 4 and 16)")
+    ap.add_argument("--attn-kv", default="both", choices=["both", "f16", "q8_0"],
+                    help="attn: KV cache types to time (default both)")
     ap.add_argument("--profile-range", action="store_true",
                     help="open the profiler range around the timed decode steps only")
     ap.add_argument("--qtype", default="q4_k", choices=sorted(TYPE_NAMES), help="gemv_op weight type")

@@ -419,6 +419,69 @@ B2_API int b2_generate(b2_context* c, const int32_t* first, const int32_t* seq, 
                        int32_t* out);
 B2_API int b2_synchronize_context(b2_context* c);
 
+/* ------------------------------------------------------------------------ */
+/* Sampler chain on the device                                               */
+/* ------------------------------------------------------------------------ */
+
+/* The chain Milda's rebuild_sampler builds (Milda/src/engine.cpp:1321-1384)
+ * from llama.cpp's samplers, with its state (penalty window, mt19937) in
+ * device memory:
+ *   penalties (llama_sampler_init_penalties; when penalty_last_n > 0 and a
+ *   penalty is set) over the last penalty_last_n accepted tokens: a logit
+ *   l <= 0 becomes l·repeat, else l/repeat; then l − (count·freq +
+ *   (count > 0)·present);
+ *   temperature <= 0: greedy (the first largest logit);
+ *   else top_k (k largest, in descending order; equal logits by lower id),
+ *   top_p (softmax with the C library's expf, the shortest prefix whose
+ *   running probability reaches p; off for p <= 0 or >= 1), min_p (logits >=
+ *   the largest + logf(p); off for p <= 0), temperature (l/t) and dist
+ *   (softmax, then std::discrete_distribution over the probabilities in
+ *   candidate order with a std::mt19937 seeded by `seed`, as the GNU C++
+ *   library draws it: u = (r1 + r2·2^32)/2^64, the first normalized running
+ *   sum, in double, not below u).
+ * Sampling accepts the sampled token (as llama_sampler_sample does);
+ * b2_sampler_accept adds one more (Milda accepts again, :2029).
+ * Device limits: penalty_last_n <= 256; with temperature > 0, 1 <= top_k <=
+ * 256; vocabularies up to 131072 entries (B2_ERR_UNSUPPORTED otherwise). */
+typedef struct b2_sampler b2_sampler;
+typedef struct b2_sampler_params {
+    int32_t  penalty_last_n;   /* 0: no penalties */
+    float    penalty_repeat;   /* 1: off */
+    float    penalty_freq;     /* 0: off */
+    float    penalty_present;  /* 0: off */
+    int32_t  top_k;
+    float    top_p;
+    float    min_p;
+    float    temperature;      /* <= 0: greedy */
+    uint32_t seed;             /* llama_sampler_init_dist */
+} b2_sampler_params;
+/* Milda's defaults (Milda/include/milda/engine.hpp:79-84, window 64):
+ * penalty 1.08 over 64 tokens, top_k 40, top_p 0.90, min_p 0.05,
+ * temperature 0.75, seed 42. */
+B2_API void b2_sampler_default_params(b2_sampler_params* p);
+/* llama_sampler_chain_init + _add (rebuild_sampler): a chain whose state
+ * lives on the context's GPU and whose calls run on the context's stream. */
+B2_API int  b2_sampler_create(b2_context* c, const b2_sampler_params* p, b2_sampler** out);
+B2_API int  b2_sampler_free(b2_sampler* s);                   /* llama_sampler_free   */
+/* llama_sampler_reset (Milda/src/engine.cpp:1693, 1710, 1839): empty window,
+ * generator re-seeded. */
+B2_API int  b2_sampler_reset(b2_sampler* s);
+/* llama_sampler_accept; token in [0, 131072). */
+B2_API int  b2_sampler_accept(b2_sampler* s, int32_t token);
+/* llama_sampler_sample(s, ctx, idx) (Milda/src/engine.cpp:1970): samples
+ * logits row idx (negative: from the end) of the context's last decode on
+ * the device and accepts the token; only the token comes back to the host. */
+B2_API int  b2_sampler_sample(b2_sampler* s, int32_t idx, int32_t* token);
+/* The same draw over a device array of n_vocab fp32 logits (any vocabulary
+ * up to 131072), on the sampler's context stream. */
+B2_API int  b2_sampler_sample_logits(b2_sampler* s, const float* logits, int32_t n_vocab, int32_t* token);
+/* b2_generate with row i drawn by samplers[i] (distinct samplers of this
+ * context) instead of the greedy argmax: the device-resident form of Milda's
+ * sampled turn loop, no logits leave the device.  Row i's step-t token lands
+ * in out[t*n + i]. */
+B2_API int  b2_generate_sampled(b2_context* c, b2_sampler* const* samplers, const int32_t* first,
+                                const int32_t* seq, int32_t n, int32_t n_steps, int32_t* out);
+
 /* KV cache: llama_memory_clear / seq_rm / seq_add / seq_pos_max
  * (Milda/src/engine.cpp:1650-1658, 1686, 2125-2148).  seq_rm of a suffix
  * truncates; seq_rm of [p0,p1) followed by seq_add(p1, -1, -(p1-p0)) is

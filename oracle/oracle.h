@@ -115,6 +115,23 @@ void orc_attn_decode_typed(const float* q, const void* kc, int ktype, size_t k_s
 void orc_kv_shift_k_typed(void* kc, int ktype, size_t k_stride, int n_pos, int n_kv_heads, int hd, int delta,
                           float theta);
 
+/* ---- Sampler chain (oracle_sampler.c) ---- */
+typedef struct orc_sampler orc_sampler;
+/* Milda's chain (rebuild_sampler): penalties, then greedy (temp <= 0) or
+ * top_k (<= 0: all), top_p, min_p, temp, dist(seed). */
+orc_sampler* orc_sampler_new(int last_n, float rep, float freq, float pres, int top_k, float top_p, float min_p,
+                             float temp, uint32_t seed);
+void    orc_sampler_free(orc_sampler* s);
+void    orc_sampler_reset(orc_sampler* s);
+void    orc_sampler_accept(orc_sampler* s, int32_t tok);
+/* llama_sampler_sample over one logits row; accepts the token. */
+int32_t orc_sampler_sample(orc_sampler* s, const float* logits, int n_vocab);
+/* std::mt19937(seed)'s first n outputs. */
+void    orc_mt19937(uint32_t seed, uint32_t* out, int n);
+/* std::discrete_distribution<int>(p, p + n) drawn once with the sampler's
+ * generator (GNU C++ library arithmetic). */
+int     orc_discrete_draw(orc_sampler* s, const float* p, int n);
+
 /* ---- Device-order arithmetic (the GPU kernels' evaluation order) ---- */
 float orc_expf_dev(float x);
 void  orc_silu_mul_dev(float* hb, const float* hb2, int n);

@@ -65,6 +65,13 @@ def _load() -> ctypes.CDLL:
                                          _vp]),
         "orc_kv_shift_k_typed": (None, [_vp, _i, ctypes.c_size_t, _i, _i, _i, _i, _f]),
         "orc_model_set_kv_types": (_i, [_vp, _i, _i]),
+        "orc_sampler_new": (_vp, [_i, _f, _f, _f, _i, _f, _f, _f, ctypes.c_uint32]),
+        "orc_sampler_free": (None, [_vp]),
+        "orc_sampler_reset": (None, [_vp]),
+        "orc_sampler_accept": (None, [_vp, ctypes.c_int32]),
+        "orc_sampler_sample": (ctypes.c_int32, [_vp, _vp, _i]),
+        "orc_mt19937": (None, [ctypes.c_uint32, _vp, _i]),
+        "orc_discrete_draw": (_i, [_vp, _vp, _i]),
         "orc_model_open": (_vp, [ctypes.c_char_p]),
         "orc_model_from_memory": (_vp, [_vp, ctypes.c_size_t]),
         "orc_model_free": (None, [_vp]),
@@ -292,6 +299,42 @@ def kv_shift_k_typed(kc: np.ndarray, ktype: int, n_pos: int, n_kv: int, hd: int,
     kc = np.array(kc, np.uint8, copy=True, order="C").reshape(n_pos, -1)
     lib.orc_kv_shift_k_typed(_p(kc), ktype, kc.shape[1], n_pos, n_kv, hd, delta, theta)
     return kc
+
+
+def mt19937(seed: int, n: int) -> np.ndarray:
+    out = np.zeros(n, np.uint32)
+    lib.orc_mt19937(seed, _p(out), n)
+    return out
+
+
+class Sampler:
+    """Milda's sampler chain over llama.cpp's samplers (orc_sampler)."""
+
+    def __init__(self, last_n=64, repeat=1.08, freq=0.0, present=0.0, top_k=40, top_p=0.9, min_p=0.05,
+                 temperature=0.75, seed=42):
+        self.h = lib.orc_sampler_new(last_n, repeat, freq, present, top_k, top_p, min_p, temperature, seed)
+        if not self.h:
+            raise ValueError("oracle sampler parameters")
+
+    def sample(self, logits: np.ndarray) -> int:
+        x = np.ascontiguousarray(logits, np.float32)
+        return int(lib.orc_sampler_sample(self.h, _p(x), x.size))
+
+    def accept(self, tok: int) -> None:
+        lib.orc_sampler_accept(self.h, tok)
+
+    def reset(self) -> None:
+        lib.orc_sampler_reset(self.h)
+
+    def draw(self, p: np.ndarray) -> int:
+        """One std::discrete_distribution draw over weights p."""
+        x = np.ascontiguousarray(p, np.float32)
+        return int(lib.orc_discrete_draw(self.h, _p(x), x.size))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.orc_sampler_free(self.h)
+            self.h = None
 
 
 class Model:
