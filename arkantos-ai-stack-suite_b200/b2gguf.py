@@ -82,6 +82,10 @@ def _bind() -> None:
         "b2_gemv": (_i, [_vp, _vp, _i, _vp, _vp]),
         "b2_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _sz, _vp, _vp]),
         "b2_gemv_multi": (_i, [_vp, _i, _vp, _i, _vp, _vp]),
+        "b2_moe_route": (_i, [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _vp, _vp, _vp]),
+        "b2_moe_gemv": (_i, [_vp, ctypes.c_int32, _vp, ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_int32, _vp,
+                             _vp]),
+        "b2_moe_combine": (_i, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _vp, _vp]),
         "b2_gemm_workspace_bytes": (_i, [_vp, _i, _vp]),
         "b2_gemm_host": (_i, [_vp, _vp, _i, _vp]),
         "b2_gemv_host": (_i, [_vp, _vp, _i, _vp]),

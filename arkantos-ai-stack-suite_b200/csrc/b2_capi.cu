@@ -316,6 +316,64 @@ int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, void* stre
   return B2_OK;
 }
 
+int b2_moe_route(const float* logits, int32_t n_tok, int32_t n_expert, int32_t n_used, int32_t norm_weights,
+                 int32_t* ids, float* weights, void* stream) {
+  return launch_moe_route(logits, n_tok, n_expert, n_used, norm_weights, ids, weights, as_stream(stream));
+}
+
+int b2_moe_gemv(const b2_qmatrix* experts, int32_t n_expert, const float* x, int32_t x_per_expert, int32_t n_tok,
+                const int32_t* ids, int32_t n_used, float* y, void* stream) {
+  B2_CHECK_ARG(experts && x && ids && y && n_expert >= 1 && n_tok >= 1 && n_used >= 1 && n_used <= 64,
+               "moe_gemv arguments (1 <= n_used <= 64)");
+  const QMatrix& st = experts->m;
+  B2_CHECK_ARG(st.n_rows % n_expert == 0 && (st.n_rows / n_expert) % 8 == 0,
+               "moe_gemv: the stack holds n_expert matrices of a multiple of 8 rows each");
+  // expert 0 of the stack; expert e is e whole tile runs further
+  QMatrix e0 = st;
+  e0.n_rows = st.n_rows / n_expert;
+  e0.n_tiles = e0.n_rows / 8;
+  e0.owns = false;
+  GemvArgs a = {};
+  a.w = &e0;
+  a.x_stride = st.k;
+  a.n_tok = 1;
+  a.y_stride = e0.n_rows;
+  a.epilogue = EPI_STORE;
+  a.n_mat = n_used;
+  a.n_expert = n_expert;
+  a.mat_stride = e0.n_tiles * e0.tile_bytes;
+  a.y_mat_stride = e0.n_rows;
+  cudaStream_t s = as_stream(stream);
+  const bool img = gemv_needs_image(e0, 1);
+  if (img) B2_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&a.act_img), gemv_act_image_bytes(e0, 1), s));
+  int rc = B2_OK;
+  // One launch per token over its experts; with per-expert inputs each
+  // expert's CTAs quantize their own input (inputs of up to 8192 values),
+  // else one launch per (token, expert).
+  const bool split = x_per_expert && img;
+  const int per = split ? 1 : n_used;
+  if (x_per_expert && !img) a.x_mat_stride = st.k;
+  a.n_mat = per;
+  for (int t = 0; t < n_tok && rc == B2_OK; ++t)
+    for (int j = 0; j < n_used && rc == B2_OK; j += per) {
+      a.x = x + ((int64_t)t * (x_per_expert ? n_used : 1) + (x_per_expert ? j : 0)) * st.k;
+      a.mat_ids = ids + (int64_t)t * n_used + j;
+      a.y = y + ((int64_t)t * n_used + j) * e0.n_rows;
+      rc = launch_gemv(a, s);
+    }
+  if (img) {
+    const cudaError_t e = cudaFreeAsync(a.act_img, s);
+    if (rc) return rc;
+    B2_CUDA_TRY(e);
+  }
+  return rc;
+}
+
+int b2_moe_combine(const float* y, const float* weights, int32_t n_tok, int32_t n_used, int32_t n, float* out,
+                   void* stream) {
+  return launch_moe_combine(y, weights, n_tok, n_used, n, out, as_stream(stream));
+}
+
 int b2_gemm_workspace_bytes(const b2_qmatrix* w, int n_tok, size_t* bytes) {
   B2_CHECK_ARG(w && bytes && n_tok >= 1, "gemm_workspace_bytes arguments");
   *bytes = gemm_act_image_bytes(w->m, n_tok);

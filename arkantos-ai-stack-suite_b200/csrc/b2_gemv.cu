@@ -94,7 +94,29 @@ struct GemvP {
   int64_t tpm;             // tiles per matrix
   const uint8_t* wl[kMaxMat];
   float* yl[kMaxMat];
+  // Grouped experts (mixture of experts): matrix i of the launch is expert
+  // mat_ids[i] (device ids, read after the grid dependency) of a stack whose
+  // experts lie mat_stride bytes apart from wl[0]; its output is yl[0] +
+  // i·y_mat_stride.  Null: the host lists above.
+  const int32_t* mat_ids;
+  int n_expert;
+  int64_t mat_stride, y_mat_stride;
+  // Per-matrix inputs (grouped experts): matrix i reads x + i·x_mat_stride;
+  // the CTAs split into n_mat equal sets, set i over matrix i's tiles only,
+  // so each CTA quantizes the one input its items need.  0: one shared x.
+  int64_t x_mat_stride;
 };
+
+// Weights and output of matrix mi of the launch.  Expert ids outside
+// [0, n_expert) are clamped (the copies stay inside the stack).
+__device__ __forceinline__ const uint8_t* mat_weights(const GemvP& p, int64_t mi) {
+  if (!p.mat_ids) return p.wl[mi];
+  const int e = min(max(__ldg(p.mat_ids + mi), 0), p.n_expert - 1);
+  return p.wl[0] + (int64_t)e * p.mat_stride;
+}
+__device__ __forceinline__ float* mat_out(const GemvP& p, int64_t mi) {
+  return p.mat_ids ? p.yl[0] + mi * p.y_mat_stride : p.yl[mi];
+}
 
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
@@ -625,7 +647,7 @@ __device__ __forceinline__ void copy_part(const GemvP& p, int64_t item, int u0, 
     const int64_t mi = p.n_mat > 1 ? item / p.tpm : 0;
     const int64_t tl = item - mi * p.tpm;
     mbar_arrive_expect_tx(bar, bytes);
-    bulk_g2s(dst, p.wl[mi] + tl * p.tile_bytes + (int64_t)u0 * p.slot_bytes, bytes, bar);
+    bulk_g2s(dst, mat_weights(p, mi) + tl * p.tile_bytes + (int64_t)u0 * p.slot_bytes, bytes, bar);
   }
 }
 
@@ -796,9 +818,17 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
   __syncthreads();
   pdl_launch_dependents();
 
-  // This CTA's items (contiguous, balanced).
+  // This CTA's items (contiguous, balanced; with per-matrix inputs, within
+  // its matrix).
   const int64_t n_items = MODE == 3 ? (p.tpm + 1) / 2 : p.tpm * p.n_mat;
-  const int64_t t0 = n_items * blockIdx.x / gridDim.x, t1 = n_items * (blockIdx.x + 1) / gridDim.x;
+  int64_t t0 = n_items * blockIdx.x / gridDim.x, t1 = n_items * (blockIdx.x + 1) / gridDim.x;
+  const float* xin = p.x;
+  if (p.x_mat_stride) {
+    const int cpm = gridDim.x / p.n_mat, mi = blockIdx.x / cpm, lc = blockIdx.x - mi * cpm;
+    t0 = mi * p.tpm + p.tpm * lc / cpm;
+    t1 = mi * p.tpm + p.tpm * (lc + 1) / cpm;
+    xin = p.x + mi * p.x_mat_stride;
+  }
   // KS: the group's one item; otherwise the warp's items, every nw-th.
   const int64_t item0 = t0 + (KS ? grp : warp);
   const int64_t my_items = KS ? (grp < R && item0 < t1 ? 1 : 0) : (item0 < t1 ? (t1 - item0 + nw - 1) / nw : 0);
@@ -806,8 +836,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
   const int cps = KS ? p.Ug / p.U : 1;               // chunks per group stage
   const int n_gst = KS ? (p.nu + p.Ug - 1) / p.Ug : 0;
   const int64_t n_stages_total = KS ? 0 : my_items * p.n_ch;
-  // Weights do not depend on the previous kernel: fill the ring now, one
-  // stage per lane (two lanes per stage for pairs).
+  // Weights do not depend on the previous kernel (except which experts a
+  // grouped launch reads): fill the ring now, one stage per lane (two lanes
+  // per stage for pairs).
+  if (p.mat_ids) pdl_wait();
   int64_t issued = 0;   // whole items: stages issued so far (every lane keeps the count)
   {
     const int st_lane = lane / p.ipt, part = lane - st_lane * p.ipt;
@@ -839,7 +871,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
     ai.n_act_tok = p.n_tok;
     ai.off_dx = p.off_dx;
     ai.off_bs = p.off_bs;
-    quantize_image(p.x, p.x_stride, p.n_tok, ai, threadIdx.x, blockDim.x);
+    quantize_image(xin, p.x_stride, p.n_tok, ai, threadIdx.x, blockDim.x);
     __syncthreads();
   }
   ok = __all_sync(0xffffffffu, ok);
@@ -851,7 +883,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
     const int64_t item = item0 + it * nw;   // KS: one item
     const int64_t mi = p.n_mat > 1 ? item / p.tpm : 0;
     const int64_t tl = item - mi * p.tpm;
-    float* y = p.yl[mi];
+    float* y = mat_out(p, mi);
     if constexpr (MODE == 3) {
       const int g = lane >> 2, q = lane & 3;   // rows g of tiles 2·item and 2·item+1, tokens 2q and 2q+1
       const PairLane PL = pair_lane(p, act, g, q);
@@ -1199,7 +1231,21 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   }
   GemvP p = {};
   p.n_mat = a.n_mat;
-  if (a.n_mat == 1) {
+  if (a.mat_ids) {
+    B2_CHECK_ARG(a.n_mat >= 1 && a.n_mat <= kMaxMat && a.n_expert >= 1 && a.mat_stride > 0,
+                 "grouped-expert GEMV: 1..64 matrices");
+    B2_CHECK_ARG(a.n_tok <= kDp4aMaxTok && a.epilogue == EPI_STORE && !(a.peer && a.peer->n > 0) && !a.image_ready,
+                 "grouped-expert GEMV: 1-2 tokens, plain store");
+    p.wl[0] = w.data;
+    p.yl[0] = a.y;
+    p.mat_ids = a.mat_ids;
+    p.n_expert = a.n_expert;
+    p.mat_stride = a.mat_stride;
+    p.y_mat_stride = a.y_mat_stride;
+    p.x_mat_stride = a.x_mat_stride;
+    B2_CHECK_ARG(a.x_mat_stride == 0 || !gemv_needs_image(w, a.n_tok),
+                 "grouped-expert GEMV: per-expert inputs of at most 8192 values");
+  } else if (a.n_mat == 1) {
     p.wl[0] = w.data;
     p.yl[0] = a.y;
   } else {
@@ -1261,8 +1307,13 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   const bool pairs = a.n_tok > kDp4aMaxTok;
   p.ipt = pairs ? 2 : 1;
   const int64_t n_items = pairs ? (w.n_tiles + 1) / 2 : p.tpm * p.n_mat;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, n_items));
-  const int64_t per_cta = (n_items + grid - 1) / grid;
+  int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, n_items));
+  int64_t per_cta = (n_items + grid - 1) / grid;
+  if (p.x_mat_stride) {   // n_mat sets of CTAs, each over one matrix's tiles
+    const int cpm = (int)std::max<int64_t>(1, std::min<int64_t>(sms / p.n_mat, p.tpm));
+    grid = cpm * p.n_mat;
+    per_cta = (p.tpm + cpm - 1) / cpm;
+  }
   const int gran = pairs ? 1 : 4;   // units that one step of the fold takes
   int S = 1, nw, U = 0;
   if (per_cta <= kKsMaxItems) {

@@ -286,6 +286,13 @@ struct GemvArgs {
   int n_mat = 1;
   const QMatrix* const* wlist = nullptr;
   float* const* ylist = nullptr;
+  // Grouped experts (1-2 tokens, plain store): matrix i is expert mat_ids[i]
+  // (device) of a stack of n_expert matrices shaped like w, mat_stride bytes
+  // apart from w->data; its output is y + i·y_mat_stride.
+  const int32_t* mat_ids = nullptr;
+  int n_expert = 0;
+  int64_t mat_stride = 0, y_mat_stride = 0;
+  int64_t x_mat_stride = 0;   // matrix i reads x + i·x_mat_stride (0: all read x)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t s);
 size_t gemv_act_image_bytes(const QMatrix& w, int n_tok);

@@ -52,6 +52,10 @@ int launch_kv_shift(void* kc, int kt, int n_kv, int hd, int seq, const KvSeqStat
                     const RotTable& cs, cudaStream_t s);
 int launch_kv_compact(void* kc, int kt, void* vc, int vt, int n_kv, int hd, int seq, const KvSeqState& st, int cap,
                       int dst0, int src0, int n, const RotTable& cs, cudaStream_t s);
+// Mixture-of-experts routing and combination (b2_moe.cu).
+int launch_moe_route(const float* logits, int n_tok, int n_expert, int n_used, int norm, int32_t* ids, float* weights,
+                     cudaStream_t s);
+int launch_moe_combine(const float* y, const float* w, int n_tok, int n_used, int n, float* out, cudaStream_t s);
 // Device-side greedy loop: argmax ids become the next step's tokens.
 struct GreedyFeed {
   int32_t* tok = nullptr;    // [n_tok] next step's tokens (null: no feed)

@@ -1099,13 +1099,93 @@ def run_gemv_op(args, dist, rank, world, local):
             "gpu_launches": args.steps}
 
 
+# MoE FFN layers of the MoE GGUFs the engines load (their ffn_*_exps tensors):
+# name -> (n_embd, expert FFN, experts, experts used)
+MOE_SHAPES = {"qwen3_moe_30b_a3b": (2048, 768, 128, 8), "mixtral_8x7b": (4096, 14336, 8, 2)}
+
+
+def moe_measure(b2, name: str, steps: int) -> dict:
+    """One token through one routed FFN layer, batch 1 (the decode case):
+    router GEMV (Q8_0), routing, gate and up grouped expert GEMVs (Q4_K), the
+    down grouped GEMV over per-expert inputs, and the weighted combination;
+    CUDA events over a graph of `steps` tokens.  Each token has its own
+    input (its own experts), and the layer's expert stacks are rotated over
+    copies larger than L2.  (The SiLU·mul between up and down is left out:
+    the down GEMV reads the gate outputs, same bytes.)"""
+    d, ff, ne, nu = MOE_SHAPES[name]
+    stack_bytes = 3 * ne * ff * (d // 256) * 144
+    copies = max(2, -(-300_000_000 // stack_bytes))
+    def mk(seed, rows, k):   # one expert's weights, repeated for every expert of the stack (timing only)
+        one = b2.quantize_weights(b2.Q4_K, b2.synth_normal(seed, rows * k, std=0.02).reshape(rows, k))
+        return np.tile(one, (ne, 1))
+
+    g, u, dn = mk(31, ff, d), mk(32, ff, d), mk(33, d, ff)
+    router = b2.quantize_weights(b2.Q8_0, b2.synth_normal(34, ne * d, std=0.05).reshape(ne, d))
+    layers = [(b2.QMatrix(b2.Q4_K, g, ne * ff, d), b2.QMatrix(b2.Q4_K, u, ne * ff, d),
+               b2.QMatrix(b2.Q4_K, dn, ne * d, ff), b2.QMatrix(b2.Q8_0, router, ne, d)) for _ in range(copies)]
+    n_x = 64
+    xs = b2.DeviceBuffer.from_array(b2.synth_normal(35, n_x * d).reshape(n_x, d))
+    lg, ids, wts = b2.DeviceBuffer(ne * 4), b2.DeviceBuffer(nu * 4), b2.DeviceBuffer(nu * 4)
+    gy, uy = b2.DeviceBuffer(nu * ff * 4), b2.DeviceBuffer(nu * ff * 4)
+    dy, out = b2.DeviceBuffer(nu * d * 4), b2.DeviceBuffer(d * 4)
+    stream = b2.Stream()
+
+    def one(i, s):
+        mg, mu, md, mr = layers[i % copies]
+        x = xs.ptr + (i % n_x) * d * 4
+        b2.check(b2.lib.b2_gemv(mr.h, x, 1, lg.ptr, s), "router gemv")
+        b2.check(b2.lib.b2_moe_route(lg.ptr, 1, ne, nu, 1, ids.ptr, wts.ptr, s), "moe_route")
+        b2.check(b2.lib.b2_moe_gemv(mg.h, ne, x, 0, 1, ids.ptr, nu, gy.ptr, s), "moe gate")
+        b2.check(b2.lib.b2_moe_gemv(mu.h, ne, x, 0, 1, ids.ptr, nu, uy.ptr, s), "moe up")
+        b2.check(b2.lib.b2_moe_gemv(md.h, ne, gy.ptr, 1, 1, ids.ptr, nu, dy.ptr, s), "moe down")
+        b2.check(b2.lib.b2_moe_combine(dy.ptr, wts.ptr, 1, nu, d, out.ptr, s), "moe_combine")
+
+    for i in range(2 * copies):
+        one(i, stream.h)
+    graph = b2.Graph(stream, lambda s: [one(i, s) for i in range(steps)])
+    graph.launch()
+    stream.synchronize()
+    e0, e1 = b2.Event(), b2.Event()
+    e0.record(stream.h)
+    graph.launch()
+    e1.record(stream.h)
+    stream.synchronize()
+    ms = e0.elapsed_ms(e1) / steps
+    expert_bytes = nu * 3 * ff * (d // 256) * 144
+    nbytes = expert_bytes + ne * (d // 32) * 34
+    return {"layer": name, "n_embd": d, "expert_ffn": ff, "experts": ne, "used": nu, "us_per_token": ms * 1e3,
+            "bytes_per_token": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9, "copies": copies,
+            "launches_per_token": 5 + (2 * nu if ff * 4 > 32 * 1024 else 1)}
+
+
+def run_moe_ours(args, dist, rank, world, local):
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    res = [moe_measure(b2, n, args.steps) for n in MOE_SHAPES]
+    peaks = measured_peaks()
+    q = res[0]
+    return {"metric": "MoE FFN layer decode HBM GB/s (Qwen3-MoE-like: d 2048, 128 experts of 768, top-8, Q4_K)",
+            "value": round(q["gbs"] * world, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 3,
+            "ms_per_step": q["us_per_token"] / 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k experts, q8_0 router x q8 -> int32 -> f32",
+            "data": "synthetic: W N(0,0.02) seeds 31-34, x N(0,1) seed 35 (64 inputs, their own experts)",
+            "config": {"workload": "moe: one routed FFN layer per token, batch 1; all shapes in 'layers'",
+                       "l2": "inputs larger than L2 (rotating expert stacks)"},
+            "roofline": {"bound": "hbm", "achieved": round(q["gbs"], 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(q["gbs"] / peaks["hbm_gbs"], 4), "traffic": None, "peak_src": peaks["src"],
+                         "algorithmic_bytes_per_launch": q["bytes_per_token"]},
+            "layers": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()} for r in res],
+            "gpu_launches": args.steps * q["launches_per_token"]}
+
+
 WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
              "gemv_q4_0": (run_gemv_ours, run_gemv_reference),
              "decode_1b_q4_0": (run_decode1b_ours, None),
              "gemv_op": (run_gemv_op, None),
              "gemm_q4k": (run_gemm_ours, run_gemm_reference),
              "gemm_q8_0": (run_gemm_ours, run_gemm_reference),
-             "attn": (run_attn_ours, None)}
+             "attn": (run_attn_ours, None),
+             "moe": (run_moe_ours, None)}
 
 
 def main():

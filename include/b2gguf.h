@@ -167,6 +167,33 @@ B2_API int b2_gemv(const b2_qmatrix* w, const float* x, int n_tok, float* y, voi
 B2_API int b2_gemv_multi(const b2_qmatrix* const* w, int n_mat, const float* x, int n_tok, float* const* y,
                          void* stream);
 
+/* Mixture-of-experts FFN pieces: the MoE layers of the GGUFs Milda and Sutra
+ * load, whose blk.N.ffn_{gate,up,down}_exps tensors they place with tensor
+ * buffer overrides (Milda/src/engine.cpp:860-885,
+ * Sutra/src/llm_backends.cpp:1716-1747), computed as llama.cpp's MoE FFN
+ * does (restated; equal probabilities choose the lower expert id).
+ * b2_moe_route: per token, softmax of the router logits [n_tok][n_expert]
+ * (e = expf(l − max), the sum in double, p = e·(float)(1/sum)), the n_used
+ * largest p (expert ids [n_tok][n_used]) and their weights, divided by
+ * their sum (double, rounded to float) when norm_weights != 0.
+ * n_expert <= 256, n_used <= 64.
+ * b2_moe_gemv: y[t][j] = W_{ids[t][j]}·x_{t,j} over a stack of n_expert
+ * expert matrices uploaded as one b2_qmatrix of n_expert·rows rows (the GGUF
+ * [k, rows, n_expert] tensor in its own byte order; rows a multiple of 8),
+ * each output bit-identical to b2_gemv with that expert's matrix; the ids are
+ * read on the device.  x_{t,j} = x[t] ([n_tok][k], gate and up) or, with
+ * x_per_expert, x[t][j] ([n_tok][n_used][k], down).  y [n_tok][n_used][rows].
+ * One launch per token (per token and expert for per-expert inputs of more
+ * than 8192 values).  Ids outside [0, n_expert) are clamped.
+ * b2_moe_combine: out[t][i] = Σ_j y[t][j][i]·weights[t][j], each product
+ * rounded and added in choice order.  All on `stream`, no host sync. */
+B2_API int b2_moe_route(const float* logits, int32_t n_tok, int32_t n_expert, int32_t n_used, int32_t norm_weights,
+                        int32_t* ids, float* weights, void* stream);
+B2_API int b2_moe_gemv(const b2_qmatrix* experts, int32_t n_expert, const float* x, int32_t x_per_expert,
+                       int32_t n_tok, const int32_t* ids, int32_t n_used, float* y, void* stream);
+B2_API int b2_moe_combine(const float* y, const float* weights, int32_t n_tok, int32_t n_used, int32_t n, float* out,
+                          void* stream);
+
 /* Device scratch b2_gemm needs for n_tok tokens (the quantized activations). */
 B2_API int b2_gemm_workspace_bytes(const b2_qmatrix* w, int n_tok, size_t* bytes);
 

@@ -132,6 +132,13 @@ void    orc_mt19937(uint32_t seed, uint32_t* out, int n);
  * generator (GNU C++ library arithmetic). */
 int     orc_discrete_draw(orc_sampler* s, const float* p, int n);
 
+/* ---- Mixture of experts (oracle_moe.c) ---- */
+/* One token: softmax of the router logits, the n_used largest probabilities
+ * (ids, weights; norm: divided by their sum). */
+void orc_moe_route(const float* logits, int n_expert, int n_used, int norm, int32_t* ids, float* weights);
+/* out[i] = Σ_j y[j][i]·w[j] in order (y [n_used][n]). */
+void orc_moe_combine(const float* y, const float* w, int n_used, int n, float* out);
+
 /* ---- Device-order arithmetic (the GPU kernels' evaluation order) ---- */
 float orc_expf_dev(float x);
 void  orc_silu_mul_dev(float* hb, const float* hb2, int n);

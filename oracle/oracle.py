@@ -72,6 +72,8 @@ def _load() -> ctypes.CDLL:
         "orc_sampler_sample": (ctypes.c_int32, [_vp, _vp, _i]),
         "orc_mt19937": (None, [ctypes.c_uint32, _vp, _i]),
         "orc_discrete_draw": (_i, [_vp, _vp, _i]),
+        "orc_moe_route": (None, [_vp, _i, _i, _i, _vp, _vp]),
+        "orc_moe_combine": (None, [_vp, _vp, _i, _i, _vp]),
         "orc_model_open": (_vp, [ctypes.c_char_p]),
         "orc_model_from_memory": (_vp, [_vp, ctypes.c_size_t]),
         "orc_model_free": (None, [_vp]),
@@ -299,6 +301,25 @@ def kv_shift_k_typed(kc: np.ndarray, ktype: int, n_pos: int, n_kv: int, hd: int,
     kc = np.array(kc, np.uint8, copy=True, order="C").reshape(n_pos, -1)
     lib.orc_kv_shift_k_typed(_p(kc), ktype, kc.shape[1], n_pos, n_kv, hd, delta, theta)
     return kc
+
+
+def moe_route(logits: np.ndarray, n_used: int, norm: bool = True):
+    """Per token (rows of logits): expert ids [n_tok, n_used], weights."""
+    lg = np.ascontiguousarray(np.atleast_2d(logits), np.float32)
+    ids = np.zeros((lg.shape[0], n_used), np.int32)
+    w = np.zeros((lg.shape[0], n_used), np.float32)
+    for t in range(lg.shape[0]):
+        lib.orc_moe_route(_p(lg[t]), lg.shape[1], n_used, 1 if norm else 0, _p(ids[t]), _p(w[t]))
+    return ids, w
+
+
+def moe_combine(y: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """y [n_used, n], w [n_used] -> out [n]."""
+    y = np.ascontiguousarray(y, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.zeros(y.shape[1], np.float32)
+    lib.orc_moe_combine(_p(y), _p(w), y.shape[0], y.shape[1], _p(out))
+    return out
 
 
 def mt19937(seed: int, n: int) -> np.ndarray:
