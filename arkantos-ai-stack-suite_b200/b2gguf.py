@@ -437,7 +437,7 @@ def write_synthetic_llama(path: str, n_layer: int, n_embd: int, n_ff: int, n_hea
 
 class ModelParams(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32),
-                ("nccl_id", ctypes.c_void_p)]
+                ("nccl_id", ctypes.c_void_p), ("keep_page_cache", ctypes.c_int32)]
 
 
 class ContextParams(ctypes.Structure):
@@ -455,9 +455,11 @@ class Model:
     INFO = ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "n_vocab", "head_dim", "n_ctx_train", "wtype",
             "out_type", "tp_rank", "tp_size")
 
-    def __init__(self, path: str, device: int = -1, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None):
+    def __init__(self, path: str, device: int = -1, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
+                 keep_page_cache: bool = False):
         self._id = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
-        p = ModelParams(device, tp_rank, tp_size, ctypes.cast(self._id, ctypes.c_void_p) if self._id else None)
+        p = ModelParams(device, tp_rank, tp_size, ctypes.cast(self._id, ctypes.c_void_p) if self._id else None,
+                        1 if keep_page_cache else 0)
         h = ctypes.c_void_p()
         check(lib.b2_model_load(path.encode(), ctypes.byref(p), ctypes.byref(h)), "model_load")
         self.h = h.value

@@ -140,6 +140,7 @@ struct b2_context {
   cudaEvent_t pf_ev = nullptr;  // the staging's last copy
   float *pf_x = nullptr, *pf_xn = nullptr, *pf_delta = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
   float *pf_att = nullptr, *pf_gu = nullptr, *pf_h = nullptr, *pf_scores = nullptr;
+  float* pf_gather = nullptr;   // [tp][cap][n_embd]: the ranks' partial projections (tensor parallelism)
   uint8_t* pf_ws = nullptr;     // GEMM activation images
   // last decode
   int last_n = 0;
@@ -392,7 +393,9 @@ int load_model(b2_model* m, const char* path, const b2_model_params* p) {
     m->layers.push_back(std::move(L));
   }
   m->device_bytes += m->head.m.bytes();
-  return stager.finish();
+  const int frc = stager.finish();   // every upload has landed
+  if (frc == B2_OK && !p->keep_page_cache) m->gguf.release_pages();
+  return frc;
 }
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
@@ -789,7 +792,7 @@ bool gemm_type(int t) { return t == B2_Q4_K || t == B2_Q8_0; }
 
 bool prefill_eligible(const b2_context* c) {
   const b2_model* m = c->model;
-  if (!c->prefill_gemm || c->eval_cb || m->tp_size != 1) return false;
+  if (!c->prefill_gemm || c->eval_cb) return false;
   for (const auto& L : m->layers)
     if (!gemm_type(L->wqkv.m.type) || !gemm_type(L->wo.m.type) || !gemm_type(L->wgu.m.type) ||
         !gemm_type(L->wdown.m.type))
@@ -815,7 +818,8 @@ int prefill_alloc(b2_context* c) {
       (rc = dalloc(c, &c->pf_att, (size_t)cap * nq)) || (rc = dalloc(c, &c->pf_gu, (size_t)cap * 2 * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_h, (size_t)cap * m->ff_l)) ||
       (rc = dalloc(c, &c->pf_scores, attn_scratch_floats(cap, m->nh_l, m->nkv_l, c->n_ctx))) ||
-      (rc = dalloc(c, &c->pf_ws, ws))) {
+      (rc = dalloc(c, &c->pf_ws, ws)) ||
+      (m->tp_size > 1 && (rc = dalloc(c, &c->pf_gather, (size_t)m->tp_size * cap * d)))) {
     // A context short of memory keeps none of the chunk buffers: free the
     // ones this call took (nothing has been enqueued on them).
     for (size_t i = n_before; i < c->allocs.size(); ++i) cudaFree(c->allocs[i]);
@@ -824,12 +828,25 @@ int prefill_alloc(b2_context* c) {
     c->pf_x = c->pf_xn = c->pf_delta = c->pf_qkv = c->pf_q = c->pf_att = c->pf_gu = c->pf_h = nullptr;
     c->pf_scores = nullptr;
     c->pf_ws = nullptr;
+    c->pf_gather = nullptr;
     return rc;
   }
   B2_CUDA_TRY(cudaMallocHost(&c->pf_in_h, (size_t)3 * cap * sizeof(int32_t)));
   B2_CUDA_TRY(cudaEventCreateWithFlags(&c->pf_ev, cudaEventDisableTiming));
   c->pf_cap = cap;
   return B2_OK;
+}
+
+// Under tensor parallelism the attention-out and FFN-down GEMMs of a chunk
+// give each rank a partial over its input columns: the ranks gather all
+// partials (NCCL all-gather) and each sums them in rank order, the order of
+// the decode step's exchange.
+int prefill_reduce(b2_context* c, int nt) {
+  b2_model* m = c->model;
+  if (m->tp_size == 1) return B2_OK;
+  const size_t n = (size_t)nt * m->n_embd;
+  B2_NCCL_TRY(ncclAllGather(c->pf_delta, c->pf_gather, n, ncclFloat, m->comm, c->stream));
+  return launch_rank_sum(c->pf_gather, m->tp_size, (int64_t)n, c->pf_delta, c->stream);
 }
 
 // One chunk of nt tokens staged in pf_in: the layers up to the KV cache.
@@ -849,11 +866,13 @@ int enqueue_prefill_chunk(b2_context* c, int nt) {
         (rc = launch_attention(c->pf_q, nt, m->nh_l, m->nkv_l, hd, pos, seq, c->kc[l], c->type_k, c->vc[l],
                                c->type_v, c->st_d, c->n_seq, c->n_ctx, c->pf_scores, c->pf_att, s, c->status)) ||
         (rc = launch_gemm(L.wo.m, c->pf_att, nq, nt, c->pf_delta, c->pf_ws, c->status, s)) ||
+        (rc = prefill_reduce(c, nt)) ||
         (rc = launch_add_rmsnorm(c->pf_x, c->pf_delta, L.ffn_norm, c->pf_xn, nt, d, m->eps, s, nullptr,
                                  c->status)) ||
         (rc = launch_gemm(L.wgu.m, c->pf_xn, d, nt, c->pf_gu, c->pf_ws, c->status, s)) ||
         (rc = launch_swiglu_pairs(c->pf_gu, nt, m->ff_l, c->pf_h, s)) ||
-        (rc = launch_gemm(L.wdown.m, c->pf_h, m->ff_l, nt, c->pf_delta, c->pf_ws, c->status, s)))
+        (rc = launch_gemm(L.wdown.m, c->pf_h, m->ff_l, nt, c->pf_delta, c->pf_ws, c->status, s)) ||
+        (rc = prefill_reduce(c, nt)))
       break;
   }
   return rc;
@@ -1145,6 +1164,7 @@ void b2_model_default_params(b2_model_params* p) {
   p->tp_rank = 0;
   p->tp_size = 1;
   p->nccl_id = nullptr;
+  p->keep_page_cache = 0;
 }
 
 int b2_nccl_unique_id(void* out) {

@@ -116,7 +116,29 @@ bool GgufFile::open(const std::string& path, std::string* err) {
   }
   map_ = p;
   map_size_ = (size_t)st.st_size;
+  path_ = path;
+  // One pass in file order over the tensors: read ahead aggressively and
+  // start now (Milda advises MADV_WILLNEED on the large mapped segments,
+  // Milda/src/engine.cpp:980-993).
+  (void)madvise(map_, map_size_, MADV_SEQUENTIAL);
+  (void)madvise(map_, map_size_, MADV_WILLNEED);
   return parse(static_cast<const uint8_t*>(p), map_size_, err);
+}
+
+void GgufFile::release_pages() {
+  if (!map_) return;
+  // Milda evicts the page-cache ranges of the tensors it offloaded to the GPU
+  // (POSIX_FADV_DONTNEED, Milda/src/engine.cpp:1018-1041, 1127-1137); here
+  // every tensor is on the device, so the whole file goes.  Tensor records
+  // keep their metadata; their data pointers are not used after the upload.
+  (void)madvise(map_, map_size_, MADV_DONTNEED);
+  munmap(map_, map_size_);
+  map_ = nullptr;
+  const int fd = ::open(path_.c_str(), O_RDONLY);
+  if (fd >= 0) {
+    (void)posix_fadvise(fd, 0, 0, POSIX_FADV_DONTNEED);
+    ::close(fd);
+  }
 }
 
 bool GgufFile::parse(const uint8_t* data, size_t size, std::string* err) {

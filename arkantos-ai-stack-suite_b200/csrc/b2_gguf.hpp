@@ -41,7 +41,11 @@ class GgufFile {
  public:
   ~GgufFile();
   // Maps a file read-only; returns false with an error message on failure.
+  // The mapping is advised for one sequential pass with read-ahead.
   bool open(const std::string& path, std::string* err);
+  // Drops the mapping and asks the kernel to evict the file's pages from the
+  // page cache (the weights now live on the device); metadata stays.
+  void release_pages();
   // Parses a caller-owned buffer (must outlive this object).
   bool parse(const uint8_t* data, size_t size, std::string* err);
 
@@ -65,6 +69,7 @@ class GgufFile {
   size_t size_ = 0;
   void* map_ = nullptr;
   size_t map_size_ = 0;
+  std::string path_;
 };
 
 // Minimal writer: metadata then tensors, data aligned to `alignment`.

@@ -640,6 +640,24 @@ int launch_kv_compact(void* kc, int kt, void* vc, int vt, int n_kv, int hd, int 
   return B2_OK;
 }
 
+// out[i] = ((p_0[i] + p_1[i]) + p_2[i]) + ... over n_parts partials laid out
+// [n_parts][n]: the ranks' partial projections summed in rank order.
+__global__ void rank_sum_kernel(const float* __restrict__ parts, int n_parts, int64_t n, float* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = parts[i];
+    for (int r = 1; r < n_parts; ++r) acc = __fadd_rn(acc, parts[(int64_t)r * n + i]);
+    out[i] = acc;
+  }
+}
+
+int launch_rank_sum(const float* parts, int n_parts, int64_t n, float* out, cudaStream_t s) {
+  B2_CHECK_ARG(parts && out && n_parts >= 1 && n > 0, "rank_sum arguments");
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 8 * kSMs);
+  rank_sum_kernel<<<grid, 256, 0, s>>>(parts, n_parts, n, out);
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
 // SwiGLU over (gate, up) row pairs, as the GEMV's SwiGLU epilogue computes
 // it: h[t][f] = silu(gu[t][2f]) * gu[t][2f+1] in the reference's order
 // (silu_mul_ref).

@@ -52,6 +52,8 @@ int launch_kv_shift(void* kc, int kt, int n_kv, int hd, int seq, const KvSeqStat
                     const RotTable& cs, cudaStream_t s);
 int launch_kv_compact(void* kc, int kt, void* vc, int vt, int n_kv, int hd, int seq, const KvSeqState& st, int cap,
                       int dst0, int src0, int n, const RotTable& cs, cudaStream_t s);
+// out = the n_parts partials [n_parts][n] summed in part order.
+int launch_rank_sum(const float* parts, int n_parts, int64_t n, float* out, cudaStream_t s);
 // Mixture-of-experts routing and combination (b2_moe.cu).
 int launch_moe_route(const float* logits, int n_tok, int n_expert, int n_used, int norm, int32_t* ids, float* weights,
                      cudaStream_t s);

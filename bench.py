@@ -521,6 +521,10 @@ def run_decode_ours(args, dist, rank, world, local):
     t0 = time.perf_counter()
     model = b2.Model(path, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     t_load = time.perf_counter() - t0
+    load = {"seconds": round(t_load, 3), "file_bytes": os.path.getsize(path), "device_bytes": model.device_bytes(),
+            "file_gb_per_s": round(os.path.getsize(path) / t_load / 1e9, 2),
+            "path": "mmap (sequential read-ahead) -> multithreaded repack into two pinned slabs -> async H2D; "
+                    "page cache released after the upload"}
     warm = max(args.warmup, 3)
     n_ctx = PROMPT + warm + CLOCK_LOAD_STEPS + args.steps + 8
     ctx = b2.Context(model, n_ctx=n_ctx, n_seq=BATCH)
@@ -625,6 +629,7 @@ def run_decode_ours(args, dist, rank, world, local):
         "gpu_launches": launches_per_step(c["n_layer"]) * args.steps,
         "clocks": clk.summary(),
         "setup_s": {"write_gguf": round(t_write, 1), "load": round(t_load, 1), "prefill": round(t_prefill, 1)},
+        "load": load,
         "prefill_tok_s": round(BATCH * PROMPT / t_prefill, 1),
         "prefill": prefill_report(c, t_prefill, world, peaks),
     }

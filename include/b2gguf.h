@@ -370,6 +370,10 @@ typedef struct b2_model_params {
     int32_t     tp_size;    /* tensor-parallel degree (1 = whole model here) */
     const void* nccl_id;    /* B2_NCCL_ID_BYTES from b2_nccl_unique_id (rank 0),
                                the same bytes on every rank; NULL when tp_size = 1 */
+    int32_t     keep_page_cache; /* 0 (default): once the weights are on the device the
+                               file's mapping is dropped and its pages are evicted from
+                               the page cache, as Milda evicts the ranges of tensors it
+                               offloaded (Milda/src/engine.cpp:1018-1041); 1: keep them */
 } b2_model_params;
 
 /* llama_model_default_params (Milda/src/engine.cpp:897). */
@@ -394,7 +398,10 @@ typedef struct b2_context_params {
                              call of n tokens that asks no logits of its first n - 8, with
                              n - 8 >= 64, runs those first tokens through the layers in chunks
                              whose projections are tensor-core GEMMs, when every layer's
-                             projections are Q4_K or Q8_0 and the model is not tensor-parallel.
+                             projections are Q4_K or Q8_0.  Under tensor parallelism each
+                             rank runs its shards' GEMMs and the ranks' attention-out and
+                             FFN-down partials are all-gathered (NCCL) and summed in rank
+                             order, as the decode step's exchange sums them.
                              Their projections then sum in the reference's row order (the
                              CPU matmul_quantized's) instead of the decode GEMV's tile order;
                              the last 8 tokens take the decode step. */

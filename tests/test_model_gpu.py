@@ -295,3 +295,20 @@ def test_abort_callback_stops_decode_and_generate(model_file):
     ctx.set_abort_callback(None)
     ctx.decode([4], want_logits=1)
     assert np.all(np.isfinite(ctx.logits(0)))
+
+
+def test_page_cache_release_keeps_results(model_file):
+    """After the upload the model drops its file mapping and evicts the
+    file's pages (Milda's eviction of offloaded tensor ranges); a model that
+    keeps them computes the same logits, and the file loads again."""
+    rng = np.random.default_rng(12)
+    prompt = rng.integers(0, 200, 9).tolist()
+    out = []
+    for keep in (False, True, False):
+        gm = b2.Model(model_file, keep_page_cache=keep)
+        ctx = b2.Context(gm, n_ctx=32, n_seq=1)
+        ctx.decode(prompt, want_logits=2)
+        out.append(ctx.logits(-1))
+        del ctx, gm
+    assert_same(out[0], out[1], "released vs kept page cache")
+    assert_same(out[2], out[1], "reloaded after release")
