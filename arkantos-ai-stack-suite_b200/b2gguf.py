@@ -115,6 +115,7 @@ def _bind() -> None:
         "b2_get_logits": (_i, [_vp, ctypes.c_int32, _vp, _i64]),
         "b2_get_argmax": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32]),
         "b2_generate": (_i, [_vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp]),
+        "b2_context_exchange_wait_ns": (_i, [_vp, _vp, ctypes.c_int32]),
         "b2_sampler_default_params": (None, [_vp]),
         "b2_sampler_create": (_i, [_vp, _vp, _vp]),
         "b2_sampler_free": (_i, [_vp]),
@@ -586,6 +587,11 @@ class Context:
         check(rc, "generate_sampled")
         self.last_n = f.size
         return out[:n_steps]
+
+    def exchange_wait_ns(self, reset: bool = False) -> int:
+        v = ctypes.c_uint64()
+        check(lib.b2_context_exchange_wait_ns(self.h, ctypes.byref(v), 1 if reset else 0), "context_exchange_wait_ns")
+        return v.value
 
     def synchronize(self) -> None:
         check(lib.b2_synchronize_context(self.h), "synchronize_context")

@@ -129,6 +129,17 @@ __device__ __forceinline__ bool wait_peer_flags(const unsigned long long* flags,
   return true;
 }
 
+// The exchange wait of a consumer kernel (one thread), its wall time added to
+// in.wait_ns by the grid's first CTA: the time a rank spends waiting for its
+// peers' partials.
+__device__ __forceinline__ bool peer_wait(const PeerIn& in, int* status, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  const bool ok = wait_peer_flags(in.flags, in.n, *in.epoch, status, code);
+  if (in.wait_ns && blockIdx.x == 0 && blockIdx.y == 0)
+    atomicAdd(in.wait_ns, (unsigned long long)(globaltimer_ns() - t0));
+  return ok;
+}
+
 // ---- bulk async copy (1-D TMA, global -> shared, completes on an mbarrier) ----
 // Both addresses 16-byte aligned, size a multiple of 16 bytes.  No multicast.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {

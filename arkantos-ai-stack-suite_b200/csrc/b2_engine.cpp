@@ -126,6 +126,7 @@ struct b2_context {
   // [ids kStepMax | top-1, margin 2*kStepMax | status] in one allocation: one
   // D2H copy returns a step's greedy result and the device-wait status
   int32_t* res = nullptr;
+  unsigned long long* wait_ns = nullptr;   // exchange waits' wall time (tensor parallelism)
   int32_t* ids = nullptr;
   int* status = nullptr;
   // device-side greedy loop: [n_ctx][kStepMax] generated ids, per-row counts
@@ -488,6 +489,7 @@ PeerIn peer_in(const b2_context* c, int phase) {
   in.slot = (int64_t)kStepMax * m->n_embd;
   in.flags = reinterpret_cast<const unsigned long long*>(c->xbuf + c->x_flags) + (size_t)phase * tp;
   in.epoch = reinterpret_cast<const unsigned long long*>(c->xbuf + c->x_epoch) + phase;
+  in.wait_ns = c->wait_ns;
   return in;
 }
 
@@ -552,7 +554,11 @@ int create_context(b2_context* c, b2_model* m, const b2_context_params* p) {
   c->top = reinterpret_cast<float*>(c->res + kStepMax);
   c->status = c->res + 3 * kStepMax;
   B2_CUDA_TRY(cudaMemset(c->res, 0, kResWords * 4));
-  if (m->tp_size > 1) return setup_exchange(c);
+  if (m->tp_size > 1) {
+    if ((rc = dalloc(c, &c->wait_ns, 1))) return rc;
+    B2_CUDA_TRY(cudaMemset(c->wait_ns, 0, sizeof(unsigned long long)));
+    return setup_exchange(c);
+  }
   return B2_OK;
 }
 
@@ -1449,6 +1455,19 @@ int b2_get_argmax(b2_context* c, int32_t* ids, float* top1, float* margin, int32
     if (margin) margin[i] = top[2 * i + 1];
   }
   if (r[3 * kStepMax] != 0) return check_status(c);
+  return B2_OK;
+}
+
+int b2_context_exchange_wait_ns(b2_context* c, uint64_t* ns, int32_t reset) {
+  B2_CHECK_ARG(c && ns, "context_exchange_wait_ns arguments");
+  *ns = 0;
+  if (!c->wait_ns) return B2_OK;
+  B2_CUDA_TRY(cudaSetDevice(c->model->device));
+  unsigned long long v = 0;
+  B2_CUDA_TRY(cudaMemcpyAsync(&v, c->wait_ns, sizeof v, cudaMemcpyDeviceToHost, c->stream));
+  if (reset) B2_CUDA_TRY(cudaMemsetAsync(c->wait_ns, 0, sizeof v, c->stream));
+  B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  *ns = v;
   return B2_OK;
 }
 

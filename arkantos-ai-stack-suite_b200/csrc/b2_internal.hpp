@@ -263,6 +263,7 @@ struct PeerIn {
   int64_t slot = 0;                            // elements between slots
   const unsigned long long* flags = nullptr;   // local flags of the phase [n]
   const unsigned long long* epoch = nullptr;   // local epoch counter of the phase
+  unsigned long long* wait_ns = nullptr;       // accumulated wall time of the waits (CTA 0), or null
 };
 
 struct GemvArgs {

@@ -101,7 +101,7 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ x, const float* __restric
   const float* dr = delta ? delta + (int64_t)b * n : nullptr;
   if (in.n) {
     if (threadIdx.x == 0) {
-      wait_peer_flags(in.flags, in.n, *in.epoch, status, 3);
+      peer_wait(in, status, 3);
       __threadfence();
     }
     __syncthreads();
@@ -154,7 +154,7 @@ __global__ void add_rmsnorm_q_kernel(float* __restrict__ x, const float* __restr
   float* xr = x + (int64_t)b * n + i0;
   if (in.n) {
     if (tid == 0) {
-      wait_peer_flags(in.flags, in.n, *in.epoch, status, 3);
+      peer_wait(in, status, 3);
       __threadfence();
     }
     __syncthreads();
@@ -486,7 +486,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n_tok, int n
   if (!feed.tok) pdl_launch_dependents();
   if (in.n) {   // the ranks' head shards arrive in the gather layout
     if (threadIdx.x == 0) {
-      wait_peer_flags(in.flags, in.n, *in.epoch, status, 4);
+      peer_wait(in, status, 4);
       __threadfence();
     }
     __syncthreads();

@@ -555,6 +555,7 @@ def run_decode_ours(args, dist, rank, world, local):
     with ClockSampler(local) as clk:
         ctx.generate(start_tok, CLOCK_LOAD_STEPS, seq=seqs)     # untimed load: clocks seen under work
         rewind()
+        ctx.exchange_wait_ns(reset=True)
         barrier(dist)
         if args.profile_range:
             b2.check(b2.lib.b2_profiler_range(1), "profiler_range")
@@ -562,11 +563,20 @@ def run_decode_ours(args, dist, rank, world, local):
         gen = ctx.generate(start_tok, args.steps, seq=seqs)
         e1.record(ctx.stream)
         ctx.synchronize()
+        wait_us = ctx.exchange_wait_ns() / 1e3 / args.steps
         if args.profile_range:
             b2.check(b2.lib.b2_profiler_range(0), "profiler_range")
     ms_total = dist_max(dist, e0.elapsed_ms(e1))
     ms_step = ms_total / args.steps
     tok_s = BATCH * args.steps / (ms_total * 1e-3)
+    exchange = None
+    if world > 1:
+        # each waiting kernel's first CTA adds the wall time of its wait for
+        # the peers' partials (attention-out, FFN-down, the head shards)
+        exchange = {"wait_us_per_step_max_rank": round(dist_max(dist, wait_us), 1),
+                    "wait_us_per_step_rank0": round(wait_us, 1), "step_us": round(ms_step * 1e3, 1),
+                    "waits_per_step": 2 * c["n_layer"] + 1,
+                    "note": "wall time of the exchange waits (globaltimer, 256 ns resolution) against the step"}
 
     # e2e: the llama-style host loop through the C ABI (b2_decode with host
     # token/pos/seq arrays, b2_get_argmax back to the host) from the same state.
@@ -630,6 +640,7 @@ def run_decode_ours(args, dist, rank, world, local):
         "clocks": clk.summary(),
         "setup_s": {"write_gguf": round(t_write, 1), "load": round(t_load, 1), "prefill": round(t_prefill, 1)},
         "load": load,
+        "exchange": exchange,
         "prefill_tok_s": round(BATCH * PROMPT / t_prefill, 1),
         "prefill": prefill_report(c, t_prefill, world, peaks),
     }

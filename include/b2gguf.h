@@ -452,6 +452,11 @@ B2_API int b2_get_argmax(b2_context* c, int32_t* ids, float* top1, float* margin
 B2_API int b2_generate(b2_context* c, const int32_t* first, const int32_t* seq, int32_t n, int32_t n_steps,
                        int32_t* out);
 B2_API int b2_synchronize_context(b2_context* c);
+/* Tensor parallelism: the wall time this rank's decode steps have spent in
+ * the exchange waits (each waiting kernel's first CTA adds its wait), since
+ * the context was created or last reset (reset != 0 zeroes it after the
+ * read).  0 without tensor parallelism.  Synchronizes the context stream. */
+B2_API int b2_context_exchange_wait_ns(b2_context* c, uint64_t* ns, int32_t reset);
 
 /* ------------------------------------------------------------------------ */
 /* Sampler chain on the device                                               */
