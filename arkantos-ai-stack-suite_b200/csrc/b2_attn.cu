@@ -135,9 +135,16 @@ __device__ __forceinline__ SlotRun slot_run(const KvSeqState& st, int p, int end
 // Shared memory of a scores CTA: barrier, the chunk's K rows, then q (fp16
 // K: head pairs [HD][NP] of 8 bytes; Q8_0 K: the G heads' Q8_0 codes [G][HD]
 // and scales [G][HD/32] as fp32).
+// K rows in shared memory: Q8_0 rows as cached (hd + 16 bytes); fp16 rows
+// padded by 16 bytes, so the rows that the 8 threads of a 16-byte load phase
+// read start on different banks.
+template <int HD, int KT>
+__host__ __device__ constexpr int scores_row_stride() {
+  return KT == B2_Q8_0 ? (int)kv_row_bytes(KT, HD) : (int)kv_row_bytes(KT, HD) + 16;
+}
 template <int HD, int G, int KT>
 __host__ __device__ constexpr size_t scores_smem_bytes() {
-  return 128 + (size_t)kScoreP * kv_row_bytes(KT, HD) +
+  return 128 + (size_t)kScoreP * scores_row_stride<HD, KT>() +
          (KT == B2_Q8_0 ? (size_t)G * HD + (size_t)G * (HD / 32) * 4 : (size_t)HD * ((G + 1) / 2) * 8);
 }
 
@@ -152,11 +159,12 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   constexpr int P = kScoreP;
   constexpr int NP = (G + 1) / 2;              // head pairs (the last one half used when G is odd)
   constexpr int RB = (int)kv_row_bytes(KT, HD);
-  constexpr int KB = P * RB;                   // K rows of the chunk
+  constexpr int RS = scores_row_stride<HD, KT>();
+  constexpr int KB = P * RS;                   // K rows of the chunk
   constexpr int NB = HD / 32;                  // Q8_0 blocks per row
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  uint8_t* ks = smem + 128;                                      // [P][RB]
+  uint8_t* ks = smem + 128;                                      // [P][RS]
   uint64_t* qs = reinterpret_cast<uint64_t*>(smem + 128 + KB);   // fp16 K: [HD][NP]: (q_2j[i], q_2j+1[i])
   int8_t* qq = reinterpret_cast<int8_t*>(smem + 128 + KB);       // Q8_0 K: codes [G][HD]
   float* qd = reinterpret_cast<float*>(smem + 128 + KB + G * HD);   // Q8_0 K: scales [G][NB]
@@ -176,7 +184,20 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
   float* srow = grp;                           // head g's scores at srow + g * capS
   float* mrow = grp + m_offset(G, cap);        // head g's chunk maxima at mrow + g * nchS
   const KvSeqState sst = st ? st[s] : KvSeqState{0, 0};
-  if (warp == 0) {
+  if constexpr (KT != B2_Q8_0) {
+    // fp16 rows: one bulk copy per row into its padded slot (the lanes'
+    // copies overlap)
+    if (tid == 0) {
+      mbar_init(&bar[0], 1);
+      fence_mbar_init();
+      mbar_arrive_expect_tx(&bar[0], (uint32_t)(n * RB));
+    }
+    __syncthreads();
+    if (tid < n) {
+      const int64_t slot = kv_slot(sst, t0 + tid, cap);
+      bulk_g2s(ks + tid * RS, kc + (((int64_t)s * n_kv + kh) * cap + slot) * RB, (uint32_t)RB, &bar[0]);
+    }
+  } else if (warp == 0) {
     // one lane per run of consecutive slots (at most three): a bulk copy
     // costs its issuing thread a few hundred cycles, copies from different
     // lanes overlap
@@ -258,7 +279,7 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
     // the row of position t0 + tid, then the chains in dim order
     constexpr int NPc = HD / 8;
     const Ones k2{pack2(one, one), pack2(neg_zero, neg_zero)};
-    const uint8_t* rp = ks + tid * RB;
+    const uint8_t* rp = ks + tid * RS;
     uint64_t acc[NP];
 #pragma unroll
     for (int j = 0; j < NP; ++j) acc[j] = 0ull;   // (+0, +0)

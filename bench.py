@@ -439,12 +439,13 @@ def prompts_8b() -> np.ndarray:
 def launches_per_step(n_layer: int, small_o: bool = False) -> int:
     """Kernels of this library one decode step launches: embed; per layer
     RMSNorm (+ Q8 image), QKV GEMV (RoPE + KV store epilogue), attention
-    scores (+ softmax in the last CTAs), attention P.V, quantize (O input;
+    scores, attention exponentials, attention sum + P.V, quantize (O input;
     none when the O input is small enough for the GEMV to quantize it
     itself), O GEMV, RMSNorm (+ image), gate|up GEMV (SwiGLU epilogue),
-    quantize (down input), down GEMV; then RMSNorm, head GEMV and argmax.
-    No library collective runs in a step."""
-    return 1 + (9 if small_o else 10) * n_layer + 3
+    quantize (down input), down GEMV; then RMSNorm, head GEMV and argmax
+    (the launch list of one 8B step counts 356).  No library collective runs
+    in a step."""
+    return 1 + (10 if small_o else 11) * n_layer + 3
 
 
 def time_gemv_shape(b2, qtype: int, n: int, k: int, n_tok: int, steps: int, seed: int) -> dict:
@@ -578,6 +579,20 @@ def run_decode_ours(args, dist, rank, world, local):
                     "waits_per_step": 2 * c["n_layer"] + 1,
                     "note": "wall time of the exchange waits (globaltimer, 256 ns resolution) against the step"}
 
+    # The same steps with Milda's sampler chain drawing every row on the
+    # device (penalties, top-k 40, top-p 0.9, min-p 0.05, temperature 0.75,
+    # dist; one chain per row, seeds 42 + row) instead of the greedy argmax.
+    progress("sampled steps")
+    samplers = [b2.Sampler(ctx, seed=42 + i) for i in range(BATCH)]
+    rewind()
+    barrier(dist)
+    e0.record(ctx.stream)
+    ctx.generate_sampled(samplers, start_tok, args.steps, seq=seqs)
+    e1.record(ctx.stream)
+    ctx.synchronize()
+    ms_sampled = dist_max(dist, e0.elapsed_ms(e1)) / args.steps
+    del samplers
+
     # e2e: the llama-style host loop through the C ABI (b2_decode with host
     # token/pos/seq arrays, b2_get_argmax back to the host) from the same state.
     progress("e2e host loop")
@@ -641,6 +656,10 @@ def run_decode_ours(args, dist, rank, world, local):
         "setup_s": {"write_gguf": round(t_write, 1), "load": round(t_load, 1), "prefill": round(t_prefill, 1)},
         "load": load,
         "exchange": exchange,
+        "decode_sampled": {"value": round(BATCH / (ms_sampled * 1e-3), 1), "unit": "tok/s",
+                           "ms_per_step": ms_sampled, "steps": args.steps,
+                           "chain": "Milda's defaults on the device: penalties over 64 tokens (1.08), top-k 40, "
+                                    "top-p 0.90, min-p 0.05, temperature 0.75, dist (mt19937, seed 42 + row)"},
         "prefill_tok_s": round(BATCH * PROMPT / t_prefill, 1),
         "prefill": prefill_report(c, t_prefill, world, peaks),
     }
