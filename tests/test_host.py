@@ -69,6 +69,34 @@ def test_kv_row_bytes():
     assert b2.lib.b2_kv_row_bytes(b2.Q4_K, 128) == 0
 
 
+def test_sampler_default_params_are_mildas():
+    """Milda/include/milda/engine.hpp:79-84 and the window of 64
+    (Milda/src/engine.cpp:1354-1355)."""
+    p = b2.SamplerParams()
+    b2.lib.b2_sampler_default_params(ctypes.byref(p))
+    assert (p.penalty_last_n, p.top_k, p.seed) == (64, 40, 42)
+    assert np.float32(p.penalty_repeat) == np.float32(1.08) and np.float32(p.temperature) == np.float32(0.75)
+    assert np.float32(p.top_p) == np.float32(0.90) and np.float32(p.min_p) == np.float32(0.05)
+    assert p.penalty_freq == 0.0 and p.penalty_present == 0.0
+
+
+def test_new_entry_points_refuse_bad_arguments():
+    """Argument checks run on the host before anything reaches a GPU."""
+    assert b2.lib.b2_moe_route(None, 1, 8, 2, 1, None, None, None) == b2.ERR_INVALID
+    fake = ctypes.c_void_p(16)                      # never dereferenced: the checks fail first
+    assert b2.lib.b2_moe_route(fake, 1, 300, 8, 1, fake, fake, None) == b2.ERR_INVALID   # > 256 experts
+    assert b2.lib.b2_moe_route(fake, 1, 8, 9, 1, fake, fake, None) == b2.ERR_INVALID     # n_used > n_expert
+    assert b2.lib.b2_moe_combine(None, None, 1, 2, 8, None, None) == b2.ERR_INVALID
+    assert b2.lib.b2_moe_gemv(None, 8, None, 0, 1, None, 2, None, None) == b2.ERR_INVALID
+    assert b2.lib.b2_sampler_create(None, None, None) == b2.ERR_INVALID
+    assert b2.lib.b2_sampler_accept(None, 1) == b2.ERR_INVALID
+    assert b2.lib.b2_attn_decode_typed(None, None, b2.F16, None, b2.F16, None, None, 1, 1, 8, 8, 128, 64, None,
+                                       None) == b2.ERR_INVALID
+    assert b2.lib.b2_kv_shift_k_typed(None, b2.Q8_0, 0, 8, 128, 64, 0, 8, 1, 10000.0, None) == b2.ERR_INVALID
+    ns = ctypes.c_uint64(7)
+    assert b2.lib.b2_context_exchange_wait_ns(None, ctypes.byref(ns), 0) == b2.ERR_INVALID
+
+
 def _write_small_llama(path):
     b2.write_synthetic_llama(str(path), 1, 64, 128, 2, 1, 64, b2.Q8_0, embd_type=b2.Q8_0, out_type=b2.Q8_0, seed=3)
     return path.read_bytes()
