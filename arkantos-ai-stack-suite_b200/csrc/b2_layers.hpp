@@ -24,8 +24,16 @@ bool add_rmsnorm_q_supported(int n, int act_type);
 // rows per cache.  F16: hd fp16 values.  Q8_0: hd int8 codes, then the hd/32
 // fp16 block scales, padded to a multiple of 16 bytes (so every row, and
 // every run of rows, starts 16-byte aligned for bulk and tensor copies).
-__host__ __device__ constexpr int64_t kv_row_bytes(int type, int hd) { return type == B2_Q8_0 ? hd + 16 : 2 * hd; }
-inline bool kv_type_ok(int type) { return type == B2_F16 || type == B2_Q8_0; }
+// Q4_0: hd/2 bytes of 4-bit codes (block b at 16·b: byte j holds element j
+// in its low nibble and element j+16 in its high one), then the block
+// scales, padded the same way.
+__host__ __device__ constexpr int64_t kv_code_bytes(int type, int hd) {
+  return type == B2_Q8_0 ? hd : type == B2_Q4_0 ? hd / 2 : 2 * hd;
+}
+__host__ __device__ constexpr int64_t kv_row_bytes(int type, int hd) {
+  return type == B2_F16 ? 2 * hd : kv_code_bytes(type, hd) + 16;
+}
+inline bool kv_type_ok(int type) { return type == B2_F16 || type == B2_Q8_0 || type == B2_Q4_0; }
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                    const float* rope, float* q_out, void* kc, int kt, void* vc, int vt, const KvSeqState* st, int n_seq,
                    int cap, cudaStream_t s);

@@ -100,13 +100,15 @@ void orc_kv_shift_k(uint16_t* kc, int64_t kv_stride, int n_pos, int n_kv_heads, 
 
 /* Quantized KV cache (llama.cpp cache types; Milda's default is Q8_0 K and
  * V).  Rows hold hd values of one kv head in the type's storage: fp16, or
- * ggml Q8_0 blocks.  A row is stored with the type's quantizer (Q8_0:
- * orc_quantize_row_q8_0).  Attention: with a Q8_0 K the query head is
- * quantized to Q8_0 and scored with orc_vec_dot_q8_0_q8_0 (times 1/√hd);
+ * ggml Q8_0 or Q4_0 blocks.  A row is stored with the type's quantizer
+ * (orc_quantize_row_q8_0, orc_quantize_row_q4_0).  Attention: with a Q8_0
+ * or Q4_0 K the query head is quantized to Q8_0 (both types' dot type) and
+ * scored with orc_vec_dot_q8_0_q8_0 / orc_vec_dot_q4_0_q8_0 (times 1/√hd);
  * V rows are dequantized before the weighted sum; softmax and summation
  * order as orc_attn_decode.  Row (t, kvh) at base + t*stride + kvh*row
  * bytes; strides in bytes.  The shift dequantizes, rotates as
  * orc_kv_shift_k and stores back with the type's quantizer. */
+void orc_quantize_row_q4_0(const float* x, void* y, int k);   /* ggml formula */
 void orc_kv_store_row(int type, const float* x, void* row, int n);
 void orc_kv_store_rows(int type, const float* x, void* rows, int64_t n_rows, int n);
 void orc_attn_decode_typed(const float* q, const void* kc, int ktype, size_t k_stride, const void* vc,

@@ -43,7 +43,7 @@ struct orc_model {
     /* runtime */
     int n_seq, n_ctx;
     uint8_t *kc, *vc;  /* [seq][layer][pos][kv_dim], rows in the cache types' storage */
-    int ktype, vtype;  /* ORC_F16 (default) or ORC_Q8_0 */
+    int ktype, vtype;  /* ORC_F16 (default), ORC_Q8_0 or ORC_Q4_0 */
     float *x, *xb, *xb2, *q, *k, *v, *hb, *hb2;
     void* xq;
     float* rope;
@@ -59,7 +59,9 @@ struct orc_model {
 void orc_model_set_device_order(orc_model* m, int on) { m->device_order = on; }
 
 int orc_model_set_kv_types(orc_model* m, int ktype, int vtype) {
-    if ((ktype != ORC_F16 && ktype != ORC_Q8_0) || (vtype != ORC_F16 && vtype != ORC_Q8_0)) return -1;
+    if ((ktype != ORC_F16 && ktype != ORC_Q8_0 && ktype != ORC_Q4_0) ||
+        (vtype != ORC_F16 && vtype != ORC_Q8_0 && vtype != ORC_Q4_0))
+        return -1;
     m->ktype = ktype;
     m->vtype = vtype;
     return m->kc ? orc_model_init_cache(m, m->n_seq, m->n_ctx) : 0;
@@ -307,7 +309,13 @@ int orc_model_init_cache(orc_model* m, int n_seq, int n_ctx) {
 /* fp16 rows take `bits` in every value; Q8_0 rows take `bits` as every
  * block's scale and 1 as every code. */
 static void cache_fill_rows(uint8_t* c, int type, size_t n_vals, uint16_t bits) {
-    if (type == ORC_Q8_0) {
+    if (type == ORC_Q4_0) {
+        for (size_t b = 0; b < n_vals / 32; ++b) {
+            uint8_t* blk = c + b * ORC_Q4_0_BYTES;
+            memcpy(blk, &bits, 2);
+            memset(blk + 2, 0x99, 16);
+        }
+    } else if (type == ORC_Q8_0) {
         for (size_t b = 0; b < n_vals / 32; ++b) {
             uint8_t* blk = c + b * ORC_Q8_0_BYTES;
             memcpy(blk, &bits, 2);

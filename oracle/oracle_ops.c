@@ -872,8 +872,40 @@ void orc_kv_shift_k(uint16_t* kc, int64_t kv_stride, int n_pos, int n_kv_heads, 
 
 static size_t kv_row_bytes(int type, int hd) { return orc_row_bytes(type, hd); }
 
+/* ggml's quantize_row_q4_0_ref (llama.cpp's Q4_0 cache type; the same
+ * formula as the library's GGUF weight quantizer, pinned to gguf-py): the
+ * value of largest magnitude (first such), d = max/−8, id = 1/d, code =
+ * min(15, trunc(x·id + 8.5)), element j low nibble and j+16 high nibble of
+ * byte j. */
+void orc_quantize_row_q4_0(const float* x, void* vy, int k) {
+    blk_q4_0* y = (blk_q4_0*)vy;
+    for (int b = 0; b < k / 32; ++b) {
+        const float* xb = x + b * 32;
+        float amax = 0.0f, max = 0.0f;
+        for (int j = 0; j < 32; ++j) {
+            const float v = xb[j];
+            const float av = v < 0.0f ? -v : v;
+            if (amax < av) {
+                amax = av;
+                max = v;
+            }
+        }
+        const float d = max / -8.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        y[b].d = orc_fp32_to_fp16(d);
+        for (int j = 0; j < 16; ++j) {
+            const float x0 = xb[j] * id, x1 = xb[16 + j] * id;
+            int q0 = (int)(int8_t)(x0 + 8.5f), q1 = (int)(int8_t)(x1 + 8.5f);
+            q0 = q0 < 15 ? q0 : 15;
+            q1 = q1 < 15 ? q1 : 15;
+            y[b].qs[j] = (uint8_t)(q0 | (q1 << 4));
+        }
+    }
+}
+
 void orc_kv_store_row(int type, const float* x, void* row, int n) {
     if (type == ORC_Q8_0) orc_quantize_row_q8_0(x, row, n);
+    else if (type == ORC_Q4_0) orc_quantize_row_q4_0(x, row, n);
     else orc_fp32_to_fp16_row(x, (uint16_t*)row, n);
 }
 
@@ -898,12 +930,14 @@ void orc_attn_decode_typed(const float* q, const void* kc, int ktype, size_t k_s
         int kvh = h / gqa;
         if (kvh > n_kv_heads - 1) kvh = n_kv_heads - 1;
         const float* qh = q + (size_t)h * hd;
-        if (ktype == ORC_Q8_0) orc_quantize_row_q8_0(qh, qq, hd);
+        if (ktype == ORC_Q8_0 || ktype == ORC_Q4_0) orc_quantize_row_q8_0(qh, qq, hd);
         for (int t = 0; t < n_pos; ++t) {
             const uint8_t* krow = kb + (size_t)t * k_stride + (size_t)kvh * krb;
             float score = 0.0f;
             if (ktype == ORC_Q8_0) {
                 score = orc_vec_dot_q8_0_q8_0(hd, krow, qq);
+            } else if (ktype == ORC_Q4_0) {
+                score = orc_vec_dot_q4_0_q8_0(hd, krow, qq);
             } else {
                 orc_fp16_to_fp32_row((const uint16_t*)krow, tmp, hd);
                 for (int i = 0; i < hd; ++i) score += qh[i] * tmp[i];
