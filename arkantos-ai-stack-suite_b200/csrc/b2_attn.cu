@@ -135,17 +135,24 @@ __device__ __forceinline__ SlotRun slot_run(const KvSeqState& st, int p, int end
 // Shared memory of a scores CTA: barrier, the chunk's K rows, then q (fp16
 // K: head pairs [HD][NP] of 8 bytes; Q8_0 K: the G heads' Q8_0 codes [G][HD]
 // and scales [G][HD/32] as fp32).
-// K rows in shared memory: Q8_0 rows as cached (hd + 16 bytes); fp16 rows
-// padded by 16 bytes, so the rows that the 8 threads of a 16-byte load phase
-// read start on different banks.
+// K rows in shared memory: Q8_0 and Q4_0 rows as cached (hd + 16 and hd/2
+// + 16 bytes); fp16 rows padded by 16 bytes, so the rows that the 8 threads
+// of a 16-byte load phase read start on different banks.
 template <int HD, int KT>
 __host__ __device__ constexpr int scores_row_stride() {
-  return KT == B2_Q8_0 ? (int)kv_row_bytes(KT, HD) : (int)kv_row_bytes(KT, HD) + 16;
+  return KT != B2_F16 ? (int)kv_row_bytes(KT, HD) : (int)kv_row_bytes(KT, HD) + 16;
 }
 template <int HD, int G, int KT>
 __host__ __device__ constexpr size_t scores_smem_bytes() {
   return 128 + (size_t)kScoreP * scores_row_stride<HD, KT>() +
-         (KT == B2_Q8_0 ? (size_t)G * HD + (size_t)G * (HD / 32) * 4 : (size_t)HD * ((G + 1) / 2) * 8);
+         (KT != B2_F16 ? (size_t)G * HD + (size_t)G * (HD / 32) * 4 : (size_t)HD * ((G + 1) / 2) * 8);
+}
+
+// Unsigned 4 bytes · signed 4 bytes (the Q4_0 codes against Q8_0 codes).
+__device__ __forceinline__ int dp4a_u8s8(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 template <int HD, int G, int KT>
@@ -216,10 +223,10 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
     }
   }
   // q of the G heads while the copies fly: head pairs for fp16 K; for Q8_0
-  // K each head quantized to Q8_0 (one warp per 32-value block), the dot
-  // type that pairs with a Q8_0 K row
+  // and Q4_0 K each head quantized to Q8_0 (one warp per 32-value block),
+  // the dot type that pairs with both
   const float* qg = q + ((int64_t)b * n_head + hq0) * HD;
-  if constexpr (KT == B2_Q8_0) {
+  if constexpr (KT != B2_F16) {
     for (int blk = warp; blk < G * NB; blk += P / 32) {
       uint16_t d16;
       const int8_t c = quant_q8_0_lane(qg[blk * 32 + lane], &d16);
@@ -266,6 +273,46 @@ __global__ void __launch_bounds__(kScoreP) attn_scores_kernel(const float* __res
           si = __dp4a((int)k1.z, (int)q1.z, si);
           si = __dp4a((int)k1.w, (int)q1.w, si);
           sumf[g] = __fadd_rn(sumf[g], __fmul_rn(__fmul_rn(dk, qd[g * NB + bi]), (float)si));
+        }
+      }
+      const int t = t0 + tid;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sc[g] = __fmul_rn(sumf[g], scale);
+        srow[(int64_t)g * capS + t] = sc[g];
+      }
+    }
+  } else if constexpr (KT == B2_Q4_0) {
+    if (ok && tid < n) {
+      // the Q4_0·Q8_0 block dot of ref_vec_dot_q4_0_q8_0
+      // (Singularity/tests/test_and_bench_a5.cpp:184-203): sumi =
+      // Σ (lo_j − 8)·q_j + (hi_j − 8)·q_{j+16} (exact), then sumf +=
+      // (d_k·d_q)·sumi over the blocks in order
+      const uint8_t* rp = ks + tid * RS;
+      float sumf[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) sumf[g] = 0.0f;
+#pragma unroll
+      for (int bi = 0; bi < NB; ++bi) {
+        const uint4 kw = *reinterpret_cast<const uint4*>(rp + bi * 16);
+        const uint32_t lo[4] = {kw.x & 0x0F0F0F0Fu, kw.y & 0x0F0F0F0Fu, kw.z & 0x0F0F0F0Fu, kw.w & 0x0F0F0F0Fu};
+        const uint32_t hi[4] = {(kw.x >> 4) & 0x0F0F0F0Fu, (kw.y >> 4) & 0x0F0F0F0Fu, (kw.z >> 4) & 0x0F0F0F0Fu,
+                                (kw.w >> 4) & 0x0F0F0F0Fu};
+        const float dk = h2f(*reinterpret_cast<const uint16_t*>(rp + HD / 2 + 2 * bi));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const uint4 q0 = *reinterpret_cast<const uint4*>(qq + g * HD + bi * 32);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(qq + g * HD + bi * 32 + 16);
+          const uint32_t qa[4] = {q0.x, q0.y, q0.z, q0.w}, qb[4] = {q1.x, q1.y, q1.z, q1.w};
+          int si = 0, sq = 0;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            si = dp4a_u8s8(lo[w], qa[w], si);
+            si = dp4a_u8s8(hi[w], qb[w], si);
+            sq = __dp4a(0x01010101, (int)qa[w], sq);
+            sq = __dp4a(0x01010101, (int)qb[w], sq);
+          }
+          sumf[g] = __fadd_rn(sumf[g], __fmul_rn(__fmul_rn(dk, qd[g * NB + bi]), (float)(si - 8 * sq)));
         }
       }
       const int t = t0 + tid;
@@ -410,11 +457,18 @@ constexpr int kPvChP = kPvCh + 2;
 // 16 (a tensor copy's smallest inner box), starting at the slice's first dim
 // rounded down to 16.
 __host__ __device__ constexpr int pv_code_bytes(int ds) { return ds < 16 ? 16 : ds; }
+// Q4_0: the slice's blocks' 16-byte nibble runs (one for slices of up to 32
+// dims), from its first block.
+__host__ __device__ constexpr int pv_code_bytes_q4(int ds) { return ds <= 32 ? 16 : ds / 2; }
+template <int VT>
+__host__ __device__ constexpr int pv_codes(int ds) {
+  return VT == B2_Q4_0 ? pv_code_bytes_q4(ds) : pv_code_bytes(ds);
+}
 // Raw V rows of a stage: fp16 [CH][ds]; Q8_0 codes [CH][pv_code_bytes] then
 // the rows' scale words [CH][8] (16 bytes: the hd/32 scales and padding).
 template <int VT>
 __host__ __device__ constexpr size_t pv_rawv_bytes(int ds) {
-  return VT == B2_Q8_0 ? (size_t)kPvCh * (pv_code_bytes(ds) + 16) : (size_t)kPvCh * ds * 2;
+  return VT != B2_F16 ? (size_t)kPvCh * (pv_codes<VT>(ds) + 16) : (size_t)kPvCh * ds * 2;
 }
 template <int G, int VT>
 __host__ __device__ constexpr size_t pv_stage_bytes(int ds) {
@@ -498,7 +552,7 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
   float* inv_l = reinterpret_cast<float*>(part + kSumParts);   // [G]
   constexpr size_t SB = pv_stage_bytes<G, VT>(DS);
   constexpr int RAWV = (int)pv_rawv_bytes<VT>(DS);
-  constexpr int DSL = pv_code_bytes(DS);
+  constexpr int DSL = pv_codes<VT>(DS);
   const int WA = wa;                                    // positions per window of the sum (a multiple of 4)
   uint8_t* stages = smem + 256;
   const int slice = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -565,12 +619,13 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
       uint8_t* sp = stages + si * SB;
       if (lane == 0) {
         mbar_arrive_expect_tx(&full[si], (uint32_t)(RAWV + r.len * GP * 4));
-        tma_load_2d(sp, &vmap, VT == B2_Q8_0 ? (d0 & ~15) : d0, row0 + (int)r.slot, &full[si]);
+        tma_load_2d(sp, &vmap, VT == B2_Q8_0 ? (d0 & ~15) : VT == B2_Q4_0 ? (d0 >> 5) * 16 : d0, row0 + (int)r.slot,
+                    &full[si]);
       } else if (lane == 1) {
         bulk_g2s(sp + RAWV, erow + (int64_t)r.p * GP, (uint32_t)(r.len * GP * 4), &full[si]);
-      } else if (VT == B2_Q8_0 && lane == 2) {
-        // the rows' scale words: 8 fp16 from byte HD of each row
-        tma_load_2d(sp + CH * DSL, &smap, HD / 2, row0 + (int)r.slot, &full[si]);
+      } else if (VT != B2_F16 && lane == 2) {
+        // the rows' scale words: 8 fp16 from the end of the codes
+        tma_load_2d(sp + CH * DSL, &smap, (int)kv_code_bytes(VT, HD) / 2, row0 + (int)r.slot, &full[si]);
       }
       p_iss += r.len;
       ++c_iss;
@@ -610,6 +665,21 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
                 vp[(4 * c + k) * kPvChP + t] =
                     pack2(__fmul_rn((float)(int8_t)(h & 0xFFu), d), __fmul_rn((float)(int8_t)(h >> 8), d));
               }
+            }
+          } else if constexpr (VT == B2_Q4_0) {
+            // (code − 8) · block scale, exact in fp32 (ggml's
+            // dequantize_row_q4_0): dim e of a block is byte e % 16's low
+            // nibble for e < 16, its high one above
+            const uint8_t* rc = sp + t * DSL;
+            const uint16_t* rs = reinterpret_cast<const uint16_t*>(sp + CH * DSL) + t * 8;
+#pragma unroll
+            for (int k = 0; k < DS / 2; ++k) {
+              const int dd = d0 + 2 * k, e = dd & 31;
+              const int bo = ((dd >> 5) - (d0 >> 5)) * 16 + (e & 15);
+              const int sh = (e & 16) ? 4 : 0;
+              const float d = h2f(rs[dd >> 5]);
+              const int c0 = (rc[bo] >> sh) & 15, c1 = (rc[bo + 1] >> sh) & 15;
+              vp[k * kPvChP + t] = pack2(__fmul_rn((float)(c0 - 8), d), __fmul_rn((float)(c1 - 8), d));
             }
           } else {
             const uint4* rv = reinterpret_cast<const uint4*>(sp);   // [CH][DS/8] raw V
@@ -764,8 +834,9 @@ int make_v_maps(const void* vc, int vt, int64_t n_rows, int hd, int ds, CUtensor
     return B2_OK;
   };
   int rc;
-  if (vt == B2_Q8_0) {
-    if ((rc = enc(vmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, (cuuint32_t)pv_code_bytes(ds)))) return rc;
+  if (vt == B2_Q8_0 || vt == B2_Q4_0) {
+    const cuuint32_t cb = (cuuint32_t)(vt == B2_Q8_0 ? pv_code_bytes(ds) : pv_code_bytes_q4(ds));
+    if ((rc = enc(vmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, cb))) return rc;
     return enc(smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, rb / 2, 8);
   }
   if ((rc = enc(vmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, (cuuint64_t)hd, (cuuint32_t)ds))) return rc;
@@ -818,10 +889,15 @@ int launch_types(const float* q, int n_tok, int n_head, int n_kv, const int32_t*
                                       status);
   B2_ATTN_TYPES(B2_F16, B2_F16)
   B2_ATTN_TYPES(B2_F16, B2_Q8_0)
+  B2_ATTN_TYPES(B2_F16, B2_Q4_0)
   B2_ATTN_TYPES(B2_Q8_0, B2_F16)
   B2_ATTN_TYPES(B2_Q8_0, B2_Q8_0)
+  B2_ATTN_TYPES(B2_Q8_0, B2_Q4_0)
+  B2_ATTN_TYPES(B2_Q4_0, B2_F16)
+  B2_ATTN_TYPES(B2_Q4_0, B2_Q8_0)
+  B2_ATTN_TYPES(B2_Q4_0, B2_Q4_0)
 #undef B2_ATTN_TYPES
-  set_error("attention: KV cache types %d / %d (F16 or Q8_0)", kt, vt);
+  set_error("attention: KV cache types %d / %d (F16, Q8_0 or Q4_0)", kt, vt);
   return B2_ERR_INVALID;
 }
 

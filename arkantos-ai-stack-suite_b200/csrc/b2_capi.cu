@@ -521,7 +521,7 @@ int b2_attn_decode_typed(const float* q, const void* k_cache, int type_k, const 
   B2_CHECK_ARG(q && k_cache && v_cache && pos && seq && out && n_q > 0 && n_seq > 0 && cap > 0,
                "attn_decode arguments");
   B2_CHECK_ARG(n_kv > 0 && n_head % n_kv == 0, "n_head must be a multiple of n_kv");
-  B2_CHECK_ARG(kv_type_ok(type_k) && kv_type_ok(type_v), "KV cache types must be B2_F16 or B2_Q8_0");
+  B2_CHECK_ARG(kv_type_ok(type_k) && kv_type_ok(type_v), "KV cache types must be B2_F16, B2_Q8_0 or B2_Q4_0");
   cudaStream_t s = as_stream(stream);
   // scores, exponentials and chunk maxima (no initialisation needed)
   void* scratch = nullptr;
@@ -543,7 +543,7 @@ int b2_kv_shift_k_typed(void* k_cache, int type_k, int seq, int n_kv, int head_d
                         int delta, float theta, void* stream) {
   B2_CHECK_ARG(k_cache && seq >= 0 && p_begin >= 0 && p_end <= cap && head_dim % 32 == 0 && head_dim <= 2 * kRotPairs,
                "kv_shift_k arguments");
-  B2_CHECK_ARG(kv_type_ok(type_k), "KV cache type must be B2_F16 or B2_Q8_0");
+  B2_CHECK_ARG(kv_type_ok(type_k), "KV cache type must be B2_F16, B2_Q8_0 or B2_Q4_0");
   RotTable cs;
   rope_table(theta, head_dim, delta, 1, cs.cs);
   const KvSeqState st{0, 0};

@@ -1240,7 +1240,7 @@ int b2_context_create(b2_model* m, const b2_context_params* params, b2_context**
   b2_context_default_params(&p);
   if (params) p = *params;
   B2_CHECK_ARG(p.n_ctx > 0 && p.n_seq_max > 0, "n_ctx and n_seq_max must be positive");
-  B2_CHECK_ARG(kv_type_ok(p.type_k) && kv_type_ok(p.type_v), "type_k / type_v must be B2_F16 or B2_Q8_0");
+  B2_CHECK_ARG(kv_type_ok(p.type_k) && kv_type_ok(p.type_v), "type_k / type_v must be B2_F16, B2_Q8_0 or B2_Q4_0");
   b2_context* c = new (std::nothrow) b2_context;
   if (!c) return B2_ERR_OOM;
   int rc;

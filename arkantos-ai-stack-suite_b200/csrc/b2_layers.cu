@@ -3,7 +3,7 @@
 //   embed         token row dequantization (:1066-1105)
 //   add_rmsnorm   residual add fused with RMSNorm (:1121, :1259-1266, :1284-1287)
 //   rope_kv       RoPE on q/k (adjacent pairs, :1187-1192) + K/V store (:1195-1203) into an
-//                 fp16 or Q8_0 cache (llama.cpp cache types, Milda/src/engine.cpp:74-87)
+//                 fp16, Q8_0 or Q4_0 cache (llama.cpp cache types, Milda/src/engine.cpp:74-87)
 //   attn_split / attn_combine
 //                 split-K GQA decode attention over the fp16 cache (:1205-1254)
 //   kv_shift      in-place K re-rotation for Milda's KV shift (Milda/src/engine.cpp:1642-1675)
@@ -262,18 +262,36 @@ __device__ __forceinline__ uint8_t* kv_row(uint8_t* c, int type, int hd, int s, 
                                            int64_t slot) {
   return c + (((int64_t)s * n_kv + kh) * cap + slot) * kv_row_bytes(type, hd);
 }
-// Value i of a row (fp16, or Q8_0 code · block scale: exact in fp32).
+// Byte of a Q4_0 row holding value i (its low nibble for i % 32 < 16).
+__device__ __forceinline__ int q4_byte(int i) { return (i >> 5) * 16 + (i & 15); }
+// Value i of a row (fp16, or code · block scale: exact in fp32; Q4_0 codes
+// are offset by 8).
 template <int T>
 __device__ __forceinline__ float kv_load(const uint8_t* row, int hd, int i) {
   if constexpr (T == B2_Q8_0) {
     const float d = h2f(*reinterpret_cast<const uint16_t*>(row + hd + 2 * (i >> 5)));
     return __fmul_rn((float)(int8_t)row[i], d);
+  } else if constexpr (T == B2_Q4_0) {
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(row + hd / 2 + 2 * (i >> 5)));
+    const int nib = (row[q4_byte(i)] >> ((i & 16) ? 4 : 0)) & 15;
+    return __fmul_rn((float)(nib - 8), d);
   } else {
     return h2f(reinterpret_cast<const uint16_t*>(row)[i]);
   }
 }
-// Stores value i of a row; for Q8_0 the whole warp stores one 32-value block
-// (lane = value i % 32), the block's scale from lane 0.
+// Q4_0 block scale of ggml's quantize_row_q4_0_ref from the value of largest
+// magnitude (the first such; +0 when all are zero): d = max/−8, id = 1/d.
+__device__ __forceinline__ void q4_0_scale(float mx, float* d, float* id) {
+  *d = __fdiv_rn(mx, -8.0f);
+  *id = *d != 0.0f ? __fdiv_rn(1.0f, *d) : 0.0f;
+}
+// Code of x: min(15, trunc(x·id + 8.5)).
+__device__ __forceinline__ uint32_t q4_0_code(float x, float id) {
+  const int c = __float2int_rz(__fadd_rn(__fmul_rn(x, id), 8.5f));
+  return (uint32_t)(c < 15 ? c : 15);
+}
+// Stores value i of a row; for Q8_0 and Q4_0 the whole warp stores one
+// 32-value block (lane = value i % 32), the block's scale from lane 0.
 template <int T>
 __device__ __forceinline__ void kv_store(uint8_t* row, int hd, int i, float y) {
   if constexpr (T == B2_Q8_0) {
@@ -281,6 +299,26 @@ __device__ __forceinline__ void kv_store(uint8_t* row, int hd, int i, float y) {
     const int8_t q = quant_q8_0_lane(y, &d16);
     row[i] = (uint8_t)q;
     if ((threadIdx.x & 31) == 0) *reinterpret_cast<uint16_t*>(row + hd + 2 * (i >> 5)) = d16;
+  } else if constexpr (T == B2_Q4_0) {
+    const int lane = threadIdx.x & 31;
+    float av = fabsf(y), v = y;
+    int idx = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float a2 = __shfl_xor_sync(0xffffffffu, av, o), v2 = __shfl_xor_sync(0xffffffffu, v, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (a2 > av || (a2 == av && i2 < idx)) {
+        av = a2;
+        v = v2;
+        idx = i2;
+      }
+    }
+    float d, id;
+    q4_0_scale(av > 0.0f ? v : 0.0f, &d, &id);
+    const uint32_t c = q4_0_code(y, id);
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, c, 16);   // value i + 16's code
+    if (lane < 16) row[q4_byte(i)] = (uint8_t)(c | (hi << 4));
+    if (lane == 0) *reinterpret_cast<uint16_t*>(row + hd / 2 + 2 * (i >> 5)) = f2h_rn(d);
   } else {
     reinterpret_cast<uint16_t*>(row)[i] = f2h_rn(y);
   }
@@ -372,6 +410,14 @@ __global__ void kv_shift_kernel(uint8_t* __restrict__ kc, int n_kv, int hd, int 
 #pragma unroll
         for (int k = 0; k < 4; ++k) x[k] = __fmul_rn((float)(int8_t)(w >> (8 * k)), d);
       }
+    } else if constexpr (KT == B2_Q4_0) {
+      if (on) {
+        // values i..i+3 share one word of nibbles (low for i % 32 < 16)
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(rp + q4_byte(i)) >> ((i & 16) ? 4 : 0);
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(rp + hd / 2 + 2 * (i >> 5)));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = __fmul_rn((float)((int)((w >> (8 * k)) & 15u) - 8), d);
+      }
     } else if (on) {
       const uint2 w = *reinterpret_cast<const uint2*>(rp + 2 * i);
       x[0] = h2f((uint16_t)(w.x & 0xFFFFu));
@@ -386,7 +432,41 @@ __global__ void kv_shift_kernel(uint8_t* __restrict__ kc, int n_kv, int hd, int 
       y[k] = __fsub_rn(__fmul_rn(x[k], c), __fmul_rn(x[k + 1], sn));
       y[k + 1] = __fadd_rn(__fmul_rn(x[k], sn), __fmul_rn(x[k + 1], c));
     }
-    if constexpr (KT == B2_Q8_0) {
+    if constexpr (KT == B2_Q4_0) {
+      // the block's 32 values sit on 8 consecutive lanes: the value of
+      // largest magnitude (the first such), then codes; the lanes of values
+      // 16..31 hand their codes to the lanes of values 0..15 (lane ^ 4), whose
+      // bytes take them as high nibbles
+      float av = fabsf(y[0]), v = y[0];
+      int idx = i;
+#pragma unroll
+      for (int k = 1; k < 4; ++k)
+        if (fabsf(y[k]) > av) {
+          av = fabsf(y[k]);
+          v = y[k];
+          idx = i + k;
+        }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        const float a2 = __shfl_xor_sync(0xffffffffu, av, o), v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (a2 > av || (a2 == av && i2 < idx)) {
+          av = a2;
+          v = v2;
+          idx = i2;
+        }
+      }
+      float d, id;
+      q4_0_scale(av > 0.0f ? v : 0.0f, &d, &id);
+      uint32_t w = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w |= q4_0_code(y[k], id) << (8 * k);
+      const uint32_t hi = __shfl_xor_sync(0xffffffffu, w, 4);
+      if (on && (i & 16) == 0) {
+        *reinterpret_cast<uint32_t*>(rp + q4_byte(i)) = w | (hi << 4);
+        if ((i & 31) == 0) *reinterpret_cast<uint16_t*>(rp + hd / 2 + 2 * (i >> 5)) = f2h_rn(d);
+      }
+    } else if constexpr (KT == B2_Q8_0) {
       // the block's 32 values sit on 8 consecutive lanes
       float amax = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
 #pragma unroll
@@ -435,20 +515,23 @@ __global__ void kv_compact_kernel(uint8_t* __restrict__ kc, uint8_t* __restrict_
     const uint8_t* vsrc = kv_row(vc, VT, hd, s, n_kv, kh, cap, ss);
     uint8_t* vdst = kv_row(vc, VT, hd, s, n_kv, kh, cap, ds);
     const float y = rotate_lane(kv_load<KT>(ksrc, hd, i), i, cs);
-    // the V row moves as bytes: 2 per value for fp16, codes then scales for Q8_0
+    // the V row moves as bytes: 2 per value for fp16, codes then scales for
+    // Q8_0 and Q4_0
+    constexpr int vq = VT != B2_F16;
+    const int cb = (int)kv_code_bytes(VT, hd);
     uint16_t v0 = 0;
     uint8_t v1 = 0;
-    if constexpr (VT == B2_Q8_0) {
-      v1 = vsrc[i];
-      if (i < (vb - hd) / 2) v0 = reinterpret_cast<const uint16_t*>(vsrc + hd)[i];
+    if constexpr (vq) {
+      if (i < cb) v1 = vsrc[i];
+      if (i < (vb - cb) / 2) v0 = reinterpret_cast<const uint16_t*>(vsrc + cb)[i];
     } else {
       v0 = reinterpret_cast<const uint16_t*>(vsrc)[i];
     }
     __syncthreads();
     kv_store<KT>(kdst, hd, i, y);
-    if constexpr (VT == B2_Q8_0) {
-      vdst[i] = v1;
-      if (i < (vb - hd) / 2) reinterpret_cast<uint16_t*>(vdst + hd)[i] = v0;
+    if constexpr (vq) {
+      if (i < cb) vdst[i] = v1;
+      if (i < (vb - cb) / 2) reinterpret_cast<uint16_t*>(vdst + cb)[i] = v0;
     } else {
       reinterpret_cast<uint16_t*>(vdst)[i] = v0;
     }
@@ -590,7 +673,7 @@ int launch_add_rmsnorm_q(float* x, const float* delta, const float* w, float* ou
 int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, const int32_t* pos, const int32_t* seq,
                    const float* rope, float* q_out, void* kc, int kt, void* vc, int vt, const KvSeqState* st, int n_seq,
                    int cap, cudaStream_t s) {
-  B2_CHECK_ARG(kv_type_ok(kt) && kv_type_ok(vt), "KV cache types must be F16 or Q8_0");
+  B2_CHECK_ARG(kv_type_ok(kt) && kv_type_ok(vt), "KV cache types must be F16, Q8_0 or Q4_0");
   B2_CHECK_ARG(hd % 32 == 0, "head_dim must be a multiple of 32");
   uint8_t* k8 = static_cast<uint8_t*>(kc);
   uint8_t* v8 = static_cast<uint8_t*>(vc);
@@ -600,8 +683,13 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
                       q_out, k8, v8, st, n_seq, cap);
   B2_ROPE_KV(B2_F16, B2_F16)
   B2_ROPE_KV(B2_F16, B2_Q8_0)
+  B2_ROPE_KV(B2_F16, B2_Q4_0)
   B2_ROPE_KV(B2_Q8_0, B2_F16)
   B2_ROPE_KV(B2_Q8_0, B2_Q8_0)
+  B2_ROPE_KV(B2_Q8_0, B2_Q4_0)
+  B2_ROPE_KV(B2_Q4_0, B2_F16)
+  B2_ROPE_KV(B2_Q4_0, B2_Q8_0)
+  B2_ROPE_KV(B2_Q4_0, B2_Q4_0)
 #undef B2_ROPE_KV
   return B2_ERR_INVALID;
 }
@@ -609,13 +697,14 @@ int launch_rope_kv(const float* qkv, int n_tok, int n_head, int n_kv, int hd, co
 int launch_kv_shift(void* kc, int kt, int n_kv, int hd, int seq, const KvSeqState& st, int cap, int p_begin, int p_end,
                     const RotTable& cs, cudaStream_t s) {
   B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
-  B2_CHECK_ARG(hd % 32 == 0 && kv_type_ok(kt), "KV shift: head_dim % 32 and an F16 or Q8_0 cache");
+  B2_CHECK_ARG(hd % 32 == 0 && kv_type_ok(kt), "KV shift: head_dim % 32 and an F16, Q8_0 or Q4_0 cache");
   if (p_end <= p_begin) return B2_OK;
   const int64_t quads = (int64_t)(p_end - p_begin) * n_kv * (hd / 4);
   B2_CHECK_ARG(quads < (int64_t)1 << 30, "KV shift range too large");
   const int grid = (int)std::min<int64_t>((quads + 255) / 256, 4 * kSMs);
   uint8_t* k8 = static_cast<uint8_t*>(kc);
   if (kt == B2_Q8_0) kv_shift_kernel<B2_Q8_0><<<grid, 256, 0, s>>>(k8, n_kv, hd, seq, st, cap, p_begin, p_end, cs);
+  else if (kt == B2_Q4_0) kv_shift_kernel<B2_Q4_0><<<grid, 256, 0, s>>>(k8, n_kv, hd, seq, st, cap, p_begin, p_end, cs);
   else kv_shift_kernel<B2_F16><<<grid, 256, 0, s>>>(k8, n_kv, hd, seq, st, cap, p_begin, p_end, cs);
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
@@ -624,7 +713,8 @@ int launch_kv_shift(void* kc, int kt, int n_kv, int hd, int seq, const KvSeqStat
 int launch_kv_compact(void* kc, int kt, void* vc, int vt, int n_kv, int hd, int seq, const KvSeqState& st, int cap,
                       int dst0, int src0, int n, const RotTable& cs, cudaStream_t s) {
   B2_CHECK_ARG(hd <= 2 * kRotPairs, "head_dim too large for the rotation table");
-  B2_CHECK_ARG(hd % 32 == 0 && kv_type_ok(kt) && kv_type_ok(vt), "KV compact: head_dim % 32, F16 or Q8_0 caches");
+  B2_CHECK_ARG(hd % 32 == 0 && kv_type_ok(kt) && kv_type_ok(vt),
+               "KV compact: head_dim % 32, F16, Q8_0 or Q4_0 caches");
   if (n <= 0) return B2_OK;
   uint8_t* k8 = static_cast<uint8_t*>(kc);
   uint8_t* v8 = static_cast<uint8_t*>(vc);
@@ -633,8 +723,13 @@ int launch_kv_compact(void* kc, int kt, void* vc, int vt, int n_kv, int hd, int 
     kv_compact_kernel<KT, VT><<<n_kv, hd, 0, s>>>(k8, v8, n_kv, hd, seq, st, cap, dst0, src0, n, cs);
   B2_COMPACT(B2_F16, B2_F16)
   B2_COMPACT(B2_F16, B2_Q8_0)
+  B2_COMPACT(B2_F16, B2_Q4_0)
   B2_COMPACT(B2_Q8_0, B2_F16)
   B2_COMPACT(B2_Q8_0, B2_Q8_0)
+  B2_COMPACT(B2_Q8_0, B2_Q4_0)
+  B2_COMPACT(B2_Q4_0, B2_F16)
+  B2_COMPACT(B2_Q4_0, B2_Q8_0)
+  B2_COMPACT(B2_Q4_0, B2_Q4_0)
 #undef B2_COMPACT
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;

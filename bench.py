@@ -907,9 +907,10 @@ def attn_measure(b2, n_seq: int, steps: int, kv_type: int = 1) -> dict:
     if kv_type == b2.F16:
         kv = rng.standard_normal(rows * ATTN_HD, dtype=np.float32).astype(np.float16).view(np.uint8)
     else:
+        cb = ATTN_HD if kv_type == b2.Q8_0 else ATTN_HD // 2      # code bytes of a row
         kv = np.zeros((rows, rb), np.uint8)
-        kv[:, :ATTN_HD] = rng.integers(-127, 128, (rows, ATTN_HD), dtype=np.int8).view(np.uint8)
-        kv[:, ATTN_HD:ATTN_HD + ATTN_HD // 16] = np.frombuffer(np.float16(0.01).tobytes() * (ATTN_HD // 32), np.uint8)
+        kv[:, :cb] = rng.integers(0, 256, (rows, cb), dtype=np.uint8)
+        kv[:, cb:cb + ATTN_HD // 16] = np.frombuffer(np.float16(0.01).tobytes() * (ATTN_HD // 32), np.uint8)
         kv = kv.ravel()
     ks = [b2.DeviceBuffer.from_array(kv) for _ in range(copies)]
     vs = [b2.DeviceBuffer.from_array(kv[::-1].copy()) for _ in range(copies)]
@@ -951,7 +952,7 @@ def attn_measure(b2, n_seq: int, steps: int, kv_type: int = 1) -> dict:
     stream.synchronize()
     ms_shift = e0.elapsed_ms(e1) / max(1, steps // 4)
     shift_bytes = n_seq * 2 * (ATTN_CTX - 1024) * ATTN_KV * rb
-    return {"batch": n_seq, "kv_type": "q8_0" if kv_type == b2.Q8_0 else "f16", "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes, "copies": copies,
+    return {"batch": n_seq, "kv_type": {b2.Q8_0: "q8_0", b2.Q4_0: "q4_0"}.get(kv_type, "f16"), "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes, "copies": copies,
             "shift_ms": ms_shift, "shift_gbs": shift_bytes / (ms_shift * 1e-3) / 1e9, "shift_bytes": shift_bytes}
 
 
@@ -959,12 +960,14 @@ def run_attn_ours(args, dist, rank, world, local):
     import b2gguf as b2
     b2.check(b2.lib.b2_set_device(local), "set_device")
     batches = (1, 4, 16) if args.attn_batch is None else (args.attn_batch,)
-    res = [attn_measure(b2, n, args.steps) for n in batches] if args.attn_kv != "q8_0" else []
-    # Milda's default cache type (Q8_0 K and V), the same batches
-    res_q8 = [attn_measure(b2, n, args.steps, b2.Q8_0) for n in batches] if args.attn_kv != "f16" else []
+    want = lambda t: args.attn_kv in ("all", t) or (args.attn_kv == "both" and t in ("f16", "q8_0"))
+    res = [attn_measure(b2, n, args.steps) for n in batches] if want("f16") else []
+    # Milda's default cache type (Q8_0 K and V) and its other one (Q4_0), the same batches
+    res_q8 = [attn_measure(b2, n, args.steps, b2.Q8_0) for n in batches] if want("q8_0") else []
+    res_q4 = [attn_measure(b2, n, args.steps, b2.Q4_0) for n in batches] if want("q4_0") else []
     peaks = measured_peaks()
-    big = (res or res_q8)[-1]
-    kvn = "fp16" if big["kv_type"] == "f16" else "Q8_0"
+    big = (res or res_q8 or res_q4)[-1]
+    kvn = {"f16": "fp16", "q8_0": "Q8_0", "q4_0": "Q4_0"}[big["kv_type"]]
     return {"metric": f"decode attention HBM GB/s (32 q / 8 kv heads, hd 128, ctx 4096, {kvn} KV)",
             "value": round(big["gbs"] * world, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 2,
             "ms_per_step": big["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -977,6 +980,7 @@ def run_attn_ours(args, dist, rank, world, local):
                          "algorithmic_bytes_per_launch": big["bytes"]},
             "batches": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()} for r in res],
             "batches_q8_0": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()} for r in res_q8],
+            "batches_q4_0": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()} for r in res_q4],
             "gpu_launches": args.steps * 3}
 
 
@@ -1234,8 +1238,8 @@ def main():
     ap.add_argument("--keep-model", action="store_true", help="keep the synthetic GGUF file after the run")
     ap.add_argument("--skip-1b", action="store_true", help="decode_8b_q4k: leave out the 1.1B Q4_0 (config 4) line")
     ap.add_argument("--attn-batch", type=int, default=None, help="attn: one batch size (default 1, 4 and 16)")
-    ap.add_argument("--attn-kv", default="both", choices=["both", "f16", "q8_0"],
-                    help="attn: KV cache types to time (default both)")
+    ap.add_argument("--attn-kv", default="all", choices=["all", "both", "f16", "q8_0", "q4_0"],
+                    help="attn: KV cache types to time (default all; both = f16 and q8_0)")
     ap.add_argument("--profile-range", action="store_true",
                     help="open the profiler range around the timed decode steps only")
     ap.add_argument("--qtype", default="q4_k", choices=sorted(TYPE_NAMES), help="gemv_op weight type")

@@ -269,19 +269,22 @@ B2_API int b2_attn_decode(const float* q, const uint16_t* k_cache, const uint16_
                           const int32_t* seq, int n_q, int n_seq, int n_head, int n_kv, int head_dim, int cap,
                           float* out, void* stream);
 
-/* KV caches of either type (B2_F16 or B2_Q8_0; llama.cpp's cache types,
+/* KV caches of any of llama.cpp's cache types (B2_F16, B2_Q8_0, B2_Q4_0;
  * Milda/src/engine.cpp:74-87).  Rows of one kv head at one slot,
  * [n_seq][n_kv][cap] rows per cache, b2_kv_row_bytes(type, head_dim) bytes
- * each: B2_F16 head_dim fp16 values; B2_Q8_0 head_dim int8 codes followed by
- * the head_dim/32 fp16 block scales, padded to head_dim + 16 bytes.
+ * each: B2_F16 head_dim fp16 values; B2_Q8_0 head_dim int8 codes, B2_Q4_0
+ * head_dim/2 bytes of 4-bit codes (block b's 16 bytes at 16·b, byte j: value
+ * j in the low nibble, value j+16 in the high one), each followed by the
+ * head_dim/32 fp16 block scales and padded to a multiple of 16 bytes.
  * Storing quantizes each 32-value block as ref_quantize_row_q8_0
- * (Singularity/tests/test_and_bench_a5.cpp:223-245).  Attention over a Q8_0
- * K quantizes each query head to Q8_0 and scores position t as
- * ref_vec_dot_q8_0_q8_0 (:205-221) of the K row and the query, times
- * 1/sqrt(hd); over a Q8_0 V it sums p_t·(d·q) with the dequantized values
- * (exact in fp32); everything else as b2_attn_decode.  The shift
- * dequantizes, rotates and re-quantizes K.  head_dim a multiple of 32.
- * b2_kv_row_bytes returns 0 for other types. */
+ * (Singularity/tests/test_and_bench_a5.cpp:223-245) or ggml's
+ * quantize_row_q4_0_ref.  Attention over a Q8_0 or Q4_0 K quantizes each
+ * query head to Q8_0 (the dot type of both) and scores position t as
+ * ref_vec_dot_q8_0_q8_0 (:205-221) or ref_vec_dot_q4_0_q8_0 (:184-203) of the
+ * K row and the query, times 1/sqrt(hd); over a quantized V it sums
+ * p_t·(dequantized value) (exact in fp32); everything else as
+ * b2_attn_decode.  The shift dequantizes, rotates and re-quantizes K.
+ * head_dim a multiple of 32.  b2_kv_row_bytes returns 0 for other types. */
 B2_API int64_t b2_kv_row_bytes(int type, int head_dim);
 B2_API int b2_rope_kv_store_typed(const float* qkv, int n_tok, int n_seq, int n_head, int n_kv, int head_dim,
                                   const int32_t* pos, const int32_t* seq, const float* rope, float* q_out,
@@ -406,9 +409,10 @@ typedef struct b2_context_params {
                              CPU matmul_quantized's) instead of the decode GEMV's tile order;
                              the last 8 tokens take the decode step. */
     int32_t type_k;       /* K cache type (llama_context_params.type_k, set from Milda's
-                             cache_type_k at Milda/src/engine.cpp:1195): B2_F16 (default) or
-                             B2_Q8_0 */
-    int32_t type_v;       /* V cache type (type_v, :1196): B2_F16 (default) or B2_Q8_0 */
+                             cache_type_k at Milda/src/engine.cpp:1195): B2_F16 (default),
+                             B2_Q8_0 or B2_Q4_0 */
+    int32_t type_v;       /* V cache type (type_v, :1196): B2_F16 (default), B2_Q8_0 or
+                             B2_Q4_0 */
 } b2_context_params;
 
 /* llama_context_default_params / llama_init_from_model

@@ -1,10 +1,11 @@
-"""Q8_0 KV cache (Milda's default cache_type_k / cache_type_v,
-Milda/include/milda/engine.hpp:85-86) on the GPU against the oracle, through
-the C ABI.
+"""Quantized KV caches (Milda's default cache_type_k / cache_type_v is Q8_0,
+Milda/include/milda/engine.hpp:85-86; Q4_0 is its other choice) on the GPU
+against the oracle, through the C ABI.
 
-Rows are stored with the reference's Q8_0 quantizer; attention over a Q8_0 K
-quantizes the query to Q8_0 and scores with the reference's Q8_0·Q8_0 block
-dot; a Q8_0 V is dequantized (d·q, exact) before the reference-order P·V;
+Rows are stored with the reference's Q8_0 quantizer or ggml's Q4_0 one;
+attention over a quantized K quantizes the query to Q8_0 and scores with the
+reference's Q8_0·Q8_0 or Q4_0·Q8_0 block dot; a quantized V is dequantized
+(exact) before the reference-order P·V;
 the shift dequantizes, rotates and re-quantizes K.  Everything is checked bit
 for bit: stored rows, attention outputs, shifted rows, and model logits over
 prefill, greedy decode, batched sequences, the in-place and compacting KV
@@ -18,7 +19,9 @@ pytestmark = pytest.mark.gpu
 
 b2 = pytest.importorskip("b2gguf")
 
-TYPES = [(b2.Q8_0, b2.Q8_0), (b2.F16, b2.Q8_0), (b2.Q8_0, b2.F16)]
+TYPES = [(b2.Q8_0, b2.Q8_0), (b2.F16, b2.Q8_0), (b2.Q8_0, b2.F16), (b2.Q4_0, b2.Q4_0), (b2.Q4_0, b2.Q8_0),
+         (b2.F16, b2.Q4_0)]
+CODE_BYTES = {b2.Q8_0: 32, b2.Q4_0: 16}   # per 32-value block
 
 
 def _bits(a):
@@ -34,16 +37,16 @@ def row_bytes(t, hd):
 
 
 def to_gpu_rows(t, rows, hd):
-    """Oracle rows (fp16 bits, or ggml Q8_0 blocks) -> the cache's rows
-    (codes, then the block scales, zero padding)."""
+    """Oracle rows (fp16 bits, or ggml Q8_0 / Q4_0 blocks) -> the cache's
+    rows (codes, then the block scales, zero padding)."""
     rows = np.ascontiguousarray(rows, np.uint8)
     if t == b2.F16:
         return rows
-    nb = hd // 32
-    blk = rows.reshape(rows.shape[:-1] + (nb, 34))
-    out = np.zeros(rows.shape[:-1] + (hd + 16,), np.uint8)
-    out[..., :hd] = blk[..., 2:].reshape(rows.shape[:-1] + (hd,))
-    out[..., hd:hd + 2 * nb] = blk[..., :2].reshape(rows.shape[:-1] + (2 * nb,))
+    nb, cb = hd // 32, CODE_BYTES[t]
+    blk = rows.reshape(rows.shape[:-1] + (nb, 2 + cb))
+    out = np.zeros(rows.shape[:-1] + (row_bytes(t, hd),), np.uint8)
+    out[..., :nb * cb] = blk[..., 2:].reshape(rows.shape[:-1] + (nb * cb,))
+    out[..., nb * cb:nb * cb + 2 * nb] = blk[..., :2].reshape(rows.shape[:-1] + (2 * nb,))
     return out
 
 
@@ -51,11 +54,11 @@ def to_oracle_rows(t, rows, hd):
     rows = np.ascontiguousarray(rows, np.uint8)
     if t == b2.F16:
         return rows
-    nb = hd // 32
-    blk = np.zeros(rows.shape[:-1] + (nb, 34), np.uint8)
-    blk[..., 2:] = rows[..., :hd].reshape(rows.shape[:-1] + (nb, 32))
-    blk[..., :2] = rows[..., hd:hd + 2 * nb].reshape(rows.shape[:-1] + (nb, 2))
-    return blk.reshape(rows.shape[:-1] + (nb * 34,))
+    nb, cb = hd // 32, CODE_BYTES[t]
+    blk = np.zeros(rows.shape[:-1] + (nb, 2 + cb), np.uint8)
+    blk[..., 2:] = rows[..., :nb * cb].reshape(rows.shape[:-1] + (nb, cb))
+    blk[..., :2] = rows[..., nb * cb:nb * cb + 2 * nb].reshape(rows.shape[:-1] + (nb, 2))
+    return blk.reshape(rows.shape[:-1] + (nb * (2 + cb),))
 
 
 def random_cache(rng, t, n_seq, n_kv, cap, hd):
@@ -102,7 +105,7 @@ def test_rope_kv_store_rows_bit_exact(kt, vt, n_head, n_kv, hd):
     (1, 1, 4, 2, 64), (3, 300, 32, 4, 64), (1, 4096, 32, 8, 128), (16, 4096, 32, 8, 128), (2, 129, 16, 8, 64),
     (5, 700, 8, 8, 128), (2, 2049, 32, 4, 64)])
 def test_attn_decode_typed_matches_oracle(kt, vt, n_q, n_pos, n_head, n_kv, hd):
-    if (kt, vt) != (b2.Q8_0, b2.Q8_0) and n_q * n_pos > 8192:
+    if kt != vt and n_q * n_pos > 8192:
         pytest.skip("mixed types are covered at the smaller shapes")
     rng = np.random.default_rng(n_pos + 7 * kt + vt)
     cap = max(n_pos, 64)
@@ -124,19 +127,20 @@ def test_attn_decode_typed_matches_oracle(kt, vt, n_q, n_pos, n_head, n_kv, hd):
         assert np.array_equal(_bits(got[i]), _bits(want)), f"query {i}: not bit-exact with the oracle"
 
 
+@pytest.mark.parametrize("kt", [b2.Q8_0, b2.Q4_0])
 @pytest.mark.parametrize("delta", [-1024, 5])
-def test_kv_shift_q8_0_bit_exact(delta):
+def test_kv_shift_quantized_bit_exact(kt, delta):
     rng = np.random.default_rng(4)
     n_seq, n_kv, cap, hd, theta = 2, 8, 2048, 128, 500000.0
-    kc = random_cache(rng, b2.Q8_0, n_seq, n_kv, cap, hd)
+    kc = random_cache(rng, kt, n_seq, n_kv, cap, hd)
     kd = _dev(kc)
     p0, p1 = 512, 2048
-    b2.check(b2.lib.b2_kv_shift_k_typed(kd.ptr, b2.Q8_0, 1, n_kv, hd, cap, p0, p1, delta, np.float32(theta), None))
+    b2.check(b2.lib.b2_kv_shift_k_typed(kd.ptr, kt, 1, n_kv, hd, cap, p0, p1, delta, np.float32(theta), None))
     got = kd.download(np.uint8).reshape(kc.shape)
     assert np.array_equal(got[0], kc[0])
     assert np.array_equal(got[1, :, :p0], kc[1, :, :p0])
-    want = O.kv_shift_k_typed(oracle_view(b2.Q8_0, kc, 1, cap, hd)[p0:p1], b2.Q8_0, p1 - p0, n_kv, hd, delta, theta)
-    assert np.array_equal(oracle_view(b2.Q8_0, got, 1, cap, hd)[p0:p1], want)
+    want = O.kv_shift_k_typed(oracle_view(kt, kc, 1, cap, hd)[p0:p1], kt, p1 - p0, n_kv, hd, delta, theta)
+    assert np.array_equal(oracle_view(kt, got, 1, cap, hd)[p0:p1], want)
 
 
 # ---- model level ----------------------------------------------------------------------------
@@ -191,17 +195,18 @@ def test_model_decode_q8_0_cache_bit_exact(model_file, kt, vt):
         pos += 1
 
 
+@pytest.mark.parametrize("kvt", [b2.Q8_0, b2.Q4_0])
 @pytest.mark.parametrize("n_keep", [0, 4])
-def test_model_kv_shift_q8_0_bit_exact(model_file, n_keep):
+def test_model_kv_shift_quantized_bit_exact(model_file, n_keep, kvt):
     """Milda's in-place shift over a Q8_0 cache: the ring path (n_keep 0)
     and the compacting path (n_keep 4) re-quantize the rotated K rows as the
     oracle does."""
     rng = np.random.default_rng(2)
     om = O.Model(model_file)
-    om.set_kv_types(b2.Q8_0, b2.Q8_0)
+    om.set_kv_types(kvt, kvt)
     om.init_cache(1, 64)
     gm = b2.Model(model_file)
-    ctx = b2.Context(gm, n_ctx=64, n_seq=1, type_k=b2.Q8_0, type_v=b2.Q8_0)
+    ctx = b2.Context(gm, n_ctx=64, n_seq=1, type_k=kvt, type_v=kvt)
     toks = rng.integers(0, om.vocab, 40).tolist()
     ctx.decode(toks, want_logits=2)
     for p, t in enumerate(toks):

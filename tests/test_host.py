@@ -61,11 +61,13 @@ def test_context_default_params():
 
 
 def test_kv_row_bytes():
-    """Cache rows: fp16 values, or Q8_0 codes + block scales padded to
-    head_dim + 16 bytes; other types are refused (0)."""
+    """Cache rows: fp16 values, or Q8_0 / Q4_0 codes + block scales padded
+    to a multiple of 16 bytes; other types are refused (0)."""
     assert b2.lib.b2_kv_row_bytes(b2.F16, 128) == 256
     assert b2.lib.b2_kv_row_bytes(b2.Q8_0, 128) == 144
     assert b2.lib.b2_kv_row_bytes(b2.Q8_0, 64) == 80
+    assert b2.lib.b2_kv_row_bytes(b2.Q4_0, 128) == 80
+    assert b2.lib.b2_kv_row_bytes(b2.Q4_0, 64) == 48
     assert b2.lib.b2_kv_row_bytes(b2.Q4_K, 128) == 0
 
 
