@@ -1217,6 +1217,36 @@ def run_moe_ours(args, dist, rank, world, local):
             "gpu_launches": args.steps * q["launches_per_token"]}
 
 
+def run_sampler_ours(args, dist, rank, world, local):
+    """One draw of Milda's sampler chain (penalties over 64, top-k 40, top-p
+    0.9, min-p 0.05, temperature 0.75, dist) over a 128256-entry logits row
+    on the device: b2_sampler_sample_logits per step (two kernels, the token
+    read back), the penalty window full, host wall clock per draw."""
+    import b2gguf as b2
+    b2.check(b2.lib.b2_set_device(local), "set_device")
+    path = model_path("sampler_tiny")
+    b2.write_synthetic_llama(path, 1, 256, 512, 4, 2, 512, b2.Q8_0, embd_type=b2.Q8_0, out_type=b2.Q8_0, seed=3)
+    m = b2.Model(path)
+    ctx = b2.Context(m, n_ctx=32, n_seq=1)
+    sm = b2.Sampler(ctx)
+    nv = 128256
+    rng = np.random.default_rng(5)
+    rows = [b2.DeviceBuffer.from_array((rng.standard_normal(nv) * 3).astype(np.float32)) for _ in range(8)]
+    for i in range(max(args.warmup, 3) + 64):
+        sm.accept(sm.sample_logits(rows[i % 8].ptr, nv))
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        sm.sample_logits(rows[i % 8].ptr, nv)
+    us = (time.perf_counter() - t0) / args.steps * 1e6
+    del sm, ctx, m
+    os.remove(path)
+    return {"metric": "sampler chain draw latency (128256-entry logits, Milda's chain)", "value": round(us, 2),
+            "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32 logits",
+            "data": "synthetic: logits N(0,3) seed 5, 8 rows rotating", "config": {"workload": "sampler"},
+            "gpu_launches": 2 * args.steps, "timing": "host wall clock per b2_sampler_sample_logits (synchronous)"}
+
+
 WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
              "gemv_q4_0": (run_gemv_ours, run_gemv_reference),
              "decode_1b_q4_0": (run_decode1b_ours, None),
@@ -1224,7 +1254,8 @@ WORKLOADS = {"decode_8b_q4k": (run_decode_ours, run_decode_reference),
              "gemm_q4k": (run_gemm_ours, run_gemm_reference),
              "gemm_q8_0": (run_gemm_ours, run_gemm_reference),
              "attn": (run_attn_ours, None),
-             "moe": (run_moe_ours, None)}
+             "moe": (run_moe_ours, None),
+             "sampler": (run_sampler_ours, None)}
 
 
 def main():
