@@ -585,6 +585,10 @@ def run_decode_ours(args, dist, rank, world, local):
     progress("sampled steps")
     samplers = [b2.Sampler(ctx, seed=42 + i) for i in range(BATCH)]
     rewind()
+    ctx.generate_sampled(samplers, start_tok, 2, seq=seqs)    # untimed: the sampled step's graph is captured
+    rewind()
+    for sm in samplers:
+        sm.reset()
     barrier(dist)
     e0.record(ctx.stream)
     ctx.generate_sampled(samplers, start_tok, args.steps, seq=seqs)
