@@ -116,6 +116,7 @@ def _bind() -> None:
         "b2_get_argmax": (_i, [_vp, _vp, _vp, _vp, ctypes.c_int32]),
         "b2_generate": (_i, [_vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp]),
         "b2_context_exchange_wait_ns": (_i, [_vp, _vp, ctypes.c_int32]),
+        "b2_get_last_rows": (_i, [_vp, _vp]),
         "b2_sampler_default_params": (None, [_vp]),
         "b2_sampler_create": (_i, [_vp, _vp, _vp]),
         "b2_sampler_free": (_i, [_vp]),
@@ -550,7 +551,9 @@ class Context:
         rc = lib.b2_decode(self.h, ptr(t), ptr(pp) if pp is not None else None, ptr(ss) if ss is not None else None,
                            t.size, want_logits)
         check(rc, "decode")
-        self.last_n = min(t.size, 8) if t.size <= 8 else (t.size - 1) % 8 + 1
+        n = ctypes.c_int32()
+        check(lib.b2_get_last_rows(self.h, ctypes.byref(n)), "get_last_rows")
+        self.last_n = n.value if n.value else min(t.size, 8)
         return rc
 
     def logits(self, i: int = -1) -> np.ndarray:

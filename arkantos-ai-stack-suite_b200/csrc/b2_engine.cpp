@@ -1471,6 +1471,12 @@ int b2_context_exchange_wait_ns(b2_context* c, uint64_t* ns, int32_t reset) {
   return B2_OK;
 }
 
+int b2_get_last_rows(b2_context* c, int32_t* n) {
+  B2_CHECK_ARG(c && n, "get_last_rows arguments");
+  *n = c->last_logits ? c->last_n : 0;
+  return B2_OK;
+}
+
 int b2_synchronize_context(b2_context* c) {
   B2_CHECK_ARG(c, "context");
   B2_CUDA_TRY(cudaStreamSynchronize(c->stream));

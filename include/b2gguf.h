@@ -442,6 +442,11 @@ B2_API int b2_get_logits(b2_context* c, int32_t i, float* out, int64_t n);
 /* Greedy pick on the device for every logits row of that step: token id,
  * top-1 logit and top-1 − top-2 margin (NULL outputs are skipped). */
 B2_API int b2_get_argmax(b2_context* c, int32_t* ids, float* top1, float* margin, int32_t n);
+/* Logits rows of that step (the rows b2_get_argmax fills; 0 when the last
+ * decode computed no logits).  A call's tokens run in steps of up to 8, and a
+ * long prompt's first tokens may run through the prefill GEMMs, so the last
+ * step holds the call's last 1-8 tokens. */
+B2_API int b2_get_last_rows(b2_context* c, int32_t* n);
 /* Greedy generation with the loop on the device.  No llama.cpp counterpart:
  * it is the device-resident form of Milda's greedy turn loop, llama_decode of
  * one token → llama_get_logits_ith → pick → feed (Milda/src/engine.cpp:1962-2117),
