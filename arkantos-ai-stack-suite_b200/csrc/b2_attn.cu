@@ -673,13 +673,19 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
             const uint8_t* rc = sp + t * DSL;
             const uint16_t* rs = reinterpret_cast<const uint16_t*>(sp + CH * DSL) + t * 8;
 #pragma unroll
-            for (int k = 0; k < DS / 2; ++k) {
-              const int dd = d0 + 2 * k, e = dd & 31;
+            for (int c = 0; c < DS / 8; ++c) {   // 8 dims: 8 bytes, one half of a block
+              const int dd = d0 + 8 * c, e = dd & 31;
               const int bo = ((dd >> 5) - (d0 >> 5)) * 16 + (e & 15);
               const int sh = (e & 16) ? 4 : 0;
               const float d = h2f(rs[dd >> 5]);
-              const int c0 = (rc[bo] >> sh) & 15, c1 = (rc[bo + 1] >> sh) & 15;
-              vp[k * kPvChP + t] = pack2(__fmul_rn((float)(c0 - 8), d), __fmul_rn((float)(c1 - 8), d));
+              const uint2 w = *reinterpret_cast<const uint2*>(rc + bo);
+              const uint32_t ww[2] = {(w.x >> sh) & 0x0F0F0F0Fu, (w.y >> sh) & 0x0F0F0F0Fu};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t h = ww[k >> 1] >> (16 * (k & 1));
+                vp[(4 * c + k) * kPvChP + t] = pack2(__fmul_rn((float)((int)(h & 0xFFu) - 8), d),
+                                                     __fmul_rn((float)((int)((h >> 8) & 0xFFu) - 8), d));
+              }
             }
           } else {
             const uint4* rv = reinterpret_cast<const uint4*>(sp);   // [CH][DS/8] raw V
