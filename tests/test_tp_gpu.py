@@ -100,8 +100,8 @@ def test_tp2_lost_peer_times_out(tmp_path):
     """Failure detection without a GPU fault: rank 1 skips a decode step while
     staying alive with its exchange buffer mapped (NVLS off, plain peer
     stores and flag loads).  Rank 0's exchange waits, bounded to 2 s of wall
-    time, expire; its b2_decode returns B2_ERR_TIMEOUT and both processes end
-    normally."""
+    time, expire; the step's synchronization returns B2_ERR_TIMEOUT and both
+    processes end normally."""
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
     L, d, ff, nh, nkv, V, wt, ot, theta = MODELS["q4_0_hd64"]

@@ -56,9 +56,10 @@ def main() -> int:
 def skip_step(rank: int, ctx, out: str) -> int:
     """A lost peer, made on the host: both ranks run the prompt; then rank 0
     decodes one more token while rank 1 skips it, alive and with its
-    exchange buffer mapped.  Rank 0's bounded exchange waits run out and its
-    b2_decode returns B2_ERR_TIMEOUT; rank 1 then exits between steps, with
-    nothing of its own in flight."""
+    exchange buffer mapped.  Rank 0's bounded exchange waits run out and the
+    step's synchronization (b2_decode is asynchronous) returns
+    B2_ERR_TIMEOUT; rank 1 then exits between steps, with nothing of its own
+    in flight."""
     ctx.decode(PROMPT, want_logits=2)
     ctx.synchronize()
     done = out + ".done"
@@ -69,6 +70,8 @@ def skip_step(rank: int, ctx, out: str) -> int:
         seq = np.array([0], np.int32)
         t0 = time.time()
         rc = b2.lib.b2_decode(ctx.h, b2.ptr(toks), b2.ptr(pos), b2.ptr(seq), 1, 1)
+        if rc == 0:   # the step runs asynchronously; its status comes with the synchronization
+            rc = b2.lib.b2_synchronize_context(ctx.h)
         secs = time.time() - t0
         with open(done, "w") as f:
             f.write("1")
