@@ -29,9 +29,9 @@
 //     kSampSlice logits into shared memory, applies the penalties of the
 //     window tokens that fall into it, sorts (logit, id) keys with a bitonic
 //     network and writes its best min(k, slice) keys;
-//   * sample_chain_kernel: one CTA per row sorts the slices' keys, keeps the
-//     top k and runs the rest of the chain on one thread (k <= 256 values),
-//     accepts the token and feeds the next step.
+//   * sample_chain_kernel: one CTA per row merges the slices' sorted keys
+//     into the top k (one warp), runs the rest of the chain on one thread
+//     (k <= 256 values), accepts the token and feeds the next step.
 #include <float.h>
 
 #include "b2_common.cuh"
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(256) sample_chain_kernel(int n_tok, int row0, 
                                                            SamplerDev* const* sps,
                                                            const unsigned long long* __restrict__ keys,
                                                            int32_t* __restrict__ ids, GreedyFeed feed) {
-  extern __shared__ unsigned long long mk[];   // [np * kSampTopKMax rounded up to a power of two]
+  extern __shared__ unsigned long long mk[];   // [np][kk]: each slice's best keys, largest first
   __shared__ float cl[kSampTopKMax], cp[kSampTopKMax];
   __shared__ int ci[kSampTopKMax];
   __shared__ unsigned long long tab[32];
@@ -196,19 +196,38 @@ __global__ void __launch_bounds__(256) sample_chain_kernel(int n_tok, int row0, 
   exp_table_to_smem(tab, threadIdx.x, blockDim.x);
   const int kk = k_eff(*sp);
   const int per = (n_vocab + np - 1) / np;
-  int nk = 1;
-  while (nk < np * kk) nk <<= 1;
-  for (int t = threadIdx.x; t < nk; t += blockDim.x) {
+  for (int t = threadIdx.x; t < np * kk; t += blockDim.x) {
     const int part = t / kk, j = t - part * kk;
     const int len = max(0, min(n_vocab, part * per + per) - part * per);
-    mk[t] = (t < np * kk && j < len) ? __ldcg(keys + ((int64_t)i * kSampParts + part) * kSampTopKMax + j) : 0ull;
+    mk[t] = j < len ? __ldcg(keys + ((int64_t)i * kSampParts + part) * kSampTopKMax + j) : 0ull;
   }
   __syncthreads();
-  bitonic_desc(mk, nk);
+  // The K largest keys by merging the slices' sorted lists: warp 0's lane l
+  // watches the heads of slices l and l + 32; each round the largest head
+  // (keys are distinct: they carry the token id) is taken and its list
+  // advances.  The same K keys, in the same order, as sorting them all.
   const int K = min(kk, n_vocab);
-  for (int t = threadIdx.x; t < K; t += blockDim.x) {
-    cl[t] = key_logit(mk[t]);
-    ci[t] = key_id(mk[t]);
+  if ((threadIdx.x >> 5) == 0) {
+    const int lane = threadIdx.x & 31, pa = lane, pb = lane + 32;
+    int ha = 0, hb = 0;
+    for (int j = 0; j < K; ++j) {
+      const unsigned long long a = (pa < np && ha < kk) ? mk[pa * kk + ha] : 0ull;
+      const unsigned long long c = (pb < np && hb < kk) ? mk[pb * kk + hb] : 0ull;
+      unsigned long long best = a > c ? a : c;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      if (best != 0ull) {
+        if (best == a) ++ha;
+        else if (best == c) ++hb;
+      }
+      if (lane == 0) {
+        cl[j] = key_logit(best);
+        ci[j] = key_id(best);
+      }
+    }
   }
   __syncthreads();
   // thread 0 runs the chain up to the draw; the CTA then takes the two
@@ -330,9 +349,7 @@ int launch_sample(const float* logits, int n_tok, int row0, int n, int n_vocab, 
   int rc = launch_pdl(sample_slices_kernel, dim3(np, n), dim3(256), 0, s, logits, n_tok, row0, n_vocab, v_local, sps,
                       keys);
   if (rc) return rc;
-  size_t nk = 1;
-  while (nk < (size_t)np * kSampTopKMax) nk <<= 1;
-  const size_t smem = nk * 8;
+  const size_t smem = (size_t)np * kSampTopKMax * 8;
   static bool attr_set = false;   // per process: the attribute is per function, not per device
   if (!attr_set) {
     B2_CUDA_TRY(cudaFuncSetAttribute(sample_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
