@@ -433,7 +433,11 @@ B2_API int  b2_context_stream(b2_context* c, void** stream);
  * sequence seq[i] (pos/seq NULL = next position of sequence 0).  Each token
  * must extend its sequence at its next position.  want_logits: 0 none,
  * 1 every token, 2 the last token of the call.  Returns 1 when a sequence is
- * full (no KV slot), 2 when the abort callback asked to stop. */
+ * full (no KV slot), 2 when the abort callback asked to stop.  The steps run
+ * asynchronously on the context stream: a device-side failure of a step (an
+ * expired tensor-parallel exchange wait: B2_ERR_TIMEOUT) is returned by the
+ * next call that synchronizes (b2_get_logits, b2_get_argmax,
+ * b2_synchronize_context, b2_sampler_sample). */
 B2_API int b2_decode(b2_context* c, const int32_t* tokens, const int32_t* pos, const int32_t* seq,
                      int32_t n_tokens, int32_t want_logits);
 /* llama_get_logits_ith (Milda/src/engine.cpp:2019, Sutra/src/llm_backends.cpp:3335):
