@@ -1395,7 +1395,7 @@ int b2_sampler_sample(b2_sampler* sm, int32_t idx, int32_t* token) {
   B2_CUDA_TRY(cudaMemcpyAsync(c->res_h, c->ids + idx, 4, cudaMemcpyDeviceToHost, c->stream));
   B2_CUDA_TRY(cudaStreamSynchronize(c->stream));
   *token = c->res_h[0];
-  return B2_OK;
+  return check_status(c);
 }
 
 int b2_sampler_sample_logits(b2_sampler* sm, const float* logits, int32_t n_vocab, int32_t* token) {
