@@ -30,8 +30,9 @@
 //     window tokens that fall into it, sorts (logit, id) keys with a bitonic
 //     network and writes its best min(k, slice) keys;
 //   * sample_chain_kernel: one CTA per row merges the slices' sorted keys
-//     into the top k (one warp), runs the rest of the chain on one thread
-//     (k <= 256 values), accepts the token and feeds the next step.
+//     into the top k (one warp), runs the rest of the chain on one warp
+//     (elementwise steps on the lanes, every sum in order on lane 0; k <= 256
+//     values), accepts the token and feeds the next step.
 #include <float.h>
 
 #include "b2_common.cuh"
@@ -169,16 +170,19 @@ __device__ void ring_push(SamplerDev* s, int32_t tok) {
   }
 }
 
-// softmax_impl over c[0..n) (sorted, largest first): p = expf(l − l_0)
-// summed in order, then each p divided by the sum.
-__device__ void softmax_sorted(const float* l, float* p, int n, const unsigned long long* tab) {
+// softmax_impl over l[0..n) (sorted, largest first) by one warp: p =
+// expf(l − l_0) on the lanes, their sum in order on lane 0, then each p
+// divided by the sum on the lanes.
+__device__ void softmax_sorted_warp(const float* l, float* p, int n, const unsigned long long* tab, int lane) {
   const float mx = l[0];
+  for (int i = lane; i < n; i += 32) p[i] = b2_expf_ref(__fsub_rn(l[i], mx), tab);
+  __syncwarp();
   float sum = 0.0f;
-  for (int i = 0; i < n; ++i) {
-    p[i] = b2_expf_ref(__fsub_rn(l[i], mx), tab);
-    sum = __fadd_rn(sum, p[i]);
-  }
-  for (int i = 0; i < n; ++i) p[i] = __fdiv_rn(p[i], sum);
+  if (lane == 0)
+    for (int i = 0; i < n; ++i) sum = __fadd_rn(sum, p[i]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  for (int i = lane; i < n; i += 32) p[i] = __fdiv_rn(p[i], sum);
+  __syncwarp();
 }
 
 __global__ void __launch_bounds__(256) sample_chain_kernel(int n_tok, int row0, int n_vocab, int np,
@@ -230,39 +234,54 @@ __global__ void __launch_bounds__(256) sample_chain_kernel(int n_tok, int row0, 
     }
   }
   __syncthreads();
-  // thread 0 runs the chain up to the draw; the CTA then takes the two
-  // generator words the draw needs (twisting the state when it runs out)
+  // warp 0 runs the chain up to the draw (its elementwise expf, divisions
+  // and comparisons over the candidates spread on the lanes, every sum on
+  // lane 0 in candidate order); the CTA then takes the two generator words
+  // the draw needs (twisting the state when it runs out)
   __shared__ int s_size;
   __shared__ uint32_t s_r[2];
   __shared__ uint32_t smt[kMtN];
-  if (threadIdx.x == 0) {
+  if ((threadIdx.x >> 5) == 0) {
+    const int lane = threadIdx.x & 31;
     int size = 0;
     if (sp->temp > 0.0f) {
       size = K;
       if (sp->top_p > 0.0f && sp->top_p < 1.0f) {
-        softmax_sorted(cl, cp, size, tab);
-        float run = 0.0f;
+        softmax_sorted_warp(cl, cp, size, tab, lane);
+        // the shortest prefix whose running sum reaches top_p (lane 0)
         int last = size;
-        for (int t = 0; t < size; ++t) {
-          run = __fadd_rn(run, cp[t]);
-          if (run >= sp->top_p && t + 1 >= 1) {
-            last = t + 1;
+        if (lane == 0) {
+          float run = 0.0f;
+          for (int t = 0; t < size; ++t) {
+            run = __fadd_rn(run, cp[t]);
+            if (run >= sp->top_p && t + 1 >= 1) {
+              last = t + 1;
+              break;
+            }
+          }
+        }
+        size = __shfl_sync(0xffffffffu, last, 0);
+      }
+      if (sp->min_p > 0.0f) {
+        // the first candidate below the largest + logf(min_p) (candidates
+        // sorted: a ballot per group of 32)
+        const float min_logit = __fadd_rn(cl[0], sp->logf_min_p);
+        int cut = size;
+        for (int t0 = 1; t0 < size; t0 += 32) {
+          const int t = t0 + lane;
+          const unsigned below = __ballot_sync(0xffffffffu, t < size && cl[t] < min_logit);
+          if (below) {
+            cut = t0 + __ffs(below) - 1;
             break;
           }
         }
-        size = last;
+        size = cut;
       }
-      if (sp->min_p > 0.0f) {
-        const float min_logit = __fadd_rn(cl[0], sp->logf_min_p);
-        int t = 1;
-        for (; t < size; ++t)
-          if (cl[t] < min_logit) break;
-        size = t;
-      }
-      for (int t = 0; t < size; ++t) cl[t] = __fdiv_rn(cl[t], sp->temp);
-      softmax_sorted(cl, cp, size, tab);
+      for (int t = lane; t < size; t += 32) cl[t] = __fdiv_rn(cl[t], sp->temp);
+      __syncwarp();
+      softmax_sorted_warp(cl, cp, size, tab, lane);
     }
-    s_size = size;
+    if (lane == 0) s_size = size;
   }
   __syncthreads();
   if (s_size >= 2) {
@@ -290,29 +309,45 @@ __global__ void __launch_bounds__(256) sample_chain_kernel(int n_tok, int row0, 
     }
     __syncthreads();
   }
-  if (threadIdx.x != 0) return;
+  if ((threadIdx.x >> 5) != 0) return;
+  const int lane = threadIdx.x & 31;
   const int size = s_size;
   int pick = 0;
   if (size >= 2) {
-    double sum = 0.0;
-    for (int t = 0; t < size; ++t) sum = __dadd_rn(sum, (double)cp[t]);
-    double run = 0.0;
-    for (int t = 0; t < size; ++t) {
-      run = __dadd_rn(run, __ddiv_rn((double)cp[t], sum));
-      cum[t] = run;
+    // the GNU C++ library's discrete_distribution: the weights summed in
+    // double (lane 0, in order), each divided by the sum (lanes), running
+    // sums with the last set to 1 (lane 0), the first not below u
+    __shared__ double s_sum;
+    if (lane == 0) {
+      double sum = 0.0;
+      for (int t = 0; t < size; ++t) sum = __dadd_rn(sum, (double)cp[t]);
+      s_sum = sum;
     }
-    cum[size - 1] = 1.0;
-    double u = __ddiv_rn(__dadd_rn((double)s_r[0], __dmul_rn((double)s_r[1], 4294967296.0)), 18446744073709551616.0);
-    if (u >= 1.0) u = 1.0 - 1.1102230246251565e-16;   // nextafter(1, 0)
-    // the first running sum not below u among the first size-1
-    int lo = 0, hi = size - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (cum[mid] < u) lo = mid + 1;
-      else hi = mid;
+    __syncwarp();
+    const double sum = s_sum;
+    for (int t = lane; t < size; t += 32) cum[t] = __ddiv_rn((double)cp[t], sum);
+    __syncwarp();
+    if (lane == 0) {
+      double run = 0.0;
+      for (int t = 0; t < size; ++t) {
+        run = __dadd_rn(run, cum[t]);
+        cum[t] = run;
+      }
+      cum[size - 1] = 1.0;
+      double u =
+          __ddiv_rn(__dadd_rn((double)s_r[0], __dmul_rn((double)s_r[1], 4294967296.0)), 18446744073709551616.0);
+      if (u >= 1.0) u = 1.0 - 1.1102230246251565e-16;   // nextafter(1, 0)
+      // the first running sum not below u among the first size-1
+      int lo = 0, hi = size - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (cum[mid] < u) lo = mid + 1;
+        else hi = mid;
+      }
+      pick = lo;
     }
-    pick = lo;
   }
+  if (lane != 0) return;
   const int32_t tok = ci[pick];
   ring_push(sp, tok);   // llama_sampler_sample accepts the token it returns
   ids[b] = tok;
