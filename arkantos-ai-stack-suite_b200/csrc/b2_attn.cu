@@ -32,9 +32,9 @@
 //     bulk copies, in parts the chain starts on as each lands) and take
 //     1/l.  Then a loader warp brings each chunk of up to 128 positions in
 //     with one 2-D tensor copy of the V slice and one bulk copy of the E
-//     rows, turns V into fp32 and forms (p_t, p_t) = e_t·(1/l); the chain
+//     rows, turns V into fp32 pairs and forms p_t = e_t·(1/l); the chain
 //     warp's lane (head, dim pair) runs out += p_t·v_t over the positions in
-//     order with packed f32x2 operations.
+//     order as two scalar chains (one per dim).
 // Q8_0 caches (llama.cpp's cache type that Milda asks for by default,
 // Milda/src/engine.cpp:74-87, 1195-1196): rows of hd int8 codes then the
 // hd/32 fp16 block scales (kv_row_bytes).  With a Q8_0 K the CTA quantizes
@@ -90,17 +90,6 @@ __device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
 struct Ones {
   uint64_t one, neg_zero;
 };
-// The two halves of mul_add2: p = a·b (rounded), acc + p (rounded).
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b, const Ones& k) {
-  uint64_t p;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(a), "l"(b), "l"(k.neg_zero));
-  return p;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t acc, uint64_t p, const Ones& k) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(p), "l"(k.one), "l"(acc));
-  return r;
-}
 __device__ __forceinline__ uint64_t mul_add2(uint64_t acc, uint64_t a, uint64_t b, const Ones& k) {
   uint64_t p, r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(a), "l"(b), "l"(k.neg_zero));
@@ -472,15 +461,10 @@ __host__ __device__ constexpr size_t pv_rawv_bytes(int ds) {
 }
 template <int G, int VT>
 __host__ __device__ constexpr size_t pv_stage_bytes(int ds) {
-  // raw V | raw E [CH][GP] | V pairs [ds/2][CHP] | (p, p) pairs [G][CHP],
+  // raw V | raw E [CH][GP] | V pairs [ds/2][CHP] | p [G][2·CHP] floats,
   // rounded up to 128 bytes (the tensor copy's destination alignment)
   return (pv_rawv_bytes<VT>(ds) + (size_t)kPvCh * gp_of(G) * 4 + (size_t)(ds / 2) * kPvChP * 8 +
           (size_t)G * kPvChP * 8 + 127) / 128 * 128;
-}
-__device__ __forceinline__ uint64_t u64_of(uint32_t lo, uint32_t hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-  return r;
 }
 
 // l = Σ_t e_t in position order for lane g < G, over rows e[t * GP + g] of
@@ -527,9 +511,9 @@ __device__ __forceinline__ float sum_run(const float* e, int a, int b, float l) 
 // memory, in kSumParts parts on their own mbarriers, and warp 0's lanes
 // 0..G-1 add them in position order.  P.V phase: warp 1 issues each chunk's
 // V rows (one 2-D tensor copy of kPvCh rows x DS dims from the first slot of
-// a run) and E rows (one bulk copy) into a raw stage, converts V to fp32 and
-// forms (p, p) = e·(1/l) pairs; warp 0's lane (head g, dim pair j) runs out
-// += p_t·v_t over the positions in order.
+// a run) and E rows (one bulk copy) into a raw stage, converts V to fp32
+// pairs and forms p = e·(1/l); warp 0's lane (head g, dim pair j) runs out
+// += p_t·v_t over the positions in order, one scalar chain per dim.
 template <int HD, int G, int VT>
 __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__ pos, const int32_t* __restrict__ seq,
                                                      const __grid_constant__ CUtensorMap vmap,
@@ -646,9 +630,9 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
         uint8_t* sp = stages + si * SB;
         const float4* re = reinterpret_cast<const float4*>(sp + RAWV);  // [CH][GP/4] raw E
         uint64_t* vp = reinterpret_cast<uint64_t*>(sp + RAWV + CH * GP * 4);   // [DS/2][CHP]
-        uint64_t* pp = vp + (DS / 2) * kPvChP;                                // [G][CHP]
+        uint64_t* pp = vp + (DS / 2) * kPvChP;                                // p: [G][2·CHP] floats
         // lane t owns positions t, t + 32, ...: its V row becomes DS/2 pairs
-        // and its E row G pairs (p, p) = e·(1/l)
+        // and its E row G values p = e·(1/l)
         for (int t = lane; t < len; t += 32) {
           if constexpr (VT == B2_Q8_0) {
             // code · block scale, exact in fp32 (ggml's dequantize_row_q8_0)
@@ -705,8 +689,7 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               if (4 * c + k < G) {
-                const float pv = __fmul_rn(ev[k], inv[4 * c + k]);
-                pp[(4 * c + k) * kPvChP + t] = pack2(pv, pv);
+                reinterpret_cast<float*>(pp)[(4 * c + k) * 2 * kPvChP + t] = __fmul_rn(ev[k], inv[4 * c + k]);
               }
           }
         }
@@ -731,10 +714,10 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
     }
     return;
   }
-  // chain warp: lane = (head g, dim pair j)
+  // chain warp: lane = (head g, dim pair j), two scalar chains (dims 2j and
+  // 2j + 1): each product and each add one rounded fp32 operation
   const int g = lane / (DS / 2), j = lane - g * (DS / 2);
-  const Ones k2{pack2(one, one), pack2(neg_zero, neg_zero)};
-  uint64_t acc = 0ull;
+  float acc0 = 0.0f, acc1 = 0.0f;
   int p = 0;
   for (int c = 0; p < n_pos; ++c) {
     const int si = c % NS;
@@ -743,70 +726,90 @@ __global__ void __launch_bounds__(64) attn_pv_kernel(const int32_t* __restrict__
     if (ok) {
       const uint8_t* sp = stages + si * SB;
       const uint64_t* vr = reinterpret_cast<const uint64_t*>(sp + RAWV + CH * GP * 4) + j * kPvChP;
-      const uint64_t* pr = reinterpret_cast<const uint64_t*>(sp + RAWV + CH * GP * 4) + (DS / 2) * kPvChP + g * kPvChP;
-      // positions in groups of 8, two per 16-byte load, in two buffers that
-      // take turns: the next group's (p, v) are read while the current
-      // group's chain runs, with no register copies between the steps
+      const float* pf = reinterpret_cast<const float*>(reinterpret_cast<const uint64_t*>(sp + RAWV + CH * GP * 4) +
+                                                       (DS / 2) * kPvChP) +
+                        g * 2 * kPvChP;
+      // positions in groups of 8 (p four per 16-byte load, v pairs two), in
+      // two buffers that take turns: the next group is read while the
+      // current group's adds run
       const int len16 = len & ~15;
-      uint4 ap[4], av[4], bp[4], bv[4];
+      float4 ap[2], bp[2];
+      uint4 av[4], bv[4];
       if (len16 > 0) {
+        ap[0] = *reinterpret_cast<const float4*>(pf);
+        ap[1] = *reinterpret_cast<const float4*>(pf + 4);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          ap[k] = *reinterpret_cast<const uint4*>(pr + 2 * k);
-          av[k] = *reinterpret_cast<const uint4*>(vr + 2 * k);
-        }
+        for (int k = 0; k < 4; ++k) av[k] = *reinterpret_cast<const uint4*>(vr + 2 * k);
       }
       for (int t = 0; t < len16; t += 16) {
-        // the 8 products of the group first, then the 8 adds in position
-        // order with the next group's reads between them
-        uint64_t pa[8];
+        // the group's 16 products first, then its adds in position order
+        // with the next group's reads between them
+        float m0[8], m1[8];
+        {
+          const float pa[8] = {ap[0].x, ap[0].y, ap[0].z, ap[0].w, ap[1].x, ap[1].y, ap[1].z, ap[1].w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          pa[2 * k] = mul2(u64_of(ap[k].x, ap[k].y), u64_of(av[k].x, av[k].y), k2);
-          pa[2 * k + 1] = mul2(u64_of(ap[k].z, ap[k].w), u64_of(av[k].z, av[k].w), k2);
+          for (int k = 0; k < 4; ++k) {
+            m0[2 * k] = __fmul_rn(pa[2 * k], __uint_as_float(av[k].x));
+            m1[2 * k] = __fmul_rn(pa[2 * k], __uint_as_float(av[k].y));
+            m0[2 * k + 1] = __fmul_rn(pa[2 * k + 1], __uint_as_float(av[k].z));
+            m1[2 * k + 1] = __fmul_rn(pa[2 * k + 1], __uint_as_float(av[k].w));
+          }
         }
+        bp[0] = *reinterpret_cast<const float4*>(pf + t + 8);
+        bp[1] = *reinterpret_cast<const float4*>(pf + t + 12);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          bp[k] = *reinterpret_cast<const uint4*>(pr + t + 8 + 2 * k);
           bv[k] = *reinterpret_cast<const uint4*>(vr + t + 8 + 2 * k);
-          acc = add2(acc, pa[2 * k], k2);
-          acc = add2(acc, pa[2 * k + 1], k2);
+          acc0 = __fadd_rn(acc0, m0[2 * k]);
+          acc1 = __fadd_rn(acc1, m1[2 * k]);
+          acc0 = __fadd_rn(acc0, m0[2 * k + 1]);
+          acc1 = __fadd_rn(acc1, m1[2 * k + 1]);
         }
+        {
+          const float pb[8] = {bp[0].x, bp[0].y, bp[0].z, bp[0].w, bp[1].x, bp[1].y, bp[1].z, bp[1].w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          pa[2 * k] = mul2(u64_of(bp[k].x, bp[k].y), u64_of(bv[k].x, bv[k].y), k2);
-          pa[2 * k + 1] = mul2(u64_of(bp[k].z, bp[k].w), u64_of(bv[k].z, bv[k].w), k2);
+          for (int k = 0; k < 4; ++k) {
+            m0[2 * k] = __fmul_rn(pb[2 * k], __uint_as_float(bv[k].x));
+            m1[2 * k] = __fmul_rn(pb[2 * k], __uint_as_float(bv[k].y));
+            m0[2 * k + 1] = __fmul_rn(pb[2 * k + 1], __uint_as_float(bv[k].z));
+            m1[2 * k + 1] = __fmul_rn(pb[2 * k + 1], __uint_as_float(bv[k].w));
+          }
         }
         const int tn = t + 16 < len16 ? t + 16 : t;   // the last trip re-reads in range
+        ap[0] = *reinterpret_cast<const float4*>(pf + tn);
+        ap[1] = *reinterpret_cast<const float4*>(pf + tn + 4);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          ap[k] = *reinterpret_cast<const uint4*>(pr + tn + 2 * k);
           av[k] = *reinterpret_cast<const uint4*>(vr + tn + 2 * k);
-          acc = add2(acc, pa[2 * k], k2);
-          acc = add2(acc, pa[2 * k + 1], k2);
+          acc0 = __fadd_rn(acc0, m0[2 * k]);
+          acc1 = __fadd_rn(acc1, m1[2 * k]);
+          acc0 = __fadd_rn(acc0, m0[2 * k + 1]);
+          acc1 = __fadd_rn(acc1, m1[2 * k + 1]);
         }
       }
       // the last (fewer than 16) positions: all reads first, then the steps
       const int rem = len - len16;
-      uint64_t tp[16], tv[16];
+      float tp[16];
+      uint64_t tv[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
-        tp[k] = k < rem ? pr[len16 + k] : 0ull;
+        tp[k] = k < rem ? pf[len16 + k] : 0.0f;
         tv[k] = k < rem ? vr[len16 + k] : 0ull;
       }
 #pragma unroll
       for (int k = 0; k < 16; ++k)
-        if (k < rem) acc = mul_add2(acc, tp[k], tv[k], k2);
+        if (k < rem) {
+          acc0 = __fadd_rn(acc0, __fmul_rn(tp[k], __uint_as_float((uint32_t)tv[k])));
+          acc1 = __fadd_rn(acc1, __fmul_rn(tp[k], __uint_as_float((uint32_t)(tv[k] >> 32))));
+        }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[si]);
     p += len;
   }
-  float o0, o1;
-  unpack2(acc, o0, o1);
   float* op = out + ((int64_t)b * n_head + kh * G + g) * HD + d0 + 2 * j;
-  op[0] = o0;
-  op[1] = o1;
+  op[0] = acc0;
+  op[1] = acc1;
 }
 
 // The V cache as 2-D tensors over its rows ([n_seq*n_kv*cap rows]), boxes of
