@@ -512,7 +512,8 @@ typedef struct b2_sampler_params {
  * temperature 0.75, seed 42. */
 B2_API void b2_sampler_default_params(b2_sampler_params* p);
 /* llama_sampler_chain_init + _add (rebuild_sampler): a chain whose state
- * lives on the context's GPU and whose calls run on the context's stream. */
+ * lives on the context's GPU and whose calls run on the context's stream.
+ * Free a context's samplers before the context. */
 B2_API int  b2_sampler_create(b2_context* c, const b2_sampler_params* p, b2_sampler** out);
 B2_API int  b2_sampler_free(b2_sampler* s);                   /* llama_sampler_free   */
 /* llama_sampler_reset (Milda/src/engine.cpp:1693, 1710, 1839): empty window,
