@@ -118,13 +118,34 @@ __global__ void __launch_bounds__(256) sample_slices_kernel(const float* __restr
     }
   }
   __syncthreads();
+  const int kk = k_eff(*sp);
+  unsigned long long* dst = keys + ((int64_t)i * kSampParts + pi) * kSampTopKMax;
+  if (kk == 1) {
+    // greedy: the slice's largest key (a maximum: any order)
+    unsigned long long best = 0ull;
+    for (int t = threadIdx.x; t < len; t += blockDim.x) {
+      const unsigned long long k = make_key(sl[t], va + t);
+      best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = sk[w] > best ? sk[w] : best;
+      dst[0] = best;
+    }
+    pdl_launch_dependents();
+    return;
+  }
   int n2 = 1;
   while (n2 < len) n2 <<= 1;
   for (int t = threadIdx.x; t < n2; t += blockDim.x) sk[t] = t < len ? make_key(sl[t], va + t) : 0ull;
   __syncthreads();
   bitonic_desc(sk, n2);
-  const int kk = k_eff(*sp);
-  unsigned long long* dst = keys + ((int64_t)i * kSampParts + pi) * kSampTopKMax;
   for (int t = threadIdx.x; t < kk; t += blockDim.x) dst[t] = t < len ? sk[t] : 0ull;
   pdl_launch_dependents();
 }
