@@ -105,6 +105,11 @@ struct GemvP {
   // the CTAs split into n_mat equal sets, set i over matrix i's tiles only,
   // so each CTA quantizes the one input its items need.  0: one shared x.
   int64_t x_mat_stride;
+  // Row-fold form (gemv_rows_kernel): rows of the terms table per token
+  // (8 x the most tiles a CTA takes), floats per table row, and the bytes of
+  // the CTA's weights in shared memory.
+  int rf_rows, rf_stride;
+  uint32_t rf_w_bytes;
 };
 
 // Weights and output of matrix mi of the launch.  Expert ids outside
@@ -181,39 +186,69 @@ __device__ void quantize_image(const float* __restrict__ x, int64_t x_stride, in
                                int64_t tid, int64_t nthreads) {
   const int nu = img.nu;
   if (img.type == B2_Q4_0 || img.type == B2_Q8_0) {
-    // One 32-value block per thread: eight float4 loads in flight, then the
-    // reference quantizer on registers.
-    for (int64_t i = tid; i < (int64_t)n_tok * nu; i += nthreads) {
-      const int t = (int)(i / nu), b = (int)(i - (int64_t)t * nu);
-      uint32_t w[8];
-      int sum = 0;
+    // One 32-value block per 8 lanes, one float4 per lane; the block's amax
+    // and code sum by xor shuffles inside the 8 lanes (max and integer sums
+    // are exact in any order, and every code is the reference quantizer's
+    // own formula).  Each round loads four float4s per lane before any
+    // arithmetic.  Rounds are warp-uniform: tid and nthreads are whole warps
+    // and the lane count is a multiple of 8, so a group of 8 lanes is wholly
+    // inside or outside the range.
+    const int total = n_tok * nu * 8;   // lanes; token t's block b is lane group t·nu + b
+    const int lane = (int)(tid & 31);
+    float* dxs = reinterpret_cast<float*>(img.img + img.off_dx);
+    int16_t* bss = reinterpret_cast<int16_t*>(img.img + img.off_bs);
+    for (int64_t base = tid - lane; base < total; base += 4 * nthreads) {
+      float4 f[4];
+      int tk[4], bk[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) w[j] = 0;
-      const float4* src = reinterpret_cast<const float4*>(x + t * x_stride + (int64_t)b * 32);
-      float v[32];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 f = __ldg(src + j);
-        v[4 * j] = f.x;
-        v[4 * j + 1] = f.y;
-        v[4 * j + 2] = f.z;
-        v[4 * j + 3] = f.w;
+      for (int r = 0; r < 4; ++r) {
+        const int64_t i = base + r * nthreads + lane;
+        int b = 0, t = 0;
+        f[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < total) {
+          b = (int)(i >> 3);
+          while (b >= nu) {   // at most n_tok - 1 steps
+            b -= nu;
+            ++t;
+          }
+          f[r] = __ldg(reinterpret_cast<const float4*>(x + t * x_stride + b * 32) + (i & 7));
+        }
+        tk[r] = t;
+        bk[r] = b;
       }
-      float amax = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-      const float d = __fmul_rn(amax, 1.0f / 127.0f);
-      const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+      for (int r = 0; r < 4; ++r) {
+        if (base + r * nthreads >= total) break;   // warp-uniform
+        const int part = lane & 7, t = tk[r], b = bk[r];
+        const float v[4] = {f[r].x, f[r].y, f[r].z, f[r].w};
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        const float d = __fmul_rn(amax, 1.0f / 127.0f);
+        const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+        uint32_t wd = 0;
+        int sum = 0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float sc = __fmul_rn(v[j], id);
-        const float tt = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
-        int q = __float2int_rz(tt);
-        q = q < -127 ? -127 : (q > 127 ? 127 : q);
-        sum += q;
-        w[j >> 2] |= ((uint32_t)(uint8_t)q) << (8 * (j & 3));
+        for (int j = 0; j < 4; ++j) {
+          const float sc = __fmul_rn(v[j], id);
+          const float tt = sc >= 0.0f ? __fadd_rn(sc, 0.5f) : __fsub_rn(sc, 0.5f);
+          int q = __float2int_rz(tt);
+          q = q < -127 ? -127 : (q > 127 ? 127 : q);
+          sum += q;
+          wd |= ((uint32_t)(uint8_t)q) << (8 * j);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        if (base + r * nthreads + lane < total) {
+          *reinterpret_cast<uint32_t*>(img.img + t * img.kq + b * 32 + part * 4) = wd;
+          if (part == 0) {
+            dxs[t * nu + b] = h2f(f2h_rn(d));
+            if (img.type == B2_Q4_0) bss[t * nu + b] = (int16_t)sum;
+          }
+        }
       }
-      store_q8_0_block(img, t, b, w, h2f(f2h_rn(d)), sum);
     }
   } else {
     // One 256-value super-block per warp, 8 values per lane.
@@ -1100,6 +1135,175 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_kernel(const GemvP p) 
   }
 }
 
+// Row-fold form for 1-2 tokens over few tiles per CTA.  The CTA's whole run
+// of tiles (a contiguous range of the tiled matrix) is copied into shared
+// memory before the grid dependency resolves; a CTA takes at most
+// kRowsSmemCap bytes, so two fit on an SM and the next launch's weights
+// stream while this launch computes.  After the activations are in place,
+// all warps (16 for Q4_0 / Q8_0, 8 for the K-quants) compute unit terms of
+// any (tile, unit) — lane (g, j) the
+// term of row g and unit 4q + j, exactly as dp4a_terms forms it — into a
+// [token][row][unit] table, and then one thread per (token, row) folds its
+// row's terms in unit order: the reference's left fold, sumf = ((0 + p_0) +
+// p_1) + ... (Q4_K: ((sumf + a_u) − b_u)), so the outputs are the same bits
+// as gemv_kernel's.  The fold is one chain of nu adds per row; the terms,
+// which are most of the work, are spread over every warp whatever the
+// number of tiles.
+// 16 warps for Q4_0 / Q8_0 (64 registers a thread, so two CTAs fit), 8 for
+// the K-quants, whose unit terms take more registers.
+__host__ __device__ constexpr int rows_threads(int type) { return type == B2_Q4_0 || type == B2_Q8_0 ? 512 : 256; }
+constexpr int kRowsSmemCap = 112 * 1024;
+constexpr int kRowsHdr = 128;   // the weights' and the activations' mbarriers
+
+template <int WT, int NB>
+__global__ void __launch_bounds__(rows_threads(WT), 2) gemv_rows_kernel(const GemvP p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int NT = WT == B2_Q4_K ? 2 : 1;   // term tables: a (and b for Q4_K)
+  uint64_t* wbar = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* abar = wbar + 1;
+  uint8_t* act = smem + kRowsHdr;
+  uint8_t* wsm = act + p.act_region;
+  float* terms = reinterpret_cast<float*>(wsm + p.rf_w_bytes);   // [NT][NB][rf_rows][rf_stride]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t t0 = p.n_tiles * blockIdx.x / gridDim.x, t1 = p.n_tiles * (blockIdx.x + 1) / gridDim.x;
+  const int nt = (int)(t1 - t0);
+  if (tid == 0) {
+    mbar_init(wbar, 1);
+    mbar_init(abar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  // The weights do not depend on the previous kernel: one bulk copy per
+  // tile, from different lanes so that they overlap.
+  if (warp == 0) {
+    if (lane == 0) mbar_arrive_expect_tx(wbar, (uint32_t)nt * (uint32_t)p.tile_bytes);
+    __syncwarp();
+    if (lane < nt)
+      bulk_g2s(wsm + (size_t)lane * p.tile_bytes, p.wl[0] + (t0 + lane) * p.tile_bytes, (uint32_t)p.tile_bytes, wbar);
+  }
+  pdl_wait();
+  bool ok = true;
+  if (p.act_img) {
+    if (tid == 0) {
+      mbar_arrive_expect_tx(abar, p.act_bytes);
+      bulk_g2s(act, p.act_img, p.act_bytes, abar);
+    }
+    ok = mbar_wait_bounded(abar, 0, p.status, 3);
+  } else {
+    ActImage ai;
+    ai.img = act;
+    ai.kq = p.kq;
+    ai.nu = p.nu;
+    ai.type = p.type;
+    ai.n_act_tok = p.n_tok;
+    ai.off_dx = p.off_dx;
+    ai.off_bs = p.off_bs;
+    quantize_image(p.x, p.x_stride, p.n_tok, ai, tid, rows_threads(WT));
+  }
+  if (ok) ok = mbar_wait_bounded(wbar, 0, p.status, 1);
+  ok = __syncthreads_and(ok);
+  const int stride = p.rf_stride, rows = p.rf_rows;
+  if (ok) {
+    // Terms: quad q of tile i is (tile i, units 4q..4q+3); a table row's
+    // stride is 4 (mod 32) words, so the 32 lanes' stores hit 32 banks.
+    // Two quads per round (w and w + 8), whose loads and integer work
+    // interleave.
+    constexpr int NW = rows_threads(WT) / 32;
+    const int nq = (p.nu + 3) >> 2, g = lane & 7, j = lane >> 3, n_w = nt * nq;
+    int wi = 0, wq = warp;   // quad w0 = wi·nq + wq, kept without a division
+    while (wq >= nq) {
+      wq -= nq;
+      ++wi;
+    }
+    for (int w0 = warp; w0 < n_w; w0 += 2 * NW) {
+      float pa[2][NB], pb[2][NB];
+      int i[2], u[2];
+      i[0] = wi;
+      u[0] = wq * 4 + j;
+      i[1] = wi;
+      int q1 = wq + NW;
+      while (q1 >= nq) {
+        q1 -= nq;
+        ++i[1];
+      }
+      u[1] = q1 * 4 + j;
+      wi = i[1];
+      wq = q1 + NW;
+      while (wq >= nq) {
+        wq -= nq;
+        ++wi;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int w = w0 + h * NW;
+        if (w < n_w && u[h] < p.nu)
+          dp4a_terms<WT, NB>(p, wsm + (size_t)i[h] * p.tile_bytes + (size_t)u[h] * p.slot_bytes, act, u[h], g,
+                             pa[h], pb[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (w0 + h * NW < n_w && u[h] < p.nu) {
+#pragma unroll
+          for (int t = 0; t < NB; ++t) {
+            terms[((size_t)t * rows + i[h] * 8 + g) * stride + u[h]] = pa[h][t];
+            if constexpr (NT == 2) terms[((size_t)(NB + t) * rows + i[h] * 8 + g) * stride + u[h]] = pb[h][t];
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // The fold: thread (t, r) over row r's terms of token t, in unit order.
+  const int t = tid / rows, r = tid - t * rows;
+  const bool mine = ok && t < NB && r < nt * 8;
+  float acc = 0.0f;
+  if (mine) {
+    const float* ta = terms + ((size_t)t * rows + r) * stride;
+    const float* tb = terms + ((size_t)(NB + t) * rows + r) * stride;
+    int u = 0;
+    for (; u + 4 <= p.nu; u += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(ta + u);
+      if constexpr (NT == 2) {
+        const float4 b = *reinterpret_cast<const float4*>(tb + u);
+        acc = __fsub_rn(__fadd_rn(acc, a.x), b.x);
+        acc = __fsub_rn(__fadd_rn(acc, a.y), b.y);
+        acc = __fsub_rn(__fadd_rn(acc, a.z), b.z);
+        acc = __fsub_rn(__fadd_rn(acc, a.w), b.w);
+      } else {
+        acc = __fadd_rn(acc, a.x);
+        acc = __fadd_rn(acc, a.y);
+        acc = __fadd_rn(acc, a.z);
+        acc = __fadd_rn(acc, a.w);
+      }
+    }
+    for (; u < p.nu; ++u) {
+      acc = __fadd_rn(acc, ta[u]);
+      if constexpr (NT == 2) acc = __fsub_rn(acc, tb[u]);
+    }
+  }
+  // rows r and r + 1 (r even) are neighbouring lanes of one warp: rows is a
+  // multiple of 8
+  const float other = __shfl_down_sync(0xffffffffu, acc, 1);
+  if (mine) {
+    const int64_t row = t0 * 8 + r;
+    float* y = p.yl[0];
+    if (p.epilogue == EPI_ROPE_KV || p.epilogue == EPI_SWIGLU) {
+      if ((r & 1) == 0) emit_pair(p, y, t, row, acc, other);
+    } else if (row < p.n_rows) {
+      store_y(p, y, t, row, acc);
+    }
+  }
+  if (!ok && tid == 0) {   // copies still in flight after a failed wait (bounded)
+    mbar_wait_bounded(wbar, 0, nullptr, 0);
+    if (p.act_img) mbar_wait_bounded(abar, 0, nullptr, 0);
+  }
+  if (p.peer.n) {
+    __syncthreads();
+    if (tid == 0) signal_peers(p);
+  }
+}
+
 constexpr int kSmemCap = 227 * 1024;
 
 template <int WT, int MODE, bool KS>
@@ -1110,7 +1314,10 @@ int set_attr() {
 
 template <int WT>
 int set_attr_all() {
-  int rc = set_attr<WT, 1, false>();
+  int rc = 0;
+  B2_CUDA_TRY(cudaFuncSetAttribute(gemv_rows_kernel<WT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemCap));
+  B2_CUDA_TRY(cudaFuncSetAttribute(gemv_rows_kernel<WT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemCap));
+  rc = set_attr<WT, 1, false>();
   if (!rc) rc = set_attr<WT, 2, false>();
   if (!rc) rc = set_attr<WT, 3, false>();
   if (!rc) rc = set_attr<WT, 1, true>();
@@ -1143,13 +1350,33 @@ int launch_k(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
 }
 
 template <int WT>
+int launch_rows(const GemvP& p, int grid, size_t smem, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(rows_threads(WT));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (p.n_tok == 1) {
+    B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_rows_kernel<WT, 1>, p));
+  } else {
+    B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_rows_kernel<WT, 2>, p));
+  }
+  return B2_OK;
+}
+
+template <int WT>
 int launch_w(const GemvP& p, int grid, int nw, size_t smem, cudaStream_t s) {
   return p.S > 1 ? launch_k<WT, true>(p, grid, nw, smem, s) : launch_k<WT, false>(p, grid, nw, smem, s);
 }
 
 int launch_quantize_image(const float* x, int64_t x_stride, int n_tok, const ActImage& g, cudaStream_t s) {
   const bool k_quant = g.type == B2_Q4_K || g.type == B2_Q6_K;
-  const int64_t work = (int64_t)n_tok * g.nu * (k_quant ? 32 : 1);   // threads wanted
+  const int64_t work = (int64_t)n_tok * g.nu * (k_quant ? 32 : 2);   // threads wanted (Q8_0: 8 lanes per block, 4 rounds)
   const int block = 256;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + block - 1) / block, 4 * sm_count()));
   cudaLaunchConfig_t cfg = {};
@@ -1305,6 +1532,33 @@ int launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.tpm = w.n_tiles;
   const int sms = sm_count();
   const bool pairs = a.n_tok > kDp4aMaxTok;
+  // Row-fold form: 1-2 tokens of one matrix, where a CTA's run of tiles fits
+  // in kRowsSmemCap with the activations and the terms table; one CTA per
+  // SM, or two where one SM's share does not fit.
+  for (int per_sm = 1; per_sm <= 2 && !pairs && a.n_mat == 1 && !a.mat_ids; ++per_sm) {
+    const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)per_sm * sms, w.n_tiles));
+    const int64_t max_tiles = (w.n_tiles + rgrid - 1) / rgrid;
+    const int64_t rows = max_tiles * 8;
+    const size_t stride = align_up((size_t)w.nu, 32) + 4;
+    const size_t wbytes = align_up((size_t)max_tiles * (size_t)w.tile_bytes, 128);
+    const size_t tbytes = (size_t)(w.type == B2_Q4_K ? 2 : 1) * a.n_tok * rows * stride * 4;
+    const size_t rsmem = kRowsHdr + p.act_region + wbytes + tbytes;
+    if (a.n_tok * rows <= rows_threads(w.type) && rsmem <= kRowsSmemCap) {
+      p.rf_rows = (int)rows;
+      p.rf_stride = (int)stride;
+      p.rf_w_bytes = (uint32_t)wbytes;
+      if (!in_kernel && !a.image_ready) {
+        const int qrc = launch_quantize_image(a.x, a.x_stride, a.n_tok, ag, s);
+        if (qrc) return qrc;
+      }
+      switch (w.type) {
+        case B2_Q4_0: return launch_rows<B2_Q4_0>(p, rgrid, rsmem, s);
+        case B2_Q8_0: return launch_rows<B2_Q8_0>(p, rgrid, rsmem, s);
+        case B2_Q4_K: return launch_rows<B2_Q4_K>(p, rgrid, rsmem, s);
+        case B2_Q6_K: return launch_rows<B2_Q6_K>(p, rgrid, rsmem, s);
+      }
+    }
+  }
   p.ipt = pairs ? 2 : 1;
   const int64_t n_items = pairs ? (w.n_tiles + 1) / 2 : p.tpm * p.n_mat;
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, n_items));
