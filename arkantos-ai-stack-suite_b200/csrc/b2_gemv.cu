@@ -417,6 +417,73 @@ __device__ __forceinline__ void dp4a_terms(const GemvP& p, const uint8_t* sl, co
   }
 }
 
+// Q4_0 / Q8_0 terms of unit u for all 8 rows of a tile from one lane (the
+// row-fold form): the unit's activation codes, scale and block sum are read
+// once, then each row's block sum and its update term exactly as dp4a_terms
+// forms them, (d_r·dx_t)·isum, stored at out[t·tok_stride + r·row_stride].
+template <int WT, int NB>
+__device__ __forceinline__ void unit_terms8(const GemvP& p, const uint8_t* sl, const uint8_t* act, int u, float* out,
+                                            int row_stride, int tok_stride) {
+  static_assert(WT == B2_Q4_0 || WT == B2_Q8_0, "Q4_0 / Q8_0 slots");
+  const float* dxs = reinterpret_cast<const float*>(act + p.off_dx);
+  const int16_t* bss = reinterpret_cast<const int16_t*>(act + p.off_bs);
+  uint4 xa[NB], xb[NB];
+  float dx[NB];
+  int off[NB];
+#pragma unroll
+  for (int t = 0; t < NB; ++t) {
+    const uint8_t* xr = act + t * p.kq + u * 32;
+    xa[t] = lds128(xr);
+    xb[t] = lds128(xr + 16);
+    dx[t] = dxs[t * p.nu + u];
+    off[t] = WT == B2_Q4_0 ? 8 * (int)bss[t * p.nu + u] : 0;
+  }
+  const uint4 dq = lds128(sl + (WT == B2_Q4_0 ? 128 : 256));   // the 8 rows' fp16 scales
+  const uint32_t dqw[4] = {dq.x, dq.y, dq.z, dq.w};
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const float dw = h2f((uint16_t)(dqw[r >> 1] >> (16 * (r & 1))));
+    uint32_t lo[4], hi[4];
+    if constexpr (WT == B2_Q4_0) {
+      const uint4 w = lds128(sl + 16 * r);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        lo[c] = ww[c] & kM4;
+        hi[c] = (ww[c] >> 4) & kM4;
+      }
+    } else {
+      const uint4 a = lds128(sl + 16 * r), b = lds128(sl + 128 + 16 * r);
+      lo[0] = a.x; lo[1] = a.y; lo[2] = a.z; lo[3] = a.w;
+      hi[0] = b.x; hi[1] = b.y; hi[2] = b.z; hi[3] = b.w;
+    }
+#pragma unroll
+    for (int t = 0; t < NB; ++t) {
+      int s0, s1;
+      if constexpr (WT == B2_Q4_0) {
+        s0 = dp4a_us(lo[0], xa[t].x, 0);
+        s1 = dp4a_us(hi[0], xb[t].x, 0);
+        s0 = dp4a_us(lo[1], xa[t].y, s0);
+        s1 = dp4a_us(hi[1], xb[t].y, s1);
+        s0 = dp4a_us(lo[2], xa[t].z, s0);
+        s1 = dp4a_us(hi[2], xb[t].z, s1);
+        s0 = dp4a_us(lo[3], xa[t].w, s0);
+        s1 = dp4a_us(hi[3], xb[t].w, s1);
+      } else {
+        s0 = dp4a_ss(lo[0], xa[t].x, 0);
+        s1 = dp4a_ss(hi[0], xb[t].x, 0);
+        s0 = dp4a_ss(lo[1], xa[t].y, s0);
+        s1 = dp4a_ss(hi[1], xb[t].y, s1);
+        s0 = dp4a_ss(lo[2], xa[t].z, s0);
+        s1 = dp4a_ss(hi[2], xb[t].z, s1);
+        s0 = dp4a_ss(lo[3], xa[t].w, s0);
+        s1 = dp4a_ss(hi[3], xb[t].w, s1);
+      }
+      out[t * tok_stride + r * row_stride] = __fmul_rn(__fmul_rn(dw, dx[t]), (float)(s0 + s1 - off[t]));
+    }
+  }
+}
+
 // ---- rows-as-M path: the terms of one unit u of two tiles for lane 4g+q ---------------------
 // i = 2·(tile B) + (token 2q+1): a[i] / b[i] as in dp4a_terms for row g of
 // tile A (i = 0, 1) or of tile B (i = 2, 3) and token 2q (i even) or 2q+1.
@@ -1205,10 +1272,23 @@ __global__ void __launch_bounds__(rows_threads(WT), 2) gemv_rows_kernel(const Ge
   ok = __syncthreads_and(ok);
   const int stride = p.rf_stride, rows = p.rf_rows;
   if (ok) {
-    // Terms: quad q of tile i is (tile i, units 4q..4q+3); a table row's
-    // stride is 4 (mod 32) words, so the 32 lanes' stores hit 32 banks.
-    // Two quads per round (w and w + 8), whose loads and integer work
-    // interleave.
+    if constexpr (WT == B2_Q4_0 || WT == B2_Q8_0) {
+    // Terms, Q4_0 / Q8_0: item (tile i, unit u) per lane, all 8 rows of the
+    // tile (unit_terms8), so a unit's activation codes are read once per
+    // tile.  Lanes take consecutive units: slots 144 or 272 bytes apart (4
+    // words mod 32) and table rows whose stride is 4 (mod 32) words, so
+    // neither the loads nor the stores conflict on banks.
+    const int n_items = nt * p.nu;
+    for (int it = tid; it < n_items; it += rows_threads(WT)) {
+      const int i = it / p.nu, u = it - i * p.nu;
+      unit_terms8<WT, NB>(p, wsm + (size_t)i * p.tile_bytes + (size_t)u * p.slot_bytes, act, u,
+                          terms + (size_t)i * 8 * stride + u, stride, rows * stride);
+    }
+    } else {
+    // Terms, K-quants: quad q of tile i is (tile i, units 4q..4q+3); a table
+    // row's stride is 4 (mod 32) words, so the 32 lanes' stores hit 32
+    // banks.  Two quads per round (w and w + 8), whose loads and integer
+    // work interleave.
     constexpr int NW = rows_threads(WT) / 32;
     const int nq = (p.nu + 3) >> 2, g = lane & 7, j = lane >> 3, n_w = nt * nq;
     int wi = 0, wq = warp;   // quad w0 = wi·nq + wq, kept without a division
@@ -1251,6 +1331,7 @@ __global__ void __launch_bounds__(rows_threads(WT), 2) gemv_rows_kernel(const Ge
           }
         }
       }
+    }
     }
   }
   __syncthreads();
